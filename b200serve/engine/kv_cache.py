@@ -1,0 +1,123 @@
+"""Paged KV cache: device storage plus the host-side block allocator.
+
+Storage per layer is [num_blocks, kv_heads, 16, head_dim] for K and for V, so
+one (page, head) is a contiguous 16 x head_dim tile. Blocks are handed out by
+``BlockAllocator``, which also keeps a prefix index (hash of the token ids of
+each full block chained with its predecessor's hash) so a new request whose
+prompt starts with cached blocks reuses them (reference idea: KV-session reuse
+on exact prefix extension, webgpu/src/engine/generate.ts:89-117).
+"""
+
+from __future__ import annotations
+
+import hashlib
+from collections import OrderedDict
+
+import torch
+
+BLOCK = 16
+
+
+class KVCache:
+    def __init__(self, num_layers, num_blocks, kv_heads, head_dim, dtype=torch.bfloat16, device="cpu",
+                 kv_format="bf16"):
+        self.num_layers = num_layers
+        self.num_blocks = num_blocks
+        self.kv_heads = kv_heads
+        self.head_dim = head_dim
+        self.kv_format = kv_format
+        shape = (num_layers, num_blocks, kv_heads, BLOCK, head_dim)
+        self.k = torch.zeros(shape, dtype=dtype, device=device)
+        self.v = torch.zeros(shape, dtype=dtype, device=device)
+
+    @staticmethod
+    def bytes_per_block(num_layers, kv_heads, head_dim, elem_bytes=2) -> int:
+        return 2 * num_layers * kv_heads * BLOCK * head_dim * elem_bytes
+
+
+def _block_hash(prev: bytes, tokens) -> bytes:
+    h = hashlib.blake2b(prev, digest_size=16)
+    h.update(bytes(memoryview(torch.as_tensor(list(tokens), dtype=torch.int32).numpy())))
+    return h.digest()
+
+
+class BlockAllocator:
+    """Reference-counted page allocator with an LRU prefix cache of freed full blocks."""
+
+    def __init__(self, num_blocks: int, enable_prefix_cache: bool = True):
+        self.num_blocks = num_blocks
+        self.free = list(range(num_blocks - 1, -1, -1))
+        self.ref = [0] * num_blocks
+        self.hash_of = {}                  # block -> hash (full, registered blocks)
+        self.by_hash = {}                  # hash -> block
+        self.evictable = OrderedDict()     # hash -> block (ref == 0, still cached)
+        self.prefix = enable_prefix_cache
+
+    @property
+    def num_free(self) -> int:
+        return len(self.free) + len(self.evictable)
+
+    def _take(self) -> int:
+        if self.free:
+            return self.free.pop()
+        if self.evictable:
+            hsh, blk = self.evictable.popitem(last=False)
+            del self.by_hash[hsh]
+            del self.hash_of[blk]
+            return blk
+        raise MemoryError("KV cache out of blocks")
+
+    def allocate(self, n: int) -> list:
+        if n > self.num_free:
+            raise MemoryError(f"need {n} KV blocks, {self.num_free} free")
+        out = []
+        for _ in range(n):
+            b = self._take()
+            self.ref[b] = 1
+            out.append(b)
+        return out
+
+    def release(self, blocks) -> None:
+        for b in blocks:
+            self.ref[b] -= 1
+            assert self.ref[b] >= 0
+            if self.ref[b] == 0:
+                h = self.hash_of.get(b)
+                if h is not None and self.prefix:
+                    self.evictable[h] = b
+                else:
+                    self.hash_of.pop(b, None)
+                    self.free.append(b)
+
+    def match_prefix(self, tokens) -> tuple:
+        """Longest run of cached full blocks that starts ``tokens``: (blocks, hashes)."""
+        if not self.prefix:
+            return [], []
+        blocks, hashes, prev = [], [], b""
+        for i in range(len(tokens) // BLOCK):
+            hsh = _block_hash(prev, tokens[i * BLOCK:(i + 1) * BLOCK])
+            b = self.by_hash.get(hsh)
+            if b is None:
+                break
+            blocks.append(b)
+            hashes.append(hsh)
+            prev = hsh
+        for hsh, b in zip(hashes, blocks):
+            if self.ref[b] == 0:
+                self.evictable.pop(hsh, None)
+            self.ref[b] += 1
+        return blocks, hashes
+
+    def register(self, blocks, tokens, start_block: int = 0, prev_hash: bytes = b"") -> bytes:
+        """Index the full blocks of a sequence (blocks[i] holds tokens[16i:16i+16])."""
+        if not self.prefix:
+            return prev_hash
+        prev = prev_hash
+        for i in range(start_block, len(tokens) // BLOCK):
+            hsh = _block_hash(prev, tokens[i * BLOCK:(i + 1) * BLOCK])
+            b = blocks[i]
+            if hsh not in self.by_hash and b not in self.hash_of:
+                self.by_hash[hsh] = b
+                self.hash_of[b] = hsh
+            prev = hsh
+        return prev

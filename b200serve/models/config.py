@@ -1,0 +1,134 @@
+"""Model shapes.
+
+The three built-in shapes are the configurations the benchmarks name:
+* ``tiny-qwen2``: 2 layers, hidden 256, 4 query / 2 KV heads (head_dim 64),
+  SwiGLU 688, vocab 32000, q/k/v bias (Qwen2), RMSNorm eps 1e-6, RoPE 1e6;
+* ``qwen3-8b``: 36 layers, hidden 4096, 32/8 heads (head_dim 128), SwiGLU
+  12288, vocab 151936, per-head q/k RMSNorm (Qwen3), RoPE 1e6;
+* ``qwen3-30b-a3b``: 48 layers, hidden 2048, 32/4 heads (head_dim 128), 128
+  experts with top-8 softmax routing, expert FFN 768, vocab 151936.
+HF ``config.json`` files of the qwen2 / qwen3 / qwen3_moe families map onto
+the same dataclass.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+from dataclasses import dataclass, replace
+
+
+@dataclass
+class ModelConfig:
+    name: str
+    vocab_size: int
+    hidden_size: int
+    num_layers: int
+    num_heads: int
+    num_kv_heads: int
+    head_dim: int
+    intermediate_size: int
+    rms_eps: float = 1e-6
+    rope_theta: float = 1e6
+    attn_bias: bool = False          # Qwen2: bias on q/k/v projections
+    qk_norm: bool = False            # Qwen3: RMSNorm over head_dim on q and k
+    tie_embeddings: bool = False
+    num_experts: int = 0             # 0 = dense FFN
+    experts_per_tok: int = 0
+    moe_intermediate_size: int = 0
+    norm_topk_prob: bool = True
+    max_position: int = 40960
+    bos_token_id: int = 1
+    eos_token_id: int = 2
+
+    @property
+    def is_moe(self) -> bool:
+        return self.num_experts > 0
+
+    @property
+    def q_size(self) -> int:
+        return self.num_heads * self.head_dim
+
+    @property
+    def kv_size(self) -> int:
+        return self.num_kv_heads * self.head_dim
+
+    def num_params(self) -> int:
+        h, l = self.hidden_size, self.num_layers
+        attn = h * (self.q_size + 2 * self.kv_size) + self.q_size * h
+        if self.is_moe:
+            ffn = self.num_experts * 3 * h * self.moe_intermediate_size + self.num_experts * h
+        else:
+            ffn = 3 * h * self.intermediate_size
+        emb = self.vocab_size * h * (1 if self.tie_embeddings else 2)
+        return l * (attn + ffn + 2 * h) + emb + h
+
+    def to_hf_dict(self) -> dict:
+        """A config.json body understood by transformers for this shape."""
+        d = {
+            "vocab_size": self.vocab_size, "hidden_size": self.hidden_size,
+            "num_hidden_layers": self.num_layers, "num_attention_heads": self.num_heads,
+            "num_key_value_heads": self.num_kv_heads, "head_dim": self.head_dim,
+            "intermediate_size": self.intermediate_size, "rms_norm_eps": self.rms_eps,
+            "rope_theta": self.rope_theta, "tie_word_embeddings": self.tie_embeddings,
+            "max_position_embeddings": self.max_position, "hidden_act": "silu",
+            "bos_token_id": self.bos_token_id, "eos_token_id": self.eos_token_id,
+            "initializer_range": 0.02, "attention_dropout": 0.0,
+        }
+        if self.is_moe:
+            d.update(model_type="qwen3_moe", architectures=["Qwen3MoeForCausalLM"],
+                     num_experts=self.num_experts, num_experts_per_tok=self.experts_per_tok,
+                     moe_intermediate_size=self.moe_intermediate_size,
+                     norm_topk_prob=self.norm_topk_prob, decoder_sparse_step=1, mlp_only_layers=[])
+        elif self.qk_norm:
+            d.update(model_type="qwen3", architectures=["Qwen3ForCausalLM"], attention_bias=False)
+        else:
+            d.update(model_type="qwen2", architectures=["Qwen2ForCausalLM"])
+        return d
+
+
+BUILTIN = {
+    "tiny-qwen2": ModelConfig("tiny-qwen2", 32000, 256, 2, 4, 2, 64, 688, attn_bias=True),
+    "qwen3-8b": ModelConfig("qwen3-8b", 151936, 4096, 36, 32, 8, 128, 12288, qk_norm=True),
+    "qwen3-30b-a3b": ModelConfig("qwen3-30b-a3b", 151936, 2048, 48, 32, 4, 128, 6144, qk_norm=True,
+                                 num_experts=128, experts_per_tok=8, moe_intermediate_size=768),
+}
+
+
+def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
+    mt = d.get("model_type", "qwen2")
+    heads = d["num_attention_heads"]
+    hd = d.get("head_dim") or d["hidden_size"] // heads
+    return ModelConfig(
+        name=name, vocab_size=d["vocab_size"], hidden_size=d["hidden_size"],
+        num_layers=d["num_hidden_layers"], num_heads=heads,
+        num_kv_heads=d.get("num_key_value_heads", heads), head_dim=hd,
+        intermediate_size=d.get("intermediate_size", 0), rms_eps=d.get("rms_norm_eps", 1e-6),
+        rope_theta=d.get("rope_theta", 1e6) or (d.get("rope_parameters") or {}).get("rope_theta", 1e6),
+        attn_bias=(mt == "qwen2") or bool(d.get("attention_bias", False)),
+        qk_norm=mt in ("qwen3", "qwen3_moe"),
+        tie_embeddings=bool(d.get("tie_word_embeddings", False)),
+        num_experts=d.get("num_experts", 0) if mt == "qwen3_moe" else 0,
+        experts_per_tok=d.get("num_experts_per_tok", 0) if mt == "qwen3_moe" else 0,
+        moe_intermediate_size=d.get("moe_intermediate_size", 0) if mt == "qwen3_moe" else 0,
+        norm_topk_prob=d.get("norm_topk_prob", True),
+        max_position=d.get("max_position_embeddings", 40960),
+        bos_token_id=d.get("bos_token_id") or 1,
+        eos_token_id=(d.get("eos_token_id") if isinstance(d.get("eos_token_id"), int) else 2),
+    )
+
+
+def get_model_config(name_or_path: str, num_layers: int = 0) -> ModelConfig:
+    if name_or_path in BUILTIN:
+        cfg = BUILTIN[name_or_path]
+    elif os.path.isdir(name_or_path):
+        with open(os.path.join(name_or_path, "config.json")) as fh:
+            cfg = from_hf_config(json.load(fh), os.path.basename(name_or_path.rstrip("/")))
+    elif name_or_path.endswith(".gguf"):
+        from b200serve.models.gguf import config_from_gguf
+        cfg = config_from_gguf(name_or_path)
+    else:
+        raise ValueError(f"unknown model {name_or_path!r}")
+    if num_layers:
+        cfg = replace(cfg, num_layers=num_layers)
+    return cfg

@@ -1,0 +1,140 @@
+"""Qwen2 / Qwen3 / Qwen3-MoE decoder over a paged KV cache.
+
+One ``forward`` serves prefill (many tokens per sequence, causal attention
+against the paged cache, so chunked prefill and prefix reuse come for free)
+and decode (one token per sequence, split-KV attention). Every heavy op goes
+through ``b200serve.ops`` (sm_100a kernels on CUDA tensors).
+
+Tensor parallelism (Megatron layout): q/k/v and gate/up are column-parallel,
+o and down are row-parallel; the two row-parallel outputs per layer are
+combined by ``comm`` (an all-reduce: NCCL, or the fused in-kernel NVLink path),
+and the sum is consumed directly by the next fused add+RMSNorm kernel.
+The vocabulary is split across ranks for lm_head.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from b200serve import ops
+from b200serve.models.config import ModelConfig
+from b200serve.models.weights import ModelWeights
+
+
+@dataclass
+class ForwardBatch:
+    """Token-level inputs of one forward pass (all int32, on the model device).
+
+    Decode: T == number of sequences, one new token each.
+    Prefill: ``cu_q`` [S+1] offsets of each sequence's new tokens, ``q_start`` [S]
+    absolute position of its first new token.
+    """
+
+    input_ids: torch.Tensor
+    positions: torch.Tensor
+    slots: torch.Tensor
+    block_tables: torch.Tensor
+    seq_lens: torch.Tensor
+    logit_rows: torch.Tensor            # rows whose logits are returned
+    is_decode: bool = True
+    cu_q: torch.Tensor = None
+    q_start: torch.Tensor = None
+    max_q: int = 0
+
+
+class NoComm:
+    """Single-rank stand-in for the tensor-parallel reduction."""
+
+    world = 1
+    rank = 0
+
+    def reduce_parts(self, t: torch.Tensor, tag: str):
+        return [t]
+
+    def gather_vocab(self, x):
+        return x
+
+
+class Decoder:
+    def __init__(self, cfg: ModelConfig, weights: ModelWeights, kv_cache, comm=None, attn_splits=None,
+                 device="cpu"):
+        self.cfg = cfg
+        self.w = weights
+        self.kv = kv_cache
+        self.comm = comm or NoComm()
+        self.device = torch.device(device)
+        tp = weights.tp_size
+        self.nq = cfg.num_heads // tp
+        self.nkv = cfg.num_kv_heads // tp
+        self.hd = cfg.head_dim
+        self.scale = ops.softmax_scale(cfg.head_dim)
+        self.cos_sin = ops.rope_cos_sin(cfg.head_dim, cfg.max_position, cfg.rope_theta, self.device)
+        self.attn_ws = None
+        self.moe = None
+        if cfg.is_moe:
+            from b200serve.models.moe import MoEBlock
+            self.moe = MoEBlock(cfg, weights, comm=self.comm, device=self.device)
+
+    # -------------------------------------------------------------- helpers
+    def decode_attn_plan(self, batch: int, max_seq: int):
+        """Tokens per split and split count for the decode attention grid: aim for
+        >= 2 CTAs per SM over (batch x kv heads x splits)."""
+        target = 2 * 148
+        per = max(1, batch * self.nkv)
+        want = max(1, (target + per - 1) // per)
+        tps = max(64, ((max_seq + want - 1) // want + 15) // 16 * 16)
+        tps = min(tps, 1024)
+        nsplit = (max_seq + tps - 1) // tps
+        return tps, nsplit
+
+    def ensure_attn_workspace(self, batch: int, nsplit: int):
+        ws = self.attn_ws
+        need_b = max(batch, 1)
+        if ws is None or ws.max_splits < nsplit or ws.acc.numel() < need_b * self.nkv * nsplit * (
+                self.nq // self.nkv) * self.hd:
+            self.attn_ws = ops.AttnWorkspace(self.device, need_b, self.nkv, self.nq // self.nkv, self.hd,
+                                             max(nsplit, ws.max_splits if ws else 1))
+        return self.attn_ws
+
+    # -------------------------------------------------------------- forward
+    def forward(self, fb: ForwardBatch, attn_plan=None) -> torch.Tensor:
+        """Returns fp32 logits [len(logit_rows), vocab shard of this rank]."""
+        cfg, w = self.cfg, self.w
+        eps = cfg.rms_eps
+        T = fb.input_ids.shape[0]
+        h = ops.embedding(fb.input_ids, w.embed)
+        residual = torch.empty_like(h)
+        x = ops.rmsnorm([h], w.layers[0].input_norm, eps, residual_out=residual)
+        if fb.is_decode:
+            tps, nsplit = attn_plan or self.decode_attn_plan(T, int(fb.block_tables.shape[1]) * 16)
+            ws = self.ensure_attn_workspace(T, nsplit) if nsplit > 1 else None
+        k_all, v_all = self.kv.k, self.kv.v
+        for i, lw in enumerate(w.layers):
+            if i > 0:
+                x = ops.rmsnorm(mlp_parts, lw.input_norm, eps, residual=residual, residual_out=residual)
+            qkv = ops.linear(x, lw.qkv, bias=lw.qkv_bias)
+            kc, vc = k_all[i], v_all[i]
+            q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots, kc, vc,
+                             self.nq, self.nkv, eps)
+            if fb.is_decode:
+                attn = ops.paged_decode_attention(q, kc, vc, fb.block_tables, fb.seq_lens, self.scale, tps,
+                                                  nsplit, ws)
+            else:
+                attn = ops.paged_prefill_attention(q, kc, vc, fb.block_tables, fb.seq_lens, fb.q_start, fb.cu_q,
+                                                   self.scale, max_q=fb.max_q)
+            o = ops.linear(attn.view(T, self.nq * self.hd), lw.o)
+            o_parts = self.comm.reduce_parts(o, "o")
+            x = ops.rmsnorm(o_parts, lw.post_norm, eps, residual=residual, residual_out=residual)
+            if self.moe is not None:
+                d = self.moe(i, x)
+            else:
+                act = ops.linear(x, lw.gate_up, epilogue=ops.EPI_SWIGLU)
+                d = ops.linear(act, lw.down)
+            mlp_parts = self.comm.reduce_parts(d, "mlp")
+        rows = fb.logit_rows
+        x = ops.rmsnorm(mlp_parts, w.final_norm, eps, residual=residual)
+        if rows is not None:
+            x = x.index_select(0, rows)
+        return ops.linear(x, w.lm_head, epilogue=ops.EPI_F32)

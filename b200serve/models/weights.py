@@ -1,0 +1,291 @@
+"""Weight containers, random initialisation, HF-checkpoint import and TP sharding.
+
+Layouts used by the kernels (per layer, per tensor-parallel rank):
+* ``qkv``     [(nq + 2 nkv) * hd, H]   q heads, then k heads, then v heads of this rank
+* ``qkv_bias``[(nq + 2 nkv) * hd]      Qwen2 only
+* ``o``       [H, nq * hd]             row-parallel slice
+* ``gate_up`` [2 * I_pad, H]           64-row blocks interleaved g0..63, u0..63, g64.., so one
+                                       128-row GEMM tile holds matching gate and up rows
+* ``down``    [H, I_pad]               row-parallel slice (columns >= I are zero)
+I is padded to a multiple of 64 (zero rows / columns) so the interleave is exact.
+Embedding and final norm are replicated; ``lm_head`` is split by vocabulary rows.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from b200serve.models.config import ModelConfig
+
+
+def pad64(n: int) -> int:
+    return (n + 63) // 64 * 64
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """[I, H] gate and up -> [2*I_pad, H] in 64-row interleaved blocks."""
+    I, H = gate.shape
+    Ip = pad64(I)
+    if Ip != I:
+        z = gate.new_zeros(Ip - I, H)
+        gate, up = torch.cat([gate, z]), torch.cat([up, z])
+    return torch.stack([gate.view(Ip // 64, 64, H), up.view(Ip // 64, 64, H)], 1).reshape(2 * Ip, H)
+
+
+def deinterleave_gate_up(gu: torch.Tensor, I: int):
+    Ip = gu.shape[0] // 2
+    v = gu.view(Ip // 64, 2, 64, -1)
+    return v[:, 0].reshape(Ip, -1)[:I], v[:, 1].reshape(Ip, -1)[:I]
+
+
+def pad_down(down: torch.Tensor) -> torch.Tensor:
+    H, I = down.shape
+    Ip = pad64(I)
+    if Ip == I:
+        return down
+    return torch.cat([down, down.new_zeros(H, Ip - I)], 1)
+
+
+@dataclass
+class LayerWeights:
+    input_norm: torch.Tensor
+    post_norm: torch.Tensor
+    qkv: torch.Tensor
+    o: torch.Tensor
+    qkv_bias: torch.Tensor = None
+    q_norm: torch.Tensor = None
+    k_norm: torch.Tensor = None
+    gate_up: torch.Tensor = None       # dense FFN
+    down: torch.Tensor = None
+    router: torch.Tensor = None        # MoE: [E, H]
+    experts_gate_up: torch.Tensor = None  # [E_local, 2*Ie_pad, H]
+    experts_down: torch.Tensor = None     # [E_local, H, Ie_pad]
+
+
+@dataclass
+class ModelWeights:
+    embed: torch.Tensor
+    final_norm: torch.Tensor
+    lm_head: torch.Tensor              # [V_local, H]
+    layers: list = field(default_factory=list)
+    vocab_start: int = 0               # first vocabulary row held by this rank
+    tp_rank: int = 0
+    tp_size: int = 1
+    ep_rank: int = 0
+    ep_size: int = 1
+
+    def nbytes(self) -> int:
+        n = 0
+        for t in [self.embed, self.final_norm, self.lm_head]:
+            n += t.numel() * t.element_size()
+        for lw in self.layers:
+            for v in vars(lw).values():
+                if isinstance(v, torch.Tensor):
+                    n += v.numel() * v.element_size()
+        return n
+
+
+def _shard_rows(t, rank, size):
+    n = t.shape[0]
+    assert n % size == 0, f"cannot split {n} rows over {size} ranks"
+    k = n // size
+    return t[rank * k:(rank + 1) * k]
+
+
+def vocab_shard(V: int, rank: int, size: int):
+    per = (V + size - 1) // size
+    per = (per + 127) // 128 * 128 if size > 1 else per
+    start = min(V, rank * per)
+    return start, min(V, start + per)
+
+
+def shard_layer_dense(cfg: ModelConfig, full: dict, rank: int, size: int, dtype, device) -> LayerWeights:
+    """``full`` holds unsharded HF-named tensors of one layer (q,k,v,o,gate,up,down,...)."""
+    hd = cfg.head_dim
+    assert cfg.num_heads % size == 0 and cfg.num_kv_heads % size == 0, "heads must divide tp_size"
+    q = _shard_rows(full["q"], rank, size)
+    k = _shard_rows(full["k"], rank, size)
+    v = _shard_rows(full["v"], rank, size)
+    qkv = torch.cat([q, k, v])
+    bias = None
+    if cfg.attn_bias:
+        bias = torch.cat([_shard_rows(full["q_bias"], rank, size), _shard_rows(full["k_bias"], rank, size),
+                          _shard_rows(full["v_bias"], rank, size)])
+    o = full["o"]
+    oc = o.shape[1] // size
+    o = o[:, rank * oc:(rank + 1) * oc]
+    lw = LayerWeights(input_norm=full["input_norm"], post_norm=full["post_norm"], qkv=qkv, o=o, qkv_bias=bias,
+                      q_norm=full.get("q_norm"), k_norm=full.get("k_norm"))
+    if not cfg.is_moe:
+        I = cfg.intermediate_size
+        assert I % size == 0
+        Ir = I // size
+        g = full["gate"][rank * Ir:(rank + 1) * Ir]
+        u = full["up"][rank * Ir:(rank + 1) * Ir]
+        d = full["down"][:, rank * Ir:(rank + 1) * Ir]
+        lw.gate_up = interleave_gate_up(g, u)
+        lw.down = pad_down(d)
+    for name, val in vars(lw).items():
+        if isinstance(val, torch.Tensor):
+            setattr(lw, name, val.to(device=device, dtype=dtype).contiguous())
+    return lw
+
+
+
+
+def build_weights(cfg: ModelConfig, layer_source, embed, lm_head, final_norm, tp_rank=0, tp_size=1,
+                  ep_rank=0, ep_size=1, dtype=torch.bfloat16, device="cpu") -> ModelWeights:
+    """Assemble a rank's weights. ``layer_source(i)`` returns the unsharded dict of layer i."""
+    from b200serve.models.moe import shard_layer_moe
+    layers = []
+    for i in range(cfg.num_layers):
+        full = layer_source(i)
+        lw = shard_layer_dense(cfg, full, tp_rank, tp_size, dtype, device)
+        if cfg.is_moe:
+            shard_layer_moe(cfg, full, lw, ep_rank, ep_size, dtype, device)
+        layers.append(lw)
+        del full
+    v0, v1 = vocab_shard(cfg.vocab_size, tp_rank, tp_size)
+    return ModelWeights(
+        embed=embed.to(device=device, dtype=dtype).contiguous(),
+        final_norm=final_norm.to(device=device, dtype=dtype).contiguous(),
+        lm_head=lm_head[v0:v1].to(device=device, dtype=dtype).contiguous(),
+        layers=layers, vocab_start=v0, tp_rank=tp_rank, tp_size=tp_size, ep_rank=ep_rank, ep_size=ep_size)
+
+
+def random_weights(cfg: ModelConfig, seed=0, std=0.02, tp_rank=0, tp_size=1, ep_rank=0, ep_size=1,
+                   dtype=torch.bfloat16, device="cpu") -> ModelWeights:
+    """Random-init weights. Every rank draws the same full tensors from ``seed`` and keeps its
+    shard, so a TP=N model equals the TP=1 model. Large shapes are generated on the target
+    device layer by layer to keep host memory and time bounded."""
+    gen_dev = device if (torch.device(device).type == "cuda") else "cpu"
+    gen = torch.Generator(device=gen_dev)
+    gen.manual_seed(seed)
+    H, V = cfg.hidden_size, cfg.vocab_size
+
+    def n(*shape):
+        return torch.randn(*shape, generator=gen, device=gen_dev, dtype=torch.float32).mul_(std).to(dtype)
+
+    embed = n(V, H)
+    lm_head = embed if cfg.tie_embeddings else n(V, H)
+    final_norm = torch.ones(H, dtype=dtype, device=gen_dev)
+
+    class _Gen:
+        def __call__(self, i):
+            hd = cfg.head_dim
+            d = {"q": n(cfg.q_size, H), "k": n(cfg.kv_size, H), "v": n(cfg.kv_size, H), "o": n(H, cfg.q_size),
+                 "input_norm": torch.ones(H, dtype=dtype, device=gen_dev),
+                 "post_norm": torch.ones(H, dtype=dtype, device=gen_dev)}
+            if cfg.attn_bias:
+                d.update(q_bias=torch.zeros(cfg.q_size, dtype=dtype, device=gen_dev),
+                         k_bias=torch.zeros(cfg.kv_size, dtype=dtype, device=gen_dev),
+                         v_bias=torch.zeros(cfg.kv_size, dtype=dtype, device=gen_dev))
+            if cfg.qk_norm:
+                d.update(q_norm=torch.ones(hd, dtype=dtype, device=gen_dev),
+                         k_norm=torch.ones(hd, dtype=dtype, device=gen_dev))
+            if cfg.is_moe:
+                E, Ie = cfg.num_experts, cfg.moe_intermediate_size
+                d.update(router=n(E, H), exp_gate=n(E, Ie, H), exp_up=n(E, Ie, H), exp_down=n(E, H, Ie))
+            else:
+                I = cfg.intermediate_size
+                d.update(gate=n(I, H), up=n(I, H), down=n(H, I))
+            return d
+
+    return build_weights(cfg, _Gen(), embed, lm_head, final_norm, tp_rank, tp_size, ep_rank, ep_size,
+                         dtype, device)
+
+
+# ---------------------------------------------------------------- HF checkpoints
+_HF_LAYER_KEYS = {
+    "q": "self_attn.q_proj.weight", "k": "self_attn.k_proj.weight", "v": "self_attn.v_proj.weight",
+    "o": "self_attn.o_proj.weight", "q_bias": "self_attn.q_proj.bias", "k_bias": "self_attn.k_proj.bias",
+    "v_bias": "self_attn.v_proj.bias", "q_norm": "self_attn.q_norm.weight", "k_norm": "self_attn.k_norm.weight",
+    "input_norm": "input_layernorm.weight", "post_norm": "post_attention_layernorm.weight",
+    "gate": "mlp.gate_proj.weight", "up": "mlp.up_proj.weight", "down": "mlp.down_proj.weight",
+    "router": "mlp.gate.weight",
+}
+
+
+def hf_layer_dict(get, cfg: ModelConfig, i: int) -> dict:
+    """Collect layer ``i`` from an HF-named tensor getter (``get(name)`` -> tensor or None)."""
+    pre = f"model.layers.{i}."
+    d = {}
+    for k, name in _HF_LAYER_KEYS.items():
+        t = get(pre + name)
+        if t is not None:
+            d[k] = t
+    if cfg.is_moe:
+        E = cfg.num_experts
+        d["exp_gate"] = torch.stack([get(pre + f"mlp.experts.{e}.gate_proj.weight") for e in range(E)])
+        d["exp_up"] = torch.stack([get(pre + f"mlp.experts.{e}.up_proj.weight") for e in range(E)])
+        d["exp_down"] = torch.stack([get(pre + f"mlp.experts.{e}.down_proj.weight") for e in range(E)])
+    return d
+
+
+def load_hf_state_dict(cfg: ModelConfig, sd: dict, **kw) -> ModelWeights:
+    get = sd.get
+    embed = get("model.embed_tokens.weight")
+    lm = get("lm_head.weight")
+    if lm is None:
+        lm = embed
+    return build_weights(cfg, lambda i: hf_layer_dict(get, cfg, i), embed, lm, get("model.norm.weight"), **kw)
+
+
+def load_safetensors_dir(cfg: ModelConfig, path: str, **kw) -> ModelWeights:
+    """Load an HF safetensors checkpoint directory (single file or sharded index)."""
+    import glob
+    import os
+    from safetensors import safe_open
+    files = sorted(glob.glob(os.path.join(path, "*.safetensors")))
+    if not files:
+        raise FileNotFoundError(f"no .safetensors in {path}")
+    handles = [safe_open(f, framework="pt") for f in files]
+    where = {}
+    for h in handles:
+        for k in h.keys():
+            where[k] = h
+
+    def get(name):
+        h = where.get(name)
+        return h.get_tensor(name) if h is not None else None
+
+    embed = get("model.embed_tokens.weight")
+    lm = get("lm_head.weight")
+    if lm is None:
+        lm = embed
+    return build_weights(cfg, lambda i: hf_layer_dict(get, cfg, i), embed, lm, get("model.norm.weight"), **kw)
+
+
+def to_hf_state_dict(cfg: ModelConfig, w: ModelWeights) -> dict:
+    """Inverse of the loader for a TP=1 model (used by tests and the reference arm)."""
+    assert w.tp_size == 1
+    sd = {"model.embed_tokens.weight": w.embed, "model.norm.weight": w.final_norm, "lm_head.weight": w.lm_head}
+    q, kv = cfg.q_size, cfg.kv_size
+    for i, lw in enumerate(w.layers):
+        pre = f"model.layers.{i}."
+        sd[pre + _HF_LAYER_KEYS["q"]] = lw.qkv[:q]
+        sd[pre + _HF_LAYER_KEYS["k"]] = lw.qkv[q:q + kv]
+        sd[pre + _HF_LAYER_KEYS["v"]] = lw.qkv[q + kv:]
+        sd[pre + _HF_LAYER_KEYS["o"]] = lw.o
+        sd[pre + _HF_LAYER_KEYS["input_norm"]] = lw.input_norm
+        sd[pre + _HF_LAYER_KEYS["post_norm"]] = lw.post_norm
+        if lw.qkv_bias is not None:
+            sd[pre + _HF_LAYER_KEYS["q_bias"]] = lw.qkv_bias[:q]
+            sd[pre + _HF_LAYER_KEYS["k_bias"]] = lw.qkv_bias[q:q + kv]
+            sd[pre + _HF_LAYER_KEYS["v_bias"]] = lw.qkv_bias[q + kv:]
+        if lw.q_norm is not None:
+            sd[pre + _HF_LAYER_KEYS["q_norm"]] = lw.q_norm
+            sd[pre + _HF_LAYER_KEYS["k_norm"]] = lw.k_norm
+        if lw.gate_up is not None:
+            g, u = deinterleave_gate_up(lw.gate_up, cfg.intermediate_size)
+            sd[pre + _HF_LAYER_KEYS["gate"]] = g
+            sd[pre + _HF_LAYER_KEYS["up"]] = u
+            sd[pre + _HF_LAYER_KEYS["down"]] = lw.down[:, :cfg.intermediate_size]
+        if lw.router is not None:
+            from b200serve.models.moe import expert_hf_tensors
+            sd[pre + _HF_LAYER_KEYS["router"]] = lw.router
+            sd.update(expert_hf_tensors(cfg, lw, pre))
+    return sd

@@ -1,0 +1,332 @@
+"""Operator facade over the sm_100a extension.
+
+Every op has two implementations:
+* the CUDA kernel in ``csrc/`` (used for every CUDA tensor);
+* a plain PyTorch version used for CPU tensors (CPU tests, oracles).
+A CUDA tensor never silently takes the PyTorch path: if the extension cannot
+be loaded on a machine with a GPU, the first op raises.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import threading
+
+import torch
+
+_ext = None
+_ext_error = None
+_lock = threading.Lock()
+
+EPI_BF16, EPI_F32, EPI_SWIGLU = 0, 1, 2
+
+
+def _load():
+    global _ext, _ext_error
+    if _ext is not None or _ext_error is not None:
+        return _ext
+    with _lock:
+        if _ext is None and _ext_error is None:
+            try:
+                from b200serve.ops.build import build, built_library_path, EXT_NAME
+                path = built_library_path()
+                if os.path.exists(path) and not os.environ.get("B200_JIT"):
+                    # import the in-tree build as is (no ninja staleness check on a copied tree)
+                    import importlib.machinery
+                    import importlib.util
+                    loader = importlib.machinery.ExtensionFileLoader(EXT_NAME, path)
+                    spec = importlib.util.spec_from_file_location(EXT_NAME, path, loader=loader)
+                    mod = importlib.util.module_from_spec(spec)
+                    loader.exec_module(mod)
+                    _ext = mod
+                else:
+                    _ext = build(verbose=bool(os.environ.get("B200_BUILD_VERBOSE")))
+            except Exception as e:  # recorded and re-raised at first CUDA use
+                _ext_error = e
+    return _ext
+
+
+def ext():
+    """The compiled extension; raises if it cannot be built or loaded."""
+    m = _load()
+    if m is None:
+        raise RuntimeError(f"b200serve CUDA extension unavailable: {_ext_error}")
+    return m
+
+
+def extension_loaded() -> bool:
+    return _ext is not None
+
+
+def extension_path() -> str:
+    from b200serve.ops.build import built_library_path
+    return built_library_path()
+
+
+def _cuda(t: torch.Tensor) -> bool:
+    return t.is_cuda
+
+
+# ------------------------------------------------------------------ RMSNorm
+def rmsnorm(parts, weight, eps, residual=None, residual_out=None, out=None):
+    """out = RMSNorm(sum(parts) + residual) * weight; residual_out = the pre-norm sum.
+
+    ``parts`` is a tensor or a list of up to 8 tensors (e.g. tensor-parallel partials).
+    """
+    if isinstance(parts, torch.Tensor):
+        parts = [parts]
+    x0 = parts[0]
+    if _cuda(x0):
+        out = out if out is not None else torch.empty_like(x0)
+        ext().rmsnorm_fused(list(parts), residual, residual_out, weight, out, float(eps))
+        return out
+    s = sum(p.float() for p in parts)
+    if residual is not None:
+        s = s + residual.float()
+    s = s.to(x0.dtype)
+    if residual_out is not None:
+        residual_out.copy_(s)
+    sf = s.float()
+    n = (sf * torch.rsqrt(sf.pow(2).mean(-1, keepdim=True) + eps)).to(x0.dtype)
+    r = weight * n
+    if out is not None:
+        out.copy_(r)
+        return out
+    return r
+
+
+# ------------------------------------------------------------------ RoPE table
+def rope_cos_sin(head_dim: int, max_pos: int, theta: float, device) -> torch.Tensor:
+    """[max_pos, head_dim] fp32: cos of the head_dim/2 frequencies, then their sin."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))
+    pos = torch.arange(max_pos, dtype=torch.int64).float()
+    f = torch.outer(pos, inv)
+    return torch.cat([f.cos(), f.sin()], dim=-1).to(device)
+
+
+# ------------------------------------------------------------------ QKV post
+def qkv_post(qkv, bias, q_norm, k_norm, cos_sin, positions, slots, k_cache, v_cache, nq, nkv, eps,
+             q_out=None):
+    """Split the fused QKV projection, add bias, per-head q/k RMSNorm, RoPE, and
+    write K/V rows into the paged cache at ``slots`` (block*16 + offset; -1 = skip).
+    Returns q [T, nq, hd]. Caches are [num_blocks, nkv, 16, hd]."""
+    T = qkv.shape[0]
+    hd = cos_sin.shape[1]
+    if _cuda(qkv):
+        q_out = q_out if q_out is not None else torch.empty(T, nq, hd, dtype=qkv.dtype, device=qkv.device)
+        ext().qkv_post(qkv, bias, q_norm, k_norm, cos_sin, positions, slots, q_out, k_cache, v_cache,
+                       nq, nkv, float(eps))
+        return q_out
+    x = qkv.float()
+    if bias is not None:
+        x = (x + bias.float()).to(qkv.dtype).float()
+    q = x[:, : nq * hd].view(T, nq, hd)
+    k = x[:, nq * hd:(nq + nkv) * hd].view(T, nkv, hd)
+    v = x[:, (nq + nkv) * hd:].view(T, nkv, hd)
+
+    def norm(t, w):
+        n = (t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + eps)).to(qkv.dtype)
+        return (w * n).float()
+
+    if q_norm is not None:
+        q, k = norm(q, q_norm), norm(k, k_norm)
+    cs = cos_sin[positions.long()]
+    c = torch.cat([cs[:, : hd // 2]] * 2, -1)[:, None, :]
+    s = torch.cat([cs[:, hd // 2:]] * 2, -1)[:, None, :]
+
+    def rot(t):
+        t1, t2 = t[..., : hd // 2], t[..., hd // 2:]
+        return t * c + torch.cat([-t2, t1], -1) * s
+
+    q, k = rot(q), rot(k)
+    sl = slots.long()
+    ok = sl >= 0
+    blk, off = sl[ok] // 16, sl[ok] % 16
+    k_cache[blk, :, off] = k[ok].to(k_cache.dtype)
+    v_cache[blk, :, off] = v[ok].to(v_cache.dtype)
+    r = q.to(qkv.dtype)
+    if q_out is not None:
+        q_out.copy_(r)
+        return q_out
+    return r
+
+
+# ------------------------------------------------------------------ SwiGLU
+def silu_mul(gu, out=None):
+    """act = silu(gate) * up on the 64-column interleaved [g|u] layout."""
+    I = gu.shape[-1] // 2
+    if _cuda(gu):
+        out = out if out is not None else torch.empty(*gu.shape[:-1], I, dtype=gu.dtype, device=gu.device)
+        ext().silu_mul(gu, out)
+        return out
+    v = gu.view(*gu.shape[:-1], I // 64, 2, 64)
+    g, u = v[..., 0, :].reshape(*gu.shape[:-1], I), v[..., 1, :].reshape(*gu.shape[:-1], I)
+    r = (torch.nn.functional.silu(g.float()).to(gu.dtype) * u)
+    if out is not None:
+        out.copy_(r)
+        return out
+    return r
+
+
+def embedding(ids, table, out=None):
+    if _cuda(table):
+        out = out if out is not None else torch.empty(ids.numel(), table.shape[1], dtype=table.dtype,
+                                                      device=table.device)
+        ext().embedding(ids, table, out)
+        return out
+    r = table[ids.long().clamp(0, table.shape[0] - 1)]
+    if out is not None:
+        out.copy_(r)
+        return out
+    return r
+
+
+# ------------------------------------------------------------------ GEMM
+class GemmWorkspace:
+    """fp32 split-K workspace and per-tile counters shared by the GEMMs of one stream.
+
+    Counters must be zero before a launch; every kernel leaves them at zero.
+    """
+
+    def __init__(self, device, max_elems: int = 32 << 20, max_tiles: int = 1 << 16):
+        self.ws = torch.empty(max_elems, dtype=torch.float32, device=device)
+        self.counters = torch.zeros(max_tiles, dtype=torch.int32, device=device)
+
+
+_workspaces = {}
+
+
+def default_workspace(device) -> GemmWorkspace:
+    key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+    if key not in _workspaces:
+        _workspaces[key] = GemmWorkspace(device)
+    return _workspaces[key]
+
+
+def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspace=None, splits=0):
+    """y = x @ w^T (+bias) (+residual) with x [M, K], w [N, K].
+
+    epilogue EPI_F32 writes fp32 (logits); EPI_SWIGLU treats w as the 64-row
+    interleaved gate/up weight and writes silu(gate)*up of width N/2.
+    """
+    M, K = x.shape
+    N = w.shape[0]
+    if _cuda(x):
+        if out is None:
+            if epilogue == EPI_SWIGLU:
+                out = torch.empty(M, N // 2, dtype=x.dtype, device=x.device)
+            else:
+                out = torch.empty(M, N, dtype=torch.float32 if epilogue == EPI_F32 else x.dtype,
+                                  device=x.device)
+        ws = workspace or default_workspace(x.device)
+        ext().gemm_tc(x, w, out, bias, residual, ws.ws, ws.counters, epilogue, splits)
+        return out
+    y = x.float() @ w.float().t()
+    if bias is not None:
+        y = y + bias.float()
+    if epilogue == EPI_F32:
+        r = y
+    elif epilogue == EPI_SWIGLU:
+        r = silu_mul(y.to(x.dtype))
+    else:
+        r = y.to(x.dtype)
+        if residual is not None:
+            r = (r.float() + residual.float()).to(x.dtype)
+    if out is not None:
+        out.copy_(r)
+        return out
+    return r
+
+
+# ------------------------------------------------------------------ attention
+class AttnWorkspace:
+    def __init__(self, device, max_batch, nkv, group, head_dim, max_splits):
+        n = max_batch * nkv * max_splits * group
+        self.acc = torch.empty(n * head_dim, dtype=torch.float32, device=device)
+        self.ml = torch.empty(n * 2, dtype=torch.float32, device=device)
+        self.max_splits = max_splits
+
+
+def paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, scale, tps=256, nsplit=1,
+                           workspace=None, out=None):
+    """One query token per sequence. q [B, nq, hd]; seq_lens include the new token."""
+    if _cuda(q):
+        out = out if out is not None else torch.empty_like(q)
+        if nsplit > 1:
+            assert workspace is not None and workspace.max_splits >= nsplit
+            acc, ml = workspace.acc, workspace.ml
+        else:
+            acc = ml = torch.empty(0, dtype=torch.float32, device=q.device)
+        ext().paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, out, acc, ml,
+                                     float(scale), int(tps), int(nsplit))
+        return out
+    B, nq, hd = q.shape
+    nkv = k_cache.shape[1]
+    res = torch.zeros_like(q)
+    for b in range(B):
+        L = int(seq_lens[b])
+        if L == 0:
+            continue
+        nb = (L + 15) // 16
+        blocks = block_tables[b, :nb].long()
+        k = k_cache[blocks].permute(1, 0, 2, 3).reshape(nkv, nb * 16, hd)[:, :L].float()
+        v = v_cache[blocks].permute(1, 0, 2, 3).reshape(nkv, nb * 16, hd)[:, :L].float()
+        qq = q[b].float().view(nkv, nq // nkv, hd)
+        s = torch.einsum("kgd,ktd->kgt", qq, k) * scale
+        p = torch.softmax(s, -1)
+        res[b] = torch.einsum("kgt,ktd->kgd", p, v).reshape(nq, hd).to(q.dtype)
+    if out is not None:
+        out.copy_(res)
+        return out
+    return res
+
+
+def paged_prefill_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, cu_q, scale, out=None,
+                            max_q=None):
+    """Causal attention for chunks of new tokens against the paged cache.
+
+    q [T, nq, hd] holds the new tokens of all sequences back to back; sequence i
+    owns rows cu_q[i]:cu_q[i+1], whose absolute positions start at q_start[i];
+    seq_lens[i] = q_start[i] + its new-token count (its K/V are already written).
+    """
+    if _cuda(q):
+        out = out if out is not None else torch.empty_like(q)
+        ext().paged_prefill_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, cu_q, out,
+                                      float(scale), int(max_q if max_q is not None else q.shape[0]))
+        return out
+    T, nq, hd = q.shape
+    nkv = k_cache.shape[1]
+    res = torch.zeros_like(q)
+    for i in range(len(seq_lens)):
+        a, b_ = int(cu_q[i]), int(cu_q[i + 1])
+        if b_ == a:
+            continue
+        L = int(seq_lens[i])
+        s0 = int(q_start[i])
+        nb = (L + 15) // 16
+        blocks = block_tables[i, :nb].long()
+        k = k_cache[blocks].permute(1, 0, 2, 3).reshape(nkv, nb * 16, hd)[:, :L].float()
+        v = v_cache[blocks].permute(1, 0, 2, 3).reshape(nkv, nb * 16, hd)[:, :L].float()
+        g = nq // nkv
+        k = k.repeat_interleave(g, 0)
+        v = v.repeat_interleave(g, 0)
+        qq = q[a:b_].float().permute(1, 0, 2)  # [nq, n, hd]
+        s = torch.einsum("hnd,htd->hnt", qq, k) * scale
+        pos = torch.arange(s0, s0 + (b_ - a))[:, None]
+        mask = torch.arange(L)[None, :] > pos
+        s = s.masked_fill(mask[None], float("-inf"))
+        p = torch.softmax(s, -1)
+        res[a:b_] = torch.einsum("hnt,htd->hnd", p, v).permute(1, 0, 2).to(q.dtype)
+    if out is not None:
+        out.copy_(res)
+        return out
+    return res
+
+
+def gemm_error_flag(reset: bool = True) -> int:
+    return int(ext().gemm_error_flag(reset)) if extension_loaded() else 0
+
+
+def softmax_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

@@ -1,0 +1,249 @@
+// Paged GQA decode attention (split-KV flash-decoding) over 16-token KV pages.
+//
+// Restates the math of the reference's fused attention kernel
+// (webgpu/src/shaders/attention.wgsl:63: QK^T, causal softmax, .V) for one new
+// query token per sequence, reading K/V through a block table instead of a
+// contiguous per-session buffer (forward-pass.ts:322-342 in the reference).
+//
+// Grid (nsplit, nkv, B); 4 warps per CTA. A CTA owns tokens
+// [split*tps, min(len, (split+1)*tps)) of one (sequence, kv head) and all G
+// query heads that share the kv head. Each warp streams whole 16-token pages:
+//   QK: lane l takes token l&15 and half (l>>4) of the head dims, so every
+//       16-byte load instruction of the warp covers 32 contiguous bytes of
+//       each of the 16 key rows (full 32-byte sectors);
+//   PV: lane l takes dims [l*E, l*E+E) of every value row (contiguous rows).
+// Partial (m, l, acc) per CTA go to a workspace; a second kernel merges splits.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include "common.cuh"
+
+namespace b200 {
+
+constexpr int kPage = 16;
+constexpr int kAttnWarps = 4;
+
+template <int HD, int G>
+__global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_cache,
+    const __nv_bfloat16* __restrict__ v_cache, const int* __restrict__ block_tables,
+    const int* __restrict__ seq_lens, int max_blocks, int nkv, float scale_log2, int tps,
+    float* __restrict__ part_acc, float* __restrict__ part_ml, __nv_bfloat16* __restrict__ out, int nsplit) {
+  constexpr int E = HD / 32;          // value dims per lane
+  constexpr int NCH = HD / 8;         // 16-byte chunks per key row
+  __shared__ float q_s[G][HD];
+  __shared__ __align__(16) float p_s[kAttnWarps][kPage][G < 4 ? 4 : G];
+  __shared__ float m_s[kAttnWarps][G], l_s[kAttnWarps][G];
+  __shared__ float acc_s[kAttnWarps][G][HD];
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int len = seq_lens[b];
+  const int nq = nkv * G;
+  const int start = split * tps;
+  const int stop = min(len, start + tps);
+
+  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+    const int g = i / HD, d = i % HD;
+    q_s[g][d] = __bfloat162float(q[((size_t)b * nq + kvh * G + g) * HD + d]) * scale_log2;
+  }
+  __syncthreads();
+
+  float m[G], l[G], acc[G][E];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[g][e] = 0.f;
+  }
+
+  const int tok = lane & 15, half = lane >> 4;
+  const int* bt = block_tables + (size_t)b * max_blocks;
+  for (int page_start = start + warp * kPage; page_start < stop; page_start += kAttnWarps * kPage) {
+    const int phys = bt[page_start / kPage];
+    const size_t page_off = ((size_t)phys * nkv + kvh) * kPage * HD;
+    // ---- scores for 16 tokens ----
+    const __nv_bfloat16* krow = k_cache + page_off + (size_t)tok * HD;
+    float s[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) s[g] = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH / 2; ++c) {
+      const int chunk = c * 2 + half;
+      bf16x8 kv = *reinterpret_cast<const bf16x8*>(krow + chunk * 8);
+      float kf[8];
+      unpack8(kv, kf);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s[g] = fmaf(q_s[g][chunk * 8 + j], kf[j], s[g]);
+      }
+    }
+    const bool valid = page_start + tok < stop;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      s[g] += __shfl_xor_sync(0xffffffffu, s[g], 16);
+      if (!valid) s[g] = -INFINITY;
+    }
+    // ---- online softmax over the page ----
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float bm = s[g];
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+      const float m_new = fmaxf(m[g], bm);
+      const float p = exp2f(s[g] - m_new);
+      float ps = p;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      const float alpha = exp2f(m[g] - m_new);
+      l[g] = l[g] * alpha + ps;
+      m[g] = m_new;
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[g][e] *= alpha;
+      if (half == 0) p_s[warp][tok][g] = p;
+    }
+    __syncwarp();
+    // ---- acc += p . V ----
+    const __nv_bfloat16* vpage = v_cache + page_off + lane * E;
+#pragma unroll 4
+    for (int t = 0; t < kPage; ++t) {
+      float vf[E];
+      if constexpr (E == 4) {
+        uint2 raw = *reinterpret_cast<const uint2*>(vpage + (size_t)t * HD);
+        vf[0] = bf16_lo(raw.x); vf[1] = bf16_hi(raw.x); vf[2] = bf16_lo(raw.y); vf[3] = bf16_hi(raw.y);
+      } else {
+        uint32_t raw = *reinterpret_cast<const uint32_t*>(vpage + (size_t)t * HD);
+        vf[0] = bf16_lo(raw); vf[1] = bf16_hi(raw);
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float p = p_s[warp][t][g];
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[g][e] = fmaf(p, vf[e], acc[g][e]);
+      }
+    }
+    __syncwarp();
+  }
+
+  // ---- merge the 4 warps ----
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) { m_s[warp][g] = m[g]; l_s[warp][g] = l[g]; }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc_s[warp][g][lane * E + e] = acc[g][e];
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+    const int g = i / HD, d = i % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, m_s[w][g]);
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float f = exp2f(m_s[w][g] - M);
+        L += l_s[w][g] * f;
+        A += acc_s[w][g][d] * f;
+      }
+    }
+    if (nsplit == 1) {
+      out[((size_t)b * nq + kvh * G + g) * HD + d] = __float2bfloat16_rn(L > 0.f ? A / L : 0.f);
+    } else {
+      const size_t slot = (((size_t)b * nkv + kvh) * nsplit + split) * G + g;
+      part_acc[slot * HD + d] = A;
+      if (d == 0) { part_ml[slot * 2] = M; part_ml[slot * 2 + 1] = L; }
+    }
+  }
+}
+
+// out[b, h] = sum_s w_s acc_s / sum_s w_s l_s with w_s = 2^(m_s - max m). One warp per (b, q head).
+template <int HD>
+__global__ void paged_decode_combine_kernel(const float* __restrict__ part_acc, const float* __restrict__ part_ml,
+                                            const int* __restrict__ seq_lens, __nv_bfloat16* __restrict__ out,
+                                            int B, int nkv, int G, int nsplit, int tps) {
+  constexpr int E = HD / 32;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nq = nkv * G;
+  if (warp >= B * nq) return;
+  const int b = warp / nq, h = warp % nq, kvh = h / G, g = h % G;
+  const int used = min(nsplit, (seq_lens[b] + tps - 1) / tps);
+  float M = -INFINITY;
+  for (int s = 0; s < used; ++s) M = fmaxf(M, part_ml[((((size_t)b * nkv + kvh) * nsplit + s) * G + g) * 2]);
+  float L = 0.f, A[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) A[e] = 0.f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < used; ++s) {
+      const size_t slot = (((size_t)b * nkv + kvh) * nsplit + s) * G + g;
+      const float f = exp2f(part_ml[slot * 2] - M);
+      L += part_ml[slot * 2 + 1] * f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) A[e] += part_acc[slot * HD + lane * E + e] * f;
+    }
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) out[((size_t)b * nq + h) * HD + lane * E + e] = __float2bfloat16_rn(A[e] * inv);
+}
+
+}  // namespace b200
+
+using namespace b200;
+
+// q [B, nq, HD]; caches [nblocks, nkv, 16, HD]; block_tables [B, max_blocks] int32; seq_lens [B] int32
+// (length including the current token). workspace: part_acc [B*nkv*nsplit*G*HD], part_ml [B*nkv*nsplit*G*2].
+void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                            torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
+                            torch::Tensor part_acc, torch::Tensor part_ml, double scale, int64_t tps,
+                            int64_t nsplit) {
+  const int B = q.size(0), nq = q.size(1), HD = q.size(2);
+  const int nkv = k_cache.size(1);
+  const int G = nq / nkv;
+  TORCH_CHECK(k_cache.size(2) == kPage && tps % kPage == 0 && nsplit >= 1);
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt);
+  if (nsplit > 1) {
+    TORCH_CHECK(part_acc.numel() >= (int64_t)B * nkv * nsplit * G * HD, "attention workspace too small");
+    TORCH_CHECK(part_ml.numel() >= (int64_t)B * nkv * nsplit * G * 2, "attention workspace too small");
+  }
+  if (B == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const float sl2 = (float)(scale * 1.4426950408889634);
+  dim3 grid(nsplit, nkv, B);
+  auto qp = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  auto kp = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
+  auto vp = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
+  auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  float* pa = nsplit > 1 ? part_acc.data_ptr<float>() : nullptr;
+  float* pm = nsplit > 1 ? part_ml.data_ptr<float>() : nullptr;
+#define B200_DEC(HDV, GV)                                                                                    \
+  paged_decode_kernel<HDV, GV><<<grid, kAttnWarps * 32, 0, stream>>>(qp, kp, vp, block_tables.data_ptr<int>(), \
+                                                                    seq_lens.data_ptr<int>(),                 \
+                                                                    block_tables.size(1), nkv, sl2, tps, pa, pm, op, nsplit)
+  if (HD == 128 && G == 4) B200_DEC(128, 4);
+  else if (HD == 128 && G == 8) B200_DEC(128, 8);
+  else if (HD == 128 && G == 2) B200_DEC(128, 2);
+  else if (HD == 128 && G == 1) B200_DEC(128, 1);
+  else if (HD == 64 && G == 2) B200_DEC(64, 2);
+  else if (HD == 64 && G == 1) B200_DEC(64, 1);
+  else if (HD == 64 && G == 4) B200_DEC(64, 4);
+  else TORCH_CHECK(false, "unsupported head_dim/group ", HD, "/", G);
+#undef B200_DEC
+  B200_CHECK_CUDA(cudaGetLastError());
+  if (nsplit > 1) {
+    const int warps = B * nq;
+    const int threads = 128;
+    const int blocks = (warps * 32 + threads - 1) / threads;
+    if (HD == 128)
+      paged_decode_combine_kernel<128><<<blocks, threads, 0, stream>>>(pa, pm, seq_lens.data_ptr<int>(), op, B, nkv,
+                                                                       G, nsplit, tps);
+    else
+      paged_decode_combine_kernel<64><<<blocks, threads, 0, stream>>>(pa, pm, seq_lens.data_ptr<int>(), op, B, nkv, G,
+                                                                      nsplit, tps);
+    B200_CHECK_CUDA(cudaGetLastError());
+  }
+}

@@ -1,0 +1,36 @@
+// Python bindings of the b200serve CUDA extension.
+#include <torch/extension.h>
+
+void rmsnorm_fused(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
+                   c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps);
+void qkv_post(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
+              c10::optional<torch::Tensor> kn_w, torch::Tensor cos_sin, torch::Tensor positions,
+              torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache, int64_t nq,
+              int64_t nkv, double eps);
+void silu_mul(torch::Tensor gu, torch::Tensor act);
+void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
+void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                            torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
+                            torch::Tensor part_acc, torch::Tensor part_ml, double scale, int64_t tps,
+                            int64_t nsplit);
+void paged_prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                             torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor q_start,
+                             torch::Tensor cu_q, torch::Tensor out, double scale, int64_t max_q);
+std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi, int64_t num_sms);
+void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> bias,
+             c10::optional<torch::Tensor> residual, torch::Tensor ws, torch::Tensor counters, int64_t epi,
+             int64_t force_splits);
+int64_t gemm_error_flag(bool reset);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "b200serve sm_100a kernels";
+  m.def("rmsnorm_fused", &rmsnorm_fused);
+  m.def("qkv_post", &qkv_post);
+  m.def("silu_mul", &silu_mul);
+  m.def("embedding", &embedding);
+  m.def("paged_decode_attention", &paged_decode_attention);
+  m.def("paged_prefill_attention", &paged_prefill_attention);
+  m.def("gemm_plan", &gemm_plan);
+  m.def("gemm_tc", &gemm_tc);
+  m.def("gemm_error_flag", &gemm_error_flag);
+}

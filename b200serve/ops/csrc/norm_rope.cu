@@ -1,0 +1,256 @@
+// Row-wise kernels of the decoder: fused (partials + residual) RMSNorm, the QKV
+// post-processing step (bias, per-head q/k RMSNorm, rotate-half RoPE, paged KV
+// write), SwiGLU on the tile-interleaved gate/up layout, and the embedding gather.
+//
+// Reference kernels restated here: rmsnorm.wgsl:20 (RMSNorm), rope.wgsl:29
+// (rotate-half RoPE), elementwise.wgsl:96 (gate_silu), embed.wgsl:26 (embed).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include "common.cuh"
+
+namespace b200 {
+
+struct PartPtrs {
+  const __nv_bfloat16* p[8];
+};
+
+// y = rmsnorm(sum(parts) [+ residual_in]) * w ; residual_out = the pre-norm sum.
+// One CTA per row, 8 bf16 per thread per step, at most 4 steps (H <= 32768 with 1024 threads).
+template <int VPT>
+__global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
+    PartPtrs parts, int nparts, const __nv_bfloat16* residual_in, __nv_bfloat16* residual_out,
+    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H, float eps) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const size_t base = (size_t)row * H;
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int s = 0; s < VPT; ++s) {
+    const int col = (threadIdx.x + s * blockDim.x) * 8;
+    if (col < H) {
+      float acc[8];
+      bf16x8 a = *reinterpret_cast<const bf16x8*>(parts.p[0] + base + col);
+      unpack8(a, acc);
+      for (int k = 1; k < nparts; ++k) {
+        float t[8];
+        unpack8(*reinterpret_cast<const bf16x8*>(parts.p[k] + base + col), t);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] += t[i];
+      }
+      if (residual_in) {
+        float r[8];
+        unpack8(*reinterpret_cast<const bf16x8*>(residual_in + base + col), r);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] += r[i];
+      }
+      // the residual stream is stored in bf16; normalise the rounded value
+      bf16x8 rounded = pack8(acc);
+      unpack8(rounded, v[s]);
+      if (residual_out) *reinterpret_cast<bf16x8*>(residual_out + base + col) = rounded;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += v[s][i] * v[s][i];
+    }
+  }
+  const float inv = rsqrtf(block_sum(ss, red) / (float)H + eps);
+#pragma unroll
+  for (int s = 0; s < VPT; ++s) {
+    const int col = (threadIdx.x + s * blockDim.x) * 8;
+    if (col < H) {
+      float wf[8], o[8];
+      unpack8(*reinterpret_cast<const bf16x8*>(w + col), wf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        // round the normalised value to bf16 before the weight multiply
+        const float n = __bfloat162float(__float2bfloat16_rn(v[s][i] * inv));
+        o[i] = n * wf[i];
+      }
+      *reinterpret_cast<bf16x8*>(out + base + col) = pack8(o);
+    }
+  }
+}
+
+// QKV post-processing. One warp per (token, head slot); head slots are
+// [0, nq) query heads, [nq, nq+nkv) key heads, [nq+nkv, nq+2nkv) value heads.
+// E = HD/32 elements per lane; the rotate-half partner of lane l is lane l^16.
+template <int HD>
+__global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ bias,
+                                const __nv_bfloat16* __restrict__ qn_w, const __nv_bfloat16* __restrict__ kn_w,
+                                const float* __restrict__ cos_sin, const int* __restrict__ positions,
+                                const int* __restrict__ slots, __nv_bfloat16* __restrict__ q_out,
+                                __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache, int T,
+                                int nq, int nkv, float eps) {
+  constexpr int E = HD / 32;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nslots = nq + 2 * nkv;
+  if (warp >= T * nslots) return;
+  const int t = warp / nslots, h = warp % nslots;
+  const int width = nslots * HD;
+  const __nv_bfloat16* src = qkv + (size_t)t * width + h * HD + lane * E;
+  float x[E];
+#pragma unroll
+  for (int i = 0; i < E; ++i) {
+    x[i] = __bfloat162float(src[i]);
+    if (bias) x[i] = __bfloat162float(__float2bfloat16_rn(x[i] + __bfloat162float(bias[h * HD + lane * E + i])));
+  }
+  const bool is_q = h < nq, is_k = !is_q && h < nq + nkv;
+  if (is_q || is_k) {
+    const __nv_bfloat16* nw = is_q ? qn_w : kn_w;
+    if (nw) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < E; ++i) ss += x[i] * x[i];
+      const float inv = rsqrtf(warp_sum(ss) / (float)HD + eps);
+#pragma unroll
+      for (int i = 0; i < E; ++i)
+        x[i] = __bfloat162float(__float2bfloat16_rn(x[i] * inv)) * __bfloat162float(nw[lane * E + i]);
+#pragma unroll
+      for (int i = 0; i < E; ++i) x[i] = __bfloat162float(__float2bfloat16_rn(x[i]));
+    }
+    const int pos = positions[t];
+    const float* cs = cos_sin + (size_t)pos * HD;  // [cos(HD/2) | sin(HD/2)]
+    float y[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      const float partner = __shfl_xor_sync(0xffffffffu, x[i], 16);
+      const int d = lane * E + i;
+      const int f = d & (HD / 2 - 1);
+      const float c = cs[f], s = cs[HD / 2 + f];
+      y[i] = lane < 16 ? x[i] * c - partner * s : x[i] * c + partner * s;
+    }
+#pragma unroll
+    for (int i = 0; i < E; ++i) x[i] = y[i];
+  }
+  if (is_q) {
+    __nv_bfloat16* dst = q_out + ((size_t)t * nq + h) * HD + lane * E;
+#pragma unroll
+    for (int i = 0; i < E; ++i) dst[i] = __float2bfloat16_rn(x[i]);
+  } else {
+    const int slot = slots[t];
+    if (slot < 0) return;
+    const int kvh = is_k ? h - nq : h - nq - nkv;
+    const size_t off = (((size_t)(slot >> 4) * nkv + kvh) * 16 + (slot & 15)) * HD + lane * E;
+    __nv_bfloat16* dst = (is_k ? k_cache : v_cache) + off;
+#pragma unroll
+    for (int i = 0; i < E; ++i) dst[i] = __float2bfloat16_rn(x[i]);
+  }
+}
+
+// act[t, j] = silu(g) * u where the gate/up GEMM output interleaves 64-wide
+// column blocks: [g(0..63) u(0..63) g(64..127) u(64..127) ...].
+__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ act, int T,
+                                int I) {
+  const size_t n8 = (size_t)T * I / 8;
+  for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < n8; v += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = v * 8;
+    const size_t t = e / I;
+    const int j = (int)(e % I);
+    const int blk = j >> 6, within = j & 63;
+    const __nv_bfloat16* row = gu + t * 2 * (size_t)I;
+    float g[8], u[8], o[8];
+    unpack8(*reinterpret_cast<const bf16x8*>(row + blk * 128 + within), g);
+    unpack8(*reinterpret_cast<const bf16x8*>(row + blk * 128 + 64 + within), u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float gg = __bfloat162float(__float2bfloat16_rn(g[i] / (1.f + __expf(-g[i]))));
+      o[i] = gg * u[i];
+    }
+    *reinterpret_cast<bf16x8*>(act + e) = pack8(o);
+  }
+}
+
+__global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
+                                 __nv_bfloat16* __restrict__ out, int H, int vocab) {
+  const int t = blockIdx.x;
+  int id = ids[t];
+  id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
+  const bf16x8* src = reinterpret_cast<const bf16x8*>(table + (size_t)id * H);
+  bf16x8* dst = reinterpret_cast<bf16x8*>(out + (size_t)t * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+}  // namespace b200
+
+using namespace b200;
+
+void rmsnorm_fused(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
+                   c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps) {
+  TORCH_CHECK(!parts.empty() && parts.size() <= 8, "1..8 partial inputs");
+  const int H = parts[0].size(-1);
+  const int T = parts[0].numel() / H;
+  TORCH_CHECK(H % 8 == 0, "hidden size must be a multiple of 8");
+  PartPtrs pp{};
+  for (size_t i = 0; i < parts.size(); ++i) {
+    TORCH_CHECK(parts[i].is_contiguous() && parts[i].scalar_type() == at::kBFloat16);
+    pp.p[i] = reinterpret_cast<const __nv_bfloat16*>(parts[i].data_ptr());
+  }
+  if (T == 0) return;
+  int threads = std::min(1024, ((H / 8 + 31) / 32) * 32);
+  const int vpt = (H / 8 + threads - 1) / threads;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto rin = residual_in ? reinterpret_cast<const __nv_bfloat16*>(residual_in->data_ptr()) : nullptr;
+  auto rout = residual_out ? reinterpret_cast<__nv_bfloat16*>(residual_out->data_ptr()) : nullptr;
+  auto wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  switch (vpt) {
+    case 1: rmsnorm_fused_kernel<1><<<T, threads, 0, stream>>>(pp, parts.size(), rin, rout, wp, op, H, eps); break;
+    case 2: rmsnorm_fused_kernel<2><<<T, threads, 0, stream>>>(pp, parts.size(), rin, rout, wp, op, H, eps); break;
+    case 3:
+    case 4: rmsnorm_fused_kernel<4><<<T, threads, 0, stream>>>(pp, parts.size(), rin, rout, wp, op, H, eps); break;
+    default: TORCH_CHECK(false, "hidden size too large");
+  }
+  B200_CHECK_CUDA(cudaGetLastError());
+}
+
+void qkv_post(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
+              c10::optional<torch::Tensor> kn_w, torch::Tensor cos_sin, torch::Tensor positions,
+              torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache, int64_t nq,
+              int64_t nkv, double eps) {
+  const int T = qkv.size(0);
+  const int HD = cos_sin.size(1);
+  TORCH_CHECK(qkv.size(1) == (nq + 2 * nkv) * HD, "qkv width mismatch");
+  TORCH_CHECK(positions.scalar_type() == at::kInt && slots.scalar_type() == at::kInt);
+  if (T == 0) return;
+  const int warps = T * (nq + 2 * nkv);
+  const int threads = 256;
+  const int blocks = (warps * 32 + threads - 1) / threads;
+  auto stream = at::cuda::getCurrentCUDAStream();
+#define B200_QKV(HDV)                                                                                       \
+  qkv_post_kernel<HDV><<<blocks, threads, 0, stream>>>(                                                     \
+      reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),                                               \
+      bias ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr,                            \
+      qn_w ? reinterpret_cast<const __nv_bfloat16*>(qn_w->data_ptr()) : nullptr,                            \
+      kn_w ? reinterpret_cast<const __nv_bfloat16*>(kn_w->data_ptr()) : nullptr, cos_sin.data_ptr<float>(), \
+      positions.data_ptr<int>(), slots.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), \
+      reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()), reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), T, \
+      nq, nkv, eps)
+  if (HD == 128) B200_QKV(128);
+  else if (HD == 64) B200_QKV(64);
+  else TORCH_CHECK(false, "head_dim must be 64 or 128");
+#undef B200_QKV
+  B200_CHECK_CUDA(cudaGetLastError());
+}
+
+void silu_mul(torch::Tensor gu, torch::Tensor act) {
+  const int I = act.size(-1);
+  const int T = act.numel() / I;
+  TORCH_CHECK(I % 64 == 0 && gu.size(-1) == 2 * I);
+  if (T == 0) return;
+  const size_t n8 = (size_t)T * I / 8;
+  const int threads = 256;
+  const int blocks = (int)std::min<size_t>((n8 + threads - 1) / threads, 148 * 16);
+  silu_mul_kernel<<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), reinterpret_cast<__nv_bfloat16*>(act.data_ptr()), T, I);
+  B200_CHECK_CUDA(cudaGetLastError());
+}
+
+void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out) {
+  const int T = ids.numel();
+  const int H = table.size(1);
+  if (T == 0) return;
+  embedding_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ids.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), H, table.size(0));
+  B200_CHECK_CUDA(cudaGetLastError());
+}

@@ -1,0 +1,95 @@
+"""Kernel micro-benchmarks (device-timed, L2 flushed) with roofline fractions.
+
+python -m b200serve.utils.kbench [gemm|attn|all]
+Prints one JSON line per case: achieved GB/s or TFLOP/s and the fraction of
+the measured peaks in MEASURED_PEAKS.json (HBM copy bandwidth, cuBLAS bf16).
+"""
+
+from __future__ import annotations
+
+import json
+import math
+import os
+import sys
+
+import torch
+
+from b200serve import ops
+from b200serve.utils.timing import time_cuda
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as fh:
+            d = json.load(fh)
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def bench_gemm(cases=None):
+    hbm, tf, src = peaks()
+    cases = cases or [
+        # (name, M, N, K) -- Qwen3-8B decode (M = batch) and prefill shapes, TP=1
+        ("qkv_b32", 32, 6144, 4096), ("o_b32", 32, 4096, 4096), ("gate_up_b32", 32, 24576, 4096),
+        ("down_b32", 32, 4096, 12288), ("lm_head_b32", 32, 151936, 4096), ("qkv_b1", 1, 6144, 4096),
+        ("gate_up_b1", 1, 24576, 4096), ("prefill_qkv_4k", 4096, 6144, 4096),
+        ("prefill_gate_up_4k", 4096, 24576, 4096), ("prefill_down_8k", 8192, 4096, 12288),
+    ]
+    out = []
+    for name, M, N, K in cases:
+        x = torch.randn(M, K, device="cuda").bfloat16()
+        w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+        epi = ops.EPI_F32 if "lm_head" in name else ops.EPI_BF16
+        y = ops.linear(x, w, epilogue=epi)
+        ms = time_cuda(lambda: ops.linear(x, w, epilogue=epi, out=y))
+        ms_ref = time_cuda(lambda: torch.matmul(x, w.t()))
+        byts = (M * K + N * K) * 2 + M * N * (4 if epi == ops.EPI_F32 else 2)
+        flops = 2.0 * M * N * K
+        plan = ops.ext().gemm_plan(M, N, K, epi, torch.cuda.get_device_properties(0).multi_processor_count)
+        r = {"kernel": "gemm_tc", "case": name, "M": M, "N": N, "K": K, "ms": round(ms, 4),
+             "GBps": round(byts / ms / 1e6, 1), "TFLOPs": round(flops / ms / 1e9, 1),
+             "hbm_frac": round(byts / ms / 1e6 / hbm, 3), "tc_frac": round(flops / ms / 1e9 / tf, 3),
+             "cublas_ms": round(ms_ref, 4), "speedup_vs_cublas": round(ms_ref / ms, 3),
+             "plan": plan, "peaks": src}
+        print(json.dumps(r), flush=True)
+        out.append(r)
+    return out
+
+
+def bench_attn():
+    hbm, tf, src = peaks()
+    out = []
+    for B, L, nq, nkv, hd in [(32, 2304, 32, 8, 128), (1, 2304, 32, 8, 128), (64, 4096, 32, 8, 128),
+                              (32, 2304, 4, 1, 128)]:
+        nblk = (L + 15) // 16
+        kc = torch.randn(B * nblk, nkv, 16, hd, device="cuda").bfloat16()
+        vc = torch.randn_like(kc)
+        bt = torch.arange(B * nblk, device="cuda", dtype=torch.int32).view(B, nblk)
+        sl = torch.full((B,), L, dtype=torch.int32, device="cuda")
+        q = torch.randn(B, nq, hd, device="cuda").bfloat16()
+        target = 2 * 148
+        want = max(1, (target + B * nkv - 1) // (B * nkv))
+        tps = max(64, ((L + want - 1) // want + 15) // 16 * 16)
+        nsplit = (L + tps - 1) // tps
+        ws = ops.AttnWorkspace("cuda", B, nkv, nq // nkv, hd, nsplit)
+        scale = 1 / math.sqrt(hd)
+        ms = time_cuda(lambda: ops.paged_decode_attention(q, kc, vc, bt, sl, scale, tps, nsplit, ws))
+        byts = 2 * B * L * nkv * hd * 2
+        r = {"kernel": "paged_decode_attention", "B": B, "L": L, "nq": nq, "nkv": nkv, "tps": tps,
+             "nsplit": nsplit, "ms": round(ms, 4), "GBps": round(byts / ms / 1e6, 1),
+             "hbm_frac": round(byts / ms / 1e6 / hbm, 3), "peaks": src}
+        print(json.dumps(r), flush=True)
+        out.append(r)
+    return out
+
+
+if __name__ == "__main__":
+    what = sys.argv[1] if len(sys.argv) > 1 else "all"
+    ops.ext()
+    if what in ("gemm", "all"):
+        bench_gemm()
+    if what in ("attn", "all"):
+        bench_attn()

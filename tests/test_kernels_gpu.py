@@ -1,0 +1,182 @@
+"""Numerics of every sm_100a kernel against a plain PyTorch fp32 reference."""
+
+import math
+
+import pytest
+import torch
+
+from b200serve import ops
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+@pytest.fixture(autouse=True)
+def _seed():
+    torch.manual_seed(0)
+    ops.ext()  # the CUDA path must be the one under test
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 256), (7, 384, 512), (32, 4096, 4096), (32, 6144, 4096),
+                                   (64, 1000, 704), (130, 512, 1024), (256, 2048, 1024), (600, 1536, 2048),
+                                   (33, 18992, 512)])
+def test_gemm_bf16(M, N, K):
+    x = torch.randn(M, K, device=dev).bfloat16()
+    w = (torch.randn(N, K, device=dev) * 0.05).bfloat16()
+    y = ops.linear(x, w)
+    ref = x.float() @ w.float().t()
+    assert y.shape == (M, N)
+    assert _rel(y, ref) < 1e-2, _rel(y, ref)
+    assert ops.gemm_error_flag() == 0
+
+
+@pytest.mark.parametrize("splits", [1, 2, 5])
+def test_gemm_forced_splits_bias_residual(splits):
+    M, N, K = 48, 640, 1024
+    x = torch.randn(M, K, device=dev).bfloat16()
+    w = (torch.randn(N, K, device=dev) * 0.05).bfloat16()
+    b = torch.randn(N, device=dev).bfloat16()
+    r = torch.randn(M, N, device=dev).bfloat16()
+    y = ops.linear(x, w, bias=b, residual=r, splits=splits)
+    ref = x.float() @ w.float().t() + b.float() + r.float()
+    assert _rel(y, ref) < 1e-2
+
+
+def test_gemm_f32_logits():
+    M, N, K = 32, 32000, 256
+    x = torch.randn(M, K, device=dev).bfloat16()
+    w = (torch.randn(N, K, device=dev) * 0.05).bfloat16()
+    y = ops.linear(x, w, epilogue=ops.EPI_F32)
+    assert y.dtype == torch.float32
+    ref = x.float() @ w.float().t()
+    assert _rel(y, ref) < 1e-4
+    assert torch.equal(y.argmax(-1), ref.argmax(-1))
+
+
+@pytest.mark.parametrize("M,I,K", [(5, 704, 256), (32, 1536, 4096), (200, 3072, 1024)])
+def test_gemm_swiglu(M, I, K):
+    from b200serve.models.weights import interleave_gate_up
+    x = torch.randn(M, K, device=dev).bfloat16()
+    g = (torch.randn(I, K, device=dev) * 0.05).bfloat16()
+    u = (torch.randn(I, K, device=dev) * 0.05).bfloat16()
+    w = interleave_gate_up(g, u)
+    y = ops.linear(x, w, epilogue=ops.EPI_SWIGLU)
+    ref = torch.nn.functional.silu(x.float() @ g.float().t()) * (x.float() @ u.float().t())
+    assert _rel(y, ref) < 2e-2
+
+
+def test_gemm_repeated_calls_reuse_counters():
+    x = torch.randn(16, 4096, device=dev).bfloat16()
+    w = (torch.randn(4096, 4096, device=dev) * 0.02).bfloat16()
+    ref = x.float() @ w.float().t()
+    for _ in range(5):
+        assert _rel(ops.linear(x, w), ref) < 1e-2
+
+
+@pytest.mark.parametrize("H,nparts", [(256, 1), (4096, 1), (4096, 4), (2048, 8)])
+def test_rmsnorm_fused(H, nparts):
+    T = 37
+    parts = [torch.randn(T, H, device=dev).bfloat16() for _ in range(nparts)]
+    res = torch.randn(T, H, device=dev).bfloat16()
+    w = torch.randn(H, device=dev).bfloat16()
+    res_out = torch.empty_like(res)
+    y = ops.rmsnorm(parts, w, 1e-6, residual=res, residual_out=res_out)
+    s = sum(p.float() for p in parts) + res.float()
+    ref = s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+    assert _rel(res_out, s) < 1e-2
+    assert _rel(y, ref) < 1e-2
+
+
+@pytest.mark.parametrize("hd,nq,nkv,qk_norm,bias", [(128, 32, 8, True, False), (64, 4, 2, False, True)])
+def test_qkv_post(hd, nq, nkv, qk_norm, bias):
+    T, nb = 21, 8
+    qkv = torch.randn(T, (nq + 2 * nkv) * hd, device=dev).bfloat16()
+    b = torch.randn((nq + 2 * nkv) * hd, device=dev).bfloat16() if bias else None
+    qn = torch.randn(hd, device=dev).bfloat16() if qk_norm else None
+    kn = torch.randn(hd, device=dev).bfloat16() if qk_norm else None
+    cs = ops.rope_cos_sin(hd, 4096, 1e6, dev)
+    pos = torch.randint(0, 4000, (T,), device=dev, dtype=torch.int32)
+    slots = torch.randperm(nb * 16, device=dev)[:T].int()
+    kc = torch.zeros(nb, nkv, 16, hd, device=dev).bfloat16()
+    vc = torch.zeros_like(kc)
+    kc2, vc2 = kc.clone().cpu(), vc.clone().cpu()
+    q = ops.qkv_post(qkv, b, qn, kn, cs, pos, slots, kc, vc, nq, nkv, 1e-6)
+    qr = ops.qkv_post(qkv.cpu(), b.cpu() if bias else None, qn.cpu() if qk_norm else None,
+                      kn.cpu() if qk_norm else None, cs.cpu(), pos.cpu(), slots.cpu(), kc2, vc2, nq, nkv, 1e-6)
+    assert _rel(q.cpu(), qr) < 1e-2
+    assert _rel(kc.cpu(), kc2) < 1e-2
+    assert _rel(vc.cpu(), vc2) < 1e-2
+
+
+def _make_paged(B, lens, nkv, hd, nb_total):
+    kc = torch.randn(nb_total, nkv, 16, hd, device=dev).bfloat16()
+    vc = torch.randn(nb_total, nkv, 16, hd, device=dev).bfloat16()
+    maxb = max((l + 15) // 16 for l in lens)
+    perm = torch.randperm(nb_total, device=dev)
+    bt = torch.zeros(B, maxb, dtype=torch.int32, device=dev)
+    used = 0
+    for b, l in enumerate(lens):
+        n = (l + 15) // 16
+        bt[b, :n] = perm[used:used + n].int()
+        used += n
+    return kc, vc, bt
+
+
+@pytest.mark.parametrize("hd,nq,nkv,lens,tps", [(128, 32, 8, [1, 17, 300, 2048], 256),
+                                                 (128, 32, 4, [5, 999], 64), (64, 4, 2, [64, 65], 1024),
+                                                 (128, 4, 1, [2304] * 3, 128)])
+def test_paged_decode_attention(hd, nq, nkv, lens, tps):
+    B = len(lens)
+    kc, vc, bt = _make_paged(B, lens, nkv, hd, 1024)
+    q = torch.randn(B, nq, hd, device=dev).bfloat16()
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    scale = 1 / math.sqrt(hd)
+    nsplit = (max(lens) + tps - 1) // tps
+    ws = ops.AttnWorkspace(dev, B, nkv, nq // nkv, hd, nsplit)
+    y = ops.paged_decode_attention(q, kc, vc, bt, sl, scale, tps, nsplit, ws)
+    ref = ops.paged_decode_attention(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), sl.cpu(), scale)
+    assert _rel(y.cpu(), ref) < 1e-2
+    y1 = ops.paged_decode_attention(q, kc, vc, bt, sl, scale, 4096, 1)
+    assert _rel(y1.cpu(), ref) < 1e-2
+
+
+@pytest.mark.parametrize("hd,nq,nkv,chunks", [(128, 32, 8, [(0, 100), (0, 64), (37, 50)]),
+                                               (64, 4, 2, [(0, 200), (128, 1)]),
+                                               (128, 8, 8, [(0, 1030)])])
+def test_paged_prefill_attention(hd, nq, nkv, chunks):
+    lens = [s + n for s, n in chunks]
+    S = len(chunks)
+    kc, vc, bt = _make_paged(S, lens, nkv, hd, 512)
+    T = sum(n for _, n in chunks)
+    q = torch.randn(T, nq, hd, device=dev).bfloat16()
+    cu = [0]
+    for _, n in chunks:
+        cu.append(cu[-1] + n)
+    cu_q = torch.tensor(cu, dtype=torch.int32, device=dev)
+    q_start = torch.tensor([s for s, _ in chunks], dtype=torch.int32, device=dev)
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    scale = 1 / math.sqrt(hd)
+    max_q = max(n for _, n in chunks)
+    y = ops.paged_prefill_attention(q, kc, vc, bt, sl, q_start, cu_q, scale, max_q=max_q)
+    ref = ops.paged_prefill_attention(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), sl.cpu(), q_start.cpu(),
+                                      cu_q.cpu(), scale)
+    assert _rel(y.cpu(), ref) < 1e-2
+
+
+def test_silu_mul_and_embedding():
+    from b200serve.models.weights import interleave_gate_up
+    T, I, H = 9, 704, 256
+    g = torch.randn(T, I, device=dev).bfloat16()
+    u = torch.randn(T, I, device=dev).bfloat16()
+    gu = interleave_gate_up(g.t().contiguous(), u.t().contiguous()).t().contiguous()
+    y = ops.silu_mul(gu)
+    ref = torch.nn.functional.silu(g.float()) * u.float()
+    assert _rel(y, ref) < 1e-2
+    table = torch.randn(1000, H, device=dev).bfloat16()
+    ids = torch.randint(0, 1000, (T,), device=dev, dtype=torch.int32)
+    assert torch.equal(ops.embedding(ids, table), table[ids.long()])
