@@ -1,0 +1,388 @@
+"""OpenAI-compatible HTTP API (reference: api/server.py).
+
+Routes: /health, /metrics, /v1/queue, /v1/models, /v1/tokenize, /v1/engine
+(GET, POST switch, POST /reload), /v1/chat/completions (streaming SSE and
+plain JSON). SSE chunks carry the reference's extensions: ``x_thinking``
+deltas for reasoning text, ``x_context_fit`` when the pre-flight fit compacted
+or trimmed the conversation, and ``x_usage`` / ``x_backend`` on the final chunk.
+
+Unlike the reference, requests are not serialised behind one lock: every
+request runs its own producer thread into the engine, whose scheduler
+batches them continuously. The model queue only serialises model switches.
+"""
+
+
+
+import asyncio
+import json
+import logging
+import queue
+import threading
+import time
+import uuid
+from typing import List, Literal, Optional, Union
+
+from pydantic import BaseModel, Field
+
+from b200serve.core import config as cfgmod
+from b200serve.core.api_keys import KeyStore
+from b200serve.core.inference import ThinkFilter, ensure_context_fit
+from b200serve.core.model_queue import ModelBusyError, get_model_queue
+from b200serve.core.sampling import PRESETS, get_preset
+
+_log = logging.getLogger(__name__)
+
+_engine = None
+_engine_lock = threading.Lock()
+_keystore = None
+_auth_failures = {}
+_AUTH_FAIL_WINDOW, _AUTH_FAIL_MAX = 60.0, 10
+
+
+def set_engine(engine):
+    """Install an engine instance (tests, embedding in another process)."""
+    global _engine
+    _engine = engine
+
+
+def _get_engine():
+    global _engine
+    with _engine_lock:
+        if _engine is None:
+            from b200serve.core.engine_factory import create_engine
+            _engine = create_engine()
+        if not _engine.is_loaded():
+            _engine.load(status_callback=lambda m: _log.info(m))
+        return _engine
+
+
+def _check_auth(request) -> bool:
+    if _keystore is None or not _keystore.configured():
+        return True
+    ip = request.client.host if request.client else "unknown"
+    now = time.time()
+    fails = [t for t in _auth_failures.get(ip, []) if now - t < _AUTH_FAIL_WINDOW]
+    auth = request.headers.get("Authorization", "")
+    token = auth[7:] if auth.startswith("Bearer ") else request.headers.get("X-API-Key", "")
+    if token and _keystore.match(token) is not None:
+        _auth_failures[ip] = fails
+        return True
+    if len(fails) < _AUTH_FAIL_MAX:
+        fails.append(now)
+    _auth_failures[ip] = fails
+    return False
+
+
+class ChatMessage(BaseModel):
+    role: str = Field(..., examples=["user"])
+    content: Union[str, List[dict]] = Field(..., examples=["What is the capital of France?"])
+
+
+class ChatCompletionRequest(BaseModel):
+    model: Optional[str] = None
+    messages: List[ChatMessage]
+    max_tokens: Optional[int] = Field(None, ge=1)
+    temperature: Optional[float] = Field(0.7, ge=0.0, le=2.0)
+    top_p: Optional[float] = Field(None, gt=0.0, le=1.0)
+    top_k: Optional[int] = Field(None, ge=0)
+    min_p: Optional[float] = Field(None, ge=0.0, le=1.0)
+    presence_penalty: Optional[float] = None
+    frequency_penalty: Optional[float] = None
+    seed: Optional[int] = None
+    stop: Optional[Union[str, List[str]]] = None
+    stream: Optional[bool] = False
+    options: Optional[dict] = None
+    web_tools: Optional[bool] = False
+    grammar: Optional[str] = None
+    response_format: Optional[dict] = None
+    backend: Optional[Literal["b200", "ollama", "transformers", "llama_cpp", "claude_cli"]] = None
+
+
+class TokenizeRequest(BaseModel):
+    text: Optional[str] = None
+    messages: Optional[List[ChatMessage]] = None
+
+
+class EngineSwitchRequest(BaseModel):
+    model: Optional[str] = None
+    backend: Optional[str] = None
+    turboquant_kv: Optional[bool] = None
+
+
+_SENTINEL = object()
+
+
+class _StreamAbandoned(Exception):
+    """The reader of a stream went away; raised inside the producer's put()."""
+
+
+class _StreamQueue(queue.Queue):
+    """Bounded hand-off from a generation thread to the SSE generator; after
+    abandon() every put() raises so the producer stops generating."""
+
+    def __init__(self):
+        super().__init__(maxsize=256)
+        self._abandoned = threading.Event()
+
+    def put(self, item, block=True, timeout=None):
+        while True:
+            if self._abandoned.is_set():
+                raise _StreamAbandoned()
+            try:
+                return super().put(item, timeout=0.25)
+            except queue.Full:
+                continue
+
+    def finish(self):
+        try:
+            self.put(_SENTINEL)
+        except _StreamAbandoned:
+            pass
+
+    def abandon(self):
+        self._abandoned.set()
+        try:
+            queue.Queue.put(self, _SENTINEL, block=False)
+        except queue.Full:
+            pass
+
+
+def _make_sse_chunk(chat_id, model, delta, finish_reason=None, extra=None) -> str:
+    ev = {"id": chat_id, "object": "chat.completion.chunk", "created": int(time.time()), "model": model,
+          "choices": [{"index": 0, "delta": delta, "finish_reason": finish_reason}]}
+    if extra:
+        ev.update(extra)
+    return f"data: {json.dumps(ev)}\n\n"
+
+
+def _sampling_from_request(body: ChatCompletionRequest) -> dict:
+    opts = body.options or {}
+    preset = opts.get("preset")
+    samp = get_preset(preset) if preset in PRESETS else {}
+    samp.update(opts.get("sampling") or {})
+    samp["temperature"] = samp.get("temperature", body.temperature) if preset else body.temperature
+    for k in ("top_p", "top_k", "min_p", "presence_penalty", "frequency_penalty", "seed", "stop"):
+        v = getattr(body, k)
+        if v is not None:
+            samp[k] = v
+    return samp
+
+
+def _produce(engine, messages, max_tokens, samp, q: _StreamQueue, enable_thinking):
+    """Producer thread: stream thinking/content pieces into ``q``."""
+    tf = ThinkFilter(on_response=lambda t: q.put(("content", t)),
+                     on_thinking=lambda t: q.put(("thinking", t)),
+                     starts_in_think=bool(enable_thinking and getattr(engine, "stream_starts_in_think", True)))
+    try:
+        engine.generate_streaming(messages, max_tokens=max_tokens, temperature=samp.get("temperature", 0.7),
+                                  on_token=tf.feed, enable_thinking=enable_thinking, sampling=samp)
+        tf.flush()
+        st = getattr(engine, "_last_gen_stats", None) or {}
+        q.put(("usage", {"prompt_tokens": st.get("prompt_tokens", 0),
+                         "completion_tokens": st.get("completion_tokens", 0),
+                         "finish_reason": st.get("finish_reason", "stop"),
+                         "ttft": st.get("ttft"), "decode_tok_per_sec": st.get("decode_tok_per_sec")}))
+    except _StreamAbandoned:
+        pass
+    except Exception as e:  # surfaced to the client as an SSE error event
+        _log.exception("generation failed")
+        try:
+            q.put(("error", str(e)))
+        except _StreamAbandoned:
+            pass
+    finally:
+        q.finish()
+
+
+def create_app(engine=None, keystore: KeyStore = None):
+    from fastapi import FastAPI, HTTPException, Request
+    from fastapi.middleware.cors import CORSMiddleware
+    from fastapi.responses import PlainTextResponse, StreamingResponse
+
+    global _keystore
+    _keystore = keystore or KeyStore()
+    if engine is not None:
+        set_engine(engine)
+    app = FastAPI(title="b200serve", version="0.1.0")
+    app.add_middleware(CORSMiddleware, allow_origins=["*"], allow_methods=["*"], allow_headers=["*"])
+    mq = get_model_queue()
+    mq.register_engine_unload(lambda: _engine.unload() if _engine is not None else None)
+
+    def auth(request):
+        if not _check_auth(request):
+            raise HTTPException(status_code=401, detail="Invalid API key")
+
+    @app.get("/health")
+    async def health(request: Request):
+        auth(request)
+        from b200serve.core.health import run_health_check
+        rep = await asyncio.to_thread(run_health_check, _engine)
+        rep["backend"] = cfgmod.get_active_backend()
+        return rep
+
+    @app.get("/metrics")
+    async def metrics(request: Request):
+        auth(request)
+        m = _engine.metrics() if _engine is not None and _engine.is_loaded() else {}
+        lines = [f"b200serve_{k} {v}" for k, v in m.items() if isinstance(v, (int, float))]
+        lines += [f"b200serve_queue_{k} {v}" for k, v in mq.stats.items() if isinstance(v, (int, float))]
+        return PlainTextResponse("\n".join(lines) + "\n")
+
+    @app.get("/v1/queue")
+    async def queue_status(request: Request):
+        auth(request)
+        return mq.stats
+
+    @app.get("/v1/models")
+    async def list_models(request: Request, backend: str = None):
+        auth(request)
+        active = cfgmod.get_active_model_name()
+        ctx = _engine.get_context_size() if _engine is not None else 0
+        data = []
+        for name in cfgmod.get_model_names():
+            data.append({"id": name, "object": "model", "created": int(time.time()), "owned_by": "local",
+                         "x_backend": "b200", "x_capabilities": ["text"], "x_size": 0,
+                         "x_context_length": ctx if name == active else 0,
+                         "x_recommended_max_completion": ctx // 2 if name == active else 0,
+                         "x_image_token_cost_per_megapixel": None, "x_active": name == active})
+        return {"object": "list", "data": data}
+
+    @app.post("/v1/tokenize")
+    async def tokenize(request: Request, body: TokenizeRequest):
+        auth(request)
+        if not body.text and not body.messages:
+            raise HTTPException(status_code=400, detail="Provide 'text' or 'messages'")
+        if body.messages:
+            text = "\n".join(f"{m.role}: {m.content}" if isinstance(m.content, str) else f"{m.role}: [multimodal]"
+                             for m in body.messages)
+        else:
+            text = body.text
+        eng = await asyncio.to_thread(_get_engine)
+        return {"token_count": eng.count_tokens(text), "text_length": len(text)}
+
+    @app.get("/v1/engine")
+    async def engine_info(request: Request):
+        auth(request)
+        e = _engine
+        return {"backend": cfgmod.get_active_backend(), "model": cfgmod.get_active_model_name(),
+                "loaded": bool(e and e.is_loaded()), "turboquant_kv": cfgmod.get_turboquant_kv(),
+                "config": e.config.to_dict() if e is not None else None,
+                "metrics": e.metrics() if e is not None and e.is_loaded() else {}}
+
+    @app.post("/v1/engine")
+    async def engine_switch(request: Request, body: EngineSwitchRequest):
+        auth(request)
+        if body.backend and not cfgmod.set_active_backend(body.backend):
+            raise HTTPException(status_code=400, detail=f"unknown backend {body.backend}")
+        if body.turboquant_kv is not None:
+            cfgmod.set_turboquant_kv(body.turboquant_kv)
+        if body.model:
+            if not cfgmod.set_active_model(body.model):
+                raise HTTPException(status_code=400, detail=f"unknown model {body.model}")
+            try:
+                await mq.switch_if_needed(body.model, cfgmod.get_active_backend())
+            except ModelBusyError as e:
+                raise HTTPException(status_code=409, detail=str(e))
+        return {"ok": True, "model": cfgmod.get_active_model_name(), "backend": cfgmod.get_active_backend()}
+
+    @app.post("/v1/engine/reload")
+    async def engine_reload(request: Request):
+        auth(request)
+        await mq.unload_current()
+        await asyncio.to_thread(_get_engine)
+        return {"ok": True}
+
+    @app.post("/v1/chat/completions")
+    async def chat_completions(request: Request, body: ChatCompletionRequest):
+        auth(request)
+        messages = [m.model_dump() for m in body.messages]
+        if not messages:
+            raise HTTPException(status_code=400, detail="messages is required")
+        opts = body.options or {}
+        enable_thinking = opts.get("think", True)
+        backend = body.backend or cfgmod.get_active_backend()
+        model = body.model or cfgmod.get_active_model_name()
+        samp = _sampling_from_request(body)
+        eng = await asyncio.to_thread(_get_engine)
+        max_tokens = body.max_tokens or max(1, eng.get_context_size() // 2)
+        messages, fit = ensure_context_fit(messages, eng.get_context_size(), max_tokens,
+                                           count_fn=eng.count_tokens)
+        mq.request_started()
+        chat_id = f"chatcmpl-{uuid.uuid4().hex[:12]}"
+
+        if body.stream:
+            async def gen():
+                q = _StreamQueue()
+                th = threading.Thread(target=_produce, args=(eng, messages, max_tokens, samp, q, enable_thinking),
+                                      daemon=True)
+                th.start()
+                usage = {"prompt_tokens": 0, "completion_tokens": 0}
+                finish = "stop"
+                loop = asyncio.get_running_loop()
+                try:
+                    if fit["compacted"] or fit["trimmed"]:
+                        yield f"data: {json.dumps({'x_context_fit': fit})}\n\n"
+                    while True:
+                        item = await loop.run_in_executor(None, q.get)
+                        if item is _SENTINEL:
+                            break
+                        kind, data = item
+                        if kind == "thinking":
+                            yield _make_sse_chunk(chat_id, model, {"x_thinking": data})
+                        elif kind == "content":
+                            yield _make_sse_chunk(chat_id, model, {"content": data})
+                        elif kind == "usage":
+                            finish = data.pop("finish_reason", "stop")
+                            usage = data
+                        elif kind == "error":
+                            yield f"data: {json.dumps({'error': data})}\n\n"
+                    usage["total_tokens"] = usage.get("prompt_tokens", 0) + usage.get("completion_tokens", 0)
+                    yield _make_sse_chunk(chat_id, model, {}, finish_reason=finish,
+                                          extra={"x_usage": usage, "x_backend": backend})
+                    yield "data: [DONE]\n\n"
+                finally:
+                    q.abandon()
+                    mq.request_finished()
+
+            return StreamingResponse(gen(), media_type="text/event-stream",
+                                     headers={"Cache-Control": "no-cache", "X-Accel-Buffering": "no"})
+
+        try:
+            text = await asyncio.to_thread(
+                lambda: eng.generate_streaming(messages, max_tokens=max_tokens, temperature=samp["temperature"],
+                                               enable_thinking=enable_thinking, raw_output=True, sampling=samp))
+        finally:
+            mq.request_finished()
+        st = getattr(eng, "_last_gen_stats", None) or {}
+        pt, ct = st.get("prompt_tokens", 0), st.get("completion_tokens", 0)
+        return {"id": chat_id, "object": "chat.completion", "created": int(time.time()), "model": model,
+                "choices": [{"index": 0, "message": {"role": "assistant", "content": text or ""},
+                             "finish_reason": st.get("finish_reason", "stop")}],
+                "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct},
+                "x_backend": backend, "x_stats": st}
+
+    return app
+
+
+def main(argv=None):
+    import argparse
+    import uvicorn
+    from b200serve.core.config import add_engine_cli_args, engine_config_from_args, set_engine_config
+    from b200serve.core.logging_config import setup_logging
+    ap = argparse.ArgumentParser("b200serve")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    add_engine_cli_args(ap)
+    a = ap.parse_args(argv)
+    setup_logging()
+    cfg = engine_config_from_args(a)
+    set_engine_config(cfg)
+    cfgmod.set_active_model(cfg.model)
+    if cfg.tp_size > 1:
+        from b200serve.parallel.launch import serve_tp
+        return serve_tp(cfg, a.host, a.port, create_app)
+    uvicorn.run(create_app(), host=a.host, port=a.port, log_level="info")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,293 @@
+"""B200Engine: the BaseEngine implementation that owns the decoder forward.
+
+load() builds one model replica (tensor-parallel over ``tp_size`` ranks, one
+process per GPU), sizes the paged KV cache from free device memory, and starts
+the scheduler loop thread on rank 0. generate_streaming() keeps the
+reference's contract (core/engine_transformers.py:1204-1518): chat template ->
+token stream through ``on_token`` -> cleaned answer, and the same
+``_last_gen_stats`` keys (tokens, prompt_tokens, completion_tokens,
+finish_reason, wall_time, tok_per_sec, ttft, decode_tok_per_sec).
+generate() is the batch API: many token-id prompts in, completions out.
+"""
+
+from __future__ import annotations
+
+import logging
+import os
+import queue
+import threading
+import time
+
+import torch
+
+from b200serve.core.config import EngineConfig
+from b200serve.core.engine_base import BaseEngine
+from b200serve.core.inference import _clean_response, strip_think_blocks, STOP_STRINGS
+from b200serve.engine.kv_cache import BLOCK, KVCache
+from b200serve.engine.sampler import SamplingParams
+from b200serve.engine.scheduler import Request, Scheduler
+from b200serve.engine.tokenizer import IncrementalDecoder, load_tokenizer
+
+_log = logging.getLogger(__name__)
+
+
+def _dtype(name):
+    return {"bfloat16": torch.bfloat16, "bf16": torch.bfloat16, "float32": torch.float32,
+            "fp32": torch.float32}[name]
+
+
+class B200Engine(BaseEngine):
+    stream_starts_in_think = True
+
+    def __init__(self, config: EngineConfig = None, weights=None, tokenizer=None):
+        self.config = (config or EngineConfig()).validate()
+        self._injected_weights = weights
+        self._injected_tokenizer = tokenizer
+        self.model_cfg = None
+        self.weights = None
+        self.kv = None
+        self.runner = None
+        self.scheduler = None
+        self.tokenizer = None
+        self.comm = None
+        self._loaded_model = None
+        self._thread = None
+        self._stop = threading.Event()
+        self._wake = threading.Condition()
+        self._error = None
+        self._last_gen_stats = None
+        self.rank = 0
+        self.world = 1
+
+    # ------------------------------------------------------------ lifecycle
+    def is_loaded(self) -> bool:
+        return self.runner is not None
+
+    def needs_reload(self) -> bool:
+        from b200serve.core.config import get_active_model_name
+        return self._loaded_model is not None and self._loaded_model != self.config.model
+
+    def load(self, status_callback=None):
+        if self.is_loaded():
+            return
+        cfgE = self.config
+        say = status_callback or (lambda m: _log.info(m))
+        from b200serve.models.config import get_model_config
+        from b200serve.parallel import dist as pdist
+        self.rank, self.world = pdist.rank_world()
+        tp = cfgE.tp_size
+        if tp > 1 and self.world != tp:
+            raise RuntimeError(f"tp_size={tp} needs {tp} ranks (torchrun), found world={self.world}")
+        if cfgE.device == "cuda" and torch.cuda.is_available():
+            dev = torch.device("cuda", pdist.local_rank() if tp > 1 else torch.cuda.current_device())
+            torch.cuda.set_device(dev)
+        else:
+            dev = torch.device("cpu")
+        self.device = dev
+        mc = get_model_config(cfgE.model, cfgE.num_layers_override)
+        self.model_cfg = mc
+        dtype = _dtype(cfgE.dtype)
+        say(f"b200: building {mc.name} ({mc.num_params() / 1e9:.2f}B params) tp={tp} on {dev}")
+        self.weights = self._injected_weights or self._load_weights(mc, dtype, dev)
+        self.comm = pdist.make_comm(cfgE, dev, self.model_cfg) if tp > 1 else None
+        nkv_local = mc.num_kv_heads // tp
+        num_blocks = self._size_kv(mc, nkv_local, dtype, dev)
+        self.kv = KVCache(mc.num_layers, num_blocks, nkv_local, mc.head_dim, dtype=dtype, device=dev,
+                          kv_format=cfgE.kv_format)
+        from b200serve.engine.runner import ModelRunner
+        runner = ModelRunner(mc, self.weights, self.kv, comm=self.comm, device=dev, max_batch=cfgE.max_batch,
+                             max_seq=cfgE.max_seq, use_graphs=cfgE.cuda_graphs)
+        if tp > 1:
+            from b200serve.parallel.worker import BroadcastRunner
+            runner = BroadcastRunner(runner, self.comm)
+        self.runner = runner
+        self.scheduler = Scheduler(runner, num_blocks, max_batch=cfgE.max_batch, prefill_chunk=cfgE.prefill_chunk,
+                                   max_seq=cfgE.max_seq)
+        self.tokenizer = self._injected_tokenizer or load_tokenizer(self._model_path(), mc.vocab_size)
+        from b200serve.core import inference
+        inference._tokenizer = self.tokenizer
+        self._loaded_model = cfgE.model
+        say(f"b200: ready, {num_blocks} KV pages ({num_blocks * BLOCK} tokens)")
+
+    def _model_path(self):
+        m = self.config.model
+        return m if os.path.exists(m) else None
+
+    def _load_weights(self, mc, dtype, dev):
+        cfgE = self.config
+        from b200serve.models import weights as W
+        kw = dict(tp_rank=self.rank if cfgE.tp_size > 1 else 0, tp_size=cfgE.tp_size,
+                  ep_rank=self.rank if cfgE.ep_size > 1 else 0, ep_size=cfgE.ep_size, dtype=dtype, device=dev)
+        if cfgE.weights == "random":
+            return W.random_weights(mc, seed=cfgE.seed, std=cfgE.init_std, **kw)
+        if cfgE.weights == "safetensors":
+            return W.load_safetensors_dir(mc, cfgE.model, **kw)
+        if cfgE.weights == "gguf":
+            from b200serve.models.gguf import load_gguf_weights
+            return load_gguf_weights(mc, cfgE.model, **kw)
+        raise ValueError(f"unknown weights source {cfgE.weights!r}")
+
+    def _size_kv(self, mc, nkv_local, dtype, dev) -> int:
+        cfgE = self.config
+        per_block = KVCache.bytes_per_block(mc.num_layers, nkv_local, mc.head_dim,
+                                            torch.tensor([], dtype=dtype).element_size())
+        want = cfgE.max_batch * ((cfgE.max_seq + BLOCK - 1) // BLOCK) + 64
+        if cfgE.kv_blocks:
+            return cfgE.kv_blocks
+        if dev.type == "cuda":
+            free, _ = torch.cuda.mem_get_info(dev)
+            budget = int((free - (6 << 30)) * cfgE.kv_mem_fraction)
+            n = max(64, budget // per_block)
+            return int(min(n, want))
+        return int(min(want, 4096))
+
+    def unload(self, status_callback=None):
+        self.stop_loop()
+        if self.runner is not None:
+            inner = getattr(self.runner, "inner", self.runner)
+            inner.release_graphs()
+        self.runner = self.scheduler = self.kv = self.weights = None
+        if torch.cuda.is_available():
+            torch.cuda.empty_cache()
+
+    def periodic_cleanup(self):
+        if torch.cuda.is_available() and self.scheduler is not None and not self.scheduler.has_work():
+            torch.cuda.empty_cache()
+
+    def get_context_size(self) -> int:
+        return self.config.max_seq
+
+    def count_tokens(self, text: str) -> int:
+        if self.tokenizer is None:
+            return len(text) // 4
+        return len(self.tokenizer.encode(text, add_special_tokens=False))
+
+    def metrics(self) -> dict:
+        return self.scheduler.metrics() if self.scheduler else {}
+
+    # ------------------------------------------------------------ loop thread
+    def start_loop(self):
+        if self._thread is not None:
+            return
+        self._stop.clear()
+        self._thread = threading.Thread(target=self._loop, name="b200-engine", daemon=True)
+        self._thread.start()
+
+    def stop_loop(self):
+        if self._thread is None:
+            return
+        self._stop.set()
+        with self._wake:
+            self._wake.notify_all()
+        self._thread.join(timeout=30)
+        self._thread = None
+        if self.world > 1 and hasattr(self.runner, "shutdown_workers"):
+            self.runner.shutdown_workers()
+
+    def _loop(self):
+        if self.device.type == "cuda":
+            torch.cuda.set_device(self.device)
+        while not self._stop.is_set():
+            if not self.scheduler.has_work():
+                with self._wake:
+                    self._wake.wait(timeout=0.05)
+                continue
+            try:
+                self.scheduler.step()
+            except Exception as e:  # fail every in-flight request, keep the loop alive
+                _log.exception("engine step failed")
+                self._error = e
+                for r in list(self.scheduler.running) + list(self.scheduler.waiting):
+                    r.aborted = True
+                    self.scheduler._finish(r, "error")
+                self.scheduler.running.clear()
+                self.scheduler.waiting.clear()
+
+    def submit(self, req: Request) -> Request:
+        self.load()
+        self.start_loop()
+        self.scheduler.add(req)
+        with self._wake:
+            self._wake.notify_all()
+        return req
+
+    # ------------------------------------------------------------ batch API
+    def generate(self, prompts, params: SamplingParams = None, timeout: float = None):
+        """Token-id prompts -> finished Requests (output ids, ttft, finish_reason)."""
+        params = params or SamplingParams()
+        stop_ids = set() if params.ignore_eos else self.tokenizer.stop_ids
+        reqs = [self.submit(Request(prompt=list(p), params=params, stop_ids=stop_ids)) for p in prompts]
+        for r in reqs:
+            if not r.done_event.wait(timeout):
+                raise TimeoutError(f"{r.rid} did not finish")
+        return reqs
+
+    # ------------------------------------------------------------ BaseEngine
+    def generate_streaming(self, messages, max_tokens, temperature, on_token=None, on_complete=None,
+                           enable_thinking=True, grammar=None, response_format=None, raw_output=False,
+                           web_tools=False, reasoning_effort=None, on_telemetry=None, sampling=None) -> str:
+        self.load()
+        params = SamplingParams.from_dict(sampling, temperature=temperature,
+                                          max_tokens=max_tokens if max_tokens and max_tokens > 0 else 8192)
+        prompt = self.tokenizer.apply_chat_template(messages, add_generation_prompt=True,
+                                                    enable_thinking=enable_thinking)
+        prompt = prompt[-(self.config.max_seq - 1):]
+        stop_strings = list(STOP_STRINGS) + list(params.stop)
+        q = queue.Queue()
+        dec = IncrementalDecoder(self.tokenizer)
+        text_so_far = [""]
+
+        def _cb(req, tok):
+            delta = dec.push(tok)
+            if tok in req.stop_ids:
+                delta = ""
+            q.put(("tok", delta))
+            if delta:
+                text_so_far[0] += delta
+                tail = text_so_far[0][-64:]
+                if any(s in tail for s in params.stop):
+                    return True
+            return False
+
+        t_start = time.perf_counter()
+        req = self.submit(Request(prompt=prompt, params=params, stop_ids=self.tokenizer.stop_ids, on_token=_cb))
+        full, t_first, callback_error = "", None, None
+        try:
+            while True:
+                try:
+                    kind, delta = q.get(timeout=0.1)
+                except queue.Empty:
+                    if req.done_event.is_set() and q.empty():
+                        break
+                    continue
+                if delta:
+                    if t_first is None:
+                        t_first = time.perf_counter()
+                    full += delta
+                    if on_token:
+                        on_token(delta)
+        except BaseException as e:  # the consumer raised: abort generation, re-raise after cleanup
+            callback_error = e
+            self.scheduler.abort(req)
+            req.done_event.wait(30)
+        t_end = time.perf_counter()
+        n = len(req.output)
+        wall = t_end - t_start
+        ttft = (t_first - t_start) if t_first else (req.ttft or 0.0)
+        dec_time = (t_end - t_first) if t_first else wall
+        self._last_gen_stats = {
+            "tokens": n, "prompt_tokens": len(prompt), "completion_tokens": n,
+            "finish_reason": req.finish_reason if req.finish_reason in ("length", "stop") else "stop",
+            "wall_time": round(wall, 2), "tok_per_sec": round(n / wall, 1) if wall > 0 else 0,
+            "ttft": round(ttft, 3), "decode_tok_per_sec": round(max(n - 1, 0) / dec_time, 1) if dec_time > 0 else 0,
+            "prefix_hit_tokens": req.prefix_hit,
+        }
+        if callback_error is not None:
+            raise callback_error
+        if self._error is not None and req.finish_reason == "error":
+            err, self._error = self._error, None
+            raise err
+        clean = strip_think_blocks(full) if raw_output else _clean_response(full)
+        if on_complete:
+            on_complete(clean)
+        return clean

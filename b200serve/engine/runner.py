@@ -1,0 +1,227 @@
+"""Model runner: static decode buffers, CUDA-graph capture per batch bucket,
+and the prefill path.
+
+Decode steps are launch-bound at small batch (36 layers x ~8 kernels), so each
+batch-size bucket is captured once into a CUDA graph whose inputs live in
+static device buffers; a step copies the host-built inputs (pinned memory)
+into those buffers and replays the graph. The attention grid of a bucket is
+sized for ``max_seq``; splits beyond a sequence's length exit at once.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from b200serve import ops
+from b200serve.models.qwen import Decoder, ForwardBatch
+
+DECODE_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
+
+
+class ModelRunner:
+    def __init__(self, cfg, weights, kv, comm=None, device="cuda", max_batch=64, max_seq=4096,
+                 use_graphs=True):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.decoder = Decoder(cfg, weights, kv, comm=comm, device=self.device)
+        self.comm = self.decoder.comm
+        self.max_batch = max_batch
+        self.max_seq = max_seq
+        self.max_blocks = (max_seq + 15) // 16
+        self.use_graphs = use_graphs and self.device.type == "cuda"
+        self.buckets = [b for b in DECODE_BUCKETS if b < max_batch] + [max_batch]
+        B, d = max_batch, self.device
+        i32 = dict(dtype=torch.int32, device=d)
+        self.s_ids = torch.zeros(B, **i32)
+        self.s_pos = torch.zeros(B, **i32)
+        self.s_slots = torch.full((B,), -1, **i32)
+        self.s_bt = torch.zeros(B, self.max_blocks, **i32)
+        self.s_lens = torch.zeros(B, **i32)
+        self.s_tokens = torch.zeros(B, **i32)
+        self.graphs = {}
+        self.graph_out = {}
+        self.launches_per_step = {}
+        self.last_loop_ms = None
+        self.vocab_start = weights.vocab_start
+        self.greedy_buf = None
+        pin = self.device.type == "cuda"
+        self.h_pack = torch.zeros(B * (4 + self.max_blocks), dtype=torch.int32, pin_memory=pin)
+        self.s_pack = torch.zeros(B * (4 + self.max_blocks), **i32)
+
+    # ------------------------------------------------------------ helpers
+    def bucket(self, n: int) -> int:
+        for b in self.buckets:
+            if b >= n:
+                return b
+        raise ValueError(f"batch {n} > max_batch {self.max_batch}")
+
+    def attn_plan(self, bucket: int):
+        per = bucket * self.decoder.nkv
+        tps = 64 if per <= 16 else 128 if per <= 64 else 256
+        return tps, (self.max_seq + tps - 1) // tps
+
+    def _decode_fb(self, bucket: int) -> ForwardBatch:
+        return ForwardBatch(input_ids=self.s_ids[:bucket], positions=self.s_pos[:bucket],
+                            slots=self.s_slots[:bucket], block_tables=self.s_bt[:bucket],
+                            seq_lens=self.s_lens[:bucket], logit_rows=None, is_decode=True)
+
+    def _decode_body(self, bucket: int, greedy: bool):
+        logits = self.decoder.forward(self._decode_fb(bucket), attn_plan=self.attn_plan(bucket))
+        if greedy:
+            return logits, self.greedy_tokens(logits)
+        return logits, None
+
+    def greedy_tokens(self, logits: torch.Tensor) -> torch.Tensor:
+        """Global argmax over the vocabulary split across tensor-parallel ranks (int32)."""
+        B = logits.shape[0]
+        idx = torch.empty(B, dtype=torch.int32, device=logits.device)
+        if logits.is_cuda:
+            val = torch.empty(B, dtype=torch.float32, device=logits.device)
+            ops.argmax_rows(logits, idx, val, self.vocab_start)
+        else:
+            val, i64 = logits.max(-1)
+            idx.copy_(i64 + self.vocab_start)
+        if self.comm.world == 1:
+            return idx
+        vals, idxs = self.comm.all_gather_small(val), self.comm.all_gather_small(idx)
+        out = torch.empty(B, dtype=torch.int32, device=logits.device)
+        if logits.is_cuda:
+            ops.argmax_merge(vals, idxs, out)
+        else:
+            best = vals.argmax(0)
+            out.copy_(idxs.gather(0, best[None])[0])
+        return out
+
+    # ------------------------------------------------------------ decode
+    def load_decode_inputs(self, ids, pos, slots, block_tables, lens):
+        """Host lists -> pinned pack -> one H2D copy -> static buffers."""
+        B = len(ids)
+        bucket = self.bucket(B)
+        mb = self.max_blocks
+        pack = self.h_pack
+        pack.zero_()
+        v = pack[: bucket * (4 + mb)].view(bucket, 4 + mb)
+        if B:
+            v[:B, 0] = torch.as_tensor(ids, dtype=torch.int32)
+            v[:B, 1] = torch.as_tensor(pos, dtype=torch.int32)
+            v[:B, 2] = torch.as_tensor(slots, dtype=torch.int32)
+            v[:B, 3] = torch.as_tensor(lens, dtype=torch.int32)
+            for i, bt in enumerate(block_tables):
+                if bt:
+                    v[i, 4:4 + len(bt)] = torch.as_tensor(bt, dtype=torch.int32)
+        v[B:, 2] = -1
+        dev = self.s_pack[: bucket * (4 + mb)]
+        dev.copy_(pack[: bucket * (4 + mb)], non_blocking=True)
+        dv = dev.view(bucket, 4 + mb)
+        self.s_ids[:bucket].copy_(dv[:, 0])
+        self.s_pos[:bucket].copy_(dv[:, 1])
+        self.s_slots[:bucket].copy_(dv[:, 2])
+        self.s_lens[:bucket].copy_(dv[:, 3])
+        self.s_bt[:bucket].copy_(dv[:, 4:])
+        return bucket, pack[: bucket * (4 + mb)].numel() * 4
+
+    def decode(self, ids, pos, slots, block_tables, lens, greedy=True):
+        """One decode step for B sequences. Returns (logits [B, V_local], tokens [B] or None)."""
+        B = len(ids)
+        bucket, _ = self.load_decode_inputs(ids, pos, slots, block_tables, lens)
+        if self.use_graphs:
+            key = (bucket, greedy)
+            if key not in self.graphs:
+                self.capture(bucket, greedy)
+            self.graphs[key].replay()
+            logits, toks = self.graph_out[key]
+        else:
+            logits, toks = self._decode_body(bucket, greedy)
+        return logits[:B], (toks[:B] if toks is not None else None)
+
+    def capture(self, bucket: int, greedy: bool):
+        # warm up outside the graph (lazy workspace allocation, kernel attributes)
+        for _ in range(2):
+            self._decode_body(bucket, greedy)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out = self._decode_body(bucket, greedy)
+        self.graphs[(bucket, greedy)] = g
+        self.graph_out[(bucket, greedy)] = out
+
+    # ------------------------------------------------------------ timed decode loop
+    def _advance(self, toks, B):
+        """Feed the sampled tokens back and move every sequence one position on (device only)."""
+        self.s_ids[:B].copy_(toks[:B])
+        self.s_pos[:B] += 1
+        self.s_lens[:B] += 1
+        p = self.s_pos[:B].long()
+        self.s_slots[:B] = (self.s_bt[:B].gather(1, (p // 16)[:, None])[:, 0] * 16 + p % 16).int()
+
+    def decode_loop(self, ids, pos, slots, block_tables, lens, warmup: int, steps: int) -> dict:
+        """Run ``warmup`` + ``steps`` greedy decode steps without host round trips and time the
+        last ``steps`` with CUDA events (bracketed by barrier + synchronize)."""
+        bucket, _ = self.load_decode_inputs(ids, pos, slots, block_tables, lens)
+        return self.loop_body(len(ids), bucket, warmup, steps)
+
+    def loop_body(self, B, bucket, warmup, steps) -> dict:
+        key = (bucket, "loop", B)
+        if key not in self.graphs:
+            for _ in range(2):
+                _, toks = self._decode_body(bucket, True)
+            torch.cuda.synchronize()
+            ops.reset_launch_count()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                _, toks = self._decode_body(bucket, True)
+                self._advance(toks, B)
+            self.launches_per_step[bucket] = ops.launch_count()
+            self.graphs[key] = g
+        g = self.graphs[key]
+        for _ in range(warmup):
+            g.replay()
+        if self.comm.world > 1:
+            self.comm.barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            g.replay()
+        end.record()
+        torch.cuda.synchronize()
+        if self.comm.world > 1:
+            self.comm.barrier()
+        ms = start.elapsed_time(end)
+        self.last_loop_ms = ms
+        return {"ms": ms, "launches_per_step": self.launches_per_step.get(bucket)}
+
+    def release_graphs(self):
+        self.graphs.clear()
+        self.graph_out.clear()
+
+    # ------------------------------------------------------------ prefill / mixed
+    def prefill(self, seqs):
+        """``seqs``: list of dicts with ids (new tokens), start (position of the first new
+        token), block_table, want_logits. Returns fp32 logits for sequences with want_logits,
+        in order."""
+        d = self.device
+        ids, pos, slots, cu, qs, lens, rows = [], [], [], [0], [], [], []
+        maxb = max(len(s["block_table"]) for s in seqs)
+        bt = torch.zeros(len(seqs), maxb, dtype=torch.int32)
+        for i, s in enumerate(seqs):
+            n = len(s["ids"])
+            st = s["start"]
+            ids += list(s["ids"])
+            pos += list(range(st, st + n))
+            table = s["block_table"]
+            slots += [table[p // 16] * 16 + p % 16 for p in range(st, st + n)]
+            cu.append(cu[-1] + n)
+            qs.append(st)
+            lens.append(st + n)
+            bt[i, : len(table)] = torch.as_tensor(table, dtype=torch.int32)
+            if s.get("want_logits", True):
+                rows.append(cu[-1] - 1)
+        T = len(ids)
+        t = lambda x: torch.as_tensor(x, dtype=torch.int32).to(d, non_blocking=True)
+        fb = ForwardBatch(input_ids=t(ids), positions=t(pos), slots=t(slots), block_tables=bt.to(d),
+                          seq_lens=t(lens), logit_rows=torch.as_tensor(rows, dtype=torch.long).to(d),
+                          is_decode=False, cu_q=t(cu), q_start=t(qs), max_q=max(len(s["ids"]) for s in seqs))
+        if T == 0:
+            return None
+        return self.decoder.forward(fb)

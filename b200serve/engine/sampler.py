@@ -1,0 +1,119 @@
+"""Sampling parameters and the batched sampler.
+
+Semantics follow the reference CPU sampler (webgpu/src/engine/generate.ts:274-510)
+and HF logits processors: repetition penalty (divide positive / multiply
+negative logits of seen tokens), presence and frequency penalties, temperature,
+top-k, top-p (nucleus over the sorted distribution, always keeping the top
+token), min-p (relative to the top probability), then a draw. Temperature 0
+means greedy argmax (lowest index on ties). Draws use a per-request seeded
+generator so a seed reproduces a completion.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from b200serve import ops
+
+
+@dataclass
+class SamplingParams:
+    temperature: float = 0.0
+    top_k: int = 0
+    top_p: float = 1.0
+    min_p: float = 0.0
+    repeat_penalty: float = 1.0
+    presence_penalty: float = 0.0
+    frequency_penalty: float = 0.0
+    repeat_last_n: int = 64
+    seed: int = None
+    max_tokens: int = 256
+    stop: tuple = ()
+    ignore_eos: bool = False
+
+    @property
+    def greedy(self) -> bool:
+        return not self.temperature or self.temperature <= 0
+
+    @classmethod
+    def from_dict(cls, d: dict, temperature=None, max_tokens=None) -> "SamplingParams":
+        d = dict(d or {})
+        t = d.get("temperature", temperature)
+        sp = cls(temperature=float(t or 0.0), top_k=int(d.get("top_k", 0) or 0),
+                 top_p=float(d.get("top_p", 1.0)), min_p=float(d.get("min_p", 0.0)),
+                 repeat_penalty=float(d.get("repeat_penalty", 1.0)),
+                 presence_penalty=float(d.get("presence_penalty", 0.0)),
+                 frequency_penalty=float(d.get("frequency_penalty", 0.0)),
+                 repeat_last_n=int(d.get("repeat_last_n", 64)), seed=d.get("seed"))
+        if max_tokens:
+            sp.max_tokens = int(max_tokens)
+        stop = d.get("stop")
+        if stop:
+            sp.stop = tuple([stop] if isinstance(stop, str) else stop)
+        return sp
+
+
+def apply_penalties(logits: torch.Tensor, history: list, params: list) -> torch.Tensor:
+    """In place on fp32 logits [B, V]; ``history`` holds each row's recent token ids."""
+    for i, (p, hist) in enumerate(zip(params, history)):
+        if p.repeat_penalty == 1.0 and not p.presence_penalty and not p.frequency_penalty:
+            continue
+        recent = hist[-p.repeat_last_n:] if p.repeat_last_n > 0 else hist
+        if not recent:
+            continue
+        ids, counts = torch.unique(torch.as_tensor(recent, device=logits.device, dtype=torch.long),
+                                   return_counts=True)
+        ids = ids[(ids >= 0) & (ids < logits.shape[1])]
+        counts = counts[: ids.numel()]
+        row = logits[i]
+        vals = row[ids]
+        if p.repeat_penalty != 1.0:
+            vals = torch.where(vals > 0, vals / p.repeat_penalty, vals * p.repeat_penalty)
+        vals = vals - p.presence_penalty - p.frequency_penalty * counts.float()
+        row[ids] = vals
+    return logits
+
+
+def sample(logits: torch.Tensor, params: list, history: list = None, generators: list = None) -> torch.Tensor:
+    """Next token ids [B] (int64) from fp32 logits [B, V]."""
+    if all(p.greedy for p in params) and not any(
+            p.repeat_penalty != 1.0 or p.presence_penalty or p.frequency_penalty for p in params):
+        return argmax(logits)
+    logits = logits.clone()
+    if history is not None:
+        apply_penalties(logits, history, params)
+    out = torch.empty(logits.shape[0], dtype=torch.long, device=logits.device)
+    for i, p in enumerate(params):
+        row = logits[i]
+        if p.greedy:
+            out[i] = torch.argmax(row)
+            continue
+        row = row / p.temperature
+        if p.top_k and p.top_k > 0:
+            k = min(p.top_k, row.numel())
+            kth = torch.topk(row, k).values[-1]
+            row = row.masked_fill(row < kth, float("-inf"))
+        probs = torch.softmax(row, -1)
+        if p.min_p and p.min_p > 0:
+            probs = probs.masked_fill(probs < probs.max() * p.min_p, 0.0)
+        if p.top_p < 1.0:
+            sp, si = torch.sort(probs, descending=True)
+            cum = torch.cumsum(sp, -1)
+            drop = cum - sp > p.top_p
+            sp = sp.masked_fill(drop, 0.0)
+            probs = torch.zeros_like(probs).scatter_(0, si, sp)
+        probs = probs / probs.sum()
+        g = generators[i] if generators else None
+        out[i] = torch.multinomial(probs, 1, generator=g)[0]
+    return out
+
+
+def argmax(logits: torch.Tensor) -> torch.Tensor:
+    if logits.is_cuda:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+        vals = torch.empty(logits.shape[0], dtype=torch.float32, device=logits.device)
+        ops.argmax_rows(logits.contiguous(), out, vals, 0)
+        return out.long()
+    return torch.argmax(logits, dim=-1)

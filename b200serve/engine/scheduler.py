@@ -1,0 +1,281 @@
+"""Continuous-batching scheduler with chunked prefill and a paged KV cache.
+
+A request holds ``tokens`` (prompt + generated) and ``num_computed`` (how many
+of them have K/V in the cache). Each step:
+* admit waiting requests while batch slots and KV pages allow (prefix-cache
+  hits skip the matched full pages);
+* if some running request has more than one token to compute, run a *mixed*
+  step: every decode-ready request contributes its one token and prefilling
+  requests contribute chunks up to ``prefill_chunk`` tokens in total;
+  otherwise run a *decode* step (CUDA-graph path);
+* sample for every request whose computed range reached its last token.
+When pages run out the most recently admitted request is preempted: its pages
+are freed and it is recomputed later from its tokens (nothing is lost).
+
+The reference serialises requests (core/model_queue.py:55-66); this replaces
+that with in-replica continuous batching.
+"""
+
+from __future__ import annotations
+
+import itertools
+import threading
+import time
+from dataclasses import dataclass, field
+
+import torch
+
+from b200serve.engine.kv_cache import BLOCK, BlockAllocator
+from b200serve.engine.sampler import SamplingParams, sample
+
+_ids = itertools.count()
+
+
+@dataclass
+class Request:
+    prompt: list
+    params: SamplingParams
+    stop_ids: set = field(default_factory=set)
+    on_token: object = None          # callable(req, token_id) -> bool (True = stop now)
+    rid: str = field(default_factory=lambda: f"req-{next(_ids)}")
+    tokens: list = None
+    output: list = field(default_factory=list)
+    blocks: list = field(default_factory=list)
+    num_computed: int = 0
+    state: str = "waiting"
+    finish_reason: str = None
+    arrival: float = field(default_factory=time.perf_counter)
+    first_token_time: float = None
+    finish_time: float = None
+    aborted: bool = False
+    generator: object = None
+    registered: int = 0
+    prefix_hit: int = 0
+    done_event: threading.Event = field(default_factory=threading.Event)
+
+    def __post_init__(self):
+        if self.tokens is None:
+            self.tokens = list(self.prompt)
+
+    @property
+    def prompt_len(self) -> int:
+        return len(self.prompt)
+
+    @property
+    def ttft(self):
+        return None if self.first_token_time is None else self.first_token_time - self.arrival
+
+
+class Scheduler:
+    def __init__(self, runner, num_blocks: int, max_batch: int = 64, prefill_chunk: int = 8192,
+                 max_seq: int = 4096, prefix_cache: bool = True):
+        self.runner = runner
+        self.alloc = BlockAllocator(num_blocks, enable_prefix_cache=prefix_cache)
+        self.max_batch = max_batch
+        self.prefill_chunk = prefill_chunk
+        self.max_seq = max_seq
+        self.waiting = []
+        self.running = []
+        self.lock = threading.Lock()
+        self.stats = {"steps": 0, "decode_steps": 0, "mixed_steps": 0, "preemptions": 0,
+                      "generated": 0, "prefill_tokens": 0, "prefix_hit_tokens": 0}
+
+    # ------------------------------------------------------------ queue ops
+    def add(self, req: Request) -> Request:
+        if len(req.tokens) == 0:
+            raise ValueError("empty prompt")
+        if len(req.tokens) >= self.max_seq:
+            raise ValueError(f"prompt of {len(req.tokens)} tokens exceeds max_seq {self.max_seq}")
+        if req.params.seed is not None and not req.params.greedy:
+            dev = self.runner.device if self.runner.device.type == "cuda" else "cpu"
+            req.generator = torch.Generator(device=dev)
+            req.generator.manual_seed(int(req.params.seed))
+        with self.lock:
+            self.waiting.append(req)
+        return req
+
+    def abort(self, req: Request):
+        req.aborted = True
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    def metrics(self) -> dict:
+        return {**self.stats, "running": len(self.running), "waiting": len(self.waiting),
+                "kv_blocks_free": self.alloc.num_free, "kv_blocks_total": self.alloc.num_blocks}
+
+    # ------------------------------------------------------------ internals
+    def _blocks_needed(self, req: Request, upto: int) -> int:
+        return max(0, (upto + BLOCK - 1) // BLOCK - len(req.blocks))
+
+    def _admit(self):
+        with self.lock:
+            while self.waiting and len(self.running) < self.max_batch:
+                req = self.waiting[0]
+                if req.aborted:
+                    self.waiting.pop(0)
+                    self._finish(req, "abort")
+                    continue
+                matched, _ = self.alloc.match_prefix(req.tokens[:-1])
+                need = (len(req.tokens) + 1 + BLOCK - 1) // BLOCK - len(matched)
+                if need > self.alloc.num_free:
+                    self.alloc.release(matched)
+                    break
+                self.waiting.pop(0)
+                req.blocks = matched + self.alloc.allocate(need)
+                req.num_computed = len(matched) * BLOCK
+                req.prefix_hit = req.num_computed
+                req.registered = len(matched)
+                self.stats["prefix_hit_tokens"] += req.num_computed
+                req.state = "running"
+                self.running.append(req)
+
+    def _preempt_one(self, keep: Request) -> bool:
+        for victim in reversed(self.running):
+            if victim is keep:
+                continue
+            self.running.remove(victim)
+            self.alloc.release(victim.blocks)
+            victim.blocks = []
+            victim.num_computed = 0
+            victim.registered = 0
+            victim.state = "waiting"
+            with self.lock:
+                self.waiting.insert(0, victim)
+            self.stats["preemptions"] += 1
+            return True
+        return False
+
+    def _ensure_blocks(self, req: Request, upto: int) -> bool:
+        need = self._blocks_needed(req, upto)
+        while need > self.alloc.num_free:
+            if not self._preempt_one(req):
+                return False
+        if need:
+            req.blocks += self.alloc.allocate(need)
+        return True
+
+    def _finish(self, req: Request, reason: str):
+        req.state = "finished"
+        req.finish_reason = reason
+        req.finish_time = time.perf_counter()
+        if req.blocks:
+            self.alloc.register(req.blocks, req.tokens[: req.num_computed])
+            self.alloc.release(req.blocks)
+            req.blocks = []
+        req.done_event.set()
+
+    def _accept_token(self, req: Request, tok: int):
+        now = time.perf_counter()
+        if req.first_token_time is None:
+            req.first_token_time = now
+        req.tokens.append(tok)
+        req.output.append(tok)
+        self.stats["generated"] += 1
+        stop = False
+        if req.on_token is not None:
+            try:
+                stop = bool(req.on_token(req, tok))
+            except BaseException:  # the consumer is gone: stop this request
+                stop = True
+                req.aborted = True
+        if req.aborted:
+            self._finish(req, "abort")
+        elif tok in req.stop_ids and not req.params.ignore_eos:
+            self._finish(req, "stop")
+        elif stop:
+            self._finish(req, "stop")
+        elif len(req.output) >= req.params.max_tokens or len(req.tokens) >= self.max_seq:
+            self._finish(req, "length")
+
+    # ------------------------------------------------------------ step
+    def step(self) -> int:
+        """Run one forward pass. Returns the number of tokens sampled."""
+        self._admit()
+        for r in [r for r in self.running if r.aborted]:
+            self.running.remove(r)
+            self._finish(r, "abort")
+        if not self.running:
+            return 0
+        self.stats["steps"] += 1
+        if any(r.num_computed < len(r.tokens) - 1 for r in self.running):
+            return self._mixed_step()
+        return self._decode_step()
+
+    def _decode_step(self) -> int:
+        batch = []
+        for r in list(self.running):
+            if r not in self.running:
+                continue
+            if self._ensure_blocks(r, len(r.tokens)):
+                batch.append(r)
+        batch = [r for r in batch if r in self.running]
+        if not batch:
+            return 0
+        ids = [r.tokens[-1] for r in batch]
+        pos = [len(r.tokens) - 1 for r in batch]
+        slots = [r.blocks[p // BLOCK] * BLOCK + p % BLOCK for r, p in zip(batch, pos)]
+        lens = [p + 1 for p in pos]
+        greedy = all(r.params.greedy and r.params.repeat_penalty == 1.0 and not r.params.presence_penalty
+                     and not r.params.frequency_penalty for r in batch)
+        logits, toks = self.runner.decode(ids, pos, slots, [r.blocks for r in batch], lens, greedy=greedy)
+        if toks is None:
+            toks = self._sample(logits, batch)
+        toks = toks.tolist()
+        self.stats["decode_steps"] += 1
+        for r, t in zip(batch, toks):
+            r.num_computed = len(r.tokens)
+            self._accept_token(r, int(t))
+            if r.state == "finished":
+                self.running.remove(r)
+        return len(batch)
+
+    def _mixed_step(self) -> int:
+        budget = self.prefill_chunk
+        seqs, reqs = [], []
+        # decode-ready requests first (one token each), then prefill chunks
+        order = sorted(self.running, key=lambda r: 0 if r.num_computed == len(r.tokens) - 1 else 1)
+        for r in order:
+            if r not in self.running:
+                continue
+            remaining = len(r.tokens) - r.num_computed
+            if remaining <= 0:
+                continue
+            n = 1 if remaining == 1 else min(remaining, budget)
+            if n <= 0:
+                continue
+            if not self._ensure_blocks(r, r.num_computed + n):
+                continue
+            if r not in self.running:
+                continue
+            seqs.append({"ids": r.tokens[r.num_computed:r.num_computed + n], "start": r.num_computed,
+                         "block_table": r.blocks, "want_logits": r.num_computed + n == len(r.tokens)})
+            reqs.append((r, n))
+            if remaining > 1:
+                budget -= n
+                self.stats["prefill_tokens"] += n
+        # a preemption inside the loop may have removed an earlier entry
+        keep = [(s, rn) for s, rn in zip(seqs, reqs) if rn[0] in self.running]
+        if not keep:
+            return 0
+        seqs = [s for s, _ in keep]
+        reqs = [rn for _, rn in keep]
+        logits = self.runner.prefill(seqs)
+        self.stats["mixed_steps"] += 1
+        sample_reqs = [r for (r, n), s in zip(reqs, seqs) if s["want_logits"]]
+        for r, n in reqs:
+            r.num_computed += n
+        if not sample_reqs:
+            return 0
+        toks = self._sample(logits, sample_reqs).tolist()
+        for r, t in zip(sample_reqs, toks):
+            self._accept_token(r, int(t))
+            if r.state == "finished":
+                self.running.remove(r)
+        return len(sample_reqs)
+
+    def _sample(self, logits, reqs) -> torch.Tensor:
+        """``logits`` covers the whole vocabulary (the runner gathers tensor-parallel shards)."""
+        params = [r.params for r in reqs]
+        hist = [r.tokens for r in reqs]
+        return sample(logits, params, hist, [r.generator for r in reqs])

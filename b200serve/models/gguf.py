@@ -1,0 +1,422 @@
+"""GGUF files: reader, writer, and block quantisation for Q8_0 / Q4_K / Q6_K.
+
+Format (ggml GGUF v3, little endian): magic "GGUF", version, tensor count,
+metadata count, metadata key/values, tensor infos (name, dims innermost-first,
+type, offset), padding to ``general.alignment`` (32), tensor data.
+
+Block formats (per ggml, the same layouts the reference's CPU dequantiser
+restates in webgpu/src/model/gguf-dequant.ts:152-406):
+* Q8_0 (34 B / 32 weights): fp16 d, int8 q[32]; w = d * q.
+* Q4_K (144 B / 256): fp16 d, fp16 dmin, 12 bytes of 6-bit scales and mins for
+  8 sub-blocks of 32, 128 bytes of 4-bit codes (each 32-byte group holds two
+  sub-blocks: low nibbles the first, high nibbles the second);
+  w = d * sc[j] * q - dmin * m[j].
+* Q6_K (210 B / 256): 128 bytes low 4 bits, 64 bytes high 2 bits, int8 scales
+  for 16 sub-blocks of 16, fp16 d; w = d * sc[j] * (q - 32).
+The quantisers below are simple (min/max per sub-block, no iterative search):
+they produce valid files for random-init test models.
+"""
+
+from __future__ import annotations
+
+import struct
+from dataclasses import dataclass, field
+
+import numpy as np
+
+GGUF_MAGIC = 0x46554747
+GGML_F32, GGML_F16, GGML_Q8_0, GGML_Q4_K, GGML_Q5_K, GGML_Q6_K, GGML_BF16 = 0, 1, 8, 12, 13, 14, 30
+BLOCK_SIZE = {GGML_F32: 1, GGML_F16: 1, GGML_BF16: 1, GGML_Q8_0: 32, GGML_Q4_K: 256, GGML_Q5_K: 256,
+              GGML_Q6_K: 256}
+TYPE_SIZE = {GGML_F32: 4, GGML_F16: 2, GGML_BF16: 2, GGML_Q8_0: 34, GGML_Q4_K: 144, GGML_Q5_K: 176,
+             GGML_Q6_K: 210}
+TYPE_NAME = {GGML_F32: "F32", GGML_F16: "F16", GGML_BF16: "BF16", GGML_Q8_0: "Q8_0", GGML_Q4_K: "Q4_K",
+             GGML_Q5_K: "Q5_K", GGML_Q6_K: "Q6_K"}
+
+# metadata value types
+_U8, _I8, _U16, _I16, _U32, _I32, _F32, _BOOL, _STR, _ARR, _U64, _I64, _F64 = range(13)
+_SCALAR = {_U8: "<B", _I8: "<b", _U16: "<H", _I16: "<h", _U32: "<I", _I32: "<i", _F32: "<f", _BOOL: "<?",
+           _U64: "<Q", _I64: "<q", _F64: "<d"}
+
+
+@dataclass
+class GGUFTensor:
+    name: str
+    shape: tuple          # numpy order (outermost first): (rows, cols) for a matrix
+    ggml_type: int
+    offset: int           # absolute file offset of the data
+    nbytes: int
+
+
+@dataclass
+class GGUFFile:
+    path: str
+    version: int
+    metadata: dict = field(default_factory=dict)
+    tensors: dict = field(default_factory=dict)
+    alignment: int = 32
+
+    def raw(self, name: str) -> np.ndarray:
+        t = self.tensors[name]
+        return np.memmap(self.path, dtype=np.uint8, mode="r", offset=t.offset, shape=(t.nbytes,))
+
+    def dequantize(self, name: str) -> np.ndarray:
+        t = self.tensors[name]
+        return dequantize(self.raw(name), t.ggml_type, t.shape)
+
+
+class GGUFReadError(Exception):
+    pass
+
+
+def _read_value(f, vt):
+    if vt in _SCALAR:
+        fmt = _SCALAR[vt]
+        return struct.unpack(fmt, f.read(struct.calcsize(fmt)))[0]
+    if vt == _STR:
+        (n,) = struct.unpack("<Q", f.read(8))
+        return f.read(n).decode("utf-8", errors="replace")
+    if vt == _ARR:
+        (et,) = struct.unpack("<I", f.read(4))
+        (n,) = struct.unpack("<Q", f.read(8))
+        if et in _SCALAR and et != _BOOL:
+            fmt = _SCALAR[et]
+            sz = struct.calcsize(fmt)
+            return list(np.frombuffer(f.read(sz * n), dtype=np.dtype(fmt)).tolist())
+        return [_read_value(f, et) for _ in range(n)]
+    raise GGUFReadError(f"bad metadata type {vt}")
+
+
+def read_gguf_file(path: str, tensors: bool = True) -> GGUFFile:
+    with open(path, "rb") as f:
+        try:
+            magic, version = struct.unpack("<II", f.read(8))
+            if magic != GGUF_MAGIC:
+                raise GGUFReadError("not a GGUF file")
+            if version < 2:
+                raise GGUFReadError(f"GGUF version {version} unsupported")
+            n_t, n_kv = struct.unpack("<QQ", f.read(16))
+            meta = {}
+            for _ in range(n_kv):
+                (kl,) = struct.unpack("<Q", f.read(8))
+                key = f.read(kl).decode()
+                (vt,) = struct.unpack("<I", f.read(4))
+                meta[key] = _read_value(f, vt)
+            out = GGUFFile(path, version, meta, alignment=int(meta.get("general.alignment", 32)))
+            if not tensors:
+                return out
+            infos = []
+            for _ in range(n_t):
+                (nl,) = struct.unpack("<Q", f.read(8))
+                name = f.read(nl).decode()
+                (nd,) = struct.unpack("<I", f.read(4))
+                dims = struct.unpack(f"<{nd}Q", f.read(8 * nd))
+                tt, off = struct.unpack("<IQ", f.read(12))
+                infos.append((name, tuple(reversed(dims)), tt, off))
+        except struct.error as e:
+            raise GGUFReadError(f"truncated header: {e}") from None
+        base = f.tell()
+        base = (base + out.alignment - 1) // out.alignment * out.alignment
+    for name, shape, tt, off in infos:
+        n = int(np.prod(shape))
+        nb = n // BLOCK_SIZE.get(tt, 1) * TYPE_SIZE.get(tt, 0)
+        out.tensors[name] = GGUFTensor(name, shape, tt, base + off, nb)
+    return out
+
+
+def _write_value(f, v):
+    if isinstance(v, bool):
+        f.write(struct.pack("<I?", _BOOL, v))
+    elif isinstance(v, int):
+        f.write(struct.pack("<Iq", _I64, v) if v < 0 or v >= 2 ** 32 else struct.pack("<II", _U32, v))
+    elif isinstance(v, float):
+        f.write(struct.pack("<If", _F32, v))
+    elif isinstance(v, str):
+        b = v.encode()
+        f.write(struct.pack("<IQ", _STR, len(b)) + b)
+    elif isinstance(v, (list, tuple)):
+        if v and isinstance(v[0], str):
+            f.write(struct.pack("<IIQ", _ARR, _STR, len(v)))
+            for s in v:
+                b = s.encode()
+                f.write(struct.pack("<Q", len(b)) + b)
+        else:
+            is_f = v and isinstance(v[0], float)
+            f.write(struct.pack("<IIQ", _ARR, _F32 if is_f else _I32, len(v)))
+            f.write(np.asarray(v, dtype=np.float32 if is_f else np.int32).tobytes())
+    else:
+        raise TypeError(type(v))
+
+
+def write_gguf(path: str, metadata: dict, tensors: list, alignment: int = 32):
+    """``tensors``: list of (name, ggml_type, shape (numpy order), raw bytes)."""
+    with open(path, "wb") as f:
+        f.write(struct.pack("<IIQQ", GGUF_MAGIC, 3, len(tensors), len(metadata) + 1))
+        md = dict(metadata)
+        md["general.alignment"] = alignment
+        for k, v in md.items():
+            kb = k.encode()
+            f.write(struct.pack("<Q", len(kb)) + kb)
+            _write_value(f, v)
+        off = 0
+        offsets = []
+        for name, tt, shape, data in tensors:
+            offsets.append(off)
+            off += (len(data) + alignment - 1) // alignment * alignment
+        for (name, tt, shape, data), o in zip(tensors, offsets):
+            nb = name.encode()
+            dims = tuple(reversed(shape))
+            f.write(struct.pack("<Q", len(nb)) + nb + struct.pack("<I", len(dims)))
+            f.write(struct.pack(f"<{len(dims)}Q", *dims) + struct.pack("<IQ", tt, o))
+        pos = f.tell()
+        f.write(b"\0" * ((pos + alignment - 1) // alignment * alignment - pos))
+        for name, tt, shape, data in tensors:
+            f.write(data)
+            pad = (len(data) + alignment - 1) // alignment * alignment - len(data)
+            f.write(b"\0" * pad)
+
+
+# ------------------------------------------------------------------ quantisers
+def quantize_q8_0(x: np.ndarray) -> bytes:
+    b = x.astype(np.float32).reshape(-1, 32)
+    amax = np.abs(b).max(1)
+    d = amax / 127.0
+    inv = np.where(d > 0, 1.0 / np.where(d > 0, d, 1), 0)
+    q = np.clip(np.rint(b * inv[:, None]), -127, 127).astype(np.int8)
+    out = np.zeros(b.shape[0], dtype=[("d", "<f2"), ("q", "i1", 32)])
+    out["d"] = d.astype(np.float16)
+    out["q"] = q
+    return out.tobytes()
+
+
+def dequantize_q8_0(raw: np.ndarray) -> np.ndarray:
+    blk = np.frombuffer(raw, dtype=[("d", "<f2"), ("q", "i1", 32)])
+    return (blk["d"].astype(np.float32)[:, None] * blk["q"].astype(np.float32)).reshape(-1)
+
+
+def _pack_k4_scales(sc: np.ndarray, mn: np.ndarray) -> np.ndarray:
+    """sc, mn: [nb, 8] ints in 0..63 -> [nb, 12] bytes (ggml get_scale_min_k4 layout)."""
+    out = np.zeros((sc.shape[0], 12), dtype=np.uint8)
+    out[:, 0:4] = (sc[:, 0:4] & 63) | ((sc[:, 4:8] >> 4) << 6)
+    out[:, 4:8] = (mn[:, 0:4] & 63) | ((mn[:, 4:8] >> 4) << 6)
+    out[:, 8:12] = (sc[:, 4:8] & 15) | ((mn[:, 4:8] & 15) << 4)
+    return out
+
+
+def _unpack_k4_scales(s: np.ndarray):
+    s = s.astype(np.int32)
+    sc = np.zeros((s.shape[0], 8), dtype=np.int32)
+    mn = np.zeros_like(sc)
+    sc[:, 0:4] = s[:, 0:4] & 63
+    mn[:, 0:4] = s[:, 4:8] & 63
+    sc[:, 4:8] = (s[:, 8:12] & 15) | ((s[:, 0:4] >> 6) << 4)
+    mn[:, 4:8] = (s[:, 8:12] >> 4) | ((s[:, 4:8] >> 6) << 4)
+    return sc, mn
+
+
+_Q4K = [("d", "<f2"), ("dmin", "<f2"), ("scales", "u1", 12), ("qs", "u1", 128)]
+_Q6K = [("ql", "u1", 128), ("qh", "u1", 64), ("scales", "i1", 16), ("d", "<f2")]
+
+
+def quantize_q4_k(x: np.ndarray) -> bytes:
+    b = x.astype(np.float32).reshape(-1, 8, 32)
+    lo = np.minimum(b.min(2), 0.0)          # ggml keeps the min <= 0
+    hi = b.max(2)
+    scale = (hi - lo) / 15.0
+    mins = -lo
+    d = scale.max(1) / 63.0
+    dmin = mins.max(1) / 63.0
+    d16, dm16 = d.astype(np.float16), dmin.astype(np.float16)
+    d, dmin = d16.astype(np.float32), dm16.astype(np.float32)
+    sc = np.clip(np.rint(np.where(d[:, None] > 0, scale / np.where(d[:, None] > 0, d[:, None], 1), 0)), 0,
+                 63).astype(np.int32)
+    mn = np.clip(np.rint(np.where(dmin[:, None] > 0, mins / np.where(dmin[:, None] > 0, dmin[:, None], 1), 0)),
+                 0, 63).astype(np.int32)
+    eff_s = d[:, None] * sc
+    eff_m = dmin[:, None] * mn
+    q = np.where(eff_s[..., None] > 0,
+                 np.rint((b + eff_m[..., None]) / np.where(eff_s[..., None] > 0, eff_s[..., None], 1)), 0)
+    q = np.clip(q, 0, 15).astype(np.uint8)                 # [nb, 8, 32]
+    qs = (q[:, 0::2, :] | (q[:, 1::2, :] << 4)).reshape(-1, 128)
+    out = np.zeros(b.shape[0], dtype=_Q4K)
+    out["d"], out["dmin"] = d16, dm16
+    out["scales"] = _pack_k4_scales(sc, mn)
+    out["qs"] = qs
+    return out.tobytes()
+
+
+def dequantize_q4_k(raw: np.ndarray) -> np.ndarray:
+    blk = np.frombuffer(raw, dtype=_Q4K)
+    d = blk["d"].astype(np.float32)[:, None]
+    dmin = blk["dmin"].astype(np.float32)[:, None]
+    sc, mn = _unpack_k4_scales(blk["scales"])
+    qs = blk["qs"].reshape(-1, 4, 32)
+    q = np.empty((blk.shape[0], 8, 32), dtype=np.float32)
+    q[:, 0::2, :] = qs & 15
+    q[:, 1::2, :] = qs >> 4
+    w = (d * sc)[..., None] * q - (dmin * mn)[..., None]
+    return w.reshape(-1)
+
+
+def quantize_q6_k(x: np.ndarray) -> bytes:
+    b = x.astype(np.float32).reshape(-1, 16, 16)
+    amax = np.abs(b).max(2)
+    sub = amax / 32.0
+    d = sub.max(1) / 127.0
+    d16 = d.astype(np.float16)
+    d = d16.astype(np.float32)
+    sc = np.clip(np.rint(np.where(d[:, None] > 0, sub / np.where(d[:, None] > 0, d[:, None], 1), 0)), -128,
+                 127).astype(np.int32)
+    eff = d[:, None] * sc
+    q = np.where(eff[..., None] != 0, np.rint(b / np.where(eff[..., None] != 0, eff[..., None], 1)), 0)
+    q = (np.clip(q, -32, 31) + 32).astype(np.uint8).reshape(-1, 2, 128)   # two halves of 128
+    ql = np.zeros((q.shape[0], 2, 64), dtype=np.uint8)
+    qh = np.zeros((q.shape[0], 2, 32), dtype=np.uint8)
+    for h in range(2):
+        v = q[:, h]
+        ql[:, h, :32] = (v[:, 0:32] & 15) | ((v[:, 64:96] & 15) << 4)
+        ql[:, h, 32:] = (v[:, 32:64] & 15) | ((v[:, 96:128] & 15) << 4)
+        qh[:, h] = ((v[:, 0:32] >> 4) & 3) | (((v[:, 32:64] >> 4) & 3) << 2) | \
+            (((v[:, 64:96] >> 4) & 3) << 4) | (((v[:, 96:128] >> 4) & 3) << 6)
+    out = np.zeros(q.shape[0], dtype=_Q6K)
+    out["ql"] = ql.reshape(-1, 128)
+    out["qh"] = qh.reshape(-1, 64)
+    out["scales"] = sc.astype(np.int8)
+    out["d"] = d16
+    return out.tobytes()
+
+
+def dequantize_q6_k(raw: np.ndarray) -> np.ndarray:
+    blk = np.frombuffer(raw, dtype=_Q6K)
+    d = blk["d"].astype(np.float32)
+    sc = blk["scales"].astype(np.float32)
+    ql = blk["ql"].reshape(-1, 2, 64).astype(np.int32)
+    qh = blk["qh"].reshape(-1, 2, 32).astype(np.int32)
+    q = np.empty((blk.shape[0], 2, 128), dtype=np.int32)
+    q[:, :, 0:32] = (ql[:, :, :32] & 15) | ((qh & 3) << 4)
+    q[:, :, 32:64] = (ql[:, :, 32:] & 15) | (((qh >> 2) & 3) << 4)
+    q[:, :, 64:96] = (ql[:, :, :32] >> 4) | (((qh >> 4) & 3) << 4)
+    q[:, :, 96:128] = (ql[:, :, 32:] >> 4) | (((qh >> 6) & 3) << 4)
+    q = (q - 32).reshape(-1, 16, 16).astype(np.float32)
+    return (d[:, None, None] * sc.reshape(-1, 16)[..., None] * q).reshape(-1)
+
+
+QUANTIZE = {GGML_Q8_0: quantize_q8_0, GGML_Q4_K: quantize_q4_k, GGML_Q6_K: quantize_q6_k}
+
+
+def quantize(x: np.ndarray, ggml_type: int) -> bytes:
+    if ggml_type == GGML_F32:
+        return x.astype(np.float32).tobytes()
+    if ggml_type == GGML_F16:
+        return x.astype(np.float16).tobytes()
+    if ggml_type == GGML_BF16:
+        import torch
+        return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).bfloat16().view(torch.int16).numpy().tobytes()
+    return QUANTIZE[ggml_type](x)
+
+
+def dequantize(raw: np.ndarray, ggml_type: int, shape) -> np.ndarray:
+    raw = np.asarray(raw)
+    if ggml_type == GGML_F32:
+        out = np.frombuffer(raw, dtype=np.float32)
+    elif ggml_type == GGML_F16:
+        out = np.frombuffer(raw, dtype=np.float16).astype(np.float32)
+    elif ggml_type == GGML_BF16:
+        out = (np.frombuffer(raw, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+    elif ggml_type == GGML_Q8_0:
+        out = dequantize_q8_0(raw)
+    elif ggml_type == GGML_Q4_K:
+        out = dequantize_q4_k(raw)
+    elif ggml_type == GGML_Q6_K:
+        out = dequantize_q6_k(raw)
+    else:
+        raise NotImplementedError(f"ggml type {ggml_type}")
+    return out.reshape(shape)
+
+
+# ------------------------------------------------------------------ model I/O
+_LAYER_MAP = {"q": "attn_q", "k": "attn_k", "v": "attn_v", "o": "attn_output", "gate": "ffn_gate", "up": "ffn_up",
+              "down": "ffn_down", "input_norm": "attn_norm", "post_norm": "ffn_norm", "q_norm": "attn_q_norm",
+              "k_norm": "attn_k_norm", "q_bias": "attn_q.bias", "k_bias": "attn_k.bias", "v_bias": "attn_v.bias"}
+
+
+def q4_k_m_type(key: str) -> int:
+    """Q4_K_M mix: attn_v and ffn_down in Q6_K, everything else Q4_K (norms in F32)."""
+    return GGML_Q6_K if key in ("v", "down") else GGML_Q4_K
+
+
+def export_gguf(path: str, cfg, weights_full: dict, layer_full, mix: str = "Q4_K_M"):
+    """Write a GGUF of a dense model. ``weights_full``: embed, lm_head, final_norm (numpy);
+    ``layer_full(i)``: unsharded layer dict of numpy arrays (HF orientation [out, in])."""
+    arch = "qwen3" if cfg.qk_norm else "qwen2"
+    md = {"general.architecture": arch, "general.name": cfg.name, "general.file_type": 15,
+          f"{arch}.block_count": cfg.num_layers, f"{arch}.context_length": cfg.max_position,
+          f"{arch}.embedding_length": cfg.hidden_size, f"{arch}.feed_forward_length": cfg.intermediate_size,
+          f"{arch}.attention.head_count": cfg.num_heads, f"{arch}.attention.head_count_kv": cfg.num_kv_heads,
+          f"{arch}.attention.key_length": cfg.head_dim, f"{arch}.attention.value_length": cfg.head_dim,
+          f"{arch}.rope.freq_base": float(cfg.rope_theta),
+          f"{arch}.attention.layer_norm_rms_epsilon": float(cfg.rms_eps), "tokenizer.ggml.model": "gpt2"}
+    tensors = []
+    tt = GGML_Q8_0 if mix == "Q4_K_M" else GGML_F32
+    tensors.append(("token_embd.weight", tt, weights_full["embed"].shape, quantize(weights_full["embed"], tt)))
+    tensors.append(("output.weight", tt, weights_full["lm_head"].shape, quantize(weights_full["lm_head"], tt)))
+    tensors.append(("output_norm.weight", GGML_F32, weights_full["final_norm"].shape,
+                    quantize(weights_full["final_norm"], GGML_F32)))
+    for i in range(cfg.num_layers):
+        d = layer_full(i)
+        for key, arr in d.items():
+            if key not in _LAYER_MAP:
+                continue
+            gname = f"blk.{i}.{_LAYER_MAP[key]}" + ("" if key.endswith("bias") else ".weight")
+            if arr.ndim == 1:
+                t = GGML_F32
+            else:
+                t = q4_k_m_type(key) if mix == "Q4_K_M" else GGML_F32
+            tensors.append((gname, t, arr.shape, quantize(arr, t)))
+    write_gguf(path, md, tensors)
+
+
+def config_from_gguf(path: str):
+    from b200serve.models.config import ModelConfig
+    g = read_gguf_file(path, tensors=True)
+    m = g.metadata
+    arch = m["general.architecture"]
+    a = lambda k, d=0: m.get(f"{arch}.{k}", d)
+    emb = g.tensors["token_embd.weight"].shape
+    heads = int(a("attention.head_count"))
+    hd = int(a("attention.key_length", 0)) or int(a("embedding_length")) // heads
+    return ModelConfig(name=str(m.get("general.name", "gguf")), vocab_size=emb[0], hidden_size=int(a("embedding_length")),
+                       num_layers=int(a("block_count")), num_heads=heads,
+                       num_kv_heads=int(a("attention.head_count_kv", heads)), head_dim=hd,
+                       intermediate_size=int(a("feed_forward_length")),
+                       rms_eps=float(a("attention.layer_norm_rms_epsilon", 1e-6)),
+                       rope_theta=float(a("rope.freq_base", 1e6)), attn_bias=arch == "qwen2",
+                       qk_norm=arch in ("qwen3", "qwen3moe"), tie_embeddings="output.weight" not in g.tensors,
+                       max_position=int(a("context_length", 40960)))
+
+
+def load_gguf_weights(cfg, path: str, **kw):
+    """Dequantise a GGUF checkpoint into the engine's bf16 layout (kernel-side
+    quantised weights are handled by QuantLinear in ops.gguf_ops)."""
+    import torch
+    from b200serve.models.weights import build_weights
+    g = read_gguf_file(path)
+    inv = {v: k for k, v in _LAYER_MAP.items()}
+
+    def T(name):
+        return torch.from_numpy(np.array(g.dequantize(name), dtype=np.float32))
+
+    def layer(i):
+        d = {}
+        pre = f"blk.{i}."
+        for name in g.tensors:
+            if name.startswith(pre):
+                rest = name[len(pre):]
+                base = rest[:-len(".weight")] if rest.endswith(".weight") else rest
+                if base in inv:
+                    d[inv[base]] = T(name)
+        return d
+
+    embed = T("token_embd.weight")
+    lm = T("output.weight") if "output.weight" in g.tensors else embed
+    return build_weights(cfg, layer, embed, lm, T("output_norm.weight"), **kw)

@@ -64,8 +64,23 @@ def extension_path() -> str:
     return built_library_path()
 
 
-def _cuda(t: torch.Tensor) -> bool:
-    return t.is_cuda
+_launches = [0]
+
+
+def reset_launch_count():
+    _launches[0] = 0
+
+
+def launch_count() -> int:
+    """Kernels of this extension launched since the last reset (counted at the call sites)."""
+    return _launches[0]
+
+
+def _cuda(t: torch.Tensor, n: int = 1) -> bool:
+    if t.is_cuda:
+        _launches[0] += n
+        return True
+    return False
 
 
 # ------------------------------------------------------------------ RMSNorm
@@ -251,7 +266,7 @@ class AttnWorkspace:
 def paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, scale, tps=256, nsplit=1,
                            workspace=None, out=None):
     """One query token per sequence. q [B, nq, hd]; seq_lens include the new token."""
-    if _cuda(q):
+    if _cuda(q, 2 if nsplit > 1 else 1):
         out = out if out is not None else torch.empty_like(q)
         if nsplit > 1:
             assert workspace is not None and workspace.max_splits >= nsplit
@@ -322,6 +337,17 @@ def paged_prefill_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start
         out.copy_(res)
         return out
     return res
+
+
+def argmax_rows(logits, out_idx, out_val, index_offset=0):
+    """Row-wise argmax (lowest index on ties) of fp32 logits into int32 ``out_idx``."""
+    _cuda(logits)
+    ext().argmax_rows(logits, out_idx, out_val, int(index_offset))
+
+
+def argmax_merge(vals, idx, out):
+    _cuda(vals)
+    ext().argmax_merge(vals, idx, out)
 
 
 def gemm_error_flag(reset: bool = True) -> int:

@@ -21,6 +21,8 @@ void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optiona
              c10::optional<torch::Tensor> residual, torch::Tensor ws, torch::Tensor counters, int64_t epi,
              int64_t force_splits);
 int64_t gemm_error_flag(bool reset);
+void argmax_rows(torch::Tensor logits, torch::Tensor out_idx, torch::Tensor out_val, int64_t index_offset);
+void argmax_merge(torch::Tensor vals, torch::Tensor idx, torch::Tensor out);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "b200serve sm_100a kernels";
@@ -33,4 +35,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_plan", &gemm_plan);
   m.def("gemm_tc", &gemm_tc);
   m.def("gemm_error_flag", &gemm_error_flag);
+  m.def("argmax_rows", &argmax_rows);
+  m.def("argmax_merge", &argmax_merge);
 }

@@ -349,7 +349,8 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi, int
   const int kb_total = (int)((K + 63) / 64);
   const int tiles = m_tiles * n_tiles;
   int best_s = 1, best_kbp = kb_total;
-  if (tiles < num_sms) {
+  if (m_tiles * BN <= 256) {
+    // decode-sized M: weight streaming, balance the busiest SM with split-K
     double best = -1.0;
     for (int s = 1; s <= 32; ++s) {
       const int kbp = (kb_total + s - 1) / s;

@@ -1,0 +1,134 @@
+"""Lock-step execution of the model runner on every tensor-parallel rank.
+
+Rank 0 owns the scheduler. Before each forward it broadcasts a fixed-size
+header (op, sizes, flags) and an int32 payload with the step's inputs; worker
+ranks (``worker_loop``) receive them and make the identical runner call, so
+every rank issues the same kernels and collectives in the same order.
+Logits that rank 0 needs for sampling are gathered collectively inside the
+step on all ranks.
+"""
+
+from __future__ import annotations
+
+import torch
+
+OP_DECODE, OP_PREFILL, OP_STOP, OP_LOOP = 1, 2, 3, 4
+HDR = 8
+
+
+class BroadcastRunner:
+    def __init__(self, inner, comm):
+        self.inner = inner
+        self.comm = comm
+        self.device = inner.device
+        self.vocab_start = 0   # logits handed to the sampler are gathered (full vocabulary)
+        self.hdr = torch.zeros(HDR, dtype=torch.int64, device=inner.device)
+
+    def __getattr__(self, name):
+        return getattr(self.inner, name)
+
+    def _send(self, header, payload: torch.Tensor = None):
+        h = torch.tensor(header + [0] * (HDR - len(header)), dtype=torch.int64)
+        self.hdr.copy_(h)
+        self.comm.broadcast(self.hdr, 0)
+        if payload is not None:
+            self.comm.broadcast(payload, 0)
+
+    def decode(self, ids, pos, slots, block_tables, lens, greedy=True):
+        B = len(ids)
+        bucket, _ = self.inner.load_decode_inputs(ids, pos, slots, block_tables, lens)
+        n = bucket * (4 + self.inner.max_blocks)
+        self._send([OP_DECODE, B, bucket, int(greedy)], self.inner.s_pack[:n])
+        return _decode_after_inputs(self.inner, self.comm, B, bucket, greedy)
+
+    def prefill(self, seqs):
+        flat = [len(seqs)]
+        for s in seqs:
+            flat += [len(s["ids"]), s["start"], int(s.get("want_logits", True)), len(s["block_table"])]
+            flat += list(s["ids"]) + list(s["block_table"])
+        payload = torch.as_tensor(flat, dtype=torch.int32).to(self.device)
+        self._send([OP_PREFILL, payload.numel()], payload)
+        logits = self.inner.prefill(seqs)
+        return self.comm.gather_vocab(logits)
+
+    def decode_loop(self, ids, pos, slots, block_tables, lens, warmup, steps):
+        B = len(ids)
+        bucket, _ = self.inner.load_decode_inputs(ids, pos, slots, block_tables, lens)
+        n = bucket * (4 + self.inner.max_blocks)
+        self._send([OP_LOOP, B, bucket, warmup, steps], self.inner.s_pack[:n])
+        _unpack_static(self.inner, bucket)
+        return self.inner.loop_body(B, bucket, warmup, steps)
+
+    def shutdown_workers(self):
+        self._send([OP_STOP])
+
+
+def _unpack_static(runner, bucket):
+    mb = runner.max_blocks
+    dv = runner.s_pack[: bucket * (4 + mb)].view(bucket, 4 + mb)
+    runner.s_ids[:bucket].copy_(dv[:, 0])
+    runner.s_pos[:bucket].copy_(dv[:, 1])
+    runner.s_slots[:bucket].copy_(dv[:, 2])
+    runner.s_lens[:bucket].copy_(dv[:, 3])
+    runner.s_bt[:bucket].copy_(dv[:, 4:])
+
+
+def _decode_after_inputs(runner, comm, B, bucket, greedy):
+    """Unpack the static inputs (already in s_pack) and run the step."""
+    _unpack_static(runner, bucket)
+    if runner.use_graphs:
+        key = (bucket, greedy)
+        if key not in runner.graphs:
+            runner.capture(bucket, greedy)
+        runner.graphs[key].replay()
+        logits, toks = runner.graph_out[key]
+    else:
+        logits, toks = runner._decode_body(bucket, greedy)
+    if toks is None:
+        logits = comm.gather_vocab(logits[:B])
+        return logits, None
+    return logits[:B], toks[:B]
+
+
+def _unpack_prefill(flat):
+    n = flat[0]
+    i = 1
+    seqs = []
+    for _ in range(n):
+        L, start, want, nb = flat[i:i + 4]
+        i += 4
+        ids = flat[i:i + L]
+        i += L
+        bt = flat[i:i + nb]
+        i += nb
+        seqs.append({"ids": ids, "start": start, "want_logits": bool(want), "block_table": bt})
+    return seqs
+
+
+def worker_loop(runner, comm):
+    """Serve rank 0's step broadcasts until OP_STOP."""
+    hdr = torch.zeros(HDR, dtype=torch.int64, device=runner.device)
+    while True:
+        comm.broadcast(hdr, 0)
+        h = hdr.tolist()
+        op = h[0]
+        if op == OP_STOP:
+            return
+        if op == OP_DECODE:
+            B, bucket, greedy = h[1], h[2], bool(h[3])
+            n = bucket * (4 + runner.max_blocks)
+            comm.broadcast(runner.s_pack[:n], 0)
+            _decode_after_inputs(runner, comm, B, bucket, greedy)
+        elif op == OP_LOOP:
+            B, bucket, warmup, steps = h[1], h[2], h[3], h[4]
+            n = bucket * (4 + runner.max_blocks)
+            comm.broadcast(runner.s_pack[:n], 0)
+            _unpack_static(runner, bucket)
+            runner.loop_body(B, bucket, warmup, steps)
+        elif op == OP_PREFILL:
+            payload = torch.empty(h[1], dtype=torch.int32, device=runner.device)
+            comm.broadcast(payload, 0)
+            logits = runner.prefill(_unpack_prefill(payload.tolist()))
+            comm.gather_vocab(logits)
+        else:
+            raise RuntimeError(f"unknown step op {op}")
