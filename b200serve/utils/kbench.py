@@ -86,9 +86,23 @@ def bench_attn():
     return out
 
 
+def run_one(M, N, K, iters=5):
+    """A few launches of one GEMM shape (small case for an ncu capture)."""
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+    y = ops.linear(x, w)
+    for _ in range(iters):
+        ops.linear(x, w, out=y)
+    torch.cuda.synchronize()
+    print(json.dumps({"case": "one", "M": M, "N": N, "K": K, "ok": True}))
+
+
 if __name__ == "__main__":
     what = sys.argv[1] if len(sys.argv) > 1 else "all"
     ops.ext()
+    if what == "one":
+        run_one(*[int(v) for v in sys.argv[2:5]])
+        sys.exit(0)
     if what in ("gemm", "all"):
         bench_gemm()
     if what in ("attn", "all"):

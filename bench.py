@@ -281,7 +281,8 @@ def _synthetic_hf_tokenizer(vocab):
     concatenates message contents, so a prompt of ids round-trips exactly."""
     from tokenizers import Tokenizer, models, pre_tokenizers, decoders
     from transformers import PreTrainedTokenizerFast
-    vocab_map = {f"t{i}": i for i in range(vocab - 1)}
+    vocab_map = {f"t{i}": i for i in range(vocab - 2)}
+    vocab_map["abcdef"] = vocab - 2     # the probe string HF's stop-string matcher encodes
     vocab_map["<unk>"] = vocab - 1
     tk = Tokenizer(models.WordLevel(vocab=vocab_map, unk_token="<unk>"))
     tk.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
