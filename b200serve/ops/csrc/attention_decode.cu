@@ -247,3 +247,104 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tenso
     B200_CHECK_CUDA(cudaGetLastError());
   }
 }
+
+// ---------------------------------------------------------------------------
+// Entry point without device allocation (declared in noalloc.h; no counterpart
+// in the reference). The split-KV partials go to a fixed array compiled into
+// this file instead of a caller- or framework-allocated workspace.
+// ---------------------------------------------------------------------------
+#include <mutex>
+#include <stdio.h>
+#include "noalloc.h"
+
+namespace b200 {
+
+static __device__ __align__(256) float g_noalloc_scratch[B200_NOALLOC_MAX_ACC_FLOATS + B200_NOALLOC_MAX_ML_FLOATS];
+
+constexpr int kNoAllocMaxDevices = 64;
+static float* g_noalloc_ptr[kNoAllocMaxDevices] = {nullptr};
+static cudaError_t g_noalloc_setup_err[kNoAllocMaxDevices] = {cudaSuccess};
+static std::once_flag g_noalloc_once[kNoAllocMaxDevices];
+static thread_local char g_noalloc_msg[256] = "";
+
+static int noalloc_fail(int code, const char* fmt, long a = 0, long b = 0) {
+  snprintf(g_noalloc_msg, sizeof(g_noalloc_msg), fmt, a, b);
+  return code;
+}
+
+}  // namespace b200
+
+extern "C" __attribute__((visibility("default"))) const char* b200_noalloc_last_error(void) {
+  return b200::g_noalloc_msg;
+}
+
+extern "C" __attribute__((visibility("default"))) int b200_paged_decode_attention_noalloc(
+    const void* q, const void* k_cache, const void* v_cache, const int* block_tables, const int* seq_lens,
+    void* out, int B, int nq, int nkv, int head_dim, int max_blocks, float scale, int tokens_per_split, int nsplit,
+    cudaStream_t stream) {
+  using namespace b200;
+  g_noalloc_msg[0] = '\0';
+  if (B < 0 || nq <= 0 || nkv <= 0 || nq % nkv != 0 || nsplit < 1 || tokens_per_split <= 0 ||
+      tokens_per_split % kPage != 0)
+    return noalloc_fail(1, "invalid shape (B=%ld, nsplit=%ld)", B, nsplit);
+  const int G = nq / nkv;
+  const long need_acc = (long)B * nkv * nsplit * G * head_dim;
+  const long need_ml = (long)B * nkv * nsplit * G * 2;
+  if (need_acc > (long)B200_NOALLOC_MAX_ACC_FLOATS)
+    return noalloc_fail(2, "scratch limit: needs %ld accumulator floats, maximum is %ld", need_acc,
+                        (long)B200_NOALLOC_MAX_ACC_FLOATS);
+  if (need_ml > (long)B200_NOALLOC_MAX_ML_FLOATS)
+    return noalloc_fail(2, "scratch limit: needs %ld max/sum floats, maximum is %ld", need_ml,
+                        (long)B200_NOALLOC_MAX_ML_FLOATS);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return noalloc_fail(3, "cudaGetDevice failed (%ld)", (long)e);
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return noalloc_fail(3, "device %ld out of range", dev);
+  // once per device, with that device current: resolve the device address of the array
+  std::call_once(g_noalloc_once[dev], [dev] {
+    void* p = nullptr;
+    g_noalloc_setup_err[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  });
+  if (g_noalloc_setup_err[dev] != cudaSuccess || g_noalloc_ptr[dev] == nullptr)
+    return noalloc_fail(4, "cudaGetSymbolAddress failed on device %ld (error %ld)", dev,
+                        (long)g_noalloc_setup_err[dev]);
+  if (B == 0) return 0;
+  float* acc = g_noalloc_ptr[dev];
+  float* ml = acc + B200_NOALLOC_MAX_ACC_FLOATS;
+  const float sl2 = scale * 1.4426950408889634f;
+  dim3 grid(nsplit, nkv, B);
+  auto qp = reinterpret_cast<const __nv_bfloat16*>(q);
+  auto kp = reinterpret_cast<const __nv_bfloat16*>(k_cache);
+  auto vp = reinterpret_cast<const __nv_bfloat16*>(v_cache);
+  auto op = reinterpret_cast<__nv_bfloat16*>(out);
+  float* pa = nsplit > 1 ? acc : nullptr;
+  float* pm = nsplit > 1 ? ml : nullptr;
+#define B200_NA(HDV, GV)                                                                                \
+  paged_decode_kernel<HDV, GV><<<grid, kAttnWarps * 32, 0, stream>>>(qp, kp, vp, block_tables, seq_lens, \
+                                                                    max_blocks, nkv, sl2, tokens_per_split, pa, pm, op, nsplit)
+  if (head_dim == 128 && G == 4) B200_NA(128, 4);
+  else if (head_dim == 128 && G == 8) B200_NA(128, 8);
+  else if (head_dim == 128 && G == 2) B200_NA(128, 2);
+  else if (head_dim == 128 && G == 1) B200_NA(128, 1);
+  else if (head_dim == 64 && G == 2) B200_NA(64, 2);
+  else if (head_dim == 64 && G == 1) B200_NA(64, 1);
+  else if (head_dim == 64 && G == 4) B200_NA(64, 4);
+  else return noalloc_fail(5, "unsupported head_dim %ld with group %ld", head_dim, G);
+#undef B200_NA
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return noalloc_fail(6, "attention launch failed (error %ld)", (long)e);
+  if (nsplit > 1) {
+    const int threads = 128;
+    const int blocks = (B * nq * 32 + threads - 1) / threads;
+    if (head_dim == 128)
+      paged_decode_combine_kernel<128><<<blocks, threads, 0, stream>>>(pa, pm, seq_lens, op, B, nkv, G, nsplit,
+                                                                       tokens_per_split);
+    else
+      paged_decode_combine_kernel<64><<<blocks, threads, 0, stream>>>(pa, pm, seq_lens, op, B, nkv, G, nsplit,
+                                                                      tokens_per_split);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return noalloc_fail(6, "combine launch failed (error %ld)", (long)e);
+  }
+  return 0;
+}
