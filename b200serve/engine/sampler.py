@@ -76,8 +76,45 @@ def apply_penalties(logits: torch.Tensor, history: list, params: list) -> torch.
     return logits
 
 
-def sample(logits: torch.Tensor, params: list, history: list = None, generators: list = None) -> torch.Tensor:
+def sample_cuda(logits: torch.Tensor, params: list, history: list, seeds: list, steps: list) -> torch.Tensor:
+    """GPU path: one kernel applies penalties and draws (ops/csrc/sampling.cu)."""
+    import collections
+    B = logits.shape[0]
+    logits = logits.contiguous()
+    need_pen = [p.repeat_penalty != 1.0 or p.presence_penalty or p.frequency_penalty for p in params]
+    pen = None
+    if any(need_pen):
+        rows = []
+        for p, hist, need in zip(params, history, need_pen):
+            if not need or not hist:
+                rows.append({})
+                continue
+            recent = hist[-p.repeat_last_n:] if p.repeat_last_n > 0 else hist
+            rows.append(collections.Counter(recent))
+        P = max(1, max(len(r) for r in rows))
+        ids = torch.full((B, P), -1, dtype=torch.int32)
+        cnt = torch.zeros((B, P), dtype=torch.float32)
+        vals = torch.tensor([[p.repeat_penalty, p.presence_penalty, p.frequency_penalty] for p in params],
+                            dtype=torch.float32)
+        for i, r in enumerate(rows):
+            if r:
+                ks = list(r.keys())
+                ids[i, :len(ks)] = torch.tensor(ks, dtype=torch.int32)
+                cnt[i, :len(ks)] = torch.tensor([r[k] for k in ks], dtype=torch.float32)
+        dev = logits.device
+        pen = (ids.to(dev), cnt.to(dev), vals.to(dev))
+    args = ([p.temperature if not p.greedy else 0.0 for p in params], [p.top_k for p in params],
+            [p.top_p for p in params], [p.min_p for p in params], seeds, steps)
+    if pen is None:
+        return ops.sample_rows(logits, *args).long()
+    return ops.sample_rows(logits, *args, *pen).long()
+
+
+def sample(logits: torch.Tensor, params: list, history: list = None, generators: list = None,
+           seeds: list = None, steps: list = None) -> torch.Tensor:
     """Next token ids [B] (int64) from fp32 logits [B, V]."""
+    if logits.is_cuda and seeds is not None:
+        return sample_cuda(logits, params, history or [[] for _ in params], seeds, steps)
     if all(p.greedy for p in params) and not any(
             p.repeat_penalty != 1.0 or p.presence_penalty or p.frequency_penalty for p in params):
         return argmax(logits)

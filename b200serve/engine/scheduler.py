@@ -19,6 +19,7 @@ that with in-replica continuous batching.
 from __future__ import annotations
 
 import itertools
+import os
 import threading
 import time
 from dataclasses import dataclass, field
@@ -51,6 +52,7 @@ class Request:
     generator: object = None
     registered: int = 0
     prefix_hit: int = 0
+    seed: int = 0
     done_event: threading.Event = field(default_factory=threading.Event)
 
     def __post_init__(self):
@@ -86,9 +88,12 @@ class Scheduler:
             raise ValueError("empty prompt")
         if len(req.tokens) >= self.max_seq:
             raise ValueError(f"prompt of {len(req.tokens)} tokens exceeds max_seq {self.max_seq}")
-        if req.params.seed is not None and not req.params.greedy:
-            dev = self.runner.device if self.runner.device.type == "cuda" else "cpu"
-            req.generator = torch.Generator(device=dev)
+        if req.params.seed is not None:
+            req.seed = int(req.params.seed)
+        else:
+            req.seed = int.from_bytes(os.urandom(8), "little")
+        if req.params.seed is not None and not req.params.greedy and self.runner.device.type != "cuda":
+            req.generator = torch.Generator(device="cpu")
             req.generator.manual_seed(int(req.params.seed))
         with self.lock:
             self.waiting.append(req)
@@ -278,4 +283,6 @@ class Scheduler:
         """``logits`` covers the whole vocabulary (the runner gathers tensor-parallel shards)."""
         params = [r.params for r in reqs]
         hist = [r.tokens for r in reqs]
+        if logits.is_cuda:
+            return sample(logits, params, hist, seeds=[r.seed for r in reqs], steps=[len(r.output) for r in reqs])
         return sample(logits, params, hist, [r.generator for r in reqs])

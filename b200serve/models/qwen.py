@@ -50,6 +50,12 @@ class NoComm:
     world = 1
     rank = 0
 
+    def begin_step(self):
+        pass
+
+    def linear_reduce(self, x, w, tag):
+        return [ops.linear(x, w)]
+
     def reduce_parts(self, t: torch.Tensor, tag: str):
         return [t]
 
@@ -73,9 +79,27 @@ class Decoder:
         self.cos_sin = ops.rope_cos_sin(cfg.head_dim, cfg.max_position, cfg.rope_theta, self.device)
         self.attn_ws = None
         self.moe = None
+        if self.device.type == "cuda":
+            self.pack_weights()
         if cfg.is_moe:
             from b200serve.models.moe import MoEBlock
             self.moe = MoEBlock(cfg, weights, comm=self.comm, device=self.device)
+
+    def pack_weights(self):
+        """Re-lay every GEMM weight tile-contiguous (ops.PackedWeight), in place, one at a time."""
+        w = self.w
+        for lw in w.layers:
+            for name in ("qkv", "o", "gate_up", "down", "router"):
+                t = getattr(lw, name)
+                if isinstance(t, torch.Tensor):
+                    setattr(lw, name, ops.pack_weight(t))
+            del t
+        if isinstance(w.lm_head, torch.Tensor) and w.lm_head.data_ptr() != w.embed.data_ptr():
+            w.lm_head = ops.pack_weight(w.lm_head)
+        elif isinstance(w.lm_head, torch.Tensor):
+            w.lm_head = ops.pack_weight(w.lm_head.clone())
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
 
     # -------------------------------------------------------------- helpers
     def decode_attn_plan(self, batch: int, max_seq: int):
@@ -98,12 +122,21 @@ class Decoder:
                                              max(nsplit, ws.max_splits if ws else 1))
         return self.attn_ws
 
+    def _row_parallel(self, x, w, tag):
+        """Row-parallel linear whose output is summed over tensor-parallel ranks."""
+        if hasattr(self.comm, "linear_reduce"):
+            return self.comm.linear_reduce(x, w, tag)
+        return self.comm.reduce_parts(ops.linear(x, w), tag)
+
     # -------------------------------------------------------------- forward
     def forward(self, fb: ForwardBatch, attn_plan=None) -> torch.Tensor:
         """Returns fp32 logits [len(logit_rows), vocab shard of this rank]."""
         cfg, w = self.cfg, self.w
         eps = cfg.rms_eps
         T = fb.input_ids.shape[0]
+        comm = self.comm
+        if hasattr(comm, "begin_step"):
+            comm.begin_step()
         h = ops.embedding(fb.input_ids, w.embed)
         residual = torch.empty_like(h)
         x = ops.rmsnorm([h], w.layers[0].input_norm, eps, residual_out=residual)
@@ -124,15 +157,13 @@ class Decoder:
             else:
                 attn = ops.paged_prefill_attention(q, kc, vc, fb.block_tables, fb.seq_lens, fb.q_start, fb.cu_q,
                                                    self.scale, max_q=fb.max_q)
-            o = ops.linear(attn.view(T, self.nq * self.hd), lw.o)
-            o_parts = self.comm.reduce_parts(o, "o")
+            o_parts = self._row_parallel(attn.view(T, self.nq * self.hd), lw.o, "o")
             x = ops.rmsnorm(o_parts, lw.post_norm, eps, residual=residual, residual_out=residual)
             if self.moe is not None:
-                d = self.moe(i, x)
+                mlp_parts = self.comm.reduce_parts(self.moe(i, x), "mlp")
             else:
                 act = ops.linear(x, lw.gate_up, epilogue=ops.EPI_SWIGLU)
-                d = ops.linear(act, lw.down)
-            mlp_parts = self.comm.reduce_parts(d, "mlp")
+                mlp_parts = self._row_parallel(act, lw.down, "mlp")
         rows = fb.logit_rows
         x = ops.rmsnorm(mlp_parts, w.final_norm, eps, residual=residual)
         if rows is not None:

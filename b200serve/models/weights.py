@@ -83,7 +83,7 @@ class ModelWeights:
             n += t.numel() * t.element_size()
         for lw in self.layers:
             for v in vars(lw).values():
-                if isinstance(v, torch.Tensor):
+                if hasattr(v, "numel") and hasattr(v, "element_size"):
                     n += v.numel() * v.element_size()
         return n
 

@@ -94,7 +94,12 @@ def rmsnorm(parts, weight, eps, residual=None, residual_out=None, out=None):
     x0 = parts[0]
     if _cuda(x0):
         out = out if out is not None else torch.empty_like(x0)
-        ext().rmsnorm_fused(list(parts), residual, residual_out, weight, out, float(eps))
+        flags = getattr(parts, "flags_ptr", None)
+        if flags is not None:   # parts pushed by peers: wait for their flags first
+            ext().rmsnorm_fused_wait(list(parts), residual, residual_out, weight, out, float(eps), flags,
+                                     parts.epoch_ptr, parts.err_ptr)
+        else:
+            ext().rmsnorm_fused(list(parts), residual, residual_out, weight, out, float(eps))
         return out
     s = sum(p.float() for p in parts)
     if residual is not None:
@@ -219,6 +224,41 @@ def default_workspace(device) -> GemmWorkspace:
     return _workspaces[key]
 
 
+class PackedWeight:
+    """A [N, K] weight stored tile-contiguous for the tcgen05 GEMM: tiles of
+    128 output rows x 64 K columns laid out [n_tile][k_block][128][64], so each
+    TMA box of the kernel is one contiguous 16 KB read. N and K are zero-padded
+    to multiples of 128 and 64."""
+
+    def __init__(self, w: torch.Tensor):
+        N, K = w.shape
+        self.N, self.K = N, K
+        Np, Kp = (N + 127) // 128 * 128, (K + 63) // 64 * 64
+        if (Np, Kp) != (N, K):
+            w = torch.nn.functional.pad(w, (0, Kp - K, 0, Np - N))
+        self.data = w.view(Np // 128, 128, Kp // 64, 64).permute(0, 2, 1, 3).contiguous().view(-1, 64)
+        self.shape = (N, K)
+        self.dtype = w.dtype
+        self.device = w.device
+
+    def unpacked(self) -> torch.Tensor:
+        Np, Kp = (self.N + 127) // 128 * 128, (self.K + 63) // 64 * 64
+        return self.data.view(Np // 128, Kp // 64, 128, 64).permute(0, 2, 1, 3).reshape(Np, Kp)[:self.N, :self.K]
+
+    def numel(self):
+        return self.data.numel()
+
+    def element_size(self):
+        return self.data.element_size()
+
+
+def pack_weight(w):
+    """Pack a CUDA weight for the GEMM (idempotent; CPU tensors stay plain)."""
+    if isinstance(w, PackedWeight) or w is None or not w.is_cuda or w.dim() != 2:
+        return w
+    return PackedWeight(w)
+
+
 def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspace=None, splits=0):
     """y = x @ w^T (+bias) (+residual) with x [M, K], w [N, K].
 
@@ -227,6 +267,11 @@ def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspac
     """
     M, K = x.shape
     N = w.shape[0]
+    packed_n = 0
+    if isinstance(w, PackedWeight):
+        packed_n = w.N
+        if not x.is_cuda:
+            w = w.unpacked()
     if _cuda(x):
         if out is None:
             if epilogue == EPI_SWIGLU:
@@ -235,7 +280,8 @@ def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspac
                 out = torch.empty(M, N, dtype=torch.float32 if epilogue == EPI_F32 else x.dtype,
                                   device=x.device)
         ws = workspace or default_workspace(x.device)
-        ext().gemm_tc(x, w, out, bias, residual, ws.ws, ws.counters, epilogue, splits)
+        wt = w.data if packed_n else w
+        ext().gemm_tc(x, wt, out, bias, residual, ws.ws, ws.counters, epilogue, splits, packed_n)
         return out
     y = x.float() @ w.float().t()
     if bias is not None:
@@ -263,6 +309,9 @@ class AttnWorkspace:
         self.max_splits = max_splits
 
 
+_FORCE_SIMT_DECODE = os.environ.get("B200_TC_DECODE", "0") != "1"   # tensor-core decode attention: opt-in until validated on GPU
+
+
 def paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, scale, tps=256, nsplit=1,
                            workspace=None, out=None):
     """One query token per sequence. q [B, nq, hd]; seq_lens include the new token."""
@@ -273,8 +322,14 @@ def paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, scale, t
             acc, ml = workspace.acc, workspace.ml
         else:
             acc = ml = torch.empty(0, dtype=torch.float32, device=q.device)
-        ext().paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, out, acc, ml,
-                                     float(scale), int(tps), int(nsplit))
+        B, nq, hd = q.shape
+        G = nq // k_cache.shape[1]
+        if hd == 128 and G in (1, 2, 4, 8, 16) and not _FORCE_SIMT_DECODE:
+            ext().paged_decode_attention_tc(q, k_cache, v_cache, block_tables, seq_lens, out, acc, ml,
+                                            float(scale), int(tps), int(nsplit))
+        else:
+            ext().paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, out, acc, ml,
+                                         float(scale), int(tps), int(nsplit))
         return out
     B, nq, hd = q.shape
     nkv = k_cache.shape[1]
@@ -348,6 +403,42 @@ def argmax_rows(logits, out_idx, out_val, index_offset=0):
 def argmax_merge(vals, idx, out):
     _cuda(vals)
     ext().argmax_merge(vals, idx, out)
+
+
+_SAMPLE_ROW = None
+
+
+def _sample_row_dtype():
+    global _SAMPLE_ROW
+    if _SAMPLE_ROW is None:
+        import numpy as np
+        _SAMPLE_ROW = np.dtype([("temperature", "<f4"), ("top_p", "<f4"), ("min_p", "<f4"), ("top_k", "<i4"),
+                                ("seed", "<u8"), ("step", "<u4"), ("pad", "<u4")])
+    return _SAMPLE_ROW
+
+
+def sample_rows(logits, temperature, top_k, top_p, min_p, seeds, steps, pen_ids=None, pen_counts=None,
+                pen_vals=None):
+    """One token per row of fp32 ``logits`` [B, V] (penalties are applied in place).
+
+    Per-row lists: temperature (<= 0 = greedy), top_k (0 = off), top_p, min_p, seeds,
+    steps (draw counter). pen_ids [B, P] int32 (-1 pad, unique per row), pen_counts
+    [B, P] fp32, pen_vals [B, 3] fp32 = (repeat, presence, frequency)."""
+    import numpy as np
+    B = logits.shape[0]
+    rec = np.zeros(B, dtype=_sample_row_dtype())
+    rec["temperature"], rec["top_p"], rec["min_p"] = temperature, top_p, min_p
+    rec["top_k"], rec["seed"], rec["step"] = top_k, [int(x) & (2 ** 64 - 1) for x in seeds], steps
+    params = torch.from_numpy(rec.view(np.uint8)).to(logits.device, non_blocking=True)
+    dev = logits.device
+    if pen_ids is None:
+        pen_ids = torch.empty(0, dtype=torch.int32, device=dev)
+        pen_counts = torch.empty(0, dtype=torch.float32, device=dev)
+        pen_vals = torch.empty(0, dtype=torch.float32, device=dev)
+    out = torch.empty(B, dtype=torch.int32, device=dev)
+    _cuda(logits)
+    ext().sample_rows(logits, params, pen_ids, pen_counts, pen_vals, out)
+    return out
 
 
 def gemm_error_flag(reset: bool = True) -> int:

@@ -22,6 +22,33 @@ namespace b200 {
 constexpr int kPage = 16;
 constexpr int kAttnWarps = 4;
 
+template <int HD>
+struct PageRegs {
+  uint4 k[HD / 16];               // this lane's key chunks: 16-byte chunk (2c + half) of row (lane & 15)
+  uint32_t v[16][HD / 64];        // this lane's value dims [lane*E, lane*E+E) of all 16 rows
+};
+
+template <int HD>
+__device__ __forceinline__ void load_page(PageRegs<HD>& r, const __nv_bfloat16* __restrict__ k_cache,
+                                          const __nv_bfloat16* __restrict__ v_cache, size_t page_off, int tok,
+                                          int half, int lane) {
+  constexpr int E = HD / 32;
+  const __nv_bfloat16* krow = k_cache + page_off + (size_t)tok * HD;
+#pragma unroll
+  for (int c = 0; c < HD / 16; ++c) r.k[c] = __ldg(reinterpret_cast<const uint4*>(krow + (c * 2 + half) * 8));
+  const __nv_bfloat16* vpage = v_cache + page_off + lane * E;
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    if constexpr (E == 4) {
+      const uint2 raw = __ldg(reinterpret_cast<const uint2*>(vpage + (size_t)t * HD));
+      r.v[t][0] = raw.x;
+      r.v[t][1] = raw.y;
+    } else {
+      r.v[t][0] = __ldg(reinterpret_cast<const uint32_t*>(vpage + (size_t)t * HD));
+    }
+  }
+}
+
 template <int HD, int G>
 __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_cache,
@@ -29,12 +56,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
     const int* __restrict__ seq_lens, int max_blocks, int nkv, float scale_log2, int tps,
     float* __restrict__ part_acc, float* __restrict__ part_ml, __nv_bfloat16* __restrict__ out, int nsplit) {
   constexpr int E = HD / 32;          // value dims per lane
-  constexpr int NCH = HD / 8;         // 16-byte chunks per key row
   __shared__ float q_s[G][HD];
   __shared__ __align__(16) float p_s[kAttnWarps][kPage][G < 4 ? 4 : G];
   __shared__ float m_s[kAttnWarps][G], l_s[kAttnWarps][G];
   __shared__ float acc_s[kAttnWarps][G][HD];
 
+  pdl_wait();
+  pdl_trigger();
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int len = seq_lens[b];
@@ -59,20 +87,22 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
 
   const int tok = lane & 15, half = lane >> 4;
   const int* bt = block_tables + (size_t)b * max_blocks;
-  for (int page_start = start + warp * kPage; page_start < stop; page_start += kAttnWarps * kPage) {
-    const int phys = bt[page_start / kPage];
-    const size_t page_off = ((size_t)phys * nkv + kvh) * kPage * HD;
-    // ---- scores for 16 tokens ----
-    const __nv_bfloat16* krow = k_cache + page_off + (size_t)tok * HD;
+  auto page_offset = [&](int page_start) {
+    return ((size_t)bt[page_start / kPage] * nkv + kvh) * kPage * HD;
+  };
+
+  // one page: scores, online softmax, p.V
+  auto consume = [&](const PageRegs<HD>& r, int page_start) {
     float s[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) s[g] = 0.f;
 #pragma unroll
-    for (int c = 0; c < NCH / 2; ++c) {
+    for (int c = 0; c < HD / 16; ++c) {
       const int chunk = c * 2 + half;
-      bf16x8 kv = *reinterpret_cast<const bf16x8*>(krow + chunk * 8);
       float kf[8];
-      unpack8(kv, kf);
+      const uint4 kv = r.k[c];
+      kf[0] = bf16_lo(kv.x); kf[1] = bf16_hi(kv.x); kf[2] = bf16_lo(kv.y); kf[3] = bf16_hi(kv.y);
+      kf[4] = bf16_lo(kv.z); kf[5] = bf16_hi(kv.z); kf[6] = bf16_lo(kv.w); kf[7] = bf16_hi(kv.w);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
 #pragma unroll
@@ -85,7 +115,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
       s[g] += __shfl_xor_sync(0xffffffffu, s[g], 16);
       if (!valid) s[g] = -INFINITY;
     }
-    // ---- online softmax over the page ----
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       float bm = s[g];
@@ -104,17 +133,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
       if (half == 0) p_s[warp][tok][g] = p;
     }
     __syncwarp();
-    // ---- acc += p . V ----
-    const __nv_bfloat16* vpage = v_cache + page_off + lane * E;
-#pragma unroll 4
+#pragma unroll
     for (int t = 0; t < kPage; ++t) {
       float vf[E];
       if constexpr (E == 4) {
-        uint2 raw = *reinterpret_cast<const uint2*>(vpage + (size_t)t * HD);
-        vf[0] = bf16_lo(raw.x); vf[1] = bf16_hi(raw.x); vf[2] = bf16_lo(raw.y); vf[3] = bf16_hi(raw.y);
+        vf[0] = bf16_lo(r.v[t][0]); vf[1] = bf16_hi(r.v[t][0]); vf[2] = bf16_lo(r.v[t][1]); vf[3] = bf16_hi(r.v[t][1]);
       } else {
-        uint32_t raw = *reinterpret_cast<const uint32_t*>(vpage + (size_t)t * HD);
-        vf[0] = bf16_lo(raw); vf[1] = bf16_hi(raw);
+        vf[0] = bf16_lo(r.v[t][0]); vf[1] = bf16_hi(r.v[t][0]);
       }
 #pragma unroll
       for (int g = 0; g < G; ++g) {
@@ -124,6 +149,26 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
       }
     }
     __syncwarp();
+  };
+
+  // pages of this warp: start + warp*16, then every 4*16 tokens; keep the next page in flight
+  constexpr int STRIDE = kAttnWarps * kPage;
+  int pg = start + warp * kPage;
+  if (pg < stop) {
+    PageRegs<HD> ra, rb;
+    load_page<HD>(ra, k_cache, v_cache, page_offset(pg), tok, half, lane);
+    while (true) {
+      const int pn = pg + STRIDE;
+      if (pn < stop) load_page<HD>(rb, k_cache, v_cache, page_offset(pn), tok, half, lane);
+      consume(ra, pg);
+      if (pn >= stop) break;
+      pg = pn;
+      const int pn2 = pg + STRIDE;
+      if (pn2 < stop) load_page<HD>(ra, k_cache, v_cache, page_offset(pn2), tok, half, lane);
+      consume(rb, pg);
+      if (pn2 >= stop) break;
+      pg = pn2;
+    }
   }
 
   // ---- merge the 4 warps ----
@@ -166,6 +211,8 @@ __global__ void paged_decode_combine_kernel(const float* __restrict__ part_acc, 
                                             const int* __restrict__ seq_lens, __nv_bfloat16* __restrict__ out,
                                             int B, int nkv, int G, int nsplit, int tps) {
   constexpr int E = HD / 32;
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int nq = nkv * G;
@@ -221,9 +268,9 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tenso
   float* pa = nsplit > 1 ? part_acc.data_ptr<float>() : nullptr;
   float* pm = nsplit > 1 ? part_ml.data_ptr<float>() : nullptr;
 #define B200_DEC(HDV, GV)                                                                                    \
-  paged_decode_kernel<HDV, GV><<<grid, kAttnWarps * 32, 0, stream>>>(qp, kp, vp, block_tables.data_ptr<int>(), \
-                                                                    seq_lens.data_ptr<int>(),                 \
-                                                                    block_tables.size(1), nkv, sl2, tps, pa, pm, op, nsplit)
+  launch_pdl(paged_decode_kernel<HDV, GV>, grid, dim3(kAttnWarps * 32), 0, stream, qp, kp, vp,                \
+             (const int*)block_tables.data_ptr<int>(), (const int*)seq_lens.data_ptr<int>(),                  \
+             (int)block_tables.size(1), nkv, sl2, (int)tps, pa, pm, op, (int)nsplit)
   if (HD == 128 && G == 4) B200_DEC(128, 4);
   else if (HD == 128 && G == 8) B200_DEC(128, 8);
   else if (HD == 128 && G == 2) B200_DEC(128, 2);
@@ -239,13 +286,30 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tenso
     const int threads = 128;
     const int blocks = (warps * 32 + threads - 1) / threads;
     if (HD == 128)
-      paged_decode_combine_kernel<128><<<blocks, threads, 0, stream>>>(pa, pm, seq_lens.data_ptr<int>(), op, B, nkv,
-                                                                       G, nsplit, tps);
+      launch_pdl(paged_decode_combine_kernel<128>, dim3(blocks), dim3(threads), 0, stream, (const float*)pa,
+                 (const float*)pm, (const int*)seq_lens.data_ptr<int>(), op, B, nkv, G, (int)nsplit, (int)tps);
     else
-      paged_decode_combine_kernel<64><<<blocks, threads, 0, stream>>>(pa, pm, seq_lens.data_ptr<int>(), op, B, nkv, G,
-                                                                      nsplit, tps);
-    B200_CHECK_CUDA(cudaGetLastError());
+      launch_pdl(paged_decode_combine_kernel<64>, dim3(blocks), dim3(threads), 0, stream, (const float*)pa,
+                 (const float*)pm, (const int*)seq_lens.data_ptr<int>(), op, B, nkv, G, (int)nsplit, (int)tps);
   }
+}
+
+// Merge split-KV partials into out [B, nq, HD] (used by the tensor-core decode kernel).
+void paged_decode_combine(torch::Tensor part_acc, torch::Tensor part_ml, torch::Tensor seq_lens, torch::Tensor out,
+                          int64_t nkv, int64_t G, int64_t nsplit, int64_t tps) {
+  const int B = out.size(0), nq = out.size(1), HD = out.size(2);
+  const int threads = 128;
+  const int blocks = (B * nq * 32 + threads - 1) / threads;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  if (HD == 128)
+    launch_pdl(paged_decode_combine_kernel<128>, dim3(blocks), dim3(threads), 0, stream,
+               (const float*)part_acc.data_ptr<float>(), (const float*)part_ml.data_ptr<float>(),
+               (const int*)seq_lens.data_ptr<int>(), op, B, (int)nkv, (int)G, (int)nsplit, (int)tps);
+  else
+    launch_pdl(paged_decode_combine_kernel<64>, dim3(blocks), dim3(threads), 0, stream,
+               (const float*)part_acc.data_ptr<float>(), (const float*)part_ml.data_ptr<float>(),
+               (const int*)seq_lens.data_ptr<int>(), op, B, (int)nkv, (int)G, (int)nsplit, (int)tps);
 }
 
 // ---------------------------------------------------------------------------

@@ -48,6 +48,8 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(
   __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);          // [2][64][LD]
   __nv_bfloat16* vs = ks + 2 * PF_BK * LD;                                  // [2][64][LD]
 
+  pdl_wait();
+  pdl_trigger();
   const int seq = blockIdx.z, h = blockIdx.y, qt = blockIdx.x;
   const int row0 = cu_q[seq], nrows = cu_q[seq + 1] - row0;
   if (qt * PF_BQ >= nrows) return;
@@ -231,11 +233,11 @@ void paged_prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tens
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));            \
       attr = true;                                                                                              \
     }                                                                                                           \
-    paged_prefill_kernel<HDV><<<grid, 128, smem, stream>>>(                                                     \
+    launch_pdl(paged_prefill_kernel<HDV>, grid, dim3(128), smem, stream,                                        \
         reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr()), \
-        reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()), block_tables.data_ptr<int>(),               \
-        block_tables.size(1), seq_lens.data_ptr<int>(), q_start.data_ptr<int>(), cu_q.data_ptr<int>(),           \
-        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nq, nkv, sl2);                                        \
+        reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()), (const int*)block_tables.data_ptr<int>(),   \
+        (int)block_tables.size(1), (const int*)seq_lens.data_ptr<int>(), (const int*)q_start.data_ptr<int>(),    \
+        (const int*)cu_q.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nq, nkv, sl2);        \
   }
   if (HD == 128) B200_PF(128)
   else if (HD == 64) B200_PF(64)

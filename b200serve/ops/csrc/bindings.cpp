@@ -3,6 +3,20 @@
 
 void rmsnorm_fused(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
                    c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps);
+void rmsnorm_fused_wait(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
+                        c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps,
+                        int64_t flags_ptr, int64_t epoch_ptr, int64_t err_ptr);
+void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, int64_t ldo, torch::Tensor flag_ptrs,
+                  int64_t epoch_ptr, torch::Tensor tile_done, c10::optional<torch::Tensor> bias, torch::Tensor ws,
+                  torch::Tensor counters, int64_t err_ptr, int64_t packed_n);
+int64_t ipc_malloc(int64_t bytes);
+void ipc_free(int64_t ptr);
+torch::Tensor ipc_handle(int64_t ptr);
+int64_t ipc_open(torch::Tensor handle);
+void ipc_close(int64_t ptr);
+torch::Tensor host_error_word();
+int64_t read_host_word(int64_t host_ptr, int64_t index, bool reset);
+void epoch_inc(int64_t epoch_ptr);
 void qkv_post(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
               c10::optional<torch::Tensor> kn_w, torch::Tensor cos_sin, torch::Tensor positions,
               torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache, int64_t nq,
@@ -16,25 +30,43 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tenso
 void paged_prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                              torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor q_start,
                              torch::Tensor cu_q, torch::Tensor out, double scale, int64_t max_q);
+void paged_decode_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                               torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
+                               torch::Tensor part_acc, torch::Tensor part_ml, double scale, int64_t tps,
+                               int64_t nsplit);
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi, int64_t num_sms);
 void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> bias,
              c10::optional<torch::Tensor> residual, torch::Tensor ws, torch::Tensor counters, int64_t epi,
-             int64_t force_splits);
+             int64_t force_splits, int64_t packed_n);
 int64_t gemm_error_flag(bool reset);
 void argmax_rows(torch::Tensor logits, torch::Tensor out_idx, torch::Tensor out_val, int64_t index_offset);
 void argmax_merge(torch::Tensor vals, torch::Tensor idx, torch::Tensor out);
+void sample_rows(torch::Tensor logits, torch::Tensor params, torch::Tensor pen_ids, torch::Tensor pen_counts,
+                 torch::Tensor pen_vals, torch::Tensor out);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "b200serve sm_100a kernels";
   m.def("rmsnorm_fused", &rmsnorm_fused);
   m.def("qkv_post", &qkv_post);
+  m.def("rmsnorm_fused_wait", &rmsnorm_fused_wait);
+  m.def("gemm_tc_push", &gemm_tc_push);
+  m.def("ipc_malloc", &ipc_malloc);
+  m.def("ipc_free", &ipc_free);
+  m.def("ipc_handle", &ipc_handle);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("host_error_word", &host_error_word);
+  m.def("read_host_word", &read_host_word);
+  m.def("epoch_inc", &epoch_inc);
   m.def("silu_mul", &silu_mul);
   m.def("embedding", &embedding);
   m.def("paged_decode_attention", &paged_decode_attention);
   m.def("paged_prefill_attention", &paged_prefill_attention);
+  m.def("paged_decode_attention_tc", &paged_decode_attention_tc);
   m.def("gemm_plan", &gemm_plan);
   m.def("gemm_tc", &gemm_tc);
   m.def("gemm_error_flag", &gemm_error_flag);
   m.def("argmax_rows", &argmax_rows);
   m.def("argmax_merge", &argmax_merge);
+  m.def("sample_rows", &sample_rows);
 }

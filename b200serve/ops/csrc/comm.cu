@@ -1,0 +1,83 @@
+// Cross-GPU plumbing for the fused tensor-parallel kernels: CUDA IPC buffers
+// shared between the ranks of one node, the per-step epoch counter, and the
+// bounded flag wait used by consumers of peer-pushed data.
+//
+// Protocol of one fused all-reduce site (decode-sized row-parallel output):
+//  * every rank's GEMM epilogue stores its partial tile into slot
+//    [site % 2][its own rank] of EVERY rank's receive buffer (NVLink P2P stores);
+//  * when all tiles of the GEMM are pushed, the rank's last CTA publishes
+//    flag[site][its rank] = epoch on every peer (st.release.sys after fences);
+//  * the consumer kernel on each rank waits until flag[site][r] == epoch for all
+//    r (ld.acquire.sys, bounded by a deadline), then sums the world slots locally.
+// Two slots alternate by site parity; a rank can only overwrite slot (site % 2)
+// after every peer has pushed site+1, which each peer does only after it has
+// finished reading site (stream order), so no slot is overwritten while read.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include "common.cuh"
+
+namespace b200 {
+
+__global__ void epoch_inc_kernel(int* epoch) {
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x == 0) *epoch += 1;
+}
+
+}  // namespace b200
+
+using namespace b200;
+
+int64_t ipc_malloc(int64_t bytes) {
+  void* p = nullptr;
+  B200_CHECK_CUDA(cudaMalloc(&p, bytes));
+  B200_CHECK_CUDA(cudaMemset(p, 0, bytes));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_free(int64_t ptr) { B200_CHECK_CUDA(cudaFree(reinterpret_cast<void*>(ptr))); }
+
+torch::Tensor ipc_handle(int64_t ptr) {
+  cudaIpcMemHandle_t h;
+  B200_CHECK_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(ptr)));
+  auto t = torch::empty({(int64_t)sizeof(h)}, torch::kUInt8);
+  memcpy(t.data_ptr(), &h, sizeof(h));
+  return t;
+}
+
+int64_t ipc_open(torch::Tensor handle) {
+  TORCH_CHECK(handle.numel() == sizeof(cudaIpcMemHandle_t));
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle.data_ptr(), sizeof(h));
+  void* p = nullptr;
+  B200_CHECK_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close(int64_t ptr) { B200_CHECK_CUDA(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr))); }
+
+// Host-mapped error word: kernels that give up a bounded wait write a code here;
+// the host reads it after each step without a device synchronisation.
+torch::Tensor host_error_word() {
+  int* h = nullptr;
+  B200_CHECK_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h), 64, cudaHostAllocMapped));
+  memset(h, 0, 64);
+  int* d = nullptr;
+  B200_CHECK_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&d), h, 0));
+  auto t = torch::empty({2}, torch::kInt64);
+  t[0] = reinterpret_cast<int64_t>(h);
+  t[1] = reinterpret_cast<int64_t>(d);
+  return t;
+}
+
+int64_t read_host_word(int64_t host_ptr, int64_t index, bool reset) {
+  volatile int* h = reinterpret_cast<volatile int*>(host_ptr);
+  const int v = h[index];
+  if (reset) h[index] = 0;
+  return v;
+}
+
+void epoch_inc(int64_t epoch_ptr) {
+  launch_pdl(epoch_inc_kernel, dim3(1), dim3(32), 0, at::cuda::getCurrentCUDAStream(),
+             reinterpret_cast<int*>(epoch_ptr));
+}

@@ -75,3 +75,34 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 }  // namespace b200
+
+namespace b200 {
+
+// Programmatic dependent launch (PDL). A kernel launched with
+// launch_pdl() may start while the previous kernel on the stream is still
+// running; it must call pdl_wait() before touching anything the previous
+// kernel writes (or writing anything it reads). pdl_trigger() lets the next
+// kernel start its own prologue early. Both are no-ops without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) TORCH_CHECK(false, "launch failed: ", cudaGetErrorString(e));
+}
+
+}  // namespace b200

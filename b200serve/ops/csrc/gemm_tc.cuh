@@ -1,0 +1,381 @@
+// Persistent tcgen05/TMEM GEMM for the decoder's linear layers:
+//   out[m, n] = sum_k act[m, k] * W[n, k]  (+ bias[n]) (+ residual[m, n])
+// with fused epilogues (bf16 store, fp32 store for logits, SwiGLU on the
+// 64-row interleaved gate/up layout).
+//
+// The weight is the MMA "A" operand (128 output features per tile = the 128
+// TMEM lanes) and the activations are the MMA "B" operand (BN tokens per tile =
+// BN TMEM columns), so a decode batch of 16..256 tokens maps onto the MMA N
+// dimension and every CTA streams weight tiles at full width.
+//
+// Roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA
+// issuer (one elected thread), warps 2..5 = epilogue (warp w reads TMEM lanes
+// 32*(w%4) .. 32*(w%4)+31). Shared memory holds STAGES stages of
+// [W tile 128x64 | act tile BNx64] in the 128-byte-swizzled K-major layout
+// written by TMA; the accumulator is double-buffered in TMEM so the epilogue of
+// one work unit overlaps the main loop of the next.
+//
+// Work units are (n tile, m tile, k split). With fewer tiles than SMs the K
+// loop is split; every split writes an fp32 partial tile to a workspace and
+// the last CTA to finish a tile (counter per tile) sums the partials and runs
+// the epilogue.
+//
+// Reference kernels restated: matmul.wgsl:133,201 (matmul_bt_bf16, C = A B^T).
+#pragma once
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include "tc_primitives.cuh"
+
+namespace b200 {
+
+enum GemmEpi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_PUSH = 3 };
+
+constexpr int kMaxPeers = 8;
+
+struct GemmParams {
+  int M, N, K;                  // tokens, output features, reduction
+  int w_packed;                 // 1: W stored tile-contiguous [n_tile][k_block][128][64]
+  int n_tiles, m_tiles, splits, kb_per_split, kb_total, units;
+  void* out;                    // bf16 or fp32, row stride ldo (elements)
+  int ldo;
+  const __nv_bfloat16* bias;    // [N] or null
+  const __nv_bfloat16* residual;  // [M, ldr] or null
+  int ldr;
+  float* ws;                    // [splits, m_tiles*BN, N] fp32 (splits > 1)
+  int* counters;                // [m_tiles * n_tiles], zero on entry and on exit
+  int* err;
+  // EPI_PUSH: bf16 tile stored to every rank's receive slot, then per-rank flags raised
+  int world;
+  __nv_bfloat16* push_dst[kMaxPeers];   // slot base on rank r (row stride ldo)
+  int* push_flag[kMaxPeers];            // flag word on rank r for (site, this rank)
+  const int* epoch;                     // this step's epoch (device)
+  int* tile_done;                       // local counter of pushed tiles, zero on entry and exit
+};
+
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr int W_BYTES = BM * BK * 2;
+  static constexpr int A_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = W_BYTES + A_BYTES;
+  // decode-sized tiles keep ~100 KB so the next kernel's CTA fits beside this one (PDL overlap)
+  static constexpr int BUDGET = BN <= 64 ? 104 * 1024 : 200 * 1024;
+  static constexpr int STAGES = BUDGET / STAGE_BYTES > 12 ? 12 : BUDGET / STAGE_BYTES;
+  static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;
+  static constexpr int XCHG_FLOATS = 64 * 17;
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + XCHG_FLOATS * 4 + 256;
+};
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Final epilogue for 16 consecutive tokens [t0, t0+16) of this thread's feature row.
+template <int EPI>
+__device__ __forceinline__ void epilogue_store(const GemmParams& p, float* v, int row, int n_tile, int t0,
+                                               float* xchg, int quad, int lane) {
+  if constexpr (EPI == EPI_SWIGLU) {
+    // rows 0..63 hold gate features, rows 64..127 the up features of the same 64 columns
+    if (quad >= 2) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) xchg[((quad - 2) * 32 + lane) * 17 + j] = v[j];
+    }
+    epi_bar();
+    if (quad < 2) {
+      const int col = n_tile * 64 + quad * 32 + lane;
+      const int half_n = p.N / 2;
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int t = t0 + j;
+        if (t < p.M && col < half_n) {
+          const float g = v[j];
+          const float u = xchg[(quad * 32 + lane) * 17 + j];
+          const float sg = __bfloat162float(__float2bfloat16_rn(g / (1.f + __expf(-g))));
+          // gate and up are rounded to bf16 first, as a bf16 framework would store them
+          out[(size_t)t * p.ldo + col] =
+              __float2bfloat16_rn(sg * __bfloat162float(__float2bfloat16_rn(u)));
+        }
+      }
+    }
+    epi_bar();
+  } else if constexpr (EPI == EPI_PUSH) {
+    const int col = n_tile * 128 + row;
+    if (col >= p.N) return;
+    const float b = p.bias ? __bfloat162float(p.bias[col]) : 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int t = t0 + j;
+      if (t >= p.M) break;
+      const __nv_bfloat16 v16 = __float2bfloat16_rn(v[j] + b);
+      for (int r = 0; r < p.world; ++r) p.push_dst[r][(size_t)t * p.ldo + col] = v16;
+    }
+  } else {
+    const int col = n_tile * 128 + row;
+    if (col >= p.N) return;
+    const float b = p.bias ? __bfloat162float(p.bias[col]) : 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int t = t0 + j;
+      if (t >= p.M) break;
+      float x = v[j] + b;
+      if constexpr (EPI == EPI_F32) {
+        reinterpret_cast<float*>(p.out)[(size_t)t * p.ldo + col] = x;
+      } else {
+        if (p.residual) x = __bfloat162float(__float2bfloat16_rn(x)) + __bfloat162float(p.residual[(size_t)t * p.ldr + col]);
+        reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)t * p.ldo + col] = __float2bfloat16_rn(x);
+      }
+    }
+  }
+}
+
+// TMA coordinates of the weight tile (n_tile, k block kb) in the plain [N, K]
+// layout or the tile-contiguous packed layout (each 128x64 tile one 16 KB run).
+__device__ __forceinline__ int w_x(const GemmParams& p, int kb) { return p.w_packed ? 0 : kb * 64; }
+__device__ __forceinline__ int w_y(const GemmParams& p, int n_tile, int kb) {
+  return p.w_packed ? (n_tile * p.kb_total + kb) * 128 : n_tile * 128;
+}
+
+// EPI_PUSH: after a tile's stores reached every peer, count it; the CTA that
+// completes the last tile raises flag[r] = epoch on every rank (system-scope release).
+__device__ __forceinline__ void publish_tile(const GemmParams& p, int* scratch) {
+  __threadfence_system();
+  epi_bar();
+  if (threadIdx.x == 64) {
+    const int total = p.m_tiles * p.n_tiles;
+    const int old = atomicAdd(p.tile_done, 1);
+    if (old == total - 1) {
+      *p.tile_done = 0;
+      __threadfence_system();
+      const int e = *p.epoch;
+      for (int r = 0; r < p.world; ++r)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.push_flag[r]), "r"(e) : "memory");
+    }
+  }
+  epi_bar();
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(192, 2)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
+                   const GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, BN);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_w = smem;
+  uint8_t* s_a = smem + STAGES * Cfg::W_BYTES;
+  float* xchg = reinterpret_cast<float*>(s_a + STAGES * Cfg::A_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(xchg + Cfg::XCHG_FLOATS);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* last_flag = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_slot + 2));
+  (void)last_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* err = p.err;  // never null: the host passes its error word
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { tc::mbar_init(&full[s], 1); tc::mbar_init(&empty[s], 1); }
+    for (int i = 0; i < 2; ++i) { tc::mbar_init(&tfull[i], 1); tc::mbar_init(&tempty[i], 4); }
+    tc::mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+    tc::fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tmap(&tm_w);
+    tc::prefetch_tmap(&tm_a);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
+  if (warp != 0) pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      const uint64_t pol_w = tc::policy_evict_first(), pol_a = tc::policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      // Weights never depend on the previous kernel: stream the first stages of W
+      // while that kernel finishes, then wait for it before loading activations.
+      int pre = 0;
+      if ((int)blockIdx.x < p.units) {
+        const int split = blockIdx.x % p.splits, tile = blockIdx.x / p.splits;
+        const int n_tile = tile % p.n_tiles;
+        const int kb0 = split * p.kb_per_split, kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        pre = min(kb1 - kb0, STAGES);
+        for (int i = 0; i < pre; ++i) {
+          tc::mbar_arrive_expect_tx(&full[i], Cfg::STAGE_BYTES);
+          tc::tma_load_2d(s_w + i * Cfg::W_BYTES, &tm_w, &full[i], w_x(p, kb0 + i), w_y(p, n_tile, kb0 + i), pol_w);
+        }
+        pdl_wait();
+        const int m_tile = tile / p.n_tiles;
+        for (int i = 0; i < pre; ++i)
+          tc::tma_load_2d(s_a + i * Cfg::A_BYTES, &tm_a, &full[i], (kb0 + i) * 64, m_tile * BN, pol_a);
+        stage = pre % STAGES;
+        phase = pre == STAGES ? 1 : 0;
+      } else {
+        pdl_wait();
+      }
+      for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
+        const int split = u % p.splits, tile = u / p.splits;
+        const int n_tile = tile % p.n_tiles, m_tile = tile / p.n_tiles;
+        const int kb0 = split * p.kb_per_split, kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        for (int kb = kb0 + (u == (int)blockIdx.x ? pre : 0); kb < kb1; ++kb) {
+          if (!tc::mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, err, 1)) break;
+          tc::mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          tc::tma_load_2d(s_w + stage * Cfg::W_BYTES, &tm_w, &full[stage], w_x(p, kb), w_y(p, n_tile, kb), pol_w);
+          tc::tma_load_2d(s_a + stage * Cfg::A_BYTES, &tm_a, &full[stage], kb * 64, m_tile * BN, pol_a);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t acc_phase[2] = {0, 0};
+      int acc = 0;
+      for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
+        const int split = u % p.splits;
+        const int kb0 = split * p.kb_per_split, kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        if (!tc::mbar_wait_bounded(&tempty[acc], acc_phase[acc] ^ 1, abort_flag, err, 2)) break;
+        tc::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!tc::mbar_wait_bounded(&full[stage], phase, abort_flag, err, 3)) break;
+          tc::tc_fence_after();
+          const uint64_t a0 = tc::sw128_kmajor_desc(tc::smem_u32(s_w + stage * Cfg::W_BYTES));
+          const uint64_t b0 = tc::sw128_kmajor_desc(tc::smem_u32(s_a + stage * Cfg::A_BYTES));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            // 16 bf16 = 32 bytes along K per MMA: +2 in the 16-byte-unit address field
+            tc::mma_bf16(d_tmem, a0 + 2 * kk, b0 + 2 * kk, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          tc::mma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        tc::mma_commit(&tfull[acc]);
+        acc_phase[acc] ^= 1;
+        acc ^= 1;
+      }
+      // no tcgen05.mma may still be running when TMEM is released below
+      tc::mma_commit(mma_done);
+      volatile int never = 0;
+      tc::mbar_wait_bounded(mma_done, 0, &never, err, 5);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    uint32_t acc_phase[2] = {0, 0};
+    int acc = 0;
+    for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
+      const int split = u % p.splits, tile = u / p.splits;
+      const int n_tile = tile % p.n_tiles, m_tile = tile / p.n_tiles;
+      if (!tc::mbar_wait_bounded(&tfull[acc], acc_phase[acc], abort_flag, err, 4)) break;
+      tc::tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
+      const int feat = n_tile * 128 + row;
+      if (p.splits == 1) {
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tc::tmem_ld16(t_row + c0, v);
+          epilogue_store<EPI>(p, v, row, n_tile, m_tile * BN + c0, xchg, quad, lane);
+        }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+        if constexpr (EPI == EPI_PUSH) publish_tile(p, last_flag);
+      } else {
+        const size_t ws_rows = (size_t)p.m_tiles * BN;
+        float* ws_split = p.ws + (size_t)split * ws_rows * p.N;
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tc::tmem_ld16(t_row + c0, v);
+          if (feat < p.N) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) ws_split[((size_t)m_tile * BN + c0 + j) * p.N + feat] = v[j];
+          }
+        }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+        __threadfence();
+        epi_bar();
+        if (threadIdx.x == 64) {
+          const int old = atomicAdd(&p.counters[tile], 1);
+          *last_flag = (old == p.splits - 1);
+        }
+        epi_bar();
+        const bool last = *last_flag != 0;
+        epi_bar();  // everyone has read last_flag before it is rewritten
+        if (last) {
+          __threadfence();
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = 0.f;
+            if (feat < p.N) {
+              for (int s = 0; s < p.splits; ++s) {
+                const float* src = p.ws + (size_t)s * ws_rows * p.N + ((size_t)m_tile * BN + c0) * p.N + feat;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] += __ldcg(src + (size_t)j * p.N);
+              }
+            }
+            epilogue_store<EPI>(p, v, row, n_tile, m_tile * BN + c0, xchg, quad, lane);
+          }
+          if (threadIdx.x == 64) p.counters[tile] = 0;
+          if constexpr (EPI == EPI_PUSH) publish_tile(p, last_flag);
+        }
+      }
+      acc_phase[acc] ^= 1;
+      acc ^= 1;
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) {
+    // error path: give TMA copies that may still be landing in shared memory time to finish
+    const uint64_t until = globaltimer_ns() + 100000ull;
+    while (globaltimer_ns() < until) {
+    }
+  }
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+
+template <int BN, int EPI>
+void launch_gemm(const CUtensorMap& tw, const CUtensorMap& ta, const GemmParams& p, int grid, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    B200_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)Cfg::SMEM));
+    attr_set = true;
+  }
+  launch_pdl(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(192), Cfg::SMEM, stream, tw, ta, p);
+}
+
+// one translation unit per BN (gemm_tc_bn*.cu) instantiates this for every epilogue
+template <int BN>
+void launch_gemm_bn(int epi, const CUtensorMap& tw, const CUtensorMap& ta, const GemmParams& p, int grid,
+                    cudaStream_t stream);
+
+}  // namespace b200

@@ -16,11 +16,39 @@ struct PartPtrs {
 
 // y = rmsnorm(sum(parts) [+ residual_in]) * w ; residual_out = the pre-norm sum.
 // One CTA per row, 8 bf16 per thread per step, at most 4 steps (H <= 32768 with 1024 threads).
+// Wait (one thread per CTA) until every rank has published this step's epoch
+// for the site; bounded by a 2 s deadline, after which an error code is
+// recorded and the CTA proceeds (the host raises on the error word).
+__device__ __forceinline__ void wait_peer_flags(const int* flags, const int* epoch, int n, int* err) {
+  if (threadIdx.x == 0) {
+    const int e = *epoch;
+    const uint64_t deadline = globaltimer_ns() + 2000000000ull;
+    for (int r = 0; r < n; ++r) {
+      uint32_t it = 0;
+      while (true) {
+        int v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
+        if (v == e) break;
+        if ((++it & 1023u) == 0 && globaltimer_ns() > deadline) {
+          if (err) atomicExch(err, 100 + r);
+          r = n;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
 template <int VPT>
 __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
     PartPtrs parts, int nparts, const __nv_bfloat16* residual_in, __nv_bfloat16* residual_out,
-    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H, float eps) {
+    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H, float eps,
+    const int* wait_flags, const int* epoch, int* err) {
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
+  if (wait_flags) wait_peer_flags(wait_flags, epoch, nparts, err);
   const int row = blockIdx.x;
   const size_t base = (size_t)row * H;
   float v[VPT][8];
@@ -30,11 +58,13 @@ __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
     const int col = (threadIdx.x + s * blockDim.x) * 8;
     if (col < H) {
       float acc[8];
-      bf16x8 a = *reinterpret_cast<const bf16x8*>(parts.p[0] + base + col);
-      unpack8(a, acc);
+      // partials may have been written by other GPUs: read through L2, not L1
+      uint4 a4 = __ldcg(reinterpret_cast<const uint4*>(parts.p[0] + base + col));
+      unpack8(*reinterpret_cast<bf16x8*>(&a4), acc);
       for (int k = 1; k < nparts; ++k) {
         float t[8];
-        unpack8(*reinterpret_cast<const bf16x8*>(parts.p[k] + base + col), t);
+        uint4 t4 = __ldcg(reinterpret_cast<const uint4*>(parts.p[k] + base + col));
+        unpack8(*reinterpret_cast<bf16x8*>(&t4), t);
 #pragma unroll
         for (int i = 0; i < 8; ++i) acc[i] += t[i];
       }
@@ -81,6 +111,8 @@ __global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __n
                                 __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache, int T,
                                 int nq, int nkv, float eps) {
   constexpr int E = HD / 32;
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int nslots = nq + 2 * nkv;
@@ -141,6 +173,8 @@ __global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __n
 // column blocks: [g(0..63) u(0..63) g(64..127) u(64..127) ...].
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ act, int T,
                                 int I) {
+  pdl_wait();
+  pdl_trigger();
   const size_t n8 = (size_t)T * I / 8;
   for (size_t v = blockIdx.x * (size_t)blockDim.x + threadIdx.x; v < n8; v += (size_t)gridDim.x * blockDim.x) {
     const size_t e = v * 8;
@@ -162,6 +196,8 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloa
 
 __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                                  __nv_bfloat16* __restrict__ out, int H, int vocab) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   int id = ids[t];
   id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
@@ -174,8 +210,9 @@ __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat1
 
 using namespace b200;
 
-void rmsnorm_fused(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
-                   c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps) {
+void rmsnorm_fused_impl(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
+                        c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps,
+                        const int* wait_flags, const int* epoch, int* err) {
   TORCH_CHECK(!parts.empty() && parts.size() <= 8, "1..8 partial inputs");
   const int H = parts[0].size(-1);
   const int T = parts[0].numel() / H;
@@ -194,13 +231,27 @@ void rmsnorm_fused(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor
   auto wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   switch (vpt) {
-    case 1: rmsnorm_fused_kernel<1><<<T, threads, 0, stream>>>(pp, parts.size(), rin, rout, wp, op, H, eps); break;
-    case 2: rmsnorm_fused_kernel<2><<<T, threads, 0, stream>>>(pp, parts.size(), rin, rout, wp, op, H, eps); break;
+    case 1: launch_pdl(rmsnorm_fused_kernel<1>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err); break;
+    case 2: launch_pdl(rmsnorm_fused_kernel<2>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err); break;
     case 3:
-    case 4: rmsnorm_fused_kernel<4><<<T, threads, 0, stream>>>(pp, parts.size(), rin, rout, wp, op, H, eps); break;
+    case 4: launch_pdl(rmsnorm_fused_kernel<4>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err); break;
     default: TORCH_CHECK(false, "hidden size too large");
   }
   B200_CHECK_CUDA(cudaGetLastError());
+}
+
+void rmsnorm_fused(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
+                   c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps) {
+  rmsnorm_fused_impl(parts, residual_in, residual_out, w, out, eps, nullptr, nullptr, nullptr);
+}
+
+// Same, after waiting for the peers' flags of a fused all-reduce site
+// (flags_ptr: this rank's [world] flag words of the site; one per part).
+void rmsnorm_fused_wait(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
+                        c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps,
+                        int64_t flags_ptr, int64_t epoch_ptr, int64_t err_ptr) {
+  rmsnorm_fused_impl(parts, residual_in, residual_out, w, out, eps, reinterpret_cast<const int*>(flags_ptr),
+                     reinterpret_cast<const int*>(epoch_ptr), reinterpret_cast<int*>(err_ptr));
 }
 
 void qkv_post(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
@@ -217,14 +268,14 @@ void qkv_post(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optiona
   const int blocks = (warps * 32 + threads - 1) / threads;
   auto stream = at::cuda::getCurrentCUDAStream();
 #define B200_QKV(HDV)                                                                                       \
-  qkv_post_kernel<HDV><<<blocks, threads, 0, stream>>>(                                                     \
+  launch_pdl(qkv_post_kernel<HDV>, dim3(blocks), dim3(threads), 0, stream,                                  \
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),                                               \
       bias ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr,                            \
       qn_w ? reinterpret_cast<const __nv_bfloat16*>(qn_w->data_ptr()) : nullptr,                            \
       kn_w ? reinterpret_cast<const __nv_bfloat16*>(kn_w->data_ptr()) : nullptr, cos_sin.data_ptr<float>(), \
       positions.data_ptr<int>(), slots.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), \
       reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()), reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), T, \
-      nq, nkv, eps)
+      (int)nq, (int)nkv, (float)eps)
   if (HD == 128) B200_QKV(128);
   else if (HD == 64) B200_QKV(64);
   else TORCH_CHECK(false, "head_dim must be 64 or 128");
@@ -240,8 +291,8 @@ void silu_mul(torch::Tensor gu, torch::Tensor act) {
   const size_t n8 = (size_t)T * I / 8;
   const int threads = 256;
   const int blocks = (int)std::min<size_t>((n8 + threads - 1) / threads, 148 * 16);
-  silu_mul_kernel<<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), reinterpret_cast<__nv_bfloat16*>(act.data_ptr()), T, I);
+  launch_pdl(silu_mul_kernel, dim3(blocks), dim3(threads), 0, at::cuda::getCurrentCUDAStream(),
+             reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), reinterpret_cast<__nv_bfloat16*>(act.data_ptr()), T, I);
   B200_CHECK_CUDA(cudaGetLastError());
 }
 
@@ -249,8 +300,8 @@ void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out) {
   const int T = ids.numel();
   const int H = table.size(1);
   if (T == 0) return;
-  embedding_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
-      ids.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), H, table.size(0));
+  launch_pdl(embedding_kernel, dim3(T), dim3(128), 0, at::cuda::getCurrentCUDAStream(),
+             (const int*)ids.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
+             reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), H, (int)table.size(0));
   B200_CHECK_CUDA(cudaGetLastError());
 }

@@ -1,0 +1,172 @@
+"""In-kernel tensor-parallel all-reduce over NVLink P2P (decode-sized outputs).
+
+Each rank owns one CUDA IPC region, mapped by every other rank:
+  data  [2 slots][world][max_tokens][hidden] bf16   (slot = site parity)
+  flags [n_sites][world] int32                      (flag[site][r] = epoch of r's push)
+Row-parallel GEMMs (o_proj, down) run ``gemm_tc_push``: the epilogue stores
+each bf16 tile into slot [site % 2][my rank] of every rank and the last CTA
+raises flag[site][my rank] = epoch on every rank. The next fused add+RMSNorm
+kernel waits for all ``world`` flags of the site (bounded wait) and sums the
+``world`` local slots, so the reduction costs no extra kernel and no NCCL
+call. Outputs with more tokens than ``max_tokens`` (prefill chunks) use NCCL,
+which runs them through NVLS at full bandwidth.
+
+The epoch is a device counter bumped by a one-thread kernel at the start of
+every forward (inside the CUDA graph as well), so flags never need resetting.
+A wait that runs out records a code in a host-mapped error word; ``check()``
+raises ``CollectiveTimeout`` on the host.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from b200serve import ops
+from b200serve.parallel.dist import NcclComm
+
+
+class CollectiveTimeout(RuntimeError):
+    """A fused collective's bounded wait expired (a peer rank did not publish)."""
+
+
+def fused_available() -> bool:
+    try:
+        return hasattr(ops.ext(), "gemm_tc_push")
+    except Exception:
+        return False
+
+
+class FusedParts(list):
+    """The local receive slots of one site plus what the consumer must wait for."""
+
+    def __init__(self, views, flags_ptr, epoch_ptr, err_ptr):
+        super().__init__(views)
+        self.flags_ptr, self.epoch_ptr, self.err_ptr = flags_ptr, epoch_ptr, err_ptr
+
+
+class FusedComm:
+    kind = "fused-p2p"
+
+    def __init__(self, group, device, model_cfg, cfgE, max_tokens: int = None):
+        self.nccl = NcclComm(group, device)
+        self.group = group
+        self.world = self.nccl.world
+        self.rank = self.nccl.rank
+        self.device = torch.device(device)
+        H = model_cfg.hidden_size
+        self.H = H
+        self.max_tokens = max_tokens or max(cfgE.max_batch, 64)
+        self.n_sites = 2 * model_cfg.num_layers + 4
+        self.slot_elems = self.max_tokens * H
+        data_bytes = 2 * self.world * self.slot_elems * 2
+        self.flag_off = (data_bytes + 4095) // 4096 * 4096
+        total = self.flag_off + self.n_sites * self.world * 4
+        e = ops.ext()
+        self.base = e.ipc_malloc(total)
+        handle = e.ipc_handle(self.base)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.tolist(), group=group)
+        self.peer = []
+        for r in range(self.world):
+            if r == self.rank:
+                self.peer.append(self.base)
+            else:
+                self.peer.append(e.ipc_open(torch.tensor(handles[r], dtype=torch.uint8)))
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.tile_done = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.err = e.host_error_word()       # [host ptr, device ptr]
+        self.err_host, self.err_dev = int(self.err[0]), int(self.err[1])
+        self.ws = ops.GemmWorkspace(self.device, max_elems=8 << 20, max_tiles=1 << 14)
+        self.site = 0
+        self._views = {}
+        self._ptrs = {}
+        dist.barrier(group=group)
+
+    # ------------------------------------------------------------ helpers
+    def _slot_ptr(self, rank_base: int, slot: int, src_rank: int) -> int:
+        return rank_base + (slot * self.world + src_rank) * self.slot_elems * 2
+
+    def _flag_ptr(self, rank_base: int, site: int, src_rank: int) -> int:
+        return rank_base + self.flag_off + (site * self.world + src_rank) * 4
+
+    def _local_views(self, slot: int, T: int):
+        key = (slot, T)
+        if key not in self._views:
+            vs = []
+            for r in range(self.world):
+                storage = _tensor_from_ptr(self._slot_ptr(self.base, slot, r), T * self.H, self.device)
+                vs.append(storage.view(T, self.H))
+            self._views[key] = vs
+        return self._views[key]
+
+    def _push_ptrs(self, site: int):
+        if site not in self._ptrs:
+            slot = site % 2
+            dst = torch.tensor([self._slot_ptr(self.peer[r], slot, self.rank) for r in range(self.world)],
+                               dtype=torch.int64)
+            flg = torch.tensor([self._flag_ptr(self.peer[r], site, self.rank) for r in range(self.world)],
+                               dtype=torch.int64)
+            self._ptrs[site] = (dst, flg)
+        return self._ptrs[site]
+
+    # ------------------------------------------------------------ comm interface
+    def begin_step(self):
+        ops._cuda(self.epoch)
+        ops.ext().epoch_inc(self.epoch.data_ptr())
+        self.site = 0
+
+    def linear_reduce(self, x: torch.Tensor, w: torch.Tensor, tag: str):
+        """Row-parallel GEMM + all-reduce. Returns the parts the next RMSNorm sums."""
+        T = x.shape[0]
+        if T > self.max_tokens:
+            y = ops.linear(x, w)
+            return self.nccl.reduce_parts(y, tag)
+        site = self.site
+        self.site += 1
+        assert site < self.n_sites, "more fused sites than allocated"
+        dst, flg = self._push_ptrs(site)
+        ops._cuda(x)
+        packed_n = w.N if isinstance(w, ops.PackedWeight) else 0
+        ops.ext().gemm_tc_push(x, w.data if packed_n else w, dst, self.H, flg, self.epoch.data_ptr(), self.tile_done,
+                               None, self.ws.ws, self.ws.counters, self.err_dev, packed_n)
+        return FusedParts(self._local_views(site % 2, T), self._flag_ptr(self.base, site, 0),
+                          self.epoch.data_ptr(), self.err_dev)
+
+    def reduce_parts(self, t: torch.Tensor, tag: str):
+        return self.nccl.reduce_parts(t, tag)
+
+    def all_gather_small(self, t):
+        return self.nccl.all_gather_small(t)
+
+    def gather_vocab(self, logits):
+        return self.nccl.gather_vocab(logits)
+
+    def broadcast(self, t, src=0):
+        return self.nccl.broadcast(t, src)
+
+    def barrier(self):
+        self.nccl.barrier()
+
+    def check(self):
+        code = ops.ext().read_host_word(self.err_host, 0, True)
+        if code:
+            raise CollectiveTimeout(f"fused all-reduce wait expired on rank {self.rank} (code {code})")
+
+    def close(self):
+        e = ops.ext()
+        for r, p in enumerate(self.peer):
+            if r != self.rank:
+                e.ipc_close(p)
+        e.ipc_free(self.base)
+        self.peer = []
+
+
+def _tensor_from_ptr(ptr: int, numel: int, device) -> torch.Tensor:
+    """A bf16 view of device memory owned by FusedComm (no copy, no ownership):
+    built through the CUDA array interface on int16, then reinterpreted."""
+    class _CAI:
+        def __init__(self):
+            self.__cuda_array_interface__ = {"shape": (numel,), "typestr": "<i2", "data": (ptr, False),
+                                             "version": 3, "strides": None}
+    return torch.as_tensor(_CAI(), device=device).view(torch.bfloat16)

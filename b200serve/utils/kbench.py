@@ -43,9 +43,11 @@ def bench_gemm(cases=None):
         x = torch.randn(M, K, device="cuda").bfloat16()
         w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
         epi = ops.EPI_F32 if "lm_head" in name else ops.EPI_BF16
+        w_plain = w
+        w = ops.pack_weight(w)
         y = ops.linear(x, w, epilogue=epi)
         ms = time_cuda(lambda: ops.linear(x, w, epilogue=epi, out=y))
-        ms_ref = time_cuda(lambda: torch.matmul(x, w.t()))
+        ms_ref = time_cuda(lambda: torch.matmul(x, w_plain.t()))
         byts = (M * K + N * K) * 2 + M * N * (4 if epi == ops.EPI_F32 else 2)
         flops = 2.0 * M * N * K
         plan = ops.ext().gemm_plan(M, N, K, epi, torch.cuda.get_device_properties(0).multi_processor_count)
@@ -70,9 +72,8 @@ def bench_attn():
         bt = torch.arange(B * nblk, device="cuda", dtype=torch.int32).view(B, nblk)
         sl = torch.full((B,), L, dtype=torch.int32, device="cuda")
         q = torch.randn(B, nq, hd, device="cuda").bfloat16()
-        target = 2 * 148
-        want = max(1, (target + B * nkv - 1) // (B * nkv))
-        tps = max(64, ((L + want - 1) // want + 15) // 16 * 16)
+        per = B * nkv               # the engine's plan (engine/runner.py attn_plan)
+        tps = 64 if per <= 16 else 128 if per <= 64 else 256
         nsplit = (L + tps - 1) // tps
         ws = ops.AttnWorkspace("cuda", B, nkv, nq // nkv, hd, nsplit)
         scale = 1 / math.sqrt(hd)
@@ -97,11 +98,40 @@ def run_one(M, N, K, iters=5):
     print(json.dumps({"case": "one", "M": M, "N": N, "K": K, "ok": True}))
 
 
+def decode_step(layers=2, B=32, ctx=2304, iters=3):
+    """Eager decode steps of the Qwen3-8B shape (``layers`` layers) at batch B and
+    context ``ctx``: the kernel sequence of one step, for launch lists / ncu."""
+    from b200serve.engine.kv_cache import KVCache
+    from b200serve.engine.runner import ModelRunner
+    from b200serve.models.config import get_model_config
+    from b200serve.models.weights import random_weights
+    cfg = get_model_config("qwen3-8b", layers)
+    w = random_weights(cfg, seed=0, device="cuda")
+    nb = (ctx + 32) // 16
+    kv = KVCache(cfg.num_layers, B * nb + 8, cfg.num_kv_heads, cfg.head_dim, device="cuda")
+    kv.k.normal_(0, 1)
+    kv.v.normal_(0, 1)
+    r = ModelRunner(cfg, w, kv, device="cuda", max_batch=B, max_seq=nb * 16, use_graphs=False)
+    tables = [list(range(b * nb, (b + 1) * nb)) for b in range(B)]
+    ids = [1] * B
+    pos = [ctx] * B
+    slots = [t[ctx // 16] * 16 + ctx % 16 for t in tables]
+    lens = [ctx + 1] * B
+    for _ in range(iters):
+        r.decode(ids, pos, slots, tables, lens, greedy=True)
+    torch.cuda.synchronize()
+    ms = time_cuda(lambda: r.decode(ids, pos, slots, tables, lens, greedy=True), iters=10, warmup=2)
+    print(json.dumps({"case": "decode_step", "layers": layers, "B": B, "ctx": ctx, "eager_ms": round(ms, 3)}))
+
+
 if __name__ == "__main__":
     what = sys.argv[1] if len(sys.argv) > 1 else "all"
     ops.ext()
     if what == "one":
         run_one(*[int(v) for v in sys.argv[2:5]])
+        sys.exit(0)
+    if what == "decode_step":
+        decode_step(*[int(v) for v in sys.argv[2:5]])
         sys.exit(0)
     if what in ("gemm", "all"):
         bench_gemm()

@@ -180,3 +180,72 @@ def test_silu_mul_and_embedding():
     table = torch.randn(1000, H, device=dev).bfloat16()
     ids = torch.randint(0, 1000, (T,), device=dev, dtype=torch.int32)
     assert torch.equal(ops.embedding(ids, table), table[ids.long()])
+
+
+def _sample_many(logits, n, **kw):
+    B = logits.shape[0]
+    outs = []
+    for step in range(n):
+        outs.append(ops.sample_rows(logits.clone(), [kw.get("t", 1.0)] * B, [kw.get("k", 0)] * B,
+                                    [kw.get("p", 1.0)] * B, [kw.get("minp", 0.0)] * B, [123] * B, [step] * B))
+    return torch.stack(outs)
+
+
+def test_sampler_greedy_and_support():
+    V = 151936
+    logits = torch.randn(4, V, device=dev) * 3
+    g = ops.sample_rows(logits.clone(), [0.0] * 4, [0] * 4, [1.0] * 4, [0.0] * 4, [1] * 4, [0] * 4)
+    assert torch.equal(g.long(), logits.argmax(-1))
+    # top-k: every draw is within the k largest
+    draws = _sample_many(logits, 64, t=1.0, k=5)
+    top5 = logits.topk(5, dim=-1).indices
+    for b in range(4):
+        assert set(draws[:, b].tolist()) <= set(top5[b].tolist())
+    # top-p: every draw is inside the nucleus (smallest prefix with mass >= p)
+    probs = torch.softmax(logits, -1)
+    sp, si = probs.sort(-1, descending=True)
+    draws = _sample_many(logits, 64, t=1.0, p=0.5)
+    for b in range(4):
+        n = int((sp[b].cumsum(0) < 0.5).sum().item()) + 1
+        assert set(draws[:, b].tolist()) <= set(si[b, :n].tolist())
+    # min-p: only tokens with p >= 0.2 * p_max
+    draws = _sample_many(logits, 32, t=1.0, minp=0.2)
+    for b in range(4):
+        ok = (probs[b] >= 0.2 * probs[b].max()).nonzero().view(-1).tolist()
+        assert set(draws[:, b].tolist()) <= set(ok)
+
+
+def test_sampler_distribution_and_seed():
+    V = 64
+    logits = torch.randn(1, V, device=dev)
+    n = 4000
+    draws = torch.cat([ops.sample_rows(logits.clone(), [1.0], [0], [1.0], [0.0], [9], [s]) for s in range(n)])
+    freq = torch.bincount(draws.long(), minlength=V).float() / n
+    p = torch.softmax(logits[0], -1)
+    assert (freq - p).abs().max().item() < 0.04
+    again = torch.cat([ops.sample_rows(logits.clone(), [1.0], [0], [1.0], [0.0], [9], [s]) for s in range(50)])
+    assert torch.equal(again, draws[:50])
+
+
+def test_sampler_penalties():
+    V = 100
+    logits = torch.zeros(1, V, device=dev)
+    logits[0, 7] = 5.0
+    ids = torch.tensor([[7, -1]], dtype=torch.int32, device=dev)
+    cnt = torch.tensor([[3.0, 0.0]], device=dev)
+    vals = torch.tensor([[1.0, 0.0, 2.0]], device=dev)   # frequency penalty 2 * count 3 = -6
+    lg = logits.clone()
+    t = ops.sample_rows(lg, [0.0], [0], [1.0], [0.0], [1], [0], ids, cnt, vals)
+    assert lg[0, 7].item() == pytest.approx(-1.0)
+    assert t.item() != 7
+
+
+@pytest.mark.parametrize("M,N,K", [(32, 4096, 4096), (5, 1000, 704), (200, 18992, 512)])
+def test_gemm_packed_weight(M, N, K):
+    x = torch.randn(M, K, device=dev).bfloat16()
+    w = (torch.randn(N, K, device=dev) * 0.05).bfloat16()
+    pw = ops.pack_weight(w)
+    assert torch.equal(pw.unpacked(), w)
+    ref = x.float() @ w.float().t()
+    assert _rel(ops.linear(x, pw), ref) < 1e-2
+    assert _rel(ops.linear(x, pw, epilogue=ops.EPI_F32), ref) < 1e-4
