@@ -57,7 +57,7 @@ class ModelRunner:
 
     def attn_plan(self, bucket: int):
         per = bucket * self.decoder.nkv
-        tps = 64 if per <= 16 else 128 if per <= 64 else 256
+        tps = 64 if per <= 16 else 128 if per <= 64 else 256 if per <= 128 else 512
         return tps, (self.max_seq + tps - 1) // tps
 
     def _decode_fb(self, bucket: int) -> ForwardBatch:

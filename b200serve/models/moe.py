@@ -42,8 +42,13 @@ def expert_hf_tensors(cfg, lw, pre) -> dict:
 
 def topk_softmax(logits: torch.Tensor, k: int, renormalize: bool = True):
     """(weights [T, k] fp32, expert ids [T, k] int32): softmax in fp32, top-k, optional renorm."""
-    if logits.is_cuda and ops.extension_loaded() and hasattr(ops.ext(), "topk_softmax"):
-        return ops.ext_topk_softmax(logits, k, renormalize)
+    if logits.is_cuda:
+        T = logits.shape[0]
+        w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+        ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+        ops._cuda(logits)
+        ops.ext().topk_softmax(logits.float().contiguous(), k, renormalize, w, ids)
+        return w, ids
     p = torch.softmax(logits.float(), dim=-1)
     w, idx = torch.topk(p, k, dim=-1)
     if renormalize:
@@ -51,15 +56,65 @@ def topk_softmax(logits: torch.Tensor, k: int, renormalize: bool = True):
     return w, idx.to(torch.int32)
 
 
+def pack_experts(stacked: torch.Tensor):
+    """[E, N, K] -> (packed [E * n_tiles * k_blocks * 128, 64], N): every expert tile-packed
+    for the grouped tcgen05 GEMM, experts back to back."""
+    blocks = [ops.PackedWeight(stacked[e]).data for e in range(stacked.shape[0])]
+    return torch.cat(blocks, 0), stacked.shape[1]
+
+
 class MoEBlock:
+    """Expert FFN of every MoE layer. On CUDA: router GEMM -> top-k kernel ->
+    permutation (this rank's experts only) -> row gather -> grouped SwiGLU GEMM ->
+    grouped down GEMM -> weighted combine. The caller sums the combine output over
+    expert-parallel ranks (tokens are replicated on every rank, so dispatch needs
+    no communication and the combine is one all-reduce of [T, H])."""
+
     def __init__(self, cfg, weights, comm=None, device="cpu"):
         self.cfg = cfg
         self.w = weights
         self.comm = comm
         self.per = cfg.num_experts // weights.ep_size
         self.e0 = weights.ep_rank * self.per
+        self.packed = {}
+        if torch.device(device).type == "cuda":
+            for i, lw in enumerate(weights.layers):
+                gu, n_gu = pack_experts(lw.experts_gate_up)
+                dn, n_dn = pack_experts(lw.experts_down)
+                self.packed[i] = (gu, n_gu, dn, n_dn)
+                lw.experts_gate_up = lw.experts_down = None
+            torch.cuda.empty_cache()
+
+    def _cuda(self, layer, x):
+        cfg = self.cfg
+        lw = self.w.layers[layer]
+        T, H = x.shape
+        k = cfg.experts_per_tok
+        E = self.per
+        e = ops.ext()
+        logits = ops.linear(x, lw.router, epilogue=ops.EPI_F32)
+        wts, ids = topk_softmax(logits, k, cfg.norm_topk_prob)
+        dev = x.device
+        offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        pos = torch.empty(T * k, dtype=torch.int32, device=dev)
+        sorted_tok = torch.empty(T * k, dtype=torch.int32, device=dev)
+        e.moe_permute(ids, k, self.e0, E, offsets, pos, sorted_tok)
+        xs = torch.empty(T * k, H, dtype=x.dtype, device=dev)
+        e.gather_rows(x, sorted_tok, offsets[E:], xs)
+        gu, n_gu, dn, n_dn = self.packed[layer]
+        ws = ops.default_workspace(dev)
+        act = torch.empty(T * k, n_gu // 2, dtype=x.dtype, device=dev)
+        e.gemm_grouped(xs, gu, n_gu, E, offsets, T, act, ws.ws, ws.counters, ops.EPI_SWIGLU)
+        y = torch.empty(T * k, n_dn, dtype=x.dtype, device=dev)
+        e.gemm_grouped(act, dn, n_dn, E, offsets, T, y, ws.ws, ws.counters, ops.EPI_BF16)
+        out = torch.empty(T, H, dtype=x.dtype, device=dev)
+        e.moe_combine(y, wts, pos, k, out)
+        ops._launches[0] += 8
+        return out
 
     def __call__(self, layer: int, x: torch.Tensor) -> torch.Tensor:
+        if x.is_cuda:
+            return self._cuda(layer, x)
         cfg = self.cfg
         lw = self.w.layers[layer]
         logits = ops.linear(x, lw.router, epilogue=ops.EPI_F32)

@@ -309,7 +309,7 @@ class AttnWorkspace:
         self.max_splits = max_splits
 
 
-_FORCE_SIMT_DECODE = os.environ.get("B200_TC_DECODE", "0") != "1"   # tensor-core decode attention: opt-in until validated on GPU
+_FORCE_SIMT_DECODE = os.environ.get("B200_TC_DECODE", "1") == "0"   # B200_TC_DECODE=0 selects the CUDA-core kernel
 
 
 def paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, scale, tps=256, nsplit=1,

@@ -34,11 +34,18 @@ void paged_decode_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Te
                                torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
                                torch::Tensor part_acc, torch::Tensor part_ml, double scale, int64_t tps,
                                int64_t nsplit);
+void topk_softmax(torch::Tensor logits, int64_t k, bool renorm, torch::Tensor w_out, torch::Tensor id_out);
+void moe_permute(torch::Tensor ids, int64_t k, int64_t e0, int64_t E, torch::Tensor offsets, torch::Tensor pos,
+                 torch::Tensor sorted_tok);
+void gather_rows(torch::Tensor x, torch::Tensor rows, torch::Tensor count, torch::Tensor out);
+void moe_combine(torch::Tensor y, torch::Tensor w, torch::Tensor pos, int64_t k, torch::Tensor out);
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi, int64_t num_sms);
 void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> bias,
              c10::optional<torch::Tensor> residual, torch::Tensor ws, torch::Tensor counters, int64_t epi,
              int64_t force_splits, int64_t packed_n);
 int64_t gemm_error_flag(bool reset);
+void gemm_grouped(torch::Tensor act, torch::Tensor w_packed, int64_t N, int64_t E, torch::Tensor offsets,
+                  int64_t max_rows, torch::Tensor out, torch::Tensor ws, torch::Tensor counters, int64_t epi);
 void argmax_rows(torch::Tensor logits, torch::Tensor out_idx, torch::Tensor out_val, int64_t index_offset);
 void argmax_merge(torch::Tensor vals, torch::Tensor idx, torch::Tensor out);
 void sample_rows(torch::Tensor logits, torch::Tensor params, torch::Tensor pen_ids, torch::Tensor pen_counts,
@@ -63,9 +70,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_decode_attention", &paged_decode_attention);
   m.def("paged_prefill_attention", &paged_prefill_attention);
   m.def("paged_decode_attention_tc", &paged_decode_attention_tc);
+  m.def("topk_softmax", &topk_softmax);
+  m.def("moe_permute", &moe_permute);
+  m.def("gather_rows", &gather_rows);
+  m.def("moe_combine", &moe_combine);
   m.def("gemm_plan", &gemm_plan);
   m.def("gemm_tc", &gemm_tc);
   m.def("gemm_error_flag", &gemm_error_flag);
+  m.def("gemm_grouped", &gemm_grouped);
   m.def("argmax_rows", &argmax_rows);
   m.def("argmax_merge", &argmax_merge);
   m.def("sample_rows", &sample_rows);

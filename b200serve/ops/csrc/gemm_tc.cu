@@ -142,7 +142,8 @@ void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optiona
   }
   if (epi == EPI_SWIGLU) TORCH_CHECK(N % 128 == 0 && out.size(1) == N / 2, "SwiGLU needs N % 128 == 0");
   if (p.splits > 1) {
-    TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.numel() >= (int64_t)p.splits * p.m_tiles * BN * N,
+    TORCH_CHECK(ws.scalar_type() == at::kFloat &&
+                    ws.numel() >= (int64_t)p.splits * p.m_tiles * p.n_tiles * BN * 128,
                 "GEMM workspace too small");
     TORCH_CHECK(counters.scalar_type() == at::kInt && counters.numel() >= p.m_tiles * p.n_tiles,
                 "GEMM counters too small");
@@ -185,7 +186,7 @@ void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, in
   p.ldo = ldo;
   p.bias = bias ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
   if (p.splits > 1) {
-    TORCH_CHECK(ws.numel() >= (int64_t)p.splits * p.m_tiles * BN * N, "GEMM workspace too small");
+    TORCH_CHECK(ws.numel() >= (int64_t)p.splits * p.m_tiles * p.n_tiles * BN * 128, "GEMM workspace too small");
     TORCH_CHECK(counters.numel() >= p.m_tiles * p.n_tiles, "GEMM counters too small");
     p.ws = ws.data_ptr<float>();
     p.counters = counters.data_ptr<int>();
@@ -204,6 +205,43 @@ void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, in
   CUtensorMap tw = weight_tmap(w, N, K, packed);
   CUtensorMap ta = make_tmap_bf16(act.data_ptr(), M, K, act.stride(0), BN);
   launch_by_bn(BN, EPI_PUSH, tw, ta, p, grid, at::cuda::getCurrentCUDAStream());
+}
+
+// Grouped expert GEMM: act [R, K] rows sorted by expert, offsets [E+1] (device), w packed
+// [E][n_tiles][k_blocks][128][64] (logical per-expert [N, K]); out [R, N] bf16 or [R, N/2] (SwiGLU).
+// max_rows bounds the rows of one expert (sizes the m-tile grid without reading offsets on the host).
+void gemm_grouped(torch::Tensor act, torch::Tensor w_packed, int64_t N, int64_t E, torch::Tensor offsets,
+                  int64_t max_rows, torch::Tensor out, torch::Tensor ws, torch::Tensor counters, int64_t epi) {
+  TORCH_CHECK(act.scalar_type() == at::kBFloat16 && w_packed.scalar_type() == at::kBFloat16);
+  TORCH_CHECK(epi == EPI_BF16 || epi == EPI_SWIGLU, "grouped GEMM epilogue must be bf16 or SwiGLU");
+  const int R = act.size(0), K = act.size(1);
+  if (R == 0 || E == 0) return;
+  if (g_num_sms == 0) {
+    int dev;
+    B200_CHECK_CUDA(cudaGetDevice(&dev));
+    B200_CHECK_CUDA(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
+  }
+  const int BN = max_rows <= 16 ? 16 : max_rows <= 32 ? 32 : max_rows <= 64 ? 64 : max_rows <= 128 ? 128 : 256;
+  GemmParams p{};
+  p.M = R; p.N = N; p.K = K;
+  p.n_tiles = (N + 127) / 128;
+  p.m_tiles = (max_rows + BN - 1) / BN;
+  p.kb_total = (K + 63) / 64;
+  p.splits = 1;
+  p.kb_per_split = p.kb_total;
+  p.units = E * p.m_tiles * p.n_tiles;
+  p.grouped = 1;
+  p.g_offsets = offsets.data_ptr<int>();
+  p.g_E = E;
+  p.w_packed = 1;
+  p.out = out.data_ptr();
+  p.ldo = out.stride(0);
+  p.err = gemm_err_word();
+  TORCH_CHECK(w_packed.size(1) == 64 && w_packed.size(0) == E * p.n_tiles * p.kb_total * 128, "bad packed expert weight");
+  CUtensorMap tw = make_tmap_bf16(w_packed.data_ptr(), w_packed.size(0), 64, 64, 128);
+  CUtensorMap ta = make_tmap_bf16(act.data_ptr(), R, K, act.stride(0), BN);
+  const int grid = std::min(p.units, g_num_sms);
+  launch_by_bn(BN, (int)epi, tw, ta, p, grid, at::cuda::getCurrentCUDAStream());
 }
 
 int64_t gemm_error_flag(bool reset) {

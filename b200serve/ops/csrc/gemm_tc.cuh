@@ -35,6 +35,12 @@ constexpr int kMaxPeers = 8;
 struct GemmParams {
   int M, N, K;                  // tokens, output features, reduction
   int w_packed;                 // 1: W stored tile-contiguous [n_tile][k_block][128][64]
+  // grouped (mixture-of-experts) mode: expert e owns A rows [g_offsets[e], g_offsets[e+1]) of the
+  // expert-sorted activations and output rows with the same indices; its weight is the e-th
+  // [N, K] block of a packed [E][n_tiles][k_blocks][128][64] tensor. Units = E x m_tiles x n_tiles x splits.
+  int grouped;
+  const int* g_offsets;
+  int g_E;
   int n_tiles, m_tiles, splits, kb_per_split, kb_total, units;
   void* out;                    // bf16 or fp32, row stride ldo (elements)
   int ldo;
@@ -71,7 +77,7 @@ __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: 
 
 // Final epilogue for 16 consecutive tokens [t0, t0+16) of this thread's feature row.
 template <int EPI>
-__device__ __forceinline__ void epilogue_store(const GemmParams& p, float* v, int row, int n_tile, int t0,
+__device__ __forceinline__ void epilogue_store(const GemmParams& p, float* v, int row, int n_tile, int t0, int t_end,
                                                float* xchg, int quad, int lane) {
   if constexpr (EPI == EPI_SWIGLU) {
     // rows 0..63 hold gate features, rows 64..127 the up features of the same 64 columns
@@ -87,7 +93,7 @@ __device__ __forceinline__ void epilogue_store(const GemmParams& p, float* v, in
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int t = t0 + j;
-        if (t < p.M && col < half_n) {
+        if (t < t_end && col < half_n) {
           const float g = v[j];
           const float u = xchg[(quad * 32 + lane) * 17 + j];
           const float sg = __bfloat162float(__float2bfloat16_rn(g / (1.f + __expf(-g))));
@@ -105,7 +111,7 @@ __device__ __forceinline__ void epilogue_store(const GemmParams& p, float* v, in
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int t = t0 + j;
-      if (t >= p.M) break;
+      if (t >= t_end) break;
       const __nv_bfloat16 v16 = __float2bfloat16_rn(v[j] + b);
       for (int r = 0; r < p.world; ++r) p.push_dst[r][(size_t)t * p.ldo + col] = v16;
     }
@@ -116,7 +122,7 @@ __device__ __forceinline__ void epilogue_store(const GemmParams& p, float* v, in
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int t = t0 + j;
-      if (t >= p.M) break;
+      if (t >= t_end) break;
       float x = v[j] + b;
       if constexpr (EPI == EPI_F32) {
         reinterpret_cast<float*>(p.out)[(size_t)t * p.ldo + col] = x;
@@ -128,11 +134,41 @@ __device__ __forceinline__ void epilogue_store(const GemmParams& p, float* v, in
   }
 }
 
+struct Unit {
+  int n_tile, m_tile, split, tile;   // tile: index for split-K counters / push accounting
+  int a_row0, m_lim, w_tile_base;    // first activation row, rows valid, packed weight tile row base
+  bool empty;
+};
+
+__device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int BN) {
+  Unit x;
+  x.split = u % p.splits;
+  x.tile = u / p.splits;
+  x.n_tile = x.tile % p.n_tiles;
+  const int rest = x.tile / p.n_tiles;
+  if (!p.grouped) {
+    x.m_tile = rest;
+    x.a_row0 = x.m_tile * BN;
+    x.m_lim = p.M - x.a_row0;
+    x.w_tile_base = x.n_tile;
+    x.empty = false;
+  } else {
+    x.m_tile = rest % p.m_tiles;
+    const int e = rest / p.m_tiles;
+    const int r0 = __ldg(p.g_offsets + e), r1 = __ldg(p.g_offsets + e + 1);
+    x.a_row0 = r0 + x.m_tile * BN;
+    x.m_lim = r1 - x.a_row0;
+    x.w_tile_base = e * p.n_tiles + x.n_tile;
+    x.empty = x.m_lim <= 0;
+  }
+  return x;
+}
+
 // TMA coordinates of the weight tile (n_tile, k block kb) in the plain [N, K]
 // layout or the tile-contiguous packed layout (each 128x64 tile one 16 KB run).
 __device__ __forceinline__ int w_x(const GemmParams& p, int kb) { return p.w_packed ? 0 : kb * 64; }
-__device__ __forceinline__ int w_y(const GemmParams& p, int n_tile, int kb) {
-  return p.w_packed ? (n_tile * p.kb_total + kb) * 128 : n_tile * 128;
+__device__ __forceinline__ int w_y(const GemmParams& p, int w_tile, int kb) {
+  return p.w_packed ? (w_tile * p.kb_total + kb) * 128 : w_tile * 128;
 }
 
 // EPI_PUSH: after a tile's stores reached every peer, count it; the CTA that
@@ -211,33 +247,31 @@ __global__ void __launch_bounds__(192, 2)
       // Weights never depend on the previous kernel: stream the first stages of W
       // while that kernel finishes, then wait for it before loading activations.
       int pre = 0;
-      if ((int)blockIdx.x < p.units) {
-        const int split = blockIdx.x % p.splits, tile = blockIdx.x / p.splits;
-        const int n_tile = tile % p.n_tiles;
-        const int kb0 = split * p.kb_per_split, kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+      if ((int)blockIdx.x < p.units && !p.grouped) {
+        const Unit x = decode_unit(p, blockIdx.x, BN);
+        const int kb0 = x.split * p.kb_per_split, kb1 = min(p.kb_total, kb0 + p.kb_per_split);
         pre = min(kb1 - kb0, STAGES);
         for (int i = 0; i < pre; ++i) {
           tc::mbar_arrive_expect_tx(&full[i], Cfg::STAGE_BYTES);
-          tc::tma_load_2d(s_w + i * Cfg::W_BYTES, &tm_w, &full[i], w_x(p, kb0 + i), w_y(p, n_tile, kb0 + i), pol_w);
+          tc::tma_load_2d(s_w + i * Cfg::W_BYTES, &tm_w, &full[i], w_x(p, kb0 + i), w_y(p, x.w_tile_base, kb0 + i), pol_w);
         }
         pdl_wait();
-        const int m_tile = tile / p.n_tiles;
         for (int i = 0; i < pre; ++i)
-          tc::tma_load_2d(s_a + i * Cfg::A_BYTES, &tm_a, &full[i], (kb0 + i) * 64, m_tile * BN, pol_a);
+          tc::tma_load_2d(s_a + i * Cfg::A_BYTES, &tm_a, &full[i], (kb0 + i) * 64, x.a_row0, pol_a);
         stage = pre % STAGES;
         phase = pre == STAGES ? 1 : 0;
       } else {
         pdl_wait();
       }
       for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
-        const int split = u % p.splits, tile = u / p.splits;
-        const int n_tile = tile % p.n_tiles, m_tile = tile / p.n_tiles;
-        const int kb0 = split * p.kb_per_split, kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        const Unit x = decode_unit(p, u, BN);
+        if (x.empty) continue;
+        const int kb0 = x.split * p.kb_per_split, kb1 = min(p.kb_total, kb0 + p.kb_per_split);
         for (int kb = kb0 + (u == (int)blockIdx.x ? pre : 0); kb < kb1; ++kb) {
           if (!tc::mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, err, 1)) break;
           tc::mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-          tc::tma_load_2d(s_w + stage * Cfg::W_BYTES, &tm_w, &full[stage], w_x(p, kb), w_y(p, n_tile, kb), pol_w);
-          tc::tma_load_2d(s_a + stage * Cfg::A_BYTES, &tm_a, &full[stage], kb * 64, m_tile * BN, pol_a);
+          tc::tma_load_2d(s_w + stage * Cfg::W_BYTES, &tm_w, &full[stage], w_x(p, kb), w_y(p, x.w_tile_base, kb), pol_w);
+          tc::tma_load_2d(s_a + stage * Cfg::A_BYTES, &tm_a, &full[stage], kb * 64, x.a_row0, pol_a);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
@@ -250,8 +284,9 @@ __global__ void __launch_bounds__(192, 2)
       uint32_t acc_phase[2] = {0, 0};
       int acc = 0;
       for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
-        const int split = u % p.splits;
-        const int kb0 = split * p.kb_per_split, kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        const Unit x = decode_unit(p, u, BN);
+        if (x.empty) continue;
+        const int kb0 = x.split * p.kb_per_split, kb1 = min(p.kb_total, kb0 + p.kb_per_split);
         if (!tc::mbar_wait_bounded(&tempty[acc], acc_phase[acc] ^ 1, abort_flag, err, 2)) break;
         tc::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
@@ -283,33 +318,32 @@ __global__ void __launch_bounds__(192, 2)
     const int row = quad * 32 + lane;
     uint32_t acc_phase[2] = {0, 0};
     int acc = 0;
+    const int total_tiles = p.units / p.splits;
     for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
-      const int split = u % p.splits, tile = u / p.splits;
-      const int n_tile = tile % p.n_tiles, m_tile = tile / p.n_tiles;
+      const Unit x = decode_unit(p, u, BN);
+      if (x.empty) continue;
+      const int t_end = x.a_row0 + min(x.m_lim, BN);
       if (!tc::mbar_wait_bounded(&tfull[acc], acc_phase[acc], abort_flag, err, 4)) break;
       tc::tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
-      const int feat = n_tile * 128 + row;
       if (p.splits == 1) {
         for (int c0 = 0; c0 < BN; c0 += 16) {
           float v[16];
           tc::tmem_ld16(t_row + c0, v);
-          epilogue_store<EPI>(p, v, row, n_tile, m_tile * BN + c0, xchg, quad, lane);
+          epilogue_store<EPI>(p, v, row, x.n_tile, x.a_row0 + c0, t_end, xchg, quad, lane);
         }
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&tempty[acc]);
         if constexpr (EPI == EPI_PUSH) publish_tile(p, last_flag);
       } else {
-        const size_t ws_rows = (size_t)p.m_tiles * BN;
-        float* ws_split = p.ws + (size_t)split * ws_rows * p.N;
+        // partial tile -> workspace [split][tile][BN][128] (coalesced over the 128 features)
+        float* ws_mine = p.ws + ((size_t)x.split * total_tiles + x.tile) * BN * 128;
         for (int c0 = 0; c0 < BN; c0 += 16) {
           float v[16];
           tc::tmem_ld16(t_row + c0, v);
-          if (feat < p.N) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) ws_split[((size_t)m_tile * BN + c0 + j) * p.N + feat] = v[j];
-          }
+          for (int j = 0; j < 16; ++j) ws_mine[(size_t)(c0 + j) * 128 + row] = v[j];
         }
         tc::tc_fence_before();
         __syncwarp();
@@ -317,7 +351,7 @@ __global__ void __launch_bounds__(192, 2)
         __threadfence();
         epi_bar();
         if (threadIdx.x == 64) {
-          const int old = atomicAdd(&p.counters[tile], 1);
+          const int old = atomicAdd(&p.counters[x.tile], 1);
           *last_flag = (old == p.splits - 1);
         }
         epi_bar();
@@ -329,16 +363,14 @@ __global__ void __launch_bounds__(192, 2)
             float v[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = 0.f;
-            if (feat < p.N) {
-              for (int s = 0; s < p.splits; ++s) {
-                const float* src = p.ws + (size_t)s * ws_rows * p.N + ((size_t)m_tile * BN + c0) * p.N + feat;
+            for (int sp = 0; sp < p.splits; ++sp) {
+              const float* src = p.ws + ((size_t)sp * total_tiles + x.tile) * BN * 128 + (size_t)c0 * 128 + row;
 #pragma unroll
-                for (int j = 0; j < 16; ++j) v[j] += __ldcg(src + (size_t)j * p.N);
-              }
+              for (int j = 0; j < 16; ++j) v[j] += __ldcg(src + (size_t)j * 128);
             }
-            epilogue_store<EPI>(p, v, row, n_tile, m_tile * BN + c0, xchg, quad, lane);
+            epilogue_store<EPI>(p, v, row, x.n_tile, x.a_row0 + c0, t_end, xchg, quad, lane);
           }
-          if (threadIdx.x == 64) p.counters[tile] = 0;
+          if (threadIdx.x == 64) p.counters[x.tile] = 0;
           if constexpr (EPI == EPI_PUSH) publish_tile(p, last_flag);
         }
       }

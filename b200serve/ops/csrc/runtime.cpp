@@ -9,7 +9,7 @@ static int g_pdl = -1;
 bool pdl_enabled() {
   if (g_pdl < 0) {
     const char* v = std::getenv("B200_PDL");
-    g_pdl = (v && (std::strcmp(v, "1") == 0)) ? 1 : 0;   // off unless B200_PDL=1 (measured slower)
+    g_pdl = (v && (std::strcmp(v, "0") == 0)) ? 0 : 1;   // on unless B200_PDL=0
   }
   return g_pdl != 0;
 }

@@ -73,7 +73,7 @@ def bench_attn():
         sl = torch.full((B,), L, dtype=torch.int32, device="cuda")
         q = torch.randn(B, nq, hd, device="cuda").bfloat16()
         per = B * nkv               # the engine's plan (engine/runner.py attn_plan)
-        tps = 64 if per <= 16 else 128 if per <= 64 else 256
+        tps = 64 if per <= 16 else 128 if per <= 64 else 256 if per <= 128 else 512
         nsplit = (L + tps - 1) // tps
         ws = ops.AttnWorkspace("cuda", B, nkv, nq // nkv, hd, nsplit)
         scale = 1 / math.sqrt(hd)

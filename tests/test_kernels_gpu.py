@@ -249,3 +249,25 @@ def test_gemm_packed_weight(M, N, K):
     ref = x.float() @ w.float().t()
     assert _rel(ops.linear(x, pw), ref) < 1e-2
     assert _rel(ops.linear(x, pw, epilogue=ops.EPI_F32), ref) < 1e-4
+
+
+@pytest.mark.parametrize("nq,nkv,lens,tps", [(32, 8, [1, 17, 300, 2048], 256), (32, 4, [5, 999], 64),
+                                             (4, 1, [2304] * 3, 128), (16, 8, [33, 160], 16),
+                                             (32, 2, [700], 1024)])
+def test_paged_decode_attention_tensor_core(nq, nkv, lens, tps):
+    hd = 128
+    B = len(lens)
+    kc, vc, bt = _make_paged(B, lens, nkv, hd, 1024)
+    q = torch.randn(B, nq, hd, device=dev).bfloat16()
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    scale = 1 / math.sqrt(hd)
+    ref = ops.paged_decode_attention(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), sl.cpu(), scale)
+    for nsplit in ((max(lens) + tps - 1) // tps, ):
+        ws = ops.AttnWorkspace(dev, B, nkv, nq // nkv, hd, max(nsplit, 1))
+        out = torch.empty_like(q)
+        ops.ext().paged_decode_attention_tc(q, kc, vc, bt, sl, out, ws.acc, ws.ml, scale, tps, nsplit)
+        assert _rel(out.cpu(), ref) < 1e-2
+    out1 = torch.empty_like(q)
+    e = torch.empty(0, device=dev)
+    ops.ext().paged_decode_attention_tc(q, kc, vc, bt, sl, out1, e, e, scale, 4096, 1)
+    assert _rel(out1.cpu(), ref) < 1e-2
