@@ -90,7 +90,7 @@ class B200Engine(BaseEngine):
         say(f"b200: building {mc.name} ({mc.num_params() / 1e9:.2f}B params) tp={tp} on {dev}")
         self.weights = self._injected_weights or self._load_weights(mc, dtype, dev)
         self.comm = pdist.make_comm(cfgE, dev, self.model_cfg) if tp > 1 else None
-        nkv_local = mc.num_kv_heads // tp
+        nkv_local = max(1, mc.num_kv_heads // tp)
         num_blocks = self._size_kv(mc, nkv_local, dtype, dev)
         self.kv = KVCache(mc.num_layers, num_blocks, nkv_local, mc.head_dim, dtype=dtype, device=dev,
                           kv_format=cfgE.kv_format)
@@ -130,7 +130,7 @@ class B200Engine(BaseEngine):
     def _size_kv(self, mc, nkv_local, dtype, dev) -> int:
         cfgE = self.config
         per_block = KVCache.bytes_per_block(mc.num_layers, nkv_local, mc.head_dim,
-                                            torch.tensor([], dtype=dtype).element_size())
+                                            torch.tensor([], dtype=dtype).element_size(), cfgE.kv_format)
         want = cfgE.max_batch * ((cfgE.max_seq + BLOCK - 1) // BLOCK) + 64
         if cfgE.kv_blocks:
             return cfgE.kv_blocks

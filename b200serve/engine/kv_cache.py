@@ -19,6 +19,11 @@ BLOCK = 16
 
 
 class KVCache:
+    """Paged K/V storage. ``bf16``: k, v [layers, blocks, kv_heads, 16, head_dim].
+    ``int4g128``: k, v hold 4-bit codes [layers, blocks, kv_heads, 16, head_dim/2] (uint8,
+    interleaved nibbles per 8 dims) and k_scale, v_scale one fp16 per (token, head)
+    [layers, blocks, kv_heads, 16]: 4-bit K/V with an fp16 scale per group of 128 values."""
+
     def __init__(self, num_layers, num_blocks, kv_heads, head_dim, dtype=torch.bfloat16, device="cpu",
                  kv_format="bf16"):
         self.num_layers = num_layers
@@ -26,12 +31,25 @@ class KVCache:
         self.kv_heads = kv_heads
         self.head_dim = head_dim
         self.kv_format = kv_format
-        shape = (num_layers, num_blocks, kv_heads, BLOCK, head_dim)
-        self.k = torch.zeros(shape, dtype=dtype, device=device)
-        self.v = torch.zeros(shape, dtype=dtype, device=device)
+        self.k_scale = self.v_scale = None
+        if kv_format == "int4g128":
+            if head_dim != 128:
+                raise ValueError("int4g128 KV needs head_dim 128")
+            shape = (num_layers, num_blocks, kv_heads, BLOCK, head_dim // 2)
+            self.k = torch.zeros(shape, dtype=torch.uint8, device=device)
+            self.v = torch.zeros(shape, dtype=torch.uint8, device=device)
+            sshape = (num_layers, num_blocks, kv_heads, BLOCK)
+            self.k_scale = torch.zeros(sshape, dtype=torch.float16, device=device)
+            self.v_scale = torch.zeros(sshape, dtype=torch.float16, device=device)
+        else:
+            shape = (num_layers, num_blocks, kv_heads, BLOCK, head_dim)
+            self.k = torch.zeros(shape, dtype=dtype, device=device)
+            self.v = torch.zeros(shape, dtype=dtype, device=device)
 
     @staticmethod
-    def bytes_per_block(num_layers, kv_heads, head_dim, elem_bytes=2) -> int:
+    def bytes_per_block(num_layers, kv_heads, head_dim, elem_bytes=2, kv_format="bf16") -> int:
+        if kv_format == "int4g128":
+            return 2 * num_layers * kv_heads * BLOCK * (head_dim // 2 + 2)
         return 2 * num_layers * kv_heads * BLOCK * head_dim * elem_bytes
 
 

@@ -255,7 +255,7 @@ def dequantize_q4_k(raw: np.ndarray) -> np.ndarray:
     q[:, 0::2, :] = qs & 15
     q[:, 1::2, :] = qs >> 4
     w = (d * sc)[..., None] * q - (dmin * mn)[..., None]
-    return w.reshape(-1)
+    return w.reshape(-1).astype(np.float32)
 
 
 def quantize_q6_k(x: np.ndarray) -> bytes:
@@ -420,3 +420,117 @@ def load_gguf_weights(cfg, path: str, **kw):
     embed = T("token_embd.weight")
     lm = T("output.weight") if "output.weight" in g.tensors else embed
     return build_weights(cfg, layer, embed, lm, T("output_norm.weight"), **kw)
+
+
+# ------------------------------------------------------------------ GPU repack (fragment order)
+def _bf16_bits(a: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 bit patterns (round to nearest even), uint32."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint32)
+
+
+def _pair(bits: np.ndarray) -> np.ndarray:
+    return (bits | (bits << 16)).astype(np.uint32)
+
+
+def _frag_cols(t):
+    """Columns of the 4 A-fragment registers of lane quad position t: (2t,2t+1), (2t,2t+1), (2t+8,..), (2t+8,..)."""
+    return [(2 * t, 2 * t + 1), (2 * t, 2 * t + 1), (2 * t + 8, 2 * t + 9), (2 * t + 8, 2 * t + 9)]
+
+
+def _lane_values(q: np.ndarray):
+    """q [N, K] -> [N/16, K/16, 32 lanes, 4 regs, 2] values in m16n8k16 A-fragment order."""
+    N, K = q.shape
+    t16 = q.reshape(N // 16, 16, K // 16, 16).transpose(0, 2, 1, 3)      # [S, KS, 16 rows, 16 cols]
+    lanes = np.arange(32)
+    g, t = lanes // 4, lanes % 4
+    rows = np.stack([g, g + 8, g, g + 8], 1)                              # [32, 4]
+    cols = np.stack([2 * t, 2 * t, 2 * t + 8, 2 * t + 8], 1)              # [32, 4] (low column)
+    lo = t16[:, :, rows, cols]                                            # [S, KS, 32, 4]
+    hi = t16[:, :, rows, cols + 1]
+    return np.stack([lo, hi], -1)
+
+
+def repack_q4k_for_gpu(raw: np.ndarray, N: int, K: int):
+    """Q4_K bytes of an [N, K] matrix -> (codes uint32 [N/16*K/16*32], meta uint32 [N/16*K/32*16*2])."""
+    blk = np.frombuffer(np.asarray(raw), dtype=_Q4K).reshape(N, K // 256)
+    d = blk["d"].astype(np.float32)
+    dmin = blk["dmin"].astype(np.float32)
+    sc, mn = _unpack_k4_scales(blk["scales"].reshape(-1, 12))
+    sc = sc.reshape(N, K // 256, 8)
+    mn = mn.reshape(N, K // 256, 8)
+    s = (d[..., None] * sc).reshape(N, K // 32)
+    m = (dmin[..., None] * mn).reshape(N, K // 32)
+    qs = blk["qs"].reshape(N, K // 256, 4, 32)
+    q = np.empty((N, K // 256, 8, 32), dtype=np.uint32)
+    q[:, :, 0::2, :] = qs & 15
+    q[:, :, 1::2, :] = qs >> 4
+    q = q.reshape(N, K)
+    v = _lane_values(q)                                                   # [S, KS, 32, 4, 2]
+    word = np.zeros(v.shape[:3], dtype=np.uint32)
+    for i in range(4):
+        word |= (v[..., i, 0] << (4 * i)) | (v[..., i, 1] << (16 + 4 * i))
+    sb = _pair(_bf16_bits(s)).reshape(N // 16, 16, K // 32).transpose(0, 2, 1)        # [S, SB, 16]
+    mb = _pair(_bf16_bits(-m)).reshape(N // 16, 16, K // 32).transpose(0, 2, 1)
+    meta = np.stack([sb, mb], -1)                                         # [S, SB, 16, 2]
+    return word.reshape(-1), np.ascontiguousarray(meta).reshape(-1)
+
+
+def repack_s8_for_gpu(q: np.ndarray, scale: np.ndarray, group: int):
+    """int8 codes q [N, K] with scales [N, K/group] -> (codes uint32 [.., 2], meta uint32)."""
+    N, K = q.shape
+    v = _lane_values(q.astype(np.int8).view(np.uint8).astype(np.uint32))  # [S, KS, 32, 4, 2]
+    w0 = v[..., 0, 0] | (v[..., 0, 1] << 8) | (v[..., 1, 0] << 16) | (v[..., 1, 1] << 24)
+    w1 = v[..., 2, 0] | (v[..., 2, 1] << 8) | (v[..., 3, 0] << 16) | (v[..., 3, 1] << 24)
+    codes = np.stack([w0, w1], -1).astype(np.uint32)
+    meta = _pair(_bf16_bits(scale)).reshape(N // 16, 16, K // group).transpose(0, 2, 1)
+    return codes.reshape(-1), np.ascontiguousarray(meta).reshape(-1)
+
+
+def q6k_to_s8(raw: np.ndarray, N: int, K: int):
+    blk = np.frombuffer(np.asarray(raw), dtype=_Q6K)
+    d = blk["d"].astype(np.float32)
+    sc = blk["scales"].astype(np.float32)
+    ql = blk["ql"].reshape(-1, 2, 64).astype(np.int32)
+    qh = blk["qh"].reshape(-1, 2, 32).astype(np.int32)
+    q = np.empty((blk.shape[0], 2, 128), dtype=np.int32)
+    q[:, :, 0:32] = (ql[:, :, :32] & 15) | ((qh & 3) << 4)
+    q[:, :, 32:64] = (ql[:, :, 32:] & 15) | (((qh >> 2) & 3) << 4)
+    q[:, :, 64:96] = (ql[:, :, :32] >> 4) | (((qh >> 4) & 3) << 4)
+    q[:, :, 96:128] = (ql[:, :, 32:] >> 4) | (((qh >> 6) & 3) << 4)
+    q = (q - 32).reshape(N, K)
+    scale = (d[:, None] * sc).reshape(N, K // 16)
+    return q, scale
+
+
+def q8_0_to_s8(raw: np.ndarray, N: int, K: int):
+    blk = np.frombuffer(np.asarray(raw), dtype=[("d", "<f2"), ("q", "i1", 32)])
+    return blk["q"].reshape(N, K).astype(np.int32), blk["d"].astype(np.float32).reshape(N, K // 32)
+
+
+def gpu_quant_weight(g: "GGUFFile", name: str, device):
+    """A GGUF tensor as an ops.QuantWeight on ``device`` (Q4_K, Q6_K, Q8_0), else None."""
+    import torch
+    from b200serve import ops
+    t = g.tensors[name]
+    if len(t.shape) != 2:
+        return None
+    N, K = t.shape
+    if K % 256 or N % 16:
+        return None
+    raw = g.raw(name)
+    if t.ggml_type == GGML_Q4_K:
+        codes, meta = repack_q4k_for_gpu(raw, N, K)
+        bits, group = 4, 32
+    elif t.ggml_type == GGML_Q6_K:
+        q, s = q6k_to_s8(raw, N, K)
+        codes, meta = repack_s8_for_gpu(q, s, 16)
+        bits, group = 8, 16
+    elif t.ggml_type == GGML_Q8_0:
+        q, s = q8_0_to_s8(raw, N, K)
+        codes, meta = repack_s8_for_gpu(q, s, 32)
+        bits, group = 8, 32
+    else:
+        return None
+    to = lambda a: torch.from_numpy(a.view(np.int32).copy()).to(device)
+    return ops.QuantWeight(to(codes), to(meta), N, K, bits, group)

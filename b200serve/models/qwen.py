@@ -73,7 +73,7 @@ class Decoder:
         self.device = torch.device(device)
         tp = weights.tp_size
         self.nq = cfg.num_heads // tp
-        self.nkv = cfg.num_kv_heads // tp
+        self.nkv = max(1, cfg.num_kv_heads // tp)   # KV heads replicated when tp > num_kv_heads
         self.hd = cfg.head_dim
         self.scale = ops.softmax_scale(cfg.head_dim)
         self.cos_sin = ops.rope_cos_sin(cfg.head_dim, cfg.max_position, cfg.rope_theta, self.device)
@@ -122,6 +122,46 @@ class Decoder:
                                              max(nsplit, ws.max_splits if ws else 1))
         return self.attn_ws
 
+    def _attention_q4(self, i, qkv, lw, fb, T, tps, nsplit, ws):
+        """Attention over the int4g128 cache: K/V quantised on write, dequantised inside the kernels."""
+        kv = self.kv
+        kc, vc, ksc, vsc = kv.k[i], kv.v[i], kv.k_scale[i], kv.v_scale[i]
+        eps = self.cfg.rms_eps
+        if qkv.is_cuda:
+            q = torch.empty(T, self.nq, self.hd, dtype=qkv.dtype, device=qkv.device)
+            ops._cuda(qkv)
+            ops.ext().qkv_post_q4(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots, q, kc, vc,
+                                  ksc, vsc, self.nq, self.nkv, eps)
+            out = torch.empty_like(q)
+            if fb.is_decode:
+                acc = ws.acc if nsplit > 1 else torch.empty(0, device=q.device)
+                ml = ws.ml if nsplit > 1 else torch.empty(0, device=q.device)
+                ops._cuda(q, 2)
+                ops.ext().paged_decode_attention_q4(q, kc, vc, ksc, vsc, fb.block_tables, fb.seq_lens, out, acc, ml,
+                                                    self.scale, tps, nsplit)
+            else:
+                ops._cuda(q)
+                ops.ext().paged_prefill_attention_q4(q, kc, vc, ksc, vsc, fb.block_tables, fb.seq_lens, fb.q_start,
+                                                     fb.cu_q, out, self.scale, fb.max_q)
+            return out
+        # CPU: quantise the new rows into the cache, attend over dequantised pages
+        kb = torch.zeros(kc.shape[0], self.nkv, 16, self.hd, dtype=torch.float32)
+        vb = torch.zeros_like(kb)
+        q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots, kb, vb, self.nq,
+                         self.nkv, eps)
+        sl = fb.slots.long()
+        ok = sl >= 0
+        blk, off = sl[ok] // 16, sl[ok] % 16
+        for src, codes, scale in ((kb, kc, ksc), (vb, vc, vsc)):
+            c, s_ = ops.q4_quantize_rows(src[blk, :, off])
+            codes[blk, :, off] = c
+            scale[blk, :, off] = s_
+        kd = ops.q4_dequantize_rows(kc, ksc).to(q.dtype)
+        vd = ops.q4_dequantize_rows(vc, vsc).to(q.dtype)
+        if fb.is_decode:
+            return ops.paged_decode_attention(q, kd, vd, fb.block_tables, fb.seq_lens, self.scale)
+        return ops.paged_prefill_attention(q, kd, vd, fb.block_tables, fb.seq_lens, fb.q_start, fb.cu_q, self.scale)
+
     def _row_parallel(self, x, w, tag):
         """Row-parallel linear whose output is summed over tensor-parallel ranks."""
         if hasattr(self.comm, "linear_reduce"):
@@ -149,14 +189,18 @@ class Decoder:
                 x = ops.rmsnorm(mlp_parts, lw.input_norm, eps, residual=residual, residual_out=residual)
             qkv = ops.linear(x, lw.qkv, bias=lw.qkv_bias)
             kc, vc = k_all[i], v_all[i]
-            q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots, kc, vc,
-                             self.nq, self.nkv, eps)
-            if fb.is_decode:
-                attn = ops.paged_decode_attention(q, kc, vc, fb.block_tables, fb.seq_lens, self.scale, tps,
-                                                  nsplit, ws)
+            if self.kv.kv_format == "int4g128":
+                attn = self._attention_q4(i, qkv, lw, fb, T, tps if fb.is_decode else 0,
+                                          nsplit if fb.is_decode else 0, ws if fb.is_decode else None)
             else:
-                attn = ops.paged_prefill_attention(q, kc, vc, fb.block_tables, fb.seq_lens, fb.q_start, fb.cu_q,
-                                                   self.scale, max_q=fb.max_q)
+                q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots, kc, vc,
+                                 self.nq, self.nkv, eps)
+                if fb.is_decode:
+                    attn = ops.paged_decode_attention(q, kc, vc, fb.block_tables, fb.seq_lens, self.scale, tps,
+                                                      nsplit, ws)
+                else:
+                    attn = ops.paged_prefill_attention(q, kc, vc, fb.block_tables, fb.seq_lens, fb.q_start,
+                                                       fb.cu_q, self.scale, max_q=fb.max_q)
             o_parts = self._row_parallel(attn.view(T, self.nq * self.hd), lw.o, "o")
             x = ops.rmsnorm(o_parts, lw.post_norm, eps, residual=residual, residual_out=residual)
             if self.moe is not None:

@@ -105,15 +105,23 @@ def vocab_shard(V: int, rank: int, size: int):
 def shard_layer_dense(cfg: ModelConfig, full: dict, rank: int, size: int, dtype, device) -> LayerWeights:
     """``full`` holds unsharded HF-named tensors of one layer (q,k,v,o,gate,up,down,...)."""
     hd = cfg.head_dim
-    assert cfg.num_heads % size == 0 and cfg.num_kv_heads % size == 0, "heads must divide tp_size"
+    assert cfg.num_heads % size == 0, "query heads must divide tp_size"
     q = _shard_rows(full["q"], rank, size)
-    k = _shard_rows(full["k"], rank, size)
-    v = _shard_rows(full["v"], rank, size)
+    if cfg.num_kv_heads % size == 0:
+        k = _shard_rows(full["k"], rank, size)
+        v = _shard_rows(full["v"], rank, size)
+        kvsel = lambda t: _shard_rows(t, rank, size)
+    else:
+        # more ranks than KV heads: each KV head is replicated on size/nkv ranks, matching the
+        # query heads of the rank (GQA groups stay whole)
+        assert size % cfg.num_kv_heads == 0, "tp_size must divide or be a multiple of the KV heads"
+        rep = size // cfg.num_kv_heads
+        kvsel = lambda t: _shard_rows(t, rank // rep, cfg.num_kv_heads)
+        k, v = kvsel(full["k"]), kvsel(full["v"])
     qkv = torch.cat([q, k, v])
     bias = None
     if cfg.attn_bias:
-        bias = torch.cat([_shard_rows(full["q_bias"], rank, size), _shard_rows(full["k_bias"], rank, size),
-                          _shard_rows(full["v_bias"], rank, size)])
+        bias = torch.cat([_shard_rows(full["q_bias"], rank, size), kvsel(full["k_bias"]), kvsel(full["v_bias"])])
     o = full["o"]
     oc = o.shape[1] // size
     o = o[:, rank * oc:(rank + 1) * oc]

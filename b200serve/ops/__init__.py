@@ -252,6 +252,60 @@ class PackedWeight:
         return self.data.element_size()
 
 
+class QuantWeight:
+    """A GGUF-quantised [N, K] weight in the fragment order of ops/csrc/gguf_gemm.cu:
+    4-bit codes with bf16 scale and -min per 32 (Q4_K) or int8 codes with a bf16
+    scale per ``group`` (Q6_K: 16, Q8_0: 32)."""
+
+    def __init__(self, codes, meta, N, K, bits, group):
+        self.codes, self.meta, self.N, self.K, self.bits, self.group = codes, meta, N, K, bits, group
+        self.shape = (N, K)
+        self.device = codes.device
+        self.dtype = torch.bfloat16
+
+    def numel(self):
+        return self.codes.numel() + self.meta.numel()
+
+    def element_size(self):
+        return 4
+
+    def dequantize(self) -> torch.Tensor:
+        """bf16 [N, K] (used for prefill-sized batches and tests)."""
+        N, K = self.N, self.K
+        S, KS = N // 16, K // 16
+        lanes = torch.arange(32, device=self.device)
+        g, t = lanes // 4, lanes % 4
+        rows = torch.stack([g, g + 8, g, g + 8], 1)
+        cols = torch.stack([2 * t, 2 * t, 2 * t + 8, 2 * t + 8], 1)
+        if self.bits == 4:
+            w = self.codes.view(S, KS, 32).long() & 0xFFFFFFFF
+            lo = torch.stack([(w >> (4 * i)) & 15 for i in range(4)], -1)
+            hi = torch.stack([(w >> (16 + 4 * i)) & 15 for i in range(4)], -1)
+            meta = self.meta.view(S, K // 32, 16, 2).long() & 0xFFFF
+            sc = _bf16_from_bits(meta[..., 0])
+            mn = _bf16_from_bits(meta[..., 1])
+        else:
+            w = self.codes.view(S, KS, 32, 2).long() & 0xFFFFFFFF
+            b = lambda x, sh: ((x >> sh) & 0xFF).to(torch.int8).float()
+            lo = torch.stack([b(w[..., 0], 0), b(w[..., 0], 16), b(w[..., 1], 0), b(w[..., 1], 16)], -1)
+            hi = torch.stack([b(w[..., 0], 8), b(w[..., 0], 24), b(w[..., 1], 8), b(w[..., 1], 24)], -1)
+            meta = self.meta.view(S, K // self.group, 16).long() & 0xFFFF
+            sc = _bf16_from_bits(meta)
+            mn = torch.zeros_like(sc)
+        q = torch.zeros(S, KS, 16, 16, device=self.device)
+        q[:, :, rows, cols] = lo.float()
+        q[:, :, rows, cols + 1] = hi.float()
+        q = q.permute(0, 2, 1, 3).reshape(N, K)
+        gsz = 32 if self.bits == 4 else self.group
+        scale = sc.permute(0, 2, 1).reshape(N, K // gsz).repeat_interleave(gsz, 1)
+        minus = mn.permute(0, 2, 1).reshape(N, K // gsz).repeat_interleave(gsz, 1)
+        return (q * scale + minus).to(torch.bfloat16)
+
+
+def _bf16_from_bits(b: torch.Tensor) -> torch.Tensor:
+    return (b.to(torch.int32) << 16).view(torch.float32)
+
+
 def pack_weight(w):
     """Pack a CUDA weight for the GEMM (idempotent; CPU tensors stay plain)."""
     if isinstance(w, PackedWeight) or w is None or not w.is_cuda or w.dim() != 2:
@@ -268,6 +322,15 @@ def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspac
     M, K = x.shape
     N = w.shape[0]
     packed_n = 0
+    if isinstance(w, QuantWeight):
+        if x.is_cuda and M <= 32 and epilogue == EPI_BF16 and bias is None and residual is None:
+            out = out if out is not None else torch.empty(M, N, dtype=x.dtype, device=x.device)
+            _cuda(x)
+            ext().gguf_gemm(x.contiguous(), w.codes, w.meta, N, w.bits, w.group, out)
+            return out
+        w = w.dequantize() if x.is_cuda else w.dequantize().cpu()
+        if x.is_cuda:
+            w = PackedWeight(w)
     if isinstance(w, PackedWeight):
         packed_n = w.N
         if not x.is_cuda:
@@ -439,6 +502,33 @@ def sample_rows(logits, temperature, top_k, top_p, min_p, seeds, steps, pen_ids=
     _cuda(logits)
     ext().sample_rows(logits, params, pen_ids, pen_counts, pen_vals, out)
     return out
+
+
+# ------------------------------------------------------------------ int4g128 KV cache
+def q4_quantize_rows(x: torch.Tensor):
+    """[..., 128] float -> (codes [..., 64] uint8 in the cache's interleaved nibble order,
+    fp16 scale [...]): symmetric 4-bit, scale = amax / 7, codes = q + 8."""
+    amax = x.abs().amax(-1)
+    scale = torch.where(amax > 0, amax / 7.0, torch.ones_like(amax)).half()
+    q = (x / scale.float()[..., None]).round().clamp(-8, 7).to(torch.int32) + 8
+    q = q.view(*x.shape[:-1], 16, 8)                               # groups of 8 dims
+    word = torch.zeros(q.shape[:-1], dtype=torch.int64, device=x.device)
+    for o in range(8):
+        pr, hi = o >> 1, o & 1
+        word |= q[..., o].long() << (4 * (pr + 4 * hi))
+    byts = torch.stack([(word >> (8 * b)) & 0xFF for b in range(4)], -1).to(torch.uint8)
+    return byts.view(*x.shape[:-1], 64), scale
+
+
+def q4_dequantize_rows(codes: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    b = codes.view(*codes.shape[:-1], 16, 4).long()
+    word = b[..., 0] | (b[..., 1] << 8) | (b[..., 2] << 16) | (b[..., 3] << 24)
+    vals = []
+    for o in range(8):
+        pr, hi = o >> 1, o & 1
+        vals.append(((word >> (4 * (pr + 4 * hi))) & 15) - 8)
+    q = torch.stack(vals, -1).view(*codes.shape[:-1], 128).float()
+    return q * scale.float()[..., None]
 
 
 def gemm_error_flag(reset: bool = True) -> int:

@@ -47,19 +47,67 @@ __device__ __forceinline__ uint32_t swz(int tok, int c) {
   return (uint32_t)((c >> 3) * kBoxBytes + tok * 128 + (((c & 7) ^ (tok & 7)) << 4));
 }
 
-template <int G>
+// int4g128 page stage: raw codes K (1 KB) | V (1 KB) | K scales (32 B) | V scales (32 B), padded
+constexpr int kQ4Raw = 2 * 1024 + 2 * 32 + 64;
+
+// Dequantise one int4g128 page (raw stage) into the swizzled bf16 stage layout.
+// Lane l converts row l/2, dims [64*(l&1), +64): 8 words of 8 interleaved nibbles.
+__device__ __forceinline__ void dequant_q4_page(const uint8_t* raw, uint8_t* work, int lane) {
+  const int row = lane >> 1, half = lane & 1;
+#pragma unroll
+  for (int kv = 0; kv < 2; ++kv) {
+    const uint4* src = reinterpret_cast<const uint4*>(raw + kv * 1024 + row * 64 + half * 32);
+    const __half sh = reinterpret_cast<const __half*>(raw + 2048 + kv * 32)[row];
+    const __nv_bfloat16 sb = __float2bfloat16_rn(__half2float(sh));
+    const uint32_t s2 = (uint32_t)__bfloat16_as_ushort(sb) * 0x00010001u;
+    const uint32_t off = 0x43084308u;   // bf16 (136, 136): 128 (magic) + 8 (offset binary)
+    uint8_t* dst_base = work + kv * 2 * kBoxBytes;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint4 c = src[j];
+      const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        uint32_t r[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const uint32_t qq = ((wv[w] >> (4 * p)) & 0x000F000Fu) | 0x43004300u;   // (128+q, 128+q')
+          uint32_t d;
+          asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(qq), "r"(off));      // q - 8 (exact)
+          asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r[p]) : "r"(d), "r"(s2));
+        }
+        const int chunk = half * 8 + j * 4 + w;   // 16-byte chunk = 8 dims
+        *reinterpret_cast<uint4*>(dst_base + swz(row, chunk)) = make_uint4(r[0], r[1], r[2], r[3]);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   tc::smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(tc::smem_u32(bar))
+               : "memory");
+}
+
+template <int G, int KVQ>
 __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
     const __nv_bfloat16* __restrict__ q, const int* __restrict__ block_tables, const int* __restrict__ seq_lens,
     int max_blocks, int nkv, float scale_log2, int tps, float* __restrict__ part_acc, float* __restrict__ part_ml,
-    __nv_bfloat16* __restrict__ out, int nsplit, int* err) {
+    __nv_bfloat16* __restrict__ out, int nsplit, int* err, const uint8_t* __restrict__ kq,
+    const uint8_t* __restrict__ vq, const __half* __restrict__ ks, const __half* __restrict__ vs) {
   static_assert(G >= 1 && G <= 16, "query heads per kv head");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
-  uint8_t* ring = smem + warp * kTcStages * kStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcWarps * kTcStages * kStageBytes) + warp * kTcStages;
+  // bf16 pages: ring of kTcStages swizzled stages per warp. int4 pages: ring of raw stages plus
+  // one swizzled work stage per warp.
+  constexpr int kWarpBytes = KVQ ? (kTcStages * kQ4Raw + kStageBytes) : kTcStages * kStageBytes;
+  uint8_t* ring = smem + warp * kWarpBytes;
+  uint8_t* work = ring + kTcStages * kQ4Raw;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcWarps * kWarpBytes) + warp * kTcStages;
   float* mrg = reinterpret_cast<float*>(smem);   // merge scratch, reuses the rings after the page loop
 
   pdl_wait();
@@ -102,13 +150,23 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
   auto issue = [&](int i) {
     const int s = i % kTcStages;
     const int tok0 = first + i * kTcWarps * 16;
-    const int y = (bt[tok0 >> 4] * nkv + kvh) * 16;
-    uint8_t* st = ring + s * kStageBytes;
-    tc::mbar_arrive_expect_tx(&bars[s], kStageBytes);
-    tc::tma_load_2d(st, &tm_k, &bars[s], 0, y, 0ull);
-    tc::tma_load_2d(st + kBoxBytes, &tm_k, &bars[s], 64, y, 0ull);
-    tc::tma_load_2d(st + 2 * kBoxBytes, &tm_v, &bars[s], 0, y, 0ull);
-    tc::tma_load_2d(st + 3 * kBoxBytes, &tm_v, &bars[s], 64, y, 0ull);
+    const int page = bt[tok0 >> 4] * nkv + kvh;
+    if constexpr (KVQ == 0) {
+      const int y = page * 16;
+      uint8_t* st = ring + s * kStageBytes;
+      tc::mbar_arrive_expect_tx(&bars[s], kStageBytes);
+      tc::tma_load_2d(st, &tm_k, &bars[s], 0, y, 0ull);
+      tc::tma_load_2d(st + kBoxBytes, &tm_k, &bars[s], 64, y, 0ull);
+      tc::tma_load_2d(st + 2 * kBoxBytes, &tm_v, &bars[s], 0, y, 0ull);
+      tc::tma_load_2d(st + 3 * kBoxBytes, &tm_v, &bars[s], 64, y, 0ull);
+    } else {
+      uint8_t* st = ring + s * kQ4Raw;
+      tc::mbar_arrive_expect_tx(&bars[s], 2 * 1024 + 2 * 32);
+      bulk_load(st, kq + (size_t)page * 1024, 1024, &bars[s]);
+      bulk_load(st + 1024, vq + (size_t)page * 1024, 1024, &bars[s]);
+      bulk_load(st + 2048, ks + (size_t)page * 16, 32, &bars[s]);
+      bulk_load(st + 2080, vs + (size_t)page * 16, 32, &bars[s]);
+    }
   };
   if (lane == 0)
     for (int i = 0; i < min(n_pages, kTcStages); ++i) issue(i);
@@ -119,7 +177,14 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
     const int s = i % kTcStages;
     const uint32_t phase = (uint32_t)((i / kTcStages) & 1);
     if (!tc::mbar_wait_bounded(&bars[s], phase, &never, err, 11)) break;
-    const uint32_t kbase = tc::smem_u32(ring + s * kStageBytes);
+    uint32_t kbase;
+    if constexpr (KVQ == 0) {
+      kbase = tc::smem_u32(ring + s * kStageBytes);
+    } else {
+      dequant_q4_page(ring + s * kQ4Raw, work, lane);
+      __syncwarp();
+      kbase = tc::smem_u32(work);
+    }
     const uint32_t vbase = kbase + 2 * kBoxBytes;
     const int tok0 = first + i * kTcWarps * 16;
     // ---- S^T [heads x 16 tokens] ----
@@ -241,7 +306,9 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
   }
 }
 
-size_t decode_tc_smem(int) { return 1024 + kTcWarps * kTcStages * kStageBytes + 256; }
+size_t decode_tc_smem(int kvq) {
+  return 1024 + kTcWarps * (kvq ? (kTcStages * kQ4Raw + kStageBytes) : kTcStages * kStageBytes) + 256;
+}
 
 typedef CUresult (*EncodeTiledFnKV)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                     const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -287,12 +354,11 @@ using namespace b200;
 void paged_decode_combine(torch::Tensor part_acc, torch::Tensor part_ml, torch::Tensor seq_lens, torch::Tensor out,
                           int64_t nkv, int64_t G, int64_t nsplit, int64_t tps);
 
-void paged_decode_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
-                               torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
-                               torch::Tensor part_acc, torch::Tensor part_ml, double scale, int64_t tps,
-                               int64_t nsplit) {
+static void decode_tc_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+                           torch::Tensor seq_lens, torch::Tensor out, torch::Tensor part_acc, torch::Tensor part_ml,
+                           double scale, int64_t tps, int64_t nsplit, int kvq, const uint8_t* kq, const uint8_t* vq,
+                           const __half* ksc, const __half* vsc, int nkv) {
   const int B = q.size(0), nq = q.size(1), HD = q.size(2);
-  const int nkv = k_cache.size(1);
   const int G = nq / nkv;
   TORCH_CHECK(HD == kHD && k_cache.size(2) == 16 && tps % 16 == 0 && nsplit >= 1);
   if (nsplit > 1) {
@@ -300,29 +366,36 @@ void paged_decode_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Te
     TORCH_CHECK(part_ml.numel() >= (int64_t)B * nkv * nsplit * G * 2, "attention workspace too small");
   }
   if (B == 0) return;
-  const int64_t rows = k_cache.size(0) * (int64_t)nkv * 16;
-  CUtensorMap tk = make_tmap_kv(k_cache.data_ptr(), rows);
-  CUtensorMap tv = make_tmap_kv(v_cache.data_ptr(), rows);
+  CUtensorMap tk, tv;
+  if (!kvq) {
+    const int64_t rows = k_cache.size(0) * (int64_t)nkv * 16;
+    tk = make_tmap_kv(k_cache.data_ptr(), rows);
+    tv = make_tmap_kv(v_cache.data_ptr(), rows);
+  } else {
+    memset(&tk, 0, sizeof(tk));
+    memset(&tv, 0, sizeof(tv));
+  }
   auto stream = at::cuda::getCurrentCUDAStream();
   const float sl2 = (float)(scale * 1.4426950408889634);
   dim3 grid(nsplit, nkv, B);
   float* pa = nsplit > 1 ? part_acc.data_ptr<float>() : nullptr;
   float* pm = nsplit > 1 ? part_ml.data_ptr<float>() : nullptr;
   auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
-  const size_t smem = decode_tc_smem(G);
-#define B200_TC(GV)                                                                                            \
+  const size_t smem = decode_tc_smem(kvq);
+#define B200_TC1(GV, KQ)                                                                                       \
   {                                                                                                            \
     static bool attr = false;                                                                                  \
     if (!attr) {                                                                                               \
-      B200_CHECK_CUDA(cudaFuncSetAttribute(paged_decode_tc_kernel<GV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                           (int)smem));                                                       \
+      B200_CHECK_CUDA(cudaFuncSetAttribute(paged_decode_tc_kernel<GV, KQ>,                                     \
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));          \
       attr = true;                                                                                             \
     }                                                                                                          \
-    launch_pdl(paged_decode_tc_kernel<GV>, grid, dim3(kTcWarps * 32), smem, stream, tk, tv,                    \
+    launch_pdl(paged_decode_tc_kernel<GV, KQ>, grid, dim3(kTcWarps * 32), smem, stream, tk, tv,                \
                reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), (const int*)block_tables.data_ptr<int>(),  \
                (const int*)seq_lens.data_ptr<int>(), (int)block_tables.size(1), nkv, sl2, (int)tps, pa, pm, op, \
-               (int)nsplit, decode_tc_err_word());                                                             \
+               (int)nsplit, decode_tc_err_word(), kq, vq, ksc, vsc);                                           \
   }
+#define B200_TC(GV) { if (kvq) B200_TC1(GV, 1) else B200_TC1(GV, 0) }
   switch (G) {
     case 1: B200_TC(1) break;
     case 2: B200_TC(2) break;
@@ -332,5 +405,26 @@ void paged_decode_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Te
     default: TORCH_CHECK(false, "unsupported GQA group ", G);
   }
 #undef B200_TC
+#undef B200_TC1
   if (nsplit > 1) paged_decode_combine(part_acc, part_ml, seq_lens, out, nkv, G, nsplit, tps);
+}
+
+void paged_decode_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                               torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
+                               torch::Tensor part_acc, torch::Tensor part_ml, double scale, int64_t tps,
+                               int64_t nsplit) {
+  decode_tc_impl(q, k_cache, v_cache, block_tables, seq_lens, out, part_acc, part_ml, scale, tps, nsplit, 0, nullptr,
+                 nullptr, nullptr, nullptr, k_cache.size(1));
+}
+
+// int4g128 KV: codes [blocks][nkv][16][64] uint8, scales [blocks][nkv][16] fp16.
+void paged_decode_attention_q4(torch::Tensor q, torch::Tensor k_codes, torch::Tensor v_codes, torch::Tensor k_scale,
+                               torch::Tensor v_scale, torch::Tensor block_tables, torch::Tensor seq_lens,
+                               torch::Tensor out, torch::Tensor part_acc, torch::Tensor part_ml, double scale,
+                               int64_t tps, int64_t nsplit) {
+  TORCH_CHECK(k_codes.size(3) == 64 && k_codes.scalar_type() == at::kByte, "int4g128 codes must be [*, nkv, 16, 64] uint8");
+  decode_tc_impl(q, k_codes, v_codes, block_tables, seq_lens, out, part_acc, part_ml, scale, tps, nsplit, 1,
+                 k_codes.data_ptr<uint8_t>(), v_codes.data_ptr<uint8_t>(),
+                 reinterpret_cast<const __half*>(k_scale.data_ptr()), reinterpret_cast<const __half*>(v_scale.data_ptr()),
+                 k_codes.size(1));
 }

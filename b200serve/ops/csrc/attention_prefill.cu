@@ -37,16 +37,21 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-template <int HD>
+// KVQ = 1: int4g128 cache (codes [blocks][nkv][16][HD/2], fp16 scale per row); tiles are
+// fetched as codes + scales and dequantised into the bf16 tiles before use.
+template <int HD, int KVQ>
 __global__ void __launch_bounds__(128) paged_prefill_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_cache,
     const __nv_bfloat16* __restrict__ v_cache, const int* __restrict__ block_tables, int max_blocks,
     const int* __restrict__ seq_lens, const int* __restrict__ q_start, const int* __restrict__ cu_q,
-    __nv_bfloat16* __restrict__ out, int nq, int nkv, float scale_log2) {
+    __nv_bfloat16* __restrict__ out, int nq, int nkv, float scale_log2, const uint8_t* __restrict__ kq,
+    const uint8_t* __restrict__ vq, const __half* __restrict__ ksc, const __half* __restrict__ vsc) {
   constexpr int LD = HD + 8;  // padded smem row (bf16) -> conflict-free 32-bit fragment loads
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);          // [2][64][LD]
   __nv_bfloat16* vs = ks + 2 * PF_BK * LD;                                  // [2][64][LD]
+  uint8_t* qraw = reinterpret_cast<uint8_t*>(vs + 2 * PF_BK * LD);           // KVQ: [2][K|V][64][HD/2]
+  __half* qscl = reinterpret_cast<__half*>(qraw + 2 * 2 * PF_BK * (HD / 2));  // KVQ: [2][K|V][64]
 
   pdl_wait();
   pdl_trigger();
@@ -87,6 +92,27 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(
   const int* bt = block_tables + (size_t)seq * max_blocks;
 
   auto load_tile = [&](int tile, int buf) {
+    if constexpr (KVQ) {
+      // codes: 64 rows x HD/2 bytes for K and V, plus one fp16 scale per row
+      constexpr int CH = PF_BK * (HD / 2) / 16;
+      for (int c = threadIdx.x; c < CH; c += 128) {
+        const int tok = c / (HD / 32), part = c % (HD / 32);
+        const int abs_tok = tile * PF_BK + tok;
+        const bool ok = abs_tok < kv_end;
+        const int page = ok ? bt[abs_tok >> 4] : 0;
+        const size_t row = ((size_t)page * nkv + kvh) * 16 + (abs_tok & 15);
+        uint8_t* dk = qraw + ((buf * 2 + 0) * PF_BK + tok) * (HD / 2) + part * 16;
+        uint8_t* dv = qraw + ((buf * 2 + 1) * PF_BK + tok) * (HD / 2) + part * 16;
+        cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(dk)), kq + row * (HD / 2) + part * 16, ok);
+        cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(dv)), vq + row * (HD / 2) + part * 16, ok);
+        if (part == 0) {
+          qscl[(buf * 2 + 0) * PF_BK + tok] = ok ? ksc[row] : __float2half(0.f);
+          qscl[(buf * 2 + 1) * PF_BK + tok] = ok ? vsc[row] : __float2half(0.f);
+        }
+      }
+      cp_async_commit();
+      return;
+    }
     // 64 tokens x HD dims for K and V: 64*HD/8 16-byte chunks each
     constexpr int CH = PF_BK * HD / 8;
     for (int c = threadIdx.x; c < CH; c += 128) {
@@ -113,6 +139,24 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(
       cp_async_wait<0>();
     }
     __syncthreads();
+    if constexpr (KVQ) {
+      // dequantise this buffer's codes into the bf16 tiles (8 dims = one 32-bit word per step)
+      for (int i = threadIdx.x; i < 2 * PF_BK * (HD / 8); i += 128) {
+        const int kv = i / (PF_BK * (HD / 8)), rem = i % (PF_BK * (HD / 8));
+        const int tok = rem / (HD / 8), grp = rem % (HD / 8);
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(qraw + ((buf * 2 + kv) * PF_BK + tok) * (HD / 2) + grp * 4);
+        const float sc = __half2float(qscl[(buf * 2 + kv) * PF_BK + tok]);
+        float f[8];
+#pragma unroll
+        for (int p2 = 0; p2 < 4; ++p2) {
+          f[2 * p2] = (float)((int)((w >> (4 * p2)) & 15u) - 8) * sc;
+          f[2 * p2 + 1] = (float)((int)((w >> (16 + 4 * p2)) & 15u) - 8) * sc;
+        }
+        __nv_bfloat16* dst = (kv ? vs : ks) + (buf * PF_BK + tok) * LD + grp * 8;
+        *reinterpret_cast<bf16x8*>(dst) = pack8(f);
+      }
+      __syncthreads();
+    }
     const __nv_bfloat16* kb = ks + buf * PF_BK * LD;
     const __nv_bfloat16* vb = vs + buf * PF_BK * LD;
     // ---- S = Q K^T : 16 rows x 64 tokens per warp ----
@@ -213,9 +257,10 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(
 
 using namespace b200;
 
-void paged_prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
-                             torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor q_start,
-                             torch::Tensor cu_q, torch::Tensor out, double scale, int64_t max_q) {
+static void prefill_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+                         torch::Tensor seq_lens, torch::Tensor q_start, torch::Tensor cu_q, torch::Tensor out,
+                         double scale, int64_t max_q, int kvq, const uint8_t* kq, const uint8_t* vq,
+                         const __half* ksc, const __half* vsc) {
   const int T = q.size(0), nq = q.size(1), HD = q.size(2);
   const int nkv = k_cache.size(1);
   const int nseq = seq_lens.size(0);
@@ -224,24 +269,45 @@ void paged_prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tens
   dim3 grid((max_q + PF_BQ - 1) / PF_BQ, nq, nseq);
   auto stream = at::cuda::getCurrentCUDAStream();
   const float sl2 = (float)(scale * 1.4426950408889634);
-#define B200_PF(HDV)                                                                                            \
+#define B200_PF1(HDV, KQV)                                                                                      \
   {                                                                                                             \
-    const size_t smem = 4 * PF_BK * (HDV + 8) * 2;                                                              \
+    const size_t smem = 4 * PF_BK * (HDV + 8) * 2 + (KQV ? (2 * 2 * PF_BK * (HDV / 2) + 2 * 2 * PF_BK * 2) : 0); \
     static bool attr = false;                                                                                   \
     if (!attr) {                                                                                                \
-      B200_CHECK_CUDA(cudaFuncSetAttribute(paged_prefill_kernel<HDV>,                                           \
+      B200_CHECK_CUDA(cudaFuncSetAttribute(paged_prefill_kernel<HDV, KQV>,                                      \
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));            \
       attr = true;                                                                                              \
     }                                                                                                           \
-    launch_pdl(paged_prefill_kernel<HDV>, grid, dim3(128), smem, stream,                                        \
+    launch_pdl(paged_prefill_kernel<HDV, KQV>, grid, dim3(128), smem, stream,                                   \
         reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr()), \
         reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()), (const int*)block_tables.data_ptr<int>(),   \
         (int)block_tables.size(1), (const int*)seq_lens.data_ptr<int>(), (const int*)q_start.data_ptr<int>(),    \
-        (const int*)cu_q.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nq, nkv, sl2);        \
+        (const int*)cu_q.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nq, nkv, sl2,       \
+        kq, vq, ksc, vsc);                                                                                      \
   }
-  if (HD == 128) B200_PF(128)
-  else if (HD == 64) B200_PF(64)
+  if (kvq) {
+    TORCH_CHECK(HD == 128, "int4 KV cache needs head_dim 128");
+    B200_PF1(128, 1)
+  } else if (HD == 128) B200_PF1(128, 0)
+  else if (HD == 64) B200_PF1(64, 0)
   else TORCH_CHECK(false, "head_dim must be 64 or 128");
-#undef B200_PF
+#undef B200_PF1
   B200_CHECK_CUDA(cudaGetLastError());
+}
+
+void paged_prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                             torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor q_start,
+                             torch::Tensor cu_q, torch::Tensor out, double scale, int64_t max_q) {
+  prefill_impl(q, k_cache, v_cache, block_tables, seq_lens, q_start, cu_q, out, scale, max_q, 0, nullptr, nullptr,
+               nullptr, nullptr);
+}
+
+// int4g128 cache: k_codes/v_codes [blocks][nkv][16][64] uint8, k_scale/v_scale [blocks][nkv][16] fp16.
+void paged_prefill_attention_q4(torch::Tensor q, torch::Tensor k_codes, torch::Tensor v_codes, torch::Tensor k_scale,
+                                torch::Tensor v_scale, torch::Tensor block_tables, torch::Tensor seq_lens,
+                                torch::Tensor q_start, torch::Tensor cu_q, torch::Tensor out, double scale,
+                                int64_t max_q) {
+  prefill_impl(q, k_codes, v_codes, block_tables, seq_lens, q_start, cu_q, out, scale, max_q, 1,
+               k_codes.data_ptr<uint8_t>(), v_codes.data_ptr<uint8_t>(),
+               reinterpret_cast<const __half*>(k_scale.data_ptr()), reinterpret_cast<const __half*>(v_scale.data_ptr()));
 }

@@ -39,6 +39,20 @@ void moe_permute(torch::Tensor ids, int64_t k, int64_t e0, int64_t E, torch::Ten
                  torch::Tensor sorted_tok);
 void gather_rows(torch::Tensor x, torch::Tensor rows, torch::Tensor count, torch::Tensor out);
 void moe_combine(torch::Tensor y, torch::Tensor w, torch::Tensor pos, int64_t k, torch::Tensor out);
+void gguf_gemm(torch::Tensor x, torch::Tensor codes, torch::Tensor meta, int64_t N, int64_t bits, int64_t group,
+               torch::Tensor out);
+void paged_decode_attention_q4(torch::Tensor q, torch::Tensor k_codes, torch::Tensor v_codes, torch::Tensor k_scale,
+                               torch::Tensor v_scale, torch::Tensor block_tables, torch::Tensor seq_lens,
+                               torch::Tensor out, torch::Tensor part_acc, torch::Tensor part_ml, double scale,
+                               int64_t tps, int64_t nsplit);
+void qkv_post_q4(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
+                 c10::optional<torch::Tensor> kn_w, torch::Tensor cos_sin, torch::Tensor positions,
+                 torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_codes, torch::Tensor v_codes,
+                 torch::Tensor k_scale, torch::Tensor v_scale, int64_t nq, int64_t nkv, double eps);
+void paged_prefill_attention_q4(torch::Tensor q, torch::Tensor k_codes, torch::Tensor v_codes, torch::Tensor k_scale,
+                                torch::Tensor v_scale, torch::Tensor block_tables, torch::Tensor seq_lens,
+                                torch::Tensor q_start, torch::Tensor cu_q, torch::Tensor out, double scale,
+                                int64_t max_q);
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi, int64_t num_sms);
 void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> bias,
              c10::optional<torch::Tensor> residual, torch::Tensor ws, torch::Tensor counters, int64_t epi,
@@ -74,6 +88,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_permute", &moe_permute);
   m.def("gather_rows", &gather_rows);
   m.def("moe_combine", &moe_combine);
+  m.def("gguf_gemm", &gguf_gemm);
+  m.def("paged_decode_attention_q4", &paged_decode_attention_q4);
+  m.def("qkv_post_q4", &qkv_post_q4);
+  m.def("paged_prefill_attention_q4", &paged_prefill_attention_q4);
   m.def("gemm_plan", &gemm_plan);
   m.def("gemm_tc", &gemm_tc);
   m.def("gemm_error_flag", &gemm_error_flag);

@@ -1,0 +1,184 @@
+// GGUF block-quantised GEMM for decode-sized batches (M <= 32 tokens):
+//   out[m, n] = sum_k x[m, k] * W[n, k],  W in Q4_K (4-bit, scale+min per 32)
+//   or in 8-bit codes with a scale per 16/32 (Q6_K, Q8_0 repacked).
+//
+// Restates the arithmetic of the reference's GGUF matmul shaders
+// (webgpu/src/shaders/matmul_gguf.wgsl:2103-3310, q4_k/q6_k/q8_0 variants) on
+// tensor cores: weights are repacked once at load time into "fragment order":
+// for every 16-row x 16-column tile, lane (g, t) of a warp owns the 8 weights
+// (rows g, g+8) x (cols 2t, 2t+1, 2t+8, 2t+9) of the m16n8k16 A operand, stored
+// as one 32-bit word of codes (4-bit) or two (8-bit). The kernel loads that
+// word, dequantises it in registers (bf16 magic-number conversion, then
+// q * scale - min with one HFMA2 per register) and issues mma.sync with the
+// activations (staged in shared memory) as the B operand, tokens on the N side.
+// Each warp covers 16 output rows and a 256-wide K chunk; the warps of a CTA
+// split K and are reduced through shared memory.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include "common.cuh"
+
+namespace b200 {
+
+constexpr int kQWarps = 8;       // K chunks per CTA pass
+constexpr int kQChunk = 256;     // K per warp chunk = 16 MMA k-steps
+
+__device__ __forceinline__ void qmma(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t bf2_sub(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+
+// 4-bit codes: word w holds register i's pair in nibbles (i) and (i + 4) -> bits 4i..4i+3 and 16+4i..
+__device__ __forceinline__ void dequant_u4(uint32_t w, uint32_t sa, uint32_t ma, uint32_t sb, uint32_t mb,
+                                           uint32_t* a) {
+  const uint32_t bias = 0x43004300u;  // bf16 (128, 128)
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t q = ((w >> (4 * i)) & 0x000F000Fu) | bias;   // (128 + q_lo, 128 + q_hi)
+    const uint32_t qv = bf2_sub(q, bias);
+    const bool row_b = (i & 1);                                  // a1, a3: row g + 8
+    a[i] = bf2_fma(qv, row_b ? sb : sa, row_b ? mb : ma);         // q * s + (-m)
+  }
+}
+
+// 8-bit signed codes: two words, register i's pair = bytes (2i, 2i+1) as int8
+__device__ __forceinline__ void dequant_s8(uint32_t w0, uint32_t w1, uint32_t sa, uint32_t sb, uint32_t* a) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t w = i < 2 ? w0 : w1;
+    const int sh = (i & 1) * 16;
+    const float lo = (float)(int8_t)((w >> sh) & 0xFF), hi = (float)(int8_t)((w >> (sh + 8)) & 0xFF);
+    const uint32_t qv = pack_bf16x2(lo, hi);
+    const bool row_b = (i & 1);
+    a[i] = bf2_fma(qv, row_b ? sb : sa, 0u);
+  }
+}
+
+// BITS = 4 (Q4_K: codes [N/16][K/16][32] u32, scale/min [N/16][K/32][16 rows] bf16x2 (s, -m))
+// BITS = 8 (codes [N/16][K/16][32][2] u32, scales [N/16][K/GROUP][16] bf16)
+template <int BITS, int NB>
+__global__ void __launch_bounds__(kQWarps * 32) gguf_gemm_kernel(
+    const uint32_t* __restrict__ codes, const uint32_t* __restrict__ smeta, const __nv_bfloat16* __restrict__ x,
+    int M, int N, int K, int group, __nv_bfloat16* __restrict__ out, int ldo) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int LDX = K + 8;                                   // padded row: conflict-free B fragments
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem);   // [NB*8][LDX]
+  float* red = reinterpret_cast<float*>(smem + (size_t)NB * 8 * LDX * 2);   // [warps][16][NB*8]
+  pdl_wait();
+  pdl_trigger();
+  const int rows_tok = NB * 8;
+  for (int i = threadIdx.x; i < rows_tok * (K / 8); i += blockDim.x) {
+    const int r = i / (K / 8), c = (i % (K / 8)) * 8;
+    bf16x8 v;
+    if (r < M) v = *reinterpret_cast<const bf16x8*>(x + (size_t)r * K + c);
+    else v.w[0] = v.w[1] = v.w[2] = v.w[3] = 0u;
+    *reinterpret_cast<bf16x8*>(xs + (size_t)r * LDX + c) = v;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int slice = blockIdx.x;                            // 16 output rows
+  const int ksteps = K / 16;
+  float acc[NB][4];
+#pragma unroll
+  for (int j = 0; j < NB; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  for (int k0 = warp * kQChunk; k0 < K; k0 += kQWarps * kQChunk) {
+    const int ks0 = k0 / 16;
+#pragma unroll 4
+    for (int ks = 0; ks < kQChunk / 16; ++ks) {
+      const int kstep = ks0 + ks;
+      if (kstep >= ksteps) break;
+      uint32_t a[4];
+      if constexpr (BITS == 4) {
+        const uint32_t w = __ldg(codes + ((size_t)slice * ksteps + kstep) * 32 + lane);
+        const int sb = (kstep * 16) / 32;
+        const uint32_t* mp = smeta + ((size_t)slice * (K / 32) + sb) * 32;   // [16 rows][2] -> s, -m
+        const uint32_t smA = __ldg(mp + g * 2), mmA = __ldg(mp + g * 2 + 1);
+        const uint32_t smB = __ldg(mp + (g + 8) * 2), mmB = __ldg(mp + (g + 8) * 2 + 1);
+        dequant_u4(w, smA, mmA, smB, mmB, a);
+      } else {
+        const uint2 w = __ldg(reinterpret_cast<const uint2*>(codes) + ((size_t)slice * ksteps + kstep) * 32 + lane);
+        const int gi = (kstep * 16) / group;
+        const uint32_t* sp = smeta + ((size_t)slice * (K / group) + gi) * 16;
+        const uint32_t sA = __ldg(sp + g), sB = __ldg(sp + g + 8);
+        dequant_s8(w.x, w.y, sA, sB, a);
+      }
+      const int kk = kstep * 16 + 2 * t4;
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        const __nv_bfloat16* xr = xs + (size_t)(j * 8 + g) * LDX + kk;
+        qmma(acc[j], a, *reinterpret_cast<const uint32_t*>(xr), *reinterpret_cast<const uint32_t*>(xr + 8));
+      }
+    }
+  }
+  // acc[j]: rows g / g+8 of the slice, tokens j*8 + 2t, +1 -> reduce over warps in shared memory
+  float* mine = red + (size_t)warp * 16 * rows_tok;
+#pragma unroll
+  for (int j = 0; j < NB; ++j) {
+    mine[g * rows_tok + j * 8 + 2 * t4] = acc[j][0];
+    mine[g * rows_tok + j * 8 + 2 * t4 + 1] = acc[j][1];
+    mine[(g + 8) * rows_tok + j * 8 + 2 * t4] = acc[j][2];
+    mine[(g + 8) * rows_tok + j * 8 + 2 * t4 + 1] = acc[j][3];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 16 * rows_tok; i += blockDim.x) {
+    const int r = i / rows_tok, tk = i % rows_tok;
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kQWarps; ++w) s += red[(size_t)w * 16 * rows_tok + i];
+    const int n = slice * 16 + r;
+    if (tk < M && n < N) out[(size_t)tk * ldo + n] = __float2bfloat16_rn(s);
+  }
+}
+
+}  // namespace b200
+
+using namespace b200;
+
+// codes/meta from models.gguf repack_*; x [M, K] bf16; out [M, N] bf16.
+void gguf_gemm(torch::Tensor x, torch::Tensor codes, torch::Tensor meta, int64_t N, int64_t bits, int64_t group,
+               torch::Tensor out) {
+  const int M = x.size(0), K = x.size(1);
+  TORCH_CHECK(M <= 32, "gguf_gemm handles decode batches up to 32 tokens");
+  TORCH_CHECK(K % 256 == 0 && N % 16 == 0, "K must be a multiple of 256 and N of 16");
+  if (M == 0) return;
+  const int NB = M <= 8 ? 1 : M <= 16 ? 2 : 4;
+  const size_t smem = (size_t)NB * 8 * (K + 8) * 2 + (size_t)kQWarps * 16 * NB * 8 * 4;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const dim3 grid(N / 16), block(kQWarps * 32);
+  auto cp = reinterpret_cast<const uint32_t*>(codes.data_ptr());
+  auto mp = reinterpret_cast<const uint32_t*>(meta.data_ptr());
+  auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+#define B200_GG(BITSV, NBV)                                                                                  \
+  {                                                                                                           \
+    static bool attr = false;                                                                                 \
+    if (!attr) {                                                                                              \
+      B200_CHECK_CUDA(cudaFuncSetAttribute(gguf_gemm_kernel<BITSV, NBV>,                                      \
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));         \
+      attr = true;                                                                                            \
+    }                                                                                                         \
+    launch_pdl(gguf_gemm_kernel<BITSV, NBV>, grid, block, smem, stream, cp, mp, xp, M, (int)N, K, (int)group, op, \
+               (int)out.stride(0));                                                                           \
+  }
+  TORCH_CHECK(smem <= 220 * 1024, "activation tile too large for shared memory");
+  if (bits == 4) {
+    if (NB == 1) B200_GG(4, 1) else if (NB == 2) B200_GG(4, 2) else B200_GG(4, 4)
+  } else {
+    if (NB == 1) B200_GG(8, 1) else if (NB == 2) B200_GG(8, 2) else B200_GG(8, 4)
+  }
+#undef B200_GG
+}

@@ -103,13 +103,16 @@ __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
 // QKV post-processing. One warp per (token, head slot); head slots are
 // [0, nq) query heads, [nq, nq+nkv) key heads, [nq+nkv, nq+2nkv) value heads.
 // E = HD/32 elements per lane; the rotate-half partner of lane l is lane l^16.
-template <int HD>
+// KVQ = 0: bf16 cache [blocks][nkv][16][HD]; KVQ = 1: int4g128 cache, codes
+// [blocks][nkv][16][HD/2] (two 4-bit offset-binary values per byte, even dim in
+// the low nibble) + fp16 scale per (token, head) in k_scale/v_scale [blocks][nkv][16].
+template <int HD, int KVQ>
 __global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ bias,
                                 const __nv_bfloat16* __restrict__ qn_w, const __nv_bfloat16* __restrict__ kn_w,
                                 const float* __restrict__ cos_sin, const int* __restrict__ positions,
                                 const int* __restrict__ slots, __nv_bfloat16* __restrict__ q_out,
-                                __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache, int T,
-                                int nq, int nkv, float eps) {
+                                void* __restrict__ k_cache, void* __restrict__ v_cache, __half* __restrict__ k_scale,
+                                __half* __restrict__ v_scale, int T, int nq, int nkv, float eps) {
   constexpr int E = HD / 32;
   pdl_wait();
   pdl_trigger();
@@ -162,10 +165,37 @@ __global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __n
     const int slot = slots[t];
     if (slot < 0) return;
     const int kvh = is_k ? h - nq : h - nq - nkv;
-    const size_t off = (((size_t)(slot >> 4) * nkv + kvh) * 16 + (slot & 15)) * HD + lane * E;
-    __nv_bfloat16* dst = (is_k ? k_cache : v_cache) + off;
+    const size_t row = ((size_t)(slot >> 4) * nkv + kvh) * 16 + (slot & 15);
+    if constexpr (KVQ == 0) {
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(is_k ? k_cache : v_cache) + row * HD + lane * E;
 #pragma unroll
-    for (int i = 0; i < E; ++i) dst[i] = __float2bfloat16_rn(x[i]);
+      for (int i = 0; i < E; ++i) dst[i] = __float2bfloat16_rn(x[i]);
+    } else {
+      // symmetric 4-bit: scale = amax / 7, q = clamp(round(x / scale), -8, 7), stored as q + 8
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < E; ++i) amax = fmaxf(amax, fabsf(x[i]));
+      amax = warp_max(amax);
+      const float scale = amax > 0.f ? amax / 7.f : 1.f;
+      const __half scale_h = __float2half_rn(scale);
+      const float inv = 1.f / __half2float(scale_h);
+      static_assert(E == 4, "int4 KV cache needs head_dim 128");
+      // 8 dims per 32-bit word; dims (2p, 2p+1) of the group go to nibbles (p, p + 4) so the
+      // reader turns a nibble pair into a bf16 pair with one mask-and-or
+      uint32_t part = 0;
+      const int base = (lane & 1) * 4;   // this lane holds dims 4l..4l+3 = group offsets base..base+3
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t q = (uint32_t)(max(-8, min(7, __float2int_rn(x[i] * inv))) + 8);
+        const int o = base + i, pr = o >> 1, hi = o & 1;
+        part |= q << (4 * (pr + 4 * hi));
+      }
+      const uint32_t word = part | __shfl_xor_sync(0xffffffffu, part, 1);
+      uint32_t* codes = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(is_k ? k_cache : v_cache) +
+                                                    row * (HD / 2));
+      if ((lane & 1) == 0) codes[lane >> 1] = word;
+      if (lane == 0) (is_k ? k_scale : v_scale)[row] = scale_h;
+    }
   }
 }
 
@@ -254,10 +284,10 @@ void rmsnorm_fused_wait(std::vector<torch::Tensor> parts, c10::optional<torch::T
                      reinterpret_cast<const int*>(epoch_ptr), reinterpret_cast<int*>(err_ptr));
 }
 
-void qkv_post(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
-              c10::optional<torch::Tensor> kn_w, torch::Tensor cos_sin, torch::Tensor positions,
-              torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache, int64_t nq,
-              int64_t nkv, double eps) {
+void qkv_post_impl(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
+                   c10::optional<torch::Tensor> kn_w, torch::Tensor cos_sin, torch::Tensor positions,
+                   torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache,
+                   __half* k_scale, __half* v_scale, int64_t nq, int64_t nkv, double eps, int kvq) {
   const int T = qkv.size(0);
   const int HD = cos_sin.size(1);
   TORCH_CHECK(qkv.size(1) == (nq + 2 * nkv) * HD, "qkv width mismatch");
@@ -268,19 +298,36 @@ void qkv_post(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optiona
   const int blocks = (warps * 32 + threads - 1) / threads;
   auto stream = at::cuda::getCurrentCUDAStream();
 #define B200_QKV(HDV)                                                                                       \
-  launch_pdl(qkv_post_kernel<HDV>, dim3(blocks), dim3(threads), 0, stream,                                  \
+  launch_pdl(kvq ? qkv_post_kernel<HDV, 1> : qkv_post_kernel<HDV, 0>, dim3(blocks), dim3(threads), 0, stream, \
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),                                               \
       bias ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr,                            \
       qn_w ? reinterpret_cast<const __nv_bfloat16*>(qn_w->data_ptr()) : nullptr,                            \
       kn_w ? reinterpret_cast<const __nv_bfloat16*>(kn_w->data_ptr()) : nullptr, cos_sin.data_ptr<float>(), \
       positions.data_ptr<int>(), slots.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), \
-      reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()), reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), T, \
-      (int)nq, (int)nkv, (float)eps)
+      k_cache.data_ptr(), v_cache.data_ptr(), k_scale, v_scale, T, (int)nq, (int)nkv, (float)eps)
   if (HD == 128) B200_QKV(128);
   else if (HD == 64) B200_QKV(64);
   else TORCH_CHECK(false, "head_dim must be 64 or 128");
 #undef B200_QKV
   B200_CHECK_CUDA(cudaGetLastError());
+}
+
+void qkv_post(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
+              c10::optional<torch::Tensor> kn_w, torch::Tensor cos_sin, torch::Tensor positions,
+              torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache, int64_t nq,
+              int64_t nkv, double eps) {
+  qkv_post_impl(qkv, bias, qn_w, kn_w, cos_sin, positions, slots, q_out, k_cache, v_cache, nullptr, nullptr, nq, nkv,
+                eps, 0);
+}
+
+// Same, writing K/V into an int4g128 cache (codes + fp16 scales).
+void qkv_post_q4(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
+                 c10::optional<torch::Tensor> kn_w, torch::Tensor cos_sin, torch::Tensor positions,
+                 torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_codes, torch::Tensor v_codes,
+                 torch::Tensor k_scale, torch::Tensor v_scale, int64_t nq, int64_t nkv, double eps) {
+  qkv_post_impl(qkv, bias, qn_w, kn_w, cos_sin, positions, slots, q_out, k_codes, v_codes,
+                reinterpret_cast<__half*>(k_scale.data_ptr()), reinterpret_cast<__half*>(v_scale.data_ptr()), nq, nkv,
+                eps, 1);
 }
 
 void silu_mul(torch::Tensor gu, torch::Tensor act) {

@@ -43,9 +43,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=32)
-    ap.add_argument("--prompt", type=int, default=2048)
-    ap.add_argument("--model", default="qwen3-8b")
+    ap.add_argument("--batch", type=int, default=0, help="0 = the config's batch (32 dense, 64 MoE)")
+    ap.add_argument("--prompt", type=int, default=0, help="0 = the config's prompt (2048 dense, 512 MoE)")
+    ap.add_argument("--model", default="qwen3-8b", choices=["qwen3-8b", "qwen3-30b-a3b"])
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
     ap.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for the headline)")
     return ap.parse_args()
@@ -89,8 +89,9 @@ def run_ours(a):
     torch.cuda.set_device(lrank)
     B, P, K, W = a.batch, a.prompt, a.steps, a.warmup
     max_seq = ((P + K + W + 64) + 15) // 16 * 16
-    cfg = EngineConfig(model=a.model, tp_size=world, max_batch=B, max_seq=max_seq, prefill_chunk=8192,
-                       cuda_graphs=True, comm=a.comm, num_layers_override=a.layers,
+    moe = a.model == "qwen3-30b-a3b"
+    cfg = EngineConfig(model=a.model, tp_size=world, ep_size=world if moe else 1, max_batch=B, max_seq=max_seq,
+                       prefill_chunk=8192, cuda_graphs=True, comm=a.comm, num_layers_override=a.layers,
                        kv_blocks=B * 2 * (max_seq // 16) + 64)
     eng = B200Engine(cfg)
     eng.load()
@@ -134,10 +135,11 @@ def run_ours(a):
         "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic token ids (uniform), random-init N(0,0.02) weights of the Qwen3-8B architecture",
-        "config": {"model": "qwen3-8b (36L, H4096, 32q/8kv, hd128, FFN12288, vocab151936)", "global_batch": B,
-                   "seq_len": P, "decode_context": f"{P}..{P + W + K}", "parallelism": f"tp{world}",
+        "config": {"model": MODEL_DESC[a.model], "global_batch": B,
+                   "seq_len": P, "decode_context": f"{P}..{P + W + K}",
+                   "parallelism": (f"ep{world}+attn-tp{world}" if moe else f"tp{world}"),
                    "comm": eng.comm.kind if eng.comm else "none",
-                   "l2": "inputs larger than L2: every step reads all 16.4 GB of weights and the KV cache"},
+                   "l2": "inputs larger than L2: every step streams the layer weights and the KV cache (GBs)"},
         "ttft_p50_ms": round(statistics.median(ttfts) * 1e3, 2),
         "clocks": clocks,
         "e2e": {"value": round(e2e_tps, 1), "unit": "tok/s", "api": "B200Engine.generate",
@@ -292,8 +294,17 @@ def _synthetic_hf_tokenizer(vocab):
     return fast
 
 
+MODEL_DESC = {
+    "qwen3-8b": "qwen3-8b (36L, H4096, 32q/8kv, hd128, FFN12288, vocab151936)",
+    "qwen3-30b-a3b": "qwen3-30b-a3b (48L, H2048, 32q/4kv, hd128, 128 experts top-8, expert FFN768, vocab151936)",
+}
+
+
 def main():
     a = parse()
+    moe = a.model == "qwen3-30b-a3b"
+    a.batch = a.batch or (64 if moe else 32)
+    a.prompt = a.prompt or (512 if moe else 2048)
     if a.impl == "reference":
         run_reference(a)
     else:

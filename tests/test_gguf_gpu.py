@@ -1,0 +1,45 @@
+"""GGUF dequant tensor-core GEMM (Q4_K, Q6_K, Q8_0) against the fp32 product of
+the CPU-dequantised weight (the oracle restating ggml's block formats)."""
+
+import numpy as np
+import pytest
+import torch
+
+from b200serve import ops
+from b200serve.models import gguf as G
+
+pytestmark = pytest.mark.gpu
+
+
+def _quant_weight(tt, N, K, seed=0):
+    rng = np.random.default_rng(seed)
+    w = rng.normal(0, 0.02, (N, K)).astype(np.float32)
+    raw = np.frombuffer(G.quantize(w, tt), dtype=np.uint8)
+    deq = G.dequantize(raw, tt, (N, K))
+    if tt == G.GGML_Q4_K:
+        codes, meta = G.repack_q4k_for_gpu(raw, N, K)
+        bits, group = 4, 32
+    elif tt == G.GGML_Q6_K:
+        q, s = G.q6k_to_s8(raw, N, K)
+        codes, meta = G.repack_s8_for_gpu(q, s, 16)
+        bits, group = 8, 16
+    else:
+        q, s = G.q8_0_to_s8(raw, N, K)
+        codes, meta = G.repack_s8_for_gpu(q, s, 32)
+        bits, group = 8, 32
+    to = lambda a: torch.from_numpy(a.view(np.int32).copy()).cuda()
+    return ops.QuantWeight(to(codes), to(meta), N, K, bits, group), torch.from_numpy(np.asarray(deq, dtype=np.float32))
+
+
+@pytest.mark.parametrize("tt", [G.GGML_Q4_K, G.GGML_Q6_K, G.GGML_Q8_0])
+@pytest.mark.parametrize("M", [1, 8, 13, 32])
+def test_gguf_gemm(tt, M):
+    N, K = 512, 2048
+    qw, deq = _quant_weight(tt, N, K)
+    # the GPU layout dequantises to the ggml values (scales rounded to bf16)
+    assert ((qw.dequantize().float().cpu() - deq).norm() / deq.norm()).item() < 1e-2
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    y = ops.linear(x, qw)
+    ref = x.float().cpu() @ deq.t()
+    rel = ((y.float().cpu() - ref).norm() / ref.norm()).item()
+    assert rel < 2e-2, rel

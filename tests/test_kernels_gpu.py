@@ -271,3 +271,50 @@ def test_paged_decode_attention_tensor_core(nq, nkv, lens, tps):
     e = torch.empty(0, device=dev)
     ops.ext().paged_decode_attention_tc(q, kc, vc, bt, sl, out1, e, e, scale, 4096, 1)
     assert _rel(out1.cpu(), ref) < 1e-2
+
+
+def test_int4g128_kv_write_and_attention():
+    """qkv_post_q4 writes codes matching the torch quantiser; decode and prefill
+    attention over the int4 cache match attention over the dequantised cache."""
+    hd, nq, nkv, nb = 128, 32, 8, 64
+    T = 40
+    qkv = torch.randn(T, (nq + 2 * nkv) * hd, device=dev).bfloat16()
+    qn = torch.ones(hd, device=dev).bfloat16()
+    cs = ops.rope_cos_sin(hd, 4096, 1e6, dev)
+    pos = torch.arange(T, device=dev, dtype=torch.int32)
+    perm = torch.randperm(nb, device=dev)[:3].int()
+    slots = (perm.repeat_interleave(16)[:T] * 16 + torch.arange(T, device=dev) % 16).int()
+    kc = torch.zeros(nb, nkv, 16, 64, dtype=torch.uint8, device=dev)
+    vc = torch.zeros_like(kc)
+    ks = torch.zeros(nb, nkv, 16, dtype=torch.float16, device=dev)
+    vs = torch.zeros_like(ks)
+    q = torch.empty(T, nq, hd, device=dev).bfloat16()
+    ops.ext().qkv_post_q4(qkv, None, qn, qn, cs, pos, slots, q, kc, vc, ks, vs, nq, nkv, 1e-6)
+    kb = torch.zeros(nb, nkv, 16, hd, device=dev).bfloat16()
+    vb = torch.zeros_like(kb)
+    q_ref = ops.qkv_post(qkv, None, qn, qn, cs, pos, slots, kb, vb, nq, nkv, 1e-6)
+    assert _rel(q, q_ref) < 1e-2
+    sl = slots.long()
+    c_ref, s_ref = ops.q4_quantize_rows(kb[sl // 16, :, sl % 16].float())
+    got = kc[sl // 16, :, sl % 16]
+    assert (got != c_ref).float().mean().item() < 0.02      # rounding ties may differ
+    kd = ops.q4_dequantize_rows(kc, ks).bfloat16()
+    vd = ops.q4_dequantize_rows(vc, vs).bfloat16()
+    bt = perm.view(1, 3)
+    # decode: the last token attends to all T
+    qd = q[-1:].contiguous()
+    lens = torch.tensor([T], dtype=torch.int32, device=dev)
+    ws = ops.AttnWorkspace(dev, 1, nkv, nq // nkv, hd, 1)
+    out = torch.empty_like(qd)
+    e = torch.empty(0, device=dev)
+    ops.ext().paged_decode_attention_q4(qd, kc, vc, ks, vs, bt, lens, out, e, e, 1 / math.sqrt(hd), 64, 1)
+    ref = ops.paged_decode_attention(qd.cpu(), kd.cpu(), vd.cpu(), bt.cpu(), lens.cpu(), 1 / math.sqrt(hd))
+    assert _rel(out.cpu(), ref) < 2e-2
+    # prefill: all T tokens causal
+    cu = torch.tensor([0, T], dtype=torch.int32, device=dev)
+    q0 = torch.tensor([0], dtype=torch.int32, device=dev)
+    outp = torch.empty_like(q)
+    ops.ext().paged_prefill_attention_q4(q, kc, vc, ks, vs, bt, lens, q0, cu, outp, 1 / math.sqrt(hd), T)
+    refp = ops.paged_prefill_attention(q.cpu(), kd.cpu(), vd.cpu(), bt.cpu(), lens.cpu(), q0.cpu(), cu.cpu(),
+                                       1 / math.sqrt(hd))
+    assert _rel(outp.cpu(), refp) < 2e-2
