@@ -123,7 +123,9 @@ class B200Engine(BaseEngine):
         if cfgE.weights == "safetensors":
             return W.load_safetensors_dir(mc, cfgE.model, **kw)
         if cfgE.weights == "gguf":
-            from b200serve.models.gguf import load_gguf_weights
+            from b200serve.models.gguf import load_gguf_quantized, load_gguf_weights
+            if dev.type == "cuda":
+                return load_gguf_quantized(mc, cfgE.model, **kw)
             return load_gguf_weights(mc, cfgE.model, **kw)
         raise ValueError(f"unknown weights source {cfgE.weights!r}")
 

@@ -534,3 +534,105 @@ def gpu_quant_weight(g: "GGUFFile", name: str, device):
         return None
     to = lambda a: torch.from_numpy(a.view(np.int32).copy()).to(device)
     return ops.QuantWeight(to(codes), to(meta), N, K, bits, group)
+
+
+# ------------------------------------------------------------------ quantised GPU model load
+def _raw_block_slice(g: "GGUFFile", name: str, rows=None, cols=None) -> np.ndarray:
+    """Raw block bytes of rows [r0, r1) and columns [c0, c1) of a 2-D block-quantised tensor
+    (columns must fall on block boundaries)."""
+    t = g.tensors[name]
+    N, K = t.shape
+    bs, ts = BLOCK_SIZE[t.ggml_type], TYPE_SIZE[t.ggml_type]
+    r0, r1 = rows or (0, N)
+    c0, c1 = cols or (0, K)
+    assert c0 % bs == 0 and c1 % bs == 0, "column shard must align to quantisation blocks"
+    raw = np.asarray(g.raw(name)).reshape(N, K // bs * ts)
+    return np.ascontiguousarray(raw[r0:r1, c0 // bs * ts:c1 // bs * ts]).reshape(-1)
+
+
+def _repack(raw, ggml_type, N, K, device):
+    import torch
+    from b200serve import ops
+    if ggml_type == GGML_Q4_K:
+        codes, meta = repack_q4k_for_gpu(raw, N, K)
+        bits, group = 4, 32
+    elif ggml_type == GGML_Q6_K:
+        q, s = q6k_to_s8(raw, N, K)
+        codes, meta = repack_s8_for_gpu(q, s, 16)
+        bits, group = 8, 16
+    elif ggml_type == GGML_Q8_0:
+        q, s = q8_0_to_s8(raw, N, K)
+        codes, meta = repack_s8_for_gpu(q, s, 32)
+        bits, group = 8, 32
+    else:
+        raise NotImplementedError(TYPE_NAME.get(ggml_type, ggml_type))
+    to = lambda a: torch.from_numpy(a.view(np.int32).copy()).to(device)
+    return ops.QuantWeight(to(codes), to(meta), N, K, bits, group)
+
+
+QUANT_TYPES = (GGML_Q4_K, GGML_Q6_K, GGML_Q8_0)
+
+
+class QuantGroup(list):
+    """Several QuantWeights applied to the same input, outputs concatenated (fused QKV
+    whose parts have different block types)."""
+
+    @property
+    def shape(self):
+        return (sum(w.N for w in self), self[0].K)
+
+
+def load_gguf_quantized(cfg, path: str, tp_rank=0, tp_size=1, dtype=None, device="cuda", **_):
+    """Per-rank ModelWeights whose projections stay block-quantised on the GPU
+    (ops.QuantWeight); norms, biases and the embedding table are dequantised."""
+    import torch
+    from b200serve.models.weights import LayerWeights, ModelWeights, vocab_shard
+    dtype = dtype or torch.bfloat16
+    g = read_gguf_file(path)
+    H, hd = cfg.hidden_size, cfg.head_dim
+    nq, nkv = cfg.num_heads // tp_size, cfg.num_kv_heads // tp_size
+    I = cfg.intermediate_size
+    Ir = I // tp_size
+
+    def deq(name):
+        return torch.from_numpy(np.array(g.dequantize(name), dtype=np.float32)).to(device=device, dtype=dtype)
+
+    def qw(name, rows=None, cols=None):
+        t = g.tensors[name]
+        N, K = t.shape
+        r0, r1 = rows or (0, N)
+        c0, c1 = cols or (0, K)
+        if t.ggml_type in QUANT_TYPES and (r1 - r0) % 16 == 0 and (c1 - c0) % 256 == 0:
+            return _repack(_raw_block_slice(g, name, rows, cols), t.ggml_type, r1 - r0, c1 - c0, device)
+        w = deq(name)[r0:r1, c0:c1].contiguous()
+        from b200serve import ops
+        return ops.pack_weight(w)
+
+    layers = []
+    for i in range(cfg.num_layers):
+        p = f"blk.{i}."
+        q = qw(p + "attn_q.weight", rows=(tp_rank * nq * hd, (tp_rank + 1) * nq * hd))
+        k = qw(p + "attn_k.weight", rows=(tp_rank * nkv * hd, (tp_rank + 1) * nkv * hd))
+        v = qw(p + "attn_v.weight", rows=(tp_rank * nkv * hd, (tp_rank + 1) * nkv * hd))
+        o = qw(p + "attn_output.weight", cols=(tp_rank * nq * hd, (tp_rank + 1) * nq * hd))
+        gate = qw(p + "ffn_gate.weight", rows=(tp_rank * Ir, (tp_rank + 1) * Ir))
+        up = qw(p + "ffn_up.weight", rows=(tp_rank * Ir, (tp_rank + 1) * Ir))
+        down = qw(p + "ffn_down.weight", cols=(tp_rank * Ir, (tp_rank + 1) * Ir))
+        lw = LayerWeights(input_norm=deq(p + "attn_norm.weight"), post_norm=deq(p + "ffn_norm.weight"),
+                          qkv=QuantGroup([q, k, v]), o=o)
+        if p + "attn_q_norm.weight" in g.tensors:
+            lw.q_norm, lw.k_norm = deq(p + "attn_q_norm.weight"), deq(p + "attn_k_norm.weight")
+        if p + "attn_q.bias" in g.tensors:
+            sl = lambda n, a, b: deq(n)[a:b]
+            lw.qkv_bias = torch.cat([sl(p + "attn_q.bias", tp_rank * nq * hd, (tp_rank + 1) * nq * hd),
+                                     sl(p + "attn_k.bias", tp_rank * nkv * hd, (tp_rank + 1) * nkv * hd),
+                                     sl(p + "attn_v.bias", tp_rank * nkv * hd, (tp_rank + 1) * nkv * hd)])
+        lw.gate_up = QuantGroup([gate, up])      # SwiGLU applied after the two products
+        lw.down = down
+        layers.append(lw)
+    embed = deq("token_embd.weight")
+    v0, v1 = vocab_shard(cfg.vocab_size, tp_rank, tp_size)
+    out_name = "output.weight" if "output.weight" in g.tensors else "token_embd.weight"
+    lm = qw(out_name, rows=(v0, v1)) if (v1 - v0) % 16 == 0 else deq(out_name)[v0:v1].contiguous()
+    return ModelWeights(embed=embed, final_norm=deq("output_norm.weight"), lm_head=lm, layers=layers,
+                        vocab_start=v0, tp_rank=tp_rank, tp_size=tp_size)

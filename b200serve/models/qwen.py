@@ -93,7 +93,6 @@ class Decoder:
                 t = getattr(lw, name)
                 if isinstance(t, torch.Tensor):
                     setattr(lw, name, ops.pack_weight(t))
-            del t
         if isinstance(w.lm_head, torch.Tensor) and w.lm_head.data_ptr() != w.embed.data_ptr():
             w.lm_head = ops.pack_weight(w.lm_head)
         elif isinstance(w.lm_head, torch.Tensor):

@@ -306,6 +306,12 @@ def _bf16_from_bits(b: torch.Tensor) -> torch.Tensor:
     return (b.to(torch.int32) << 16).view(torch.float32)
 
 
+def _interleave64(g, u):
+    """[T, I] gate and up -> [T, 2I] in the 64-column interleaved order silu_mul expects."""
+    T, I = g.shape
+    return torch.stack([g.view(T, I // 64, 64), u.view(T, I // 64, 64)], 2).reshape(T, 2 * I)
+
+
 def pack_weight(w):
     """Pack a CUDA weight for the GEMM (idempotent; CPU tensors stay plain)."""
     if isinstance(w, PackedWeight) or w is None or not w.is_cuda or w.dim() != 2:
@@ -320,14 +326,33 @@ def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspac
     interleaved gate/up weight and writes silu(gate)*up of width N/2.
     """
     M, K = x.shape
+    if isinstance(w, list):                         # QuantGroup: parts share the input
+        if epilogue == EPI_SWIGLU:
+            g, u = (linear(x, p) for p in w)
+            return silu_mul(_interleave64(g, u), out=out)
+        parts = [linear(x, p) for p in w]
+        y = torch.cat(parts, dim=1)
+        if bias is not None:
+            y = (y.float() + bias.float()).to(x.dtype)
+        if epilogue == EPI_F32:
+            y = y.float()
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
     N = w.shape[0]
     packed_n = 0
     if isinstance(w, QuantWeight):
-        if x.is_cuda and M <= 32 and epilogue == EPI_BF16 and bias is None and residual is None:
-            out = out if out is not None else torch.empty(M, N, dtype=x.dtype, device=x.device)
+        if x.is_cuda and M <= 32 and epilogue in (EPI_BF16, EPI_F32) and bias is None and residual is None:
+            y = torch.empty(M, N, dtype=x.dtype, device=x.device)
             _cuda(x)
-            ext().gguf_gemm(x.contiguous(), w.codes, w.meta, N, w.bits, w.group, out)
-            return out
+            ext().gguf_gemm(x.contiguous(), w.codes, w.meta, N, w.bits, w.group, y)
+            if epilogue == EPI_F32:
+                y = y.float()
+            if out is not None:
+                out.copy_(y)
+                return out
+            return y
         w = w.dequantize() if x.is_cuda else w.dequantize().cpu()
         if x.is_cuda:
             w = PackedWeight(w)

@@ -179,13 +179,13 @@ __global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __n
       const float scale = amax > 0.f ? amax / 7.f : 1.f;
       const __half scale_h = __float2half_rn(scale);
       const float inv = 1.f / __half2float(scale_h);
-      static_assert(E == 4, "int4 KV cache needs head_dim 128");
+      // (host side allows head_dim 128 only; this branch is compiled but unused for 64)
       // 8 dims per 32-bit word; dims (2p, 2p+1) of the group go to nibbles (p, p + 4) so the
       // reader turns a nibble pair into a bf16 pair with one mask-and-or
       uint32_t part = 0;
       const int base = (lane & 1) * 4;   // this lane holds dims 4l..4l+3 = group offsets base..base+3
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < E; ++i) {
         const uint32_t q = (uint32_t)(max(-8, min(7, __float2int_rn(x[i] * inv))) + 8);
         const int o = base + i, pr = o >> 1, hi = o & 1;
         part |= q << (4 * (pr + 4 * hi));
@@ -325,6 +325,7 @@ void qkv_post_q4(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::opti
                  c10::optional<torch::Tensor> kn_w, torch::Tensor cos_sin, torch::Tensor positions,
                  torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_codes, torch::Tensor v_codes,
                  torch::Tensor k_scale, torch::Tensor v_scale, int64_t nq, int64_t nkv, double eps) {
+  TORCH_CHECK(cos_sin.size(1) == 128, "int4g128 KV cache needs head_dim 128");
   qkv_post_impl(qkv, bias, qn_w, kn_w, cos_sin, positions, slots, q_out, k_codes, v_codes,
                 reinterpret_cast<__half*>(k_scale.data_ptr()), reinterpret_cast<__half*>(v_scale.data_ptr()), nq, nkv,
                 eps, 1);

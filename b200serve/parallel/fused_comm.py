@@ -119,7 +119,8 @@ class FusedComm:
     def linear_reduce(self, x: torch.Tensor, w: torch.Tensor, tag: str):
         """Row-parallel GEMM + all-reduce. Returns the parts the next RMSNorm sums."""
         T = x.shape[0]
-        if T > self.max_tokens:
+        if T > self.max_tokens or not isinstance(w, (torch.Tensor, ops.PackedWeight)):
+            # large chunks (NVLS all-reduce is bandwidth-optimal) and quantised weights take NCCL
             y = ops.linear(x, w)
             return self.nccl.reduce_parts(y, tag)
         site = self.site
