@@ -42,6 +42,8 @@ class ModelRunner:
         self.graph_out = {}
         self.launches_per_step = {}
         self.last_loop_ms = None
+        self.h_toks = None
+        self._pipe = None
         self.vocab_start = weights.vocab_start
         self.greedy_buf = None
         pin = self.device.type == "cuda"
@@ -190,6 +192,46 @@ class ModelRunner:
         ms = start.elapsed_time(end)
         self.last_loop_ms = ms
         return {"ms": ms, "launches_per_step": self.launches_per_step.get(bucket)}
+
+    # ------------------------------------------------------------ pipelined greedy decode
+    def pipeline_start(self, ids, pos, slots, block_tables, lens):
+        """Load a fresh decode state (one H2D copy); subsequent pipeline_step() calls advance
+        it on the device without host inputs."""
+        B = len(ids)
+        bucket, nbytes = self.load_decode_inputs(ids, pos, slots, block_tables, lens)
+        self._pipe = {"B": B, "bucket": bucket}
+        if self.h_toks is None:
+            pin = self.device.type == "cuda"
+            self.h_toks = [torch.zeros(self.max_batch, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+        return nbytes
+
+    def pipeline_patch_block(self, row: int, block_index: int, block: int):
+        """Point entry ``block_index`` of sequence ``row``'s block table at ``block`` (device)."""
+        self.s_bt[row, block_index] = block
+
+    def pipeline_step(self, slot: int):
+        """Replay the decode+advance graph once and start copying its tokens into pinned
+        buffer ``slot``; returns the CUDA event that marks the copy complete."""
+        B, bucket = self._pipe["B"], self._pipe["bucket"]
+        key = (bucket, "loop", B)
+        if key not in self.graphs:
+            for _ in range(2):
+                _, toks = self._decode_body(bucket, True)
+            torch.cuda.synchronize()
+            ops.reset_launch_count()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                _, toks = self._decode_body(bucket, True)
+                self._advance(toks, B)
+            self.launches_per_step[bucket] = ops.launch_count()
+            self.graphs[key] = g
+            self.graph_out[key] = toks
+        self.graphs[key].replay()
+        # s_ids now holds this step's tokens (the advance copied them); read them back async
+        self.h_toks[slot][:B].copy_(self.s_ids[:B], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        return ev
 
     def release_graphs(self):
         self.graphs.clear()

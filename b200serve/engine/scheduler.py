@@ -79,6 +79,7 @@ class Scheduler:
         self.waiting = []
         self.running = []
         self.lock = threading.Lock()
+        self.pipeline = True
         self.stats = {"steps": 0, "decode_steps": 0, "mixed_steps": 0, "preemptions": 0,
                       "generated": 0, "prefill_tokens": 0, "prefix_hit_tokens": 0}
 
@@ -194,6 +195,73 @@ class Scheduler:
             self._finish(req, "length")
 
     # ------------------------------------------------------------ step
+    # ------------------------------------------------------------ pipelined greedy decode
+    def _pipe_ok(self, batch) -> bool:
+        """The device-advanced loop applies when every request decodes greedily, nothing
+        waits for admission and the runner supports it (single rank, CUDA graphs)."""
+        r = self.runner
+        return (getattr(r, "use_graphs", False) and hasattr(r, "pipeline_step")
+                and not self.waiting and all(
+                    q.params.greedy and q.params.repeat_penalty == 1.0 and not q.params.presence_penalty
+                    and not q.params.frequency_penalty for q in batch))
+
+    def _pipelined_decode(self, batch) -> int:
+        """Decode ``batch`` until it changes, keeping one step in flight: step N runs on the
+        GPU while the host accepts the tokens of step N-1. Returns tokens accepted."""
+        r = self.runner
+        for q in batch:
+            if not self._ensure_blocks(q, len(q.tokens) + 1):
+                return self._decode_step_sync()
+        ids = [q.tokens[-1] for q in batch]
+        pos = [len(q.tokens) - 1 for q in batch]
+        slots = [q.blocks[p // BLOCK] * BLOCK + p % BLOCK for q, p in zip(batch, pos)]
+        r.pipeline_start(ids, pos, slots, [q.blocks for q in batch], [p + 1 for p in pos])
+        accepted = 0
+        pending = None            # (event, slot) of the step whose tokens are not yet accepted
+        slot = 0
+        live = list(batch)
+        while True:
+            # the step about to run computes position len(tokens) (+1 if a step is pending)
+            lag = 1 if pending is not None else 0
+            for i, q in enumerate(batch):
+                nxt = len(q.tokens) + lag          # position written by the step we launch now
+                bi = nxt // BLOCK
+                if bi >= len(q.blocks):
+                    if not self._ensure_blocks(q, nxt + 1):
+                        live = []                 # out of pages: drain and fall back
+                        break
+                    r.pipeline_patch_block(i, bi, q.blocks[bi])
+            if not live:
+                break
+            ev = r.pipeline_step(slot)
+            self.stats["steps"] += 1
+            self.stats["decode_steps"] += 1
+            if pending is not None:
+                accepted += self._accept_pipelined(batch, *pending)
+            pending = (ev, slot)
+            slot ^= 1
+            if any(q.state == "finished" for q in batch) or self.waiting or \
+                    any(len(q.tokens) + 2 >= self.max_seq for q in batch):
+                break
+        if pending is not None:
+            accepted += self._accept_pipelined(batch, *pending)
+        for q in batch:
+            if q.state == "finished" and q in self.running:
+                self.running.remove(q)
+        return accepted
+
+    def _accept_pipelined(self, batch, ev, slot) -> int:
+        ev.synchronize()
+        toks = self.runner.h_toks[slot][:len(batch)].tolist()
+        n = 0
+        for q, t in zip(batch, toks):
+            if q.state == "finished":
+                continue               # computed one step past its end: discarded
+            q.num_computed = len(q.tokens)
+            self._accept_token(q, int(t))
+            n += 1
+        return n
+
     def step(self) -> int:
         """Run one forward pass. Returns the number of tokens sampled."""
         self._admit()
@@ -205,6 +273,11 @@ class Scheduler:
         self.stats["steps"] += 1
         if any(r.num_computed < len(r.tokens) - 1 for r in self.running):
             return self._mixed_step()
+        if self.pipeline and self._pipe_ok(self.running):
+            return self._pipelined_decode(list(self.running))
+        return self._decode_step()
+
+    def _decode_step_sync(self) -> int:
         return self._decode_step()
 
     def _decode_step(self) -> int:

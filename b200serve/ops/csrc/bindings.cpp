@@ -58,6 +58,7 @@ void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optiona
              c10::optional<torch::Tensor> residual, torch::Tensor ws, torch::Tensor counters, int64_t epi,
              int64_t force_splits, int64_t packed_n);
 int64_t gemm_error_flag(bool reset);
+void gemm_set_trace(int64_t ptr);
 void gemm_grouped(torch::Tensor act, torch::Tensor w_packed, int64_t N, int64_t E, torch::Tensor offsets,
                   int64_t max_rows, torch::Tensor out, torch::Tensor ws, torch::Tensor counters, int64_t epi);
 void argmax_rows(torch::Tensor logits, torch::Tensor out_idx, torch::Tensor out_val, int64_t index_offset);
@@ -95,6 +96,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_plan", &gemm_plan);
   m.def("gemm_tc", &gemm_tc);
   m.def("gemm_error_flag", &gemm_error_flag);
+  m.def("gemm_set_trace", &gemm_set_trace);
   m.def("gemm_grouped", &gemm_grouped);
   m.def("argmax_rows", &argmax_rows);
   m.def("argmax_merge", &argmax_merge);

@@ -103,6 +103,10 @@ static CUtensorMap weight_tmap(const torch::Tensor& w, int N, int K, bool packed
   return make_tmap_bf16(w.data_ptr(), w.size(0), 64, 64, 128);
 }
 
+static unsigned long long* g_trace = nullptr;   // set by gemm_set_trace (diagnostics only)
+
+void gemm_set_trace(int64_t ptr) { g_trace = reinterpret_cast<unsigned long long*>(ptr); }
+
 void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> bias,
              c10::optional<torch::Tensor> residual, torch::Tensor ws, torch::Tensor counters, int64_t epi,
              int64_t force_splits, int64_t packed_n) {
@@ -152,6 +156,7 @@ void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optiona
   }
   p.err = gemm_err_word();
   p.w_packed = packed ? 1 : 0;
+  p.trace = g_trace;
   CUtensorMap tw = weight_tmap(w, N, K, packed);
   CUtensorMap ta = make_tmap_bf16(act.data_ptr(), M, K, act.stride(0), BN);
   auto stream = at::cuda::getCurrentCUDAStream();

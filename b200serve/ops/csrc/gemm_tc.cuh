@@ -56,7 +56,14 @@ struct GemmParams {
   int* push_flag[kMaxPeers];            // flag word on rank r for (site, this rank)
   const int* epoch;                     // this step's epoch (device)
   int* tile_done;                       // local counter of pushed tiles, zero on entry and exit
+  // optional per-CTA timeline (globaltimer ns): [cta][8] = entry, setup done, first TMA issued,
+  // first stage landed, last MMA committed, epilogue done, exit
+  unsigned long long* trace;
 };
+
+__device__ __forceinline__ void trace_mark(const GemmParams& p, int slot) {
+  if (p.trace) p.trace[blockIdx.x * 8 + slot] = globaltimer_ns();
+}
 
 
 template <int BN>
@@ -105,16 +112,29 @@ __device__ __forceinline__ void epilogue_store(const GemmParams& p, float* v, in
     }
     epi_bar();
   } else if constexpr (EPI == EPI_PUSH) {
-    const int col = n_tile * 128 + row;
-    if (col >= p.N) return;
-    const float b = p.bias ? __bfloat162float(p.bias[col]) : 0.f;
+    // stage the 16-token x 128-feature chunk as bf16 rows, then push 16-byte vectors:
+    // consecutive threads cover consecutive 16-byte pieces of a token row on every peer
+    __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(xchg);      // [16][136]
+    {
+      const int col = n_tile * 128 + row;
+      const float b = (p.bias && col < p.N) ? __bfloat162float(p.bias[col]) : 0.f;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int t = t0 + j;
-      if (t >= t_end) break;
-      const __nv_bfloat16 v16 = __float2bfloat16_rn(v[j] + b);
-      for (int r = 0; r < p.world; ++r) p.push_dst[r][(size_t)t * p.ldo + col] = v16;
+      for (int j = 0; j < 16; ++j) xs[j * 136 + row] = __float2bfloat16_rn(v[j] + b);
     }
+    epi_bar();
+    const int tid = threadIdx.x - 64;                                    // 0..127 over the epilogue warps
+#pragma unroll
+    for (int rep = 0; rep < 2; ++rep) {
+      const int piece = tid + rep * 128;                                 // 16 tokens x 16 pieces of 8 features
+      const int tok = piece >> 4, chunk = piece & 15;
+      const int t = t0 + tok, col = n_tile * 128 + chunk * 8;
+      if (t < t_end && col < p.N) {
+        const uint4 val = *reinterpret_cast<const uint4*>(xs + tok * 136 + chunk * 8);
+        for (int r = 0; r < p.world; ++r)
+          *reinterpret_cast<uint4*>(p.push_dst[r] + (size_t)t * p.ldo + col) = val;
+      }
+    }
+    epi_bar();
   } else {
     const int col = n_tile * 128 + row;
     if (col >= p.N) return;
@@ -214,6 +234,7 @@ __global__ void __launch_bounds__(192, 2)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* err = p.err;  // never null: the host passes its error word
+  if (threadIdx.x == 0) trace_mark(p, 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { tc::mbar_init(&full[s], 1); tc::mbar_init(&empty[s], 1); }
@@ -235,6 +256,7 @@ __global__ void __launch_bounds__(192, 2)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) trace_mark(p, 1);
   pdl_trigger();
   if (warp != 0) pdl_wait();
 
@@ -258,6 +280,7 @@ __global__ void __launch_bounds__(192, 2)
         pdl_wait();
         for (int i = 0; i < pre; ++i)
           tc::tma_load_2d(s_a + i * Cfg::A_BYTES, &tm_a, &full[i], (kb0 + i) * 64, x.a_row0, pol_a);
+        trace_mark(p, 2);
         stage = pre % STAGES;
         phase = pre == STAGES ? 1 : 0;
       } else {
@@ -283,11 +306,17 @@ __global__ void __launch_bounds__(192, 2)
       uint32_t phase = 0;
       uint32_t acc_phase[2] = {0, 0};
       int acc = 0;
+      bool first = true;
       for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
         const Unit x = decode_unit(p, u, BN);
         if (x.empty) continue;
         const int kb0 = x.split * p.kb_per_split, kb1 = min(p.kb_total, kb0 + p.kb_per_split);
         if (!tc::mbar_wait_bounded(&tempty[acc], acc_phase[acc] ^ 1, abort_flag, err, 2)) break;
+        if (first) {
+          tc::mbar_wait_bounded(&full[stage], phase, abort_flag, err, 3);
+          trace_mark(p, 3);
+          first = false;
+        }
         tc::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -307,6 +336,7 @@ __global__ void __launch_bounds__(192, 2)
         acc_phase[acc] ^= 1;
         acc ^= 1;
       }
+      trace_mark(p, 4);
       // no tcgen05.mma may still be running when TMEM is released below
       tc::mma_commit(mma_done);
       volatile int never = 0;
@@ -378,8 +408,10 @@ __global__ void __launch_bounds__(192, 2)
       acc ^= 1;
     }
   }
+  if (threadIdx.x == 64) trace_mark(p, 5);
   tc::tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) trace_mark(p, 6);
   if (*abort_flag) {
     // error path: give TMA copies that may still be landing in shared memory time to finish
     const uint64_t until = globaltimer_ns() + 100000ull;

@@ -12,8 +12,9 @@ from __future__ import annotations
 
 import torch
 
-OP_DECODE, OP_PREFILL, OP_STOP, OP_LOOP = 1, 2, 3, 4
-HDR = 8
+OP_DECODE, OP_PREFILL, OP_STOP, OP_LOOP, OP_PIPE_START, OP_PIPE_STEP = 1, 2, 3, 4, 5, 6
+HDR = 32
+MAX_PATCH = (HDR - 2) // 3   # block-table patches carried inline in a PIPE_STEP header
 
 
 class BroadcastRunner:
@@ -28,6 +29,7 @@ class BroadcastRunner:
         return getattr(self.inner, name)
 
     def _send(self, header, payload: torch.Tensor = None):
+        assert len(header) <= HDR
         h = torch.tensor(header + [0] * (HDR - len(header)), dtype=torch.int64)
         self.hdr.copy_(h)
         self.comm.broadcast(self.hdr, 0)
@@ -58,6 +60,35 @@ class BroadcastRunner:
         self._send([OP_LOOP, B, bucket, warmup, steps], self.inner.s_pack[:n])
         _unpack_static(self.inner, bucket)
         return self.inner.loop_body(B, bucket, warmup, steps)
+
+    # pipelined greedy decode: every rank replays the device-advancing graph in lock-step
+    def pipeline_start(self, ids, pos, slots, block_tables, lens):
+        B = len(ids)
+        nbytes = self.inner.pipeline_start(ids, pos, slots, block_tables, lens)
+        bucket = self.inner._pipe["bucket"]
+        n = bucket * (4 + self.inner.max_blocks)
+        self._send([OP_PIPE_START, B, bucket], self.inner.s_pack[:n])
+        self._patches = []
+        return nbytes
+
+    def pipeline_patch_block(self, row, block_index, block):
+        self._patches.append((row, block_index, block))
+
+    def pipeline_step(self, slot):
+        patches, self._patches = self._patches, []
+        while len(patches) > MAX_PATCH:       # overflow: ship the excess in extra headers
+            chunk, patches = patches[:MAX_PATCH], patches[MAX_PATCH:]
+            self._send([OP_PIPE_STEP, -len(chunk)] + [v for p in chunk for v in p])
+            for r, i, b in chunk:
+                self.inner.pipeline_patch_block(r, i, b)
+        self._send([OP_PIPE_STEP, len(patches)] + [v for p in patches for v in p])
+        for r, i, b in patches:
+            self.inner.pipeline_patch_block(r, i, b)
+        return self.inner.pipeline_step(slot)
+
+    @property
+    def h_toks(self):
+        return self.inner.h_toks
 
     def shutdown_workers(self):
         self._send([OP_STOP])
@@ -125,6 +156,21 @@ def worker_loop(runner, comm):
             comm.broadcast(runner.s_pack[:n], 0)
             _unpack_static(runner, bucket)
             runner.loop_body(B, bucket, warmup, steps)
+        elif op == OP_PIPE_START:
+            B, bucket = h[1], h[2]
+            n = bucket * (4 + runner.max_blocks)
+            comm.broadcast(runner.s_pack[:n], 0)
+            _unpack_static(runner, bucket)
+            runner._pipe = {"B": B, "bucket": bucket}
+            if runner.h_toks is None:
+                runner.h_toks = [torch.zeros(runner.max_batch, dtype=torch.int32, pin_memory=True)
+                                 for _ in range(2)]
+        elif op == OP_PIPE_STEP:
+            n = abs(h[1])
+            for j in range(n):
+                runner.pipeline_patch_block(h[2 + 3 * j], h[3 + 3 * j], h[4 + 3 * j])
+            if h[1] >= 0:
+                runner.pipeline_step(0)
         elif op == OP_PREFILL:
             payload = torch.empty(h[1], dtype=torch.int32, device=runner.device)
             comm.broadcast(payload, 0)

@@ -98,6 +98,84 @@ def run_one(M, N, K, iters=5):
     print(json.dumps({"case": "one", "M": M, "N": N, "K": K, "ok": True}))
 
 
+def attn_one(B=32, L=2304, nq=32, nkv=8, iters=5):
+    """A few launches of the decode attention at one shape (small case for ncu)."""
+    hd = 128
+    nblk = (L + 15) // 16
+    kc = torch.randn(B * nblk, nkv, 16, hd, device="cuda").bfloat16()
+    vc = torch.randn_like(kc)
+    bt = torch.arange(B * nblk, device="cuda", dtype=torch.int32).view(B, nblk)
+    sl = torch.full((B,), L, dtype=torch.int32, device="cuda")
+    q = torch.randn(B, nq, hd, device="cuda").bfloat16()
+    per = B * nkv
+    tps = 64 if per <= 16 else 128 if per <= 64 else 256 if per <= 128 else 512
+    nsplit = (L + tps - 1) // tps
+    ws = ops.AttnWorkspace("cuda", B, nkv, nq // nkv, hd, nsplit)
+    for _ in range(iters):
+        ops.paged_decode_attention(q, kc, vc, bt, sl, 1 / math.sqrt(hd), tps, nsplit, ws)
+    torch.cuda.synchronize()
+    ms = time_cuda(lambda: ops.paged_decode_attention(q, kc, vc, bt, sl, 1 / math.sqrt(hd), tps, nsplit, ws))
+    byts = 2 * B * L * nkv * hd * 2
+    print(json.dumps({"case": "attn_one", "B": B, "L": L, "tps": tps, "nsplit": nsplit, "ms": round(ms, 4),
+                      "GBps": round(byts / ms / 1e6, 1)}))
+
+
+def gguf_one(M=8, N=6144, K=4096, iters=5):
+    from b200serve.models.gguf_gpu import to_quant_weight
+    w = (torch.randn(N, K, device="cuda") * 0.02)
+    qw = to_quant_weight(w, "q4_k")
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    for _ in range(iters):
+        ops.linear(x, qw)
+    torch.cuda.synchronize()
+    ms = time_cuda(lambda: ops.linear(x, qw))
+    wbytes = qw.codes.numel() * 4 + qw.meta.numel() * 4
+    ms_bf16 = time_cuda(lambda: ops.linear(x, ops.pack_weight(w.bfloat16())))
+    print(json.dumps({"case": "gguf_q4k", "M": M, "N": N, "K": K, "ms": round(ms, 4),
+                      "GBps_quant": round(wbytes / ms / 1e6, 1), "bf16_gemm_ms": round(ms_bf16, 4)}))
+
+
+def sample_one(B=32, V=151936, iters=5):
+    logits = torch.randn(B, V, device="cuda") * 3
+    args = ([0.7] * B, [40] * B, [0.9] * B, [0.0] * B, [1] * B, [0] * B)
+    for _ in range(iters):
+        ops.sample_rows(logits.clone(), *args)
+    torch.cuda.synchronize()
+    ms = time_cuda(lambda: ops.sample_rows(logits, *args))
+    print(json.dumps({"case": "sampler_topk_topp", "B": B, "V": V, "ms": round(ms, 4)}))
+
+
+def gemm_trace(M=32, N=4096, K=4096):
+    """Per-CTA timeline of one GEMM launch (globaltimer ns, relative to the first CTA entry)."""
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    w = ops.pack_weight((torch.randn(N, K, device="cuda") * 0.02).bfloat16())
+    y = ops.linear(x, w)
+    buf = torch.zeros(148 * 8, dtype=torch.int64, device="cuda")
+    from b200serve.utils.timing import L2Flusher
+    fl = L2Flusher()
+    for _ in range(3):
+        ops.linear(x, w, out=y)
+    fl()
+    torch.cuda.synchronize()
+    ops.ext().gemm_set_trace(buf.data_ptr())
+    ops.linear(x, w, out=y)
+    torch.cuda.synchronize()
+    ops.ext().gemm_set_trace(0)
+    t = buf.view(148, 8)[:, :7].cpu()
+    used = t[:, 0] > 0
+    t = t[used]
+    t0 = t[:, 0].min()
+    rel = (t - t0).float() / 1000.0
+    names = ["entry", "setup", "tma_issued", "first_data", "mma_done", "epi_done", "exit"]
+    out = {"case": "gemm_trace", "M": M, "N": N, "K": K, "ctas": int(used.sum())}
+    for i, n in enumerate(names):
+        col = rel[:, i]
+        col = col[t[:, i] > 0] if (t[:, i] > 0).any() else col
+        out[n] = {"min": round(col.min().item(), 2), "med": round(col.median().item(), 2),
+                  "max": round(col.max().item(), 2)}
+    print(json.dumps(out))
+
+
 def decode_step(layers=2, B=32, ctx=2304, iters=3):
     """Eager decode steps of the Qwen3-8B shape (``layers`` layers) at batch B and
     context ``ctx``: the kernel sequence of one step, for launch lists / ncu."""
@@ -129,6 +207,18 @@ if __name__ == "__main__":
     ops.ext()
     if what == "one":
         run_one(*[int(v) for v in sys.argv[2:5]])
+        sys.exit(0)
+    if what == "gemm_trace":
+        gemm_trace(*[int(v) for v in sys.argv[2:5]])
+        sys.exit(0)
+    if what == "attn_one":
+        attn_one(*[int(v) for v in sys.argv[2:6]])
+        sys.exit(0)
+    if what == "gguf_one":
+        gguf_one(*[int(v) for v in sys.argv[2:5]])
+        sys.exit(0)
+    if what == "sample_one":
+        sample_one(*[int(v) for v in sys.argv[2:4]])
         sys.exit(0)
     if what == "decode_step":
         decode_step(*[int(v) for v in sys.argv[2:5]])

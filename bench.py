@@ -47,6 +47,8 @@ def parse():
     ap.add_argument("--prompt", type=int, default=0, help="0 = the config's prompt (2048 dense, 512 MoE)")
     ap.add_argument("--model", default="qwen3-8b", choices=["qwen3-8b", "qwen3-30b-a3b"])
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
+    ap.add_argument("--weights", default="bf16", choices=["bf16", "gguf"],
+                    help="gguf: random-init bf16 weights quantised on the GPU into the Q4_K_M mix")
     ap.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for the headline)")
     return ap.parse_args()
 
@@ -95,6 +97,10 @@ def run_ours(a):
                        kv_blocks=B * 2 * (max_seq // 16) + 64)
     eng = B200Engine(cfg)
     eng.load()
+    if a.weights == "gguf":
+        from b200serve.models.gguf_gpu import quantize_model_q4_k_m
+        quantize_model_q4_k_m(eng.weights, eng.model_cfg)
+        torch.cuda.empty_cache()
     vocab = eng.model_cfg.vocab_size
     runner = eng.runner
     inner = getattr(runner, "inner", runner)
@@ -135,7 +141,8 @@ def run_ours(a):
         "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic token ids (uniform), random-init N(0,0.02) weights of the Qwen3-8B architecture",
-        "config": {"model": MODEL_DESC[a.model], "global_batch": B,
+        "config": {"model": MODEL_DESC[a.model] + (" as GGUF Q4_K_M (Q6_K attn_v/ffn_down, Q8_0 output)"
+                                                   if a.weights == "gguf" else ""), "global_batch": B,
                    "seq_len": P, "decode_context": f"{P}..{P + W + K}",
                    "parallelism": (f"ep{world}+attn-tp{world}" if moe else f"tp{world}"),
                    "comm": eng.comm.kind if eng.comm else "none",
@@ -303,8 +310,9 @@ MODEL_DESC = {
 def main():
     a = parse()
     moe = a.model == "qwen3-30b-a3b"
-    a.batch = a.batch or (64 if moe else 32)
-    a.prompt = a.prompt or (512 if moe else 2048)
+    gguf = a.weights == "gguf"
+    a.batch = a.batch or (64 if moe else 8 if gguf else 32)
+    a.prompt = a.prompt or (512 if moe else 1024 if gguf else 2048)
     if a.impl == "reference":
         run_reference(a)
     else:

@@ -43,3 +43,16 @@ def test_gguf_gemm(tt, M):
     ref = x.float().cpu() @ deq.t()
     rel = ((y.float().cpu() - ref).norm() / ref.norm()).item()
     assert rel < 2e-2, rel
+
+
+@pytest.mark.parametrize("kind,tt", [("q4_k", G.GGML_Q4_K), ("q6_k", G.GGML_Q6_K), ("q8_0", G.GGML_Q8_0)])
+def test_gpu_quantiser_close_to_cpu(kind, tt):
+    from b200serve.models.gguf_gpu import to_quant_weight
+    rng = np.random.default_rng(3)
+    w = rng.normal(0, 0.02, (256, 1024)).astype(np.float32)
+    qw = to_quant_weight(torch.from_numpy(w).cuda(), kind)
+    cpu = G.dequantize(np.frombuffer(G.quantize(w, tt), dtype=np.uint8), tt, w.shape)
+    gpu = qw.dequantize().float().cpu().numpy()
+    # same quantiser on both sides; small differences from bf16 scale rounding
+    assert np.linalg.norm(gpu - cpu) / np.linalg.norm(w) < 0.03
+    assert np.linalg.norm(gpu - w) / np.linalg.norm(w) < {"q4_k": 0.15, "q6_k": 0.05, "q8_0": 0.02}[kind]
