@@ -248,6 +248,7 @@ __global__ void __launch_bounds__(192, 2)
     tc::prefetch_tmap(&tm_w);
     tc::prefetch_tmap(&tm_a);
   }
+  __syncwarp();
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
     tc::tmem_relinquish();
@@ -299,6 +300,7 @@ __global__ void __launch_bounds__(192, 2)
         }
       }
     }
+    __syncwarp();   // lanes 1..31 wait for the producer lane: the CTA barrier below is warp-aligned
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
@@ -342,6 +344,7 @@ __global__ void __launch_bounds__(192, 2)
       volatile int never = 0;
       tc::mbar_wait_bounded(mma_done, 0, &never, err, 5);
     }
+    __syncwarp();   // reconverge before the warp-aligned CTA barrier
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int quad = warp & 3;
@@ -393,10 +396,21 @@ __global__ void __launch_bounds__(192, 2)
             float v[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = 0.f;
-            for (int sp = 0; sp < p.splits; ++sp) {
-              const float* src = p.ws + ((size_t)sp * total_tiles + x.tile) * BN * 128 + (size_t)c0 * 128 + row;
+            // 4 splits per batch, 16 independent loads each: keeps ~64 L2 reads in flight per thread
+            for (int sp0 = 0; sp0 < p.splits; sp0 += 4) {
+              float t[4][16];
 #pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] += __ldcg(src + (size_t)j * 128);
+              for (int q = 0; q < 4; ++q) {
+                const int sp = sp0 + q;
+                const float* src = p.ws + ((size_t)min(sp, p.splits - 1) * total_tiles + x.tile) * BN * 128 +
+                                   (size_t)c0 * 128 + row;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) t[q][j] = sp < p.splits ? __ldcg(src + (size_t)j * 128) : 0.f;
+              }
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] += t[q][j];
             }
             epilogue_store<EPI>(p, v, row, x.n_tile, x.a_row0 + c0, t_end, xchg, quad, lane);
           }

@@ -21,6 +21,7 @@ namespace b200 {
 
 constexpr int kQWarps = 8;       // K chunks per CTA pass
 constexpr int kQChunk = 256;     // K per warp chunk = 16 MMA k-steps
+constexpr int kQStage = 2048;    // K columns of the activations staged in shared memory at a time
 
 __device__ __forceinline__ void qmma(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -74,20 +75,13 @@ __global__ void __launch_bounds__(kQWarps * 32) gguf_gemm_kernel(
     const uint32_t* __restrict__ codes, const uint32_t* __restrict__ smeta, const __nv_bfloat16* __restrict__ x,
     int M, int N, int K, int group, __nv_bfloat16* __restrict__ out, int ldo) {
   extern __shared__ __align__(16) uint8_t smem[];
-  const int LDX = K + 8;                                   // padded row: conflict-free B fragments
+  const int KC = min(K, kQStage);                          // K columns of x staged at a time
+  const int LDX = KC + 8;                                  // padded row: conflict-free B fragments
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem);   // [NB*8][LDX]
   float* red = reinterpret_cast<float*>(smem + (size_t)NB * 8 * LDX * 2);   // [warps][16][NB*8]
   pdl_wait();
   pdl_trigger();
   const int rows_tok = NB * 8;
-  for (int i = threadIdx.x; i < rows_tok * (K / 8); i += blockDim.x) {
-    const int r = i / (K / 8), c = (i % (K / 8)) * 8;
-    bf16x8 v;
-    if (r < M) v = *reinterpret_cast<const bf16x8*>(x + (size_t)r * K + c);
-    else v.w[0] = v.w[1] = v.w[2] = v.w[3] = 0u;
-    *reinterpret_cast<bf16x8*>(xs + (size_t)r * LDX + c) = v;
-  }
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
   const int slice = blockIdx.x;                            // 16 output rows
@@ -95,32 +89,74 @@ __global__ void __launch_bounds__(kQWarps * 32) gguf_gemm_kernel(
   float acc[NB][4];
 #pragma unroll
   for (int j = 0; j < NB; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-  for (int k0 = warp * kQChunk; k0 < K; k0 += kQWarps * kQChunk) {
-    const int ks0 = k0 / 16;
-#pragma unroll 4
-    for (int ks = 0; ks < kQChunk / 16; ++ks) {
-      const int kstep = ks0 + ks;
-      if (kstep >= ksteps) break;
-      uint32_t a[4];
+  // Each warp owns 256-wide K chunks. All codes and scales of a chunk are loaded into
+  // registers before any MMA, so a warp keeps ~1 KB of independent loads in flight.
+  constexpr int KS = kQChunk / 16;                           // 16 k-steps per chunk
+  for (int kc0 = 0; kc0 < K; kc0 += KC) {
+    const int kcn = min(KC, K - kc0);
+    if (kc0 > 0) __syncthreads();                              // previous x block fully consumed
+    for (int i = threadIdx.x; i < rows_tok * (kcn / 8); i += blockDim.x) {
+      const int r = i / (kcn / 8), c = (i % (kcn / 8)) * 8;
+      bf16x8 v;
+      if (r < M) v = *reinterpret_cast<const bf16x8*>(x + (size_t)r * K + kc0 + c);
+      else v.w[0] = v.w[1] = v.w[2] = v.w[3] = 0u;
+      *reinterpret_cast<bf16x8*>(xs + (size_t)r * LDX + c) = v;
+    }
+    __syncthreads();
+    for (int k0 = kc0 + warp * kQChunk; k0 < kc0 + kcn; k0 += kQWarps * kQChunk) {
+      const int ks0 = k0 / 16;
       if constexpr (BITS == 4) {
-        const uint32_t w = __ldg(codes + ((size_t)slice * ksteps + kstep) * 32 + lane);
-        const int sb = (kstep * 16) / 32;
-        const uint32_t* mp = smeta + ((size_t)slice * (K / 32) + sb) * 32;   // [16 rows][2] -> s, -m
-        const uint32_t smA = __ldg(mp + g * 2), mmA = __ldg(mp + g * 2 + 1);
-        const uint32_t smB = __ldg(mp + (g + 8) * 2), mmB = __ldg(mp + (g + 8) * 2 + 1);
-        dequant_u4(w, smA, mmA, smB, mmB, a);
-      } else {
-        const uint2 w = __ldg(reinterpret_cast<const uint2*>(codes) + ((size_t)slice * ksteps + kstep) * 32 + lane);
-        const int gi = (kstep * 16) / group;
-        const uint32_t* sp = smeta + ((size_t)slice * (K / group) + gi) * 16;
-        const uint32_t sA = __ldg(sp + g), sB = __ldg(sp + g + 8);
-        dequant_s8(w.x, w.y, sA, sB, a);
-      }
-      const int kk = kstep * 16 + 2 * t4;
+        uint32_t cw[KS];
+        uint32_t mt[KS / 2][4];                                // per 32-wide sub-block: sA, mA, sB, mB
 #pragma unroll
-      for (int j = 0; j < NB; ++j) {
-        const __nv_bfloat16* xr = xs + (size_t)(j * 8 + g) * LDX + kk;
-        qmma(acc[j], a, *reinterpret_cast<const uint32_t*>(xr), *reinterpret_cast<const uint32_t*>(xr + 8));
+        for (int ks = 0; ks < KS; ++ks) cw[ks] = __ldg(codes + ((size_t)slice * ksteps + ks0 + ks) * 32 + lane);
+#pragma unroll
+        for (int sb = 0; sb < KS / 2; ++sb) {
+          const uint32_t* mp = smeta + ((size_t)slice * (K / 32) + (ks0 / 2 + sb)) * 32;
+          mt[sb][0] = __ldg(mp + g * 2);
+          mt[sb][1] = __ldg(mp + g * 2 + 1);
+          mt[sb][2] = __ldg(mp + (g + 8) * 2);
+          mt[sb][3] = __ldg(mp + (g + 8) * 2 + 1);
+        }
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+          uint32_t a[4];
+          dequant_u4(cw[ks], mt[ks / 2][0], mt[ks / 2][1], mt[ks / 2][2], mt[ks / 2][3], a);
+          const int kk = (ks0 + ks) * 16 - kc0 + 2 * t4;
+#pragma unroll
+          for (int j = 0; j < NB; ++j) {
+            const __nv_bfloat16* xr = xs + (size_t)(j * 8 + g) * LDX + kk;
+            qmma(acc[j], a, *reinterpret_cast<const uint32_t*>(xr), *reinterpret_cast<const uint32_t*>(xr + 8));
+          }
+        }
+      } else {
+        uint2 cw[KS];
+        constexpr int GPC = kQChunk / 16;                      // max groups per chunk (group >= 16)
+        uint32_t sc[GPC][2];
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks)
+          cw[ks] = __ldg(reinterpret_cast<const uint2*>(codes) + ((size_t)slice * ksteps + ks0 + ks) * 32 + lane);
+        const int ngr = kQChunk / group;
+#pragma unroll
+        for (int gi = 0; gi < GPC; ++gi) {
+          if (gi < ngr) {
+            const uint32_t* sp = smeta + ((size_t)slice * (K / group) + (k0 / group + gi)) * 16;
+            sc[gi][0] = __ldg(sp + g);
+            sc[gi][1] = __ldg(sp + g + 8);
+          }
+        }
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+          uint32_t a[4];
+          const bool g16 = group == 16;                        // both indices are compile-time
+          dequant_s8(cw[ks].x, cw[ks].y, g16 ? sc[ks][0] : sc[ks / 2][0], g16 ? sc[ks][1] : sc[ks / 2][1], a);
+          const int kk = (ks0 + ks) * 16 - kc0 + 2 * t4;
+#pragma unroll
+          for (int j = 0; j < NB; ++j) {
+            const __nv_bfloat16* xr = xs + (size_t)(j * 8 + g) * LDX + kk;
+            qmma(acc[j], a, *reinterpret_cast<const uint32_t*>(xr), *reinterpret_cast<const uint32_t*>(xr + 8));
+          }
+        }
       }
     }
   }
@@ -154,9 +190,10 @@ void gguf_gemm(torch::Tensor x, torch::Tensor codes, torch::Tensor meta, int64_t
   const int M = x.size(0), K = x.size(1);
   TORCH_CHECK(M <= 32, "gguf_gemm handles decode batches up to 32 tokens");
   TORCH_CHECK(K % 256 == 0 && N % 16 == 0, "K must be a multiple of 256 and N of 16");
+  TORCH_CHECK(group == 16 || group == 32, "group must be 16 or 32");
   if (M == 0) return;
   const int NB = M <= 8 ? 1 : M <= 16 ? 2 : 4;
-  const size_t smem = (size_t)NB * 8 * (K + 8) * 2 + (size_t)kQWarps * 16 * NB * 8 * 4;
+  const size_t smem = (size_t)NB * 8 * (std::min<int>(K, kQStage) + 8) * 2 + (size_t)kQWarps * 16 * NB * 8 * 4;
   auto stream = at::cuda::getCurrentCUDAStream();
   const dim3 grid(N / 16), block(kQWarps * 32);
   auto cp = reinterpret_cast<const uint32_t*>(codes.data_ptr());

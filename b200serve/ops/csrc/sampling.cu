@@ -112,11 +112,6 @@ __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
   return c;
 }
 
-__device__ __forceinline__ uint32_t ordered_key(float f) {
-  const uint32_t b = __float_as_uint(f);
-  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
-
 struct SampleRow {
   float temperature, top_p, min_p;
   int top_k;
@@ -124,56 +119,264 @@ struct SampleRow {
   uint32_t step;
 };
 
-// Largest key K such that  sum over {key >= K} of weight  >= target  (weight = 1 for counts,
-// = exp((x - m) / t) for probability mass). Radix select over 4 digits of 8 bits.
-template <bool MASS>
-__device__ uint32_t radix_select_desc(const float* row, int V, uint32_t floor_key, float m, float inv_t,
-                                      float target, float* hist, float* sh) {
-  uint32_t prefix = 0, mask = 0;
-  float remaining = target;
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0.f;
-    __syncthreads();
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-      const float x = row[i];
-      const uint32_t key = ordered_key(x);
-      if (key >= floor_key && (key & mask) == prefix) {
-        const float wgt = MASS ? __expf((x - m) * inv_t) : 1.f;
-        atomicAdd(&hist[(key >> shift) & 255u], wgt);
-      }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float cum = 0.f;
-      int d = 255;
-      for (; d > 0; --d) {
-        if (cum + hist[d] >= remaining) break;
-        cum += hist[d];
-      }
-      sh[0] = remaining - cum;
-      sh[1] = __uint_as_float((uint32_t)d);
-    }
-    __syncthreads();
-    remaining = sh[0];
-    prefix |= __float_as_uint(sh[1]) << shift;
-    mask |= 255u << shift;
-    __syncthreads();
+// ---- filter thresholds in "distance" space -------------------------------------------------
+// Every filter keeps an upper set of the row: top-k the k largest logits, top-p the
+// largest ones up to a probability mass, min-p those with p >= min_p * p_max. With
+// d = (m - x) / t (m = row max, t = temperature) each is a threshold on d, and
+// exp(-d) is the unnormalised probability. Thresholds are found with histograms of d:
+// level 1 bins [0, R] into 256 equal bins; if the bins up to the boundary hold at most
+// kSCand tokens they are compacted and finished exactly (sort + prefix sums), else
+// the boundary bin is split again into 256 sub-bins (level 2, resolution R / 65536).
+// Tokens with d > 32 (probability below 1.3e-14 of the maximum) are excluded whenever
+// top-k or top-p is active.
+constexpr int kSThreads = 512, kSWarps = kSThreads / 32, kSBins = 256, kSCand = 4096;
+constexpr float kDFar = 32.f;
+
+struct DThr {          // keep d iff bin1(d) < b1, or bin1(d) == b1 and bin2(d) <= b2
+  float s1, lo2, s2;
+  int b1, b2;
+};
+struct DPred {
+  float dcap;          // min-p / far-tail cap: keep only d <= dcap
+  int n;
+  DThr t[3];
+};
+
+__device__ __forceinline__ int dbin1(float d, float s1) { return min((int)(d * s1), kSBins - 1); }
+__device__ __forceinline__ int dbin2(float d, float lo2, float s2) {
+  return max(0, min((int)((d - lo2) * s2), kSBins - 1));
+}
+__device__ __forceinline__ bool dkeep(float d, const DPred& p) {
+  if (!(d <= p.dcap)) return false;
+  for (int j = 0; j < p.n; ++j) {
+    const int b = dbin1(d, p.t[j].s1);
+    if (b > p.t[j].b1) return false;
+    if (b == p.t[j].b1 && p.t[j].b2 < kSBins - 1 && dbin2(d, p.t[j].lo2, p.t[j].s2) > p.t[j].b2) return false;
   }
-  return prefix;
+  return true;
 }
 
-__global__ void __launch_bounds__(1024) sample_rows_kernel(float* __restrict__ logits, int V, int ld,
-                                                           const SampleRow* __restrict__ params,
-                                                           const int* __restrict__ pen_ids,
-                                                           const float* __restrict__ pen_counts, int P,
-                                                           const float* __restrict__ pen_vals,
-                                                           int* __restrict__ out) {
-  __shared__ float hist[256];
-  __shared__ float red[32];
-  __shared__ float sh[4];
-  __shared__ int shi[32];
+struct SampShared {
+  union {
+    struct { uint32_t cnt[kSWarps][kSBins]; float mass[kSWarps][kSBins]; } h;   // per-warp histograms
+    struct { float v[kSCand]; int i[kSCand]; } c;                                 // compacted candidates
+  } u;
+  uint32_t tot_cnt[kSBins];
+  float tot_mass[kSBins];
+  float red[32];
+  int redi[32];
+  float wmin[32];
+  float f[4];
+  int n[4];
+};
+
+// Calls f(x, i) for every element of the row (float4 loads when aligned).
+template <class F>
+__device__ __forceinline__ void for_row(const float* row, int V, bool vec, F&& f) {
+  const int V4 = vec ? V / 4 : 0;
+  for (int q = threadIdx.x; q < V4; q += blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(row)[q];
+    f(v.x, 4 * q);
+    f(v.y, 4 * q + 1);
+    f(v.z, 4 * q + 2);
+    f(v.w, 4 * q + 3);
+  }
+  for (int i = V4 * 4 + threadIdx.x; i < V; i += blockDim.x) f(row[i], i);
+}
+
+// Histogram of the surviving tokens' d: level 1 (bsel < 0) over bin1 with scale s1, level 2
+// over the sub-bins of bin1 == bsel. Counts are aggregated per warp (match_any), masses use
+// per-warp shared atomics. Leaves totals in S.tot_cnt / S.tot_mass.
+__device__ void d_histogram(const float* row, int V, bool vec, float m, float inv_t, const DPred& P, float s1,
+                            int bsel, float lo2, float s2, SampShared& S) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kSWarps * kSBins; i += blockDim.x) {
+    (&S.u.h.cnt[0][0])[i] = 0u;
+    (&S.u.h.mass[0][0])[i] = 0.f;
+  }
+  __syncthreads();
+  uint32_t* cnt = S.u.h.cnt[warp];
+  float* mass = S.u.h.mass[warp];
+  for_row(row, V, vec, [&](float x, int) {
+    const float d = (m - x) * inv_t;
+    int b = -1;
+    if (dkeep(d, P)) {
+      b = dbin1(d, s1);
+      if (bsel >= 0) b = (b == bsel) ? dbin2(d, lo2, s2) : -1;
+    }
+    const unsigned act = __activemask();
+    const unsigned grp = __match_any_sync(act, b);
+    if (b >= 0) {
+      if (lane == __ffs(grp) - 1) atomicAdd(&cnt[b], (uint32_t)__popc(grp));
+      atomicAdd(&mass[b], __expf(-d));
+    }
+  });
+  __syncthreads();
+  for (int b = threadIdx.x; b < kSBins; b += blockDim.x) {
+    uint32_t c = 0;
+    float w = 0.f;
+#pragma unroll
+    for (int k = 0; k < kSWarps; ++k) {
+      c += S.u.h.cnt[k][b];
+      w += S.u.h.mass[k][b];
+    }
+    S.tot_cnt[b] = c;
+    S.tot_mass[b] = w;
+  }
+  __syncthreads();
+}
+
+// Warp 0: first bin whose inclusive cumulative count (MASS: mass) reaches the target, which is
+// frac * total when frac >= 0, else `target`. Writes S.n[0] = bin (kSBins if never reached),
+// S.f[0] = cumulative before the bin, S.n[1] = tokens through the bin, S.f[2] = the target.
+template <bool MASS>
+__device__ void d_find(float target, float frac, SampShared& S) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    float w[8], c[8];
+    float ws = 0.f, cs = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      c[k] = (float)S.tot_cnt[lane * 8 + k];
+      w[k] = MASS ? S.tot_mass[lane * 8 + k] : c[k];
+      ws += w[k];
+      cs += c[k];
+    }
+    float wi = ws, ci = cs;   // inclusive scans over lanes
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float a = __shfl_up_sync(0xffffffffu, wi, o), b = __shfl_up_sync(0xffffffffu, ci, o);
+      if (lane >= o) { wi += a; ci += b; }
+    }
+    const float total_w = __shfl_sync(0xffffffffu, wi, 31), total_c = __shfl_sync(0xffffffffu, ci, 31);
+    const float tgt = frac >= 0.f ? frac * total_w : target;
+    const unsigned hit = __ballot_sync(0xffffffffu, wi >= tgt);
+    const int L = hit ? __ffs(hit) - 1 : -1;
+    if (lane == 0 && !hit) { S.n[0] = kSBins; S.f[0] = total_w; S.n[1] = (int)total_c; }
+    if (lane == L) {
+      float cum = wi - ws, cc = ci - cs;
+      int bin = lane * 8 + 7;
+      for (int k = 0; k < 8; ++k) {
+        cc += c[k];
+        if (cum + w[k] >= tgt) { bin = lane * 8 + k; break; }
+        cum += w[k];
+      }
+      S.n[0] = bin;
+      S.f[0] = cum;
+      S.n[1] = (int)cc;
+    }
+    if (lane == 0) S.f[2] = tgt;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void block_best(float& bv, int& bi, SampShared& S) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    better(bv, bi, ov, oi);
+  }
+  __syncthreads();
+  if (lane == 0) { S.red[warp] = bv; S.redi[warp] = bi; }
+  __syncthreads();
+  bv = lane < nw ? S.red[lane] : -INFINITY;
+  bi = lane < nw ? S.redi[lane] : 0x7fffffff;
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    better(bv, bi, ov, oi);
+  }
+}
+
+__device__ __forceinline__ float gumbel(int i, uint32_t step, uint32_t row, uint2 key) {
+  const uint4 r = philox4x32_10(make_uint4((uint32_t)i, step, row, 0x5A4D504Cu), key);
+  const float u = ((float)(r.x >> 8) + 0.5f) * (1.f / 16777216.f);
+  return -__logf(-__logf(u));
+}
+
+// Sorted (descending value, ascending index) candidates: exact top-k, then exact top-p
+// (keep j while the mass before it is <= target; target = top_p * mass of the top-k
+// survivors when mass_target < 0), then the Gumbel-max draw. Returns the vocabulary id.
+__device__ int finish_candidates(int n, int top_k, float top_p, float mass_target, float m, float inv_t,
+                                 uint32_t step, uint2 key, SampShared& S) {
+  int N2 = 32;
+  while (N2 < n) N2 <<= 1;
+  for (int i = n + threadIdx.x; i < N2; i += blockDim.x) { S.u.c.v[i] = -INFINITY; S.u.c.i[i] = 0x7fffffff; }
+  __syncthreads();
+  for (int k = 2; k <= N2; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int t = threadIdx.x; t < N2; t += blockDim.x) {
+        const int u = t ^ j;
+        if (u > t) {
+          const float vt = S.u.c.v[t], vu = S.u.c.v[u];
+          const int it = S.u.c.i[t], iu = S.u.c.i[u];
+          const bool u_first = vu > vt || (vu == vt && iu < it);
+          if (((t & k) == 0) == u_first) {
+            S.u.c.v[t] = vu; S.u.c.v[u] = vt;
+            S.u.c.i[t] = iu; S.u.c.i[u] = it;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  int keep = n;
+  if (top_k > 0 && top_k < n) {
+    const float vk = S.u.c.v[top_k - 1];
+    keep = top_k;
+    while (keep < n && S.u.c.v[keep] == vk) ++keep;   // ties at the boundary stay
+  }
+  if (top_p < 1.f && keep > 1) {
+    // chunked block scan of the weights over [0, keep)
+    const int per = (keep + blockDim.x - 1) / blockDim.x;
+    const int j0 = min(keep, (int)threadIdx.x * per), j1 = min(keep, j0 + per);
+    float loc = 0.f;
+    for (int j = j0; j < j1; ++j) loc += __expf((S.u.c.v[j] - m) * inv_t);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    float inc = loc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float a = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += a;
+    }
+    if (lane == 31) S.red[warp] = inc;
+    if (threadIdx.x == 0) S.n[2] = keep;
+    __syncthreads();
+    float wbase = 0.f, total = 0.f;
+    for (int w = 0; w < nw; ++w) {
+      if (w < warp) wbase += S.red[w];
+      total += S.red[w];
+    }
+    const float tgt = mass_target >= 0.f ? mass_target : top_p * total;
+    float before = wbase + inc - loc;
+    for (int j = j0; j < j1; ++j) {
+      if (before > tgt) { atomicMin(&S.n[2], j); break; }
+      before += __expf((S.u.c.v[j] - m) * inv_t);
+    }
+    __syncthreads();
+    keep = max(1, S.n[2]);
+    __syncthreads();
+  }
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int j = threadIdx.x; j < keep; j += blockDim.x) {
+    const int id = S.u.c.i[j];
+    better(bv, bi, S.u.c.v[j] * inv_t + gumbel(id, step, blockIdx.x, key), id);
+  }
+  block_best(bv, bi, S);
+  return bi;
+}
+
+__global__ void __launch_bounds__(kSThreads) sample_rows_kernel(float* __restrict__ logits, int V, int ld,
+                                                                const SampleRow* __restrict__ params,
+                                                                const int* __restrict__ pen_ids,
+                                                                const float* __restrict__ pen_counts, int P,
+                                                                const float* __restrict__ pen_vals,
+                                                                int* __restrict__ out) {
+  __shared__ SampShared S;
   float* row = logits + (size_t)blockIdx.x * ld;
+  const bool vec = ((reinterpret_cast<uintptr_t>(row) & 15) == 0) && (ld & 3) == 0;
   const SampleRow pr = params[blockIdx.x];
   // ---- penalties (ids unique per row): repetition, presence, frequency ----
   if (P > 0) {
@@ -189,86 +392,104 @@ __global__ void __launch_bounds__(1024) sample_rows_kernel(float* __restrict__ l
     }
     __syncthreads();
   }
-  // ---- row max (also the greedy answer) ----
-  float bv = -INFINITY;
+  // ---- row max (the greedy answer) and min ----
+  float bv = -INFINITY, mn = INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) better(bv, bi, row[i], i);
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    better(bv, bi, ov, oi);
-  }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  if (lane == 0) { red[warp] = bv; shi[warp] = bi; }
+  for_row(row, V, vec, [&](float x, int i) { better(bv, bi, x, i); mn = fminf(mn, x); });
+  mn = -warp_max(-mn);
+  if ((threadIdx.x & 31) == 0) S.wmin[threadIdx.x >> 5] = mn;
+  block_best(bv, bi, S);
+  if (threadIdx.x == 0) { S.f[0] = bv; S.n[0] = bi; }
   __syncthreads();
-  if (warp == 0) {
-    bv = lane < nw ? red[lane] : -INFINITY;
-    bi = lane < nw ? shi[lane] : 0x7fffffff;
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      better(bv, bi, ov, oi);
-    }
-    if (lane == 0) { sh[2] = bv; shi[0] = bi; }
-  }
+  const float m = S.f[0];
+  const int greedy = S.n[0];
+  float xmin = INFINITY;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) xmin = fminf(xmin, S.wmin[w]);
   __syncthreads();
-  const float m = sh[2];
   if (!(pr.temperature > 0.f)) {
-    if (threadIdx.x == 0) out[blockIdx.x] = shi[0];
+    if (threadIdx.x == 0) out[blockIdx.x] = greedy;
     return;
   }
-  __syncthreads();
   const float inv_t = 1.f / pr.temperature;
-  // ---- top-k threshold ----
-  uint32_t floor_key = 0;
-  if (pr.top_k > 0 && pr.top_k < V)
-    floor_key = radix_select_desc<false>(row, V, 0, m, inv_t, (float)pr.top_k, hist, sh);
-  // ---- min-p: keep p >= min_p * p_max  <=>  x >= m + t * ln(min_p) ----
-  if (pr.min_p > 0.f) {
-    const uint32_t k2 = ordered_key(m + pr.temperature * __logf(pr.min_p));
-    floor_key = max(floor_key, k2);
-  }
-  // ---- top-p over the survivors ----
-  if (pr.top_p < 1.f) {
-    float z = 0.f;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-      const float x = row[i];
-      if (ordered_key(x) >= floor_key) z += __expf((x - m) * inv_t);
-    }
-    z = block_sum(z, red);
-    const uint32_t kp = radix_select_desc<true>(row, V, floor_key, m, inv_t, pr.top_p * z, hist, sh);
-    floor_key = max(floor_key, kp);
-  }
-  // ---- Gumbel-max draw over kept tokens ----
-  float best = -INFINITY;
-  int best_i = 0x7fffffff;
   const uint2 key = make_uint2((uint32_t)pr.seed, (uint32_t)(pr.seed >> 32));
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float x = row[i];
-    if (ordered_key(x) < floor_key) continue;
-    const uint4 r = philox4x32_10(make_uint4((uint32_t)i, pr.step, blockIdx.x, 0x5A4D504Cu), key);
-    const float u = ((float)(r.x >> 8) + 0.5f) * (1.f / 16777216.f);
-    const float g = -__logf(-__logf(u));
-    better(best, best_i, x * inv_t + g, i);
-  }
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-    better(best, best_i, ov, oi);
-  }
-  __syncthreads();
-  if (lane == 0) { red[warp] = best; shi[warp] = best_i; }
-  __syncthreads();
-  if (warp == 0) {
-    best = lane < nw ? red[lane] : -INFINITY;
-    best_i = lane < nw ? shi[lane] : 0x7fffffff;
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-      better(best, best_i, ov, oi);
+  const bool use_k = pr.top_k > 0 && pr.top_k < V, use_p = pr.top_p < 1.f;
+  DPred Pd;
+  Pd.n = 0;
+  Pd.dcap = pr.min_p > 0.f ? -__logf(pr.min_p) : INFINITY;
+  int result = -1;
+  if (use_k || use_p) {
+    Pd.dcap = fminf(Pd.dcap, kDFar);
+    float R = fminf((m - xmin) * inv_t, Pd.dcap);
+    if (!(R > 0.f)) R = 1.f;
+    int exact_k = 0;
+    float mass_target = -1.f;
+    bool cand = false;
+    for (int stage = 0; stage < 2 && !cand; ++stage) {
+      const bool mass = stage == 1;
+      if (mass ? !use_p : !use_k) continue;
+      const float s1 = (float)kSBins / R;
+      d_histogram(row, V, vec, m, inv_t, Pd, s1, -1, 0.f, 0.f, S);
+      if (mass) d_find<true>(0.f, pr.top_p, S);
+      else d_find<false>((float)pr.top_k, -1.f, S);
+      const int b1 = S.n[0];
+      const float before1 = S.f[0], tgt = S.f[2];
+      const int through = S.n[1];
+      __syncthreads();
+      if (b1 >= kSBins) continue;                       // filter keeps every survivor
+      DThr t{s1, 0.f, 0.f, b1, kSBins - 1};
+      if (through <= kSCand) {
+        Pd.t[Pd.n++] = t;
+        cand = true;
+        if (!mass) exact_k = pr.top_k;
+        else mass_target = tgt;
+        break;
+      }
+      const float lo2 = (float)b1 / s1, s2 = s1 * (float)kSBins;
+      d_histogram(row, V, vec, m, inv_t, Pd, s1, b1, lo2, s2, S);
+      if (mass) d_find<true>(tgt - before1, -1.f, S);   // the mass still needed inside bin b1
+      else d_find<false>((float)pr.top_k - before1, -1.f, S);
+      t.lo2 = lo2;
+      t.s2 = s2;
+      t.b2 = min(S.n[0], kSBins - 1);
+      Pd.t[Pd.n++] = t;
+      R = ((float)b1 + (float)(t.b2 + 1) / (float)kSBins) / s1;
+      __syncthreads();
     }
-    if (lane == 0) out[blockIdx.x] = best_i == 0x7fffffff ? shi[0] : best_i;
+    if (cand) {
+      if (threadIdx.x == 0) S.n[2] = 0;
+      __syncthreads();
+      const int lane = threadIdx.x & 31;
+      for_row(row, V, vec, [&](float x, int i) {
+        const bool k = dkeep((m - x) * inv_t, Pd);
+        const unsigned act = __activemask();
+        const unsigned bal = __ballot_sync(act, k);
+        const int leader = __ffs(act) - 1;
+        int base = 0;
+        if (lane == leader && bal) base = atomicAdd(&S.n[2], __popc(bal));
+        base = __shfl_sync(act, base, leader);
+        if (k) {
+          const int slot = base + __popc(bal & ((1u << lane) - 1u));
+          if (slot < kSCand) { S.u.c.v[slot] = x; S.u.c.i[slot] = i; }
+        }
+      });
+      __syncthreads();
+      const int n = min(S.n[2], kSCand);
+      __syncthreads();
+      result = finish_candidates(n, exact_k, use_p ? pr.top_p : 1.f, mass_target, m, inv_t, pr.step, key, S);
+    }
   }
+  if (result < 0) {
+    // ---- Gumbel-max draw over every surviving token ----
+    float best = -INFINITY;
+    int best_i = 0x7fffffff;
+    for_row(row, V, vec, [&](float x, int i) {
+      if (!dkeep((m - x) * inv_t, Pd)) return;
+      better(best, best_i, x * inv_t + gumbel(i, pr.step, blockIdx.x, key), i);
+    });
+    block_best(best, best_i, S);
+    result = best_i;
+  }
+  if (threadIdx.x == 0) out[blockIdx.x] = result == 0x7fffffff ? greedy : result;
 }
 
 }  // namespace b200
@@ -283,7 +504,7 @@ void sample_rows(torch::Tensor logits, torch::Tensor params, torch::Tensor pen_i
   const int B = logits.size(0), V = logits.size(1);
   if (B == 0) return;
   const int P = pen_ids.numel() ? pen_ids.size(1) : 0;
-  b200::sample_rows_kernel<<<B, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
+  b200::sample_rows_kernel<<<B, b200::kSThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       logits.data_ptr<float>(), V, logits.stride(0), reinterpret_cast<const b200::SampleRow*>(params.data_ptr()),
       P ? pen_ids.data_ptr<int>() : nullptr, P ? pen_counts.data_ptr<float>() : nullptr, P,
       P ? pen_vals.data_ptr<float>() : nullptr, out.data_ptr<int>());

@@ -173,6 +173,9 @@ def gemm_trace(M=32, N=4096, K=4096):
         col = col[t[:, i] > 0] if (t[:, i] > 0).any() else col
         out[n] = {"min": round(col.min().item(), 2), "med": round(col.median().item(), 2),
                   "max": round(col.max().item(), 2)}
+    # per-CTA ordering checks: the exit stamp is taken after the final CTA barrier
+    out["exit_before_epi"] = int((t[:, 6] < t[:, 5]).sum())
+    out["exit_before_mma"] = int((t[:, 6] < t[:, 4]).sum())
     print(json.dumps(out))
 
 

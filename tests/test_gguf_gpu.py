@@ -45,6 +45,19 @@ def test_gguf_gemm(tt, M):
     assert rel < 2e-2, rel
 
 
+@pytest.mark.parametrize("tt", [G.GGML_Q4_K, G.GGML_Q6_K])
+@pytest.mark.parametrize("M,K", [(32, 4608), (24, 12288)])
+def test_gguf_gemm_long_k(tt, M, K):
+    """K beyond one staged activation block (2048 columns), with a partial last block."""
+    N = 256
+    qw, deq = _quant_weight(tt, N, K, seed=1)
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    y = ops.linear(x, qw)
+    ref = x.float().cpu() @ deq.t()
+    rel = ((y.float().cpu() - ref).norm() / ref.norm()).item()
+    assert rel < 2e-2, rel
+
+
 @pytest.mark.parametrize("kind,tt", [("q4_k", G.GGML_Q4_K), ("q6_k", G.GGML_Q6_K), ("q8_0", G.GGML_Q8_0)])
 def test_gpu_quantiser_close_to_cpu(kind, tt):
     from b200serve.models.gguf_gpu import to_quant_weight

@@ -227,6 +227,56 @@ def test_sampler_distribution_and_seed():
     assert torch.equal(again, draws[:50])
 
 
+def _filtered_probs(row, t, k, p, minp):
+    """fp32 oracle of the filter chain: temperature, top-k, min-p, top-p, renormalise."""
+    probs = torch.softmax(row.float() / t, -1)
+    if k:
+        kth = probs.topk(k).values[-1]
+        probs = torch.where(probs >= kth, probs, torch.zeros_like(probs))
+    if minp:
+        probs = torch.where(probs >= probs.max() * minp, probs, torch.zeros_like(probs))
+    if p < 1.0:
+        sp, si = (probs / probs.sum()).sort(descending=True)
+        drop = (sp.cumsum(0) - sp) > p
+        keep = torch.zeros_like(probs, dtype=torch.bool)
+        keep[si[~drop]] = True
+        probs = torch.where(keep, probs, torch.zeros_like(probs))
+    return probs / probs.sum()
+
+
+@pytest.mark.parametrize("t,k,p,minp", [(0.8, 10, 0.8, 0.0), (1.0, 0, 0.7, 0.0), (1.3, 20, 1.0, 0.05)])
+def test_sampler_filtered_distribution(t, k, p, minp):
+    V, n = 96, 4000
+    torch.manual_seed(3)
+    logits = torch.randn(1, V, device=dev) * 2
+    draws = torch.cat([ops.sample_rows(logits.clone(), [t], [k], [p], [minp], [5], [s]) for s in range(n)])
+    want = _filtered_probs(logits[0], t, k, p, minp)
+    freq = torch.bincount(draws.long(), minlength=V).float() / n
+    assert set(draws.tolist()) <= set(want.nonzero().view(-1).tolist())
+    assert (freq - want).abs().max().item() < 0.04
+
+
+def test_sampler_wide_candidate_sets():
+    """Filters whose kept set exceeds the exact-path capacity take the two-level histogram path."""
+    V = 151936
+    torch.manual_seed(4)
+    logits = torch.randn(2, V, device=dev) * 0.5          # flat: the nucleus holds most of the vocabulary
+    # top-k larger than the candidate capacity: draws stay inside the k largest (+ level-2 slack)
+    k = 9000
+    draws = _sample_many(logits, 16, t=1.0, k=k)
+    for b in range(2):
+        rank = (logits[b].unsqueeze(0) > logits[b, draws[:, b].long()].unsqueeze(1)).sum(1)
+        assert int(rank.max()) < k + 64
+    # top-p over a flat row: draws are inside the nucleus up to the level-2 resolution
+    p = 0.3
+    draws = _sample_many(logits, 16, t=1.0, p=p)
+    probs = torch.softmax(logits.double(), -1)
+    for b in range(2):
+        sp, _ = probs[b].sort(descending=True)
+        cut = sp[int((sp.cumsum(0) < p).sum().item())]
+        assert bool((probs[b, draws[:, b].long()] >= cut * (1 - 1e-3)).all())
+
+
 def test_sampler_penalties():
     V = 100
     logits = torch.zeros(1, V, device=dev)
