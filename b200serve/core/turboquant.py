@@ -14,10 +14,11 @@ Codec (per head vector x of dimension d, a power of two):
    alpha = 1 / sqrt(1 + (pi/2)(d-1)/d).
 Decoding is H(u_hat [+ QJL term]) * n.
 
-The engine's paged KV formats and the fused attention kernels
-(ops/csrc/kv_quant.cu) compute scores in the rotated domain instead of
-decoding: q.k = n * (H q).(u_hat + gamma * S^T s) with gamma folded at
-encode time, so no per-key inverse transform is needed.
+The engine's paged TurboQuant KV format and its kernels
+(ops/csrc/kv_turboquant.cu, ops/csrc/attention_decode_tc.cu) compute scores in
+the rotated domain instead of decoding: q.k = n * ((H q).u_hat + gamma * (S H q).s)
+with gamma = alpha ||r|| / ||S^T s|| folded at encode time, so no per-key
+inverse transform is needed.
 """
 
 from __future__ import annotations

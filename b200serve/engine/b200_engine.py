@@ -93,7 +93,7 @@ class B200Engine(BaseEngine):
         nkv_local = max(1, mc.num_kv_heads // tp)
         num_blocks = self._size_kv(mc, nkv_local, dtype, dev)
         self.kv = KVCache(mc.num_layers, num_blocks, nkv_local, mc.head_dim, dtype=dtype, device=dev,
-                          kv_format=cfgE.kv_format)
+                          kv_format=cfgE.kv_format, key_bits=cfgE.kv_key_bits, value_bits=cfgE.kv_value_bits)
         from b200serve.engine.runner import ModelRunner
         runner = ModelRunner(mc, self.weights, self.kv, comm=self.comm, device=dev, max_batch=cfgE.max_batch,
                              max_seq=cfgE.max_seq, use_graphs=cfgE.cuda_graphs)

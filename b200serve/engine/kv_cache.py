@@ -22,17 +22,30 @@ class KVCache:
     """Paged K/V storage. ``bf16``: k, v [layers, blocks, kv_heads, 16, head_dim].
     ``int4g128``: k, v hold 4-bit codes [layers, blocks, kv_heads, 16, head_dim/2] (uint8,
     interleaved nibbles per 8 dims) and k_scale, v_scale one fp16 per (token, head)
-    [layers, blocks, kv_heads, 16]: 4-bit K/V with an fp16 scale per group of 128 values."""
+    [layers, blocks, kv_heads, 16]: 4-bit K/V with an fp16 scale per group of 128 values.
+    ``turboquant``: k, v hold one TurboQuant code (``key_bits`` / ``value_bits``) per dim as a
+    nibble [layers, blocks, kv_heads, 16, head_dim/2] (byte m = dims 2m | 2m+1 << 4); k_sign the
+    QJL sign bits [.., head_dim/8]; k_scale (norm, gamma) fp16 [.., 2]; v_scale the V norm."""
 
     def __init__(self, num_layers, num_blocks, kv_heads, head_dim, dtype=torch.bfloat16, device="cpu",
-                 kv_format="bf16"):
+                 kv_format="bf16", key_bits=4, value_bits=4):
         self.num_layers = num_layers
         self.num_blocks = num_blocks
         self.kv_heads = kv_heads
         self.head_dim = head_dim
         self.kv_format = kv_format
-        self.k_scale = self.v_scale = None
-        if kv_format == "int4g128":
+        self.key_bits, self.value_bits = key_bits, value_bits
+        self.k_scale = self.v_scale = self.k_sign = None
+        if kv_format == "turboquant":
+            if head_dim != 128:
+                raise ValueError("turboquant KV needs head_dim 128")
+            base = (num_layers, num_blocks, kv_heads, BLOCK)
+            self.k = torch.zeros(base + (head_dim // 2,), dtype=torch.uint8, device=device)
+            self.v = torch.zeros(base + (head_dim // 2,), dtype=torch.uint8, device=device)
+            self.k_sign = torch.zeros(base + (head_dim // 8,), dtype=torch.uint8, device=device)
+            self.k_scale = torch.zeros(base + (2,), dtype=torch.float16, device=device)
+            self.v_scale = torch.zeros(base, dtype=torch.float16, device=device)
+        elif kv_format == "int4g128":
             if head_dim != 128:
                 raise ValueError("int4g128 KV needs head_dim 128")
             shape = (num_layers, num_blocks, kv_heads, BLOCK, head_dim // 2)
@@ -48,6 +61,9 @@ class KVCache:
 
     @staticmethod
     def bytes_per_block(num_layers, kv_heads, head_dim, elem_bytes=2, kv_format="bf16") -> int:
+        if kv_format == "turboquant":
+            # codes (4 bits per dim) for K and V, K sign bits, K (norm, gamma), V norm
+            return num_layers * kv_heads * BLOCK * (head_dim + head_dim // 8 + 6)
         if kv_format == "int4g128":
             return 2 * num_layers * kv_heads * BLOCK * (head_dim // 2 + 2)
         return 2 * num_layers * kv_heads * BLOCK * head_dim * elem_bytes

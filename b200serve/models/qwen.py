@@ -79,6 +79,13 @@ class Decoder:
         self.cos_sin = ops.rope_cos_sin(cfg.head_dim, cfg.max_position, cfg.rope_theta, self.device)
         self.attn_ws = None
         self.moe = None
+        self.tq = None
+        want_rot = getattr(kv_cache, "kv_format", "bf16") == "turboquant"
+        if want_rot:
+            self.tq = ops.TurboQuantTables(kv_cache.key_bits, kv_cache.value_bits, self.device)
+        if want_rot != getattr(weights, "o_rotated", False):
+            self._rotate_o()
+            weights.o_rotated = want_rot
         if self.device.type == "cuda":
             self.pack_weights()
         if cfg.is_moe:
@@ -99,6 +106,52 @@ class Decoder:
             w.lm_head = ops.pack_weight(w.lm_head.clone())
         if self.device.type == "cuda":
             torch.cuda.empty_cache()
+
+    def _rotate_o(self):
+        """TurboQuant KV keeps V in the rotated domain (attention returns H o per head), so the
+        o_proj weight absorbs the transform: W_o' = W_o blockdiag(H) (H symmetric, orthonormal).
+        H is an involution, so the same call undoes it when the weights go back to a plain KV
+        format; ``weights.o_rotated`` records the current state."""
+        for lw in self.w.layers:
+            if not isinstance(lw.o, torch.Tensor):
+                raise NotImplementedError("turboquant KV needs a dense (bf16/fp32) o_proj weight")
+            o = lw.o
+            H_out, K_in = o.shape
+            blocks = o.float().reshape(H_out, K_in // self.hd, self.hd)
+            lw.o = ops._fwht(blocks).reshape(H_out, K_in).to(o.dtype).contiguous()
+
+    def _attention_tq(self, i, qkv, lw, fb, T, tps, nsplit, ws, pre):
+        """Attention over the TurboQuant cache: the new K/V rows are staged in bf16 pages, encoded
+        into the cache together with the query rotation, then decode attention scores the codes
+        directly; prefill attends over the batch's pages dequantised into ``pre``."""
+        kv, tb = self.kv, self.tq
+        eps = self.cfg.rms_eps
+        nblk = (T + 15) // 16
+        kst = torch.empty(nblk, self.nkv, 16, self.hd, dtype=qkv.dtype, device=qkv.device)
+        vst = torch.empty_like(kst)
+        stage_slots = torch.arange(T, dtype=torch.int32, device=qkv.device)
+        q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, stage_slots, kst, vst,
+                         self.nq, self.nkv, eps)
+        q_rot, q_jl = ops.tq_qkv(q, kst, vst, fb.slots, tb, kv, i)
+        if fb.is_decode:
+            return ops.tq_decode_attention(q_rot, q_jl, kv, i, tb, fb.block_tables, fb.seq_lens, self.scale, tps,
+                                           nsplit, ws)
+        ids, tables, kd, vd = pre
+        ops.tq_dequant(ids, kv, i, tb, kd, vd)
+        return ops.paged_prefill_attention(q_rot, kd, vd, tables, fb.seq_lens, fb.q_start, fb.cu_q, self.scale,
+                                           max_q=fb.max_q)
+
+    def _tq_prefill_pages(self, fb):
+        """Unique pages of the prefill batch, tables remapped onto them, and bf16 scratch pages."""
+        bt = fb.block_tables
+        flat = bt.reshape(-1)
+        ids = torch.unique(flat[flat >= 0]).to(torch.int32)
+        remap = torch.searchsorted(ids.long(), bt.long().clamp_min(0)).to(torch.int32)
+        tables = torch.where(bt >= 0, remap, bt)
+        n = max(1, ids.numel())
+        kd = torch.empty(n, self.nkv, 16, self.hd, dtype=torch.bfloat16 if bt.is_cuda else torch.float32,
+                         device=bt.device)
+        return ids, tables.contiguous(), kd, torch.empty_like(kd)
 
     # -------------------------------------------------------------- helpers
     def decode_attn_plan(self, batch: int, max_seq: int):
@@ -183,12 +236,16 @@ class Decoder:
             tps, nsplit = attn_plan or self.decode_attn_plan(T, int(fb.block_tables.shape[1]) * 16)
             ws = self.ensure_attn_workspace(T, nsplit) if nsplit > 1 else None
         k_all, v_all = self.kv.k, self.kv.v
+        tq_pre = self._tq_prefill_pages(fb) if (self.tq is not None and not fb.is_decode) else None
         for i, lw in enumerate(w.layers):
             if i > 0:
                 x = ops.rmsnorm(mlp_parts, lw.input_norm, eps, residual=residual, residual_out=residual)
             qkv = ops.linear(x, lw.qkv, bias=lw.qkv_bias)
             kc, vc = k_all[i], v_all[i]
-            if self.kv.kv_format == "int4g128":
+            if self.tq is not None:
+                attn = self._attention_tq(i, qkv, lw, fb, T, tps if fb.is_decode else 0,
+                                          nsplit if fb.is_decode else 0, ws if fb.is_decode else None, tq_pre)
+            elif self.kv.kv_format == "int4g128":
                 attn = self._attention_q4(i, qkv, lw, fb, T, tps if fb.is_decode else 0,
                                           nsplit if fb.is_decode else 0, ws if fb.is_decode else None)
             else:

@@ -76,6 +76,7 @@ class ModelWeights:
     tp_size: int = 1
     ep_rank: int = 0
     ep_size: int = 1
+    o_rotated: bool = False            # o_proj columns carry the TurboQuant per-head transform
 
     def nbytes(self) -> int:
         n = 0

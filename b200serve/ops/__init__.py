@@ -556,6 +556,165 @@ def q4_dequantize_rows(codes: torch.Tensor, scale: torch.Tensor) -> torch.Tensor
     return q * scale.float()[..., None]
 
 
+# ------------------------------------------------------------------ TurboQuant paged KV
+class TurboQuantTables:
+    """Constants of the paged TurboQuant KV format (head_dim 128) for one (key_bits, value_bits)
+    pair: the JL matrix S (seed 137), Lloyd-Max centroids and thresholds, the value of each 4-bit
+    code (sign and 1/sqrt(d) folded in), and the QJL shrinkage alpha. Codec semantics follow the
+    reference core/turboquant_cache.py:41-200 (restated in b200serve/core/turboquant.py)."""
+
+    D = 128
+
+    def __init__(self, key_bits: int, value_bits: int, device):
+        from b200serve.core.turboquant import CODEBOOK, jl_matrix
+        d = self.D
+        self.key_bits, self.value_bits = int(key_bits), int(value_bits)
+        self.device = torch.device(device)
+        self.S = jl_matrix(d).to(self.device).contiguous()
+        self.alpha = 1.0 / math.sqrt(1.0 + (math.pi / 2.0) * (d - 1) / d)
+        cents, thr, vals = [], [], []
+        for b in (self.key_bits, self.value_bits):
+            cb = CODEBOOK[b]
+            c = list(cb["centroids"])
+            t = list(cb["thresholds"])
+            cents.append(c + [0.0] * (8 - len(c)))
+            thr.append(t + [0.0] * (8 - len(t)))
+            lev = len(c)
+            v = [0.0] * 16
+            for i in range(2 * lev):
+                v[i] = (c[i] if i < lev else -c[i - lev]) / math.sqrt(d)
+            vals.append(v)
+        self.cents = torch.tensor(cents, dtype=torch.float32, device=self.device)
+        self.thr_host = torch.tensor(thr, dtype=torch.float32)
+        self.code_vals_host = torch.tensor(vals, dtype=torch.float32)
+        self.code_vals = self.code_vals_host.to(self.device)
+        self.levels = (len(CODEBOOK[self.key_bits]["centroids"]), len(CODEBOOK[self.value_bits]["centroids"]))
+
+
+def _fwht(x: torch.Tensor) -> torch.Tensor:
+    from b200serve.core.turboquant import fast_wht
+    return fast_wht(x)
+
+
+def _tq_encode_rows(x: torch.Tensor, tb: TurboQuantTables, keys: bool):
+    """CPU restatement of the GPU encoder: [N, 128] float -> (nibble codes [N, 64] uint8,
+    sign bytes [N, 16] uint8 or None, norm [N], gamma [N] or None)."""
+    d = tb.D
+    sq = math.sqrt(d)
+    x = x.float()
+    n = x.norm(dim=-1, keepdim=True).clamp_min(1e-8)
+    u = _fwht(x / n)
+    s = u * sq
+    bits = tb.key_bits if keys else tb.value_bits
+    lev = tb.levels[0 if keys else 1]
+    thr = tb.thr_host[0 if keys else 1][:lev - 1].to(x.device)
+    cent = tb.cents[0 if keys else 1][:lev].to(x.device)
+    bins = (s.abs()[..., None] > thr).sum(-1) if lev > 1 else torch.zeros_like(s, dtype=torch.long)
+    pos = s >= 0
+    idx = torch.where(pos, bins, bins + lev)
+    uh = torch.where(pos, cent[bins], -cent[bins]) / sq
+    codes = (idx[:, 0::2] | (idx[:, 1::2] << 4)).to(torch.uint8)
+    if not keys:
+        return codes, None, n.squeeze(-1), None
+    r = u - uh
+    rn = r.norm(dim=-1).clamp_min(1e-8)
+    S = tb.S.to(x.device)
+    proj = r @ S.t()
+    sbit = (proj >= 0).long()
+    sgn_bytes = (sbit.view(-1, d // 8, 8) << torch.arange(8, device=x.device)).sum(-1).to(torch.uint8)
+    t = (sbit.float() * 2 - 1) @ S
+    gamma = tb.alpha * rn / t.norm(dim=-1).clamp_min(1e-8)
+    return codes, sgn_bytes, n.squeeze(-1), gamma
+
+
+def _tq_dequant_rows(codes, sgn, meta, tb: TurboQuantTables, keys: bool):
+    """Rotated-domain estimate n (u_hat [+ gamma S^T s]) of cached rows, CPU/torch."""
+    vals = tb.code_vals[0 if keys else 1].to(codes.device)
+    c = codes.long()
+    idx = torch.stack((c & 15, c >> 4), -1).flatten(-2)
+    u = vals[idx]
+    if not keys:
+        return u * meta.float()[..., None]
+    n, g = meta[..., 0].float(), meta[..., 1].float()
+    bits = ((sgn.long()[..., None] >> torch.arange(8, device=sgn.device)) & 1).flatten(-2).float() * 2 - 1
+    t = bits @ tb.S.to(sgn.device)
+    return n[..., None] * (u + g[..., None] * t)
+
+
+def tq_qkv(q, k_stage, v_stage, slots, tb: TurboQuantTables, kv, layer: int):
+    """Rotate the queries (q_rot = H q, q_jl = S q_rot) and encode the new K/V rows of
+    ``k_stage``/``v_stage`` (token t at page t // 16, row t % 16) into the TurboQuant cache at
+    ``slots``. Returns (q_rot, q_jl)."""
+    q_rot = torch.empty_like(q)
+    q_jl = torch.empty_like(q)
+    if _cuda(q):
+        ext().tq_qkv(q, k_stage, v_stage, slots, tb.S, tb.cents, tb.thr_host, tb.key_bits, tb.value_bits,
+                     float(tb.alpha), q_rot, q_jl, kv.k[layer], kv.k_sign[layer], kv.k_scale[layer], kv.v[layer],
+                     kv.v_scale[layer])
+        return q_rot, q_jl
+    T, nq, hd = q.shape
+    qr = _fwht(q.float())
+    q_rot.copy_(qr)
+    q_jl.copy_(qr @ tb.S.t())
+    nkv = kv.k.shape[2]
+    t = torch.arange(T)
+    sl = slots.long()
+    ok = sl >= 0
+    for h in range(nkv):
+        for keys, stage in ((True, k_stage), (False, v_stage)):
+            rows = stage[t // 16, h, t % 16][ok]
+            codes, sg, n, g = _tq_encode_rows(rows, tb, keys)
+            blk, off = sl[ok] // 16, sl[ok] % 16
+            if keys:
+                kv.k[layer, blk, h, off] = codes
+                kv.k_sign[layer, blk, h, off] = sg
+                kv.k_scale[layer, blk, h, off] = torch.stack((n, g), -1).half()
+            else:
+                kv.v[layer, blk, h, off] = codes
+                kv.v_scale[layer, blk, h, off] = n.half()
+    return q_rot, q_jl
+
+
+def tq_dequant(block_ids, kv, layer: int, tb: TurboQuantTables, out_k, out_v):
+    """Pages ``block_ids`` of the TurboQuant cache -> bf16 pages 0.. of out_k / out_v in the
+    rotated domain (keys with the QJL correction)."""
+    if _cuda(out_k):
+        ext().tq_dequant(block_ids, kv.k[layer], kv.k_sign[layer], kv.k_scale[layer], kv.v[layer],
+                         kv.v_scale[layer], tb.S, tb.code_vals, out_k, out_v)
+        return
+    ids = block_ids.long()
+    n = ids.numel()
+    out_k[:n] = _tq_dequant_rows(kv.k[layer][ids], kv.k_sign[layer][ids], kv.k_scale[layer][ids], tb,
+                                 True).to(out_k.dtype)
+    out_v[:n] = _tq_dequant_rows(kv.v[layer][ids], None, kv.v_scale[layer][ids], tb, False).to(out_v.dtype)
+
+
+def tq_decode_attention(q_rot, q_jl, kv, layer: int, tb: TurboQuantTables, block_tables, seq_lens, scale,
+                        tps=256, nsplit=1, workspace=None):
+    """Decode attention over the TurboQuant cache; the output stays in the rotated domain
+    (the o_proj weight carries the inverse transform)."""
+    if _cuda(q_rot, 2 if nsplit > 1 else 1):
+        out = torch.empty_like(q_rot)
+        if nsplit > 1:
+            assert workspace is not None and workspace.max_splits >= nsplit
+            acc, ml = workspace.acc, workspace.ml
+        else:
+            acc = ml = torch.empty(0, dtype=torch.float32, device=q_rot.device)
+        ext().paged_decode_attention_tq(q_rot, q_jl, kv.k[layer], kv.k_sign[layer], kv.k_scale[layer], kv.v[layer],
+                                        kv.v_scale[layer], tb.code_vals_host, block_tables, seq_lens, out, acc,
+                                        ml, float(scale), int(tps), int(nsplit))
+        return out
+    B = q_rot.shape[0]
+    nb = block_tables.shape[1]
+    ids = block_tables.reshape(-1).clamp_min(0)
+    kd = _tq_dequant_rows(kv.k[layer][ids], kv.k_sign[layer][ids], kv.k_scale[layer][ids], tb, True)
+    vd = _tq_dequant_rows(kv.v[layer][ids], None, kv.v_scale[layer][ids], tb, False)
+    kd = kd.view(B * nb, *kd.shape[1:])
+    vd = vd.view(B * nb, *vd.shape[1:])
+    tables = torch.arange(B * nb, dtype=torch.int32).view(B, nb)
+    return paged_decode_attention(q_rot, kd, vd, tables, seq_lens, scale)
+
+
 def gemm_error_flag(reset: bool = True) -> int:
     return int(ext().gemm_error_flag(reset)) if extension_loaded() else 0
 

@@ -83,6 +83,68 @@ __device__ __forceinline__ void dequant_q4_page(const uint8_t* raw, uint8_t* wor
   }
 }
 
+// TurboQuant page stage (KVQ == 2), per (page, kv head):
+//   K codes [16][64] (one 4-bit index per dim, byte m = dims 2m | 2m+1 << 4) | K QJL signs [16][16]
+//   (bit i = sign of row i of S r) | K (norm, gamma) [16][2] fp16 | V codes [16][64] | V norm [16] fp16.
+// Scores run in the rotated domain over a 256-dim virtual key: [n u_hat | n gamma s] against the
+// query [H q | S H q], so the QJL correction is one more MMA k-range instead of a per-key transform.
+constexpr int kTqKCodes = 0, kTqKSign = 1024, kTqKMeta = 1280, kTqVCodes = 1344, kTqVMeta = 2368;
+constexpr int kTqRaw = 2400;
+constexpr int kTqLut = 2 * 256 * 4;                 // pair tables (bf16x2 per code byte) for K and V
+
+// Dequantise one TurboQuant page into the work stage: K_hat (boxes 0-1), K_sgn (boxes 2-3), V (4-5).
+// Lane l converts row l/2, dims [64*(l&1), +64).
+__device__ __forceinline__ void dequant_tq_page(const uint8_t* raw, uint8_t* work, int lane, const uint32_t* lutk,
+                                                const uint32_t* lutv) {
+  const int row = lane >> 1, half = lane & 1;
+  const __half* km = reinterpret_cast<const __half*>(raw + kTqKMeta);
+  const float kn = __half2float(km[row * 2]), kg = __half2float(km[row * 2 + 1]);
+  const float vn = __half2float(reinterpret_cast<const __half*>(raw + kTqVMeta)[row]);
+#pragma unroll
+  for (int kv = 0; kv < 2; ++kv) {
+    const uint4* src = reinterpret_cast<const uint4*>(raw + (kv ? kTqVCodes : kTqKCodes) + row * 64 + half * 32);
+    const uint32_t* lut = kv ? lutv : lutk;
+    const uint32_t n2 = pack_bf16x2(kv ? vn : kn, kv ? vn : kn);
+    uint8_t* dst = work + (kv ? 4 : 0) * kBoxBytes;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint4 c = src[j];
+      const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        uint32_t r[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const uint32_t e = lut[(wv[w] >> (8 * p)) & 255u];
+          asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r[p]) : "r"(e), "r"(n2));
+        }
+        *reinterpret_cast<uint4*>(dst + swz(row, half * 8 + j * 4 + w)) = make_uint4(r[0], r[1], r[2], r[3]);
+      }
+    }
+  }
+  // K_sgn: +-(norm * gamma) per dim from the sign bits (bit 1 = +)
+  const uint2 sb = *reinterpret_cast<const uint2*>(raw + kTqKSign + row * 16 + half * 8);
+  const uint32_t bw[2] = {sb.x, sb.y};
+  const uint32_t g2 = pack_bf16x2(kn * kg, kn * kg) & 0x7fff7fffu;
+#pragma unroll
+  for (int by = 0; by < 8; ++by) {
+    const uint32_t bits = (bw[by >> 2] >> (8 * (by & 3))) & 255u;   // dims 8*by .. 8*by+7 of this half
+    uint32_t r[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t neg_lo = ((bits >> (2 * p)) & 1u) ^ 1u, neg_hi = ((bits >> (2 * p + 1)) & 1u) ^ 1u;
+      r[p] = g2 | (neg_lo << 15) | (neg_hi << 31);
+    }
+    *reinterpret_cast<uint4*>(work + swz(row, 16 + half * 8 + by)) = make_uint4(r[0], r[1], r[2], r[3]);
+  }
+}
+
+struct TqArgs {
+  const uint8_t* ksign;             // [pages][16][16]
+  const __nv_bfloat16* qj;          // [B, nq, 128]: S H q
+  float cbk[16], cbv[16];           // value of each 4-bit code (sign and 1/sqrt(d) folded in)
+};
+
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    tc::smem_u32(dst)),
@@ -96,18 +158,31 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
     const __nv_bfloat16* __restrict__ q, const int* __restrict__ block_tables, const int* __restrict__ seq_lens,
     int max_blocks, int nkv, float scale_log2, int tps, float* __restrict__ part_acc, float* __restrict__ part_ml,
     __nv_bfloat16* __restrict__ out, int nsplit, int* err, const uint8_t* __restrict__ kq,
-    const uint8_t* __restrict__ vq, const __half* __restrict__ ks, const __half* __restrict__ vs) {
+    const uint8_t* __restrict__ vq, const __half* __restrict__ ks, const __half* __restrict__ vs, const TqArgs tq) {
   static_assert(G >= 1 && G <= 16, "query heads per kv head");
+  constexpr int KSTEPS = KVQ == 2 ? 16 : 8;        // 16-dim MMA k-steps of the (virtual) key
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
   // bf16 pages: ring of kTcStages swizzled stages per warp. int4 pages: ring of raw stages plus
   // one swizzled work stage per warp.
-  constexpr int kWarpBytes = KVQ ? (kTcStages * kQ4Raw + kStageBytes) : kTcStages * kStageBytes;
+  constexpr int kRaw = KVQ == 2 ? kTqRaw : kQ4Raw;
+  constexpr int kWarpBytes = KVQ == 2 ? (kTcStages * kTqRaw + 6 * kBoxBytes)
+                             : KVQ ? (kTcStages * kQ4Raw + kStageBytes) : kTcStages * kStageBytes;
   uint8_t* ring = smem + warp * kWarpBytes;
-  uint8_t* work = ring + kTcStages * kQ4Raw;
+  uint8_t* work = ring + kTcStages * kRaw;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcWarps * kWarpBytes) + warp * kTcStages;
+  uint32_t* lutk = reinterpret_cast<uint32_t*>(smem + kTcWarps * kWarpBytes + kTcWarps * kTcStages * 8);
+  uint32_t* lutv = lutk + 256;
+  if constexpr (KVQ == 2) {
+    for (int e = threadIdx.x; e < 512; e += blockDim.x) {
+      const float* cb = e < 256 ? tq.cbk : tq.cbv;
+      const int i = e & 255;
+      lutk[e] = pack_bf16x2(cb[i & 15], cb[i >> 4]);
+    }
+    __syncthreads();
+  }
   float* mrg = reinterpret_cast<float*>(smem);   // merge scratch, reuses the rings after the page loop
 
   pdl_wait();
@@ -126,12 +201,13 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
   __syncwarp();
 
   // Q as the A operand: rows = query heads (>= G zero), k = head dims
-  uint32_t qa[8][4];
-  {
-    const __nv_bfloat16* qb = q + ((size_t)b * nq + kvh * G) * kHD;
+  uint32_t qa[KSTEPS][4];
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const int d0 = kk * 16 + 2 * t4;
+  for (int kk = 0; kk < KSTEPS; ++kk) {
+    const __nv_bfloat16* qsrc = (KVQ == 2 && kk >= 8) ? tq.qj : q;
+    const __nv_bfloat16* qb = qsrc + ((size_t)b * nq + kvh * G) * kHD;
+    {
+      const int d0 = (kk & 7) * 16 + 2 * t4;
       qa[kk][0] = g < G ? *reinterpret_cast<const uint32_t*>(qb + g * kHD + d0) : 0u;
       qa[kk][1] = g + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * kHD + d0) : 0u;
       qa[kk][2] = g < G ? *reinterpret_cast<const uint32_t*>(qb + g * kHD + d0 + 8) : 0u;
@@ -159,6 +235,14 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
       tc::tma_load_2d(st + kBoxBytes, &tm_k, &bars[s], 64, y, 0ull);
       tc::tma_load_2d(st + 2 * kBoxBytes, &tm_v, &bars[s], 0, y, 0ull);
       tc::tma_load_2d(st + 3 * kBoxBytes, &tm_v, &bars[s], 64, y, 0ull);
+    } else if constexpr (KVQ == 2) {
+      uint8_t* st = ring + s * kTqRaw;
+      tc::mbar_arrive_expect_tx(&bars[s], kTqRaw);
+      bulk_load(st + kTqKCodes, kq + (size_t)page * 1024, 1024, &bars[s]);
+      bulk_load(st + kTqKSign, tq.ksign + (size_t)page * 256, 256, &bars[s]);
+      bulk_load(st + kTqKMeta, reinterpret_cast<const uint8_t*>(ks) + (size_t)page * 64, 64, &bars[s]);
+      bulk_load(st + kTqVCodes, vq + (size_t)page * 1024, 1024, &bars[s]);
+      bulk_load(st + kTqVMeta, reinterpret_cast<const uint8_t*>(vs) + (size_t)page * 32, 32, &bars[s]);
     } else {
       uint8_t* st = ring + s * kQ4Raw;
       tc::mbar_arrive_expect_tx(&bars[s], 2 * 1024 + 2 * 32);
@@ -180,19 +264,23 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
     uint32_t kbase;
     if constexpr (KVQ == 0) {
       kbase = tc::smem_u32(ring + s * kStageBytes);
+    } else if constexpr (KVQ == 2) {
+      dequant_tq_page(ring + s * kTqRaw, work, lane, lutk, lutv);
+      __syncwarp();
+      kbase = tc::smem_u32(work);
     } else {
       dequant_q4_page(ring + s * kQ4Raw, work, lane);
       __syncwarp();
       kbase = tc::smem_u32(work);
     }
-    const uint32_t vbase = kbase + 2 * kBoxBytes;
+    const uint32_t vbase = kbase + (KVQ == 2 ? 4 : 2) * kBoxBytes;
     const int tok0 = first + i * kTcWarps * 16;
     // ---- S^T [heads x 16 tokens] ----
     float sc[2][4];
 #pragma unroll
     for (int nb = 0; nb < 2; ++nb) sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
+    for (int kk = 0; kk < KSTEPS; ++kk) {
       // matrices: (tok 0-7, chunk 2kk), (tok 0-7, chunk 2kk+1), (tok 8-15, 2kk), (tok 8-15, 2kk+1)
       const int mi = lane >> 3, r = lane & 7;
       const int tok = (mi >> 1) * 8 + r;
@@ -307,7 +395,9 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
 }
 
 size_t decode_tc_smem(int kvq) {
-  return 1024 + kTcWarps * (kvq ? (kTcStages * kQ4Raw + kStageBytes) : kTcStages * kStageBytes) + 256;
+  const size_t per_warp = kvq == 2 ? (kTcStages * kTqRaw + 6 * kBoxBytes)
+                          : kvq ? (kTcStages * kQ4Raw + kStageBytes) : kTcStages * kStageBytes;
+  return 1024 + kTcWarps * per_warp + 256 + (kvq == 2 ? kTqLut : 0);
 }
 
 typedef CUresult (*EncodeTiledFnKV)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -357,7 +447,7 @@ void paged_decode_combine(torch::Tensor part_acc, torch::Tensor part_ml, torch::
 static void decode_tc_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                            torch::Tensor seq_lens, torch::Tensor out, torch::Tensor part_acc, torch::Tensor part_ml,
                            double scale, int64_t tps, int64_t nsplit, int kvq, const uint8_t* kq, const uint8_t* vq,
-                           const __half* ksc, const __half* vsc, int nkv) {
+                           const __half* ksc, const __half* vsc, int nkv, const TqArgs& tq) {
   const int B = q.size(0), nq = q.size(1), HD = q.size(2);
   const int G = nq / nkv;
   TORCH_CHECK(HD == kHD && k_cache.size(2) == 16 && tps % 16 == 0 && nsplit >= 1);
@@ -393,9 +483,9 @@ static void decode_tc_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor
     launch_pdl(paged_decode_tc_kernel<GV, KQ>, grid, dim3(kTcWarps * 32), smem, stream, tk, tv,                \
                reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), (const int*)block_tables.data_ptr<int>(),  \
                (const int*)seq_lens.data_ptr<int>(), (int)block_tables.size(1), nkv, sl2, (int)tps, pa, pm, op, \
-               (int)nsplit, decode_tc_err_word(), kq, vq, ksc, vsc);                                           \
+               (int)nsplit, decode_tc_err_word(), kq, vq, ksc, vsc, tq);                                       \
   }
-#define B200_TC(GV) { if (kvq) B200_TC1(GV, 1) else B200_TC1(GV, 0) }
+#define B200_TC(GV) { if (kvq == 2) B200_TC1(GV, 2) else if (kvq) B200_TC1(GV, 1) else B200_TC1(GV, 0) }
   switch (G) {
     case 1: B200_TC(1) break;
     case 2: B200_TC(2) break;
@@ -413,8 +503,9 @@ void paged_decode_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Te
                                torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
                                torch::Tensor part_acc, torch::Tensor part_ml, double scale, int64_t tps,
                                int64_t nsplit) {
+  TqArgs none{};
   decode_tc_impl(q, k_cache, v_cache, block_tables, seq_lens, out, part_acc, part_ml, scale, tps, nsplit, 0, nullptr,
-                 nullptr, nullptr, nullptr, k_cache.size(1));
+                 nullptr, nullptr, nullptr, k_cache.size(1), none);
 }
 
 // int4g128 KV: codes [blocks][nkv][16][64] uint8, scales [blocks][nkv][16] fp16.
@@ -426,5 +517,30 @@ void paged_decode_attention_q4(torch::Tensor q, torch::Tensor k_codes, torch::Te
   decode_tc_impl(q, k_codes, v_codes, block_tables, seq_lens, out, part_acc, part_ml, scale, tps, nsplit, 1,
                  k_codes.data_ptr<uint8_t>(), v_codes.data_ptr<uint8_t>(),
                  reinterpret_cast<const __half*>(k_scale.data_ptr()), reinterpret_cast<const __half*>(v_scale.data_ptr()),
-                 k_codes.size(1));
+                 k_codes.size(1), TqArgs{});
+}
+
+// TurboQuant KV: codes [blocks][nkv][16][64] uint8 (one 4-bit code per dim), k_sign [blocks][nkv][16][16]
+// uint8, k_meta [blocks][nkv][16][2] fp16 (norm, gamma), v_meta [blocks][nkv][16] fp16 (norm).
+// q_rot = H q and q_jl = S H q, [B, nq, 128] bf16; the output is in the rotated domain (H o).
+// code_vals: float [2][16] = value of each K / V code.
+void paged_decode_attention_tq(torch::Tensor q_rot, torch::Tensor q_jl, torch::Tensor k_codes, torch::Tensor k_sign,
+                               torch::Tensor k_meta, torch::Tensor v_codes, torch::Tensor v_meta,
+                               torch::Tensor code_vals, torch::Tensor block_tables, torch::Tensor seq_lens,
+                               torch::Tensor out, torch::Tensor part_acc, torch::Tensor part_ml, double scale,
+                               int64_t tps, int64_t nsplit) {
+  TORCH_CHECK(k_codes.size(3) == 64 && k_codes.scalar_type() == at::kByte && k_sign.size(3) == 16,
+              "turboquant codes must be [*, nkv, 16, 64] and signs [*, nkv, 16, 16] uint8");
+  TORCH_CHECK(q_jl.sizes() == q_rot.sizes() && q_jl.is_contiguous() && q_rot.is_contiguous());
+  TORCH_CHECK(code_vals.device().is_cpu(), "code_vals is a host tensor (baked into the launch parameters)");
+  auto cv = code_vals.to(at::kFloat).contiguous();
+  TORCH_CHECK(cv.numel() == 32, "code_vals must hold 2 x 16 values");
+  TqArgs tq{};
+  tq.ksign = k_sign.data_ptr<uint8_t>();
+  tq.qj = reinterpret_cast<const __nv_bfloat16*>(q_jl.data_ptr());
+  for (int i = 0; i < 16; ++i) { tq.cbk[i] = cv.data_ptr<float>()[i]; tq.cbv[i] = cv.data_ptr<float>()[16 + i]; }
+  decode_tc_impl(q_rot, k_codes, v_codes, block_tables, seq_lens, out, part_acc, part_ml, scale, tps, nsplit, 2,
+                 k_codes.data_ptr<uint8_t>(), v_codes.data_ptr<uint8_t>(),
+                 reinterpret_cast<const __half*>(k_meta.data_ptr()), reinterpret_cast<const __half*>(v_meta.data_ptr()),
+                 k_codes.size(1), tq);
 }

@@ -66,6 +66,19 @@ void argmax_merge(torch::Tensor vals, torch::Tensor idx, torch::Tensor out);
 void sample_rows(torch::Tensor logits, torch::Tensor params, torch::Tensor pen_ids, torch::Tensor pen_counts,
                  torch::Tensor pen_vals, torch::Tensor out);
 
+void paged_decode_attention_tq(torch::Tensor q_rot, torch::Tensor q_jl, torch::Tensor k_codes, torch::Tensor k_sign,
+                               torch::Tensor k_meta, torch::Tensor v_codes, torch::Tensor v_meta,
+                               torch::Tensor code_vals, torch::Tensor block_tables, torch::Tensor seq_lens,
+                               torch::Tensor out, torch::Tensor part_acc, torch::Tensor part_ml, double scale,
+                               int64_t tps, int64_t nsplit);
+void tq_qkv(torch::Tensor q, torch::Tensor k_stage, torch::Tensor v_stage, torch::Tensor slots, torch::Tensor S,
+            torch::Tensor cents, torch::Tensor thr, int64_t kbits, int64_t vbits, double alpha, torch::Tensor q_rot,
+            torch::Tensor q_jl, torch::Tensor k_codes, torch::Tensor k_sign, torch::Tensor k_meta,
+            torch::Tensor v_codes, torch::Tensor v_meta);
+void tq_dequant(torch::Tensor block_ids, torch::Tensor k_codes, torch::Tensor k_sign, torch::Tensor k_meta,
+                torch::Tensor v_codes, torch::Tensor v_meta, torch::Tensor S, torch::Tensor code_vals,
+                torch::Tensor out_k, torch::Tensor out_v);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "b200serve sm_100a kernels";
   m.def("rmsnorm_fused", &rmsnorm_fused);
@@ -101,4 +114,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax_rows", &argmax_rows);
   m.def("argmax_merge", &argmax_merge);
   m.def("sample_rows", &sample_rows);
+  m.def("paged_decode_attention_tq", &paged_decode_attention_tq);
+  m.def("tq_qkv", &tq_qkv);
+  m.def("tq_dequant", &tq_dequant);
 }
