@@ -50,8 +50,24 @@ static int* gemm_err_word() {
   return g_err_dev;
 }
 
-static void launch_by_bn(int BN, int epi, const CUtensorMap& tw, const CUtensorMap& ta, const GemmParams& p,
+// Shared-memory budget of the stage ring. Decode-sized token tiles (BN <= 64) default to
+// ~104 KB, which leaves room for a neighbouring kernel's CTA on the SM (programmatic dependent
+// launch overlap); B200_GEMM_DECODE_SMEM_KB overrides it. Larger tiles use 200 KB.
+static int ring_stages(int BN) {
+  static int decode_kb = -1;
+  if (decode_kb < 0) {
+    const char* e = getenv("B200_GEMM_DECODE_SMEM_KB");
+    decode_kb = e ? std::max(40, std::min(220, atoi(e))) : 104;
+  }
+  const int budget = (BN <= 64 ? decode_kb : 200) * 1024;
+  const int stage = 128 * 64 * 2 + BN * 64 * 2;
+  return std::max(2, std::min(12, budget / stage));
+}
+
+static void launch_by_bn(int BN, int epi, const CUtensorMap& tw, const CUtensorMap& ta, const GemmParams& p0,
                          int grid, cudaStream_t stream) {
+  GemmParams p = p0;
+  if (p.stages <= 0) p.stages = ring_stages(BN);
   switch (BN) {
     case 16: launch_gemm_bn<16>(epi, tw, ta, p, grid, stream); break;
     case 32: launch_gemm_bn<32>(epi, tw, ta, p, grid, stream); break;

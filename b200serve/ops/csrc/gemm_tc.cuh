@@ -42,6 +42,7 @@ struct GemmParams {
   const int* g_offsets;
   int g_E;
   int n_tiles, m_tiles, splits, kb_per_split, kb_total, units;
+  int stages;                   // shared-memory ring depth (set by the host launcher)
   void* out;                    // bf16 or fp32, row stride ldo (elements)
   int ldo;
   const __nv_bfloat16* bias;    // [N] or null
@@ -57,7 +58,7 @@ struct GemmParams {
   const int* epoch;                     // this step's epoch (device)
   int* tile_done;                       // local counter of pushed tiles, zero on entry and exit
   // optional per-CTA timeline (globaltimer ns): [cta][8] = entry, setup done, first TMA issued,
-  // first stage landed, last MMA committed, epilogue done, exit
+  // first stage landed, last MMA committed, epilogue done, exit (thread 0), exit (thread 32)
   unsigned long long* trace;
 };
 
@@ -72,12 +73,12 @@ struct GemmCfg {
   static constexpr int W_BYTES = BM * BK * 2;
   static constexpr int A_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = W_BYTES + A_BYTES;
-  // decode-sized tiles keep ~100 KB so the next kernel's CTA fits beside this one (PDL overlap)
-  static constexpr int BUDGET = BN <= 64 ? 104 * 1024 : 200 * 1024;
-  static constexpr int STAGES = BUDGET / STAGE_BYTES > 12 ? 12 : BUDGET / STAGE_BYTES;
+  // the ring depth is a launch parameter (GemmParams::stages, 2..MAX_STAGES); the barrier
+  // block is sized for MAX_STAGES so its layout does not depend on it
+  static constexpr int MAX_STAGES = 12;
   static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;
   static constexpr int XCHG_FLOATS = 64 * 17;
-  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + XCHG_FLOATS * 4 + 256;
+  static constexpr size_t smem(int stages) { return 1024 + (size_t)stages * STAGE_BYTES + XCHG_FLOATS * 4 + 256; }
 };
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -215,7 +216,7 @@ __global__ void __launch_bounds__(192, 2)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
                    const GemmParams p) {
   using Cfg = GemmCfg<BN>;
-  constexpr int STAGES = Cfg::STAGES;
+  const int STAGES = p.stages;
   constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, BN);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -223,8 +224,8 @@ __global__ void __launch_bounds__(192, 2)
   uint8_t* s_a = smem + STAGES * Cfg::W_BYTES;
   float* xchg = reinterpret_cast<float*>(s_a + STAGES * Cfg::A_BYTES);
   uint64_t* full = reinterpret_cast<uint64_t*>(xchg + Cfg::XCHG_FLOATS);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
+  uint64_t* empty = full + Cfg::MAX_STAGES;
+  uint64_t* tfull = empty + Cfg::MAX_STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* mma_done = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
@@ -426,6 +427,7 @@ __global__ void __launch_bounds__(192, 2)
   tc::tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) trace_mark(p, 6);
+  if (threadIdx.x == 32) trace_mark(p, 7);
   if (*abort_flag) {
     // error path: give TMA copies that may still be landing in shared memory time to finish
     const uint64_t until = globaltimer_ns() + 100000ull;
@@ -445,10 +447,12 @@ void launch_gemm(const CUtensorMap& tw, const CUtensorMap& ta, const GemmParams&
   static bool attr_set = false;
   if (!attr_set) {
     B200_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)Cfg::SMEM));
+                                         227 * 1024));
     attr_set = true;
   }
-  launch_pdl(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(192), Cfg::SMEM, stream, tw, ta, p);
+  TORCH_CHECK(p.stages >= 2 && p.stages <= Cfg::MAX_STAGES && Cfg::smem(p.stages) <= 227 * 1024,
+              "GEMM stage count out of range");
+  launch_pdl(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(192), Cfg::smem(p.stages), stream, tw, ta, p);
 }
 
 // one translation unit per BN (gemm_tc_bn*.cu) instantiates this for every epilogue

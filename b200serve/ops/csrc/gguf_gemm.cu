@@ -68,99 +68,119 @@ __device__ __forceinline__ void dequant_s8(uint32_t w0, uint32_t w1, uint32_t sa
   }
 }
 
+// Chunk of 256 K columns for one warp: all codes and scales are loaded into registers before the
+// MMAs, so a warp keeps ~1 KB of independent loads in flight.
+template <int BITS, int NB>
+__device__ __forceinline__ void gguf_chunk(const uint32_t* __restrict__ codes, const uint32_t* __restrict__ smeta,
+                                           const __nv_bfloat16* xs, int LDX, int slice, int ksteps, int K, int group,
+                                           int k0, int kc0, int lane, float (&acc)[NB][4]) {
+  constexpr int KS = kQChunk / 16;                           // 16 k-steps per chunk
+  const int g = lane >> 2, t4 = lane & 3;
+  const int ks0 = k0 / 16;
+  if constexpr (BITS == 4) {
+    uint32_t cw[KS];
+    uint32_t mt[KS / 2][4];                                  // per 32-wide sub-block: sA, mA, sB, mB
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) cw[ks] = __ldg(codes + ((size_t)slice * ksteps + ks0 + ks) * 32 + lane);
+#pragma unroll
+    for (int sb = 0; sb < KS / 2; ++sb) {
+      const uint32_t* mp = smeta + ((size_t)slice * (K / 32) + (ks0 / 2 + sb)) * 32;
+      mt[sb][0] = __ldg(mp + g * 2);
+      mt[sb][1] = __ldg(mp + g * 2 + 1);
+      mt[sb][2] = __ldg(mp + (g + 8) * 2);
+      mt[sb][3] = __ldg(mp + (g + 8) * 2 + 1);
+    }
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      uint32_t a[4];
+      dequant_u4(cw[ks], mt[ks / 2][0], mt[ks / 2][1], mt[ks / 2][2], mt[ks / 2][3], a);
+      const int kk = (ks0 + ks) * 16 - kc0 + 2 * t4;
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        const __nv_bfloat16* xr = xs + (size_t)(j * 8 + g) * LDX + kk;
+        qmma(acc[j], a, *reinterpret_cast<const uint32_t*>(xr), *reinterpret_cast<const uint32_t*>(xr + 8));
+      }
+    }
+  } else {
+    uint2 cw[KS];
+    constexpr int GPC = kQChunk / 16;                        // max groups per chunk (group >= 16)
+    uint32_t sc[GPC][2];
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks)
+      cw[ks] = __ldg(reinterpret_cast<const uint2*>(codes) + ((size_t)slice * ksteps + ks0 + ks) * 32 + lane);
+    const int ngr = kQChunk / group;
+#pragma unroll
+    for (int gi = 0; gi < GPC; ++gi) {
+      if (gi < ngr) {
+        const uint32_t* sp = smeta + ((size_t)slice * (K / group) + (k0 / group + gi)) * 16;
+        sc[gi][0] = __ldg(sp + g);
+        sc[gi][1] = __ldg(sp + g + 8);
+      }
+    }
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      uint32_t a[4];
+      const bool g16 = group == 16;                          // both indices are compile-time
+      dequant_s8(cw[ks].x, cw[ks].y, g16 ? sc[ks][0] : sc[ks / 2][0], g16 ? sc[ks][1] : sc[ks / 2][1], a);
+      const int kk = (ks0 + ks) * 16 - kc0 + 2 * t4;
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        const __nv_bfloat16* xr = xs + (size_t)(j * 8 + g) * LDX + kk;
+        qmma(acc[j], a, *reinterpret_cast<const uint32_t*>(xr), *reinterpret_cast<const uint32_t*>(xr + 8));
+      }
+    }
+  }
+}
+
 // BITS = 4 (Q4_K: codes [N/16][K/16][32] u32, scale/min [N/16][K/32][16 rows] bf16x2 (s, -m))
 // BITS = 8 (codes [N/16][K/16][32][2] u32, scales [N/16][K/GROUP][16] bf16)
+// A CTA covers NB 16-row slices (more tokens -> more slices share one staged activation block);
+// warp w works on slice w % NB and every (8/NB)-th 256-column chunk of each staged block.
 template <int BITS, int NB>
 __global__ void __launch_bounds__(kQWarps * 32) gguf_gemm_kernel(
     const uint32_t* __restrict__ codes, const uint32_t* __restrict__ smeta, const __nv_bfloat16* __restrict__ x,
     int M, int N, int K, int group, __nv_bfloat16* __restrict__ out, int ldo) {
+  constexpr int SPC = NB, NPH = kQWarps / SPC;
   extern __shared__ __align__(16) uint8_t smem[];
   const int KC = min(K, kQStage);                          // K columns of x staged at a time
   const int LDX = KC + 8;                                  // padded row: conflict-free B fragments
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem);   // [NB*8][LDX]
   float* red = reinterpret_cast<float*>(smem + (size_t)NB * 8 * LDX * 2);   // [warps][16][NB*8]
-  pdl_wait();
-  pdl_trigger();
   const int rows_tok = NB * 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
-  const int slice = blockIdx.x;                            // 16 output rows
+  const int nslices = N / 16;
+  const int slice = blockIdx.x * SPC + warp % SPC;          // 16 output rows
+  const int phase = warp / SPC;
+  const bool live = slice < nslices;
   const int ksteps = K / 16;
   float acc[NB][4];
 #pragma unroll
   for (int j = 0; j < NB; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-  // Each warp owns 256-wide K chunks. All codes and scales of a chunk are loaded into
-  // registers before any MMA, so a warp keeps ~1 KB of independent loads in flight.
-  constexpr int KS = kQChunk / 16;                           // 16 k-steps per chunk
+  pdl_wait();
+  pdl_trigger();
   for (int kc0 = 0; kc0 < K; kc0 += KC) {
     const int kcn = min(KC, K - kc0);
-    if (kc0 > 0) __syncthreads();                              // previous x block fully consumed
+    if (kc0 > 0) __syncthreads();                          // previous x block fully consumed
+    // stage x[:, kc0:kc0+kcn) with asynchronous 16-byte copies (rows >= M zero-filled)
+    const uint32_t xs_base = (uint32_t)__cvta_generic_to_shared(xs);
     for (int i = threadIdx.x; i < rows_tok * (kcn / 8); i += blockDim.x) {
       const int r = i / (kcn / 8), c = (i % (kcn / 8)) * 8;
-      bf16x8 v;
-      if (r < M) v = *reinterpret_cast<const bf16x8*>(x + (size_t)r * K + kc0 + c);
-      else v.w[0] = v.w[1] = v.w[2] = v.w[3] = 0u;
-      *reinterpret_cast<bf16x8*>(xs + (size_t)r * LDX + c) = v;
+      const uint32_t dst = xs_base + (uint32_t)(((size_t)r * LDX + c) * 2);
+      const __nv_bfloat16* src = x + (size_t)min(r, M - 1) * K + kc0 + c;
+      const int bytes = r < M ? 16 : 0;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    for (int k0 = kc0 + warp * kQChunk; k0 < kc0 + kcn; k0 += kQWarps * kQChunk) {
-      const int ks0 = k0 / 16;
-      if constexpr (BITS == 4) {
-        uint32_t cw[KS];
-        uint32_t mt[KS / 2][4];                                // per 32-wide sub-block: sA, mA, sB, mB
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) cw[ks] = __ldg(codes + ((size_t)slice * ksteps + ks0 + ks) * 32 + lane);
-#pragma unroll
-        for (int sb = 0; sb < KS / 2; ++sb) {
-          const uint32_t* mp = smeta + ((size_t)slice * (K / 32) + (ks0 / 2 + sb)) * 32;
-          mt[sb][0] = __ldg(mp + g * 2);
-          mt[sb][1] = __ldg(mp + g * 2 + 1);
-          mt[sb][2] = __ldg(mp + (g + 8) * 2);
-          mt[sb][3] = __ldg(mp + (g + 8) * 2 + 1);
-        }
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-          uint32_t a[4];
-          dequant_u4(cw[ks], mt[ks / 2][0], mt[ks / 2][1], mt[ks / 2][2], mt[ks / 2][3], a);
-          const int kk = (ks0 + ks) * 16 - kc0 + 2 * t4;
-#pragma unroll
-          for (int j = 0; j < NB; ++j) {
-            const __nv_bfloat16* xr = xs + (size_t)(j * 8 + g) * LDX + kk;
-            qmma(acc[j], a, *reinterpret_cast<const uint32_t*>(xr), *reinterpret_cast<const uint32_t*>(xr + 8));
-          }
-        }
-      } else {
-        uint2 cw[KS];
-        constexpr int GPC = kQChunk / 16;                      // max groups per chunk (group >= 16)
-        uint32_t sc[GPC][2];
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks)
-          cw[ks] = __ldg(reinterpret_cast<const uint2*>(codes) + ((size_t)slice * ksteps + ks0 + ks) * 32 + lane);
-        const int ngr = kQChunk / group;
-#pragma unroll
-        for (int gi = 0; gi < GPC; ++gi) {
-          if (gi < ngr) {
-            const uint32_t* sp = smeta + ((size_t)slice * (K / group) + (k0 / group + gi)) * 16;
-            sc[gi][0] = __ldg(sp + g);
-            sc[gi][1] = __ldg(sp + g + 8);
-          }
-        }
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-          uint32_t a[4];
-          const bool g16 = group == 16;                        // both indices are compile-time
-          dequant_s8(cw[ks].x, cw[ks].y, g16 ? sc[ks][0] : sc[ks / 2][0], g16 ? sc[ks][1] : sc[ks / 2][1], a);
-          const int kk = (ks0 + ks) * 16 - kc0 + 2 * t4;
-#pragma unroll
-          for (int j = 0; j < NB; ++j) {
-            const __nv_bfloat16* xr = xs + (size_t)(j * 8 + g) * LDX + kk;
-            qmma(acc[j], a, *reinterpret_cast<const uint32_t*>(xr), *reinterpret_cast<const uint32_t*>(xr + 8));
-          }
-        }
-      }
+    if (live) {
+      for (int c = phase; c < kcn / kQChunk; c += NPH)
+        gguf_chunk<BITS, NB>(codes, smeta, xs, LDX, slice, ksteps, K, group, kc0 + c * kQChunk, kc0, lane, acc);
     }
   }
-  // acc[j]: rows g / g+8 of the slice, tokens j*8 + 2t, +1 -> reduce over warps in shared memory
+  // acc[j]: rows g / g+8 of the slice, tokens j*8 + 2t, +1 -> reduce over the warps of each slice
+  __syncthreads();
   float* mine = red + (size_t)warp * 16 * rows_tok;
 #pragma unroll
   for (int j = 0; j < NB; ++j) {
@@ -170,12 +190,13 @@ __global__ void __launch_bounds__(kQWarps * 32) gguf_gemm_kernel(
     mine[(g + 8) * rows_tok + j * 8 + 2 * t4 + 1] = acc[j][3];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < 16 * rows_tok; i += blockDim.x) {
-    const int r = i / rows_tok, tk = i % rows_tok;
+  for (int i = threadIdx.x; i < SPC * 16 * rows_tok; i += blockDim.x) {
+    const int sl = i / (16 * rows_tok), rem = i % (16 * rows_tok);
+    const int r = rem / rows_tok, tk = rem % rows_tok;
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < kQWarps; ++w) s += red[(size_t)w * 16 * rows_tok + i];
-    const int n = slice * 16 + r;
+    for (int ph = 0; ph < NPH; ++ph) s += red[(size_t)(ph * SPC + sl) * 16 * rows_tok + rem];
+    const int n = (blockIdx.x * SPC + sl) * 16 + r;
     if (tk < M && n < N) out[(size_t)tk * ldo + n] = __float2bfloat16_rn(s);
   }
 }
@@ -195,7 +216,7 @@ void gguf_gemm(torch::Tensor x, torch::Tensor codes, torch::Tensor meta, int64_t
   const int NB = M <= 8 ? 1 : M <= 16 ? 2 : 4;
   const size_t smem = (size_t)NB * 8 * (std::min<int>(K, kQStage) + 8) * 2 + (size_t)kQWarps * 16 * NB * 8 * 4;
   auto stream = at::cuda::getCurrentCUDAStream();
-  const dim3 grid(N / 16), block(kQWarps * 32);
+  const dim3 grid((N / 16 + NB - 1) / NB), block(kQWarps * 32);
   auto cp = reinterpret_cast<const uint32_t*>(codes.data_ptr());
   auto mp = reinterpret_cast<const uint32_t*>(meta.data_ptr());
   auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());

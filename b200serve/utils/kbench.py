@@ -174,8 +174,13 @@ def gemm_trace(M=32, N=4096, K=4096):
         out[n] = {"min": round(col.min().item(), 2), "med": round(col.median().item(), 2),
                   "max": round(col.max().item(), 2)}
     # per-CTA ordering checks: the exit stamp is taken after the final CTA barrier
+    t8 = buf.view(148, 8).cpu()[used]
     out["exit_before_epi"] = int((t[:, 6] < t[:, 5]).sum())
     out["exit_before_mma"] = int((t[:, 6] < t[:, 4]).sum())
+    # thread 32 (the MMA issuer's warp) stamps slot 7 after the same barrier: program order
+    # requires slot 7 >= slot 4; slot 6 vs slot 7 compares two threads leaving one barrier
+    out["mma_warp_exit_minus_mma_done_us"] = round(((t8[:, 7] - t8[:, 4]).float() / 1000).median().item(), 2)
+    out["thread0_exit_minus_thread32_exit_us"] = round(((t8[:, 6] - t8[:, 7]).float() / 1000).median().item(), 2)
     print(json.dumps(out))
 
 
@@ -205,6 +210,80 @@ def decode_step(layers=2, B=32, ctx=2304, iters=3):
     print(json.dumps({"case": "decode_step", "layers": layers, "B": B, "ctx": ctx, "eager_ms": round(ms, 3)}))
 
 
+def decode_parts(layers=8, B=32, ctx=2304):
+    """Per-layer device time of the decode step and of its parts, each captured as its own
+    CUDA graph of ``layers`` layers (weights and KV far larger than L2): the full forward, the
+    four GEMMs alone, attention alone, and the norm / RoPE kernels alone. Shows where the step
+    time goes relative to the HBM roofline of each part."""
+    from b200serve.engine.kv_cache import KVCache
+    from b200serve.models.config import get_model_config
+    from b200serve.models.qwen import Decoder, ForwardBatch
+    from b200serve.models.weights import random_weights
+    hbm, _, src = peaks()
+    cfg = get_model_config("qwen3-8b", layers)
+    w = random_weights(cfg, seed=0, device="cuda")
+    nb = (ctx + 32) // 16
+    kv = KVCache(cfg.num_layers, B * nb + 8, cfg.num_kv_heads, cfg.head_dim, device="cuda")
+    kv.k.normal_(0, 1)
+    kv.v.normal_(0, 1)
+    dec = Decoder(cfg, w, kv, device="cuda")
+    i32 = dict(dtype=torch.int32, device="cuda")
+    tables = torch.arange(B * nb, **i32).view(B, nb)
+    fb = ForwardBatch(input_ids=torch.ones(B, **i32), positions=torch.full((B,), ctx, **i32),
+                      slots=tables[:, ctx // 16] * 16 + ctx % 16, block_tables=tables,
+                      seq_lens=torch.full((B,), ctx + 1, **i32), logit_rows=None, is_decode=True)
+    plan = dec.decode_attn_plan(B, nb * 16)
+    ws = dec.ensure_attn_workspace(B, plan[1])
+    H, hd, nq, nkv = cfg.hidden_size, cfg.head_dim, dec.nq, dec.nkv
+    x = torch.randn(B, H, device="cuda").bfloat16()
+    a = torch.randn(B, nq * hd, device="cuda").bfloat16()
+    act = torch.randn(B, cfg.intermediate_size, device="cuda").bfloat16()
+    q = torch.randn(B, nq, hd, device="cuda").bfloat16()
+    qkv = torch.randn(B, (nq + 2 * nkv) * hd, device="cuda").bfloat16()
+    res = torch.randn(B, H, device="cuda").bfloat16()
+
+    def full():
+        dec.forward(fb, attn_plan=plan)
+
+    def gemms():
+        for lw in w.layers:
+            ops.linear(x, lw.qkv)
+            ops.linear(a, lw.o)
+            ops.linear(x, lw.gate_up, epilogue=ops.EPI_SWIGLU)
+            ops.linear(act, lw.down)
+
+    def attn():
+        for i in range(layers):
+            ops.paged_decode_attention(q, kv.k[i], kv.v[i], tables, fb.seq_lens, dec.scale, plan[0], plan[1], ws)
+
+    def small():
+        for i, lw in enumerate(w.layers):
+            ops.rmsnorm([x], lw.input_norm, cfg.rms_eps, residual=res, residual_out=res)
+            ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, dec.cos_sin, fb.positions, fb.slots, kv.k[i], kv.v[i],
+                         nq, nkv, cfg.rms_eps)
+            ops.rmsnorm([x], lw.post_norm, cfg.rms_eps, residual=res, residual_out=res)
+
+    wbytes = sum(t.N * t.K * 2 for lw in w.layers for t in (lw.qkv, lw.o, lw.gate_up, lw.down)) / layers
+    kvbytes = B * (ctx + 1) * nkv * hd * 2 * 2
+    ideal = {"full": (wbytes + kvbytes) / hbm / 1e3, "gemms": wbytes / hbm / 1e3, "attn": kvbytes / hbm / 1e3}
+    out = {"case": "decode_parts", "layers": layers, "B": B, "ctx": ctx, "peaks": src}
+    for name, fn in (("full", full), ("gemms", gemms), ("attn", attn), ("small", small)):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        ms = time_cuda(g.replay, iters=10, warmup=3)
+        us = ms * 1e3 / layers
+        out[name + "_us_per_layer"] = round(us, 2)
+        if name in ideal:
+            out[name + "_ideal_us"] = round(ideal[name], 2)
+            out[name + "_frac"] = round(ideal[name] / us, 3)
+        del g
+    print(json.dumps(out))
+
+
 if __name__ == "__main__":
     what = sys.argv[1] if len(sys.argv) > 1 else "all"
     ops.ext()
@@ -222,6 +301,9 @@ if __name__ == "__main__":
         sys.exit(0)
     if what == "sample_one":
         sample_one(*[int(v) for v in sys.argv[2:4]])
+        sys.exit(0)
+    if what == "decode_parts":
+        decode_parts(*[int(v) for v in sys.argv[2:5]])
         sys.exit(0)
     if what == "decode_step":
         decode_step(*[int(v) for v in sys.argv[2:5]])

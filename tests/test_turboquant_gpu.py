@@ -66,7 +66,7 @@ def test_tq_decode_attention_matches_cpu(nsplit):
                        [9, 0, 8, 1, 7, 2, 6, 3, 5, 4]], dtype=torch.int32, device="cuda")
     lens = torch.tensor([160, 97, 33], dtype=torch.int32, device="cuda")
     scale = 1 / math.sqrt(128)
-    tps = 64
+    tps = 64 if nsplit > 1 else 160          # splits x tokens-per-split must cover the longest sequence
     ws = ops.AttnWorkspace("cuda", B, nkv, G, 128, nsplit) if nsplit > 1 else None
     out = ops.tq_decode_attention(qr, qj, kv, 0, tb, bt, lens, scale, tps, nsplit, ws)
     torch.cuda.synchronize()
