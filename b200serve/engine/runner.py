@@ -58,8 +58,15 @@ class ModelRunner:
         raise ValueError(f"batch {n} > max_batch {self.max_batch}")
 
     def attn_plan(self, bucket: int):
+        """Tokens per split-KV chunk for a decode batch bucket. With at least one CTA per SM
+        from (sequence, kv head) pairs alone, whole sequences up to 4096 tokens stay in one
+        chunk (no combine pass: measured 54 vs 57 us per layer at B=32, 2.3k context);
+        smaller batches split a ~2k-token context over about one wave of CTAs."""
         per = bucket * self.decoder.nkv
-        tps = 64 if per <= 16 else 128 if per <= 64 else 256 if per <= 128 else 512
+        if per >= 148:
+            tps = 4096
+        else:
+            tps = min(4096, max(64, (2048 * per // 148 + 15) // 16 * 16))
         return tps, (self.max_seq + tps - 1) // tps
 
     def _decode_fb(self, bucket: int) -> ForwardBatch:

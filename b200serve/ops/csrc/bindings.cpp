@@ -58,7 +58,7 @@ void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optiona
              c10::optional<torch::Tensor> residual, torch::Tensor ws, torch::Tensor counters, int64_t epi,
              int64_t force_splits, int64_t packed_n);
 int64_t gemm_error_flag(bool reset);
-void gemm_set_trace(int64_t ptr);
+void gemm_set_trace(int64_t ptr, int64_t slots);
 void gemm_grouped(torch::Tensor act, torch::Tensor w_packed, int64_t N, int64_t E, torch::Tensor offsets,
                   int64_t max_rows, torch::Tensor out, torch::Tensor ws, torch::Tensor counters, int64_t epi);
 void argmax_rows(torch::Tensor logits, torch::Tensor out_idx, torch::Tensor out_val, int64_t index_offset);

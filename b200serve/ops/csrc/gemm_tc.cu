@@ -68,6 +68,13 @@ static void launch_by_bn(int BN, int epi, const CUtensorMap& tw, const CUtensorM
                          int grid, cudaStream_t stream) {
   GemmParams p = p0;
   if (p.stages <= 0) p.stages = ring_stages(BN);
+  static int l2_kb = -1;
+  if (l2_kb < 0) {
+    const char* e = getenv("B200_GEMM_L2_PREFETCH_KB");
+    l2_kb = e ? std::max(0, atoi(e)) : 0;
+  }
+  if (p.w_packed && !p.grouped) p.l2_prefetch_blocks = l2_kb / 16;
+  else p.w_ptr = nullptr;
   switch (BN) {
     case 16: launch_gemm_bn<16>(epi, tw, ta, p, grid, stream); break;
     case 32: launch_gemm_bn<32>(epi, tw, ta, p, grid, stream); break;
@@ -119,9 +126,22 @@ static CUtensorMap weight_tmap(const torch::Tensor& w, int N, int K, bool packed
   return make_tmap_bf16(w.data_ptr(), w.size(0), 64, 64, 128);
 }
 
-static unsigned long long* g_trace = nullptr;   // set by gemm_set_trace (diagnostics only)
+// Per-CTA timeline capture (diagnostics only): launch i writes [2048 CTAs][8] stamps at
+// g_trace + (i % g_trace_slots) * 2048 * 8.
+static unsigned long long* g_trace = nullptr;
+static int g_trace_slots = 1, g_trace_next = 0;
+static unsigned long long* next_trace() {
+  if (!g_trace) return nullptr;
+  unsigned long long* t = g_trace + (size_t)(g_trace_next % g_trace_slots) * 2048 * 8;
+  ++g_trace_next;
+  return t;
+}
 
-void gemm_set_trace(int64_t ptr) { g_trace = reinterpret_cast<unsigned long long*>(ptr); }
+void gemm_set_trace(int64_t ptr, int64_t slots) {
+  g_trace = reinterpret_cast<unsigned long long*>(ptr);
+  g_trace_slots = (int)std::max<int64_t>(1, slots);
+  g_trace_next = 0;
+}
 
 void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> bias,
              c10::optional<torch::Tensor> residual, torch::Tensor ws, torch::Tensor counters, int64_t epi,
@@ -148,8 +168,25 @@ void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optiona
     p.kb_per_split = (p.kb_total + force_splits - 1) / force_splits;
     p.splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
   }
+  // Cluster split-K for decode-sized tiles: one CTA per (tile, split), the splits of a tile
+  // (<= 8) form a thread-block cluster and reduce through distributed shared memory.
+  static int cluster_mode = -1;
+  if (cluster_mode < 0) {
+    const char* e = getenv("B200_GEMM_CLUSTER");
+    cluster_mode = e ? atoi(e) : 0;   // measured slower than the workspace fixup at decode sizes
+  }
+  if (cluster_mode && force_splits <= 0 && BN <= 64 && p.m_tiles == 1 && epi != EPI_PUSH) {
+    const int tiles = p.n_tiles;
+    int s = std::min(8, std::max(1, (2 * g_num_sms) / tiles));
+    while (s > 1 && (p.kb_total + s - 1) / s < 4) --s;
+    if (s > 1) {
+      p.kb_per_split = (p.kb_total + s - 1) / s;
+      p.splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
+      p.cluster_red = p.splits > 1 ? 1 : 0;
+    }
+  }
   p.units = p.m_tiles * p.n_tiles * p.splits;
-  const int grid = std::min(p.units, g_num_sms);
+  const int grid = p.cluster_red ? p.units : std::min(p.units, g_num_sms);
   p.out = out.data_ptr();
   p.ldo = out.stride(0);
   p.bias = bias ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
@@ -161,7 +198,7 @@ void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optiona
     TORCH_CHECK(out.scalar_type() == at::kBFloat16);
   }
   if (epi == EPI_SWIGLU) TORCH_CHECK(N % 128 == 0 && out.size(1) == N / 2, "SwiGLU needs N % 128 == 0");
-  if (p.splits > 1) {
+  if (p.splits > 1 && !p.cluster_red) {
     TORCH_CHECK(ws.scalar_type() == at::kFloat &&
                     ws.numel() >= (int64_t)p.splits * p.m_tiles * p.n_tiles * BN * 128,
                 "GEMM workspace too small");
@@ -172,7 +209,8 @@ void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optiona
   }
   p.err = gemm_err_word();
   p.w_packed = packed ? 1 : 0;
-  p.trace = g_trace;
+  p.w_ptr = packed ? reinterpret_cast<const uint8_t*>(w.data_ptr()) : nullptr;
+  p.trace = next_trace();
   CUtensorMap tw = weight_tmap(w, N, K, packed);
   CUtensorMap ta = make_tmap_bf16(act.data_ptr(), M, K, act.stride(0), BN);
   auto stream = at::cuda::getCurrentCUDAStream();
@@ -223,6 +261,7 @@ void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, in
   p.tile_done = tile_done.data_ptr<int>();
   p.err = err_ptr ? reinterpret_cast<int*>(err_ptr) : gemm_err_word();
   p.w_packed = packed ? 1 : 0;
+  p.w_ptr = packed ? reinterpret_cast<const uint8_t*>(w.data_ptr()) : nullptr;
   CUtensorMap tw = weight_tmap(w, N, K, packed);
   CUtensorMap ta = make_tmap_bf16(act.data_ptr(), M, K, act.stride(0), BN);
   launch_by_bn(BN, EPI_PUSH, tw, ta, p, grid, at::cuda::getCurrentCUDAStream());

@@ -43,6 +43,9 @@ struct GemmParams {
   int g_E;
   int n_tiles, m_tiles, splits, kb_per_split, kb_total, units;
   int stages;                   // shared-memory ring depth (set by the host launcher)
+  int cluster_red;              // 1: the splits of a tile form one cluster and reduce through DSMEM
+  const uint8_t* w_ptr;         // packed weight base (L2 prefetch), or null
+  int l2_prefetch_blocks;       // weight tiles per CTA prefetched into L2 before the dependency wait
   void* out;                    // bf16 or fp32, row stride ldo (elements)
   int ldo;
   const __nv_bfloat16* bias;    // [N] or null
@@ -63,7 +66,7 @@ struct GemmParams {
 };
 
 __device__ __forceinline__ void trace_mark(const GemmParams& p, int slot) {
-  if (p.trace) p.trace[blockIdx.x * 8 + slot] = globaltimer_ns();
+  if (p.trace && blockIdx.x < 2048) p.trace[blockIdx.x * 8 + slot] = globaltimer_ns();
 }
 
 
@@ -211,6 +214,34 @@ __device__ __forceinline__ void publish_tile(const GemmParams& p, int* scratch) 
   epi_bar();
 }
 
+// Cluster split-K: every CTA of the cluster (one K split of the same tile) has staged its fp32
+// partial tile [BN][128] at the start of its shared memory. CTA rank r sums token columns
+// [r*ceil(BN/S), ...) over the S partials through distributed shared memory and runs the final
+// epilogue for them, so the tile is reduced in parallel without a global workspace round trip.
+template <int BN, int EPI>
+__device__ __forceinline__ void cluster_reduce_store(const GemmParams& p, const uint8_t* red_smem, float* xchg,
+                                                     int row, int quad, int lane) {
+  const Unit x = decode_unit(p, blockIdx.x, BN);
+  const int S = p.splits;
+  const int r = (int)tc::cluster_ctarank();
+  const int cpc = (BN + S - 1) / S;
+  const int c_lo = r * cpc, c_hi = min(BN, c_lo + cpc);
+  const int t_tile_end = x.a_row0 + min(x.m_lim, BN);
+  const uint32_t base = tc::smem_u32(red_smem);
+  for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = 0.f;
+    for (int sp = 0; sp < S; ++sp) {
+      const uint32_t rb = tc::map_shared_rank(base, (uint32_t)sp);
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (c0 + j < c_hi) v[j] += tc::ld_shared_cluster_f32(rb + (uint32_t)(((c0 + j) * 128 + row) * 4));
+    }
+    epilogue_store<EPI>(p, v, row, x.n_tile, x.a_row0 + c0, min(t_tile_end, x.a_row0 + c_hi), xchg, quad, lane);
+  }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 2)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
@@ -278,6 +309,19 @@ __global__ void __launch_bounds__(192, 2)
         for (int i = 0; i < pre; ++i) {
           tc::mbar_arrive_expect_tx(&full[i], Cfg::STAGE_BYTES);
           tc::tma_load_2d(s_w + i * Cfg::W_BYTES, &tm_w, &full[i], w_x(p, kb0 + i), w_y(p, x.w_tile_base, kb0 + i), pol_w);
+        }
+        // Stream further weight tiles of this CTA's units into L2 while the previous kernel
+        // finishes (tile-packed weights: each 128 x 64 tile is one contiguous 16 KB run).
+        if (p.w_ptr && p.l2_prefetch_blocks > 0) {
+          int budget = p.l2_prefetch_blocks;
+          for (int u = blockIdx.x; u < p.units && budget > 0; u += gridDim.x) {
+            const Unit y = decode_unit(p, u, BN);
+            const int a0 = y.split * p.kb_per_split + (u == (int)blockIdx.x ? pre : 0);
+            const int a1 = min(p.kb_total, y.split * p.kb_per_split + p.kb_per_split);
+            for (int kb = a0; kb < a1 && budget > 0; ++kb, --budget)
+              tc::prefetch_l2(p.w_ptr + ((size_t)y.w_tile_base * p.kb_total + kb) * (size_t)Cfg::W_BYTES,
+                              Cfg::W_BYTES);
+          }
         }
         pdl_wait();
         for (int i = 0; i < pre; ++i)
@@ -370,6 +414,19 @@ __global__ void __launch_bounds__(192, 2)
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&tempty[acc]);
         if constexpr (EPI == EPI_PUSH) publish_tile(p, last_flag);
+      } else if (p.cluster_red) {
+        // partial tile -> this CTA's shared memory (the drained stage ring), reduced after the
+        // cluster barrier below
+        float* red = reinterpret_cast<float*>(smem);
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tc::tmem_ld16(t_row + c0, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) red[(c0 + j) * 128 + row] = v[j];
+        }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&tempty[acc]);
       } else {
         // partial tile -> workspace [split][tile][BN][128] (coalesced over the 128 features)
         float* ws_mine = p.ws + ((size_t)x.split * total_tiles + x.tile) * BN * 128;
@@ -424,6 +481,18 @@ __global__ void __launch_bounds__(192, 2)
     }
   }
   if (threadIdx.x == 64) trace_mark(p, 5);
+  if constexpr (BN <= 64 && EPI != EPI_PUSH) {
+    if (p.cluster_red) {
+      // every CTA reaches both barriers, also after a timed-out wait (no cluster member may
+      // exit while a peer still reads its shared memory)
+      tc::cluster_sync();
+      if (warp >= 2 && !*abort_flag) {
+        const int quad = warp & 3;
+        cluster_reduce_store<BN, EPI>(p, smem, xchg, quad * 32 + lane, quad, lane);
+      }
+      tc::cluster_sync();
+    }
+  }
   tc::tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) trace_mark(p, 6);
@@ -452,7 +521,11 @@ void launch_gemm(const CUtensorMap& tw, const CUtensorMap& ta, const GemmParams&
   }
   TORCH_CHECK(p.stages >= 2 && p.stages <= Cfg::MAX_STAGES && Cfg::smem(p.stages) <= 227 * 1024,
               "GEMM stage count out of range");
-  launch_pdl(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(192), Cfg::smem(p.stages), stream, tw, ta, p);
+  if (p.cluster_red)
+    launch_pdl_cluster(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(192), Cfg::smem(p.stages), stream, p.splits, tw,
+                       ta, p);
+  else
+    launch_pdl(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(192), Cfg::smem(p.stages), stream, tw, ta, p);
 }
 
 // one translation unit per BN (gemm_tc_bn*.cu) instantiates this for every epilogue

@@ -150,18 +150,18 @@ def gemm_trace(M=32, N=4096, K=4096):
     x = torch.randn(M, K, device="cuda").bfloat16()
     w = ops.pack_weight((torch.randn(N, K, device="cuda") * 0.02).bfloat16())
     y = ops.linear(x, w)
-    buf = torch.zeros(148 * 8, dtype=torch.int64, device="cuda")
+    buf = torch.zeros(2048 * 8, dtype=torch.int64, device="cuda")     # >= grid size x 8 slots
     from b200serve.utils.timing import L2Flusher
     fl = L2Flusher()
     for _ in range(3):
         ops.linear(x, w, out=y)
     fl()
     torch.cuda.synchronize()
-    ops.ext().gemm_set_trace(buf.data_ptr())
+    ops.ext().gemm_set_trace(buf.data_ptr(), 1)
     ops.linear(x, w, out=y)
     torch.cuda.synchronize()
-    ops.ext().gemm_set_trace(0)
-    t = buf.view(148, 8)[:, :7].cpu()
+    ops.ext().gemm_set_trace(0, 1)
+    t = buf.view(-1, 8)[:, :7].cpu()
     used = t[:, 0] > 0
     t = t[used]
     t0 = t[:, 0].min()
@@ -174,7 +174,7 @@ def gemm_trace(M=32, N=4096, K=4096):
         out[n] = {"min": round(col.min().item(), 2), "med": round(col.median().item(), 2),
                   "max": round(col.max().item(), 2)}
     # per-CTA ordering checks: the exit stamp is taken after the final CTA barrier
-    t8 = buf.view(148, 8).cpu()[used]
+    t8 = buf.view(-1, 8).cpu()[used]
     out["exit_before_epi"] = int((t[:, 6] < t[:, 5]).sum())
     out["exit_before_mma"] = int((t[:, 6] < t[:, 4]).sum())
     # thread 32 (the MMA issuer's warp) stamps slot 7 after the same barrier: program order
@@ -208,6 +208,58 @@ def decode_step(layers=2, B=32, ctx=2304, iters=3):
     torch.cuda.synchronize()
     ms = time_cuda(lambda: r.decode(ids, pos, slots, tables, lens, greedy=True), iters=10, warmup=2)
     print(json.dumps({"case": "decode_step", "layers": layers, "B": B, "ctx": ctx, "eager_ms": round(ms, 3)}))
+
+
+def gemm_chain_trace(layers=2, B=32):
+    """Per-CTA timelines of the four decode GEMMs of ``layers`` Qwen3-8B layers captured in one
+    CUDA graph (back to back, as in the decode step): for each launch, when its CTAs start,
+    when the first weight tile lands, when the MMAs end and when the CTAs exit, relative to
+    the first launch. Shows how much of each GEMM overlaps its predecessor."""
+    from b200serve.models.config import get_model_config
+    cfg = get_model_config("qwen3-8b", layers)
+    H, I = cfg.hidden_size, cfg.intermediate_size
+    nq, nkv, hd = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+    mk = lambda n, k: ops.pack_weight((torch.randn(n, k, device="cuda") * 0.02).bfloat16())
+    Ws = [(mk((nq + 2 * nkv) * hd, H), mk(H, nq * hd), mk(2 * I, H), mk(H, I)) for _ in range(layers)]
+    x = torch.randn(B, H, device="cuda").bfloat16()
+    a = torch.randn(B, nq * hd, device="cuda").bfloat16()
+    act = torch.randn(B, I, device="cuda").bfloat16()
+
+    def chain():
+        for qkv, o, gu, dn in Ws:
+            ops.linear(x, qkv)
+            ops.linear(a, o)
+            ops.linear(x, gu, epilogue=ops.EPI_SWIGLU)
+            ops.linear(act, dn)
+
+    chain()
+    torch.cuda.synchronize()
+    n = 4 * layers
+    buf = torch.zeros(n * 2048 * 8, dtype=torch.int64, device="cuda")
+    ops.ext().gemm_set_trace(buf.data_ptr(), n)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        chain()
+    ops.ext().gemm_set_trace(0, 1)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    t = buf.view(n, 2048, 8).cpu()
+    t0 = min(int(t[i, :, 0][t[i, :, 0] > 0].min()) for i in range(n))
+    names = ["qkv", "o", "gate_up", "down"]
+    rows = []
+    for i in range(n):
+        ti = t[i]
+        ok = ti[:, 0] > 0
+        ti = ti[ok]
+        us = lambda col, f: round((float(f(ti[:, col].float())) - t0) / 1000.0, 2)
+        rows.append({"gemm": names[i % 4], "layer": i // 4, "ctas": int(ok.sum()),
+                     "entry_min": us(0, torch.min), "entry_max": us(0, torch.max),
+                     "first_data_med": us(3, torch.median), "mma_done_max": us(4, torch.max),
+                     "exit_max": us(6, torch.max)})
+    for r in rows:
+        print(json.dumps(r))
+    del g
 
 
 def decode_parts(layers=8, B=32, ctx=2304):
@@ -281,6 +333,22 @@ def decode_parts(layers=8, B=32, ctx=2304):
             out[name + "_ideal_us"] = round(ideal[name], 2)
             out[name + "_frac"] = round(ideal[name] / us, 3)
         del g
+    # attention alone at other split sizes (tokens per split): fewer splits skip the combine pass
+    for tps in (256, 1024, (nb * 16 + 15) // 16 * 16):
+        ns = (nb * 16 + tps - 1) // tps
+        ws2 = ops.AttnWorkspace("cuda", B, nkv, nq // nkv, hd, ns) if ns > 1 else None
+
+        def attn2():
+            for i in range(layers):
+                ops.paged_decode_attention(q, kv.k[i], kv.v[i], tables, fb.seq_lens, dec.scale, tps, ns, ws2)
+
+        attn2()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            attn2()
+        out[f"attn_tps{tps}_us"] = round(time_cuda(g.replay, iters=10, warmup=3) * 1e3 / layers, 2)
+        del g
     print(json.dumps(out))
 
 
@@ -301,6 +369,9 @@ if __name__ == "__main__":
         sys.exit(0)
     if what == "sample_one":
         sample_one(*[int(v) for v in sys.argv[2:4]])
+        sys.exit(0)
+    if what == "gemm_chain_trace":
+        gemm_chain_trace(*[int(v) for v in sys.argv[2:4]])
         sys.exit(0)
     if what == "decode_parts":
         decode_parts(*[int(v) for v in sys.argv[2:5]])

@@ -73,7 +73,7 @@ def _single(greedy):
         eng.unload()
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4])
 def test_tp_greedy_matches_single_rank(world):
     assert _run_tp(world, True) == _single(True)
 
