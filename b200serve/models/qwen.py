@@ -214,6 +214,54 @@ class Decoder:
             return ops.paged_decode_attention(q, kd, vd, fb.block_tables, fb.seq_lens, self.scale)
         return ops.paged_prefill_attention(q, kd, vd, fb.block_tables, fb.seq_lens, fb.q_start, fb.cu_q, self.scale)
 
+    def _attend(self, i, qkv, lw, fb, T, plan, tq_pre):
+        """QKV post-processing, KV write and attention of layer ``i`` -> [T, nq, hd]."""
+        tps, nsplit, ws = plan
+        eps = self.cfg.rms_eps
+        if self.tq is not None:
+            return self._attention_tq(i, qkv, lw, fb, T, tps, nsplit, ws, tq_pre)
+        if self.kv.kv_format == "int4g128":
+            return self._attention_q4(i, qkv, lw, fb, T, tps, nsplit, ws)
+        kc, vc = self.kv.k[i], self.kv.v[i]
+        q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots, kc, vc,
+                         self.nq, self.nkv, eps)
+        if fb.is_decode:
+            return ops.paged_decode_attention(q, kc, vc, fb.block_tables, fb.seq_lens, self.scale, tps, nsplit, ws)
+        return ops.paged_prefill_attention(q, kc, vc, fb.block_tables, fb.seq_lens, fb.q_start, fb.cu_q,
+                                           self.scale, max_q=fb.max_q)
+
+    def _forward_rsag(self, fb, h, plan, tq_pre):
+        """Tensor-parallel forward on a token-sharded residual stream (sequence parallelism for
+        the norms): each row-parallel GEMM reduce-scatters its output to the token owners
+        (GEMM -> RS), each norm runs on the owned rows only and all-gathers its output into
+        every rank's activation buffer (norm -> AG), and the next column-parallel GEMM waits
+        for the gathered rows inside the kernel while it already streams its weights
+        (AG -> GEMM). Layer 0's input norm runs on every rank (the embedding is replicated)."""
+        cfg, w, comm = self.cfg, self.w, self.comm
+        eps = cfg.rms_eps
+        T = h.shape[0]
+        Tw, row0, cnt = comm.shard(T)
+        residual = torch.zeros(Tw, h.shape[1], dtype=h.dtype, device=h.device)
+        residual[:cnt] = h[row0:row0 + cnt]
+        x, ag = ops.rmsnorm([h], w.layers[0].input_norm, eps), None
+        parts = None
+        for i, lw in enumerate(w.layers):
+            if i > 0:
+                x, ag = comm.norm_ag(parts, lw.input_norm, eps, residual)
+            qkv = ops.linear(x, lw.qkv, bias=lw.qkv_bias, ag=ag)
+            attn = self._attend(i, qkv, lw, fb, T, plan, tq_pre)
+            parts = comm.rs_linear(attn.view(T, self.nq * self.hd), lw.o, "o")
+            x, ag = comm.norm_ag(parts, lw.post_norm, eps, residual)
+            act = ops.linear(x, lw.gate_up, epilogue=ops.EPI_SWIGLU, ag=ag)
+            parts = comm.rs_linear(act, lw.down, "mlp")
+        x, ag = comm.norm_ag(parts, w.final_norm, eps, residual)
+        rows = fb.logit_rows
+        if rows is not None:
+            if ag is not None:
+                ag.wait()
+            x, ag = x.index_select(0, rows), None
+        return ops.linear(x, w.lm_head, epilogue=ops.EPI_F32, ag=ag)
+
     def _row_parallel(self, x, w, tag):
         """Row-parallel linear whose output is summed over tensor-parallel ranks."""
         if hasattr(self.comm, "linear_reduce"):
@@ -230,33 +278,20 @@ class Decoder:
         if hasattr(comm, "begin_step"):
             comm.begin_step()
         h = ops.embedding(fb.input_ids, w.embed)
-        residual = torch.empty_like(h)
-        x = ops.rmsnorm([h], w.layers[0].input_norm, eps, residual_out=residual)
         if fb.is_decode:
             tps, nsplit = attn_plan or self.decode_attn_plan(T, int(fb.block_tables.shape[1]) * 16)
             ws = self.ensure_attn_workspace(T, nsplit) if nsplit > 1 else None
-        k_all, v_all = self.kv.k, self.kv.v
         tq_pre = self._tq_prefill_pages(fb) if (self.tq is not None and not fb.is_decode) else None
+        plan = (tps, nsplit, ws) if fb.is_decode else (0, 0, None)
+        if self.moe is None and comm.world > 1 and hasattr(comm, "use_rsag") and comm.use_rsag(T):
+            return self._forward_rsag(fb, h, plan, tq_pre)
+        residual = torch.empty_like(h)
+        x = ops.rmsnorm([h], w.layers[0].input_norm, eps, residual_out=residual)
         for i, lw in enumerate(w.layers):
             if i > 0:
                 x = ops.rmsnorm(mlp_parts, lw.input_norm, eps, residual=residual, residual_out=residual)
             qkv = ops.linear(x, lw.qkv, bias=lw.qkv_bias)
-            kc, vc = k_all[i], v_all[i]
-            if self.tq is not None:
-                attn = self._attention_tq(i, qkv, lw, fb, T, tps if fb.is_decode else 0,
-                                          nsplit if fb.is_decode else 0, ws if fb.is_decode else None, tq_pre)
-            elif self.kv.kv_format == "int4g128":
-                attn = self._attention_q4(i, qkv, lw, fb, T, tps if fb.is_decode else 0,
-                                          nsplit if fb.is_decode else 0, ws if fb.is_decode else None)
-            else:
-                q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots, kc, vc,
-                                 self.nq, self.nkv, eps)
-                if fb.is_decode:
-                    attn = ops.paged_decode_attention(q, kc, vc, fb.block_tables, fb.seq_lens, self.scale, tps,
-                                                      nsplit, ws)
-                else:
-                    attn = ops.paged_prefill_attention(q, kc, vc, fb.block_tables, fb.seq_lens, fb.q_start,
-                                                       fb.cu_q, self.scale, max_q=fb.max_q)
+            attn = self._attend(i, qkv, lw, fb, T, plan, tq_pre)
             o_parts = self._row_parallel(attn.view(T, self.nq * self.hd), lw.o, "o")
             x = ops.rmsnorm(o_parts, lw.post_norm, eps, residual=residual, residual_out=residual)
             if self.moe is not None:

@@ -319,13 +319,41 @@ def pack_weight(w):
     return PackedWeight(w)
 
 
-def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspace=None, splits=0):
+class AGWait:
+    """Rows of an activation that peers are still pushing (all-gather): consumers wait until
+    ``n`` flags at ``flags_ptr`` hold the step epoch at ``epoch_ptr``."""
+
+    def __init__(self, flags_ptr: int, n: int, epoch_ptr: int, err_ptr: int = 0):
+        self.flags_ptr, self.n, self.epoch_ptr, self.err_ptr = flags_ptr, n, epoch_ptr, err_ptr
+
+    def wait(self):
+        """Make the current stream wait for the gathered rows (a one-thread kernel)."""
+        _launches[0] += 1
+        ext().flag_wait(self.flags_ptr, self.n, self.epoch_ptr, self.err_ptr)
+
+
+def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspace=None, splits=0, ag=None):
     """y = x @ w^T (+bias) (+residual) with x [M, K], w [N, K].
 
     epilogue EPI_F32 writes fp32 (logits); EPI_SWIGLU treats w as the 64-row
     interleaved gate/up weight and writes silu(gate)*up of width N/2.
+    ``ag`` (AGWait): x is being all-gathered by the peers; the tcgen05 GEMM streams its
+    weights and waits inside the kernel, other paths wait with a flag kernel first.
     """
     M, K = x.shape
+    if ag is not None and x.is_cuda:
+        fused = isinstance(w, PackedWeight) and residual is None and splits == 0
+        if not fused:
+            ag.wait()
+            return linear(x, w, bias, residual, epilogue, out, workspace, splits)
+        if out is None:
+            out = torch.empty(M, w.N // 2 if epilogue == EPI_SWIGLU else w.N,
+                              dtype=torch.float32 if epilogue == EPI_F32 else x.dtype, device=x.device)
+        ws = workspace or default_workspace(x.device)
+        _cuda(x)
+        ext().gemm_tc_ag(x, w.data, out, bias, ws.ws, ws.counters, epilogue, w.N, ag.flags_ptr, ag.n,
+                         ag.epoch_ptr)
+        return out
     if isinstance(w, list):                         # QuantGroup: parts share the input
         if epilogue == EPI_SWIGLU:
             g, u = (linear(x, p) for p in w)

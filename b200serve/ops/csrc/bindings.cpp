@@ -8,7 +8,7 @@ void rmsnorm_fused_wait(std::vector<torch::Tensor> parts, c10::optional<torch::T
                         int64_t flags_ptr, int64_t epoch_ptr, int64_t err_ptr);
 void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, int64_t ldo, torch::Tensor flag_ptrs,
                   int64_t epoch_ptr, torch::Tensor tile_done, c10::optional<torch::Tensor> bias, torch::Tensor ws,
-                  torch::Tensor counters, int64_t err_ptr, int64_t packed_n);
+                  torch::Tensor counters, int64_t err_ptr, int64_t packed_n, int64_t rs_rows);
 int64_t ipc_malloc(int64_t bytes);
 void ipc_free(int64_t ptr);
 torch::Tensor ipc_handle(int64_t ptr);
@@ -79,11 +79,23 @@ void tq_dequant(torch::Tensor block_ids, torch::Tensor k_codes, torch::Tensor k_
                 torch::Tensor v_codes, torch::Tensor v_meta, torch::Tensor S, torch::Tensor code_vals,
                 torch::Tensor out_k, torch::Tensor out_v);
 
+void gemm_tc_ag(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> bias,
+                torch::Tensor ws, torch::Tensor counters, int64_t epi, int64_t packed_n, int64_t ag_flags_ptr,
+                int64_t ag_n, int64_t ag_epoch_ptr);
+
+void rmsnorm_rs_ag(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
+                   c10::optional<torch::Tensor> residual_out, torch::Tensor w, double eps, int64_t flags_ptr,
+                   int64_t epoch_ptr, int64_t err_ptr, torch::Tensor dst_ptrs, torch::Tensor ag_flag_ptrs,
+                   int64_t row0, int64_t T, torch::Tensor done);
+
+void flag_wait(int64_t flags_ptr, int64_t n, int64_t epoch_ptr, int64_t err_ptr);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "b200serve sm_100a kernels";
   m.def("rmsnorm_fused", &rmsnorm_fused);
   m.def("qkv_post", &qkv_post);
   m.def("rmsnorm_fused_wait", &rmsnorm_fused_wait);
+  m.def("rmsnorm_rs_ag", &rmsnorm_rs_ag);
   m.def("gemm_tc_push", &gemm_tc_push);
   m.def("ipc_malloc", &ipc_malloc);
   m.def("ipc_free", &ipc_free);
@@ -93,6 +105,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("host_error_word", &host_error_word);
   m.def("read_host_word", &read_host_word);
   m.def("epoch_inc", &epoch_inc);
+  m.def("flag_wait", &flag_wait);
   m.def("silu_mul", &silu_mul);
   m.def("embedding", &embedding);
   m.def("paged_decode_attention", &paged_decode_attention);
@@ -108,6 +121,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_prefill_attention_q4", &paged_prefill_attention_q4);
   m.def("gemm_plan", &gemm_plan);
   m.def("gemm_tc", &gemm_tc);
+  m.def("gemm_tc_ag", &gemm_tc_ag);
   m.def("gemm_error_flag", &gemm_error_flag);
   m.def("gemm_set_trace", &gemm_set_trace);
   m.def("gemm_grouped", &gemm_grouped);

@@ -24,9 +24,37 @@ __global__ void epoch_inc_kernel(int* epoch) {
   if (threadIdx.x == 0) *epoch += 1;
 }
 
+// One thread waits (bounded, 2 s) until flags[0..n) all hold *epoch: orders a consumer that
+// cannot wait by itself (a library kernel) after the peers' all-gather pushes.
+__global__ void flag_wait_kernel(const int* flags, int n, const int* epoch, int* err) {
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x != 0) return;
+  const int e = *epoch;
+  const uint64_t deadline = globaltimer_ns() + 2000000000ull;
+  for (int r = 0; r < n; ++r) {
+    uint32_t it = 0;
+    while (true) {
+      int v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
+      if (v == e) break;
+      if ((++it & 1023u) == 0 && globaltimer_ns() > deadline) {
+        if (err) atomicExch(err, 140 + r);
+        return;
+      }
+    }
+  }
+}
+
 }  // namespace b200
 
 using namespace b200;
+
+void flag_wait(int64_t flags_ptr, int64_t n, int64_t epoch_ptr, int64_t err_ptr) {
+  launch_pdl(flag_wait_kernel, dim3(1), dim3(32), 0, at::cuda::getCurrentCUDAStream(),
+             reinterpret_cast<const int*>(flags_ptr), (int)n, reinterpret_cast<const int*>(epoch_ptr),
+             reinterpret_cast<int*>(err_ptr));
+}
 
 int64_t ipc_malloc(int64_t bytes) {
   void* p = nullptr;

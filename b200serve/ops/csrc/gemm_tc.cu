@@ -143,9 +143,10 @@ void gemm_set_trace(int64_t ptr, int64_t slots) {
   g_trace_next = 0;
 }
 
-void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> bias,
-             c10::optional<torch::Tensor> residual, torch::Tensor ws, torch::Tensor counters, int64_t epi,
-             int64_t force_splits, int64_t packed_n) {
+static void gemm_tc_impl(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> bias,
+                         c10::optional<torch::Tensor> residual, torch::Tensor ws, torch::Tensor counters, int64_t epi,
+                         int64_t force_splits, int64_t packed_n, const int* ag_flags, int ag_n,
+                         const int* ag_epoch) {
   TORCH_CHECK(act.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16);
   TORCH_CHECK(act.dim() == 2 && w.dim() == 2 && act.stride(1) == 1 && w.is_contiguous());
   const bool packed = packed_n > 0;
@@ -210,6 +211,9 @@ void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optiona
   p.err = gemm_err_word();
   p.w_packed = packed ? 1 : 0;
   p.w_ptr = packed ? reinterpret_cast<const uint8_t*>(w.data_ptr()) : nullptr;
+  p.ag_flags = ag_flags;
+  p.ag_n = ag_n;
+  p.ag_epoch = ag_epoch;
   p.trace = next_trace();
   CUtensorMap tw = weight_tmap(w, N, K, packed);
   CUtensorMap ta = make_tmap_bf16(act.data_ptr(), M, K, act.stride(0), BN);
@@ -217,12 +221,29 @@ void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optiona
   launch_by_bn(BN, (int)epi, tw, ta, p, grid, stream);
 }
 
+void gemm_tc(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> bias,
+             c10::optional<torch::Tensor> residual, torch::Tensor ws, torch::Tensor counters, int64_t epi,
+             int64_t force_splits, int64_t packed_n) {
+  gemm_tc_impl(act, w, out, bias, residual, ws, counters, epi, force_splits, packed_n, nullptr, 0, nullptr);
+}
+
+// All-gather -> GEMM: the activation rows are written by the ranks' norm kernels (P2P pushes);
+// the kernel streams its weights right away and loads activations once every rank's flag at
+// ag_flags_ptr[0..ag_n) holds the step epoch at ag_epoch_ptr.
+void gemm_tc_ag(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> bias,
+                torch::Tensor ws, torch::Tensor counters, int64_t epi, int64_t packed_n, int64_t ag_flags_ptr,
+                int64_t ag_n, int64_t ag_epoch_ptr) {
+  TORCH_CHECK(ag_flags_ptr && ag_epoch_ptr && ag_n >= 1 && ag_n <= kMaxPeers, "bad all-gather flags");
+  gemm_tc_impl(act, w, out, bias, c10::nullopt, ws, counters, epi, 0, packed_n,
+               reinterpret_cast<const int*>(ag_flags_ptr), (int)ag_n, reinterpret_cast<const int*>(ag_epoch_ptr));
+}
+
 // Tensor-parallel GEMM whose epilogue pushes the bf16 output tile into the
 // receive slot of every rank (P2P stores) and raises per-rank flags once the
 // whole output is pushed. dst_ptrs/flag_ptrs: int64 [world] device addresses.
 void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, int64_t ldo, torch::Tensor flag_ptrs,
                   int64_t epoch_ptr, torch::Tensor tile_done, c10::optional<torch::Tensor> bias, torch::Tensor ws,
-                  torch::Tensor counters, int64_t err_ptr, int64_t packed_n) {
+                  torch::Tensor counters, int64_t err_ptr, int64_t packed_n, int64_t rs_rows) {
   TORCH_CHECK(act.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16);
   const bool packed = packed_n > 0;
   const int M = act.size(0), K = act.size(1), N = packed ? (int)packed_n : w.size(0);
@@ -259,6 +280,8 @@ void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, in
   }
   p.epoch = reinterpret_cast<const int*>(epoch_ptr);
   p.tile_done = tile_done.data_ptr<int>();
+  p.rs_rows = (int)rs_rows;
+  TORCH_CHECK(rs_rows == 0 || (int64_t)rs_rows * world >= M, "reduce-scatter rows do not cover the tokens");
   p.err = err_ptr ? reinterpret_cast<int*>(err_ptr) : gemm_err_word();
   p.w_packed = packed ? 1 : 0;
   p.w_ptr = packed ? reinterpret_cast<const uint8_t*>(w.data_ptr()) : nullptr;

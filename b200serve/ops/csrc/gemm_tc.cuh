@@ -44,6 +44,13 @@ struct GemmParams {
   int n_tiles, m_tiles, splits, kb_per_split, kb_total, units;
   int stages;                   // shared-memory ring depth (set by the host launcher)
   int cluster_red;              // 1: the splits of a tile form one cluster and reduce through DSMEM
+  // EPI_PUSH as reduce-scatter: token row t goes only to rank t / rs_rows, at row t % rs_rows
+  int rs_rows;
+  // all-gather -> GEMM: the activation rows arrive from peers; the producer waits until
+  // ag_flags[0..ag_n) all hold *ag_epoch before loading any activation tile
+  const int* ag_flags;
+  int ag_n;
+  const int* ag_epoch;
   const uint8_t* w_ptr;         // packed weight base (L2 prefetch), or null
   int l2_prefetch_blocks;       // weight tiles per CTA prefetched into L2 before the dependency wait
   void* out;                    // bf16 or fp32, row stride ldo (elements)
@@ -134,8 +141,13 @@ __device__ __forceinline__ void epilogue_store(const GemmParams& p, float* v, in
       const int t = t0 + tok, col = n_tile * 128 + chunk * 8;
       if (t < t_end && col < p.N) {
         const uint4 val = *reinterpret_cast<const uint4*>(xs + tok * 136 + chunk * 8);
-        for (int r = 0; r < p.world; ++r)
-          *reinterpret_cast<uint4*>(p.push_dst[r] + (size_t)t * p.ldo + col) = val;
+        if (p.rs_rows > 0) {
+          const int owner = t / p.rs_rows;
+          *reinterpret_cast<uint4*>(p.push_dst[owner] + (size_t)(t - owner * p.rs_rows) * p.ldo + col) = val;
+        } else {
+          for (int r = 0; r < p.world; ++r)
+            *reinterpret_cast<uint4*>(p.push_dst[r] + (size_t)t * p.ldo + col) = val;
+        }
       }
     }
     epi_bar();
@@ -193,6 +205,28 @@ __device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int BN) 
 __device__ __forceinline__ int w_x(const GemmParams& p, int kb) { return p.w_packed ? 0 : kb * 64; }
 __device__ __forceinline__ int w_y(const GemmParams& p, int w_tile, int kb) {
   return p.w_packed ? (w_tile * p.kb_total + kb) * 128 : w_tile * 128;
+}
+
+// All-gather -> GEMM: spin (bounded, 2 s) until every rank published this step's epoch for the
+// gathered activation rows, then order the async proxy (TMA) after those acquires.
+__device__ __forceinline__ bool wait_ag_flags(const GemmParams& p, volatile int* abort_flag, int* err) {
+  const int e = *p.ag_epoch;
+  const uint64_t deadline = globaltimer_ns() + 2000000000ull;
+  for (int r = 0; r < p.ag_n; ++r) {
+    uint32_t it = 0;
+    while (true) {
+      int v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p.ag_flags + r) : "memory");
+      if (v == e) break;
+      if ((++it & 1023u) == 0 && globaltimer_ns() > deadline) {
+        atomicExch(err, 120 + r);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
 }
 
 // EPI_PUSH: after a tile's stores reached every peer, count it; the CTA that
@@ -324,6 +358,7 @@ __global__ void __launch_bounds__(192, 2)
           }
         }
         pdl_wait();
+        if (p.ag_flags) wait_ag_flags(p, abort_flag, err);
         for (int i = 0; i < pre; ++i)
           tc::tma_load_2d(s_a + i * Cfg::A_BYTES, &tm_a, &full[i], (kb0 + i) * 64, x.a_row0, pol_a);
         trace_mark(p, 2);
@@ -331,6 +366,7 @@ __global__ void __launch_bounds__(192, 2)
         phase = pre == STAGES ? 1 : 0;
       } else {
         pdl_wait();
+        if (p.ag_flags) wait_ag_flags(p, abort_flag, err);
       }
       for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
         const Unit x = decode_unit(p, u, BN);

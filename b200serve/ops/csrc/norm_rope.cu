@@ -14,6 +14,16 @@ struct PartPtrs {
   const __nv_bfloat16* p[8];
 };
 
+// Norm output as an all-gather: row i of this launch is global row row0 + i; rows < T are stored
+// into dst[r] on every rank r (P2P), then the last CTA raises flag[r] = *epoch on every rank.
+struct AgArgs {
+  __nv_bfloat16* dst[8];
+  int* flag[8];
+  int world, row0, T;
+  int* done;                 // local counter of finished CTAs, zero on entry and exit
+  const int* epoch;
+};
+
 // y = rmsnorm(sum(parts) [+ residual_in]) * w ; residual_out = the pre-norm sum.
 // One CTA per row, 8 bf16 per thread per step, at most 4 steps (H <= 32768 with 1024 threads).
 // Wait (one thread per CTA) until every rank has published this step's epoch
@@ -44,7 +54,7 @@ template <int VPT>
 __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
     PartPtrs parts, int nparts, const __nv_bfloat16* residual_in, __nv_bfloat16* residual_out,
     const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H, float eps,
-    const int* wait_flags, const int* epoch, int* err) {
+    const int* wait_flags, const int* epoch, int* err, const AgArgs ag) {
   __shared__ float red[32];
   pdl_wait();
   pdl_trigger();
@@ -95,7 +105,29 @@ __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
         const float n = __bfloat162float(__float2bfloat16_rn(v[s][i] * inv));
         o[i] = n * wf[i];
       }
-      *reinterpret_cast<bf16x8*>(out + base + col) = pack8(o);
+      const bf16x8 ov = pack8(o);
+      if (ag.world > 0) {
+        const int g = ag.row0 + row;
+        if (g < ag.T)
+          for (int r = 0; r < ag.world; ++r)
+            *reinterpret_cast<bf16x8*>(ag.dst[r] + (size_t)g * H + col) = ov;
+      } else {
+        *reinterpret_cast<bf16x8*>(out + base + col) = ov;
+      }
+    }
+  }
+  if (ag.world > 0) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const int old = atomicAdd(ag.done, 1);
+      if (old == (int)gridDim.x - 1) {
+        *ag.done = 0;
+        __threadfence_system();
+        const int e = *ag.epoch;
+        for (int r = 0; r < ag.world; ++r)
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ag.flag[r]), "r"(e) : "memory");
+      }
     }
   }
 }
@@ -242,7 +274,7 @@ using namespace b200;
 
 void rmsnorm_fused_impl(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
                         c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps,
-                        const int* wait_flags, const int* epoch, int* err) {
+                        const int* wait_flags, const int* epoch, int* err, const AgArgs& ag) {
   TORCH_CHECK(!parts.empty() && parts.size() <= 8, "1..8 partial inputs");
   const int H = parts[0].size(-1);
   const int T = parts[0].numel() / H;
@@ -261,10 +293,10 @@ void rmsnorm_fused_impl(std::vector<torch::Tensor> parts, c10::optional<torch::T
   auto wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   switch (vpt) {
-    case 1: launch_pdl(rmsnorm_fused_kernel<1>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err); break;
-    case 2: launch_pdl(rmsnorm_fused_kernel<2>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err); break;
+    case 1: launch_pdl(rmsnorm_fused_kernel<1>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag); break;
+    case 2: launch_pdl(rmsnorm_fused_kernel<2>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag); break;
     case 3:
-    case 4: launch_pdl(rmsnorm_fused_kernel<4>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err); break;
+    case 4: launch_pdl(rmsnorm_fused_kernel<4>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag); break;
     default: TORCH_CHECK(false, "hidden size too large");
   }
   B200_CHECK_CUDA(cudaGetLastError());
@@ -272,7 +304,7 @@ void rmsnorm_fused_impl(std::vector<torch::Tensor> parts, c10::optional<torch::T
 
 void rmsnorm_fused(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
                    c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps) {
-  rmsnorm_fused_impl(parts, residual_in, residual_out, w, out, eps, nullptr, nullptr, nullptr);
+  rmsnorm_fused_impl(parts, residual_in, residual_out, w, out, eps, nullptr, nullptr, nullptr, AgArgs{});
 }
 
 // Same, after waiting for the peers' flags of a fused all-reduce site
@@ -281,7 +313,33 @@ void rmsnorm_fused_wait(std::vector<torch::Tensor> parts, c10::optional<torch::T
                         c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps,
                         int64_t flags_ptr, int64_t epoch_ptr, int64_t err_ptr) {
   rmsnorm_fused_impl(parts, residual_in, residual_out, w, out, eps, reinterpret_cast<const int*>(flags_ptr),
-                     reinterpret_cast<const int*>(epoch_ptr), reinterpret_cast<int*>(err_ptr));
+                     reinterpret_cast<const int*>(epoch_ptr), reinterpret_cast<int*>(err_ptr), AgArgs{});
+}
+
+// Reduce-scatter consumer + all-gather producer: waits for the partial rows of this rank's
+// token shard (flags_ptr, 0 = no wait), normalises them, and stores row i as global row row0 + i
+// (< T) into dst_ptrs[r] (int64 [world], every rank's gathered buffer), then raises
+// ag_flag_ptrs[r] = epoch on every rank. done: int32 [1] counter, zero on entry.
+void rmsnorm_rs_ag(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
+                   c10::optional<torch::Tensor> residual_out, torch::Tensor w, double eps, int64_t flags_ptr,
+                   int64_t epoch_ptr, int64_t err_ptr, torch::Tensor dst_ptrs, torch::Tensor ag_flag_ptrs,
+                   int64_t row0, int64_t T, torch::Tensor done) {
+  const int world = dst_ptrs.numel();
+  TORCH_CHECK(world >= 1 && world <= 8 && ag_flag_ptrs.numel() == world && dst_ptrs.device().is_cpu() &&
+                  ag_flag_ptrs.device().is_cpu(), "dst/flag pointer lists: host int64 [world]");
+  AgArgs ag{};
+  ag.world = world;
+  ag.row0 = (int)row0;
+  ag.T = (int)T;
+  ag.done = done.data_ptr<int>();
+  ag.epoch = reinterpret_cast<const int*>(epoch_ptr);
+  for (int r = 0; r < world; ++r) {
+    ag.dst[r] = reinterpret_cast<__nv_bfloat16*>(dst_ptrs.data_ptr<int64_t>()[r]);
+    ag.flag[r] = reinterpret_cast<int*>(ag_flag_ptrs.data_ptr<int64_t>()[r]);
+  }
+  rmsnorm_fused_impl(parts, residual_in, residual_out, w, parts[0], eps,
+                     flags_ptr ? reinterpret_cast<const int*>(flags_ptr) : nullptr,
+                     reinterpret_cast<const int*>(epoch_ptr), reinterpret_cast<int*>(err_ptr), ag);
 }
 
 void qkv_post_impl(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,

@@ -45,6 +45,25 @@ def init_distributed(backend: str = None, timeout_s: float = 120.0):
     return dist.group.WORLD
 
 
+def tp_mode() -> str:
+    """How row-parallel outputs are combined: "ar" (all-reduce: every rank keeps the whole
+    residual stream), "rsag" (reduce-scatter to the token owner, norm on the owned rows,
+    all-gather of the normalised rows) or "auto" (rsag for prefill-sized steps, ar for decode).
+    Set with B200_TP_MODE."""
+    m = os.environ.get("B200_TP_MODE", "auto").lower()
+    return m if m in ("ar", "rsag", "auto") else "auto"
+
+
+class RSParts(list):
+    """Partials of this rank's token shard after a reduce-scatter (``T`` tokens in the step).
+    ``flags_ptr`` (fused path): flags the consumer waits for before reading the partials."""
+
+    def __init__(self, views, T, flags_ptr=None, epoch_ptr=None, err_ptr=None):
+        super().__init__(views)
+        self.T = T
+        self.flags_ptr, self.epoch_ptr, self.err_ptr = flags_ptr, epoch_ptr, err_ptr
+
+
 class NcclComm:
     """Tensor-parallel reduction through library collectives (NCCL on GPU, gloo on CPU)."""
 
@@ -55,6 +74,40 @@ class NcclComm:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.device = torch.device(device)
+
+    # ---- token-sharded residual stream: reduce-scatter + all-gather (library collectives) ----
+    def use_rsag(self, T: int) -> bool:
+        return tp_mode() == "rsag"
+
+    def shard(self, T: int):
+        """Rows per rank, first row and row count of this rank's token shard."""
+        Tw = -(-T // self.world)
+        row0 = self.rank * Tw
+        return Tw, row0, max(0, min(T, row0 + Tw) - row0)
+
+    def rs_linear(self, x, w, tag):
+        from b200serve import ops
+        y = ops.linear(x, w)
+        T, H = y.shape
+        Tw, row0, _ = self.shard(T)
+        pad = torch.zeros(Tw * self.world, H, dtype=y.dtype, device=y.device)
+        pad[:T] = y
+        if pad.is_cuda:
+            own = torch.empty(Tw, H, dtype=y.dtype, device=y.device)
+            dist.reduce_scatter_tensor(own, pad, group=self.group)
+        else:                       # gloo has no reduce-scatter: same result through all-reduce
+            dist.all_reduce(pad, group=self.group)
+            own = pad[row0:row0 + Tw].contiguous()
+        return RSParts([own], T)
+
+    def norm_ag(self, parts, weight, eps, residual):
+        """RMSNorm of this rank's rows (+ residual, updated in place), then all-gather."""
+        from b200serve import ops
+        xo = ops.rmsnorm(list(parts), weight, eps, residual=residual, residual_out=residual)
+        Tw, H = xo.shape
+        full = torch.empty(Tw * self.world * H, dtype=xo.dtype, device=xo.device)
+        dist.all_gather_into_tensor(full, xo.contiguous().view(-1), group=self.group)
+        return full.view(Tw * self.world, H)[:parts.T], None
 
     def reduce_parts(self, t: torch.Tensor, tag: str):
         dist.all_reduce(t, group=self.group)

@@ -57,10 +57,16 @@ class FusedComm:
         H = model_cfg.hidden_size
         self.H = H
         self.max_tokens = max_tokens or max(cfgE.max_batch, 64)
-        self.n_sites = 2 * model_cfg.num_layers + 4
-        self.slot_elems = self.max_tokens * H
+        # largest step (a prefill chunk plus the decode tokens riding along) for the
+        # reduce-scatter / all-gather path
+        self.max_step = max(self.max_tokens, int(getattr(cfgE, "prefill_chunk", 0) or 0) + cfgE.max_batch)
+        self.n_sites = 4 * model_cfg.num_layers + 8
+        self.slot_rows = max(self.max_tokens, -(-self.max_step // self.world))
+        self.slot_elems = self.slot_rows * H
         data_bytes = 2 * self.world * self.slot_elems * 2
-        self.flag_off = (data_bytes + 4095) // 4096 * 4096
+        self.ag_off = (data_bytes + 4095) // 4096 * 4096
+        ag_bytes = 2 * self.max_step * H * 2                  # gathered rows, [2 parities][max_step][H]
+        self.flag_off = (self.ag_off + ag_bytes + 4095) // 4096 * 4096
         total = self.flag_off + self.n_sites * self.world * 4
         e = ops.ext()
         self.base = e.ipc_malloc(total)
@@ -75,6 +81,8 @@ class FusedComm:
                 self.peer.append(e.ipc_open(torch.tensor(handles[r], dtype=torch.uint8)))
         self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.tile_done = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.ag_done = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._ag_ptrs = {}
         self.err = e.host_error_word()       # [host ptr, device ptr]
         self.err_host, self.err_dev = int(self.err[0]), int(self.err[1])
         self.ws = ops.GemmWorkspace(self.device, max_elems=8 << 20, max_tiles=1 << 14)
@@ -130,9 +138,69 @@ class FusedComm:
         ops._cuda(x)
         packed_n = w.N if isinstance(w, ops.PackedWeight) else 0
         ops.ext().gemm_tc_push(x, w.data if packed_n else w, dst, self.H, flg, self.epoch.data_ptr(), self.tile_done,
-                               None, self.ws.ws, self.ws.counters, self.err_dev, packed_n)
+                               None, self.ws.ws, self.ws.counters, self.err_dev, packed_n, 0)
         return FusedParts(self._local_views(site % 2, T), self._flag_ptr(self.base, site, 0),
                           self.epoch.data_ptr(), self.err_dev)
+
+    # ------------------------------------------------------------ reduce-scatter / all-gather
+    def use_rsag(self, T: int) -> bool:
+        from b200serve.parallel.dist import tp_mode
+        m = tp_mode()
+        if T > self.max_step:
+            return False
+        return m == "rsag" or (m == "auto" and T > self.max_tokens)
+
+    def shard(self, T: int):
+        return self.nccl.shard(T)
+
+    def _next_site(self) -> int:
+        site = self.site
+        self.site += 1
+        assert site < self.n_sites, "more fused sites than allocated"
+        return site
+
+    def rs_linear(self, x: torch.Tensor, w, tag: str):
+        """GEMM -> reduce-scatter: the epilogue pushes token row t only to its owner rank
+        (rows T/world per rank), which sums the ``world`` partials in its norm."""
+        from b200serve.parallel.dist import RSParts
+        T = x.shape[0]
+        Tw, _, _ = self.shard(T)
+        if not isinstance(w, (torch.Tensor, ops.PackedWeight)):
+            return self.nccl.rs_linear(x, w, tag)
+        site = self._next_site()
+        dst, flg = self._push_ptrs(site)
+        ops._cuda(x)
+        packed_n = w.N if isinstance(w, ops.PackedWeight) else 0
+        ops.ext().gemm_tc_push(x, w.data if packed_n else w, dst, self.H, flg, self.epoch.data_ptr(),
+                               self.tile_done, None, self.ws.ws, self.ws.counters, self.err_dev, packed_n, Tw)
+        return RSParts(self._local_views(site % 2, Tw), T, self._flag_ptr(self.base, site, 0),
+                       self.epoch.data_ptr(), self.err_dev)
+
+    def _ag_base(self, rank_base: int, parity: int) -> int:
+        return rank_base + self.ag_off + parity * self.max_step * self.H * 2
+
+    def norm_ag(self, parts, weight, eps, residual):
+        """Norm of this rank's token shard fused with the all-gather of its output rows: the
+        kernel stores each normalised row into every rank's gathered buffer and raises their
+        flags. Returns (gathered rows [T, H] on this rank, AGWait for consumers)."""
+        T = parts.T
+        Tw, row0, _ = self.shard(T)
+        if parts.flags_ptr is None:             # partials came through NCCL
+            return self.nccl.norm_ag(parts, weight, eps, residual)
+        site = self._next_site()
+        par = site % 2
+        key = (site, par)
+        if key not in self._ag_ptrs:
+            dst = torch.tensor([self._ag_base(self.peer[r], par) for r in range(self.world)], dtype=torch.int64)
+            flg = torch.tensor([self._flag_ptr(self.peer[r], site, self.rank) for r in range(self.world)],
+                               dtype=torch.int64)
+            self._ag_ptrs[key] = (dst, flg)
+        dst, flg = self._ag_ptrs[key]
+        ops._cuda(residual)
+        ops.ext().rmsnorm_rs_ag(list(parts), residual, residual, weight, float(eps), parts.flags_ptr,
+                                self.epoch.data_ptr(), self.err_dev, dst, flg, row0, T, self.ag_done)
+        full = _tensor_from_ptr(self._ag_base(self.base, par), T * self.H, self.device).view(T, self.H)
+        return full, ops.AGWait(self._flag_ptr(self.base, site, 0), self.world, self.epoch.data_ptr(), self.err_dev)
 
     def reduce_parts(self, t: torch.Tensor, tag: str):
         return self.nccl.reduce_parts(t, tag)

@@ -192,9 +192,10 @@ def decode_step(layers=2, B=32, ctx=2304, iters=3):
     from b200serve.models.config import get_model_config
     from b200serve.models.weights import random_weights
     cfg = get_model_config("qwen3-8b", layers)
-    w = random_weights(cfg, seed=0, device="cuda")
+    # tp > 1: the shard of rank 0 (all local kernels of one tensor-parallel rank, no collectives)
+    w = random_weights(cfg, seed=0, device="cuda", tp_rank=0, tp_size=tp)
     nb = (ctx + 32) // 16
-    kv = KVCache(cfg.num_layers, B * nb + 8, cfg.num_kv_heads, cfg.head_dim, device="cuda")
+    kv = KVCache(cfg.num_layers, B * nb + 8, max(1, cfg.num_kv_heads // tp), cfg.head_dim, device="cuda")
     kv.k.normal_(0, 1)
     kv.v.normal_(0, 1)
     r = ModelRunner(cfg, w, kv, device="cuda", max_batch=B, max_seq=nb * 16, use_graphs=False)
@@ -246,13 +247,14 @@ def gemm_chain_trace(layers=2, B=32):
     torch.cuda.synchronize()
     t = buf.view(n, 2048, 8).cpu()
     t0 = min(int(t[i, :, 0][t[i, :, 0] > 0].min()) for i in range(n))
+    t = torch.where(t > 0, t - t0, torch.zeros_like(t))          # int64 ns since the first entry
     names = ["qkv", "o", "gate_up", "down"]
     rows = []
     for i in range(n):
         ti = t[i]
         ok = ti[:, 0] > 0
         ti = ti[ok]
-        us = lambda col, f: round((float(f(ti[:, col].float())) - t0) / 1000.0, 2)
+        us = lambda col, f: round(float(f(ti[:, col].double())) / 1000.0, 2)
         rows.append({"gemm": names[i % 4], "layer": i // 4, "ctas": int(ok.sum()),
                      "entry_min": us(0, torch.min), "entry_max": us(0, torch.max),
                      "first_data_med": us(3, torch.median), "mma_done_max": us(4, torch.max),
@@ -262,7 +264,7 @@ def gemm_chain_trace(layers=2, B=32):
     del g
 
 
-def decode_parts(layers=8, B=32, ctx=2304):
+def decode_parts(layers=8, B=32, ctx=2304, tp=1):
     """Per-layer device time of the decode step and of its parts, each captured as its own
     CUDA graph of ``layers`` layers (weights and KV far larger than L2): the full forward, the
     four GEMMs alone, attention alone, and the norm / RoPE kernels alone. Shows where the step
@@ -273,9 +275,10 @@ def decode_parts(layers=8, B=32, ctx=2304):
     from b200serve.models.weights import random_weights
     hbm, _, src = peaks()
     cfg = get_model_config("qwen3-8b", layers)
-    w = random_weights(cfg, seed=0, device="cuda")
+    # tp > 1: the shard of rank 0 (all local kernels of one tensor-parallel rank, no collectives)
+    w = random_weights(cfg, seed=0, device="cuda", tp_rank=0, tp_size=tp)
     nb = (ctx + 32) // 16
-    kv = KVCache(cfg.num_layers, B * nb + 8, cfg.num_kv_heads, cfg.head_dim, device="cuda")
+    kv = KVCache(cfg.num_layers, B * nb + 8, max(1, cfg.num_kv_heads // tp), cfg.head_dim, device="cuda")
     kv.k.normal_(0, 1)
     kv.v.normal_(0, 1)
     dec = Decoder(cfg, w, kv, device="cuda")
@@ -289,7 +292,7 @@ def decode_parts(layers=8, B=32, ctx=2304):
     H, hd, nq, nkv = cfg.hidden_size, cfg.head_dim, dec.nq, dec.nkv
     x = torch.randn(B, H, device="cuda").bfloat16()
     a = torch.randn(B, nq * hd, device="cuda").bfloat16()
-    act = torch.randn(B, cfg.intermediate_size, device="cuda").bfloat16()
+    act = torch.randn(B, cfg.intermediate_size // tp, device="cuda").bfloat16()
     q = torch.randn(B, nq, hd, device="cuda").bfloat16()
     qkv = torch.randn(B, (nq + 2 * nkv) * hd, device="cuda").bfloat16()
     res = torch.randn(B, H, device="cuda").bfloat16()
@@ -318,7 +321,7 @@ def decode_parts(layers=8, B=32, ctx=2304):
     wbytes = sum(t.N * t.K * 2 for lw in w.layers for t in (lw.qkv, lw.o, lw.gate_up, lw.down)) / layers
     kvbytes = B * (ctx + 1) * nkv * hd * 2 * 2
     ideal = {"full": (wbytes + kvbytes) / hbm / 1e3, "gemms": wbytes / hbm / 1e3, "attn": kvbytes / hbm / 1e3}
-    out = {"case": "decode_parts", "layers": layers, "B": B, "ctx": ctx, "peaks": src}
+    out = {"case": "decode_parts", "layers": layers, "B": B, "ctx": ctx, "tp": tp, "peaks": src}
     for name, fn in (("full", full), ("gemms", gemms), ("attn", attn), ("small", small)):
         for _ in range(2):
             fn()
@@ -374,7 +377,7 @@ if __name__ == "__main__":
         gemm_chain_trace(*[int(v) for v in sys.argv[2:4]])
         sys.exit(0)
     if what == "decode_parts":
-        decode_parts(*[int(v) for v in sys.argv[2:5]])
+        decode_parts(*[int(v) for v in sys.argv[2:6]])
         sys.exit(0)
     if what == "decode_step":
         decode_step(*[int(v) for v in sys.argv[2:5]])

@@ -124,3 +124,76 @@ def test_tp2_fused_equals_nccl():
     # required to agree exactly
     a, b = _run_tp("fused"), _run_tp("nccl")
     assert [x[:4] for x in a] == [x[:4] for x in b]
+
+
+def _rsag_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+    from b200serve import ops
+    from b200serve.core.config import EngineConfig
+    from b200serve.models.config import BUILTIN
+    from b200serve.parallel.dist import init_distributed
+    from b200serve.parallel.fused_comm import FusedComm
+    init_distributed("nccl", timeout_s=60)
+    torch.cuda.set_device(rank)
+    cfg = BUILTIN["qwen3-8b"]
+    comm = FusedComm(dist.group.WORLD, torch.device("cuda", rank), cfg,
+                     EngineConfig(max_batch=32, prefill_chunk=1024))
+    g = torch.Generator(device="cuda").manual_seed(200 + rank)
+    gs = torch.Generator(device="cuda").manual_seed(7)          # same on every rank
+    errs = []
+    for step in range(4):
+        comm.begin_step()
+        for T in (37, 300, 1040):
+            x = torch.randn(T, 1536, device="cuda", generator=g).bfloat16()
+            w = ops.pack_weight((torch.randn(4096, 1536, device="cuda", generator=gs) * 0.03).bfloat16())
+            w2 = ops.pack_weight((torch.randn(1024, 4096, device="cuda", generator=gs) * 0.03).bfloat16())
+            res = torch.randn(T, 4096, device="cuda", generator=gs).bfloat16()
+            nw = torch.randn(4096, device="cuda", generator=gs).bfloat16()
+            Tw, row0, cnt = comm.shard(T)
+            res_own = torch.zeros(Tw, 4096, dtype=torch.bfloat16, device="cuda")
+            res_own[:cnt] = res[row0:row0 + cnt]
+            parts = comm.rs_linear(x, w, "o")
+            xf, ag = comm.norm_ag(parts, nw, 1e-6, res_own)
+            y2 = ops.linear(xf, w2, ag=ag)
+            y = ops.linear(x, w)
+            dist.all_reduce(y)
+            res_ref = res.clone()
+            ref = ops.rmsnorm([y], nw, 1e-6, residual=res, residual_out=res_ref)
+            ref2 = ops.linear(ref, w2)
+            errs.append(((y2.float() - ref2.float()).norm() / ref2.float().norm()).item())
+            errs.append(((res_own[:cnt].float() - res_ref[row0:row0 + cnt].float()).norm()
+                         / res_ref[row0:row0 + cnt].float().norm()).item())
+    torch.cuda.synchronize()
+    comm.check()
+    comm.close()
+    q.put((rank, max(errs)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@needs2
+def test_fused_reduce_scatter_all_gather_matches_nccl():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_rsag_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in ps)
+    for p in ps:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert max(res.values()) < 3e-2, res
+
+
+@needs2
+def test_tp2_rsag_equals_nccl():
+    os.environ["B200_TP_MODE"] = "rsag"
+    try:
+        a = _run_tp("fused")
+    finally:
+        os.environ.pop("B200_TP_MODE", None)
+    b = _run_tp("nccl")
+    assert [x[:4] for x in a] == [x[:4] for x in b]

@@ -23,9 +23,9 @@ def _prompts():
     return [torch.randint(0, 32000, (n,), generator=g).tolist() for n in (37, 64, 5)]
 
 
-def _worker(rank, world, port, out_q, greedy):
+def _worker(rank, world, port, out_q, greedy, mode="auto"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank))
+                      LOCAL_RANK=str(rank), B200_TP_MODE=mode)
     torch.set_num_threads(1)
     from b200serve.core.config import EngineConfig
     from b200serve.engine.b200_engine import B200Engine
@@ -46,11 +46,11 @@ def _worker(rank, world, port, out_q, greedy):
     torch.distributed.destroy_process_group()
 
 
-def _run_tp(world, greedy):
+def _run_tp(world, greedy, mode="auto"):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, greedy)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, greedy, mode)) for r in range(world)]
     for p in procs:
         p.start()
     out = q.get(timeout=600)
@@ -80,3 +80,9 @@ def test_tp_greedy_matches_single_rank(world):
 
 def test_tp_sampled_matches_single_rank():
     assert _run_tp(2, False) == _single(False)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_reduce_scatter_all_gather_matches_single_rank(world):
+    """Token-sharded residual stream (reduce-scatter, norm on owned rows, all-gather)."""
+    assert _run_tp(world, True, mode="rsag") == _single(True)
