@@ -97,7 +97,35 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi, int
   const int kb_total = (int)((K + 63) / 64);
   const int tiles = m_tiles * n_tiles;
   int best_s = 1, best_kbp = kb_total;
-  if (m_tiles * BN <= 256) {
+  static int planner = -1;
+  if (planner < 0) {
+    const char* e = getenv("B200_GEMM_PLANNER");
+    planner = e ? atoi(e) : 1;
+  }
+  if (m_tiles * BN <= 256 && planner == 1) {
+    // decode-sized M, latency model: the kernel takes as long as its busiest CTA streams its
+    // weight tiles, at the smaller of an equal share of HBM bandwidth and what one CTA's
+    // stage ring sustains (ring bytes per ~1.5 us round trip), plus the split-K reduction
+    // (~1.5 us + 0.15 us per split) and ~1 us per extra unit a persistent CTA runs.
+    const double hbm = 6.5e3;                                   // bytes per ns
+    const double stage = 128.0 * 64 * 2 + BN * 64 * 2;
+    const double ring = (double)ring_stages(BN) * stage;
+    const double cta_bw = ring / 1800.0;                        // bytes per ns (with margin)
+    double best = 1e30;
+    for (int s = 1; s <= 32; ++s) {
+      const int kbp = (kb_total + s - 1) / s;
+      if (kbp < 2 && s > 1) break;
+      const int se = (kb_total + kbp - 1) / kbp;
+      const long units = (long)tiles * se;
+      if (se > 1 && units > 4 * num_sms) break;
+      const long ctas = std::min<long>(units, num_sms);
+      const long waves = (units + num_sms - 1) / num_sms;
+      const double bytes = (double)waves * kbp * stage;
+      const double bw = std::min(hbm / (double)ctas, cta_bw);
+      const double t = bytes / bw + (se > 1 ? 1500.0 + 150.0 * se : 0.0) + 1000.0 * (double)(waves - 1);
+      if (t < best - 1e-6) { best = t; best_s = se; best_kbp = kbp; }
+    }
+  } else if (m_tiles * BN <= 256) {
     // decode-sized M: weight streaming, balance the busiest SM with split-K
     double best = -1.0;
     for (int s = 1; s <= 32; ++s) {

@@ -38,14 +38,14 @@ def main():
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
     cfg = BUILTIN["qwen3-8b"]
     H = cfg.hidden_size
-    comm = FusedComm(dist.group.WORLD, torch.device("cuda"), cfg, EngineConfig(max_batch=64))
+    comm = FusedComm(dist.group.WORLD, torch.device("cuda"), cfg, EngineConfig(max_batch=64, prefill_chunk=1024))
     hbm, _, src = peaks()
     results = []
     for name, Kfull in (("o_proj", cfg.q_size), ("down", cfg.intermediate_size)):
         K = Kfull // world
         w = ops.pack_weight((torch.randn(H, K, device="cuda") * 0.02).bfloat16())
         nw = torch.ones(H, device="cuda").bfloat16()
-        for T in (1, 8, 32, 64):
+        for T in (1, 8, 32, 64, 1024):
             x = torch.randn(T, K, device="cuda").bfloat16()
             res = torch.randn(T, H, device="cuda").bfloat16()
             out = torch.empty(T, H, device="cuda").bfloat16()
@@ -62,8 +62,23 @@ def main():
                     dist.all_reduce(y)
                     ops.rmsnorm([y], nw, 1e-6, residual=res, out=out)
 
+            Tw, row0, cnt = comm.shard(T)
+            res_own = torch.zeros(Tw, H, device="cuda").bfloat16()
+
+            def rsag():
+                comm.begin_step()
+                for _ in range(8):
+                    parts = comm.rs_linear(x, w, "o")
+                    _, ag = comm.norm_ag(parts, nw, 1e-6, res_own)
+                    ag.wait()
+
+            def local():
+                for _ in range(8):
+                    y = ops.linear(x, w)
+                    ops.rmsnorm([y], nw, 1e-6, residual=res, out=out)
+
             row = {"site": name, "T": T, "world": world, "K_shard": K}
-            for label, fn in (("fused", fused), ("nccl", nccl)):
+            for label, fn in (("fused", fused), ("rsag", rsag), ("nccl", nccl), ("local", local)):
                 for _ in range(3):
                     fn()
                 torch.cuda.synchronize()
@@ -88,6 +103,8 @@ def main():
             nv_bytes = (world - 1) * T * H * 2
             roof_us = max(wbytes / (hbm * 1e3), nv_bytes / (NVLINK_GBPS * 1e3)) if world > 1 else wbytes / (hbm * 1e3)
             row["roofline_us"] = round(roof_us, 2)
+            rs_bytes = 2 * (world - 1) * (-(-T // world)) * H * 2
+            row["rsag_roofline_us"] = round(max(wbytes / (hbm * 1e3), rs_bytes / (NVLINK_GBPS * 1e3)), 2)
             row["fused_frac_of_roofline"] = round(roof_us / row["fused_us"], 3)
             row["speedup_vs_nccl"] = round(row["nccl_us"] / row["fused_us"], 3)
             row["peaks"] = src
