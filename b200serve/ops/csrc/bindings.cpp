@@ -89,6 +89,8 @@ void rmsnorm_rs_ag(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor
                    int64_t row0, int64_t T, torch::Tensor done);
 
 void flag_wait(int64_t flags_ptr, int64_t n, int64_t epoch_ptr, int64_t err_ptr);
+void flag_pingpong(int64_t mine_ptr, int64_t peer_ptr, int64_t iters, int64_t initiator, int64_t mode,
+                   torch::Tensor out);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "b200serve sm_100a kernels";
@@ -106,6 +108,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("read_host_word", &read_host_word);
   m.def("epoch_inc", &epoch_inc);
   m.def("flag_wait", &flag_wait);
+  m.def("flag_pingpong", &flag_pingpong);
   m.def("silu_mul", &silu_mul);
   m.def("embedding", &embedding);
   m.def("paged_decode_attention", &paged_decode_attention);

@@ -6,9 +6,11 @@
 //  * every rank's GEMM epilogue stores its partial tile into slot
 //    [site % 2][its own rank] of EVERY rank's receive buffer (NVLink P2P stores);
 //  * when all tiles of the GEMM are pushed, the rank's last CTA publishes
-//    flag[site][its rank] = epoch on every peer (st.release.sys after fences);
-//  * the consumer kernel on each rank waits until flag[site][r] == epoch for all
-//    r (ld.acquire.sys, bounded by a deadline), then sums the world slots locally.
+//    flag[site][its rank] = epoch on every peer: one system-scope fence, then
+//    relaxed system-scope stores (a release store per peer would serialise);
+//  * the consumer kernel on each rank polls until flag[site][r] == epoch for all
+//    r (relaxed loads, bounded by a deadline), issues one acquire fence, then sums
+//    the world slots locally.
 // Two slots alternate by site parity; a rank can only overwrite slot (site % 2)
 // after every peer has pushed site+1, which each peer does only after it has
 // finished reading site (stream order), so no slot is overwritten while read.
@@ -36,7 +38,7 @@ __global__ void flag_wait_kernel(const int* flags, int n, const int* epoch, int*
     uint32_t it = 0;
     while (true) {
       int v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
+      asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
       if (v == e) break;
       if ((++it & 1023u) == 0 && globaltimer_ns() > deadline) {
         if (err) atomicExch(err, 140 + r);
@@ -44,11 +46,56 @@ __global__ void flag_wait_kernel(const int* flags, int n, const int* epoch, int*
       }
     }
   }
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
+// Cross-GPU flag round trip (diagnostics): the initiator stores i into the peer's flag and waits
+// for the peer to echo i into its own flag, `iters` times; every wait is bounded (1 s in total).
+// Writes the elapsed ns (or -1 on a timeout) to *out.
+// mode 0: st.release.sys / ld.acquire.sys; 1: st.relaxed.sys / ld.relaxed.sys; 2: volatile.
+__device__ __forceinline__ void pp_store(int* p, int v, int mode) {
+  if (mode == 0) asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+  else if (mode == 1) asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+  else asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int pp_load(volatile int* p, int mode) {
+  int v;
+  if (mode == 0) asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  else if (mode == 1) asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  else asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void flag_pingpong_kernel(volatile int* mine, int* peer, int iters, int initiator, int mode,
+                                     long long* out) {
+  if (threadIdx.x != 0) return;
+  const uint64_t t0 = globaltimer_ns();
+  const uint64_t deadline = t0 + 1000000000ull;
+  for (int i = 1; i <= iters; ++i) {
+    if (initiator) pp_store(peer, i, mode);
+    uint32_t it = 0;
+    while (pp_load(mine, mode) < i) {
+      if ((++it & 255u) == 0 && globaltimer_ns() > deadline) {
+        *out = -1;
+        return;
+      }
+    }
+    if (!initiator) pp_store(peer, i, mode);
+  }
+  *out = (long long)(globaltimer_ns() - t0);
 }
 
 }  // namespace b200
 
 using namespace b200;
+
+void flag_pingpong(int64_t mine_ptr, int64_t peer_ptr, int64_t iters, int64_t initiator, int64_t mode,
+                   torch::Tensor out) {
+  flag_pingpong_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<volatile int*>(mine_ptr), reinterpret_cast<int*>(peer_ptr), (int)iters, (int)initiator,
+      (int)mode, reinterpret_cast<long long*>(out.data_ptr<int64_t>()));
+  B200_CHECK_CUDA(cudaGetLastError());
+}
 
 void flag_wait(int64_t flags_ptr, int64_t n, int64_t epoch_ptr, int64_t err_ptr) {
   launch_pdl(flag_wait_kernel, dim3(1), dim3(32), 0, at::cuda::getCurrentCUDAStream(),

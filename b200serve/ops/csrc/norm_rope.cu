@@ -37,7 +37,7 @@ __device__ __forceinline__ void wait_peer_flags(const int* flags, const int* epo
       uint32_t it = 0;
       while (true) {
         int v;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
+        asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
         if (v == e) break;
         if ((++it & 1023u) == 0 && globaltimer_ns() > deadline) {
           if (err) atomicExch(err, 100 + r);
@@ -46,6 +46,8 @@ __device__ __forceinline__ void wait_peer_flags(const int* flags, const int* epo
         }
       }
     }
+    // relaxed polls + one acquire fence (pairs with the writer's fence before its relaxed flags)
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
   }
   __syncthreads();
 }
@@ -125,8 +127,8 @@ __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
         *ag.done = 0;
         __threadfence_system();
         const int e = *ag.epoch;
-        for (int r = 0; r < ag.world; ++r)
-          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ag.flag[r]), "r"(e) : "memory");
+        for (int r = 0; r < ag.world; ++r)   // ordered by the fence above; relaxed stores pipeline
+          asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(ag.flag[r]), "r"(e) : "memory");
       }
     }
   }

@@ -32,6 +32,14 @@ from b200serve.utils.timing import max_over_ranks
 NVLINK_GBPS = 770.0
 
 
+def _tensor_from_ptr_i32(ptr: int) -> torch.Tensor:
+    class _CAI:
+        def __init__(self):
+            self.__cuda_array_interface__ = {"shape": (1,), "typestr": "<i4", "data": (ptr, False), "version": 3,
+                                             "strides": None}
+    return torch.as_tensor(_CAI(), device="cuda")
+
+
 def main():
     init_distributed("nccl", timeout_s=120)
     rank, world = dist.get_rank(), dist.get_world_size()
@@ -41,11 +49,40 @@ def main():
     comm = FusedComm(dist.group.WORLD, torch.device("cuda"), cfg, EngineConfig(max_batch=64, prefill_chunk=1024))
     hbm, _, src = peaks()
     results = []
+    # raw cross-GPU flag round trip between rank 0 and every other rank (P2P st.release /
+    # ld.acquire .sys), the floor under any in-kernel collective on this box
+    if world > 1:
+        e = ops.ext()
+        out = torch.zeros(1, dtype=torch.int64, device="cuda")
+        rtts = {}
+        for mode, peer in [(0, p) for p in range(1, world)] + [(1, 1), (2, 1)]:
+            comm.begin_step()
+            torch.cuda.synchronize()
+            dist.barrier()
+            if rank in (0, peer):
+                other = peer if rank == 0 else 0
+                # flag words of site n_sites-1: mine = (site, src=other) locally, peer's = (site, src=me) there
+                site = comm.n_sites - 1
+                mine = comm._flag_ptr(comm.base, site, other)
+                theirs = comm._flag_ptr(comm.peer[other], site, rank)
+                e.flag_pingpong(mine, theirs, 1000, 1 if rank == 0 else 0, mode, out)
+                torch.cuda.synchronize()
+                if rank == 0:
+                    rtts[f"{['acq_rel', 'relaxed', 'volatile'][mode]}:{peer}"] = round(out.item() / 1000.0 / 1000.0, 3)
+            dist.barrier()
+            # reset the flag words used above for the next pair
+            if rank in (0, peer):
+                other = peer if rank == 0 else 0
+                _tensor_from_ptr_i32(comm._flag_ptr(comm.base, comm.n_sites - 1, other)).zero_()
+            torch.cuda.synchronize()
+            dist.barrier()
+        if rank == 0:
+            print(json.dumps({"case": "flag_round_trip_us", "world": world, "per_peer": rtts}), flush=True)
     for name, Kfull in (("o_proj", cfg.q_size), ("down", cfg.intermediate_size)):
         K = Kfull // world
         w = ops.pack_weight((torch.randn(H, K, device="cuda") * 0.02).bfloat16())
         nw = torch.ones(H, device="cuda").bfloat16()
-        for T in (1, 8, 32, 64, 1024):
+        for T in (1, 32, 1024):
             x = torch.randn(T, K, device="cuda").bfloat16()
             res = torch.randn(T, H, device="cuda").bfloat16()
             out = torch.empty(T, H, device="cuda").bfloat16()
