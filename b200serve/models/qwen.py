@@ -214,6 +214,25 @@ class Decoder:
             return ops.paged_decode_attention(q, kd, vd, fb.block_tables, fb.seq_lens, self.scale)
         return ops.paged_prefill_attention(q, kd, vd, fb.block_tables, fb.seq_lens, fb.q_start, fb.cu_q, self.scale)
 
+    def _qkv_attend(self, i, x, lw, fb, T, plan, tq_pre, ag=None):
+        """QKV projection + post-processing + attention of layer ``i`` -> [T, nq, hd]. On a bf16
+        cache the QKV GEMM's epilogue does the norm, RoPE and KV write itself."""
+        if self.tq is None and self.kv.kv_format == "bf16" and ops.qkv_fused_ok(x, lw.qkv, self.kv.k[i]):
+            kc, vc = self.kv.k[i], self.kv.v[i]
+            q = ops.qkv_fused(x, lw.qkv, lw.qkv_bias, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots,
+                              kc, vc, self.nq, self.nkv, self.cfg.rms_eps, ag=ag)
+            return self._attn_core(i, q, fb, plan)
+        qkv = ops.linear(x, lw.qkv, bias=lw.qkv_bias, ag=ag)
+        return self._attend(i, qkv, lw, fb, T, plan, tq_pre)
+
+    def _attn_core(self, i, q, fb, plan):
+        tps, nsplit, ws = plan
+        kc, vc = self.kv.k[i], self.kv.v[i]
+        if fb.is_decode:
+            return ops.paged_decode_attention(q, kc, vc, fb.block_tables, fb.seq_lens, self.scale, tps, nsplit, ws)
+        return ops.paged_prefill_attention(q, kc, vc, fb.block_tables, fb.seq_lens, fb.q_start, fb.cu_q,
+                                           self.scale, max_q=fb.max_q)
+
     def _attend(self, i, qkv, lw, fb, T, plan, tq_pre):
         """QKV post-processing, KV write and attention of layer ``i`` -> [T, nq, hd]."""
         tps, nsplit, ws = plan
@@ -225,10 +244,7 @@ class Decoder:
         kc, vc = self.kv.k[i], self.kv.v[i]
         q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots, kc, vc,
                          self.nq, self.nkv, eps)
-        if fb.is_decode:
-            return ops.paged_decode_attention(q, kc, vc, fb.block_tables, fb.seq_lens, self.scale, tps, nsplit, ws)
-        return ops.paged_prefill_attention(q, kc, vc, fb.block_tables, fb.seq_lens, fb.q_start, fb.cu_q,
-                                           self.scale, max_q=fb.max_q)
+        return self._attn_core(i, q, fb, plan)
 
     def _forward_rsag(self, fb, h, plan, tq_pre):
         """Tensor-parallel forward on a token-sharded residual stream (sequence parallelism for
@@ -248,8 +264,7 @@ class Decoder:
         for i, lw in enumerate(w.layers):
             if i > 0:
                 x, ag = comm.norm_ag(parts, lw.input_norm, eps, residual)
-            qkv = ops.linear(x, lw.qkv, bias=lw.qkv_bias, ag=ag)
-            attn = self._attend(i, qkv, lw, fb, T, plan, tq_pre)
+            attn = self._qkv_attend(i, x, lw, fb, T, plan, tq_pre, ag)
             parts = comm.rs_linear(attn.view(T, self.nq * self.hd), lw.o, "o")
             x, ag = comm.norm_ag(parts, lw.post_norm, eps, residual)
             act = ops.linear(x, lw.gate_up, epilogue=ops.EPI_SWIGLU, ag=ag)
@@ -290,8 +305,7 @@ class Decoder:
         for i, lw in enumerate(w.layers):
             if i > 0:
                 x = ops.rmsnorm(mlp_parts, lw.input_norm, eps, residual=residual, residual_out=residual)
-            qkv = ops.linear(x, lw.qkv, bias=lw.qkv_bias)
-            attn = self._attend(i, qkv, lw, fb, T, plan, tq_pre)
+            attn = self._qkv_attend(i, x, lw, fb, T, plan, tq_pre)
             o_parts = self._row_parallel(attn.view(T, self.nq * self.hd), lw.o, "o")
             x = ops.rmsnorm(o_parts, lw.post_norm, eps, residual=residual, residual_out=residual)
             if self.moe is not None:

@@ -19,7 +19,7 @@ _ext = None
 _ext_error = None
 _lock = threading.Lock()
 
-EPI_BF16, EPI_F32, EPI_SWIGLU = 0, 1, 2
+EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_PUSH, EPI_QKV = 0, 1, 2, 3, 4
 
 
 def _load():
@@ -414,6 +414,33 @@ def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspac
         out.copy_(r)
         return out
     return r
+
+
+# Off by default: measured 4.6 us/layer slower at TP1 and 3.2 us at TP8 (B=32) than the
+# separate qkv_post kernel, which overlaps the GEMM tail through PDL and spreads the work
+# over many CTAs, while the fused epilogue serialises it in each tile's last CTA.
+_QKV_FUSED = os.environ.get("B200_QKV_FUSED", "0") == "1"
+
+
+def qkv_fused_ok(x, w, k_cache) -> bool:
+    """The fused QKV epilogue applies to CUDA bf16 KV caches with head_dim 128 and a packed
+    tcgen05 weight, when enabled with B200_QKV_FUSED=1."""
+    return (_QKV_FUSED and x.is_cuda and isinstance(w, PackedWeight) and k_cache.dtype == torch.bfloat16
+            and k_cache.shape[-1] == 128)
+
+
+def qkv_fused(x, w, bias, q_norm, k_norm, cos_sin, positions, slots, k_cache, v_cache, nq, nkv, eps, ag=None,
+              workspace=None):
+    """QKV projection with bias, per-head q/k RMSNorm, RoPE and the paged KV write fused into
+    the GEMM epilogue; returns q [T, nq, 128]. Same results as linear() + qkv_post()."""
+    T = x.shape[0]
+    q = torch.empty(T, nq, 128, dtype=x.dtype, device=x.device)
+    ws = workspace or default_workspace(x.device)
+    _cuda(x)
+    ext().gemm_tc_qkv(x, w.data, w.N, bias, q_norm, k_norm, cos_sin, positions, slots, q, k_cache, v_cache, nq,
+                      nkv, float(eps), ws.ws, ws.counters, ag.flags_ptr if ag else 0, ag.n if ag else 0,
+                      ag.epoch_ptr if ag else 0)
+    return q
 
 
 # ------------------------------------------------------------------ attention

@@ -92,6 +92,12 @@ void flag_wait(int64_t flags_ptr, int64_t n, int64_t epoch_ptr, int64_t err_ptr)
 void flag_pingpong(int64_t mine_ptr, int64_t peer_ptr, int64_t iters, int64_t initiator, int64_t mode,
                    torch::Tensor out);
 
+void gemm_tc_qkv(torch::Tensor act, torch::Tensor w, int64_t packed_n, c10::optional<torch::Tensor> bias,
+                 c10::optional<torch::Tensor> q_norm, c10::optional<torch::Tensor> k_norm, torch::Tensor cos_sin,
+                 torch::Tensor positions, torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_cache,
+                 torch::Tensor v_cache, int64_t nq, int64_t nkv, double eps, torch::Tensor ws,
+                 torch::Tensor counters, int64_t ag_flags_ptr, int64_t ag_n, int64_t ag_epoch_ptr);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "b200serve sm_100a kernels";
   m.def("rmsnorm_fused", &rmsnorm_fused);
@@ -125,6 +131,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_plan", &gemm_plan);
   m.def("gemm_tc", &gemm_tc);
   m.def("gemm_tc_ag", &gemm_tc_ag);
+  m.def("gemm_tc_qkv", &gemm_tc_qkv);
   m.def("gemm_error_flag", &gemm_error_flag);
   m.def("gemm_set_trace", &gemm_set_trace);
   m.def("gemm_grouped", &gemm_grouped);

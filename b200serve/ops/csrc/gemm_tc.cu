@@ -174,7 +174,7 @@ void gemm_set_trace(int64_t ptr, int64_t slots) {
 static void gemm_tc_impl(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> bias,
                          c10::optional<torch::Tensor> residual, torch::Tensor ws, torch::Tensor counters, int64_t epi,
                          int64_t force_splits, int64_t packed_n, const int* ag_flags, int ag_n,
-                         const int* ag_epoch) {
+                         const int* ag_epoch, const GemmParams* qkv = nullptr) {
   TORCH_CHECK(act.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16);
   TORCH_CHECK(act.dim() == 2 && w.dim() == 2 && act.stride(1) == 1 && w.is_contiguous());
   const bool packed = packed_n > 0;
@@ -242,6 +242,11 @@ static void gemm_tc_impl(torch::Tensor act, torch::Tensor w, torch::Tensor out, 
   p.ag_flags = ag_flags;
   p.ag_n = ag_n;
   p.ag_epoch = ag_epoch;
+  if (qkv) {
+    p.qkv_nq = qkv->qkv_nq; p.qkv_nkv = qkv->qkv_nkv; p.q_norm = qkv->q_norm; p.k_norm = qkv->k_norm;
+    p.cos_sin = qkv->cos_sin; p.positions = qkv->positions; p.slots = qkv->slots; p.q_out = qkv->q_out;
+    p.k_cache = qkv->k_cache; p.v_cache = qkv->v_cache; p.qkv_eps = qkv->qkv_eps;
+  }
   p.trace = next_trace();
   CUtensorMap tw = weight_tmap(w, N, K, packed);
   CUtensorMap ta = make_tmap_bf16(act.data_ptr(), M, K, act.stride(0), BN);
@@ -264,6 +269,34 @@ void gemm_tc_ag(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::opti
   TORCH_CHECK(ag_flags_ptr && ag_epoch_ptr && ag_n >= 1 && ag_n <= kMaxPeers, "bad all-gather flags");
   gemm_tc_impl(act, w, out, bias, c10::nullopt, ws, counters, epi, 0, packed_n,
                reinterpret_cast<const int*>(ag_flags_ptr), (int)ag_n, reinterpret_cast<const int*>(ag_epoch_ptr));
+}
+
+// Fused QKV projection: x [T, H] @ W_qkv^T (+bias) with the per-head q/k RMSNorm, RoPE and
+// the paged bf16 KV write in the epilogue (head_dim 128): q -> q_out [T, nq, 128], k/v rows ->
+// k_cache / v_cache [blocks][nkv][16][128] at slots (-1 = skip). ag_* as in gemm_tc_ag (0 = none).
+void gemm_tc_qkv(torch::Tensor act, torch::Tensor w, int64_t packed_n, c10::optional<torch::Tensor> bias,
+                 c10::optional<torch::Tensor> q_norm, c10::optional<torch::Tensor> k_norm, torch::Tensor cos_sin,
+                 torch::Tensor positions, torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_cache,
+                 torch::Tensor v_cache, int64_t nq, int64_t nkv, double eps, torch::Tensor ws,
+                 torch::Tensor counters, int64_t ag_flags_ptr, int64_t ag_n, int64_t ag_epoch_ptr) {
+  TORCH_CHECK(cos_sin.size(1) == 128 && k_cache.size(-1) == 128 && k_cache.scalar_type() == at::kBFloat16,
+              "fused QKV epilogue needs head_dim 128 and a bf16 KV cache");
+  TORCH_CHECK(packed_n == (nq + 2 * nkv) * 128, "QKV weight rows must be (nq + 2 nkv) x 128");
+  TORCH_CHECK(q_out.is_contiguous() && q_out.size(0) == act.size(0));
+  GemmParams q{};
+  q.qkv_nq = (int)nq; q.qkv_nkv = (int)nkv;
+  q.q_norm = q_norm ? reinterpret_cast<const __nv_bfloat16*>(q_norm->data_ptr()) : nullptr;
+  q.k_norm = k_norm ? reinterpret_cast<const __nv_bfloat16*>(k_norm->data_ptr()) : nullptr;
+  q.cos_sin = cos_sin.data_ptr<float>();
+  q.positions = positions.data_ptr<int>();
+  q.slots = slots.data_ptr<int>();
+  q.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
+  q.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr());
+  q.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr());
+  q.qkv_eps = (float)eps;
+  gemm_tc_impl(act, w, q_out.view({act.size(0), -1}), bias, c10::nullopt, ws, counters, EPI_QKV, 0, packed_n,
+               ag_flags_ptr ? reinterpret_cast<const int*>(ag_flags_ptr) : nullptr, (int)ag_n,
+               ag_epoch_ptr ? reinterpret_cast<const int*>(ag_epoch_ptr) : nullptr, &q);
 }
 
 // Tensor-parallel GEMM whose epilogue pushes the bf16 output tile into the

@@ -28,7 +28,7 @@
 
 namespace b200 {
 
-enum GemmEpi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_PUSH = 3 };
+enum GemmEpi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_PUSH = 3, EPI_QKV = 4 };
 
 constexpr int kMaxPeers = 8;
 
@@ -44,6 +44,18 @@ struct GemmParams {
   int n_tiles, m_tiles, splits, kb_per_split, kb_total, units;
   int stages;                   // shared-memory ring depth (set by the host launcher)
   int cluster_red;              // 1: the splits of a tile form one cluster and reduce through DSMEM
+  // EPI_QKV: the fused QKV projection's tile n is head slot n (head_dim 128): bias, per-head
+  // q/k RMSNorm, rotate-half RoPE, then q -> q_out [T][nq][128], k/v -> paged bf16 caches
+  int qkv_nq, qkv_nkv;
+  const __nv_bfloat16* q_norm;
+  const __nv_bfloat16* k_norm;
+  const float* cos_sin;         // [max_pos][128] = cos(64) | sin(64)
+  const int* positions;
+  const int* slots;
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* k_cache;       // [blocks][nkv][16][128]
+  __nv_bfloat16* v_cache;
+  float qkv_eps;
   // EPI_PUSH as reduce-scatter: token row t goes only to rank t / rs_rows, at row t % rs_rows
   int rs_rows;
   // all-gather -> GEMM: the activation rows arrive from peers; the producer waits until
@@ -87,8 +99,11 @@ struct GemmCfg {
   // block is sized for MAX_STAGES so its layout does not depend on it
   static constexpr int MAX_STAGES = 12;
   static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;
-  static constexpr int XCHG_FLOATS = 64 * 17;
-  static constexpr size_t smem(int stages) { return 1024 + (size_t)stages * STAGE_BYTES + XCHG_FLOATS * 4 + 256; }
+  // epilogue exchange buffer: 64 rows x 17 (SwiGLU, push staging); the QKV epilogue needs 128 rows
+  static constexpr int xchg_floats(int epi) { return epi == 4 ? 128 * 17 : 64 * 17; }
+  static constexpr size_t smem(int stages, int epi) {
+    return 1024 + (size_t)stages * STAGE_BYTES + xchg_floats(epi) * 4 + 256;
+  }
 };
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -151,6 +166,76 @@ __device__ __forceinline__ void epilogue_store(const GemmParams& p, float* v, in
       }
     }
     epi_bar();
+  } else if constexpr (EPI == EPI_QKV) {
+    // this thread: dim `row` of head slot n_tile, 16 tokens; xchg holds [128 rows][17]
+    const int h = n_tile, d = row;
+    const bool is_q = h < p.qkv_nq, is_k = !is_q && h < p.qkv_nq + p.qkv_nkv;
+    float x[16];
+    const float b = p.bias ? __bfloat162float(p.bias[h * 128 + d]) : 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] = __bfloat162float(__float2bfloat16_rn(v[j] + b));
+    if (is_q || is_k) {
+      const __nv_bfloat16* nw = is_q ? p.q_norm : p.k_norm;
+      if (nw) {
+        // per-token sum of squares over the 128 dims: warp sums, then the 4 warps through xchg
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float s2 = warp_sum(x[j] * x[j]);
+          if (lane == 0) xchg[quad * 16 + j] = s2;
+        }
+        epi_bar();
+        const float wd = __bfloat162float(nw[d]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float tot = xchg[j] + xchg[16 + j] + xchg[32 + j] + xchg[48 + j];
+          const float inv = rsqrtf(tot / 128.f + p.qkv_eps);
+          x[j] = __bfloat162float(__float2bfloat16_rn(__bfloat162float(__float2bfloat16_rn(x[j] * inv)) * wd));
+        }
+        epi_bar();
+      }
+      // rotate-half RoPE: dim d pairs with d ^ 64 (thread row ^ 64). The 16 positions and
+      // their cos/sin are loaded up front (independent loads, one round trip).
+      const int f = d & 63;
+      float cv[16], sv[16];
+      {
+        int pos[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) pos[j] = p.positions[min(t0 + j, t_end - 1)];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float* cs = p.cos_sin + (size_t)pos[j] * 128;
+          cv[j] = cs[f];
+          sv[j] = cs[64 + f];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) xchg[d * 17 + j] = x[j];
+      epi_bar();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float partner = xchg[(d ^ 64) * 17 + j];
+        x[j] = d < 64 ? x[j] * cv[j] - partner * sv[j] : x[j] * cv[j] + partner * sv[j];
+      }
+      epi_bar();
+    }
+    if (is_q) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (t0 + j < t_end) p.q_out[((size_t)(t0 + j) * p.qkv_nq + h) * 128 + d] = __float2bfloat16_rn(x[j]);
+    } else {
+      int sl[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) sl[j] = t0 + j < t_end ? p.slots[t0 + j] : -1;
+      const int kvh = is_k ? h - p.qkv_nq : h - p.qkv_nq - p.qkv_nkv;
+      __nv_bfloat16* cache = is_k ? p.k_cache : p.v_cache;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (sl[j] >= 0) {
+          const size_t r = ((size_t)(sl[j] >> 4) * p.qkv_nkv + kvh) * 16 + (sl[j] & 15);
+          cache[r * 128 + d] = __float2bfloat16_rn(x[j]);
+        }
+      }
+    }
   } else {
     const int col = n_tile * 128 + row;
     if (col >= p.N) return;
@@ -292,7 +377,7 @@ __global__ void __launch_bounds__(192, 2)
   uint8_t* s_w = smem;
   uint8_t* s_a = smem + STAGES * Cfg::W_BYTES;
   float* xchg = reinterpret_cast<float*>(s_a + STAGES * Cfg::A_BYTES);
-  uint64_t* full = reinterpret_cast<uint64_t*>(xchg + Cfg::XCHG_FLOATS);
+  uint64_t* full = reinterpret_cast<uint64_t*>(xchg + Cfg::xchg_floats(EPI));
   uint64_t* empty = full + Cfg::MAX_STAGES;
   uint64_t* tfull = empty + Cfg::MAX_STAGES;
   uint64_t* tempty = tfull + 2;
@@ -559,13 +644,13 @@ void launch_gemm(const CUtensorMap& tw, const CUtensorMap& ta, const GemmParams&
                                          227 * 1024));
     attr_set = true;
   }
-  TORCH_CHECK(p.stages >= 2 && p.stages <= Cfg::MAX_STAGES && Cfg::smem(p.stages) <= 227 * 1024,
+  TORCH_CHECK(p.stages >= 2 && p.stages <= Cfg::MAX_STAGES && Cfg::smem(p.stages, EPI) <= 227 * 1024,
               "GEMM stage count out of range");
   if (p.cluster_red)
-    launch_pdl_cluster(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(192), Cfg::smem(p.stages), stream, p.splits, tw,
+    launch_pdl_cluster(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(192), Cfg::smem(p.stages, EPI), stream, p.splits, tw,
                        ta, p);
   else
-    launch_pdl(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(192), Cfg::smem(p.stages), stream, tw, ta, p);
+    launch_pdl(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(192), Cfg::smem(p.stages, EPI), stream, tw, ta, p);
 }
 
 // one translation unit per BN (gemm_tc_bn*.cu) instantiates this for every epilogue

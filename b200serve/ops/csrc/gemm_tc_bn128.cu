@@ -11,6 +11,7 @@ void launch_gemm_bn<128>(int epi, const CUtensorMap& tw, const CUtensorMap& ta, 
     case EPI_F32: launch_gemm<128, EPI_F32>(tw, ta, p, grid, stream); break;
     case EPI_SWIGLU: launch_gemm<128, EPI_SWIGLU>(tw, ta, p, grid, stream); break;
     case EPI_PUSH: launch_gemm<128, EPI_PUSH>(tw, ta, p, grid, stream); break;
+    case EPI_QKV: launch_gemm<128, EPI_QKV>(tw, ta, p, grid, stream); break;
     default: TORCH_CHECK(false, "bad epilogue");
   }
 }

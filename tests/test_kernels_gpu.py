@@ -113,6 +113,32 @@ def test_qkv_post(hd, nq, nkv, qk_norm, bias):
     assert _rel(vc.cpu(), vc2) < 1e-2
 
 
+@pytest.mark.parametrize("T", [5, 32, 300])
+@pytest.mark.parametrize("qk_norm,bias", [(True, False), (False, True)])
+def test_qkv_fused_epilogue_matches_two_kernels(T, qk_norm, bias):
+    """QKV GEMM with bias, q/k norm, RoPE and the paged KV write in its epilogue vs the
+    separate GEMM + qkv_post kernels."""
+    H, nq, nkv, hd, nb = 1024, 8, 2, 128, 32
+    x = torch.randn(T, H, device=dev).bfloat16()
+    w = ops.pack_weight((torch.randn((nq + 2 * nkv) * hd, H, device=dev) * 0.05).bfloat16())
+    b = torch.randn((nq + 2 * nkv) * hd, device=dev).bfloat16() if bias else None
+    qn = torch.randn(hd, device=dev).bfloat16() if qk_norm else None
+    kn = torch.randn(hd, device=dev).bfloat16() if qk_norm else None
+    cs = ops.rope_cos_sin(hd, 4096, 1e6, dev)
+    pos = torch.randint(0, 4000, (T,), device=dev, dtype=torch.int32)
+    slots = torch.randperm(nb * 16, device=dev)[:T].int()
+    slots[::7] = -1
+    kc = torch.zeros(nb, nkv, 16, hd, device=dev).bfloat16()
+    vc = torch.zeros_like(kc)
+    kc2, vc2 = kc.clone(), vc.clone()
+    q = ops.qkv_fused(x, w, b, qn, kn, cs, pos, slots, kc, vc, nq, nkv, 1e-6)
+    qkv = ops.linear(x, w, bias=b)
+    q2 = ops.qkv_post(qkv, None, qn, kn, cs, pos, slots, kc2, vc2, nq, nkv, 1e-6)
+    assert _rel(q, q2) < 1e-2
+    assert _rel(kc, kc2) < 1e-2
+    assert _rel(vc, vc2) < 1e-2
+
+
 def _make_paged(B, lens, nkv, hd, nb_total):
     kc = torch.randn(nb_total, nkv, 16, hd, device=dev).bfloat16()
     vc = torch.randn(nb_total, nkv, 16, hd, device=dev).bfloat16()
