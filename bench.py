@@ -50,6 +50,10 @@ def parse():
     ap.add_argument("--weights", default="bf16", choices=["bf16", "gguf"],
                     help="gguf: random-init bf16 weights quantised on the GPU into the Q4_K_M mix")
     ap.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for the headline)")
+    ap.add_argument("--serve", action="store_true",
+                    help="long-context concurrent serving through the chat API (b200serve.utils.serve_bench)")
+    ap.add_argument("--requests", type=int, default=64, help="--serve: concurrent requests")
+    ap.add_argument("--max-prompt", type=int, default=32768, help="--serve: longest prompt (tokens)")
     return ap.parse_args()
 
 
@@ -313,6 +317,17 @@ def main():
     gguf = a.weights == "gguf"
     a.batch = a.batch or (64 if moe else 8 if gguf else 32)
     a.prompt = a.prompt or (512 if moe else 1024 if gguf else 2048)
+    if a.serve:
+        if a.impl == "reference":
+            emit({"impl": "reference", "unavailable": "the reference serves one request at a time "
+                  "(core/model_queue.py); its serving number is its single-request decode rate"})
+            return
+        from b200serve.utils.serve_bench import run
+        out = run(gpus=a.gpus, requests=a.requests, max_prompt=a.max_prompt, comm=a.comm)
+        if out is not None:
+            out["impl"] = "ours"
+            emit(out)
+        return
     if a.impl == "reference":
         run_reference(a)
     else:
