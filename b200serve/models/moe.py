@@ -66,9 +66,10 @@ def pack_experts(stacked: torch.Tensor):
 class MoEBlock:
     """Expert FFN of every MoE layer. On CUDA: router GEMM -> top-k kernel ->
     permutation (this rank's experts only) -> row gather -> grouped SwiGLU GEMM ->
-    grouped down GEMM -> weighted combine. The caller sums the combine output over
-    expert-parallel ranks (tokens are replicated on every rank, so dispatch needs
-    no communication and the combine is one all-reduce of [T, H])."""
+    grouped down GEMM -> weighted combine. Tokens are replicated on every rank (the
+    attention output is all-reduced), so dispatch needs no communication; the combine
+    is summed over the expert-parallel ranks, fused into the combine kernel as NVLink
+    pushes for decode-sized steps (``reduced``)."""
 
     def __init__(self, cfg, weights, comm=None, device="cpu"):
         self.cfg = cfg
@@ -85,7 +86,7 @@ class MoEBlock:
                 lw.experts_gate_up = lw.experts_down = None
             torch.cuda.empty_cache()
 
-    def _cuda(self, layer, x):
+    def _cuda(self, layer, x, fused_reduce=False):
         cfg = self.cfg
         lw = self.w.layers[layer]
         T, H = x.shape
@@ -107,10 +108,26 @@ class MoEBlock:
         e.gemm_grouped(xs, gu, n_gu, E, offsets, T, act, ws.ws, ws.counters, ops.EPI_SWIGLU)
         y = torch.empty(T * k, n_dn, dtype=x.dtype, device=dev)
         e.gemm_grouped(act, dn, n_dn, E, offsets, T, y, ws.ws, ws.counters, ops.EPI_BF16)
+        ops._launches[0] += 7
+        if fused_reduce:
+            # combine + cross-rank sum in one kernel (NVLink pushes + flags); returns the parts
+            ops._launches[0] += 1
+            return self.comm.moe_combine_reduce(y, wts, pos, k, T)
         out = torch.empty(T, H, dtype=x.dtype, device=dev)
         e.moe_combine(y, wts, pos, k, out)
-        ops._launches[0] += 8
+        ops._launches[0] += 1
         return out
+
+    def reduced(self, layer: int, x: torch.Tensor):
+        """Expert FFN output summed over the expert-parallel ranks, as the parts the next norm
+        consumes: the fused combine-push on the NVLink communicator for decode-sized steps,
+        else the local combine followed by the communicator's all-reduce."""
+        comm = self.comm
+        if (x.is_cuda and comm is not None and hasattr(comm, "moe_combine_reduce")
+                and x.shape[0] <= getattr(comm, "max_tokens", 0)):
+            return self._cuda(layer, x, fused_reduce=True)
+        out = self(layer, x)
+        return comm.reduce_parts(out, "mlp") if comm is not None else [out]
 
     def __call__(self, layer: int, x: torch.Tensor) -> torch.Tensor:
         if x.is_cuda:

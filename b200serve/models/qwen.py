@@ -309,7 +309,7 @@ class Decoder:
             o_parts = self._row_parallel(attn.view(T, self.nq * self.hd), lw.o, "o")
             x = ops.rmsnorm(o_parts, lw.post_norm, eps, residual=residual, residual_out=residual)
             if self.moe is not None:
-                mlp_parts = self.comm.reduce_parts(self.moe(i, x), "mlp")
+                mlp_parts = self.moe.reduced(i, x)
             else:
                 act = ops.linear(x, lw.gate_up, epilogue=ops.EPI_SWIGLU)
                 mlp_parts = self._row_parallel(act, lw.down, "mlp")

@@ -98,6 +98,9 @@ void gemm_tc_qkv(torch::Tensor act, torch::Tensor w, int64_t packed_n, c10::opti
                  torch::Tensor v_cache, int64_t nq, int64_t nkv, double eps, torch::Tensor ws,
                  torch::Tensor counters, int64_t ag_flags_ptr, int64_t ag_n, int64_t ag_epoch_ptr);
 
+void moe_combine_push(torch::Tensor y, torch::Tensor w, torch::Tensor pos, int64_t k, int64_t T, int64_t H,
+                      torch::Tensor dst_ptrs, torch::Tensor flag_ptrs, int64_t epoch_ptr, torch::Tensor done);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "b200serve sm_100a kernels";
   m.def("rmsnorm_fused", &rmsnorm_fused);
@@ -124,6 +127,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_permute", &moe_permute);
   m.def("gather_rows", &gather_rows);
   m.def("moe_combine", &moe_combine);
+  m.def("moe_combine_push", &moe_combine_push);
   m.def("gguf_gemm", &gguf_gemm);
   m.def("paged_decode_attention_q4", &paged_decode_attention_q4);
   m.def("qkv_post_q4", &qkv_post_q4);

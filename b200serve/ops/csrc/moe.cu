@@ -130,6 +130,49 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const fl
   }
 }
 
+// Combine fused with the expert-parallel reduction: like moe_combine_kernel, but every CTA
+// stores its combined row into the receive slot of every rank (NVLink P2P); the CTA that
+// finishes last publishes flag[r] = epoch on every rank (one system fence, relaxed stores).
+struct CombinePush {
+  __nv_bfloat16* dst[8];
+  int* flag[8];
+  int world;
+  int* done;                 // local counter of finished CTAs, zero on entry and exit
+  const int* epoch;
+};
+
+__global__ void moe_combine_push_kernel(const __nv_bfloat16* __restrict__ y, const float* __restrict__ w,
+                                        const int* __restrict__ pos, int k, int H, const CombinePush cp) {
+  pdl_wait();
+  const int t = blockIdx.x;
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int j = 0; j < k; ++j) {
+      const int p = pos[t * k + j];
+      if (p < 0) continue;
+      const float wt = w[t * k + j];
+      float f[8];
+      unpack8(*reinterpret_cast<const bf16x8*>(y + (size_t)p * H + c), f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += wt * f[i];
+    }
+    const bf16x8 v = pack8(acc);
+    for (int r = 0; r < cp.world; ++r) *reinterpret_cast<bf16x8*>(cp.dst[r] + (size_t)t * H + c) = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int old = atomicAdd(cp.done, 1);
+    if (old == (int)gridDim.x - 1) {
+      *cp.done = 0;
+      __threadfence_system();
+      const int e = *cp.epoch;
+      for (int r = 0; r < cp.world; ++r)
+        asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(cp.flag[r]), "r"(e) : "memory");
+    }
+  }
+}
+
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ rows,
                                    const int* __restrict__ count, int H, __nv_bfloat16* __restrict__ out) {
   pdl_wait();
@@ -191,4 +234,23 @@ void moe_combine(torch::Tensor y, torch::Tensor w, torch::Tensor pos, int64_t k,
       reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), w.data_ptr<float>(), pos.data_ptr<int>(), (int)k, H,
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
   B200_CHECK_CUDA(cudaGetLastError());
+}
+
+// y [rows, H] expert outputs, w/pos [T, k]; dst_ptrs/flag_ptrs host int64 [world]; done int32 [1].
+void moe_combine_push(torch::Tensor y, torch::Tensor w, torch::Tensor pos, int64_t k, int64_t T, int64_t H,
+                      torch::Tensor dst_ptrs, torch::Tensor flag_ptrs, int64_t epoch_ptr, torch::Tensor done) {
+  const int world = dst_ptrs.numel();
+  TORCH_CHECK(H % 8 == 0 && world >= 1 && world <= 8 && flag_ptrs.numel() == world && dst_ptrs.device().is_cpu());
+  if (T == 0) return;
+  CombinePush cp{};
+  cp.world = world;
+  cp.done = done.data_ptr<int>();
+  cp.epoch = reinterpret_cast<const int*>(epoch_ptr);
+  for (int r = 0; r < world; ++r) {
+    cp.dst[r] = reinterpret_cast<__nv_bfloat16*>(dst_ptrs.data_ptr<int64_t>()[r]);
+    cp.flag[r] = reinterpret_cast<int*>(flag_ptrs.data_ptr<int64_t>()[r]);
+  }
+  launch_pdl(moe_combine_push_kernel, dim3((unsigned)T), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+             reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), w.data_ptr<float>(), pos.data_ptr<int>(), (int)k,
+             (int)H, cp);
 }

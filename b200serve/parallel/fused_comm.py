@@ -202,6 +202,17 @@ class FusedComm:
         full = _tensor_from_ptr(self._ag_base(self.base, par), T * self.H, self.device).view(T, self.H)
         return full, ops.AGWait(self._flag_ptr(self.base, site, 0), self.world, self.epoch.data_ptr(), self.err_dev)
 
+    def moe_combine_reduce(self, y, wts, pos, k, T):
+        """Expert-parallel combine fused with the cross-rank sum: the combine kernel pushes each
+        token's weighted expert sum into every rank's slot and raises the site's flags; the
+        next norm waits for them and sums the ``world`` slots."""
+        site = self._next_site()
+        dst, flg = self._push_ptrs(site)
+        ops._cuda(y)
+        ops.ext().moe_combine_push(y, wts, pos, k, T, self.H, dst, flg, self.epoch.data_ptr(), self.ag_done)
+        return FusedParts(self._local_views(site % 2, T), self._flag_ptr(self.base, site, 0),
+                          self.epoch.data_ptr(), self.err_dev)
+
     def reduce_parts(self, t: torch.Tensor, tag: str):
         return self.nccl.reduce_parts(t, tag)
 

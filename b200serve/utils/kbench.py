@@ -120,6 +120,40 @@ def attn_one(B=32, L=2304, nq=32, nkv=8, iters=5):
                       "GBps": round(byts / ms / 1e6, 1)}))
 
 
+def prefill_attn_one(q_len=2048, kv_len=8192, nq=32, nkv=8, kvq=0, iters=3):
+    """Chunked-prefill attention: one sequence, ``q_len`` new tokens at the end of ``kv_len``
+    cached tokens (causal), bf16 (kvq=0) or int4g128 (kvq=1) KV. Reports TFLOP/s of the
+    causal QK^T + PV work (4 * q * kv_effective * heads * 128)."""
+    hd = 128
+    nblk = (kv_len + 15) // 16
+    bt = torch.arange(nblk, device="cuda", dtype=torch.int32).view(1, nblk)
+    sl = torch.tensor([kv_len], dtype=torch.int32, device="cuda")
+    qs = torch.tensor([kv_len - q_len], dtype=torch.int32, device="cuda")
+    cu = torch.tensor([0, q_len], dtype=torch.int32, device="cuda")
+    q = torch.randn(q_len, nq, hd, device="cuda").bfloat16()
+    scale = 1 / math.sqrt(hd)
+    if kvq:
+        kc = torch.randint(0, 255, (nblk, nkv, 16, hd // 2), dtype=torch.uint8, device="cuda")
+        vc = torch.randint(0, 255, (nblk, nkv, 16, hd // 2), dtype=torch.uint8, device="cuda")
+        ks = (torch.rand(nblk, nkv, 16, device="cuda") * 0.1 + 0.01).half()
+        vs = (torch.rand(nblk, nkv, 16, device="cuda") * 0.1 + 0.01).half()
+        out = torch.empty_like(q)
+        fn = lambda: ops.ext().paged_prefill_attention_q4(q, kc, vc, ks, vs, bt, sl, qs, cu, out, scale, q_len)
+    else:
+        kc = torch.randn(nblk, nkv, 16, hd, device="cuda").bfloat16()
+        vc = torch.randn_like(kc)
+        fn = lambda: ops.paged_prefill_attention(q, kc, vc, bt, sl, qs, cu, scale, max_q=q_len)
+    for _ in range(iters):
+        fn()
+    torch.cuda.synchronize()
+    ms = time_cuda(fn, iters=5, warmup=1)
+    # causal: query i (at position kv_len - q_len + i) sees kv_len - q_len + i + 1 keys
+    keys = q_len * (kv_len - q_len) + q_len * (q_len + 1) / 2
+    flops = 4.0 * keys * nq * hd
+    print(json.dumps({"case": "prefill_attn", "q_len": q_len, "kv_len": kv_len, "kvq": kvq, "ms": round(ms, 3),
+                      "TFLOPs": round(flops / ms / 1e9, 1)}))
+
+
 def gguf_one(M=8, N=6144, K=4096, iters=5):
     from b200serve.models.gguf_gpu import to_quant_weight
     w = (torch.randn(N, K, device="cuda") * 0.02)
@@ -366,6 +400,9 @@ if __name__ == "__main__":
         sys.exit(0)
     if what == "attn_one":
         attn_one(*[int(v) for v in sys.argv[2:6]])
+        sys.exit(0)
+    if what == "prefill_attn_one":
+        prefill_attn_one(*[int(v) for v in sys.argv[2:7]])
         sys.exit(0)
     if what == "gguf_one":
         gguf_one(*[int(v) for v in sys.argv[2:5]])

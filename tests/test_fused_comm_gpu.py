@@ -78,15 +78,16 @@ def test_fused_allreduce_matches_nccl():
     assert max(res.values()) < 2e-2, res
 
 
-def _tp_worker(rank, world, port, comm_kind, q):
+def _tp_worker(rank, world, port, comm_kind, q, model="qwen3-8b"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     from b200serve.core.config import EngineConfig
     from b200serve.engine.b200_engine import B200Engine
     from b200serve.engine.sampler import SamplingParams
     from b200serve.parallel.worker import worker_loop
-    cfg = EngineConfig(model="qwen3-8b", num_layers_override=2, tp_size=world, comm=comm_kind, max_batch=8,
-                       max_seq=512, kv_blocks=256)
+    moe = model != "qwen3-8b"
+    cfg = EngineConfig(model=model, num_layers_override=2, tp_size=world, ep_size=world if moe else 1,
+                       comm=comm_kind, max_batch=8, max_seq=512, kv_blocks=256)
     eng = B200Engine(cfg)
     eng.load()
     if rank == 0:
@@ -103,11 +104,11 @@ def _tp_worker(rank, world, port, comm_kind, q):
     dist.destroy_process_group()
 
 
-def _run_tp(kind):
+def _run_tp(kind, model="qwen3-8b"):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_tp_worker, args=(r, 2, port, kind, q)) for r in range(2)]
+    ps = [ctx.Process(target=_tp_worker, args=(r, 2, port, kind, q, model)) for r in range(2)]
     for p in ps:
         p.start()
     out = q.get(timeout=600)
@@ -196,4 +197,11 @@ def test_tp2_rsag_equals_nccl():
     finally:
         os.environ.pop("B200_TP_MODE", None)
     b = _run_tp("nccl")
+    assert [x[:4] for x in a] == [x[:4] for x in b]
+
+
+@needs2
+def test_ep2_moe_fused_combine_equals_nccl():
+    """Expert parallelism with the combine kernel pushing its sums over NVLink vs NCCL."""
+    a, b = _run_tp("fused", "qwen3-30b-a3b"), _run_tp("nccl", "qwen3-30b-a3b")
     assert [x[:4] for x in a] == [x[:4] for x in b]
