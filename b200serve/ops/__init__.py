@@ -453,6 +453,7 @@ class AttnWorkspace:
 
 
 _FORCE_SIMT_DECODE = os.environ.get("B200_TC_DECODE", "1") == "0"   # B200_TC_DECODE=0 selects the CUDA-core kernel
+_TC_PREFILL = os.environ.get("B200_TC_PREFILL", "1") != "0"         # tcgen05 prefill attention (bf16 KV)
 
 
 def paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, scale, tps=256, nsplit=1,
@@ -505,8 +506,15 @@ def paged_prefill_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start
     """
     if _cuda(q):
         out = out if out is not None else torch.empty_like(q)
-        ext().paged_prefill_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, cu_q, out,
-                                      float(scale), int(max_q if max_q is not None else q.shape[0]))
+        mq = int(max_q if max_q is not None else q.shape[0])
+        G = q.shape[1] // k_cache.shape[1]
+        if (_TC_PREFILL and q.shape[2] == 128 and k_cache.dtype == torch.bfloat16 and G in (1, 2, 4, 8)
+                and q.is_contiguous()):
+            ext().paged_prefill_attention_tc(q, k_cache, v_cache, block_tables, seq_lens, q_start, cu_q, out,
+                                             float(scale), mq)
+        else:
+            ext().paged_prefill_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, cu_q, out,
+                                          float(scale), mq)
         return out
     T, nq, hd = q.shape
     nkv = k_cache.shape[1]

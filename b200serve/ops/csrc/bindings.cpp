@@ -101,6 +101,11 @@ void gemm_tc_qkv(torch::Tensor act, torch::Tensor w, int64_t packed_n, c10::opti
 void moe_combine_push(torch::Tensor y, torch::Tensor w, torch::Tensor pos, int64_t k, int64_t T, int64_t H,
                       torch::Tensor dst_ptrs, torch::Tensor flag_ptrs, int64_t epoch_ptr, torch::Tensor done);
 
+void paged_prefill_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                                torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor q_start,
+                                torch::Tensor cu_q, torch::Tensor out, double scale, int64_t max_q);
+int64_t prefill_tc_error(bool reset);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "b200serve sm_100a kernels";
   m.def("rmsnorm_fused", &rmsnorm_fused);
@@ -122,6 +127,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding", &embedding);
   m.def("paged_decode_attention", &paged_decode_attention);
   m.def("paged_prefill_attention", &paged_prefill_attention);
+  m.def("paged_prefill_attention_tc", &paged_prefill_attention_tc);
+  m.def("prefill_tc_error", &prefill_tc_error);
   m.def("paged_decode_attention_tc", &paged_decode_attention_tc);
   m.def("topk_softmax", &topk_softmax);
   m.def("moe_permute", &moe_permute);

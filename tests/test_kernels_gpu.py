@@ -139,6 +139,46 @@ def test_qkv_fused_epilogue_matches_two_kernels(T, qk_norm, bias):
     assert _rel(vc, vc2) < 1e-2
 
 
+@pytest.mark.parametrize("G", [1, 4, 8])
+@pytest.mark.parametrize("case", ["single", "chunked", "batch"])
+def test_prefill_attention_tcgen05_matches_reference(G, case):
+    """tcgen05 prefill attention (bf16 paged KV) against the fp32 reference of the same op."""
+    torch.manual_seed(5)
+    nkv, hd = 2, 128
+    nq = nkv * G
+    if case == "single":
+        qlens, starts = [300], [0]
+    elif case == "chunked":
+        qlens, starts = [77], [390]
+    else:
+        qlens, starts = [130, 5, 257], [0, 200, 31]
+    lens = [s0 + n for s0, n in zip(starts, qlens)]
+    nb_total = sum((l + 15) // 16 for l in lens) + 4
+    kc = torch.randn(nb_total, nkv, 16, hd, device=dev).bfloat16()
+    vc = torch.randn_like(kc)
+    maxb = max((l + 15) // 16 for l in lens)
+    perm = torch.randperm(nb_total, device=dev)
+    bt = torch.zeros(len(lens), maxb, dtype=torch.int32, device=dev)
+    used = 0
+    for b, l in enumerate(lens):
+        n = (l + 15) // 16
+        bt[b, :n] = perm[used:used + n].int()
+        used += n
+    T = sum(qlens)
+    q = torch.randn(T, nq, hd, device=dev).bfloat16()
+    cu = torch.tensor([0] + list(torch.tensor(qlens).cumsum(0)), dtype=torch.int32, device=dev)
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    qs = torch.tensor(starts, dtype=torch.int32, device=dev)
+    scale = 1 / math.sqrt(hd)
+    out = torch.empty_like(q)
+    ops.ext().paged_prefill_attention_tc(q, kc, vc, bt, sl, qs, cu, out, scale, max(qlens))
+    torch.cuda.synchronize()
+    assert ops.ext().prefill_tc_error(True) == 0
+    ref = ops.paged_prefill_attention(q.float().cpu(), kc.float().cpu(), vc.float().cpu(), bt.cpu(), sl.cpu(),
+                                      qs.cpu(), cu.cpu(), scale)
+    assert _rel(out.float().cpu(), ref) < 2e-2
+
+
 def _make_paged(B, lens, nkv, hd, nb_total):
     kc = torch.randn(nb_total, nkv, 16, hd, device=dev).bfloat16()
     vc = torch.randn(nb_total, nkv, 16, hd, device=dev).bfloat16()
