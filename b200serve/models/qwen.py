@@ -174,7 +174,7 @@ class Decoder:
                                              max(nsplit, ws.max_splits if ws else 1))
         return self.attn_ws
 
-    def _attention_q4(self, i, qkv, lw, fb, T, tps, nsplit, ws):
+    def _attention_q4(self, i, qkv, lw, fb, T, tps, nsplit, ws, pre=None):
         """Attention over the int4g128 cache: K/V quantised on write, dequantised inside the kernels."""
         kv = self.kv
         kc, vc, ksc, vsc = kv.k[i], kv.v[i], kv.k_scale[i], kv.v_scale[i]
@@ -191,6 +191,13 @@ class Decoder:
                 ops._cuda(q, 2)
                 ops.ext().paged_decode_attention_q4(q, kc, vc, ksc, vsc, fb.block_tables, fb.seq_lens, out, acc, ml,
                                                     self.scale, tps, nsplit)
+            elif ops._TC_PREFILL and pre is not None:
+                # the batch's pages dequantised to bf16, then the tcgen05 prefill attention
+                ids, tables, kd, vd = pre
+                ops.q4_dequant_pages(ids, kc, ksc, kd)
+                ops.q4_dequant_pages(ids, vc, vsc, vd)
+                ops.paged_prefill_attention(q, kd, vd, tables, fb.seq_lens, fb.q_start, fb.cu_q, self.scale,
+                                            out=out, max_q=fb.max_q)
             else:
                 ops._cuda(q)
                 ops.ext().paged_prefill_attention_q4(q, kc, vc, ksc, vsc, fb.block_tables, fb.seq_lens, fb.q_start,
@@ -240,7 +247,7 @@ class Decoder:
         if self.tq is not None:
             return self._attention_tq(i, qkv, lw, fb, T, tps, nsplit, ws, tq_pre)
         if self.kv.kv_format == "int4g128":
-            return self._attention_q4(i, qkv, lw, fb, T, tps, nsplit, ws)
+            return self._attention_q4(i, qkv, lw, fb, T, tps, nsplit, ws, tq_pre)
         kc, vc = self.kv.k[i], self.kv.v[i]
         q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots, kc, vc,
                          self.nq, self.nkv, eps)
@@ -296,7 +303,8 @@ class Decoder:
         if fb.is_decode:
             tps, nsplit = attn_plan or self.decode_attn_plan(T, int(fb.block_tables.shape[1]) * 16)
             ws = self.ensure_attn_workspace(T, nsplit) if nsplit > 1 else None
-        tq_pre = self._tq_prefill_pages(fb) if (self.tq is not None and not fb.is_decode) else None
+        quant_kv = self.tq is not None or (self.kv.kv_format == "int4g128" and h.is_cuda and ops._TC_PREFILL)
+        tq_pre = self._tq_prefill_pages(fb) if (quant_kv and not fb.is_decode) else None
         plan = (tps, nsplit, ws) if fb.is_decode else (0, 0, None)
         if self.moe is None and comm.world > 1 and hasattr(comm, "use_rsag") and comm.use_rsag(T):
             return self._forward_rsag(fb, h, plan, tq_pre)

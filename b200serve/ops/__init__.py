@@ -778,6 +778,17 @@ def tq_decode_attention(q_rot, q_jl, kv, layer: int, tb: TurboQuantTables, block
     return paged_decode_attention(q_rot, kd, vd, tables, seq_lens, scale)
 
 
+def q4_dequant_pages(block_ids, codes, scales, out):
+    """int4g128 pages ``block_ids`` of codes [blocks][nkv][16][64] + scales [blocks][nkv][16] ->
+    bf16 pages 0.. of ``out`` [n][nkv][16][128]."""
+    if _cuda(out):
+        ext().q4_dequant_pages(block_ids, codes, scales, out)
+        return out
+    ids = block_ids.long()
+    out[:ids.numel()] = q4_dequantize_rows(codes[ids], scales[ids]).to(out.dtype)
+    return out
+
+
 def gemm_error_flag(reset: bool = True) -> int:
     return int(ext().gemm_error_flag(reset)) if extension_loaded() else 0
 

@@ -253,6 +253,33 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(
   }
 }
 
+// int4g128 pages -> bf16 pages (for the tensor-core prefill attention): pages block_ids[j] of
+// codes [blocks][nkv][16][64] + fp16 scale [blocks][nkv][16] -> out [j][nkv][16][128]. Dims
+// (2p, 2p+1) of each 8-dim group sit in nibbles (p, p + 4) of the group's 32-bit word.
+__global__ void q4_dequant_pages_kernel(const int* __restrict__ block_ids, int n, int nkv,
+                                        const uint32_t* __restrict__ codes, const __half* __restrict__ scales,
+                                        __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t words = (int64_t)n * nkv * 16 * 16;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < words; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i >> 4;                      // (j, h, token) row of the output
+    const int g = (int)(i & 15);
+    const int j = (int)(row / (nkv * 16));
+    const int64_t src_row = (int64_t)block_ids[j] * nkv * 16 + row % (nkv * 16);
+    const uint32_t w = codes[src_row * 16 + g];
+    const float sc = __half2float(scales[src_row]);
+    uint32_t o[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const float lo = (float)((int)((w >> (4 * p)) & 15u) - 8) * sc;
+      const float hi = (float)((int)((w >> (4 * (p + 4))) & 15u) - 8) * sc;
+      o[p] = pack_bf16x2(lo, hi);
+    }
+    *reinterpret_cast<uint4*>(out + row * 128 + g * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 }  // namespace b200
 
 using namespace b200;
@@ -310,4 +337,15 @@ void paged_prefill_attention_q4(torch::Tensor q, torch::Tensor k_codes, torch::T
   prefill_impl(q, k_codes, v_codes, block_tables, seq_lens, q_start, cu_q, out, scale, max_q, 1,
                k_codes.data_ptr<uint8_t>(), v_codes.data_ptr<uint8_t>(),
                reinterpret_cast<const __half*>(k_scale.data_ptr()), reinterpret_cast<const __half*>(v_scale.data_ptr()));
+}
+
+void q4_dequant_pages(torch::Tensor block_ids, torch::Tensor codes, torch::Tensor scales, torch::Tensor out) {
+  const int n = block_ids.numel(), nkv = codes.size(1);
+  TORCH_CHECK(codes.size(2) == 16 && codes.size(3) == 64 && out.size(0) >= n && out.size(3) == 128);
+  if (n == 0) return;
+  const int64_t words = (int64_t)n * nkv * 16 * 16;
+  const int blocks = (int)std::min<int64_t>((words + 255) / 256, 148 * 8);
+  launch_pdl(q4_dequant_pages_kernel, dim3(blocks), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+             (const int*)block_ids.data_ptr<int>(), n, nkv, reinterpret_cast<const uint32_t*>(codes.data_ptr()),
+             reinterpret_cast<const __half*>(scales.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
 }

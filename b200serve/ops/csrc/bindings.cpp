@@ -106,6 +106,8 @@ void paged_prefill_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::T
                                 torch::Tensor cu_q, torch::Tensor out, double scale, int64_t max_q);
 int64_t prefill_tc_error(bool reset);
 
+void q4_dequant_pages(torch::Tensor block_ids, torch::Tensor codes, torch::Tensor scales, torch::Tensor out);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "b200serve sm_100a kernels";
   m.def("rmsnorm_fused", &rmsnorm_fused);
@@ -128,6 +130,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_decode_attention", &paged_decode_attention);
   m.def("paged_prefill_attention", &paged_prefill_attention);
   m.def("paged_prefill_attention_tc", &paged_prefill_attention_tc);
+  m.def("q4_dequant_pages", &q4_dequant_pages);
   m.def("prefill_tc_error", &prefill_tc_error);
   m.def("paged_decode_attention_tc", &paged_decode_attention_tc);
   m.def("topk_softmax", &topk_softmax);

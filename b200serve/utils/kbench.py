@@ -154,6 +154,37 @@ def prefill_attn_one(q_len=2048, kv_len=8192, nq=32, nkv=8, kvq=0, iters=3):
                       "TFLOPs": round(flops / ms / 1e9, 1)}))
 
 
+def tq_attn_one(B=32, L=2304, nq=32, nkv=8, kbits=4, vbits=4, iters=5):
+    """Decode attention over the TurboQuant paged KV (random codes) at one shape. Reports the
+    code bytes streamed per second (K+V codes, QJL signs, per-row scalars)."""
+    from b200serve.engine.kv_cache import KVCache
+    hd = 128
+    nblk = (L + 15) // 16
+    kv = KVCache(1, B * nblk, nkv, hd, kv_format="turboquant", key_bits=kbits, value_bits=vbits, device="cuda")
+    kv.k.random_(0, 256)
+    kv.v.random_(0, 256)
+    kv.k_sign.random_(0, 256)
+    kv.k_scale.uniform_(0.5, 2.0)
+    kv.v_scale.uniform_(0.5, 2.0)
+    tb = ops.TurboQuantTables(kbits, vbits, "cuda")
+    bt = torch.arange(B * nblk, device="cuda", dtype=torch.int32).view(B, nblk)
+    sl = torch.full((B,), L, dtype=torch.int32, device="cuda")
+    qr = torch.randn(B, nq, hd, device="cuda").bfloat16()
+    qj = torch.randn(B, nq, hd, device="cuda").bfloat16()
+    per = B * nkv
+    tps = 4096 if per >= 148 else min(4096, max(64, (2048 * per // 148 + 15) // 16 * 16))
+    nsplit = (L + tps - 1) // tps
+    ws = ops.AttnWorkspace("cuda", B, nkv, nq // nkv, hd, nsplit) if nsplit > 1 else None
+    fn = lambda: ops.tq_decode_attention(qr, qj, kv, 0, tb, bt, sl, 1 / math.sqrt(hd), tps, nsplit, ws)
+    for _ in range(iters):
+        fn()
+    torch.cuda.synchronize()
+    ms = time_cuda(fn)
+    byts = B * L * nkv * (hd + hd // 8 + 6)
+    print(json.dumps({"case": "tq_attn_one", "B": B, "L": L, "tps": tps, "nsplit": nsplit, "ms": round(ms, 4),
+                      "GBps": round(byts / ms / 1e6, 1), "bf16_equiv_bytes_ratio": round(4 * hd / (hd + hd // 8 + 6), 2)}))
+
+
 def gguf_one(M=8, N=6144, K=4096, iters=5):
     from b200serve.models.gguf_gpu import to_quant_weight
     w = (torch.randn(N, K, device="cuda") * 0.02)
@@ -403,6 +434,9 @@ if __name__ == "__main__":
         sys.exit(0)
     if what == "prefill_attn_one":
         prefill_attn_one(*[int(v) for v in sys.argv[2:7]])
+        sys.exit(0)
+    if what == "tq_attn_one":
+        tq_attn_one(*[int(v) for v in sys.argv[2:8]])
         sys.exit(0)
     if what == "gguf_one":
         gguf_one(*[int(v) for v in sys.argv[2:5]])

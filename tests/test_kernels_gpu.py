@@ -179,6 +179,16 @@ def test_prefill_attention_tcgen05_matches_reference(G, case):
     assert _rel(out.float().cpu(), ref) < 2e-2
 
 
+def test_q4_dequant_pages_matches_cpu():
+    codes = torch.randint(0, 256, (12, 2, 16, 64), dtype=torch.uint8, device=dev)
+    scales = (torch.rand(12, 2, 16, device=dev) + 0.05).half()
+    ids = torch.tensor([7, 0, 11, 3], dtype=torch.int32, device=dev)
+    out = torch.empty(4, 2, 16, 128, dtype=torch.bfloat16, device=dev)
+    ops.q4_dequant_pages(ids, codes, scales, out)
+    ref = ops.q4_dequantize_rows(codes.cpu()[ids.cpu().long()], scales.cpu()[ids.cpu().long()])
+    assert _rel(out.float().cpu(), ref) < 1e-2
+
+
 def _make_paged(B, lens, nkv, hd, nb_total):
     kc = torch.randn(nb_total, nkv, 16, hd, device=dev).bfloat16()
     vc = torch.randn(nb_total, nkv, 16, hd, device=dev).bfloat16()
