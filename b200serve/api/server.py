@@ -361,6 +361,8 @@ def create_app(engine=None, keystore: KeyStore = None):
                 "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct},
                 "x_backend": backend, "x_stats": st}
 
+    from b200serve.api.chat_jobs import register_chat_job_routes
+    register_chat_job_routes(app, auth, _get_engine)
     return app
 
 

@@ -14,8 +14,9 @@
 //                  [key][dim] tile, O in TMEM.
 // O is rescaled in TMEM only when a row maximum grows by more than 8 (log2 units); until then
 // the stale maximum keeps exp2() <= 256, which fp32/bf16 absorb.
-// Roles (192 threads): warp 0 lane 0 = TMA producer (K/V pages, 2 stages), warp 1 = TMEM
-// allocator + MMA issuer, warps 2..5 = softmax and the output epilogue. Every wait is bounded.
+// Roles (320 threads): warp 0 lane 0 = TMA producer (K/V pages, 2 stages), warp 1 = TMEM
+// allocator + MMA issuer, warps 2..9 = softmax and the output epilogue (two warps per TMEM lane
+// quadrant, each taking half of the key and output columns). Every wait is bounded.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <mutex>
@@ -28,7 +29,14 @@ constexpr int kPT_Half = kPT_Rows * 128;            // 128 rows x 64 bf16 = 16 K
 constexpr int kPT_Tile = 2 * kPT_Half;              // 128 x 128 bf16 = 32 KB
 // smem: Q | K[2] | V[2] | P | barriers
 constexpr int kPT_Q = 0, kPT_K = kPT_Tile, kPT_V = 3 * kPT_Tile, kPT_P = 5 * kPT_Tile, kPT_Bar = 6 * kPT_Tile;
-constexpr size_t kPT_Smem = 1024 + 6 * kPT_Tile + 256;
+constexpr size_t kPT_Smem = 1024 + 6 * kPT_Tile + 256 + 2048 + 64;   // + row max/sum exchange, flags
+
+// 2^x with the hardware approximation (PTX ex2.approx.ftz.f32, one MUFU instruction)
+__device__ __forceinline__ float pt_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // byte offset of (row r, 16-byte chunk c of 16) in a 128-row SW128 K-major tile of two 64-col halves
 __device__ __forceinline__ uint32_t pt_swz(int r, int c) {
@@ -36,7 +44,7 @@ __device__ __forceinline__ uint32_t pt_swz(int r, int c) {
 }
 
 template <int G>
-__global__ void __launch_bounds__(192, 1) paged_prefill_tc_kernel(
+__global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(
     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
     const __nv_bfloat16* __restrict__ q, const int* __restrict__ block_tables, int max_blocks,
     const int* __restrict__ seq_lens, const int* __restrict__ q_start, const int* __restrict__ cu_q,
@@ -70,7 +78,7 @@ __global__ void __launch_bounds__(192, 1) paged_prefill_tc_kernel(
   const int* bt = block_tables + (size_t)seq * max_blocks;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 12; ++i) tc::mbar_init(&bars[i], (i == 9 || i == 10) ? 4 : 1);
+    for (int i = 0; i < 12; ++i) tc::mbar_init(&bars[i], (i == 9 || i == 10) ? 8 : 1);
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -167,10 +175,16 @@ __global__ void __launch_bounds__(192, 1) paged_prefill_tc_kernel(
     }
     __syncwarp();
   } else {
-    // ---------------- softmax + epilogue: thread = row ----------------
-    const int quad = warp & 3;
+    // ---------------- softmax + epilogue: 8 warps, thread = (row, half of the columns) ----------
+    // Warps 2..5 and 6..9 cover the four TMEM lane quadrants twice; the first set handles key
+    // (and output) columns 0..63 of its rows, the second 64..127. Row maxima and sums are
+    // combined through shared memory under named barrier 2 (the 256 softmax threads).
+    const int quad = warp & 3, half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
+    const int cbase = half * 64;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    float* xmax = reinterpret_cast<float*>(smem + kPT_Bar + 256);   // [2][128]
+    float* xsum = xmax + 256;                                        // [2][128]
     const int t = tq0 + r / G;
     const int pos = t < nrows ? qs + t : -1;                  // -1: padding row, attends nothing
     float m = -INFINITY, l = 0.f;
@@ -180,49 +194,82 @@ __global__ void __launch_bounds__(192, 1) paged_prefill_tc_kernel(
       if (lane == 0) ok = tc::mbar_wait_bounded(bar, parity, abort_flag, err, code) ? 1 : 0;
       return __shfl_sync(0xffffffffu, ok, 0) != 0;
     };
+    // Named barriers: 1 = all 8 softmax warps (once per tile, `agree`); 2 + quad = the two warps
+    // of one lane quadrant (the row max / sum exchange, whose pass count can differ between
+    // quadrants but never between the two halves of the same rows).
+    const int pair_bar = 2 + quad;
+    auto pair_sync = [pair_bar] { asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory"); };
+    int* xok = reinterpret_cast<int*>(xsum + 256);                   // [8]
+    // every softmax warp calls agree() the same number of times: a timed-out wait in any of
+    // them makes all eight leave together
+    auto agree = [&](bool v) -> bool {
+      if (lane == 0) xok[warp - 2] = v ? 1 : 0;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      int all = 1;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) all &= xok[i];
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      return all != 0;
+    };
     int j = 0;
+    bool ok = true;
     for (; j < n_tiles; ++j) {
-      if (!warp_wait(s_full, (uint32_t)(j & 1), 37)) break;
+      ok = warp_wait(s_full, (uint32_t)(j & 1), 37);
+      if (ok && j > 0) ok = warp_wait(pv_done, (uint32_t)((j - 1) & 1), 38);
+      ok = agree(ok);
+      if (!ok) break;
       tc::tc_fence_after();
       const int key0 = j * kPT_Keys;
       const int lim = min(len - 1, pos);                       // last key this row may see
-      // P of the previous tile and O must be settled before either is touched
-      if (j > 0 && !warp_wait(pv_done, (uint32_t)((j - 1) & 1), 38)) break;
-      tc::tc_fence_after();
       // one pass over S in the common case: p = exp2(s - m) with the running (possibly stale)
-      // maximum m; only if this tile raises the maximum by more than 8 (or it is the row's first
-      // tile) is the pass repeated with the new maximum after O is rescaled
+      // maximum m; the pass is repeated only when a row sees its first visible key here or its
+      // maximum grows by more than 8, after O is rescaled
       float rs = 0.f;
-      float mx = -INFINITY;
+      int lim_min = lim;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) lim_min = min(lim_min, __shfl_xor_sync(0xffffffffu, lim_min, o));
+      const bool full_tile = key0 + cbase + 63 <= lim_min;      // warp-uniform: no per-key mask
       for (int pass = 0; pass < 2; ++pass) {
         rs = 0.f;
-        mx = -INFINITY;
+        float mxr = -INFINITY;                                 // max of the raw (unscaled) scores
         const float mref = m == -INFINITY ? 0.f : m;
+        uint32_t raw[64];
 #pragma unroll
-        for (int c0 = 0; c0 < kPT_Keys; c0 += 64) {
-          uint32_t raw[64];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) tc::tmem_ld16_async(tS + lane_off + c0 + 16 * u, raw + 16 * u);
-          tc::tmem_wait_ld();
-          uint32_t pk[32];
+        for (int u = 0; u < 4; ++u) tc::tmem_ld16_async(tS + lane_off + cbase + 16 * u, raw + 16 * u);
+        tc::tmem_wait_ld();
+        uint32_t pk[32];
+        if (full_tile) {
 #pragma unroll
           for (int i = 0; i < 64; i += 2) {
-            const int kk = key0 + c0 + i;
-            const float s0 = kk <= lim ? __uint_as_float(raw[i]) * scale_log2 : -INFINITY;
-            const float s1 = kk + 1 <= lim ? __uint_as_float(raw[i + 1]) * scale_log2 : -INFINITY;
-            mx = fmaxf(mx, fmaxf(s0, s1));
-            const float p0 = exp2f(s0 - mref), p1 = exp2f(s1 - mref);
+            const float s0 = __uint_as_float(raw[i]), s1 = __uint_as_float(raw[i + 1]);
+            mxr = fmaxf(mxr, fmaxf(s0, s1));
+            const float p0 = pt_ex2(fmaf(s0, scale_log2, -mref)), p1 = pt_ex2(fmaf(s1, scale_log2, -mref));
             rs += p0 + p1;
             pk[i >> 1] = pack_bf16x2(p0, p1);
           }
+        } else {
 #pragma unroll
-          for (int cc = 0; cc < 8; ++cc)
-            *reinterpret_cast<uint4*>(smem + kPT_P + pt_swz(r, (c0 >> 3) + cc)) =
-                make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+          for (int i = 0; i < 64; i += 2) {
+            const int kk = key0 + cbase + i;
+            const float s0 = kk <= lim ? __uint_as_float(raw[i]) : -INFINITY;
+            const float s1 = kk + 1 <= lim ? __uint_as_float(raw[i + 1]) : -INFINITY;
+            mxr = fmaxf(mxr, fmaxf(s0, s1));
+            const float p0 = kk <= lim ? pt_ex2(fmaf(s0, scale_log2, -mref)) : 0.f;
+            const float p1 = kk + 1 <= lim ? pt_ex2(fmaf(s1, scale_log2, -mref)) : 0.f;
+            rs += p0 + p1;
+            pk[i >> 1] = pack_bf16x2(p0, p1);
+          }
         }
-        // a row needs a second pass when it sees its first visible key here (exact maximum) or
-        // when its maximum grew by more than 8. The decisions below are warp-uniform: the TMEM
-        // loads/stores are warp-collective and must never run in a partial warp.
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc)
+          *reinterpret_cast<uint4*>(smem + kPT_P + pt_swz(r, (cbase >> 3) + cc)) =
+              make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+        xmax[half * 128 + r] = mxr == -INFINITY ? -INFINITY : mxr * scale_log2;
+        pair_sync();
+        const float mx = fmaxf(xmax[r], xmax[128 + r]);
+        pair_sync();                                           // both halves read before reuse
+        // decisions are identical for the two warps of a row set and warp-uniform: the TMEM
+        // loads/stores below are warp-collective and must never run in a partial warp
         const bool redo = mx != -INFINITY && (m == -INFINITY || mx > m + 8.f);
         if (pass == 1 || !__any_sync(0xffffffffu, redo)) break;
         const bool grow = redo && m != -INFINITY;
@@ -230,12 +277,12 @@ __global__ void __launch_bounds__(192, 1) paged_prefill_tc_kernel(
         if (__any_sync(0xffffffffu, grow)) {
           l *= alpha;
 #pragma unroll
-          for (int c0 = 0; c0 < kPT_HD; c0 += 16) {
+          for (int c0 = 0; c0 < 64; c0 += 16) {
             float v[16];
-            tc::tmem_ld16(tO + lane_off + c0, v);
+            tc::tmem_ld16(tO + lane_off + cbase + c0, v);
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[i] *= alpha;
-            tc::tmem_st16(tO + lane_off + c0, v);
+            tc::tmem_st16(tO + lane_off + cbase + c0, v);
           }
         }
         if (redo) m = mx;
@@ -249,16 +296,20 @@ __global__ void __launch_bounds__(192, 1) paged_prefill_tc_kernel(
         tc::mbar_arrive(p_full);
       }
     }
-    // ---- epilogue: O / l -> out rows ----
-    if (j == n_tiles && n_tiles > 0 &&
-        warp_wait(pv_done, (uint32_t)((n_tiles - 1) & 1), 39)) {
+    // ---- epilogue: O / (l_lo + l_hi) -> out rows, each half its 64 dims ----
+    if (ok && n_tiles > 0) ok = warp_wait(pv_done, (uint32_t)((n_tiles - 1) & 1), 39);
+    ok = agree(ok);
+    xsum[half * 128 + r] = l;
+    pair_sync();
+    const float lt = xsum[r] + xsum[128 + r];
+    if (ok) {
       tc::tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* dst = out + ((size_t)(row0 + t) * nq + kvh * G + r % G) * kPT_HD;
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      __nv_bfloat16* dst = out + ((size_t)(row0 + t) * nq + kvh * G + r % G) * kPT_HD + cbase;
 #pragma unroll
-      for (int c0 = 0; c0 < kPT_HD; c0 += 16) {
+      for (int c0 = 0; c0 < 64; c0 += 16) {
         float v[16];
-        tc::tmem_ld16(tO + lane_off + c0, v);
+        tc::tmem_ld16(tO + lane_off + cbase + c0, v);
         if (t < nrows) {
           uint32_t pk[8];
 #pragma unroll
@@ -352,7 +403,7 @@ void paged_prefill_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::T
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPT_Smem));     \
       attr = true;                                                                                           \
     }                                                                                                        \
-    launch_pdl(paged_prefill_tc_kernel<GV>, grid, dim3(192), kPT_Smem, stream, tk, tv,                       \
+    launch_pdl(paged_prefill_tc_kernel<GV>, grid, dim3(320), kPT_Smem, stream, tk, tv,                       \
                reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), (const int*)block_tables.data_ptr<int>(), \
                (int)block_tables.size(1), (const int*)seq_lens.data_ptr<int>(),                              \
                (const int*)q_start.data_ptr<int>(), (const int*)cu_q.data_ptr<int>(),                       \

@@ -95,3 +95,36 @@ def test_auth(tmp_path):
         assert c.get("/v1/queue", headers={"Authorization": f"Bearer {key}"}).status_code == 200
         assert c.get("/v1/queue", headers={"X-API-Key": key}).status_code == 200
     server._keystore = KeyStore(path="")
+
+
+def test_chat_jobs_run_and_reattach(client):
+    body = {"messages": [{"role": "user", "content": "hello there"}], "max_tokens": 10, "temperature": 0.0}
+    r = client.post("/v1/chat/jobs", json=body)
+    assert r.status_code == 200
+    job_id = r.json()["job_id"]
+    events = _sse(client.get(f"/v1/chat/jobs/{job_id}/events"))
+    assert "x_snapshot" in events[0] and events[-1] == "[DONE]"
+    # the stream ends with the job's end record once it finished
+    ends = [e for e in events if isinstance(e, dict) and "x_job_end" in e]
+    snap = client.get(f"/v1/chat/jobs/{job_id}").json()
+    assert snap["status"] == "done" and snap["usage"]["completion_tokens"] > 0
+    if ends:
+        assert ends[0]["x_job_end"]["status"] == "done"
+    # re-attaching after the end returns the full snapshot and [DONE]
+    again = _sse(client.get(f"/v1/chat/jobs/{job_id}/events"))
+    assert again[0]["x_snapshot"]["text"] == snap["text"] and again[-1] == "[DONE]"
+    assert client.get("/v1/chat/jobs/nope").status_code == 404
+
+
+def test_chat_job_stop(client):
+    body = {"messages": [{"role": "user", "content": "a long answer please"}], "max_tokens": 200,
+            "temperature": 0.0}
+    job_id = client.post("/v1/chat/jobs", json=body).json()["job_id"]
+    assert client.post(f"/v1/chat/jobs/{job_id}/stop").json()["ok"]
+    import time
+    for _ in range(200):
+        st = client.get(f"/v1/chat/jobs/{job_id}").json()["status"]
+        if st != "running":
+            break
+        time.sleep(0.05)
+    assert st in ("stopped", "done")
