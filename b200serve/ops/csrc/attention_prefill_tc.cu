@@ -57,11 +57,11 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(
   uint64_t* vfull = bars + 2;      // [2]
   uint64_t* kempty = bars + 4;     // [2]
   uint64_t* vempty = bars + 6;     // [2]
-  uint64_t* s_full = bars + 8;
-  uint64_t* s_free = bars + 9;
-  uint64_t* p_full = bars + 10;
-  uint64_t* pv_done = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* s_full = bars + 8;     // [2]: S buffer b holds a finished Q K^T
+  uint64_t* s_free = bars + 10;    // [2]: the softmax warps finished reading S buffer b
+  uint64_t* p_full = bars + 12;
+  uint64_t* pv_done = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(
   const int* bt = block_tables + (size_t)seq * max_blocks;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 12; ++i) tc::mbar_init(&bars[i], (i == 9 || i == 10) ? 8 : 1);
+    for (int i = 0; i < 14; ++i) tc::mbar_init(&bars[i], (i == 10 || i == 11 || i == 12) ? 8 : 1);
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(
     tc::prefetch_tmap(&tm_v);
   }
   if (warp == 1) {
-    tc::tmem_alloc(tmem_slot, 256);
+    tc::tmem_alloc(tmem_slot, 512);
     tc::tmem_relinquish();
   }
   // ---- Q rows (token-major, G heads per token) -> swizzled K-major smem tile ----
@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128;
+  const uint32_t tO = tmem + 256;                            // S buffers at columns 0 and 128
 
   if (warp == 0) {
     if (lane == 0) {
@@ -141,22 +141,31 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(
       constexpr uint32_t IDESC_S = tc::idesc_bf16_f32(128, 128);
       constexpr uint32_t IDESC_PV = tc::idesc_bf16_f32_bmn(128, 128);
       const uint32_t q_addr = tc::smem_u32(smem + kPT_Q), p_addr = tc::smem_u32(smem + kPT_P);
-      for (int j = 0; j < n_tiles && !*abort_flag; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (uint32_t)((j >> 1) & 1);
-        if (!tc::mbar_wait_bounded(&kfull[s], ph, abort_flag, err, 33)) break;
-        if (j > 0 && !tc::mbar_wait_bounded(s_free, (uint32_t)((j - 1) & 1), abort_flag, err, 34)) break;
+      // S(j+1) is issued before PV(j), into the other S buffer, so the tensor core computes the
+      // next scores while the softmax warps work on this tile
+      auto issue_s = [&](int t) -> bool {
+        const int b = t & 1;
+        if (!tc::mbar_wait_bounded(&kfull[b], (uint32_t)((t >> 1) & 1), abort_flag, err, 33)) return false;
+        if (t >= 2 && !tc::mbar_wait_bounded(&s_free[b], (uint32_t)(((t - 2) >> 1) & 1), abort_flag, err, 34))
+          return false;
         tc::tc_fence_after();
-        const uint32_t k_addr = tc::smem_u32(smem + kPT_K + s * kPT_Tile);
+        const uint32_t k_addr = tc::smem_u32(smem + kPT_K + b * kPT_Tile);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kPT_Half;
           const uint64_t a = tc::sw128_kmajor_desc(q_addr + off) + 2 * (kk & 3);
-          const uint64_t b = tc::sw128_kmajor_desc(k_addr + off) + 2 * (kk & 3);
-          tc::mma_bf16(tS, a, b, IDESC_S, kk > 0 ? 1u : 0u);
+          const uint64_t bd = tc::sw128_kmajor_desc(k_addr + off) + 2 * (kk & 3);
+          tc::mma_bf16(tmem + b * 128, a, bd, IDESC_S, kk > 0 ? 1u : 0u);
         }
-        tc::mma_commit(s_full);
-        tc::mma_commit(&kempty[s]);
+        tc::mma_commit(&s_full[b]);
+        tc::mma_commit(&kempty[b]);
+        return true;
+      };
+      bool live = n_tiles > 0 && issue_s(0);
+      for (int j = 0; j < n_tiles && live && !*abort_flag; ++j) {
+        const int s = j & 1;
+        const uint32_t ph = (uint32_t)((j >> 1) & 1);
+        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
         // O += P V once the softmax warps have written P of this tile
         if (!tc::mbar_wait_bounded(p_full, (uint32_t)(j & 1), abort_flag, err, 35)) break;
         if (!tc::mbar_wait_bounded(&vfull[s], ph, abort_flag, err, 36)) break;
@@ -166,8 +175,8 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t a = tc::sw128_kmajor_desc(p_addr + (kk >> 2) * kPT_Half) + 2 * (kk & 3);
           // 16 keys = two 8-row groups (1024 B apart); the 128 dims span the two 64-dim halves
-          const uint64_t b = tc::sw128_mnmajor_desc(v_addr + kk * 2048, kPT_Half, 1024);
-          tc::mma_bf16(tO, a, b, IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+          const uint64_t bd = tc::sw128_mnmajor_desc(v_addr + kk * 2048, kPT_Half, 1024);
+          tc::mma_bf16(tO, a, bd, IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
         }
         tc::mma_commit(pv_done);
         tc::mma_commit(&vempty[s]);
@@ -214,12 +223,13 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(
     int j = 0;
     bool ok = true;
     for (; j < n_tiles; ++j) {
-      ok = warp_wait(s_full, (uint32_t)(j & 1), 37);
+      ok = warp_wait(&s_full[j & 1], (uint32_t)((j >> 1) & 1), 37);
       if (ok && j > 0) ok = warp_wait(pv_done, (uint32_t)((j - 1) & 1), 38);
       ok = agree(ok);
       if (!ok) break;
       tc::tc_fence_after();
       const int key0 = j * kPT_Keys;
+      const uint32_t tSj = tmem + (uint32_t)(j & 1) * 128;    // this tile's S buffer
       const int lim = min(len - 1, pos);                       // last key this row may see
       // one pass over S in the common case: p = exp2(s - m) with the running (possibly stale)
       // maximum m; the pass is repeated only when a row sees its first visible key here or its
@@ -235,7 +245,7 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(
         const float mref = m == -INFINITY ? 0.f : m;
         uint32_t raw[64];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) tc::tmem_ld16_async(tS + lane_off + cbase + 16 * u, raw + 16 * u);
+        for (int u = 0; u < 4; ++u) tc::tmem_ld16_async(tSj + lane_off + cbase + 16 * u, raw + 16 * u);
         tc::tmem_wait_ld();
         uint32_t pk[32];
         if (full_tile) {
@@ -292,7 +302,7 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(
       tc::fence_proxy_async_smem();                            // P (generic writes) -> MMA (async proxy)
       __syncwarp();
       if (lane == 0) {
-        tc::mbar_arrive(s_free);
+        tc::mbar_arrive(&s_free[j & 1]);
         tc::mbar_arrive(p_full);
       }
     }
@@ -330,7 +340,7 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(
   }
   if (warp == 1) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tmem, 256);
+    tc::tmem_dealloc(tmem, 512);
   }
 }
 
