@@ -39,8 +39,9 @@ def _dtype(name):
 class B200Engine(BaseEngine):
     stream_starts_in_think = True
 
-    def __init__(self, config: EngineConfig = None, weights=None, tokenizer=None):
+    def __init__(self, config: EngineConfig = None, weights=None, tokenizer=None, model_config=None):
         self.config = (config or EngineConfig()).validate()
+        self._injected_model_cfg = model_config
         self._injected_weights = weights
         self._injected_tokenizer = tokenizer
         self.model_cfg = None
@@ -84,7 +85,7 @@ class B200Engine(BaseEngine):
         else:
             dev = torch.device("cpu")
         self.device = dev
-        mc = get_model_config(cfgE.model, cfgE.num_layers_override)
+        mc = self._injected_model_cfg or get_model_config(cfgE.model, cfgE.num_layers_override)
         self.model_cfg = mc
         dtype = _dtype(cfgE.dtype)
         say(f"b200: building {mc.name} ({mc.num_params() / 1e9:.2f}B params) tp={tp} on {dev}")

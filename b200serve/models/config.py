@@ -7,8 +7,9 @@ The three built-in shapes are the configurations the benchmarks name:
   12288, vocab 151936, per-head q/k RMSNorm (Qwen3), RoPE 1e6;
 * ``qwen3-30b-a3b``: 48 layers, hidden 2048, 32/4 heads (head_dim 128), 128
   experts with top-8 softmax routing, expert FFN 768, vocab 151936.
-HF ``config.json`` files of the qwen2 / qwen3 / qwen3_moe families map onto
-the same dataclass.
+HF ``config.json`` files of the qwen2 / qwen3 / qwen3_moe / llama / mistral
+families map onto the same dataclass (Llama and Mistral are the Qwen2 block
+without q/k/v bias; their RoPE may carry a ``linear`` or ``llama3`` scaling).
 """
 
 from __future__ import annotations
@@ -16,6 +17,7 @@ from __future__ import annotations
 import json
 import os
 from dataclasses import dataclass, replace
+from typing import Optional
 
 
 @dataclass
@@ -40,6 +42,10 @@ class ModelConfig:
     max_position: int = 40960
     bos_token_id: int = 1
     eos_token_id: int = 2
+    family: str = ""                 # HF model_type this shape came from ("" = inferred)
+    rope_scaling: Optional[dict] = None
+    rotary_dim: int = 0              # 0 = whole head
+    sliding_window: int = 0          # 0 = none; contexts are capped at the window
 
     @property
     def is_moe(self) -> bool:
@@ -95,26 +101,51 @@ BUILTIN = {
 }
 
 
+_FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "llama", "mistral")
+
+
+def _rope_params(d: dict):
+    """(theta, scaling dict or None) from either the classic keys or transformers 5's
+    ``rope_parameters``."""
+    rp = d.get("rope_parameters") or {}
+    theta = d.get("rope_theta") or rp.get("rope_theta") or 1e6
+    sc = d.get("rope_scaling") or (rp if rp.get("rope_type", "default") != "default" else None)
+    if sc and (sc.get("rope_type") or sc.get("type") or "default") == "default":
+        sc = None
+    return float(theta), (dict(sc) if sc else None)
+
+
 def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
     mt = d.get("model_type", "qwen2")
+    if mt not in _FAMILIES:
+        raise NotImplementedError(f"model_type {mt!r}: supported families are {', '.join(_FAMILIES)}")
+    if mt in ("llama", "mistral") and d.get("mlp_bias"):
+        raise NotImplementedError("llama mlp_bias=True")
     heads = d["num_attention_heads"]
     hd = d.get("head_dim") or d["hidden_size"] // heads
+    theta, scaling = _rope_params(d)
+    max_pos = d.get("max_position_embeddings", 40960)
+    sw = d.get("sliding_window") or 0
+    if mt == "mistral" and sw and sw < max_pos:
+        max_pos = sw        # within the window, sliding-window attention equals full attention
+    moe = mt == "qwen3_moe"
     return ModelConfig(
         name=name, vocab_size=d["vocab_size"], hidden_size=d["hidden_size"],
         num_layers=d["num_hidden_layers"], num_heads=heads,
-        num_kv_heads=d.get("num_key_value_heads", heads), head_dim=hd,
+        num_kv_heads=d.get("num_key_value_heads") or heads, head_dim=hd,
         intermediate_size=d.get("intermediate_size", 0), rms_eps=d.get("rms_norm_eps", 1e-6),
-        rope_theta=d.get("rope_theta", 1e6) or (d.get("rope_parameters") or {}).get("rope_theta", 1e6),
+        rope_theta=theta, rope_scaling=scaling,
         attn_bias=(mt == "qwen2") or bool(d.get("attention_bias", False)),
         qk_norm=mt in ("qwen3", "qwen3_moe"),
         tie_embeddings=bool(d.get("tie_word_embeddings", False)),
-        num_experts=d.get("num_experts", 0) if mt == "qwen3_moe" else 0,
-        experts_per_tok=d.get("num_experts_per_tok", 0) if mt == "qwen3_moe" else 0,
-        moe_intermediate_size=d.get("moe_intermediate_size", 0) if mt == "qwen3_moe" else 0,
+        num_experts=d.get("num_experts", 0) if moe else 0,
+        experts_per_tok=d.get("num_experts_per_tok", 0) if moe else 0,
+        moe_intermediate_size=d.get("moe_intermediate_size", 0) if moe else 0,
         norm_topk_prob=d.get("norm_topk_prob", True),
-        max_position=d.get("max_position_embeddings", 40960),
+        max_position=max_pos,
         bos_token_id=d.get("bos_token_id") or 1,
         eos_token_id=(d.get("eos_token_id") if isinstance(d.get("eos_token_id"), int) else 2),
+        family=mt, sliding_window=sw if mt == "mistral" else 0,
     )
 
 

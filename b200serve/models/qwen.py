@@ -76,7 +76,8 @@ class Decoder:
         self.nkv = max(1, cfg.num_kv_heads // tp)   # KV heads replicated when tp > num_kv_heads
         self.hd = cfg.head_dim
         self.scale = ops.softmax_scale(cfg.head_dim)
-        self.cos_sin = ops.rope_cos_sin(cfg.head_dim, cfg.max_position, cfg.rope_theta, self.device)
+        self.cos_sin = ops.rope_cos_sin(cfg.head_dim, cfg.max_position, cfg.rope_theta, self.device,
+                                       rot_dim=cfg.rotary_dim, scaling=cfg.rope_scaling)
         self.attn_ws = None
         self.moe = None
         self.tq = None

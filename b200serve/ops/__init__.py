@@ -117,9 +117,39 @@ def rmsnorm(parts, weight, eps, residual=None, residual_out=None, out=None):
 
 
 # ------------------------------------------------------------------ RoPE table
-def rope_cos_sin(head_dim: int, max_pos: int, theta: float, device) -> torch.Tensor:
-    """[max_pos, head_dim] fp32: cos of the head_dim/2 frequencies, then their sin."""
-    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))
+def rope_inv_freq(rot_dim: int, theta: float, scaling: dict = None) -> torch.Tensor:
+    """Inverse frequencies of rotate-half RoPE over ``rot_dim`` dims, with the context-extension
+    schemes HF configs name in ``rope_scaling`` / ``rope_parameters``:
+      * ``linear``: every frequency divided by ``factor`` (positions compressed);
+      * ``llama3``: the Llama 3.1 piecewise rule; wavelengths shorter than
+        original_max / high_freq_factor are kept, longer than original_max / low_freq_factor
+        divided by ``factor``, and the band between interpolates linearly in
+        original_max / wavelength.
+    Any other type raises."""
+    inv = 1.0 / (theta ** (torch.arange(0, rot_dim, 2, dtype=torch.int64).float() / rot_dim))
+    kind = (scaling or {}).get("rope_type") or (scaling or {}).get("type") or "default"
+    if kind == "default":
+        return inv
+    factor = float(scaling["factor"])
+    if kind == "linear":
+        return inv / factor
+    if kind == "llama3":
+        lo, hi = float(scaling.get("low_freq_factor", 1.0)), float(scaling.get("high_freq_factor", 4.0))
+        old = float(scaling.get("original_max_position_embeddings", 8192))
+        wavelen = 2 * math.pi / inv
+        smooth = ((old / wavelen - lo) / (hi - lo)).clamp(0.0, 1.0)
+        scaled = (1 - smooth) * inv / factor + smooth * inv
+        return torch.where(wavelen < old / hi, inv, torch.where(wavelen > old / lo, inv / factor, scaled))
+    raise NotImplementedError(f"rope scaling type {kind!r}")
+
+
+def rope_cos_sin(head_dim: int, max_pos: int, theta: float, device, rot_dim: int = 0,
+                 scaling: dict = None) -> torch.Tensor:
+    """[max_pos, rot_dim] fp32: cos of the rot_dim/2 frequencies, then their sin. ``rot_dim`` 0
+    means the whole head; a smaller value rotates the first ``rot_dim`` dims only (partial RoPE,
+    pairs (i, i + rot_dim/2)) and passes the rest through."""
+    rot = rot_dim or head_dim
+    inv = rope_inv_freq(rot, theta, scaling)
     pos = torch.arange(max_pos, dtype=torch.int64).float()
     f = torch.outer(pos, inv)
     return torch.cat([f.cos(), f.sin()], dim=-1).to(device)

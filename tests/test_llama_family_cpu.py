@@ -1,0 +1,88 @@
+"""Llama and Mistral checkpoints run through the same decoder as Qwen2 (no q/k/v bias).
+The CPU path must match HF transformers fp32 on a tiny random model, including the
+Llama 3.1 RoPE frequency rule and linear RoPE scaling."""
+
+import json
+
+import pytest
+import torch
+
+from b200serve.core.config import EngineConfig
+from b200serve.engine.b200_engine import B200Engine
+from b200serve.engine.sampler import SamplingParams
+from b200serve.models.config import from_hf_config
+from b200serve.models.weights import load_hf_state_dict
+
+transformers = pytest.importorskip("transformers")
+
+_BASE = dict(vocab_size=1000, hidden_size=128, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+             intermediate_size=256, rms_norm_eps=1e-5, max_position_embeddings=512, tie_word_embeddings=False,
+             bos_token_id=1, eos_token_id=2)
+
+_CASES = {
+    "llama": dict(model_type="llama", rope_theta=500000.0,
+                  rope_scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                                "high_freq_factor": 4.0, "original_max_position_embeddings": 64}),
+    "llama_linear": dict(model_type="llama", rope_theta=10000.0, rope_scaling={"rope_type": "linear", "factor": 2.0}),
+    "mistral": dict(model_type="mistral", rope_theta=10000.0, sliding_window=None),
+}
+
+
+def _hf(case):
+    d = dict(_BASE, **_CASES[case])
+    mt = d.pop("model_type")
+    cls_cfg = transformers.LlamaConfig if mt == "llama" else transformers.MistralConfig
+    cls = transformers.LlamaForCausalLM if mt == "llama" else transformers.MistralForCausalLM
+    hf_cfg = cls_cfg(**d)
+    torch.manual_seed(0)
+    model = cls(hf_cfg).eval()
+    cfg_d = json.loads(hf_cfg.to_json_string())
+    cfg_d["model_type"] = mt
+    return from_hf_config(cfg_d, case), model
+
+
+@pytest.mark.parametrize("case", sorted(_CASES))
+def test_family_prefill_and_greedy_match_hf(case):
+    cfg, model = _hf(case)
+    assert not cfg.attn_bias and not cfg.qk_norm
+    sd = {k: v.detach().clone() for k, v in model.state_dict().items()}
+    w = load_hf_state_dict(cfg, sd, dtype=torch.float32, device="cpu")
+    g = torch.Generator().manual_seed(1)
+    prompt = torch.randint(3, 1000, (100,), generator=g).tolist()
+    with torch.no_grad():
+        ref_logits = model(torch.tensor([prompt])).logits[0, -1]
+        hf = model.generate(torch.tensor([prompt]), max_new_tokens=16, min_new_tokens=16, do_sample=False,
+                            pad_token_id=0)[0, len(prompt):].tolist()
+    ec = EngineConfig(model=case, device="cpu", dtype="float32", cuda_graphs=False, max_seq=256, max_batch=4)
+    eng = B200Engine(ec, weights=w, model_config=cfg)
+    eng.load()
+    try:
+        bt = eng.scheduler.alloc.allocate(8)
+        logits = eng.runner.prefill([{"ids": prompt, "start": 0, "block_table": bt}])
+        eng.scheduler.alloc.release(bt)
+        assert torch.allclose(logits[0], ref_logits, atol=1e-4, rtol=1e-4)
+        [req] = eng.generate([prompt], SamplingParams(temperature=0.0, max_tokens=16, ignore_eos=True))
+    finally:
+        eng.unload()
+    assert req.output == hf
+
+
+def test_rope_scaling_tables_match_hf():
+    from transformers.modeling_rope_utils import ROPE_INIT_FUNCTIONS
+    from b200serve import ops
+    for case in ("llama", "llama_linear"):
+        d = dict(_BASE, **_CASES[case])
+        d.pop("model_type")
+        hf_cfg = transformers.LlamaConfig(**d)
+        kind = _CASES[case]["rope_scaling"]["rope_type"]
+        inv_hf, _ = ROPE_INIT_FUNCTIONS[kind](hf_cfg, "cpu")
+        cfg = from_hf_config(dict(json.loads(hf_cfg.to_json_string()), model_type="llama"))
+        inv = ops.rope_inv_freq(cfg.head_dim, cfg.rope_theta, cfg.rope_scaling)
+        assert torch.allclose(inv, inv_hf.float(), rtol=1e-6, atol=0), case
+
+
+def test_mistral_window_caps_context():
+    cfg = from_hf_config(dict(_BASE, model_type="mistral", sliding_window=256, rope_theta=1e4))
+    assert cfg.max_position == 256 and cfg.sliding_window == 256
+    with pytest.raises(NotImplementedError):
+        from_hf_config(dict(_BASE, model_type="gpt2"))
