@@ -36,6 +36,10 @@ def _dtype(name):
             "fp32": torch.float32}[name]
 
 
+def _kv_layers(mc) -> int:
+    return sum(1 for i in range(mc.num_layers) if not mc.is_linear(i))
+
+
 class B200Engine(BaseEngine):
     stream_starts_in_think = True
 
@@ -93,7 +97,8 @@ class B200Engine(BaseEngine):
         self.comm = pdist.make_comm(cfgE, dev, self.model_cfg) if tp > 1 else None
         nkv_local = max(1, mc.num_kv_heads // tp)
         num_blocks = self._size_kv(mc, nkv_local, dtype, dev)
-        self.kv = KVCache(mc.num_layers, num_blocks, nkv_local, mc.head_dim, dtype=dtype, device=dev,
+        # hybrid models page K/V for their full-attention layers only
+        self.kv = KVCache(_kv_layers(mc), num_blocks, nkv_local, mc.head_dim, dtype=dtype, device=dev,
                           kv_format=cfgE.kv_format, key_bits=cfgE.kv_key_bits, value_bits=cfgE.kv_value_bits)
         from b200serve.engine.runner import ModelRunner
         runner = ModelRunner(mc, self.weights, self.kv, comm=self.comm, device=dev, max_batch=cfgE.max_batch,
@@ -102,8 +107,9 @@ class B200Engine(BaseEngine):
             from b200serve.parallel.worker import BroadcastRunner
             runner = BroadcastRunner(runner, self.comm)
         self.runner = runner
+        # a prefix-cache hit would skip tokens whose recurrent state a hybrid model needs
         self.scheduler = Scheduler(runner, num_blocks, max_batch=cfgE.max_batch, prefill_chunk=cfgE.prefill_chunk,
-                                   max_seq=cfgE.max_seq)
+                                   max_seq=cfgE.max_seq, prefix_cache=not mc.is_hybrid)
         self.tokenizer = self._injected_tokenizer or load_tokenizer(self._model_path(), mc.vocab_size)
         from b200serve.core import inference
         inference._tokenizer = self.tokenizer
@@ -132,14 +138,18 @@ class B200Engine(BaseEngine):
 
     def _size_kv(self, mc, nkv_local, dtype, dev) -> int:
         cfgE = self.config
-        per_block = KVCache.bytes_per_block(mc.num_layers, nkv_local, mc.head_dim,
+        per_block = KVCache.bytes_per_block(_kv_layers(mc), nkv_local, mc.head_dim,
                                             torch.tensor([], dtype=dtype).element_size(), cfgE.kv_format)
+        state = 0
+        if mc.is_hybrid:
+            from b200serve.models.hybrid import LinearState
+            state = (cfgE.max_batch + 1) * LinearState.bytes_per_slot(mc, cfgE.tp_size)
         want = cfgE.max_batch * ((cfgE.max_seq + BLOCK - 1) // BLOCK) + 64
         if cfgE.kv_blocks:
             return cfgE.kv_blocks
         if dev.type == "cuda":
             free, _ = torch.cuda.mem_get_info(dev)
-            budget = int((free - (6 << 30)) * cfgE.kv_mem_fraction)
+            budget = int((free - (6 << 30) - state) * cfgE.kv_mem_fraction)
             n = max(64, budget // per_block)
             return int(min(n, want))
         return int(min(want, 4096))

@@ -15,7 +15,22 @@ import torch
 from b200serve import ops
 from b200serve.models.qwen import Decoder, ForwardBatch
 
+
+def unpack_static(runner, bucket):
+    """Copy the packed decode inputs (``s_pack``, already on the device) into the static
+    buffers the captured graphs read."""
+    mb = runner.max_blocks
+    dv = runner.s_pack[: bucket * (PACK + mb)].view(bucket, PACK + mb)
+    runner.s_ids[:bucket].copy_(dv[:, 0])
+    runner.s_pos[:bucket].copy_(dv[:, 1])
+    runner.s_slots[:bucket].copy_(dv[:, 2])
+    runner.s_lens[:bucket].copy_(dv[:, 3])
+    runner.s_state[:bucket].copy_(dv[:, 4])
+    runner.s_bt[:bucket].copy_(dv[:, PACK:])
+
 DECODE_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
+# per-row layout of the packed decode inputs: ids, pos, KV slot, len, state slot, block table
+PACK = 5
 
 
 class ModelRunner:
@@ -38,6 +53,15 @@ class ModelRunner:
         self.s_bt = torch.zeros(B, self.max_blocks, **i32)
         self.s_lens = torch.zeros(B, **i32)
         self.s_tokens = torch.zeros(B, **i32)
+        self.lin_state = None
+        self.scratch_slot = 0
+        if getattr(cfg, "is_hybrid", False):
+            from b200serve.models.hybrid import LinearState
+            tp = weights.tp_size
+            self.lin_state = LinearState(cfg, tp, max_batch, self.device)
+            self.decoder.lin_state = self.lin_state
+            self.scratch_slot = self.lin_state.scratch
+        self.s_state = torch.full((B,), self.scratch_slot, **i32)
         self.graphs = {}
         self.graph_out = {}
         self.launches_per_step = {}
@@ -47,8 +71,8 @@ class ModelRunner:
         self.vocab_start = weights.vocab_start
         self.greedy_buf = None
         pin = self.device.type == "cuda"
-        self.h_pack = torch.zeros(B * (4 + self.max_blocks), dtype=torch.int32, pin_memory=pin)
-        self.s_pack = torch.zeros(B * (4 + self.max_blocks), **i32)
+        self.h_pack = torch.zeros(B * (PACK + self.max_blocks), dtype=torch.int32, pin_memory=pin)
+        self.s_pack = torch.zeros(B * (PACK + self.max_blocks), **i32)
 
     # ------------------------------------------------------------ helpers
     def bucket(self, n: int) -> int:
@@ -72,7 +96,8 @@ class ModelRunner:
     def _decode_fb(self, bucket: int) -> ForwardBatch:
         return ForwardBatch(input_ids=self.s_ids[:bucket], positions=self.s_pos[:bucket],
                             slots=self.s_slots[:bucket], block_tables=self.s_bt[:bucket],
-                            seq_lens=self.s_lens[:bucket], logit_rows=None, is_decode=True)
+                            seq_lens=self.s_lens[:bucket], logit_rows=None, is_decode=True,
+                            state_slots=self.s_state[:bucket] if self.lin_state is not None else None)
 
     def _decode_body(self, bucket: int, greedy: bool):
         logits = self.decoder.forward(self._decode_fb(bucket), attn_plan=self.attn_plan(bucket))
@@ -102,37 +127,37 @@ class ModelRunner:
         return out
 
     # ------------------------------------------------------------ decode
-    def load_decode_inputs(self, ids, pos, slots, block_tables, lens):
-        """Host lists -> pinned pack -> one H2D copy -> static buffers."""
+    def load_decode_inputs(self, ids, pos, slots, block_tables, lens, state_slots=None):
+        """Host lists -> pinned pack -> one H2D copy -> static buffers. Padded rows of the
+        bucket write no KV (slot -1) and use the scratch recurrent-state slot."""
         B = len(ids)
         bucket = self.bucket(B)
         mb = self.max_blocks
+        W = PACK + mb
         pack = self.h_pack
         pack.zero_()
-        v = pack[: bucket * (4 + mb)].view(bucket, 4 + mb)
+        v = pack[: bucket * W].view(bucket, W)
         if B:
             v[:B, 0] = torch.as_tensor(ids, dtype=torch.int32)
             v[:B, 1] = torch.as_tensor(pos, dtype=torch.int32)
             v[:B, 2] = torch.as_tensor(slots, dtype=torch.int32)
             v[:B, 3] = torch.as_tensor(lens, dtype=torch.int32)
+            if state_slots is not None:
+                v[:B, 4] = torch.as_tensor(state_slots, dtype=torch.int32)
             for i, bt in enumerate(block_tables):
                 if bt:
-                    v[i, 4:4 + len(bt)] = torch.as_tensor(bt, dtype=torch.int32)
+                    v[i, PACK:PACK + len(bt)] = torch.as_tensor(bt, dtype=torch.int32)
         v[B:, 2] = -1
-        dev = self.s_pack[: bucket * (4 + mb)]
-        dev.copy_(pack[: bucket * (4 + mb)], non_blocking=True)
-        dv = dev.view(bucket, 4 + mb)
-        self.s_ids[:bucket].copy_(dv[:, 0])
-        self.s_pos[:bucket].copy_(dv[:, 1])
-        self.s_slots[:bucket].copy_(dv[:, 2])
-        self.s_lens[:bucket].copy_(dv[:, 3])
-        self.s_bt[:bucket].copy_(dv[:, 4:])
-        return bucket, pack[: bucket * (4 + mb)].numel() * 4
+        v[B:, 4] = self.scratch_slot
+        dev = self.s_pack[: bucket * W]
+        dev.copy_(pack[: bucket * W], non_blocking=True)
+        unpack_static(self, bucket)
+        return bucket, pack[: bucket * W].numel() * 4
 
-    def decode(self, ids, pos, slots, block_tables, lens, greedy=True):
+    def decode(self, ids, pos, slots, block_tables, lens, greedy=True, state_slots=None):
         """One decode step for B sequences. Returns (logits [B, V_local], tokens [B] or None)."""
         B = len(ids)
-        bucket, _ = self.load_decode_inputs(ids, pos, slots, block_tables, lens)
+        bucket, _ = self.load_decode_inputs(ids, pos, slots, block_tables, lens, state_slots)
         if self.use_graphs:
             key = (bucket, greedy)
             if key not in self.graphs:
@@ -163,10 +188,10 @@ class ModelRunner:
         p = self.s_pos[:B].long()
         self.s_slots[:B] = (self.s_bt[:B].gather(1, (p // 16)[:, None])[:, 0] * 16 + p % 16).int()
 
-    def decode_loop(self, ids, pos, slots, block_tables, lens, warmup: int, steps: int) -> dict:
+    def decode_loop(self, ids, pos, slots, block_tables, lens, warmup: int, steps: int, state_slots=None) -> dict:
         """Run ``warmup`` + ``steps`` greedy decode steps without host round trips and time the
         last ``steps`` with CUDA events (bracketed by barrier + synchronize)."""
-        bucket, _ = self.load_decode_inputs(ids, pos, slots, block_tables, lens)
+        bucket, _ = self.load_decode_inputs(ids, pos, slots, block_tables, lens, state_slots)
         return self.loop_body(len(ids), bucket, warmup, steps)
 
     def loop_body(self, B, bucket, warmup, steps) -> dict:
@@ -201,11 +226,11 @@ class ModelRunner:
         return {"ms": ms, "launches_per_step": self.launches_per_step.get(bucket)}
 
     # ------------------------------------------------------------ pipelined greedy decode
-    def pipeline_start(self, ids, pos, slots, block_tables, lens):
+    def pipeline_start(self, ids, pos, slots, block_tables, lens, state_slots=None):
         """Load a fresh decode state (one H2D copy); subsequent pipeline_step() calls advance
         it on the device without host inputs."""
         B = len(ids)
-        bucket, nbytes = self.load_decode_inputs(ids, pos, slots, block_tables, lens)
+        bucket, nbytes = self.load_decode_inputs(ids, pos, slots, block_tables, lens, state_slots)
         self._pipe = {"B": B, "bucket": bucket}
         if self.h_toks is None:
             pin = self.device.type == "cuda"
@@ -250,7 +275,7 @@ class ModelRunner:
         token), block_table, want_logits. Returns fp32 logits for sequences with want_logits,
         in order."""
         d = self.device
-        ids, pos, slots, cu, qs, lens, rows = [], [], [], [0], [], [], []
+        ids, pos, slots, cu, qs, lens, rows, sts = [], [], [], [0], [], [], [], []
         maxb = max(len(s["block_table"]) for s in seqs)
         bt = torch.zeros(len(seqs), maxb, dtype=torch.int32)
         for i, s in enumerate(seqs):
@@ -263,6 +288,7 @@ class ModelRunner:
             cu.append(cu[-1] + n)
             qs.append(st)
             lens.append(st + n)
+            sts.append(s.get("state_slot", self.scratch_slot))
             bt[i, : len(table)] = torch.as_tensor(table, dtype=torch.int32)
             if s.get("want_logits", True):
                 rows.append(cu[-1] - 1)
@@ -270,7 +296,8 @@ class ModelRunner:
         t = lambda x: torch.as_tensor(x, dtype=torch.int32).to(d, non_blocking=True)
         fb = ForwardBatch(input_ids=t(ids), positions=t(pos), slots=t(slots), block_tables=bt.to(d),
                           seq_lens=t(lens), logit_rows=torch.as_tensor(rows, dtype=torch.long).to(d),
-                          is_decode=False, cu_q=t(cu), q_start=t(qs), max_q=max(len(s["ids"]) for s in seqs))
+                          is_decode=False, cu_q=t(cu), q_start=t(qs), max_q=max(len(s["ids"]) for s in seqs),
+                          state_slots=t(sts) if self.lin_state is not None else None)
         if T == 0:
             return None
         return self.decoder.forward(fb)

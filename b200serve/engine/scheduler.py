@@ -53,6 +53,7 @@ class Request:
     registered: int = 0
     prefix_hit: int = 0
     seed: int = 0
+    state_slot: int = -1             # recurrent-state slot (hybrid models) while running
     done_event: threading.Event = field(default_factory=threading.Event)
 
     def __post_init__(self):
@@ -80,6 +81,8 @@ class Scheduler:
         self.running = []
         self.lock = threading.Lock()
         self.pipeline = True
+        # hybrid (DeltaNet) models keep a recurrent state per running request
+        self.free_states = list(range(max_batch)) if getattr(runner, "lin_state", None) is not None else None
         self.stats = {"steps": 0, "decode_steps": 0, "mixed_steps": 0, "preemptions": 0,
                       "generated": 0, "prefill_tokens": 0, "prefix_hit_tokens": 0}
 
@@ -128,6 +131,8 @@ class Scheduler:
                     self.alloc.release(matched)
                     break
                 self.waiting.pop(0)
+                if self.free_states is not None:
+                    req.state_slot = self.free_states.pop()
                 req.blocks = matched + self.alloc.allocate(need)
                 req.num_computed = len(matched) * BLOCK
                 req.prefix_hit = req.num_computed
@@ -145,6 +150,7 @@ class Scheduler:
             victim.blocks = []
             victim.num_computed = 0
             victim.registered = 0
+            self._release_state(victim)
             victim.state = "waiting"
             with self.lock:
                 self.waiting.insert(0, victim)
@@ -161,7 +167,13 @@ class Scheduler:
             req.blocks += self.alloc.allocate(need)
         return True
 
+    def _release_state(self, req: Request):
+        if self.free_states is not None and req.state_slot >= 0:
+            self.free_states.append(req.state_slot)
+            req.state_slot = -1
+
     def _finish(self, req: Request, reason: str):
+        self._release_state(req)
         req.state = "finished"
         req.finish_reason = reason
         req.finish_time = time.perf_counter()
@@ -215,7 +227,8 @@ class Scheduler:
         ids = [q.tokens[-1] for q in batch]
         pos = [len(q.tokens) - 1 for q in batch]
         slots = [q.blocks[p // BLOCK] * BLOCK + p % BLOCK for q, p in zip(batch, pos)]
-        r.pipeline_start(ids, pos, slots, [q.blocks for q in batch], [p + 1 for p in pos])
+        r.pipeline_start(ids, pos, slots, [q.blocks for q in batch], [p + 1 for p in pos],
+                         state_slots=[q.state_slot for q in batch])
         accepted = 0
         pending = None            # (event, slot) of the step whose tokens are not yet accepted
         slot = 0
@@ -296,7 +309,8 @@ class Scheduler:
         lens = [p + 1 for p in pos]
         greedy = all(r.params.greedy and r.params.repeat_penalty == 1.0 and not r.params.presence_penalty
                      and not r.params.frequency_penalty for r in batch)
-        logits, toks = self.runner.decode(ids, pos, slots, [r.blocks for r in batch], lens, greedy=greedy)
+        logits, toks = self.runner.decode(ids, pos, slots, [r.blocks for r in batch], lens, greedy=greedy,
+                                          state_slots=[r.state_slot for r in batch])
         if toks is None:
             toks = self._sample(logits, batch)
         toks = toks.tolist()
@@ -327,7 +341,8 @@ class Scheduler:
             if r not in self.running:
                 continue
             seqs.append({"ids": r.tokens[r.num_computed:r.num_computed + n], "start": r.num_computed,
-                         "block_table": r.blocks, "want_logits": r.num_computed + n == len(r.tokens)})
+                         "block_table": r.blocks, "want_logits": r.num_computed + n == len(r.tokens),
+                         "state_slot": r.state_slot})
             reqs.append((r, n))
             if remaining > 1:
                 budget -= n

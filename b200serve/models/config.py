@@ -10,6 +10,8 @@ The three built-in shapes are the configurations the benchmarks name:
 HF ``config.json`` files of the qwen2 / qwen3 / qwen3_moe / llama / mistral
 families map onto the same dataclass (Llama and Mistral are the Qwen2 block
 without q/k/v bias; their RoPE may carry a ``linear`` or ``llama3`` scaling).
+``qwen3_5`` (the Qwen3.5 hybrid) adds per-layer kinds: Gated DeltaNet
+linear-attention layers and gated full-attention layers with partial RoPE.
 """
 
 from __future__ import annotations
@@ -46,10 +48,30 @@ class ModelConfig:
     rope_scaling: Optional[dict] = None
     rotary_dim: int = 0              # 0 = whole head
     sliding_window: int = 0          # 0 = none; contexts are capped at the window
+    # Qwen3.5 hybrid: per-layer kind, gated full attention, Gated DeltaNet (linear) layers
+    layer_types: tuple = ()          # "full_attention" / "linear_attention" per layer; () = all full
+    attn_output_gate: bool = False   # q_proj also emits a per-head sigmoid gate on the attention output
+    norm_offset: bool = False        # RMSNorm weights stored as w with the scale (1 + w)
+    lin_k_heads: int = 0
+    lin_v_heads: int = 0
+    lin_k_dim: int = 0
+    lin_v_dim: int = 0
+    conv_kernel: int = 0
 
     @property
     def is_moe(self) -> bool:
         return self.num_experts > 0
+
+    @property
+    def is_hybrid(self) -> bool:
+        return any(t == "linear_attention" for t in self.layer_types)
+
+    def is_linear(self, i: int) -> bool:
+        return bool(self.layer_types) and self.layer_types[i] == "linear_attention"
+
+    @property
+    def lin_conv_dim(self) -> int:
+        return 2 * self.lin_k_heads * self.lin_k_dim + self.lin_v_heads * self.lin_v_dim
 
     @property
     def q_size(self) -> int:
@@ -101,7 +123,7 @@ BUILTIN = {
 }
 
 
-_FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "llama", "mistral")
+_FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "llama", "mistral", "qwen3_5_text")
 
 
 def _rope_params(d: dict):
@@ -116,6 +138,9 @@ def _rope_params(d: dict):
 
 
 def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
+    if d.get("model_type") == "qwen3_5" or "text_config" in d:
+        # the multimodal checkpoint wraps the text decoder; its language model is served alone
+        d = dict(d["text_config"], model_type="qwen3_5_text")
     mt = d.get("model_type", "qwen2")
     if mt not in _FAMILIES:
         raise NotImplementedError(f"model_type {mt!r}: supported families are {', '.join(_FAMILIES)}")
@@ -129,6 +154,18 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
     if mt == "mistral" and sw and sw < max_pos:
         max_pos = sw        # within the window, sliding-window attention equals full attention
     moe = mt == "qwen3_moe"
+    hybrid = {}
+    if mt == "qwen3_5_text":
+        n = d["num_hidden_layers"]
+        every = d.get("full_attention_interval", 4)
+        lt = d.get("layer_types") or ["linear_attention" if (i + 1) % every else "full_attention" for i in range(n)]
+        rp = d.get("rope_parameters") or {}
+        prf = d.get("partial_rotary_factor", rp.get("partial_rotary_factor", 0.25))
+        hd_full = d.get("head_dim") or d["hidden_size"] // d["num_attention_heads"]
+        hybrid = dict(layer_types=tuple(lt), attn_output_gate=True, norm_offset=True,
+                      lin_k_heads=d.get("linear_num_key_heads", 16), lin_v_heads=d.get("linear_num_value_heads", 32),
+                      lin_k_dim=d.get("linear_key_head_dim", 128), lin_v_dim=d.get("linear_value_head_dim", 128),
+                      conv_kernel=d.get("linear_conv_kernel_dim", 4), rotary_dim=int(hd_full * prf))
     return ModelConfig(
         name=name, vocab_size=d["vocab_size"], hidden_size=d["hidden_size"],
         num_layers=d["num_hidden_layers"], num_heads=heads,
@@ -136,7 +173,7 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         intermediate_size=d.get("intermediate_size", 0), rms_eps=d.get("rms_norm_eps", 1e-6),
         rope_theta=theta, rope_scaling=scaling,
         attn_bias=(mt == "qwen2") or bool(d.get("attention_bias", False)),
-        qk_norm=mt in ("qwen3", "qwen3_moe"),
+        qk_norm=mt in ("qwen3", "qwen3_moe", "qwen3_5_text"),
         tie_embeddings=bool(d.get("tie_word_embeddings", False)),
         num_experts=d.get("num_experts", 0) if moe else 0,
         experts_per_tok=d.get("num_experts_per_tok", 0) if moe else 0,
@@ -145,7 +182,7 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         max_position=max_pos,
         bos_token_id=d.get("bos_token_id") or 1,
         eos_token_id=(d.get("eos_token_id") if isinstance(d.get("eos_token_id"), int) else 2),
-        family=mt, sliding_window=sw if mt == "mistral" else 0,
+        family=mt, sliding_window=sw if mt == "mistral" else 0, **hybrid,
     )
 
 

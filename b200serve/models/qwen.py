@@ -42,6 +42,7 @@ class ForwardBatch:
     cu_q: torch.Tensor = None
     q_start: torch.Tensor = None
     max_q: int = 0
+    state_slots: torch.Tensor = None    # hybrid models: recurrent-state slot per sequence
 
 
 class NoComm:
@@ -81,6 +82,14 @@ class Decoder:
         self.attn_ws = None
         self.moe = None
         self.tq = None
+        # K/V cache index of each layer (hybrid models page only their full-attention layers)
+        self.kvi, n = [], 0
+        for i in range(cfg.num_layers):
+            self.kvi.append(-1 if cfg.is_linear(i) else n)
+            n += 0 if cfg.is_linear(i) else 1
+        self.lin_state = None
+        if cfg.is_hybrid and getattr(kv_cache, "kv_format", "bf16") != "bf16":
+            raise NotImplementedError("hybrid (DeltaNet) models run with the bf16 KV cache")
         want_rot = getattr(kv_cache, "kv_format", "bf16") == "turboquant"
         if want_rot:
             self.tq = ops.TurboQuantTables(kv_cache.key_bits, kv_cache.value_bits, self.device)
@@ -97,7 +106,7 @@ class Decoder:
         """Re-lay every GEMM weight tile-contiguous (ops.PackedWeight), in place, one at a time."""
         w = self.w
         for lw in w.layers:
-            for name in ("qkv", "o", "gate_up", "down", "router"):
+            for name in ("qkv", "o", "gate_up", "down", "router", "lin_in"):
                 t = getattr(lw, name)
                 if isinstance(t, torch.Tensor):
                     setattr(lw, name, ops.pack_weight(t))
@@ -132,7 +141,7 @@ class Decoder:
         vst = torch.empty_like(kst)
         stage_slots = torch.arange(T, dtype=torch.int32, device=qkv.device)
         q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, stage_slots, kst, vst,
-                         self.nq, self.nkv, eps)
+                         self.nq, self.nkv, eps, hd=self.hd)
         q_rot, q_jl = ops.tq_qkv(q, kst, vst, fb.slots, tb, kv, i)
         if fb.is_decode:
             return ops.tq_decode_attention(q_rot, q_jl, kv, i, tb, fb.block_tables, fb.seq_lens, self.scale, tps,
@@ -208,7 +217,7 @@ class Decoder:
         kb = torch.zeros(kc.shape[0], self.nkv, 16, self.hd, dtype=torch.float32)
         vb = torch.zeros_like(kb)
         q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots, kb, vb, self.nq,
-                         self.nkv, eps)
+                         self.nkv, eps, hd=self.hd)
         sl = fb.slots.long()
         ok = sl >= 0
         blk, off = sl[ok] // 16, sl[ok] % 16
@@ -225,13 +234,30 @@ class Decoder:
     def _qkv_attend(self, i, x, lw, fb, T, plan, tq_pre, ag=None):
         """QKV projection + post-processing + attention of layer ``i`` -> [T, nq, hd]. On a bf16
         cache the QKV GEMM's epilogue does the norm, RoPE and KV write itself."""
-        if self.tq is None and self.kv.kv_format == "bf16" and ops.qkv_fused_ok(x, lw.qkv, self.kv.k[i]):
+        plain = not self.cfg.attn_output_gate and self.cos_sin.shape[1] == self.hd
+        if plain and self.tq is None and self.kv.kv_format == "bf16" and ops.qkv_fused_ok(x, lw.qkv, self.kv.k[i]):
             kc, vc = self.kv.k[i], self.kv.v[i]
             q = ops.qkv_fused(x, lw.qkv, lw.qkv_bias, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots,
                               kc, vc, self.nq, self.nkv, self.cfg.rms_eps, ag=ag)
             return self._attn_core(i, q, fb, plan)
         qkv = ops.linear(x, lw.qkv, bias=lw.qkv_bias, ag=ag)
-        return self._attend(i, qkv, lw, fb, T, plan, tq_pre)
+        out = self._attend(i, qkv, lw, fb, T, plan, tq_pre)
+        if self.cfg.attn_output_gate:
+            # gated attention: the QKV GEMM's trailing nq*hd columns are the per-head output gate
+            w0 = (self.nq + 2 * self.nkv) * self.hd
+            ops.sigmoid_gate_mul(out.view(T, self.nq * self.hd), qkv[:, w0:w0 + self.nq * self.hd])
+        return out
+
+    def _linear_mix(self, i, x, lw, fb):
+        """Gated DeltaNet token mixing of layer ``i`` -> [T, nv_local * dv] (before out_proj)."""
+        cfg, st = self.cfg, self.lin_state
+        tp = self.w.tp_size
+        y = ops.linear(x, lw.lin_in)
+        cu = None if fb.is_decode else fb.cu_q
+        q_start = fb.positions if fb.is_decode else fb.q_start
+        return ops.deltanet_layer(y, lw.conv_w, lw.lin_A, lw.lin_dt, lw.lin_norm, st.conv[i], st.rec[i], cu, q_start,
+                                  fb.state_slots, cfg.lin_k_heads // tp, cfg.lin_v_heads // tp, cfg.lin_k_dim,
+                                  cfg.rms_eps)
 
     def _attn_core(self, i, q, fb, plan):
         tps, nsplit, ws = plan
@@ -251,7 +277,7 @@ class Decoder:
             return self._attention_q4(i, qkv, lw, fb, T, tps, nsplit, ws, tq_pre)
         kc, vc = self.kv.k[i], self.kv.v[i]
         q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots, kc, vc,
-                         self.nq, self.nkv, eps)
+                         self.nq, self.nkv, eps, hd=self.hd)
         return self._attn_core(i, q, fb, plan)
 
     def _forward_rsag(self, fb, h, plan, tq_pre):
@@ -307,15 +333,20 @@ class Decoder:
         quant_kv = self.tq is not None or (self.kv.kv_format == "int4g128" and h.is_cuda and ops._TC_PREFILL)
         tq_pre = self._tq_prefill_pages(fb) if (quant_kv and not fb.is_decode) else None
         plan = (tps, nsplit, ws) if fb.is_decode else (0, 0, None)
-        if self.moe is None and comm.world > 1 and hasattr(comm, "use_rsag") and comm.use_rsag(T):
+        if self.moe is None and not cfg.is_hybrid and comm.world > 1 and hasattr(comm, "use_rsag") and \
+                comm.use_rsag(T):
             return self._forward_rsag(fb, h, plan, tq_pre)
         residual = torch.empty_like(h)
         x = ops.rmsnorm([h], w.layers[0].input_norm, eps, residual_out=residual)
         for i, lw in enumerate(w.layers):
             if i > 0:
                 x = ops.rmsnorm(mlp_parts, lw.input_norm, eps, residual=residual, residual_out=residual)
-            attn = self._qkv_attend(i, x, lw, fb, T, plan, tq_pre)
-            o_parts = self._row_parallel(attn.view(T, self.nq * self.hd), lw.o, "o")
+            if cfg.is_linear(i):
+                mix = self._linear_mix(i, x, lw, fb)
+                o_parts = self._row_parallel(mix, lw.o, "o")
+            else:
+                attn = self._qkv_attend(self.kvi[i], x, lw, fb, T, plan, tq_pre)
+                o_parts = self._row_parallel(attn.view(T, self.nq * self.hd), lw.o, "o")
             x = ops.rmsnorm(o_parts, lw.post_norm, eps, residual=residual, residual_out=residual)
             if self.moe is not None:
                 mlp_parts = self.moe.reduced(i, x)

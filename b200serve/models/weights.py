@@ -63,6 +63,12 @@ class LayerWeights:
     router: torch.Tensor = None        # MoE: [E, H]
     experts_gate_up: torch.Tensor = None  # [E_local, 2*Ie_pad, H]
     experts_down: torch.Tensor = None     # [E_local, H, Ie_pad]
+    # Gated DeltaNet layer (Qwen3.5 hybrid); qkv is None there
+    lin_in: torch.Tensor = None        # [q | k | v | z | b | a] rows of this rank's heads
+    lin_norm: torch.Tensor = None      # [dv] gated RMSNorm weight
+    conv_w: torch.Tensor = None        # [conv_dim_local, K] fp32
+    lin_A: torch.Tensor = None         # [nv_local] fp32, -exp(A_log)
+    lin_dt: torch.Tensor = None        # [nv_local] fp32
 
 
 @dataclass
@@ -107,7 +113,13 @@ def shard_layer_dense(cfg: ModelConfig, full: dict, rank: int, size: int, dtype,
     """``full`` holds unsharded HF-named tensors of one layer (q,k,v,o,gate,up,down,...)."""
     hd = cfg.head_dim
     assert cfg.num_heads % size == 0, "query heads must divide tp_size"
-    q = _shard_rows(full["q"], rank, size)
+    gate = None
+    if cfg.attn_output_gate:
+        from b200serve.models.hybrid import split_gated_q
+        qf, gf = split_gated_q(full["q"], cfg.num_heads, hd)
+        q, gate = _shard_rows(qf, rank, size), _shard_rows(gf, rank, size)
+    else:
+        q = _shard_rows(full["q"], rank, size)
     if cfg.num_kv_heads % size == 0:
         k = _shard_rows(full["k"], rank, size)
         v = _shard_rows(full["v"], rank, size)
@@ -119,15 +131,19 @@ def shard_layer_dense(cfg: ModelConfig, full: dict, rank: int, size: int, dtype,
         rep = size // cfg.num_kv_heads
         kvsel = lambda t: _shard_rows(t, rank // rep, cfg.num_kv_heads)
         k, v = kvsel(full["k"]), kvsel(full["v"])
-    qkv = torch.cat([q, k, v])
+    qkv = torch.cat([q, k, v] + ([gate] if gate is not None else []))
     bias = None
     if cfg.attn_bias:
         bias = torch.cat([_shard_rows(full["q_bias"], rank, size), kvsel(full["k_bias"]), kvsel(full["v_bias"])])
     o = full["o"]
     oc = o.shape[1] // size
     o = o[:, rank * oc:(rank + 1) * oc]
-    lw = LayerWeights(input_norm=full["input_norm"], post_norm=full["post_norm"], qkv=qkv, o=o, qkv_bias=bias,
-                      q_norm=full.get("q_norm"), k_norm=full.get("k_norm"))
+    norms = {k_: full.get(k_) for k_ in ("input_norm", "post_norm", "q_norm", "k_norm")}
+    if cfg.norm_offset:
+        from b200serve.models.hybrid import offset_norm
+        norms = {k_: (offset_norm(t) if t is not None else None) for k_, t in norms.items()}
+    lw = LayerWeights(input_norm=norms["input_norm"], post_norm=norms["post_norm"], qkv=qkv, o=o, qkv_bias=bias,
+                      q_norm=norms["q_norm"], k_norm=norms["k_norm"])
     if not cfg.is_moe:
         I = cfg.intermediate_size
         assert I % size == 0
@@ -152,12 +168,20 @@ def build_weights(cfg: ModelConfig, layer_source, embed, lm_head, final_norm, tp
     layers = []
     for i in range(cfg.num_layers):
         full = layer_source(i)
+        if cfg.is_linear(i):
+            from b200serve.models.hybrid import shard_layer_linear
+            layers.append(shard_layer_linear(cfg, full, tp_rank, tp_size, dtype, device))
+            del full
+            continue
         lw = shard_layer_dense(cfg, full, tp_rank, tp_size, dtype, device)
         if cfg.is_moe:
             shard_layer_moe(cfg, full, lw, ep_rank, ep_size, dtype, device)
         layers.append(lw)
         del full
     v0, v1 = vocab_shard(cfg.vocab_size, tp_rank, tp_size)
+    if cfg.norm_offset:
+        from b200serve.models.hybrid import offset_norm
+        final_norm = offset_norm(final_norm)
     return ModelWeights(
         embed=embed.to(device=device, dtype=dtype).contiguous(),
         final_norm=final_norm.to(device=device, dtype=dtype).contiguous(),
@@ -180,21 +204,29 @@ def random_weights(cfg: ModelConfig, seed=0, std=0.02, tp_rank=0, tp_size=1, ep_
 
     embed = n(V, H)
     lm_head = embed if cfg.tie_embeddings else n(V, H)
-    final_norm = torch.ones(H, dtype=dtype, device=gen_dev)
+    final_norm = (torch.zeros if cfg.norm_offset else torch.ones)(H, dtype=dtype, device=gen_dev)
 
     class _Gen:
         def __call__(self, i):
             hd = cfg.head_dim
-            d = {"q": n(cfg.q_size, H), "k": n(cfg.kv_size, H), "v": n(cfg.kv_size, H), "o": n(H, cfg.q_size),
-                 "input_norm": torch.ones(H, dtype=dtype, device=gen_dev),
-                 "post_norm": torch.ones(H, dtype=dtype, device=gen_dev)}
+            # norms with a (1 + w) scale are stored as w: zeros give the unit scale
+            one = (lambda *sh: torch.zeros(*sh, dtype=dtype, device=gen_dev)) if cfg.norm_offset else \
+                (lambda *sh: torch.ones(*sh, dtype=dtype, device=gen_dev))
+            if cfg.is_linear(i):
+                from b200serve.models.hybrid import random_linear_layer
+                I = cfg.intermediate_size
+                d = random_linear_layer(cfg, n, lambda *sh: torch.ones(*sh, dtype=dtype, device=gen_dev), None)
+                d.update(input_norm=one(H), post_norm=one(H), gate=n(I, H), up=n(I, H), down=n(H, I))
+                return d
+            qrows = cfg.q_size * (2 if cfg.attn_output_gate else 1)
+            d = {"q": n(qrows, H), "k": n(cfg.kv_size, H), "v": n(cfg.kv_size, H), "o": n(H, cfg.q_size),
+                 "input_norm": one(H), "post_norm": one(H)}
             if cfg.attn_bias:
                 d.update(q_bias=torch.zeros(cfg.q_size, dtype=dtype, device=gen_dev),
                          k_bias=torch.zeros(cfg.kv_size, dtype=dtype, device=gen_dev),
                          v_bias=torch.zeros(cfg.kv_size, dtype=dtype, device=gen_dev))
             if cfg.qk_norm:
-                d.update(q_norm=torch.ones(hd, dtype=dtype, device=gen_dev),
-                         k_norm=torch.ones(hd, dtype=dtype, device=gen_dev))
+                d.update(q_norm=one(hd), k_norm=one(hd))
             if cfg.is_moe:
                 E, Ie = cfg.num_experts, cfg.moe_intermediate_size
                 d.update(router=n(E, H), exp_gate=n(E, Ie, H), exp_up=n(E, Ie, H), exp_down=n(E, H, Ie))
@@ -222,6 +254,10 @@ def hf_layer_dict(get, cfg: ModelConfig, i: int) -> dict:
     """Collect layer ``i`` from an HF-named tensor getter (``get(name)`` -> tensor or None)."""
     pre = f"model.layers.{i}."
     d = {}
+    if cfg.is_linear(i):
+        from b200serve.models.hybrid import LIN_KEYS
+        for k, name in LIN_KEYS.items():
+            d[k] = get(pre + name)
     for k, name in _HF_LAYER_KEYS.items():
         t = get(pre + name)
         if t is not None:
@@ -234,8 +270,18 @@ def hf_layer_dict(get, cfg: ModelConfig, i: int) -> dict:
     return d
 
 
+def _with_lm_prefix(get):
+    """Multimodal checkpoints nest the language model under ``model.language_model.``."""
+    def g(name):
+        t = get(name)
+        if t is None and name.startswith("model."):
+            t = get("model.language_model." + name[len("model."):])
+        return t
+    return g
+
+
 def load_hf_state_dict(cfg: ModelConfig, sd: dict, **kw) -> ModelWeights:
-    get = sd.get
+    get = _with_lm_prefix(sd.get)
     embed = get("model.embed_tokens.weight")
     lm = get("lm_head.weight")
     if lm is None:
@@ -257,9 +303,11 @@ def load_safetensors_dir(cfg: ModelConfig, path: str, **kw) -> ModelWeights:
         for k in h.keys():
             where[k] = h
 
-    def get(name):
+    def get_raw(name):
         h = where.get(name)
         return h.get_tensor(name) if h is not None else None
+
+    get = _with_lm_prefix(get_raw)
 
     embed = get("model.embed_tokens.weight")
     lm = get("lm_head.weight")

@@ -157,18 +157,21 @@ def rope_cos_sin(head_dim: int, max_pos: int, theta: float, device, rot_dim: int
 
 # ------------------------------------------------------------------ QKV post
 def qkv_post(qkv, bias, q_norm, k_norm, cos_sin, positions, slots, k_cache, v_cache, nq, nkv, eps,
-             q_out=None):
+             q_out=None, hd=None):
     """Split the fused QKV projection, add bias, per-head q/k RMSNorm, RoPE, and
     write K/V rows into the paged cache at ``slots`` (block*16 + offset; -1 = skip).
-    Returns q [T, nq, hd]. Caches are [num_blocks, nkv, 16, hd]."""
+    Returns q [T, nq, hd]. Caches are [num_blocks, nkv, 16, hd]. ``qkv`` rows may be wider
+    than (nq + 2 nkv) hd (extra columns, e.g. an output gate, are ignored); RoPE covers the
+    first ``cos_sin.shape[1]`` dims of each head (``hd`` defaults to that width)."""
     T = qkv.shape[0]
-    hd = cos_sin.shape[1]
+    hd = hd or cos_sin.shape[1]
+    rot = cos_sin.shape[1]
     if _cuda(qkv):
         q_out = q_out if q_out is not None else torch.empty(T, nq, hd, dtype=qkv.dtype, device=qkv.device)
         ext().qkv_post(qkv, bias, q_norm, k_norm, cos_sin, positions, slots, q_out, k_cache, v_cache,
                        nq, nkv, float(eps))
         return q_out
-    x = qkv.float()
+    x = qkv[:, :(nq + 2 * nkv) * hd].float()
     if bias is not None:
         x = (x + bias.float()).to(qkv.dtype).float()
     q = x[:, : nq * hd].view(T, nq, hd)
@@ -182,14 +185,15 @@ def qkv_post(qkv, bias, q_norm, k_norm, cos_sin, positions, slots, k_cache, v_ca
     if q_norm is not None:
         q, k = norm(q, q_norm), norm(k, k_norm)
     cs = cos_sin[positions.long()]
-    c = torch.cat([cs[:, : hd // 2]] * 2, -1)[:, None, :]
-    s = torch.cat([cs[:, hd // 2:]] * 2, -1)[:, None, :]
+    c = torch.cat([cs[:, : rot // 2]] * 2, -1)[:, None, :]
+    s = torch.cat([cs[:, rot // 2:]] * 2, -1)[:, None, :]
 
-    def rot(t):
-        t1, t2 = t[..., : hd // 2], t[..., hd // 2:]
-        return t * c + torch.cat([-t2, t1], -1) * s
+    def rope(t):
+        r, p = t[..., :rot], t[..., rot:]
+        t1, t2 = r[..., : rot // 2], r[..., rot // 2:]
+        return torch.cat([r * c + torch.cat([-t2, t1], -1) * s, p], -1)
 
-    q, k = rot(q), rot(k)
+    q, k = rope(q), rope(k)
     sl = slots.long()
     ok = sl >= 0
     blk, off = sl[ok] // 16, sl[ok] % 16
@@ -200,6 +204,85 @@ def qkv_post(qkv, bias, q_norm, k_norm, cos_sin, positions, slots, k_cache, v_ca
         q_out.copy_(r)
         return q_out
     return r
+
+
+# ------------------------------------------------------------------ Gated DeltaNet
+def deltanet_layer(y, conv_w, A, dt_bias, norm_w, conv_state, rec_state, cu_q, q_start, slots, nk, nv, D,
+                   eps):
+    """Token mixing of a Gated DeltaNet layer after its fused input projection
+    ``y`` [T, (2 nk + nv) D + nv D + 2 nv] = [q | k | v | z | b | a]: causal depthwise conv
+    (state carried in ``conv_state`` [slots, conv_dim, K-1] fp32), SiLU, L2-normalised q/k,
+    the gated delta-rule recurrence (state ``rec_state`` [slots, nv, D, D] fp32) and the
+    gated RMSNorm with ``norm_w``. ``cu_q`` None means one token per sequence (decode); a
+    sequence whose ``q_start`` is 0 starts from zero state. Returns [T, nv * D].
+    Reference behaviour: shaders/ssm_step.wgsl:1-12, conv1d.wgsl:28-82, l2norm.wgsl:14."""
+    T = y.shape[0]
+    conv_dim = (2 * nk + nv) * D
+    if _cuda(y, 2):
+        xc = torch.empty(T, conv_dim, dtype=y.dtype, device=y.device)
+        gb = torch.empty(T, nv, 2, dtype=torch.float32, device=y.device)
+        out = torch.empty(T, nv * D, dtype=y.dtype, device=y.device)
+        ext().deltanet_layer(y, conv_w, A, dt_bias, norm_w, conv_state, rec_state, cu_q, q_start, slots, xc, gb,
+                             out, nk, nv, D, float(eps))
+        return out
+    return _deltanet_cpu(y, conv_w, A, dt_bias, norm_w, conv_state, rec_state, cu_q, q_start, slots, nk, nv, D,
+                         eps)
+
+
+def _deltanet_cpu(y, conv_w, A, dt_bias, norm_w, conv_state, rec_state, cu_q, q_start, slots, nk, nv, D, eps):
+    """fp32 restatement of ``deltanet_layer`` (the CPU path and the GPU tests' oracle)."""
+    import torch.nn.functional as F
+    T = y.shape[0]
+    K = conv_w.shape[1]
+    conv_dim = (2 * nk + nv) * D
+    cu = cu_q.tolist() if cu_q is not None else list(range(T + 1))
+    starts, sl = q_start.tolist(), slots.tolist()
+    out = torch.empty(T, nv * D, dtype=y.dtype, device=y.device)
+    ratio = nv // nk
+    for s in range(len(cu) - 1):
+        t0, t1 = cu[s], cu[s + 1]
+        n = t1 - t0
+        if n == 0:
+            continue
+        hist = starts[s] > 0
+        yt = y[t0:t1].float()
+        prev = conv_state[sl[s]] if hist else torch.zeros(conv_dim, K - 1, dtype=torch.float32, device=y.device)
+        full = torch.cat([prev, yt[:, :conv_dim].t()], 1)
+        conv_state[sl[s]] = full[:, -(K - 1):]
+        x = F.silu(F.conv1d(full[None], conv_w.float()[:, None, :], groups=conv_dim)[0]).t()
+        q = x[:, :nk * D].reshape(n, nk, D)
+        k = x[:, nk * D:2 * nk * D].reshape(n, nk, D)
+        v = x[:, 2 * nk * D:].reshape(n, nv, D)
+        q = q * torch.rsqrt(q.pow(2).sum(-1, keepdim=True) + 1e-6)
+        k = k * torch.rsqrt(k.pow(2).sum(-1, keepdim=True) + 1e-6)
+        q = q.repeat_interleave(ratio, 1) * D ** -0.5
+        k = k.repeat_interleave(ratio, 1)
+        z = yt[:, conv_dim:conv_dim + nv * D].reshape(n, nv, D)
+        b = yt[:, conv_dim + nv * D:conv_dim + nv * D + nv]
+        a = yt[:, conv_dim + nv * D + nv:conv_dim + nv * D + 2 * nv]
+        beta = torch.sigmoid(b)
+        decay = torch.exp(A.float() * F.softplus(a + dt_bias.float()))
+        S = rec_state[sl[s]].clone() if hist else torch.zeros(nv, D, D, dtype=torch.float32, device=y.device)
+        o = torch.empty(n, nv, D, dtype=torch.float32, device=y.device)
+        for t in range(n):
+            S = S * decay[t][:, None, None]
+            kv = (S * k[t][:, :, None]).sum(1)
+            delta = (v[t] - kv) * beta[t][:, None]
+            S = S + k[t][:, :, None] * delta[:, None, :]
+            o[t] = (S * q[t][:, :, None]).sum(1)
+        rec_state[sl[s]] = S
+        on = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + eps)
+        out[t0:t1] = (norm_w.float() * on * F.silu(z)).reshape(n, nv * D).to(y.dtype)
+    return out
+
+
+def sigmoid_gate_mul(attn, gate):
+    """attn [T, W] *= sigmoid(gate) in place; ``gate`` may be a strided column view."""
+    if _cuda(attn):
+        ext().sigmoid_gate_mul(attn, gate)
+        return attn
+    attn.copy_((attn.float() * torch.sigmoid(gate.float())).to(attn.dtype))
+    return attn
 
 
 # ------------------------------------------------------------------ SwiGLU

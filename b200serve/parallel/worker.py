@@ -12,6 +12,8 @@ from __future__ import annotations
 
 import torch
 
+from b200serve.engine.runner import PACK, unpack_static
+
 OP_DECODE, OP_PREFILL, OP_STOP, OP_LOOP, OP_PIPE_START, OP_PIPE_STEP = 1, 2, 3, 4, 5, 6
 HDR = 32
 MAX_PATCH = (HDR - 2) // 3   # block-table patches carried inline in a PIPE_STEP header
@@ -36,37 +38,38 @@ class BroadcastRunner:
         if payload is not None:
             self.comm.broadcast(payload, 0)
 
-    def decode(self, ids, pos, slots, block_tables, lens, greedy=True):
+    def decode(self, ids, pos, slots, block_tables, lens, greedy=True, state_slots=None):
         B = len(ids)
-        bucket, _ = self.inner.load_decode_inputs(ids, pos, slots, block_tables, lens)
-        n = bucket * (4 + self.inner.max_blocks)
+        bucket, _ = self.inner.load_decode_inputs(ids, pos, slots, block_tables, lens, state_slots)
+        n = bucket * (PACK + self.inner.max_blocks)
         self._send([OP_DECODE, B, bucket, int(greedy)], self.inner.s_pack[:n])
         return _decode_after_inputs(self.inner, self.comm, B, bucket, greedy)
 
     def prefill(self, seqs):
         flat = [len(seqs)]
         for s in seqs:
-            flat += [len(s["ids"]), s["start"], int(s.get("want_logits", True)), len(s["block_table"])]
+            flat += [len(s["ids"]), s["start"], int(s.get("want_logits", True)), len(s["block_table"]),
+                     s.get("state_slot", self.inner.scratch_slot)]
             flat += list(s["ids"]) + list(s["block_table"])
         payload = torch.as_tensor(flat, dtype=torch.int32).to(self.device)
         self._send([OP_PREFILL, payload.numel()], payload)
         logits = self.inner.prefill(seqs)
         return self.comm.gather_vocab(logits)
 
-    def decode_loop(self, ids, pos, slots, block_tables, lens, warmup, steps):
+    def decode_loop(self, ids, pos, slots, block_tables, lens, warmup, steps, state_slots=None):
         B = len(ids)
-        bucket, _ = self.inner.load_decode_inputs(ids, pos, slots, block_tables, lens)
-        n = bucket * (4 + self.inner.max_blocks)
+        bucket, _ = self.inner.load_decode_inputs(ids, pos, slots, block_tables, lens, state_slots)
+        n = bucket * (PACK + self.inner.max_blocks)
         self._send([OP_LOOP, B, bucket, warmup, steps], self.inner.s_pack[:n])
         _unpack_static(self.inner, bucket)
         return self.inner.loop_body(B, bucket, warmup, steps)
 
     # pipelined greedy decode: every rank replays the device-advancing graph in lock-step
-    def pipeline_start(self, ids, pos, slots, block_tables, lens):
+    def pipeline_start(self, ids, pos, slots, block_tables, lens, state_slots=None):
         B = len(ids)
-        nbytes = self.inner.pipeline_start(ids, pos, slots, block_tables, lens)
+        nbytes = self.inner.pipeline_start(ids, pos, slots, block_tables, lens, state_slots)
         bucket = self.inner._pipe["bucket"]
-        n = bucket * (4 + self.inner.max_blocks)
+        n = bucket * (PACK + self.inner.max_blocks)
         self._send([OP_PIPE_START, B, bucket], self.inner.s_pack[:n])
         self._patches = []
         return nbytes
@@ -95,13 +98,7 @@ class BroadcastRunner:
 
 
 def _unpack_static(runner, bucket):
-    mb = runner.max_blocks
-    dv = runner.s_pack[: bucket * (4 + mb)].view(bucket, 4 + mb)
-    runner.s_ids[:bucket].copy_(dv[:, 0])
-    runner.s_pos[:bucket].copy_(dv[:, 1])
-    runner.s_slots[:bucket].copy_(dv[:, 2])
-    runner.s_lens[:bucket].copy_(dv[:, 3])
-    runner.s_bt[:bucket].copy_(dv[:, 4:])
+    unpack_static(runner, bucket)
 
 
 def _decode_after_inputs(runner, comm, B, bucket, greedy):
@@ -126,13 +123,13 @@ def _unpack_prefill(flat):
     i = 1
     seqs = []
     for _ in range(n):
-        L, start, want, nb = flat[i:i + 4]
-        i += 4
+        L, start, want, nb, st = flat[i:i + 5]
+        i += 5
         ids = flat[i:i + L]
         i += L
         bt = flat[i:i + nb]
         i += nb
-        seqs.append({"ids": ids, "start": start, "want_logits": bool(want), "block_table": bt})
+        seqs.append({"ids": ids, "start": start, "want_logits": bool(want), "block_table": bt, "state_slot": st})
     return seqs
 
 
@@ -147,18 +144,18 @@ def worker_loop(runner, comm):
             return
         if op == OP_DECODE:
             B, bucket, greedy = h[1], h[2], bool(h[3])
-            n = bucket * (4 + runner.max_blocks)
+            n = bucket * (PACK + runner.max_blocks)
             comm.broadcast(runner.s_pack[:n], 0)
             _decode_after_inputs(runner, comm, B, bucket, greedy)
         elif op == OP_LOOP:
             B, bucket, warmup, steps = h[1], h[2], h[3], h[4]
-            n = bucket * (4 + runner.max_blocks)
+            n = bucket * (PACK + runner.max_blocks)
             comm.broadcast(runner.s_pack[:n], 0)
             _unpack_static(runner, bucket)
             runner.loop_body(B, bucket, warmup, steps)
         elif op == OP_PIPE_START:
             B, bucket = h[1], h[2]
-            n = bucket * (4 + runner.max_blocks)
+            n = bucket * (PACK + runner.max_blocks)
             comm.broadcast(runner.s_pack[:n], 0)
             _unpack_static(runner, bucket)
             runner._pipe = {"B": B, "bucket": bucket}
