@@ -6,7 +6,10 @@ The three built-in shapes are the configurations the benchmarks name:
 * ``qwen3-8b``: 36 layers, hidden 4096, 32/8 heads (head_dim 128), SwiGLU
   12288, vocab 151936, per-head q/k RMSNorm (Qwen3), RoPE 1e6;
 * ``qwen3-30b-a3b``: 48 layers, hidden 2048, 32/4 heads (head_dim 128), 128
-  experts with top-8 softmax routing, expert FFN 768, vocab 151936.
+  experts with top-8 softmax routing, expert FFN 768, vocab 151936;
+* ``qwen3.5-9b``: the Qwen3.5 hybrid text decoder, 32 layers (every 4th gated full
+  attention with 16/4 heads of 256 and RoPE on 64 dims, the rest Gated DeltaNet with
+  16 key / 32 value heads of 128), hidden 4096, SwiGLU 12288, vocab 248320.
 HF ``config.json`` files of the qwen2 / qwen3 / qwen3_moe / llama / mistral
 families map onto the same dataclass (Llama and Mistral are the Qwen2 block
 without q/k/v bias; their RoPE may carry a ``linear`` or ``llama3`` scaling).
@@ -89,6 +92,13 @@ class ModelConfig:
         else:
             ffn = 3 * h * self.intermediate_size
         emb = self.vocab_size * h * (1 if self.tie_embeddings else 2)
+        if self.is_hybrid:
+            gate = self.q_size * h if self.attn_output_gate else 0
+            nv_dv = self.lin_v_heads * self.lin_v_dim
+            lin = h * (self.lin_conv_dim + nv_dv + 2 * self.lin_v_heads) + nv_dv * h + \
+                self.lin_conv_dim * self.conv_kernel
+            n_lin = sum(1 for i in range(l) if self.is_linear(i))
+            return n_lin * (lin + ffn + 2 * h) + (l - n_lin) * (attn + gate + ffn + 2 * h) + emb + h
         return l * (attn + ffn + 2 * h) + emb + h
 
     def to_hf_dict(self) -> dict:
@@ -103,7 +113,15 @@ class ModelConfig:
             "bos_token_id": self.bos_token_id, "eos_token_id": self.eos_token_id,
             "initializer_range": 0.02, "attention_dropout": 0.0,
         }
-        if self.is_moe:
+        if self.is_hybrid:
+            d.update(model_type="qwen3_5_text", architectures=["Qwen3_5ForCausalLM"], attention_bias=False,
+                     layer_types=list(self.layer_types), linear_num_key_heads=self.lin_k_heads,
+                     linear_num_value_heads=self.lin_v_heads, linear_key_head_dim=self.lin_k_dim,
+                     linear_value_head_dim=self.lin_v_dim, linear_conv_kernel_dim=self.conv_kernel,
+                     partial_rotary_factor=self.rotary_dim / self.head_dim,
+                     rope_parameters={"rope_type": "default", "rope_theta": self.rope_theta,
+                                      "partial_rotary_factor": self.rotary_dim / self.head_dim})
+        elif self.is_moe:
             d.update(model_type="qwen3_moe", architectures=["Qwen3MoeForCausalLM"],
                      num_experts=self.num_experts, num_experts_per_tok=self.experts_per_tok,
                      moe_intermediate_size=self.moe_intermediate_size,
@@ -120,6 +138,19 @@ BUILTIN = {
     "qwen3-8b": ModelConfig("qwen3-8b", 151936, 4096, 36, 32, 8, 128, 12288, qk_norm=True),
     "qwen3-30b-a3b": ModelConfig("qwen3-30b-a3b", 151936, 2048, 48, 32, 4, 128, 6144, qk_norm=True,
                                  num_experts=128, experts_per_tok=8, moe_intermediate_size=768),
+    # CPU-sized hybrid for tests: 3 Gated DeltaNet layers + 1 gated attention layer
+    "tiny-qwen35": ModelConfig("tiny-qwen35", 32000, 256, 4, 4, 2, 64, 512, rope_theta=1e4, qk_norm=True,
+                               max_position=4096, rotary_dim=16,
+                               layer_types=("linear_attention",) * 3 + ("full_attention",),
+                               attn_output_gate=True, norm_offset=True, lin_k_heads=2, lin_v_heads=4,
+                               lin_k_dim=32, lin_v_dim=32, conv_kernel=4),
+    # the Qwen3.5-9B text decoder: 24 Gated DeltaNet + 8 gated full-attention layers (3:1)
+    "qwen3.5-9b": ModelConfig("qwen3.5-9b", 248320, 4096, 32, 16, 4, 256, 12288, rope_theta=1e4, qk_norm=True,
+                              max_position=32768, rotary_dim=64,
+                              layer_types=tuple("full_attention" if (i + 1) % 4 == 0 else "linear_attention"
+                                                for i in range(32)),
+                              attn_output_gate=True, norm_offset=True, lin_k_heads=16, lin_v_heads=32,
+                              lin_k_dim=128, lin_v_dim=128, conv_kernel=4),
 }
 
 

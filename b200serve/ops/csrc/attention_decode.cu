@@ -39,7 +39,13 @@ __device__ __forceinline__ void load_page(PageRegs<HD>& r, const __nv_bfloat16* 
   const __nv_bfloat16* vpage = v_cache + page_off + lane * E;
 #pragma unroll
   for (int t = 0; t < 16; ++t) {
-    if constexpr (E == 4) {
+    if constexpr (E == 8) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(vpage + (size_t)t * HD));
+      r.v[t][0] = raw.x;
+      r.v[t][1] = raw.y;
+      r.v[t][2] = raw.z;
+      r.v[t][3] = raw.w;
+    } else if constexpr (E == 4) {
       const uint2 raw = __ldg(reinterpret_cast<const uint2*>(vpage + (size_t)t * HD));
       r.v[t][0] = raw.x;
       r.v[t][1] = raw.y;
@@ -136,8 +142,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
 #pragma unroll
     for (int t = 0; t < kPage; ++t) {
       float vf[E];
-      if constexpr (E == 4) {
-        vf[0] = bf16_lo(r.v[t][0]); vf[1] = bf16_hi(r.v[t][0]); vf[2] = bf16_lo(r.v[t][1]); vf[3] = bf16_hi(r.v[t][1]);
+      if constexpr (E >= 4) {
+#pragma unroll
+        for (int w = 0; w < E / 2; ++w) { vf[2 * w] = bf16_lo(r.v[t][w]); vf[2 * w + 1] = bf16_hi(r.v[t][w]); }
       } else {
         vf[0] = bf16_lo(r.v[t][0]); vf[1] = bf16_hi(r.v[t][0]);
       }
@@ -154,7 +161,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
   // pages of this warp: start + warp*16, then every 4*16 tokens; keep the next page in flight
   constexpr int STRIDE = kAttnWarps * kPage;
   int pg = start + warp * kPage;
-  if (pg < stop) {
+  if constexpr (HD > 128) {
+    // a 256-dim page already takes 128 registers per lane: no second page in flight
+    for (; pg < stop; pg += STRIDE) {
+      PageRegs<HD> ra;
+      load_page<HD>(ra, k_cache, v_cache, page_offset(pg), tok, half, lane);
+      consume(ra, pg);
+    }
+  } else if (pg < stop) {
     PageRegs<HD> ra, rb;
     load_page<HD>(ra, k_cache, v_cache, page_offset(pg), tok, half, lane);
     while (true) {
@@ -271,7 +285,11 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tenso
   launch_pdl(paged_decode_kernel<HDV, GV>, grid, dim3(kAttnWarps * 32), 0, stream, qp, kp, vp,                \
              (const int*)block_tables.data_ptr<int>(), (const int*)seq_lens.data_ptr<int>(),                  \
              (int)block_tables.size(1), nkv, sl2, (int)tps, pa, pm, op, (int)nsplit)
-  if (HD == 128 && G == 4) B200_DEC(128, 4);
+  if (HD == 256 && G == 4) B200_DEC(256, 4);
+  else if (HD == 256 && G == 2) B200_DEC(256, 2);
+  else if (HD == 256 && G == 1) B200_DEC(256, 1);
+  else if (HD == 256 && G == 8) B200_DEC(256, 8);
+  else if (HD == 128 && G == 4) B200_DEC(128, 4);
   else if (HD == 128 && G == 8) B200_DEC(128, 8);
   else if (HD == 128 && G == 2) B200_DEC(128, 2);
   else if (HD == 128 && G == 1) B200_DEC(128, 1);
@@ -285,12 +303,10 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tenso
     const int warps = B * nq;
     const int threads = 128;
     const int blocks = (warps * 32 + threads - 1) / threads;
-    if (HD == 128)
-      launch_pdl(paged_decode_combine_kernel<128>, dim3(blocks), dim3(threads), 0, stream, (const float*)pa,
-                 (const float*)pm, (const int*)seq_lens.data_ptr<int>(), op, B, nkv, G, (int)nsplit, (int)tps);
-    else
-      launch_pdl(paged_decode_combine_kernel<64>, dim3(blocks), dim3(threads), 0, stream, (const float*)pa,
-                 (const float*)pm, (const int*)seq_lens.data_ptr<int>(), op, B, nkv, G, (int)nsplit, (int)tps);
+    auto comb = HD == 256 ? paged_decode_combine_kernel<256>
+                : HD == 128 ? paged_decode_combine_kernel<128> : paged_decode_combine_kernel<64>;
+    launch_pdl(comb, dim3(blocks), dim3(threads), 0, stream, (const float*)pa, (const float*)pm,
+               (const int*)seq_lens.data_ptr<int>(), op, B, nkv, G, (int)nsplit, (int)tps);
   }
 }
 

@@ -317,7 +317,8 @@ static void prefill_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v
     B200_PF1(128, 1)
   } else if (HD == 128) B200_PF1(128, 0)
   else if (HD == 64) B200_PF1(64, 0)
-  else TORCH_CHECK(false, "head_dim must be 64 or 128");
+  else if (HD == 256) B200_PF1(256, 0)
+  else TORCH_CHECK(false, "head_dim must be 64, 128 or 256");
 #undef B200_PF1
   B200_CHECK_CUDA(cudaGetLastError());
 }

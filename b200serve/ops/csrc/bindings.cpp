@@ -107,6 +107,11 @@ void paged_prefill_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::T
 int64_t prefill_tc_error(bool reset);
 
 void q4_dequant_pages(torch::Tensor block_ids, torch::Tensor codes, torch::Tensor scales, torch::Tensor out);
+void deltanet_layer(torch::Tensor y, torch::Tensor conv_w, torch::Tensor A, torch::Tensor dt_bias,
+                    torch::Tensor norm_w, torch::Tensor conv_state, torch::Tensor rec_state,
+                    c10::optional<torch::Tensor> cu_q, torch::Tensor q_start, torch::Tensor slots, torch::Tensor xc,
+                    torch::Tensor gb, torch::Tensor out, int64_t nk, int64_t nv, int64_t D, double eps);
+void sigmoid_gate_mul(torch::Tensor attn, torch::Tensor gate);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "b200serve sm_100a kernels";
@@ -131,6 +136,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_prefill_attention", &paged_prefill_attention);
   m.def("paged_prefill_attention_tc", &paged_prefill_attention_tc);
   m.def("q4_dequant_pages", &q4_dequant_pages);
+  m.def("deltanet_layer", &deltanet_layer);
+  m.def("sigmoid_gate_mul", &sigmoid_gate_mul);
   m.def("prefill_tc_error", &prefill_tc_error);
   m.def("paged_decode_attention_tc", &paged_decode_attention_tc);
   m.def("topk_softmax", &topk_softmax);

@@ -146,7 +146,7 @@ __global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __n
                                 const float* __restrict__ cos_sin, const int* __restrict__ positions,
                                 const int* __restrict__ slots, __nv_bfloat16* __restrict__ q_out,
                                 void* __restrict__ k_cache, void* __restrict__ v_cache, __half* __restrict__ k_scale,
-                                __half* __restrict__ v_scale, int T, int nq, int nkv, float eps) {
+                                __half* __restrict__ v_scale, int T, int nq, int nkv, float eps, int width, int rot) {
   constexpr int E = HD / 32;
   pdl_wait();
   pdl_trigger();
@@ -155,7 +155,6 @@ __global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __n
   const int nslots = nq + 2 * nkv;
   if (warp >= T * nslots) return;
   const int t = warp / nslots, h = warp % nslots;
-  const int width = nslots * HD;
   const __nv_bfloat16* src = qkv + (size_t)t * width + h * HD + lane * E;
   float x[E];
 #pragma unroll
@@ -177,16 +176,23 @@ __global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __n
 #pragma unroll
       for (int i = 0; i < E; ++i) x[i] = __bfloat162float(__float2bfloat16_rn(x[i]));
     }
+    // rotate-half RoPE over the first `rot` dims (pairs (d, d + rot/2)); the rest pass through.
+    // The partner of dim d sits rot/2 dims away, i.e. in lane ^ (rot/2/E) (a power of two).
     const int pos = positions[t];
-    const float* cs = cos_sin + (size_t)pos * HD;  // [cos(HD/2) | sin(HD/2)]
+    const int hr = rot >> 1, xo = hr / E;
+    const float* cs = cos_sin + (size_t)pos * rot;  // [cos(rot/2) | sin(rot/2)]
     float y[E];
 #pragma unroll
     for (int i = 0; i < E; ++i) {
-      const float partner = __shfl_xor_sync(0xffffffffu, x[i], 16);
+      const float partner = __shfl_xor_sync(0xffffffffu, x[i], xo);
       const int d = lane * E + i;
-      const int f = d & (HD / 2 - 1);
-      const float c = cs[f], s = cs[HD / 2 + f];
-      y[i] = lane < 16 ? x[i] * c - partner * s : x[i] * c + partner * s;
+      if (d < rot) {
+        const int f = d & (hr - 1);
+        const float c = cs[f], s = cs[hr + f];
+        y[i] = d < hr ? x[i] * c - partner * s : x[i] * c + partner * s;
+      } else {
+        y[i] = x[i];
+      }
     }
 #pragma unroll
     for (int i = 0; i < E; ++i) x[i] = y[i];
@@ -349,25 +355,30 @@ void qkv_post_impl(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::op
                    torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache,
                    __half* k_scale, __half* v_scale, int64_t nq, int64_t nkv, double eps, int kvq) {
   const int T = qkv.size(0);
-  const int HD = cos_sin.size(1);
-  TORCH_CHECK(qkv.size(1) == (nq + 2 * nkv) * HD, "qkv width mismatch");
+  const int HD = q_out.size(2), rot = cos_sin.size(1);
+  const int width = (int)qkv.stride(0);
+  TORCH_CHECK(qkv.stride(1) == 1 && qkv.size(1) >= (nq + 2 * nkv) * HD, "qkv width mismatch");
+  const int hr = rot / 2, E = HD / 32;
+  TORCH_CHECK(rot <= HD && rot % 2 == 0 && hr % E == 0 && ((hr / E) & (hr / E - 1)) == 0,
+              "rotary dims must be <= head_dim with (rot/2)/(head_dim/32) a power of two");
   TORCH_CHECK(positions.scalar_type() == at::kInt && slots.scalar_type() == at::kInt);
   if (T == 0) return;
   const int warps = T * (nq + 2 * nkv);
   const int threads = 256;
   const int blocks = (warps * 32 + threads - 1) / threads;
   auto stream = at::cuda::getCurrentCUDAStream();
-#define B200_QKV(HDV)                                                                                       \
-  launch_pdl(kvq ? qkv_post_kernel<HDV, 1> : qkv_post_kernel<HDV, 0>, dim3(blocks), dim3(threads), 0, stream, \
+#define B200_QKV(KERNEL)                                                                                   \
+  launch_pdl(KERNEL, dim3(blocks), dim3(threads), 0, stream,                                                \
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),                                               \
       bias ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr,                            \
       qn_w ? reinterpret_cast<const __nv_bfloat16*>(qn_w->data_ptr()) : nullptr,                            \
       kn_w ? reinterpret_cast<const __nv_bfloat16*>(kn_w->data_ptr()) : nullptr, cos_sin.data_ptr<float>(), \
       positions.data_ptr<int>(), slots.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), \
-      k_cache.data_ptr(), v_cache.data_ptr(), k_scale, v_scale, T, (int)nq, (int)nkv, (float)eps)
-  if (HD == 128) B200_QKV(128);
-  else if (HD == 64) B200_QKV(64);
-  else TORCH_CHECK(false, "head_dim must be 64 or 128");
+      k_cache.data_ptr(), v_cache.data_ptr(), k_scale, v_scale, T, (int)nq, (int)nkv, (float)eps, width, rot)
+  if (HD == 128) { if (kvq) B200_QKV((qkv_post_kernel<128, 1>)); else B200_QKV((qkv_post_kernel<128, 0>)); }
+  else if (HD == 64 && !kvq) B200_QKV((qkv_post_kernel<64, 0>));
+  else if (HD == 256 && !kvq) B200_QKV((qkv_post_kernel<256, 0>));
+  else TORCH_CHECK(false, "head_dim must be 64, 128 or 256 (int4 KV: 128)");
 #undef B200_QKV
   B200_CHECK_CUDA(cudaGetLastError());
 }

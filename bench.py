@@ -45,7 +45,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=0, help="0 = the config's batch (32 dense, 64 MoE)")
     ap.add_argument("--prompt", type=int, default=0, help="0 = the config's prompt (2048 dense, 512 MoE)")
-    ap.add_argument("--model", default="qwen3-8b", choices=["qwen3-8b", "qwen3-30b-a3b"])
+    ap.add_argument("--model", default="qwen3-8b", choices=["qwen3-8b", "qwen3-30b-a3b", "qwen3.5-9b"])
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
     ap.add_argument("--weights", default="bf16", choices=["bf16", "gguf"],
                     help="gguf: random-init bf16 weights quantised on the GPU into the Q4_K_M mix")
@@ -139,12 +139,13 @@ def run_ours(a):
     ms = _max_over_ranks(res["ms"])
     _finish_dist(eng)
     tps = B * K / (ms / 1e3)
-    pack_bytes = inner.bucket(B) * (4 + inner.max_blocks) * 4
+    from b200serve.engine.runner import PACK
+    pack_bytes = inner.bucket(B) * (PACK + inner.max_blocks) * 4
     emit({
         "metric": METRIC, "value": round(tps, 1), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic token ids (uniform), random-init N(0,0.02) weights of the Qwen3-8B architecture",
+        "data": f"synthetic token ids (uniform), random-init N(0,0.02) weights of the {a.model} architecture",
         "config": {"model": MODEL_DESC[a.model] + (" as GGUF Q4_K_M (Q6_K attn_v/ffn_down, Q8_0 output)"
                                                    if a.weights == "gguf" else ""), "global_batch": B,
                    "seq_len": P, "decode_context": f"{P}..{P + W + K}",
@@ -171,14 +172,15 @@ def _device_loop(runner, inner, eng, B, P, K, W, vocab):
     chunk = max(1, 8192 // P)
     last = []
     for i in range(0, B, chunk):
-        seqs = [{"ids": prompts[j], "start": 0, "block_table": tables[j]} for j in range(i, min(B, i + chunk))]
+        seqs = [{"ids": prompts[j], "start": 0, "block_table": tables[j], "state_slot": j}
+                for j in range(i, min(B, i + chunk))]
         logits = runner.prefill(seqs)
         last += logits.argmax(-1).tolist()
     ids = last
     pos = [P] * B
     slots = [t[P // 16] * 16 + P % 16 for t in tables]
     lens = [P + 1] * B
-    return runner.decode_loop(ids, pos, slots, tables, lens, W, K)
+    return runner.decode_loop(ids, pos, slots, tables, lens, W, K, state_slots=list(range(B)))
 
 
 def _finish_dist(eng):
@@ -212,14 +214,16 @@ def run_reference(a):
     d = mc.to_hf_dict()
     if a.layers:
         d["num_hidden_layers"] = a.layers
-    hcfg = transformers.Qwen3Config(**{k: v for k, v in d.items() if k not in ("model_type", "architectures")})
+    hf_cfg_cls, hf_cls = {"qwen3_5_text": (transformers.Qwen3_5TextConfig, transformers.Qwen3_5ForCausalLM),
+                          "qwen3_moe": (transformers.Qwen3MoeConfig, transformers.Qwen3MoeForCausalLM)}.get(
+        d["model_type"], (transformers.Qwen3Config, transformers.Qwen3ForCausalLM))
+    hcfg = hf_cfg_cls(**{k: v for k, v in d.items() if k not in ("model_type", "architectures")})
     hcfg.eos_token_id = None
     hcfg.bos_token_id = None
     hcfg.pad_token_id = None
     torch.manual_seed(0)
     with torch.device("cuda"):
-        model = transformers.Qwen3ForCausalLM._from_config(hcfg, torch_dtype=torch.bfloat16,
-                                                           attn_implementation="sdpa").eval()
+        model = hf_cls._from_config(hcfg, torch_dtype=torch.bfloat16, attn_implementation="sdpa").eval()
     model.generation_config.eos_token_id = None
     model.generation_config.pad_token_id = None
     tok = _synthetic_hf_tokenizer(mc.vocab_size)
@@ -274,7 +278,7 @@ def run_reference(a):
         "metric": METRIC, "value": round(tps, 1), "unit": "tok/s", "n_gpus": world, "steps": n_dec, "warmup": W,
         "ms_per_step": round(per_tok_ms, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic token ids (uniform), random-init N(0,0.02) weights of the Qwen3-8B architecture",
+        "data": f"synthetic token ids (uniform), random-init N(0,0.02) weights of the {a.model} architecture",
         "config": {"model": "qwen3-8b", "global_batch": a.batch, "seq_len": P,
                    "parallelism": f"{world} independent replicas (reference has no TP; requests serialised)",
                    "l2": "inputs larger than L2 (16.4 GB weights per step)"},
@@ -308,6 +312,8 @@ def _synthetic_hf_tokenizer(vocab):
 MODEL_DESC = {
     "qwen3-8b": "qwen3-8b (36L, H4096, 32q/8kv, hd128, FFN12288, vocab151936)",
     "qwen3-30b-a3b": "qwen3-30b-a3b (48L, H2048, 32q/4kv, hd128, 128 experts top-8, expert FFN768, vocab151936)",
+    "qwen3.5-9b": "qwen3.5-9b (32L = 24 Gated DeltaNet [16k/32v heads x128] + 8 gated attention [16q/4kv, hd256, "
+                  "RoPE 64], H4096, FFN12288, vocab248320)",
 }
 
 

@@ -1,0 +1,181 @@
+"""GPU numerics of the Qwen3.5 hybrid path against fp32 PyTorch restatements: the Gated
+DeltaNet kernels (conv + recurrence + gated norm, prefill with and without history, and
+decode), qkv_post with partial RoPE and gate columns at head_dim 256, head_dim-256 paged
+attention, and a tiny hybrid engine on the GPU against the same model on the CPU."""
+
+import math
+
+import pytest
+import torch
+
+from b200serve import ops
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+@pytest.fixture(autouse=True)
+def _seed():
+    torch.manual_seed(0)
+    ops.ext()
+
+
+def _dn_inputs(T, nk, nv, D, slots_n):
+    conv_dim = (2 * nk + nv) * D
+    W = conv_dim + nv * D + 2 * nv
+    y = (torch.randn(T, W, device=dev) * 0.5).bfloat16()
+    conv_w = (torch.randn(conv_dim, 4, device=dev) * 0.4).float()
+    A = -torch.rand(nv, device=dev) * 4 - 0.1
+    dt = torch.randn(nv, device=dev) * 0.5
+    nw = (1 + 0.1 * torch.randn(D, device=dev)).bfloat16()
+    cs = torch.randn(slots_n, conv_dim, 3, device=dev)
+    rs = torch.randn(slots_n, nv, D, D, device=dev) * 0.1
+    return y, conv_w, A, dt, nw, cs, rs
+
+
+@pytest.mark.parametrize("nk,nv,D", [(16, 32, 128), (2, 4, 32), (4, 4, 64)])
+def test_deltanet_prefill_and_decode_match_fp32(nk, nv, D):
+    # prefill: three sequences, the second continues from a stored state (start > 0)
+    lens, starts, slots = [37, 5, 130], [0, 64, 0], [2, 0, 5]
+    T = sum(lens)
+    y, conv_w, A, dt, nw, cs, rs = _dn_inputs(T, nk, nv, D, 6)
+    cu = torch.tensor([0, 37, 42, T], dtype=torch.int32, device=dev)
+    qs = torch.tensor(starts, dtype=torch.int32, device=dev)
+    sl = torch.tensor(slots, dtype=torch.int32, device=dev)
+    cs_ref, rs_ref = cs.cpu().clone(), rs.cpu().clone()
+    out = ops.deltanet_layer(y, conv_w, A, dt, nw, cs, rs, cu, qs, sl, nk, nv, D, 1e-6)
+    ref = ops._deltanet_cpu(y.cpu().float(), conv_w.cpu(), A.cpu(), dt.cpu(), nw.cpu().float(), cs_ref, rs_ref,
+                            cu.cpu(), qs.cpu(), sl.cpu(), nk, nv, D, 1e-6)
+    torch.cuda.synchronize()
+    assert _rel(out.cpu(), ref) < 2e-2
+    for s in slots:
+        assert _rel(rs[s].cpu(), rs_ref[s]) < 2e-2
+        assert _rel(cs[s].cpu(), cs_ref[s]) < 1e-2
+    # decode: one token for each of the three sequences, continuing their states
+    y2 = (torch.randn(3, y.shape[1], device=dev) * 0.5).bfloat16()
+    pos = torch.tensor([37, 69, 130], dtype=torch.int32, device=dev)
+    out2 = ops.deltanet_layer(y2, conv_w, A, dt, nw, cs, rs, None, pos, sl, nk, nv, D, 1e-6)
+    ref2 = ops._deltanet_cpu(y2.cpu().float(), conv_w.cpu(), A.cpu(), dt.cpu(), nw.cpu().float(), cs_ref, rs_ref,
+                             None, pos.cpu(), sl.cpu(), nk, nv, D, 1e-6)
+    assert _rel(out2.cpu(), ref2) < 2e-2
+    for s in slots:
+        assert _rel(rs[s].cpu(), rs_ref[s]) < 2e-2
+
+
+def test_qkv_post_partial_rotary_with_gate_columns():
+    hd, nq, nkv, T, nb = 256, 16, 4, 19, 8
+    width = (nq + 2 * nkv) * hd + nq * hd          # q | k | v | gate
+    qkv = torch.randn(T, width, device=dev).bfloat16()
+    qn = (1 + 0.1 * torch.randn(hd, device=dev)).bfloat16()
+    kn = (1 + 0.1 * torch.randn(hd, device=dev)).bfloat16()
+    cs = ops.rope_cos_sin(hd, 4096, 1e7, dev, rot_dim=64)
+    pos = torch.randint(0, 4000, (T,), device=dev, dtype=torch.int32)
+    slots = torch.randperm(nb * 16, device=dev)[:T].int()
+    kc = torch.zeros(nb, nkv, 16, hd, device=dev).bfloat16()
+    vc = torch.zeros_like(kc)
+    kc2, vc2 = kc.cpu().float(), vc.cpu().float()
+    q = ops.qkv_post(qkv, None, qn, kn, cs, pos, slots, kc, vc, nq, nkv, 1e-6, hd=hd)
+    qr = ops.qkv_post(qkv.cpu().float(), None, qn.cpu().float(), kn.cpu().float(), cs.cpu(), pos.cpu(),
+                      slots.cpu(), kc2, vc2, nq, nkv, 1e-6, hd=hd)
+    assert _rel(q.cpu(), qr) < 1e-2
+    assert _rel(kc.cpu(), kc2) < 1e-2 and _rel(vc.cpu(), vc2) < 1e-2
+    a = torch.randn(T, nq * hd, device=dev).bfloat16()
+    ref = a.cpu().float() * torch.sigmoid(qkv[:, (nq + 2 * nkv) * hd:].cpu().float())
+    ops.sigmoid_gate_mul(a, qkv[:, (nq + 2 * nkv) * hd:])
+    assert _rel(a.cpu(), ref) < 1e-2
+
+
+def _make_paged(B, lens, nkv, hd, nb_total):
+    kc = torch.randn(nb_total, nkv, 16, hd, device=dev).bfloat16()
+    vc = torch.randn(nb_total, nkv, 16, hd, device=dev).bfloat16()
+    maxb = max((l + 15) // 16 for l in lens)
+    perm = torch.randperm(nb_total, device=dev)
+    bt = torch.zeros(B, maxb, dtype=torch.int32, device=dev)
+    used = 0
+    for b, l in enumerate(lens):
+        n = (l + 15) // 16
+        bt[b, :n] = perm[used:used + n].int()
+        used += n
+    return kc, vc, bt
+
+
+@pytest.mark.parametrize("nq,nkv", [(16, 4), (8, 8)])
+def test_attention_head_dim_256(nq, nkv):
+    hd = 256
+    lens = [1, 40, 700]
+    B = len(lens)
+    kc, vc, bt = _make_paged(B, lens, nkv, hd, 256)
+    q = torch.randn(B, nq, hd, device=dev).bfloat16()
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    scale = 1 / math.sqrt(hd)
+    ws = ops.AttnWorkspace(dev, B, nkv, nq // nkv, hd, 4)
+    y = ops.paged_decode_attention(q, kc, vc, bt, sl, scale, 256, 3, ws)
+    ref = ops.paged_decode_attention(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), sl.cpu(), scale)
+    assert _rel(y.cpu(), ref) < 1e-2
+    chunks = [(0, 100), (37, 50), (0, 300)]
+    plens = [s + n for s, n in chunks]
+    kc, vc, bt = _make_paged(3, plens, nkv, hd, 256)
+    T = sum(n for _, n in chunks)
+    qp = torch.randn(T, nq, hd, device=dev).bfloat16()
+    cu = torch.tensor([0, 100, 150, 450], dtype=torch.int32, device=dev)
+    q_start = torch.tensor([0, 37, 0], dtype=torch.int32, device=dev)
+    psl = torch.tensor(plens, dtype=torch.int32, device=dev)
+    yp = ops.paged_prefill_attention(qp, kc, vc, bt, psl, q_start, cu, scale, max_q=300)
+    refp = ops.paged_prefill_attention(qp.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), psl.cpu(), q_start.cpu(), cu.cpu(),
+                                       scale)
+    assert _rel(yp.cpu(), refp) < 1e-2
+
+
+def _hybrid_cfg(**kw):
+    from b200serve.models.config import ModelConfig
+    d = dict(name="tiny-hybrid", vocab_size=2048, hidden_size=512, num_layers=4, num_heads=4, num_kv_heads=2,
+             head_dim=256, intermediate_size=1024, rope_theta=1e7, qk_norm=True, rotary_dim=64,
+             layer_types=("linear_attention",) * 3 + ("full_attention",), attn_output_gate=True,
+             norm_offset=True, lin_k_heads=2, lin_v_heads=4, lin_k_dim=128, lin_v_dim=128, conv_kernel=4,
+             max_position=4096)
+    d.update(kw)
+    return ModelConfig(**d)
+
+
+def test_hybrid_engine_gpu_matches_cpu():
+    """A tiny Qwen3.5-shaped hybrid (head_dim 256, DeltaNet heads of 128) on the GPU (bf16,
+    CUDA-graph decode) against the CPU fp32 path: prefill two prompts into two state slots,
+    then decode their last two tokens together; every logits row must stay close."""
+    from b200serve.core.config import EngineConfig
+    from b200serve.engine.b200_engine import B200Engine
+    from b200serve.models.weights import random_weights
+    cfg = _hybrid_cfg()
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(3, 2048, (n,), generator=g).tolist() for n in (50, 200)]
+    outs = {}
+    for device, dtype in (("cpu", torch.float32), ("cuda", torch.bfloat16)):
+        w = random_weights(cfg, seed=1, std=0.05, dtype=dtype, device=device)
+        ec = EngineConfig(model="tiny-hybrid", device=device, dtype="float32" if device == "cpu" else "bfloat16",
+                          cuda_graphs=device == "cuda", max_seq=512, max_batch=4, kv_blocks=128)
+        eng = B200Engine(ec, weights=w, model_config=cfg)
+        eng.load()
+        try:
+            r = eng.runner
+            res, tables = [], []
+            for i, p in enumerate(prompts):
+                bt = eng.scheduler.alloc.allocate((len(p) + 15) // 16 + 1)
+                tables.append(bt)
+                lg = r.prefill([{"ids": p[:-2], "start": 0, "block_table": bt, "state_slot": i}])
+                res.append(lg[0].float().cpu())
+            for step in (2, 1):
+                pos = [len(p) - step for p in prompts]
+                ids = [p[-step] for p in prompts]
+                slots = [bt[q // 16] * 16 + q % 16 for bt, q in zip(tables, pos)]
+                lg, _ = r.decode(ids, pos, slots, tables, [q + 1 for q in pos], greedy=False, state_slots=[0, 1])
+                res += [row.float().cpu() for row in lg]
+            outs[device] = res
+        finally:
+            eng.unload()
+    assert len(outs["cuda"]) == 6
+    for a, b in zip(outs["cuda"], outs["cpu"]):
+        assert _rel(a, b) < 3e-2

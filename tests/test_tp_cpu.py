@@ -23,7 +23,7 @@ def _prompts():
     return [torch.randint(0, 32000, (n,), generator=g).tolist() for n in (37, 64, 5)]
 
 
-def _worker(rank, world, port, out_q, greedy, mode="auto"):
+def _worker(rank, world, port, out_q, greedy, mode="auto", model="tiny-qwen2"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), B200_TP_MODE=mode)
     torch.set_num_threads(1)
@@ -31,7 +31,7 @@ def _worker(rank, world, port, out_q, greedy, mode="auto"):
     from b200serve.engine.b200_engine import B200Engine
     from b200serve.engine.sampler import SamplingParams
     from b200serve.parallel.worker import worker_loop
-    cfg = EngineConfig(model="tiny-qwen2", device="cpu", dtype="float32", cuda_graphs=False, max_seq=256,
+    cfg = EngineConfig(model=model, device="cpu", dtype="float32", cuda_graphs=False, max_seq=256,
                        max_batch=4, tp_size=world, comm="nccl")
     eng = B200Engine(cfg)
     eng.load()
@@ -46,11 +46,11 @@ def _worker(rank, world, port, out_q, greedy, mode="auto"):
     torch.distributed.destroy_process_group()
 
 
-def _run_tp(world, greedy, mode="auto"):
+def _run_tp(world, greedy, mode="auto", model="tiny-qwen2"):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, greedy, mode)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, greedy, mode, model)) for r in range(world)]
     for p in procs:
         p.start()
     out = q.get(timeout=600)
@@ -60,11 +60,11 @@ def _run_tp(world, greedy, mode="auto"):
     return out
 
 
-def _single(greedy):
+def _single(greedy, model="tiny-qwen2"):
     from b200serve.core.config import EngineConfig
     from b200serve.engine.b200_engine import B200Engine
     from b200serve.engine.sampler import SamplingParams
-    eng = B200Engine(EngineConfig(model="tiny-qwen2", device="cpu", dtype="float32", cuda_graphs=False,
+    eng = B200Engine(EngineConfig(model=model, device="cpu", dtype="float32", cuda_graphs=False,
                                   max_seq=256, max_batch=4))
     try:
         sp = SamplingParams(temperature=0.0 if greedy else 0.9, top_p=0.9, seed=3, max_tokens=10, ignore_eos=True)
@@ -86,3 +86,9 @@ def test_tp_sampled_matches_single_rank():
 def test_tp_reduce_scatter_all_gather_matches_single_rank(world):
     """Token-sharded residual stream (reduce-scatter, norm on owned rows, all-gather)."""
     assert _run_tp(world, True, mode="rsag") == _single(True)
+
+
+def test_tp_hybrid_matches_single_rank():
+    """Qwen3.5-style hybrid at TP2: DeltaNet key/value heads and the recurrent state are split
+    across ranks, and the gated attention layer shards its q, gate and KV heads."""
+    assert _run_tp(2, True, model="tiny-qwen35") == _single(True, model="tiny-qwen35")
