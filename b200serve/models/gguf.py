@@ -32,6 +32,20 @@ TYPE_SIZE = {GGML_F32: 4, GGML_F16: 2, GGML_BF16: 2, GGML_Q8_0: 34, GGML_Q4_K: 1
              GGML_Q6_K: 210}
 TYPE_NAME = {GGML_F32: "F32", GGML_F16: "F16", GGML_BF16: "BF16", GGML_Q8_0: "Q8_0", GGML_Q4_K: "Q4_K",
              GGML_Q5_K: "Q5_K", GGML_Q6_K: "Q6_K"}
+# types read through models/gguf_types.py (dequantised to bf16 at load)
+GGML_Q4_0, GGML_Q4_1, GGML_Q5_0, GGML_Q5_1, GGML_Q2_K, GGML_Q3_K = 2, 3, 6, 7, 10, 11
+for _t, _name, _bs, _ts in ((GGML_Q4_0, "Q4_0", 32, 18), (GGML_Q4_1, "Q4_1", 32, 20), (GGML_Q5_0, "Q5_0", 32, 22),
+                            (GGML_Q5_1, "Q5_1", 32, 24), (GGML_Q2_K, "Q2_K", 256, 84),
+                            (GGML_Q3_K, "Q3_K", 256, 110)):
+    BLOCK_SIZE[_t], TYPE_SIZE[_t], TYPE_NAME[_t] = _bs, _ts, _name
+try:  # IQ* codebook types: sizes from the gguf package, decoded by it
+    import gguf as _gguf
+    for _name in ("IQ2_XXS", "IQ2_XS", "IQ3_XXS", "IQ1_S", "IQ4_NL", "IQ3_S", "IQ2_S", "IQ4_XS", "IQ1_M"):
+        _t = int(getattr(_gguf.GGMLQuantizationType, _name))
+        BLOCK_SIZE[_t], TYPE_SIZE[_t] = _gguf.GGML_QUANT_SIZES[getattr(_gguf.GGMLQuantizationType, _name)]
+        TYPE_NAME[_t] = _name
+except ImportError:  # pragma: no cover
+    pass
 
 # metadata value types
 _U8, _I8, _U16, _I16, _U32, _I32, _F32, _BOOL, _STR, _ARR, _U64, _I64, _F64 = range(13)
@@ -330,7 +344,16 @@ def dequantize(raw: np.ndarray, ggml_type: int, shape) -> np.ndarray:
     elif ggml_type == GGML_Q6_K:
         out = dequantize_q6_k(raw)
     else:
-        raise NotImplementedError(f"ggml type {ggml_type}")
+        from b200serve.models import gguf_types as gt
+        native = {GGML_Q4_0: gt.dequantize_q4_0, GGML_Q4_1: gt.dequantize_q4_1, GGML_Q5_0: gt.dequantize_q5_0,
+                  GGML_Q5_1: gt.dequantize_q5_1, GGML_Q2_K: gt.dequantize_q2_k, GGML_Q3_K: gt.dequantize_q3_k,
+                  GGML_Q5_K: gt.dequantize_q5_k}
+        if ggml_type in native:
+            out = native[ggml_type](raw)
+        elif TYPE_NAME.get(ggml_type, "").startswith("IQ"):
+            out = gt.dequantize_codebook(raw, TYPE_NAME[ggml_type])
+        else:
+            raise NotImplementedError(f"ggml type {ggml_type}")
     return out.reshape(shape)
 
 
@@ -348,7 +371,7 @@ def q4_k_m_type(key: str) -> int:
 def export_gguf(path: str, cfg, weights_full: dict, layer_full, mix: str = "Q4_K_M"):
     """Write a GGUF of a dense model. ``weights_full``: embed, lm_head, final_norm (numpy);
     ``layer_full(i)``: unsharded layer dict of numpy arrays (HF orientation [out, in])."""
-    arch = "qwen3" if cfg.qk_norm else "qwen2"
+    arch = "llama" if cfg.family in ("llama", "mistral") else "qwen3" if cfg.qk_norm else "qwen2"
     md = {"general.architecture": arch, "general.name": cfg.name, "general.file_type": 15,
           f"{arch}.block_count": cfg.num_layers, f"{arch}.context_length": cfg.max_position,
           f"{arch}.embedding_length": cfg.hidden_size, f"{arch}.feed_forward_length": cfg.intermediate_size,
@@ -364,6 +387,9 @@ def export_gguf(path: str, cfg, weights_full: dict, layer_full, mix: str = "Q4_K
                     quantize(weights_full["final_norm"], GGML_F32)))
     for i in range(cfg.num_layers):
         d = layer_full(i)
+        if arch == "llama":   # llama.cpp's llama graph rotates interleaved pairs: store q/k permuted
+            d = dict(d, q=d["q"][llama_qk_rows(cfg.num_heads, cfg.head_dim, to_gguf=True)],
+                     k=d["k"][llama_qk_rows(cfg.num_kv_heads, cfg.head_dim, to_gguf=True)])
         for key, arr in d.items():
             if key not in _LAYER_MAP:
                 continue
@@ -385,6 +411,9 @@ def config_from_gguf(path: str):
     emb = g.tensors["token_embd.weight"].shape
     heads = int(a("attention.head_count"))
     hd = int(a("attention.key_length", 0)) or int(a("embedding_length")) // heads
+    scaling = None
+    if "rope_freqs.weight" in g.tensors:   # Llama 3.1-style per-frequency divisors
+        scaling = {"rope_type": "freq_factors", "factors": [float(x) for x in g.dequantize("rope_freqs.weight")]}
     return ModelConfig(name=str(m.get("general.name", "gguf")), vocab_size=emb[0], hidden_size=int(a("embedding_length")),
                        num_layers=int(a("block_count")), num_heads=heads,
                        num_kv_heads=int(a("attention.head_count_kv", heads)), head_dim=hd,
@@ -392,7 +421,24 @@ def config_from_gguf(path: str):
                        rms_eps=float(a("attention.layer_norm_rms_epsilon", 1e-6)),
                        rope_theta=float(a("rope.freq_base", 1e6)), attn_bias=arch == "qwen2",
                        qk_norm=arch in ("qwen3", "qwen3moe"), tie_embeddings="output.weight" not in g.tensors,
-                       max_position=int(a("context_length", 40960)))
+                       max_position=int(a("context_length", 40960)), rope_scaling=scaling,
+                       family="llama" if arch == "llama" else arch)
+
+
+def llama_qk_rows(n_heads: int, hd: int, to_gguf: bool = False) -> np.ndarray:
+    """Row order between HF's rotate-half q/k projections and llama.cpp's ``llama`` GGUF
+    tensors, whose rows are permuted per head so that RoPE pairs are adjacent: GGUF row
+    (h, i, j) [hd/2 x 2] holds HF row (h, j, i) [2 x hd/2]. Returns idx with
+    hf = gguf[idx] (or gguf = hf[idx] with ``to_gguf``)."""
+    h, i, j = np.meshgrid(np.arange(n_heads), np.arange(hd // 2), np.arange(2), indexing="ij")
+    gguf_rows = (h * hd + i * 2 + j).reshape(-1)
+    hf_rows = (h * hd + j * (hd // 2) + i).reshape(-1)
+    idx = np.empty(n_heads * hd, dtype=np.int64)
+    if to_gguf:
+        idx[gguf_rows] = hf_rows
+    else:
+        idx[hf_rows] = gguf_rows
+    return idx
 
 
 def load_gguf_weights(cfg, path: str, **kw):
@@ -406,6 +452,8 @@ def load_gguf_weights(cfg, path: str, **kw):
     def T(name):
         return torch.from_numpy(np.array(g.dequantize(name), dtype=np.float32))
 
+    llama = g.metadata.get("general.architecture") == "llama"
+
     def layer(i):
         d = {}
         pre = f"blk.{i}."
@@ -415,6 +463,9 @@ def load_gguf_weights(cfg, path: str, **kw):
                 base = rest[:-len(".weight")] if rest.endswith(".weight") else rest
                 if base in inv:
                     d[inv[base]] = T(name)
+        if llama:
+            d["q"] = d["q"][torch.from_numpy(llama_qk_rows(cfg.num_heads, cfg.head_dim))]
+            d["k"] = d["k"][torch.from_numpy(llama_qk_rows(cfg.num_kv_heads, cfg.head_dim))]
         return d
 
     embed = T("token_embd.weight")
@@ -597,22 +648,36 @@ def load_gguf_quantized(cfg, path: str, tp_rank=0, tp_size=1, dtype=None, device
     def deq(name):
         return torch.from_numpy(np.array(g.dequantize(name), dtype=np.float32)).to(device=device, dtype=dtype)
 
-    def qw(name, rows=None, cols=None):
+    llama = g.metadata.get("general.architecture") == "llama"
+
+    def qw(name, rows=None, cols=None, perm=None):
+        """``perm``: row order applied to the whole tensor before the rank's rows are taken."""
         t = g.tensors[name]
         N, K = t.shape
         r0, r1 = rows or (0, N)
         c0, c1 = cols or (0, K)
         if t.ggml_type in QUANT_TYPES and (r1 - r0) % 16 == 0 and (c1 - c0) % 256 == 0:
-            return _repack(_raw_block_slice(g, name, rows, cols), t.ggml_type, r1 - r0, c1 - c0, device)
-        w = deq(name)[r0:r1, c0:c1].contiguous()
+            if perm is None:
+                raw = _raw_block_slice(g, name, rows, cols)
+            else:
+                full = np.asarray(g.raw(name)).reshape(N, -1)[perm]
+                bs, ts = BLOCK_SIZE[t.ggml_type], TYPE_SIZE[t.ggml_type]
+                raw = np.ascontiguousarray(full[r0:r1, c0 // bs * ts:c1 // bs * ts]).reshape(-1)
+            return _repack(raw, t.ggml_type, r1 - r0, c1 - c0, device)
+        full = deq(name)
+        if perm is not None:
+            full = full[torch.from_numpy(perm).to(full.device)]
+        w = full[r0:r1, c0:c1].contiguous()
         from b200serve import ops
         return ops.pack_weight(w)
 
     layers = []
     for i in range(cfg.num_layers):
         p = f"blk.{i}."
-        q = qw(p + "attn_q.weight", rows=(tp_rank * nq * hd, (tp_rank + 1) * nq * hd))
-        k = qw(p + "attn_k.weight", rows=(tp_rank * nkv * hd, (tp_rank + 1) * nkv * hd))
+        pq = llama_qk_rows(cfg.num_heads, hd) if llama else None
+        pk = llama_qk_rows(cfg.num_kv_heads, hd) if llama else None
+        q = qw(p + "attn_q.weight", rows=(tp_rank * nq * hd, (tp_rank + 1) * nq * hd), perm=pq)
+        k = qw(p + "attn_k.weight", rows=(tp_rank * nkv * hd, (tp_rank + 1) * nkv * hd), perm=pk)
         v = qw(p + "attn_v.weight", rows=(tp_rank * nkv * hd, (tp_rank + 1) * nkv * hd))
         o = qw(p + "attn_output.weight", cols=(tp_rank * nq * hd, (tp_rank + 1) * nq * hd))
         gate = qw(p + "ffn_gate.weight", rows=(tp_rank * Ir, (tp_rank + 1) * Ir))

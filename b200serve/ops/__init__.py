@@ -124,12 +124,15 @@ def rope_inv_freq(rot_dim: int, theta: float, scaling: dict = None) -> torch.Ten
       * ``llama3``: the Llama 3.1 piecewise rule; wavelengths shorter than
         original_max / high_freq_factor are kept, longer than original_max / low_freq_factor
         divided by ``factor``, and the band between interpolates linearly in
-        original_max / wavelength.
+        original_max / wavelength;
+      * ``freq_factors``: explicit per-frequency divisors (a GGUF ``rope_freqs`` tensor).
     Any other type raises."""
     inv = 1.0 / (theta ** (torch.arange(0, rot_dim, 2, dtype=torch.int64).float() / rot_dim))
     kind = (scaling or {}).get("rope_type") or (scaling or {}).get("type") or "default"
     if kind == "default":
         return inv
+    if kind == "freq_factors":   # per-frequency divisors stored with the checkpoint (GGUF rope_freqs)
+        return inv / torch.tensor(scaling["factors"], dtype=torch.float32)[: inv.numel()]
     factor = float(scaling["factor"])
     if kind == "linear":
         return inv / factor

@@ -69,3 +69,48 @@ def test_gguf_model_roundtrip(tmp_path):
     w2 = load_gguf_weights(c2, path, dtype=torch.float32)
     rel = (w2.layers[0].qkv - w.layers[0].qkv).norm() / w.layers[0].qkv.norm()
     assert rel < 0.15
+
+
+def test_llama_gguf_loads_with_hf_rope_order(tmp_path):
+    """A Llama checkpoint written as a ``llama`` GGUF (q/k rows permuted per head the way
+    llama.cpp stores them, F32 so the export is exact) loads back into the rotate-half
+    layout: the engine's prefill logits match HF transformers."""
+    import json
+    transformers = pytest.importorskip("transformers")
+    from b200serve.core.config import EngineConfig
+    from b200serve.engine.b200_engine import B200Engine
+    from b200serve.models.config import from_hf_config, get_model_config
+    from b200serve.models.gguf import export_gguf, load_gguf_weights, read_gguf_file
+    hc = transformers.LlamaConfig(vocab_size=512, hidden_size=128, num_hidden_layers=2, num_attention_heads=4,
+                                  num_key_value_heads=2, intermediate_size=256, rope_theta=10000.0,
+                                  max_position_embeddings=256, tie_word_embeddings=False)
+    torch.manual_seed(0)
+    model = transformers.LlamaForCausalLM(hc).eval()
+    cfg = from_hf_config(dict(json.loads(hc.to_json_string()), model_type="llama"), "tiny-llama")
+    sd = {k: v.detach().numpy() for k, v in model.state_dict().items()}
+    names = {"q": "self_attn.q_proj.weight", "k": "self_attn.k_proj.weight", "v": "self_attn.v_proj.weight",
+             "o": "self_attn.o_proj.weight", "gate": "mlp.gate_proj.weight", "up": "mlp.up_proj.weight",
+             "down": "mlp.down_proj.weight", "input_norm": "input_layernorm.weight",
+             "post_norm": "post_attention_layernorm.weight"}
+    path = str(tmp_path / "tiny-llama.gguf")
+    export_gguf(path, cfg, {"embed": sd["model.embed_tokens.weight"], "lm_head": sd["lm_head.weight"],
+                            "final_norm": sd["model.norm.weight"]},
+                lambda i: {k: sd[f"model.layers.{i}.{v}"] for k, v in names.items()}, mix="F32")
+    g = read_gguf_file(path)
+    assert g.metadata["general.architecture"] == "llama"
+    assert not np.allclose(g.dequantize("blk.0.attn_q.weight"), sd["model.layers.0.self_attn.q_proj.weight"])
+    c2 = get_model_config(path)
+    assert c2.family == "llama" and not c2.attn_bias
+    w2 = load_gguf_weights(c2, path, dtype=torch.float32)
+    ids = torch.randint(3, 512, (40,), generator=torch.Generator().manual_seed(2)).tolist()
+    eng = B200Engine(EngineConfig(model="tiny-llama", device="cpu", dtype="float32", cuda_graphs=False,
+                                  max_seq=128, max_batch=2), weights=w2, model_config=c2)
+    eng.load()
+    try:
+        bt = eng.scheduler.alloc.allocate(4)
+        logits = eng.runner.prefill([{"ids": ids, "start": 0, "block_table": bt}])
+        with torch.no_grad():
+            ref = model(torch.tensor([ids])).logits[0, -1]
+        assert torch.allclose(logits[0], ref, atol=1e-4, rtol=1e-4)
+    finally:
+        eng.unload()
