@@ -64,21 +64,28 @@ def quantize_s8_gpu(w: torch.Tensor, group: int, qmax: int):
     return q.view(N, K).int(), s
 
 
+def pack_q4(q: torch.Tensor, s: torch.Tensor, m: torch.Tensor) -> "ops.QuantWeight":
+    """4-bit codes q [N, K] (0..15) with w = s * q - m per 32 values (s, m [N, K/32]) in the
+    fragment order of the 4-bit GEMM (bf16 scale and -min per 32)."""
+    N, K = q.shape
+    v = _lane_values(q)
+    word = torch.zeros(v.shape[:3], dtype=torch.int64, device=q.device)
+    for i in range(4):
+        word |= (v[..., i, 0].long() << (4 * i)) | (v[..., i, 1].long() << (16 + 4 * i))
+    codes = word & 0xFFFFFFFF
+    codes = torch.where(codes >= 2 ** 31, codes - 2 ** 32, codes).to(torch.int32).reshape(-1)
+    sb = _bf16_pair_bits(s).view(N // 16, 16, K // 32).permute(0, 2, 1)
+    mb = _bf16_pair_bits(-m).view(N // 16, 16, K // 32).permute(0, 2, 1)
+    meta = torch.stack([sb, mb], -1).contiguous().reshape(-1)
+    return ops.QuantWeight(codes, meta, N, K, 4, 32)
+
+
 def to_quant_weight(w: torch.Tensor, kind: str) -> "ops.QuantWeight":
     """Quantise a [N, K] CUDA weight into kind in ('q4_k', 'q6_k', 'q8_0') and repack for the kernel."""
     N, K = w.shape
     if kind == "q4_k":
         q, s, m = quantize_q4k_gpu(w)
-        v = _lane_values(q)
-        word = torch.zeros(v.shape[:3], dtype=torch.int64, device=w.device)
-        for i in range(4):
-            word |= (v[..., i, 0].long() << (4 * i)) | (v[..., i, 1].long() << (16 + 4 * i))
-        codes = word & 0xFFFFFFFF
-        codes = torch.where(codes >= 2 ** 31, codes - 2 ** 32, codes).to(torch.int32).reshape(-1)
-        sb = _bf16_pair_bits(s).view(N // 16, 16, K // 32).permute(0, 2, 1)
-        mb = _bf16_pair_bits(-m).view(N // 16, 16, K // 32).permute(0, 2, 1)
-        meta = torch.stack([sb, mb], -1).contiguous().reshape(-1)
-        return ops.QuantWeight(codes, meta, N, K, 4, 32)
+        return pack_q4(q, s, m)
     group, qmax = (16, 31) if kind == "q6_k" else (32, 127)
     q, s = quantize_s8_gpu(w, group, qmax)
     v = _lane_values(q & 0xFF).long()

@@ -308,12 +308,26 @@ def load_safetensors_dir(cfg: ModelConfig, path: str, **kw) -> ModelWeights:
         return h.get_tensor(name) if h is not None else None
 
     get = _with_lm_prefix(get_raw)
+    qcfg = {}
+    cfg_path = os.path.join(path, "config.json")
+    if os.path.exists(cfg_path):
+        import json
+        with open(cfg_path) as fh:
+            qcfg = json.load(fh).get("quantization_config") or {}
+    gptq = qcfg.get("quant_method") == "gptq"
+    if gptq:   # projections stored as qweight/qzeros/scales: dequantised on load
+        from b200serve.models import gptq as GP
+        get = GP.getter(get, qcfg)
 
     embed = get("model.embed_tokens.weight")
     lm = get("lm_head.weight")
     if lm is None:
         lm = embed
-    return build_weights(cfg, lambda i: hf_layer_dict(get, cfg, i), embed, lm, get("model.norm.weight"), **kw)
+    w = build_weights(cfg, lambda i: hf_layer_dict(get, cfg, i), embed, lm, get("model.norm.weight"), **kw)
+    if gptq and torch.device(kw.get("device", "cpu")).type == "cuda" and os.environ.get("B200_GPTQ_KERNEL", "1") != "0":
+        # 4-bit layers stay 4-bit on the GPU (the same GEMM as GGUF Q4_K)
+        GP.quantize_layers(cfg, w, _with_lm_prefix(get_raw), qcfg, device=kw["device"])
+    return w
 
 
 def to_hf_state_dict(cfg: ModelConfig, w: ModelWeights) -> dict:
