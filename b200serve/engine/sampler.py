@@ -32,10 +32,24 @@ class SamplingParams:
     max_tokens: int = 256
     stop: tuple = ()
     ignore_eos: bool = False
+    dry_multiplier: float = 0.0      # DRY repetition penalty (0 = off)
+    dry_base: float = 1.75
+    dry_allowed_length: int = 2
+    dry_penalty_last_n: int = -1     # -1 = whole sequence, 0 = off
 
     @property
     def greedy(self) -> bool:
         return not self.temperature or self.temperature <= 0
+
+    @property
+    def dry(self) -> bool:
+        return self.dry_multiplier > 0 and self.dry_penalty_last_n != 0
+
+    @property
+    def plain(self) -> bool:
+        """No history-dependent logit adjustment (penalties, DRY)."""
+        return (self.repeat_penalty == 1.0 and not self.presence_penalty and not self.frequency_penalty
+                and not self.dry)
 
     @classmethod
     def from_dict(cls, d: dict, temperature=None, max_tokens=None) -> "SamplingParams":
@@ -46,13 +60,55 @@ class SamplingParams:
                  repeat_penalty=float(d.get("repeat_penalty", 1.0)),
                  presence_penalty=float(d.get("presence_penalty", 0.0)),
                  frequency_penalty=float(d.get("frequency_penalty", 0.0)),
-                 repeat_last_n=int(d.get("repeat_last_n", 64)), seed=d.get("seed"))
+                 repeat_last_n=int(d.get("repeat_last_n", 64)), seed=d.get("seed"),
+                 dry_multiplier=float(d.get("dry_multiplier", 0.0) or 0.0), dry_base=float(d.get("dry_base", 1.75)),
+                 dry_allowed_length=int(d.get("dry_allowed_length", 2)),
+                 dry_penalty_last_n=int(d.get("dry_penalty_last_n", -1)))
         if max_tokens:
             sp.max_tokens = int(max_tokens)
         stop = d.get("stop")
         if stop:
             sp.stop = tuple([stop] if isinstance(stop, str) else stop)
         return sp
+
+
+DRY_MAX_MATCH = 64
+
+
+def dry_penalties(history: list, p: "SamplingParams") -> dict:
+    """DRY ("don't repeat yourself"): a token t that would continue a sequence already seen
+    earlier in the context, where the repeated part (the context's current suffix that also
+    preceded an earlier t) is at least ``dry_allowed_length`` tokens long, loses
+    multiplier * base ** (length - allowed_length) from its logit. Returns {token: penalty}.
+    Reference behaviour: the CPU sampler's DRY step (webgpu/src/engine/generate.ts:234).
+    Match lengths are capped at DRY_MAX_MATCH tokens; text sequence breakers are not used."""
+    ctx = history[-p.dry_penalty_last_n:] if p.dry_penalty_last_n > 0 else history
+    n = len(ctx)
+    best = {}
+    for j in range(n - 2, -1, -1):            # ctx[j + 1] followed an occurrence ending at j
+        L = 0
+        while L <= j and L < DRY_MAX_MATCH and ctx[j - L] == ctx[n - 1 - L]:
+            L += 1
+        if L:
+            t = ctx[j + 1]
+            if L > best.get(t, 0):
+                best[t] = L
+    return {t: p.dry_multiplier * p.dry_base ** (L - p.dry_allowed_length)
+            for t, L in best.items() if L >= p.dry_allowed_length}
+
+
+def apply_dry(logits: torch.Tensor, history: list, params: list) -> torch.Tensor:
+    """Subtract the DRY penalties in place (one scatter per row that has any)."""
+    for i, (p, hist) in enumerate(zip(params, history)):
+        if not p.dry or not hist:
+            continue
+        pen = dry_penalties(hist, p)
+        pen = {t: v for t, v in pen.items() if 0 <= t < logits.shape[1]}
+        if pen:
+            ids = torch.tensor(list(pen.keys()), dtype=torch.long, device=logits.device)
+            vals = torch.tensor(list(pen.values()), dtype=logits.dtype, device=logits.device)
+            logits[i].index_add_(0, ids, -vals)
+    return logits
 
 
 def apply_penalties(logits: torch.Tensor, history: list, params: list) -> torch.Tensor:
@@ -113,6 +169,8 @@ def sample_cuda(logits: torch.Tensor, params: list, history: list, seeds: list, 
 def sample(logits: torch.Tensor, params: list, history: list = None, generators: list = None,
            seeds: list = None, steps: list = None) -> torch.Tensor:
     """Next token ids [B] (int64) from fp32 logits [B, V]."""
+    if history is not None and any(p.dry for p in params):
+        logits = apply_dry(logits.clone(), history, params)
     if logits.is_cuda and seeds is not None:
         return sample_cuda(logits, params, history or [[] for _ in params], seeds, steps)
     if all(p.greedy for p in params) and not any(

@@ -213,9 +213,7 @@ class Scheduler:
         waits for admission and the runner supports it (single rank, CUDA graphs)."""
         r = self.runner
         return (getattr(r, "use_graphs", False) and hasattr(r, "pipeline_step")
-                and not self.waiting and all(
-                    q.params.greedy and q.params.repeat_penalty == 1.0 and not q.params.presence_penalty
-                    and not q.params.frequency_penalty for q in batch))
+                and not self.waiting and all(q.params.greedy and q.params.plain for q in batch))
 
     def _pipelined_decode(self, batch) -> int:
         """Decode ``batch`` until it changes, keeping one step in flight: step N runs on the
@@ -307,8 +305,7 @@ class Scheduler:
         pos = [len(r.tokens) - 1 for r in batch]
         slots = [r.blocks[p // BLOCK] * BLOCK + p % BLOCK for r, p in zip(batch, pos)]
         lens = [p + 1 for p in pos]
-        greedy = all(r.params.greedy and r.params.repeat_penalty == 1.0 and not r.params.presence_penalty
-                     and not r.params.frequency_penalty for r in batch)
+        greedy = all(r.params.greedy and r.params.plain for r in batch)
         logits, toks = self.runner.decode(ids, pos, slots, [r.blocks for r in batch], lens, greedy=greedy,
                                           state_slots=[r.state_slot for r in batch])
         if toks is None:
