@@ -241,6 +241,9 @@ class EngineConfig:
     max_seq      longest sequence (prompt + completion) accepted
     kv_blocks    KV pages to allocate (0 = size from ``kv_mem_fraction`` of free memory)
     comm         "fused" (in-kernel NVLink P2P) or "nccl" (library collectives)
+    spec_ngram   draft tokens per step for n-gram speculative decoding of greedy
+                 requests (0 = off): the longest recent n-gram match in the request's
+                 own tokens proposes a continuation, one forward verifies it
     """
 
     model: str = "qwen3-8b"
@@ -264,6 +267,7 @@ class EngineConfig:
     comm: str = "fused"
     device: str = "cuda"
     num_layers_override: int = 0
+    spec_ngram: int = 0
     extra: dict = field(default_factory=dict)
 
     @classmethod

@@ -109,7 +109,8 @@ class B200Engine(BaseEngine):
         self.runner = runner
         # a prefix-cache hit would skip tokens whose recurrent state a hybrid model needs
         self.scheduler = Scheduler(runner, num_blocks, max_batch=cfgE.max_batch, prefill_chunk=cfgE.prefill_chunk,
-                                   max_seq=cfgE.max_seq, prefix_cache=not mc.is_hybrid)
+                                   max_seq=cfgE.max_seq, prefix_cache=not mc.is_hybrid,
+                                   spec_ngram=0 if mc.is_hybrid else cfgE.spec_ngram)
         self.tokenizer = self._injected_tokenizer or load_tokenizer(self._model_path(), mc.vocab_size)
         from b200serve.core import inference
         inference._tokenizer = self.tokenizer

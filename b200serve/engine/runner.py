@@ -272,8 +272,9 @@ class ModelRunner:
     # ------------------------------------------------------------ prefill / mixed
     def prefill(self, seqs):
         """``seqs``: list of dicts with ids (new tokens), start (position of the first new
-        token), block_table, want_logits. Returns fp32 logits for sequences with want_logits,
-        in order."""
+        token), block_table, want_logits, all_logits, state_slot. Returns fp32 logits, in
+        order: every new token's row for sequences with all_logits (speculative verify),
+        the last row for those with want_logits."""
         d = self.device
         ids, pos, slots, cu, qs, lens, rows, sts = [], [], [], [0], [], [], [], []
         maxb = max(len(s["block_table"]) for s in seqs)
@@ -290,7 +291,9 @@ class ModelRunner:
             lens.append(st + n)
             sts.append(s.get("state_slot", self.scratch_slot))
             bt[i, : len(table)] = torch.as_tensor(table, dtype=torch.int32)
-            if s.get("want_logits", True):
+            if s.get("all_logits"):
+                rows += list(range(cu[-2], cu[-1]))
+            elif s.get("want_logits", True):
                 rows.append(cu[-1] - 1)
         T = len(ids)
         t = lambda x: torch.as_tensor(x, dtype=torch.int32).to(d, non_blocking=True)

@@ -31,6 +31,23 @@ from b200serve.engine.sampler import SamplingParams, sample
 
 _ids = itertools.count()
 
+NGRAM_MAX, NGRAM_WINDOW = 3, 4096
+
+
+def ngram_draft(tokens: list, k: int, n_max: int = NGRAM_MAX, window: int = NGRAM_WINDOW) -> list:
+    """Up to k tokens that followed the most recent earlier occurrence of the longest
+    suffix n-gram (n = n_max .. 1) of ``tokens`` within the last ``window`` tokens."""
+    if k <= 0 or len(tokens) < 2:
+        return []
+    ctx = tokens[-window:]
+    L = len(ctx)
+    for n in range(min(n_max, L - 1), 0, -1):
+        suf = ctx[L - n:]
+        for i in range(L - n - 1, -1, -1):
+            if ctx[i:i + n] == suf:
+                return ctx[i + n:i + n + k]
+    return []
+
 
 @dataclass
 class Request:
@@ -71,7 +88,7 @@ class Request:
 
 class Scheduler:
     def __init__(self, runner, num_blocks: int, max_batch: int = 64, prefill_chunk: int = 8192,
-                 max_seq: int = 4096, prefix_cache: bool = True):
+                 max_seq: int = 4096, prefix_cache: bool = True, spec_ngram: int = 0):
         self.runner = runner
         self.alloc = BlockAllocator(num_blocks, enable_prefix_cache=prefix_cache)
         self.max_batch = max_batch
@@ -83,8 +100,10 @@ class Scheduler:
         self.pipeline = True
         # hybrid (DeltaNet) models keep a recurrent state per running request
         self.free_states = list(range(max_batch)) if getattr(runner, "lin_state", None) is not None else None
+        self.spec_ngram = spec_ngram
         self.stats = {"steps": 0, "decode_steps": 0, "mixed_steps": 0, "preemptions": 0,
-                      "generated": 0, "prefill_tokens": 0, "prefix_hit_tokens": 0}
+                      "generated": 0, "prefill_tokens": 0, "prefix_hit_tokens": 0,
+                      "spec_steps": 0, "spec_drafted": 0, "spec_accepted": 0}
 
     # ------------------------------------------------------------ queue ops
     def add(self, req: Request) -> Request:
@@ -284,6 +303,10 @@ class Scheduler:
         self.stats["steps"] += 1
         if any(r.num_computed < len(r.tokens) - 1 for r in self.running):
             return self._mixed_step()
+        if self.spec_ngram and any(self._spec_ok(r) for r in self.running):
+            n = self._spec_step()
+            if n:
+                return n
         if self.pipeline and self._pipe_ok(self.running):
             return self._pipelined_decode(list(self.running))
         return self._decode_step()
@@ -363,6 +386,66 @@ class Scheduler:
             if r.state == "finished":
                 self.running.remove(r)
         return len(sample_reqs)
+
+    # ------------------------------------------------------------ n-gram speculative decoding
+    def _spec_ok(self, r: Request) -> bool:
+        return r.params.greedy and r.params.plain and ngram_draft(r.tokens, self.spec_ngram) != []
+
+    def _spec_step(self) -> int:
+        """Verify n-gram drafts of greedy requests in one forward: each drafting request feeds
+        its last token plus k drafted tokens and gets logits for all of them; the longest
+        prefix of drafts that matches the argmax is kept, plus the model's own next token.
+        Other requests take a plain one-token step in the same forward. Greedy outputs are
+        exactly those of one-token decoding. Reference behaviour: n-gram draft and verify in
+        the generate loop (webgpu/src/engine/generate.ts:194, 619-639)."""
+        seqs, plan = [], []
+        for r in list(self.running):
+            if r not in self.running:
+                continue
+            draft = ngram_draft(r.tokens, self.spec_ngram) if (r.params.greedy and r.params.plain) else []
+            room = min(r.params.max_tokens - len(r.output), self.max_seq - len(r.tokens)) - 1
+            draft = draft[:max(0, room)]
+            if not self._ensure_blocks(r, len(r.tokens) + len(draft)):
+                continue
+            if r not in self.running:
+                continue
+            seqs.append({"ids": [r.tokens[-1]] + draft, "start": len(r.tokens) - 1, "block_table": r.blocks,
+                         "want_logits": True, "all_logits": bool(draft), "state_slot": r.state_slot})
+            plan.append((r, draft))
+        keep = [(s, pl) for s, pl in zip(seqs, plan) if pl[0] in self.running]
+        if not keep:
+            return 0
+        logits = self.runner.prefill([s for s, _ in keep])
+        self.stats["spec_steps"] += 1
+        row, accepted = 0, 0
+        plain_rows, plain_reqs, spec = [], [], []
+        for _, (r, draft) in keep:
+            n = len(draft) + 1 if draft else 1
+            if draft:
+                pred = logits[row:row + n].argmax(-1).tolist()
+                a = 0
+                while a < len(draft) and pred[a] == draft[a]:
+                    a += 1
+                spec.append((r, draft[:a] + [pred[a]]))
+                self.stats["spec_drafted"] += len(draft)
+                self.stats["spec_accepted"] += a
+            else:
+                plain_rows.append(row)
+                plain_reqs.append(r)
+            row += n
+        if plain_reqs:
+            toks = self._sample(logits[plain_rows], plain_reqs).tolist()
+            spec += [(r, [t]) for r, t in zip(plain_reqs, toks)]
+        for r, new in spec:
+            for t in new:
+                if r.state == "finished":
+                    break
+                r.num_computed = len(r.tokens)
+                self._accept_token(r, int(t))
+                accepted += 1
+            if r.state == "finished" and r in self.running:
+                self.running.remove(r)
+        return accepted
 
     def _sample(self, logits, reqs) -> torch.Tensor:
         """``logits`` covers the whole vocabulary (the runner gathers tensor-parallel shards)."""

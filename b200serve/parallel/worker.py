@@ -48,7 +48,8 @@ class BroadcastRunner:
     def prefill(self, seqs):
         flat = [len(seqs)]
         for s in seqs:
-            flat += [len(s["ids"]), s["start"], int(s.get("want_logits", True)), len(s["block_table"]),
+            want = 2 if s.get("all_logits") else int(s.get("want_logits", True))
+            flat += [len(s["ids"]), s["start"], want, len(s["block_table"]),
                      s.get("state_slot", self.inner.scratch_slot)]
             flat += list(s["ids"]) + list(s["block_table"])
         payload = torch.as_tensor(flat, dtype=torch.int32).to(self.device)
@@ -129,7 +130,8 @@ def _unpack_prefill(flat):
         i += L
         bt = flat[i:i + nb]
         i += nb
-        seqs.append({"ids": ids, "start": start, "want_logits": bool(want), "block_table": bt, "state_slot": st})
+        seqs.append({"ids": ids, "start": start, "want_logits": bool(want), "all_logits": want == 2,
+                     "block_table": bt, "state_slot": st})
     return seqs
 
 
