@@ -168,11 +168,23 @@ class ModelRunner:
             logits, toks = self._decode_body(bucket, greedy)
         return logits[:B], (toks[:B] if toks is not None else None)
 
-    def capture(self, bucket: int, greedy: bool):
-        # warm up outside the graph (lazy workspace allocation, kernel attributes)
+    def _warmup(self, bucket: int, greedy: bool):
+        """Two eager decode steps before a capture (lazy workspace allocation, kernel attributes).
+        They rewrite the same K/V the real step writes, which is harmless, but a recurrent
+        state update is not idempotent: hybrid models run them on the scratch state slot."""
+        saved = None
+        if self.lin_state is not None:
+            saved = self.s_state[:bucket].clone()
+            self.s_state[:bucket].fill_(self.scratch_slot)
         for _ in range(2):
-            self._decode_body(bucket, greedy)
+            out = self._decode_body(bucket, greedy)
+        if saved is not None:
+            self.s_state[:bucket].copy_(saved)
         torch.cuda.synchronize()
+        return out
+
+    def capture(self, bucket: int, greedy: bool):
+        self._warmup(bucket, greedy)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             out = self._decode_body(bucket, greedy)
@@ -197,9 +209,7 @@ class ModelRunner:
     def loop_body(self, B, bucket, warmup, steps) -> dict:
         key = (bucket, "loop", B)
         if key not in self.graphs:
-            for _ in range(2):
-                _, toks = self._decode_body(bucket, True)
-            torch.cuda.synchronize()
+            self._warmup(bucket, True)
             ops.reset_launch_count()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
@@ -247,9 +257,7 @@ class ModelRunner:
         B, bucket = self._pipe["B"], self._pipe["bucket"]
         key = (bucket, "loop", B)
         if key not in self.graphs:
-            for _ in range(2):
-                _, toks = self._decode_body(bucket, True)
-            torch.cuda.synchronize()
+            self._warmup(bucket, True)
             ops.reset_launch_count()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
