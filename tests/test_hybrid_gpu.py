@@ -142,6 +142,17 @@ def _hybrid_cfg(**kw):
     return ModelConfig(**d)
 
 
+def _moved(w, device, dtype):
+    keep32 = ("conv_w", "lin_A", "lin_dt")
+    for lw in w.layers:
+        for name, v in list(vars(lw).items()):
+            if isinstance(v, torch.Tensor):
+                setattr(lw, name, v.to(device=device, dtype=torch.float32 if name in keep32 else dtype))
+    for name in ("embed", "final_norm", "lm_head"):
+        setattr(w, name, getattr(w, name).to(device=device, dtype=dtype))
+    return w
+
+
 def test_hybrid_engine_gpu_matches_cpu():
     """A tiny Qwen3.5-shaped hybrid (head_dim 256, DeltaNet heads of 128) on the GPU (bf16,
     CUDA-graph decode) against the CPU fp32 path: prefill two prompts into two state slots,
@@ -154,7 +165,8 @@ def test_hybrid_engine_gpu_matches_cpu():
     prompts = [torch.randint(3, 2048, (n,), generator=g).tolist() for n in (50, 200)]
     outs = {}
     for device, dtype in (("cpu", torch.float32), ("cuda", torch.bfloat16)):
-        w = random_weights(cfg, seed=1, std=0.05, dtype=dtype, device=device)
+        # the same host-drawn weights on both sides (a CUDA generator draws other numbers)
+        w = _moved(random_weights(cfg, seed=1, std=0.05, dtype=torch.float32, device="cpu"), device, dtype)
         ec = EngineConfig(model="tiny-hybrid", device=device, dtype="float32" if device == "cpu" else "bfloat16",
                           cuda_graphs=device == "cuda", max_seq=512, max_batch=4, kv_blocks=128)
         eng = B200Engine(ec, weights=w, model_config=cfg)
