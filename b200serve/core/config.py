@@ -244,6 +244,8 @@ class EngineConfig:
     spec_ngram   draft tokens per step for n-gram speculative decoding of greedy
                  requests (0 = off): the longest recent n-gram match in the request's
                  own tokens proposes a continuation, one forward verifies it
+    shard_cache  directory of pre-sharded per-rank weights (models/shard_cache.py): a
+                 valid cache is read instead of the checkpoint, otherwise it is written
     """
 
     model: str = "qwen3-8b"
@@ -268,6 +270,7 @@ class EngineConfig:
     device: str = "cuda"
     num_layers_override: int = 0
     spec_ngram: int = 0
+    shard_cache: str = ""
     extra: dict = field(default_factory=dict)
 
     @classmethod

@@ -123,6 +123,27 @@ class B200Engine(BaseEngine):
 
     def _load_weights(self, mc, dtype, dev):
         cfgE = self.config
+        if not cfgE.shard_cache:
+            return self._load_weights_uncached(mc, dtype, dev)
+        import torch.distributed as dist
+        from b200serve.models import shard_cache as SC
+        source = cfgE.model if cfgE.weights != "random" else f"random:{cfgE.seed}:{cfgE.init_std}"
+        fp = SC.fingerprint(mc, source)
+        tp = cfgE.tp_size
+        rank = self.rank if tp > 1 else 0
+        if SC.valid(cfgE.shard_cache, fp, tp, dtype):
+            _log.info(f"b200: weights from the shard cache {cfgE.shard_cache}")
+            return SC.load(cfgE.shard_cache, rank, tp, device=dev)
+        w = self._load_weights_uncached(mc, dtype, dev)
+        barrier = dist.barrier if (tp > 1 and dist.is_initialized()) else None
+        try:
+            SC.save(w, cfgE.shard_cache, fp, dtype, barrier=barrier)
+        except TypeError as e:     # block-quantised layers stay uncached
+            _log.warning(f"b200: shard cache not written: {e}")
+        return w
+
+    def _load_weights_uncached(self, mc, dtype, dev):
+        cfgE = self.config
         from b200serve.models import weights as W
         kw = dict(tp_rank=self.rank if cfgE.tp_size > 1 else 0, tp_size=cfgE.tp_size,
                   ep_rank=self.rank if cfgE.ep_size > 1 else 0, ep_size=cfgE.ep_size, dtype=dtype, device=dev)
