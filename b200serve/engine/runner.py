@@ -14,6 +14,7 @@ import torch
 
 from b200serve import ops
 from b200serve.models.qwen import Decoder, ForwardBatch
+from b200serve.utils.nvtx import rng
 
 
 def unpack_static(runner, bucket):
@@ -158,14 +159,16 @@ class ModelRunner:
         """One decode step for B sequences. Returns (logits [B, V_local], tokens [B] or None)."""
         B = len(ids)
         bucket, _ = self.load_decode_inputs(ids, pos, slots, block_tables, lens, state_slots)
-        if self.use_graphs:
-            key = (bucket, greedy)
-            if key not in self.graphs:
-                self.capture(bucket, greedy)
-            self.graphs[key].replay()
-            logits, toks = self.graph_out[key]
-        else:
-            logits, toks = self._decode_body(bucket, greedy)
+        with rng(f"decode b{bucket}"):
+            if self.use_graphs:
+                key = (bucket, greedy)
+                if key not in self.graphs:
+                    with rng("capture"):
+                        self.capture(bucket, greedy)
+                self.graphs[key].replay()
+                logits, toks = self.graph_out[key]
+            else:
+                logits, toks = self._decode_body(bucket, greedy)
         return logits[:B], (toks[:B] if toks is not None else None)
 
     def _warmup(self, bucket: int, greedy: bool):
@@ -311,4 +314,5 @@ class ModelRunner:
                           state_slots=t(sts) if self.lin_state is not None else None)
         if T == 0:
             return None
-        return self.decoder.forward(fb)
+        with rng(f"prefill T{T}"):
+            return self.decoder.forward(fb)

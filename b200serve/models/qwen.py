@@ -21,6 +21,7 @@ import torch
 from b200serve import ops
 from b200serve.models.config import ModelConfig
 from b200serve.models.weights import ModelWeights
+from b200serve.utils.nvtx import ENABLED as _NVTX
 
 
 @dataclass
@@ -339,6 +340,8 @@ class Decoder:
         residual = torch.empty_like(h)
         x = ops.rmsnorm([h], w.layers[0].input_norm, eps, residual_out=residual)
         for i, lw in enumerate(w.layers):
+            if _NVTX:
+                torch.cuda.nvtx.range_push(f"layer {i}")
             if i > 0:
                 x = ops.rmsnorm(mlp_parts, lw.input_norm, eps, residual=residual, residual_out=residual)
             if cfg.is_linear(i):
@@ -353,6 +356,8 @@ class Decoder:
             else:
                 act = ops.linear(x, lw.gate_up, epilogue=ops.EPI_SWIGLU)
                 mlp_parts = self._row_parallel(act, lw.down, "mlp")
+            if _NVTX:
+                torch.cuda.nvtx.range_pop()
         rows = fb.logit_rows
         x = ops.rmsnorm(mlp_parts, w.final_norm, eps, residual=residual)
         if rows is not None:
