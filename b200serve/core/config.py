@@ -246,6 +246,8 @@ class EngineConfig:
                  own tokens proposes a continuation, one forward verifies it
     shard_cache  directory of pre-sharded per-rank weights (models/shard_cache.py): a
                  valid cache is read instead of the checkpoint, otherwise it is written
+    step_timeout_s  watchdog: a forward step running longer fails the requests it holds
+                 (their streams end with an error) and marks the engine stalled (0 = off)
     """
 
     model: str = "qwen3-8b"
@@ -271,6 +273,7 @@ class EngineConfig:
     num_layers_override: int = 0
     spec_ngram: int = 0
     shard_cache: str = ""
+    step_timeout_s: float = 600.0
     extra: dict = field(default_factory=dict)
 
     @classmethod

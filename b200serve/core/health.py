@@ -22,5 +22,9 @@ def run_health_check(engine=None) -> dict:
         m = getattr(engine, "metrics", None)
         if callable(m):
             checks["engine"]["metrics"] = m()
+        if getattr(engine, "stalled", False):
+            checks["engine"].update(ok=False, stalled=True)
     status = "ok" if all(c.get("ok") for k, c in checks.items() if k in ("cuda", "kernels")) else "degraded"
+    if engine is not None and getattr(engine, "stalled", False):
+        status = "degraded"
     return {"status": status, "checks": checks}

@@ -63,6 +63,9 @@ class B200Engine(BaseEngine):
         self._last_gen_stats = None
         self.rank = 0
         self.world = 1
+        self._step_t0 = None        # start of the step in progress (watchdog)
+        self.stalled = False
+        self._watch = None
 
     # ------------------------------------------------------------ lifecycle
     def is_loaded(self) -> bool:
@@ -207,6 +210,9 @@ class B200Engine(BaseEngine):
         self._stop.clear()
         self._thread = threading.Thread(target=self._loop, name="b200-engine", daemon=True)
         self._thread.start()
+        if self.config.step_timeout_s > 0 and self._watch is None:
+            self._watch = threading.Thread(target=self._watchdog, name="b200-watchdog", daemon=True)
+            self._watch.start()
 
     def stop_loop(self):
         if self._thread is None:
@@ -216,6 +222,9 @@ class B200Engine(BaseEngine):
             self._wake.notify_all()
         self._thread.join(timeout=30)
         self._thread = None
+        if self._watch is not None:
+            self._watch.join(timeout=5)
+            self._watch = None
         if self.world > 1 and hasattr(self.runner, "shutdown_workers"):
             self.runner.shutdown_workers()
 
@@ -228,8 +237,12 @@ class B200Engine(BaseEngine):
                     self._wake.wait(timeout=0.05)
                 continue
             try:
+                self._step_t0 = time.monotonic()
                 self.scheduler.step()
+                self._step_t0 = None
+                self.stalled = False
             except Exception as e:  # fail every in-flight request, keep the loop alive
+                self._step_t0 = None
                 _log.exception("engine step failed")
                 self._error = e
                 for r in list(self.scheduler.running) + list(self.scheduler.waiting):
@@ -237,6 +250,30 @@ class B200Engine(BaseEngine):
                     self.scheduler._finish(r, "error")
                 self.scheduler.running.clear()
                 self.scheduler.waiting.clear()
+
+    def _watchdog(self):
+        """Per-request watchdog: when one forward step runs past ``step_timeout_s`` (a hung
+        collective or kernel), every request it holds is finished with an error so that its
+        client is released, and the engine reports itself stalled. The scheduler's lists are
+        left alone: if the step ever returns, the loop drops the aborted requests normally."""
+        limit = self.config.step_timeout_s
+        flagged = None
+        while not self._stop.is_set():
+            self._stop.wait(min(1.0, limit / 4))
+            t0 = self._step_t0
+            if t0 is None or t0 == flagged or time.monotonic() - t0 < limit:
+                continue
+            flagged = t0
+            self.stalled = True
+            self._error = RuntimeError(f"engine step exceeded {limit:.0f} s")
+            _log.error("b200: engine step exceeded %.0f s; failing its requests", limit)
+            sched = self.scheduler
+            for r in list(sched.running) + list(sched.waiting):
+                r.aborted = True
+                if r.state != "finished":
+                    r.state, r.finish_reason = "finished", "error"
+                    r.finish_time = time.perf_counter()
+                    r.done_event.set()
 
     def submit(self, req: Request) -> Request:
         self.load()

@@ -193,6 +193,8 @@ class Scheduler:
 
     def _finish(self, req: Request, reason: str):
         self._release_state(req)
+        if req.state == "finished" and req.finish_reason == "error":
+            reason = "error"              # keep the watchdog's verdict
         req.state = "finished"
         req.finish_reason = reason
         req.finish_time = time.perf_counter()
@@ -203,6 +205,10 @@ class Scheduler:
         req.done_event.set()
 
     def _accept_token(self, req: Request, tok: int):
+        if req.state == "finished":      # failed by the watchdog while its step ran
+            if req.blocks or req.state_slot >= 0:
+                self._finish(req, req.finish_reason or "error")
+            return
         now = time.perf_counter()
         if req.first_token_time is None:
             req.first_token_time = now

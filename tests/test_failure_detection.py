@@ -108,3 +108,39 @@ def test_scheduler_fails_requests_when_step_raises():
         assert len(out[0].output) == 3
     finally:
         eng.unload()
+
+
+def test_step_watchdog_fails_requests_of_a_stalled_step():
+    """A forward step that runs past step_timeout_s (here: a step made to sleep) releases its
+    requests with finish_reason "error" and marks the engine stalled; once the step returns,
+    the engine serves new requests normally."""
+    import time as _time
+    from b200serve.core.config import EngineConfig
+    from b200serve.engine.b200_engine import B200Engine
+    from b200serve.engine.sampler import SamplingParams
+    eng = B200Engine(EngineConfig(model="tiny-qwen2", device="cpu", dtype="float32", cuda_graphs=False,
+                                  max_seq=128, max_batch=2, step_timeout_s=0.4))
+    eng.load()
+    real_step = eng.scheduler.step
+    calls = {"n": 0}
+
+    def slow_step():
+        calls["n"] += 1
+        if calls["n"] == 1:
+            _time.sleep(1.5)
+        return real_step()
+
+    eng.scheduler.step = slow_step
+    try:
+        sp = SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True)
+        t0 = _time.time()
+        [r] = eng.generate([[5, 6, 7]], sp, timeout=30)
+        assert r.finish_reason == "error" and _time.time() - t0 < 1.4
+        assert eng.stalled
+        _time.sleep(1.5)                                     # the slow step returns
+        [r2] = eng.generate([[5, 6, 7]], sp, timeout=30)
+        assert r2.finish_reason == "length" and len(r2.output) == 4
+        assert not eng.stalled
+        assert eng.scheduler.alloc.num_free == eng.scheduler.alloc.num_blocks   # nothing leaked
+    finally:
+        eng.unload()
