@@ -37,7 +37,7 @@ def _dtype(name):
 
 
 def _kv_layers(mc) -> int:
-    return sum(1 for i in range(mc.num_layers) if not mc.is_linear(i))
+    return sum(1 for i in range(mc.num_layers) if mc.has_kv(i))
 
 
 class B200Engine(BaseEngine):

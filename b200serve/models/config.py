@@ -14,7 +14,8 @@ HF ``config.json`` files of the qwen2 / qwen3 / qwen3_moe / llama / mistral
 families map onto the same dataclass (Llama and Mistral are the Qwen2 block
 without q/k/v bias; their RoPE may carry a ``linear`` or ``llama3`` scaling).
 ``qwen3_5`` (the Qwen3.5 hybrid) adds per-layer kinds: Gated DeltaNet
-linear-attention layers and gated full-attention layers with partial RoPE.
+linear-attention layers and gated full-attention layers with partial RoPE;
+``lfm2`` mixes gated short-convolution layers with attention layers.
 """
 
 from __future__ import annotations
@@ -67,10 +68,17 @@ class ModelConfig:
 
     @property
     def is_hybrid(self) -> bool:
-        return any(t == "linear_attention" for t in self.layer_types)
+        """Some layers keep a per-sequence state instead of K/V (DeltaNet or short conv)."""
+        return any(t in ("linear_attention", "conv") for t in self.layer_types)
 
     def is_linear(self, i: int) -> bool:
         return bool(self.layer_types) and self.layer_types[i] == "linear_attention"
+
+    def is_conv(self, i: int) -> bool:
+        return bool(self.layer_types) and self.layer_types[i] == "conv"
+
+    def has_kv(self, i: int) -> bool:
+        return not self.layer_types or self.layer_types[i] == "full_attention"
 
     @property
     def lin_conv_dim(self) -> int:
@@ -154,7 +162,7 @@ BUILTIN = {
 }
 
 
-_FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "llama", "mistral", "qwen3_5_text")
+_FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "llama", "mistral", "qwen3_5_text", "lfm2")
 
 
 def _rope_params(d: dict):
@@ -197,14 +205,27 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
                       lin_k_heads=d.get("linear_num_key_heads", 16), lin_v_heads=d.get("linear_num_value_heads", 32),
                       lin_k_dim=d.get("linear_key_head_dim", 128), lin_v_dim=d.get("linear_value_head_dim", 128),
                       conv_kernel=d.get("linear_conv_kernel_dim", 4), rotary_dim=int(hd_full * prf))
+    inter = d.get("intermediate_size", 0)
+    if mt == "lfm2":
+        n = d["num_hidden_layers"]
+        full = d.get("full_attn_idxs")
+        lt = d.get("layer_types") or ["full_attention" if (full is None or i in full) else "conv" for i in range(n)]
+        if d.get("block_auto_adjust_ff_dim", True):   # the FFN width LFM2 derives from its config
+            inter = int(2 * inter / 3)
+            if d.get("block_ffn_dim_multiplier") is not None:
+                m_ = d.get("block_multiple_of", 256)
+                inter = m_ * ((int(d["block_ffn_dim_multiplier"] * inter) + m_ - 1) // m_)
+        if d.get("conv_bias"):
+            raise NotImplementedError("LFM2 with conv_bias=True")
+        hybrid = dict(layer_types=tuple(lt), conv_kernel=d.get("conv_L_cache", 3))
     return ModelConfig(
         name=name, vocab_size=d["vocab_size"], hidden_size=d["hidden_size"],
         num_layers=d["num_hidden_layers"], num_heads=heads,
         num_kv_heads=d.get("num_key_value_heads") or heads, head_dim=hd,
-        intermediate_size=d.get("intermediate_size", 0), rms_eps=d.get("rms_norm_eps", 1e-6),
+        intermediate_size=inter, rms_eps=d.get("rms_norm_eps", d.get("norm_eps", 1e-6)),
         rope_theta=theta, rope_scaling=scaling,
         attn_bias=(mt == "qwen2") or bool(d.get("attention_bias", False)),
-        qk_norm=mt in ("qwen3", "qwen3_moe", "qwen3_5_text"),
+        qk_norm=mt in ("qwen3", "qwen3_moe", "qwen3_5_text", "lfm2"),
         tie_embeddings=bool(d.get("tie_word_embeddings", False)),
         num_experts=d.get("num_experts", 0) if moe else 0,
         experts_per_tok=d.get("num_experts_per_tok", 0) if moe else 0,

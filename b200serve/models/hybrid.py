@@ -1,5 +1,6 @@
-"""Qwen3.5 hybrid decoder parts: Gated DeltaNet (linear-attention) layers, the gated
-full-attention layout, and the per-sequence recurrent state.
+"""Hybrid decoder parts: Gated DeltaNet (linear-attention) layers and the gated
+full-attention layout of Qwen3.5, LFM2's gated short-convolution layers, and the
+per-sequence state both keep.
 
 Checkpoint layout (HF ``Qwen3_5ForCausalLM``; the multimodal checkpoint nests the same
 names under ``model.language_model.``):
@@ -110,7 +111,10 @@ class LinearState:
         self.scratch = self.slots - 1
         self.conv, self.rec = {}, {}
         for i in range(cfg.num_layers):
-            if cfg.is_linear(i):
+            if cfg.is_conv(i):      # LFM2 short conv: conv state over this rank's channels only
+                self.conv[i] = torch.zeros(self.slots, cfg.hidden_size // tp, cfg.conv_kernel - 1,
+                                           dtype=torch.float32, device=device)
+            elif cfg.is_linear(i):
                 self.conv[i] = torch.zeros(self.slots, conv_dim, cfg.conv_kernel - 1, dtype=torch.float32,
                                            device=device)
                 self.rec[i] = torch.zeros(self.slots, nv, cfg.lin_k_dim, cfg.lin_v_dim, dtype=torch.float32,
@@ -124,4 +128,45 @@ class LinearState:
         nk, nv = cfg.lin_k_heads // tp, cfg.lin_v_heads // tp
         conv_dim = (2 * nk + nv) * cfg.lin_k_dim
         n = sum(1 for i in range(cfg.num_layers) if cfg.is_linear(i))
-        return n * 4 * (conv_dim * (cfg.conv_kernel - 1) + nv * cfg.lin_k_dim * cfg.lin_v_dim)
+        nc = sum(1 for i in range(cfg.num_layers) if cfg.is_conv(i))
+        return n * 4 * (conv_dim * (cfg.conv_kernel - 1) + nv * cfg.lin_k_dim * cfg.lin_v_dim) + \
+            nc * 4 * (cfg.hidden_size // tp) * (cfg.conv_kernel - 1)
+
+
+# ------------------------------------------------------------------ LFM2 short convolution
+LFM2_KEYS = {
+    "q": "self_attn.q_proj.weight", "k": "self_attn.k_proj.weight", "v": "self_attn.v_proj.weight",
+    "o": "self_attn.out_proj.weight", "q_norm": "self_attn.q_layernorm.weight",
+    "k_norm": "self_attn.k_layernorm.weight", "input_norm": "operator_norm.weight", "post_norm": "ffn_norm.weight",
+    "gate": "feed_forward.w1.weight", "up": "feed_forward.w3.weight", "down": "feed_forward.w2.weight",
+    "sc_in": "conv.in_proj.weight", "sc_conv": "conv.conv.weight", "sc_out": "conv.out_proj.weight",
+}
+
+
+def shard_layer_shortconv(cfg, full: dict, rank: int, size: int, dtype, device):
+    """One LFM2 short-conv layer for tensor-parallel rank ``rank``: the B, C and x channels
+    (and their conv taps) are split by rank; out_proj is row-parallel."""
+    from b200serve.models.weights import LayerWeights, interleave_gate_up, pad_down
+    H = cfg.hidden_size
+    assert H % size == 0
+    Hr = H // size
+    sl = slice(rank * Hr, (rank + 1) * Hr)
+    w_in = full["sc_in"]
+    lin_in = torch.cat([w_in[:H][sl], w_in[H:2 * H][sl], w_in[2 * H:][sl]])
+    out = full["sc_out"][:, sl]
+    lw = LayerWeights(input_norm=full["input_norm"], post_norm=full["post_norm"], qkv=None, o=out)
+    lw.lin_in = lin_in
+    I = cfg.intermediate_size
+    Ir = I // size
+    lw.gate_up = interleave_gate_up(full["gate"][rank * Ir:(rank + 1) * Ir], full["up"][rank * Ir:(rank + 1) * Ir])
+    lw.down = pad_down(full["down"][:, rank * Ir:(rank + 1) * Ir])
+    for name, val in vars(lw).items():
+        if isinstance(val, torch.Tensor):
+            setattr(lw, name, val.to(device=device, dtype=dtype).contiguous())
+    lw.conv_w = full["sc_conv"].reshape(H, -1)[sl].to(device=device, dtype=torch.float32).contiguous()
+    return lw
+
+
+def random_conv_layer(cfg, n) -> dict:
+    H = cfg.hidden_size
+    return {"sc_in": n(3 * H, H), "sc_conv": n(H, 1, cfg.conv_kernel).float().mul_(10.0), "sc_out": n(H, H)}

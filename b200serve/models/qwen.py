@@ -86,11 +86,11 @@ class Decoder:
         # K/V cache index of each layer (hybrid models page only their full-attention layers)
         self.kvi, n = [], 0
         for i in range(cfg.num_layers):
-            self.kvi.append(-1 if cfg.is_linear(i) else n)
-            n += 0 if cfg.is_linear(i) else 1
+            self.kvi.append(n if cfg.has_kv(i) else -1)
+            n += 1 if cfg.has_kv(i) else 0
         self.lin_state = None
         if cfg.is_hybrid and getattr(kv_cache, "kv_format", "bf16") != "bf16":
-            raise NotImplementedError("hybrid (DeltaNet) models run with the bf16 KV cache")
+            raise NotImplementedError("hybrid (DeltaNet / short-conv) models run with the bf16 KV cache")
         want_rot = getattr(kv_cache, "kv_format", "bf16") == "turboquant"
         if want_rot:
             self.tq = ops.TurboQuantTables(kv_cache.key_bits, kv_cache.value_bits, self.device)
@@ -249,6 +249,14 @@ class Decoder:
             ops.sigmoid_gate_mul(out.view(T, self.nq * self.hd), qkv[:, w0:w0 + self.nq * self.hd])
         return out
 
+    def _conv_mix(self, i, x, lw, fb):
+        """LFM2 gated short convolution of layer ``i``: [B | C | x] = x W_in^T, then
+        C * conv(B * x) with the causal depthwise conv state -> [T, H_local] (before out_proj)."""
+        y = ops.linear(x, lw.lin_in)
+        cu = None if fb.is_decode else fb.cu_q
+        q_start = fb.positions if fb.is_decode else fb.q_start
+        return ops.shortconv_layer(y, lw.conv_w, self.lin_state.conv[i], cu, q_start, fb.state_slots)
+
     def _linear_mix(self, i, x, lw, fb):
         """Gated DeltaNet token mixing of layer ``i`` -> [T, nv_local * dv] (before out_proj)."""
         cfg, st = self.cfg, self.lin_state
@@ -346,6 +354,9 @@ class Decoder:
                 x = ops.rmsnorm(mlp_parts, lw.input_norm, eps, residual=residual, residual_out=residual)
             if cfg.is_linear(i):
                 mix = self._linear_mix(i, x, lw, fb)
+                o_parts = self._row_parallel(mix, lw.o, "o")
+            elif cfg.is_conv(i):
+                mix = self._conv_mix(i, x, lw, fb)
                 o_parts = self._row_parallel(mix, lw.o, "o")
             else:
                 attn = self._qkv_attend(self.kvi[i], x, lw, fb, T, plan, tq_pre)

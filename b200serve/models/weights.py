@@ -173,6 +173,11 @@ def build_weights(cfg: ModelConfig, layer_source, embed, lm_head, final_norm, tp
             layers.append(shard_layer_linear(cfg, full, tp_rank, tp_size, dtype, device))
             del full
             continue
+        if cfg.is_conv(i):
+            from b200serve.models.hybrid import shard_layer_shortconv
+            layers.append(shard_layer_shortconv(cfg, full, tp_rank, tp_size, dtype, device))
+            del full
+            continue
         lw = shard_layer_dense(cfg, full, tp_rank, tp_size, dtype, device)
         if cfg.is_moe:
             shard_layer_moe(cfg, full, lw, ep_rank, ep_size, dtype, device)
@@ -212,6 +217,12 @@ def random_weights(cfg: ModelConfig, seed=0, std=0.02, tp_rank=0, tp_size=1, ep_
             # norms with a (1 + w) scale are stored as w: zeros give the unit scale
             one = (lambda *sh: torch.zeros(*sh, dtype=dtype, device=gen_dev)) if cfg.norm_offset else \
                 (lambda *sh: torch.ones(*sh, dtype=dtype, device=gen_dev))
+            if cfg.is_conv(i):
+                from b200serve.models.hybrid import random_conv_layer
+                I = cfg.intermediate_size
+                d = random_conv_layer(cfg, n)
+                d.update(input_norm=one(H), post_norm=one(H), gate=n(I, H), up=n(I, H), down=n(H, I))
+                return d
             if cfg.is_linear(i):
                 from b200serve.models.hybrid import random_linear_layer
                 I = cfg.intermediate_size
@@ -254,6 +265,13 @@ def hf_layer_dict(get, cfg: ModelConfig, i: int) -> dict:
     """Collect layer ``i`` from an HF-named tensor getter (``get(name)`` -> tensor or None)."""
     pre = f"model.layers.{i}."
     d = {}
+    if cfg.family == "lfm2":
+        from b200serve.models.hybrid import LFM2_KEYS
+        for k, name in LFM2_KEYS.items():
+            t = get(pre + name)
+            if t is not None:
+                d[k] = t
+        return d
     if cfg.is_linear(i):
         from b200serve.models.hybrid import LIN_KEYS
         for k, name in LIN_KEYS.items():
@@ -286,7 +304,12 @@ def load_hf_state_dict(cfg: ModelConfig, sd: dict, **kw) -> ModelWeights:
     lm = get("lm_head.weight")
     if lm is None:
         lm = embed
-    return build_weights(cfg, lambda i: hf_layer_dict(get, cfg, i), embed, lm, get("model.norm.weight"), **kw)
+    return build_weights(cfg, lambda i: hf_layer_dict(get, cfg, i), embed, lm, _final_norm(get), **kw)
+
+
+def _final_norm(get):
+    t = get("model.norm.weight")
+    return t if t is not None else get("model.embedding_norm.weight")      # LFM2's name
 
 
 def load_safetensors_dir(cfg: ModelConfig, path: str, **kw) -> ModelWeights:
@@ -323,7 +346,7 @@ def load_safetensors_dir(cfg: ModelConfig, path: str, **kw) -> ModelWeights:
     lm = get("lm_head.weight")
     if lm is None:
         lm = embed
-    w = build_weights(cfg, lambda i: hf_layer_dict(get, cfg, i), embed, lm, get("model.norm.weight"), **kw)
+    w = build_weights(cfg, lambda i: hf_layer_dict(get, cfg, i), embed, lm, _final_norm(get), **kw)
     if gptq and torch.device(kw.get("device", "cpu")).type == "cuda" and os.environ.get("B200_GPTQ_KERNEL", "1") != "0":
         # 4-bit layers stay 4-bit on the GPU (the same GEMM as GGUF Q4_K)
         GP.quantize_layers(cfg, w, _with_lm_prefix(get_raw), qcfg, device=kw["device"])

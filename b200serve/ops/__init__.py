@@ -279,6 +279,37 @@ def _deltanet_cpu(y, conv_w, A, dt_bias, norm_w, conv_state, rec_state, cu_q, q_
     return out
 
 
+def shortconv_layer(y, conv_w, conv_state, cu_q, q_start, slots):
+    """LFM2 gated short convolution after the input projection ``y`` [T, 3 C] = [B | C | x]:
+    out = C * conv(B * x), a causal depthwise conv of K taps whose K-1 earlier inputs of a
+    sequence come from ``conv_state`` [slots, C, K-1] fp32 (zero when the sequence's
+    ``q_start`` is 0), which is then rolled forward. ``cu_q`` None = one token per sequence.
+    Returns [T, C]. Reference behaviour: shaders/short_conv.wgsl:37, conv1d.wgsl:57-82."""
+    T = y.shape[0]
+    C = conv_w.shape[0]
+    if _cuda(y, 2):
+        out = torch.empty(T, C, dtype=y.dtype, device=y.device)
+        ext().shortconv_layer(y, conv_w, conv_state, cu_q, q_start, slots, out)
+        return out
+    import torch.nn.functional as F
+    K = conv_w.shape[1]
+    cu = cu_q.tolist() if cu_q is not None else list(range(T + 1))
+    starts, sl = q_start.tolist(), slots.tolist()
+    out = torch.empty(T, C, dtype=y.dtype, device=y.device)
+    for s_ in range(len(cu) - 1):
+        t0, t1 = cu[s_], cu[s_ + 1]
+        if t1 == t0:
+            continue
+        yt = y[t0:t1].float()
+        bx = (yt[:, :C] * yt[:, 2 * C:3 * C]).t()
+        prev = conv_state[sl[s_]] if starts[s_] > 0 else torch.zeros(C, K - 1, dtype=torch.float32, device=y.device)
+        full = torch.cat([prev, bx], 1)
+        conv_state[sl[s_]] = full[:, -(K - 1):]
+        conv = F.conv1d(full[None], conv_w.float()[:, None, :], groups=C)[0].t()
+        out[t0:t1] = (yt[:, C:2 * C] * conv).to(y.dtype)
+    return out
+
+
 def sigmoid_gate_mul(attn, gate):
     """attn [T, W] *= sigmoid(gate) in place; ``gate`` may be a strided column view."""
     if _cuda(attn):

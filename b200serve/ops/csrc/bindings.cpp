@@ -112,6 +112,9 @@ void deltanet_layer(torch::Tensor y, torch::Tensor conv_w, torch::Tensor A, torc
                     c10::optional<torch::Tensor> cu_q, torch::Tensor q_start, torch::Tensor slots, torch::Tensor xc,
                     torch::Tensor gb, torch::Tensor out, int64_t nk, int64_t nv, int64_t D, double eps);
 void sigmoid_gate_mul(torch::Tensor attn, torch::Tensor gate);
+void shortconv_layer(torch::Tensor y, torch::Tensor conv_w, torch::Tensor conv_state,
+                     c10::optional<torch::Tensor> cu_q, torch::Tensor q_start, torch::Tensor slots,
+                     torch::Tensor out);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "b200serve sm_100a kernels";
@@ -138,6 +141,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("q4_dequant_pages", &q4_dequant_pages);
   m.def("deltanet_layer", &deltanet_layer);
   m.def("sigmoid_gate_mul", &sigmoid_gate_mul);
+  m.def("shortconv_layer", &shortconv_layer);
   m.def("prefill_tc_error", &prefill_tc_error);
   m.def("paged_decode_attention_tc", &paged_decode_attention_tc);
   m.def("topk_softmax", &topk_softmax);

@@ -191,3 +191,60 @@ def test_hybrid_engine_gpu_matches_cpu():
     assert len(outs["cuda"]) == 6
     for a, b in zip(outs["cuda"], outs["cpu"]):
         assert _rel(a, b) < 3e-2
+
+
+def test_shortconv_prefill_and_decode_match_fp32():
+    C, K = 384, 3
+    lens, starts, slots = [20, 3, 57], [0, 30, 0], [1, 0, 3]
+    T = sum(lens)
+    y = (torch.randn(T, 3 * C, device=dev) * 0.7).bfloat16()
+    w = (torch.randn(C, K, device=dev) * 0.5).float()
+    st = torch.randn(4, C, K - 1, device=dev)
+    cu = torch.tensor([0, 20, 23, T], dtype=torch.int32, device=dev)
+    qs = torch.tensor(starts, dtype=torch.int32, device=dev)
+    sl = torch.tensor(slots, dtype=torch.int32, device=dev)
+    st_ref = st.cpu().clone()
+    out = ops.shortconv_layer(y, w, st, cu, qs, sl)
+    ref = ops.shortconv_layer(y.cpu().float(), w.cpu(), st_ref, cu.cpu(), qs.cpu(), sl.cpu())
+    assert _rel(out.cpu(), ref) < 1e-2
+    for s in slots:
+        assert _rel(st[s].cpu(), st_ref[s]) < 1e-2
+    y2 = (torch.randn(3, 3 * C, device=dev) * 0.7).bfloat16()
+    pos = torch.tensor([20, 33, 57], dtype=torch.int32, device=dev)
+    out2 = ops.shortconv_layer(y2, w, st, None, pos, sl)
+    ref2 = ops.shortconv_layer(y2.cpu().float(), w.cpu(), st_ref, None, pos.cpu(), sl.cpu())
+    assert _rel(out2.cpu(), ref2) < 1e-2
+
+
+def test_lfm2_engine_gpu_matches_cpu():
+    """Tiny LFM2 (short-conv + attention layers) on the GPU against the CPU fp32 path."""
+    from b200serve.core.config import EngineConfig
+    from b200serve.engine.b200_engine import B200Engine
+    from b200serve.models.config import ModelConfig
+    from b200serve.models.weights import random_weights
+    cfg = ModelConfig("tiny-lfm2", 2048, 512, 4, 8, 2, 64, 1024, rope_theta=1e6, qk_norm=True, max_position=2048,
+                      layer_types=("conv", "full_attention", "conv", "full_attention"), conv_kernel=3,
+                      family="lfm2", tie_embeddings=True)
+    prompts = [torch.randint(3, 2048, (n,), generator=torch.Generator().manual_seed(n)).tolist() for n in (40, 150)]
+    outs = {}
+    for device, dtype in (("cpu", torch.float32), ("cuda", torch.bfloat16)):
+        w = _moved(random_weights(cfg, seed=2, std=0.05, dtype=torch.float32, device="cpu"), device, dtype)
+        ec = EngineConfig(model="tiny-lfm2", device=device, dtype="float32" if device == "cpu" else "bfloat16",
+                          cuda_graphs=device == "cuda", max_seq=512, max_batch=4, kv_blocks=128)
+        eng = B200Engine(ec, weights=w, model_config=cfg)
+        eng.load()
+        try:
+            r, res, tables = eng.runner, [], []
+            for i, p in enumerate(prompts):
+                bt = eng.scheduler.alloc.allocate((len(p) + 15) // 16 + 1)
+                tables.append(bt)
+                res.append(r.prefill([{"ids": p[:-1], "start": 0, "block_table": bt, "state_slot": i}])[0].float().cpu())
+            pos = [len(p) - 1 for p in prompts]
+            lg, _ = r.decode([p[-1] for p in prompts], pos, [bt[q // 16] * 16 + q % 16 for bt, q in zip(tables, pos)],
+                             tables, [q + 1 for q in pos], greedy=False, state_slots=[0, 1])
+            res += [row.float().cpu() for row in lg]
+            outs[device] = res
+        finally:
+            eng.unload()
+    for a, b in zip(outs["cuda"], outs["cpu"]):
+        assert _rel(a, b) < 3e-2
