@@ -12,7 +12,8 @@ The three built-in shapes are the configurations the benchmarks name:
   16 key / 32 value heads of 128), hidden 4096, SwiGLU 12288, vocab 248320.
 HF ``config.json`` files of the qwen2 / qwen3 / qwen3_moe / llama / mistral
 families map onto the same dataclass (Llama and Mistral are the Qwen2 block
-without q/k/v bias; their RoPE may carry a ``linear`` or ``llama3`` scaling).
+without q/k/v bias; their RoPE may carry a ``linear`` or ``llama3`` scaling;
+Mistral's ``sliding_window`` limits every layer's attention to that many keys).
 ``qwen3_5`` (the Qwen3.5 hybrid) adds per-layer kinds: Gated DeltaNet
 linear-attention layers and gated full-attention layers with partial RoPE;
 ``lfm2`` mixes gated short-convolution layers with attention layers.
@@ -51,7 +52,7 @@ class ModelConfig:
     family: str = ""                 # HF model_type this shape came from ("" = inferred)
     rope_scaling: Optional[dict] = None
     rotary_dim: int = 0              # 0 = whole head
-    sliding_window: int = 0          # 0 = none; contexts are capped at the window
+    sliding_window: int = 0          # keys per query of sliding-window layers (0 = none)
     # Qwen3.5 hybrid: per-layer kind, gated full attention, Gated DeltaNet (linear) layers
     layer_types: tuple = ()          # "full_attention" / "linear_attention" per layer; () = all full
     attn_output_gate: bool = False   # q_proj also emits a per-head sigmoid gate on the attention output
@@ -78,7 +79,13 @@ class ModelConfig:
         return bool(self.layer_types) and self.layer_types[i] == "conv"
 
     def has_kv(self, i: int) -> bool:
-        return not self.layer_types or self.layer_types[i] == "full_attention"
+        return not self.layer_types or self.layer_types[i] in ("full_attention", "sliding_attention")
+
+    def window(self, i: int) -> int:
+        """Sliding-window length of attention layer ``i`` (0 = full causal attention)."""
+        if self.layer_types:
+            return self.sliding_window if self.layer_types[i] == "sliding_attention" else 0
+        return self.sliding_window
 
     @property
     def lin_conv_dim(self) -> int:
@@ -190,8 +197,6 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
     theta, scaling = _rope_params(d)
     max_pos = d.get("max_position_embeddings", 40960)
     sw = d.get("sliding_window") or 0
-    if mt == "mistral" and sw and sw < max_pos:
-        max_pos = sw        # within the window, sliding-window attention equals full attention
     moe = mt == "qwen3_moe"
     hybrid = {}
     if mt == "qwen3_5_text":

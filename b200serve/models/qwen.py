@@ -88,6 +88,10 @@ class Decoder:
         for i in range(cfg.num_layers):
             self.kvi.append(n if cfg.has_kv(i) else -1)
             n += 1 if cfg.has_kv(i) else 0
+        # sliding-window length per K/V layer index (0 = full attention)
+        self.kv_window = [cfg.window(i) for i in range(cfg.num_layers) if cfg.has_kv(i)]
+        if any(self.kv_window) and getattr(kv_cache, "kv_format", "bf16") != "bf16":
+            raise NotImplementedError("sliding-window attention runs with the bf16 KV cache")
         self.lin_state = None
         if cfg.is_hybrid and getattr(kv_cache, "kv_format", "bf16") != "bf16":
             raise NotImplementedError("hybrid (DeltaNet / short-conv) models run with the bf16 KV cache")
@@ -271,10 +275,12 @@ class Decoder:
     def _attn_core(self, i, q, fb, plan):
         tps, nsplit, ws = plan
         kc, vc = self.kv.k[i], self.kv.v[i]
+        win = self.kv_window[i]
         if fb.is_decode:
-            return ops.paged_decode_attention(q, kc, vc, fb.block_tables, fb.seq_lens, self.scale, tps, nsplit, ws)
+            return ops.paged_decode_attention(q, kc, vc, fb.block_tables, fb.seq_lens, self.scale, tps, nsplit, ws,
+                                              window=win)
         return ops.paged_prefill_attention(q, kc, vc, fb.block_tables, fb.seq_lens, fb.q_start, fb.cu_q,
-                                           self.scale, max_q=fb.max_q)
+                                           self.scale, max_q=fb.max_q, window=win)
 
     def _attend(self, i, qkv, lw, fb, T, plan, tq_pre):
         """QKV post-processing, KV write and attention of layer ``i`` -> [T, nq, hd]."""

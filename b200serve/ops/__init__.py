@@ -604,8 +604,9 @@ _TC_PREFILL = os.environ.get("B200_TC_PREFILL", "1") != "0"         # tcgen05 pr
 
 
 def paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, scale, tps=256, nsplit=1,
-                           workspace=None, out=None):
-    """One query token per sequence. q [B, nq, hd]; seq_lens include the new token."""
+                           workspace=None, out=None, window=0):
+    """One query token per sequence. q [B, nq, hd]; seq_lens include the new token.
+    ``window`` > 0: sliding-window attention over the last ``window`` keys."""
     if _cuda(q, 2 if nsplit > 1 else 1):
         out = out if out is not None else torch.empty_like(q)
         if nsplit > 1:
@@ -615,12 +616,12 @@ def paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, scale, t
             acc = ml = torch.empty(0, dtype=torch.float32, device=q.device)
         B, nq, hd = q.shape
         G = nq // k_cache.shape[1]
-        if hd == 128 and G in (1, 2, 4, 8, 16) and not _FORCE_SIMT_DECODE:
+        if hd == 128 and G in (1, 2, 4, 8, 16) and not _FORCE_SIMT_DECODE and not window:
             ext().paged_decode_attention_tc(q, k_cache, v_cache, block_tables, seq_lens, out, acc, ml,
                                             float(scale), int(tps), int(nsplit))
         else:
             ext().paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, out, acc, ml,
-                                         float(scale), int(tps), int(nsplit))
+                                         float(scale), int(tps), int(nsplit), int(window))
         return out
     B, nq, hd = q.shape
     nkv = k_cache.shape[1]
@@ -635,6 +636,8 @@ def paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, scale, t
         v = v_cache[blocks].permute(1, 0, 2, 3).reshape(nkv, nb * 16, hd)[:, :L].float()
         qq = q[b].float().view(nkv, nq // nkv, hd)
         s = torch.einsum("kgd,ktd->kgt", qq, k) * scale
+        if window:
+            s[..., :max(0, L - window)] = float("-inf")
         p = torch.softmax(s, -1)
         res[b] = torch.einsum("kgt,ktd->kgd", p, v).reshape(nq, hd).to(q.dtype)
     if out is not None:
@@ -644,24 +647,25 @@ def paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, scale, t
 
 
 def paged_prefill_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, cu_q, scale, out=None,
-                            max_q=None):
+                            max_q=None, window=0):
     """Causal attention for chunks of new tokens against the paged cache.
 
     q [T, nq, hd] holds the new tokens of all sequences back to back; sequence i
     owns rows cu_q[i]:cu_q[i+1], whose absolute positions start at q_start[i];
     seq_lens[i] = q_start[i] + its new-token count (its K/V are already written).
+    ``window`` > 0: a query at position p sees keys (p - window, p] only.
     """
     if _cuda(q):
         out = out if out is not None else torch.empty_like(q)
         mq = int(max_q if max_q is not None else q.shape[0])
         G = q.shape[1] // k_cache.shape[1]
         if (_TC_PREFILL and q.shape[2] == 128 and k_cache.dtype == torch.bfloat16 and G in (1, 2, 4, 8)
-                and q.is_contiguous()):
+                and q.is_contiguous() and not window):
             ext().paged_prefill_attention_tc(q, k_cache, v_cache, block_tables, seq_lens, q_start, cu_q, out,
                                              float(scale), mq)
         else:
             ext().paged_prefill_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, cu_q, out,
-                                          float(scale), mq)
+                                          float(scale), mq, int(window))
         return out
     T, nq, hd = q.shape
     nkv = k_cache.shape[1]
@@ -683,6 +687,8 @@ def paged_prefill_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start
         s = torch.einsum("hnd,htd->hnt", qq, k) * scale
         pos = torch.arange(s0, s0 + (b_ - a))[:, None]
         mask = torch.arange(L)[None, :] > pos
+        if window:
+            mask |= torch.arange(L)[None, :] <= pos - window
         s = s.masked_fill(mask[None], float("-inf"))
         p = torch.softmax(s, -1)
         res[a:b_] = torch.einsum("hnt,htd->hnd", p, v).permute(1, 0, 2).to(q.dtype)

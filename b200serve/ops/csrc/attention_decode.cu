@@ -60,7 +60,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_cache,
     const __nv_bfloat16* __restrict__ v_cache, const int* __restrict__ block_tables,
     const int* __restrict__ seq_lens, int max_blocks, int nkv, float scale_log2, int tps,
-    float* __restrict__ part_acc, float* __restrict__ part_ml, __nv_bfloat16* __restrict__ out, int nsplit) {
+    float* __restrict__ part_acc, float* __restrict__ part_ml, __nv_bfloat16* __restrict__ out, int nsplit,
+    int window = 0) {
   constexpr int E = HD / 32;          // value dims per lane
   __shared__ float q_s[G][HD];
   __shared__ __align__(16) float p_s[kAttnWarps][kPage][G < 4 ? 4 : G];
@@ -73,8 +74,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int len = seq_lens[b];
   const int nq = nkv * G;
-  const int start = split * tps;
-  const int stop = min(len, start + tps);
+  // sliding window: keys [len - window, len) only; pages wholly before it are skipped
+  const int lo = window > 0 ? max(0, len - window) : 0;
+  const int start = max(split * tps, lo & ~(kPage - 1));
+  const int stop = min(len, split * tps + tps);
 
   for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
     const int g = i / HD, d = i % HD;
@@ -115,7 +118,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
         for (int j = 0; j < 8; ++j) s[g] = fmaf(q_s[g][chunk * 8 + j], kf[j], s[g]);
       }
     }
-    const bool valid = page_start + tok < stop;
+    const bool valid = page_start + tok < stop && page_start + tok >= lo;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       s[g] += __shfl_xor_sync(0xffffffffu, s[g], 16);
@@ -261,7 +264,7 @@ using namespace b200;
 void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                             torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
                             torch::Tensor part_acc, torch::Tensor part_ml, double scale, int64_t tps,
-                            int64_t nsplit) {
+                            int64_t nsplit, int64_t window) {
   const int B = q.size(0), nq = q.size(1), HD = q.size(2);
   const int nkv = k_cache.size(1);
   const int G = nq / nkv;
@@ -284,7 +287,7 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tenso
 #define B200_DEC(HDV, GV)                                                                                    \
   launch_pdl(paged_decode_kernel<HDV, GV>, grid, dim3(kAttnWarps * 32), 0, stream, qp, kp, vp,                \
              (const int*)block_tables.data_ptr<int>(), (const int*)seq_lens.data_ptr<int>(),                  \
-             (int)block_tables.size(1), nkv, sl2, (int)tps, pa, pm, op, (int)nsplit)
+             (int)block_tables.size(1), nkv, sl2, (int)tps, pa, pm, op, (int)nsplit, (int)window)
   if (HD == 256 && G == 4) B200_DEC(256, 4);
   else if (HD == 256 && G == 2) B200_DEC(256, 2);
   else if (HD == 256 && G == 1) B200_DEC(256, 1);

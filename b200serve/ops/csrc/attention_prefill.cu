@@ -45,7 +45,7 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(
     const __nv_bfloat16* __restrict__ v_cache, const int* __restrict__ block_tables, int max_blocks,
     const int* __restrict__ seq_lens, const int* __restrict__ q_start, const int* __restrict__ cu_q,
     __nv_bfloat16* __restrict__ out, int nq, int nkv, float scale_log2, const uint8_t* __restrict__ kq,
-    const uint8_t* __restrict__ vq, const __half* __restrict__ ksc, const __half* __restrict__ vsc) {
+    const uint8_t* __restrict__ vq, const __half* __restrict__ ksc, const __half* __restrict__ vsc, int window) {
   constexpr int LD = HD + 8;  // padded smem row (bf16) -> conflict-free 32-bit fragment loads
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);          // [2][64][LD]
@@ -89,6 +89,9 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(
   const int last_pos = pos0 + min(nrows, (qt + 1) * PF_BQ) - 1;
   const int kv_end = min(L, last_pos + 1);
   const int n_tiles = (kv_end + PF_BK - 1) / PF_BK;
+  // sliding window: a query at p sees keys (p - window, p]; tiles before the CTA's first
+  // query row's window are skipped
+  const int first_tile = window > 0 ? max(0, pos0 + qt * PF_BQ - window + 1) / PF_BK : 0;
   const int* bt = block_tables + (size_t)seq * max_blocks;
 
   auto load_tile = [&](int tile, int buf) {
@@ -129,9 +132,9 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(
     cp_async_commit();
   };
 
-  if (n_tiles > 0) load_tile(0, 0);
-  for (int tile = 0; tile < n_tiles; ++tile) {
-    const int buf = tile & 1;
+  if (n_tiles > first_tile) load_tile(first_tile, 0);
+  for (int tile = first_tile; tile < n_tiles; ++tile) {
+    const int buf = (tile - first_tile) & 1;
     if (tile + 1 < n_tiles) {
       load_tile(tile + 1, buf ^ 1);
       cp_async_wait<1>();
@@ -182,8 +185,10 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(
       for (int e = 0; e < 2; ++e) {
         const int kpos = tile * PF_BK + j * 8 + 2 * t4 + e;
         const bool valid_k = kpos < kv_end;
-        s[j][e] = (valid_k && kpos <= qpos_a) ? s[j][e] * scale_log2 : -INFINITY;
-        s[j][2 + e] = (valid_k && kpos <= qpos_b) ? s[j][2 + e] * scale_log2 : -INFINITY;
+        const bool in_a = kpos <= qpos_a && (window == 0 || kpos > qpos_a - window);
+        const bool in_b = kpos <= qpos_b && (window == 0 || kpos > qpos_b - window);
+        s[j][e] = (valid_k && in_a) ? s[j][e] * scale_log2 : -INFINITY;
+        s[j][2 + e] = (valid_k && in_b) ? s[j][2 + e] * scale_log2 : -INFINITY;
         mx_a = fmaxf(mx_a, s[j][e]);
         mx_b = fmaxf(mx_b, s[j][2 + e]);
       }
@@ -287,7 +292,7 @@ using namespace b200;
 static void prefill_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                          torch::Tensor seq_lens, torch::Tensor q_start, torch::Tensor cu_q, torch::Tensor out,
                          double scale, int64_t max_q, int kvq, const uint8_t* kq, const uint8_t* vq,
-                         const __half* ksc, const __half* vsc) {
+                         const __half* ksc, const __half* vsc, int window = 0) {
   const int T = q.size(0), nq = q.size(1), HD = q.size(2);
   const int nkv = k_cache.size(1);
   const int nseq = seq_lens.size(0);
@@ -310,7 +315,7 @@ static void prefill_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v
         reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()), (const int*)block_tables.data_ptr<int>(),   \
         (int)block_tables.size(1), (const int*)seq_lens.data_ptr<int>(), (const int*)q_start.data_ptr<int>(),    \
         (const int*)cu_q.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nq, nkv, sl2,       \
-        kq, vq, ksc, vsc);                                                                                      \
+        kq, vq, ksc, vsc, window);                                                                              \
   }
   if (kvq) {
     TORCH_CHECK(HD == 128, "int4 KV cache needs head_dim 128");
@@ -325,9 +330,9 @@ static void prefill_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v
 
 void paged_prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                              torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor q_start,
-                             torch::Tensor cu_q, torch::Tensor out, double scale, int64_t max_q) {
+                             torch::Tensor cu_q, torch::Tensor out, double scale, int64_t max_q, int64_t window) {
   prefill_impl(q, k_cache, v_cache, block_tables, seq_lens, q_start, cu_q, out, scale, max_q, 0, nullptr, nullptr,
-               nullptr, nullptr);
+               nullptr, nullptr, (int)window);
 }
 
 // int4g128 cache: k_codes/v_codes [blocks][nkv][16][64] uint8, k_scale/v_scale [blocks][nkv][16] fp16.

@@ -26,10 +26,10 @@ void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
 void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                             torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
                             torch::Tensor part_acc, torch::Tensor part_ml, double scale, int64_t tps,
-                            int64_t nsplit);
+                            int64_t nsplit, int64_t window);
 void paged_prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                              torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor q_start,
-                             torch::Tensor cu_q, torch::Tensor out, double scale, int64_t max_q);
+                             torch::Tensor cu_q, torch::Tensor out, double scale, int64_t max_q, int64_t window);
 void paged_decode_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                                torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
                                torch::Tensor part_acc, torch::Tensor part_ml, double scale, int64_t tps,

@@ -248,3 +248,31 @@ def test_lfm2_engine_gpu_matches_cpu():
             eng.unload()
     for a, b in zip(outs["cuda"], outs["cpu"]):
         assert _rel(a, b) < 3e-2
+
+
+@pytest.mark.parametrize("hd,nq,nkv", [(128, 8, 2), (256, 8, 4), (64, 4, 2)])
+def test_sliding_window_attention(hd, nq, nkv):
+    W = 48
+    lens = [5, 100, 333]
+    B = len(lens)
+    kc, vc, bt = _make_paged(B, lens, nkv, hd, 256)
+    q = torch.randn(B, nq, hd, device=dev).bfloat16()
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    scale = 1 / math.sqrt(hd)
+    ws = ops.AttnWorkspace(dev, B, nkv, nq // nkv, hd, 4)
+    ref = ops.paged_decode_attention(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), sl.cpu(), scale, window=W)
+    for tps, ns in ((128, 3), (4096, 1)):
+        y = ops.paged_decode_attention(q, kc, vc, bt, sl, scale, tps, ns, ws if ns > 1 else None, window=W)
+        assert _rel(y.cpu(), ref) < 1e-2
+    chunks = [(0, 100), (37, 50), (0, 300)]
+    plens = [s + n for s, n in chunks]
+    kc, vc, bt = _make_paged(3, plens, nkv, hd, 256)
+    T = sum(n for _, n in chunks)
+    qp = torch.randn(T, nq, hd, device=dev).bfloat16()
+    cu = torch.tensor([0, 100, 150, 450], dtype=torch.int32, device=dev)
+    q_start = torch.tensor([0, 37, 0], dtype=torch.int32, device=dev)
+    psl = torch.tensor(plens, dtype=torch.int32, device=dev)
+    yp = ops.paged_prefill_attention(qp, kc, vc, bt, psl, q_start, cu, scale, max_q=300, window=W)
+    refp = ops.paged_prefill_attention(qp.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), psl.cpu(), q_start.cpu(), cu.cpu(),
+                                       scale, window=W)
+    assert _rel(yp.cpu(), refp) < 1e-2

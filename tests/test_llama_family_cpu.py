@@ -81,8 +81,36 @@ def test_rope_scaling_tables_match_hf():
         assert torch.allclose(inv, inv_hf.float(), rtol=1e-6, atol=0), case
 
 
-def test_mistral_window_caps_context():
+def test_mistral_sliding_window_matches_hf():
+    """Mistral with a 16-token sliding window: a 100-token prompt and greedy decode attend to
+    the last 16 keys only, as in HF."""
     cfg = from_hf_config(dict(_BASE, model_type="mistral", sliding_window=256, rope_theta=1e4))
-    assert cfg.max_position == 256 and cfg.sliding_window == 256
+    assert cfg.max_position == 512 and cfg.sliding_window == 256 and cfg.window(0) == 256
     with pytest.raises(NotImplementedError):
         from_hf_config(dict(_BASE, model_type="gpt2"))
+    d = dict(_BASE, rope_theta=10000.0, sliding_window=16)
+    hf_cfg = transformers.MistralConfig(**d)
+    hf_cfg._attn_implementation = "eager"
+    torch.manual_seed(0)
+    model = transformers.MistralForCausalLM(hf_cfg).eval()
+    cfg = from_hf_config(dict(json.loads(hf_cfg.to_json_string()), model_type="mistral"), "mistral-sw")
+    assert cfg.window(1) == 16
+    sd = {k: v.detach().clone() for k, v in model.state_dict().items()}
+    w = load_hf_state_dict(cfg, sd, dtype=torch.float32, device="cpu")
+    prompt = torch.randint(3, 1000, (100,), generator=torch.Generator().manual_seed(1)).tolist()
+    with torch.no_grad():
+        ref_logits = model(torch.tensor([prompt])).logits[0, -1]
+        hf = model.generate(torch.tensor([prompt]), max_new_tokens=10, min_new_tokens=10, do_sample=False,
+                            pad_token_id=0)[0, len(prompt):].tolist()
+    eng = B200Engine(EngineConfig(model="mistral-sw", device="cpu", dtype="float32", cuda_graphs=False,
+                                  max_seq=256, max_batch=2), weights=w, model_config=cfg)
+    eng.load()
+    try:
+        bt = eng.scheduler.alloc.allocate(8)
+        logits = eng.runner.prefill([{"ids": prompt, "start": 0, "block_table": bt}])
+        eng.scheduler.alloc.release(bt)
+        assert torch.allclose(logits[0], ref_logits, atol=1e-4, rtol=1e-4)
+        [req] = eng.generate([prompt], SamplingParams(temperature=0.0, max_tokens=10, ignore_eos=True))
+    finally:
+        eng.unload()
+    assert req.output == hf
