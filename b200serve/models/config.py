@@ -16,7 +16,9 @@ without q/k/v bias; their RoPE may carry a ``linear`` or ``llama3`` scaling;
 Mistral's ``sliding_window`` limits every layer's attention to that many keys).
 ``qwen3_5`` (the Qwen3.5 hybrid) adds per-layer kinds: Gated DeltaNet
 linear-attention layers and gated full-attention layers with partial RoPE;
-``lfm2`` mixes gated short-convolution layers with attention layers.
+``lfm2`` mixes gated short-convolution layers with attention layers; ``gemma`` and
+``gemma3`` bring GeGLU, scaled embeddings, (1 + w) norms and, for Gemma 3, sliding-window
+layers with their own RoPE base and norms on each sub-block's output.
 """
 
 from __future__ import annotations
@@ -62,6 +64,13 @@ class ModelConfig:
     lin_k_dim: int = 0
     lin_v_dim: int = 0
     conv_kernel: int = 0
+    # Gemma: sqrt(H)-scaled embeddings, GeGLU, query_pre_attn_scalar, local RoPE base,
+    # and (Gemma 3) norms on the attention and MLP outputs before their residual adds
+    embed_scale: float = 0.0         # 0 = unscaled
+    attn_scale: float = 0.0          # 0 = head_dim ** -0.5
+    act: str = "silu"                # "silu" (SwiGLU) or "gelu_tanh" (GeGLU)
+    rope_local_theta: float = 0.0    # RoPE base of sliding-window layers (0 = rope_theta)
+    sandwich_norms: bool = False
 
     @property
     def is_moe(self) -> bool:
@@ -169,7 +178,7 @@ BUILTIN = {
 }
 
 
-_FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "llama", "mistral", "qwen3_5_text", "lfm2")
+_FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "llama", "mistral", "qwen3_5_text", "lfm2", "gemma", "gemma3_text")
 
 
 def _rope_params(d: dict):
@@ -184,9 +193,13 @@ def _rope_params(d: dict):
 
 
 def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
-    if d.get("model_type") == "qwen3_5" or "text_config" in d:
+    if d.get("model_type") in ("qwen3_5", "gemma3") or "text_config" in d:
         # the multimodal checkpoint wraps the text decoder; its language model is served alone
-        d = dict(d["text_config"], model_type="qwen3_5_text")
+        inner = {"qwen3_5": "qwen3_5_text", "gemma3": "gemma3_text"}.get(d.get("model_type"), None)
+        d = dict(d["text_config"])
+        d["model_type"] = inner or d.get("model_type", "qwen2")
+    if d.get("model_type") == "gemma2":
+        raise NotImplementedError("gemma2 (attention logit softcapping) is not supported")
     mt = d.get("model_type", "qwen2")
     if mt not in _FAMILIES:
         raise NotImplementedError(f"model_type {mt!r}: supported families are {', '.join(_FAMILIES)}")
@@ -195,6 +208,15 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
     heads = d["num_attention_heads"]
     hd = d.get("head_dim") or d["hidden_size"] // heads
     theta, scaling = _rope_params(d)
+    local_theta = 0.0
+    rp = d.get("rope_parameters") or {}
+    if "full_attention" in rp or "sliding_attention" in rp:     # per-layer-type RoPE (transformers 5)
+        full = rp.get("full_attention") or {}
+        theta = float(full.get("rope_theta", theta))
+        scaling = dict(full) if full.get("rope_type", "default") != "default" else None
+        local_theta = float((rp.get("sliding_attention") or {}).get("rope_theta", 0.0))
+    elif d.get("rope_local_base_freq"):
+        local_theta = float(d["rope_local_base_freq"])
     max_pos = d.get("max_position_embeddings", 40960)
     sw = d.get("sliding_window") or 0
     moe = mt == "qwen3_moe"
@@ -211,6 +233,22 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
                       lin_k_dim=d.get("linear_key_head_dim", 128), lin_v_dim=d.get("linear_value_head_dim", 128),
                       conv_kernel=d.get("linear_conv_kernel_dim", 4), rotary_dim=int(hd_full * prf))
     inter = d.get("intermediate_size", 0)
+    if mt in ("gemma", "gemma3_text"):
+        if d.get("attn_logit_softcapping") or d.get("final_logit_softcapping"):
+            raise NotImplementedError("logit softcapping")
+        act = d.get("hidden_activation") or d.get("hidden_act") or "gelu_pytorch_tanh"
+        if act not in ("gelu_pytorch_tanh", "gelu"):
+            raise NotImplementedError(f"activation {act}")
+        heads_ = d["num_attention_heads"]
+        hd_ = d.get("head_dim") or d["hidden_size"] // heads_
+        hybrid = dict(norm_offset=True, embed_scale=float(d["hidden_size"]) ** 0.5, act="gelu_tanh",
+                      attn_scale=float(d.get("query_pre_attn_scalar") or hd_) ** -0.5)
+        if mt == "gemma3_text":
+            n = d["num_hidden_layers"]
+            every = d.get("sliding_window_pattern", 6)
+            lt = d.get("layer_types") or ["full_attention" if (i + 1) % every == 0 else "sliding_attention"
+                                          for i in range(n)]
+            hybrid.update(layer_types=tuple(lt), sandwich_norms=True, rope_local_theta=local_theta)
     if mt == "lfm2":
         n = d["num_hidden_layers"]
         full = d.get("full_attn_idxs")
@@ -230,7 +268,7 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         intermediate_size=inter, rms_eps=d.get("rms_norm_eps", d.get("norm_eps", 1e-6)),
         rope_theta=theta, rope_scaling=scaling,
         attn_bias=(mt == "qwen2") or bool(d.get("attention_bias", False)),
-        qk_norm=mt in ("qwen3", "qwen3_moe", "qwen3_5_text", "lfm2"),
+        qk_norm=mt in ("qwen3", "qwen3_moe", "qwen3_5_text", "lfm2", "gemma3_text"),
         tie_embeddings=bool(d.get("tie_word_embeddings", False)),
         num_experts=d.get("num_experts", 0) if moe else 0,
         experts_per_tok=d.get("num_experts_per_tok", 0) if moe else 0,
@@ -239,7 +277,7 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         max_position=max_pos,
         bos_token_id=d.get("bos_token_id") or 1,
         eos_token_id=(d.get("eos_token_id") if isinstance(d.get("eos_token_id"), int) else 2),
-        family=mt, sliding_window=sw if mt == "mistral" else 0, **hybrid,
+        family=mt, sliding_window=sw if mt in ("mistral", "gemma3_text") else 0, **hybrid,
     )
 
 

@@ -77,9 +77,14 @@ class Decoder:
         self.nq = cfg.num_heads // tp
         self.nkv = max(1, cfg.num_kv_heads // tp)   # KV heads replicated when tp > num_kv_heads
         self.hd = cfg.head_dim
-        self.scale = ops.softmax_scale(cfg.head_dim)
+        self.scale = cfg.attn_scale or ops.softmax_scale(cfg.head_dim)
         self.cos_sin = ops.rope_cos_sin(cfg.head_dim, cfg.max_position, cfg.rope_theta, self.device,
                                        rot_dim=cfg.rotary_dim, scaling=cfg.rope_scaling)
+        # sliding-window layers may rotate with their own base (Gemma 3's local layers)
+        local = ops.rope_cos_sin(cfg.head_dim, cfg.max_position, cfg.rope_local_theta, self.device,
+                                 rot_dim=cfg.rotary_dim) if cfg.rope_local_theta else self.cos_sin
+        self.kv_cos = [local if cfg.window(i) and cfg.rope_local_theta else self.cos_sin
+                       for i in range(cfg.num_layers) if cfg.has_kv(i)]
         self.attn_ws = None
         self.moe = None
         self.tq = None
@@ -145,7 +150,7 @@ class Decoder:
         kst = torch.empty(nblk, self.nkv, 16, self.hd, dtype=qkv.dtype, device=qkv.device)
         vst = torch.empty_like(kst)
         stage_slots = torch.arange(T, dtype=torch.int32, device=qkv.device)
-        q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, stage_slots, kst, vst,
+        q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.kv_cos[i], fb.positions, stage_slots, kst, vst,
                          self.nq, self.nkv, eps, hd=self.hd)
         q_rot, q_jl = ops.tq_qkv(q, kst, vst, fb.slots, tb, kv, i)
         if fb.is_decode:
@@ -197,7 +202,7 @@ class Decoder:
         if qkv.is_cuda:
             q = torch.empty(T, self.nq, self.hd, dtype=qkv.dtype, device=qkv.device)
             ops._cuda(qkv)
-            ops.ext().qkv_post_q4(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots, q, kc, vc,
+            ops.ext().qkv_post_q4(qkv, None, lw.q_norm, lw.k_norm, self.kv_cos[i], fb.positions, fb.slots, q, kc, vc,
                                   ksc, vsc, self.nq, self.nkv, eps)
             out = torch.empty_like(q)
             if fb.is_decode:
@@ -221,7 +226,7 @@ class Decoder:
         # CPU: quantise the new rows into the cache, attend over dequantised pages
         kb = torch.zeros(kc.shape[0], self.nkv, 16, self.hd, dtype=torch.float32)
         vb = torch.zeros_like(kb)
-        q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots, kb, vb, self.nq,
+        q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.kv_cos[i], fb.positions, fb.slots, kb, vb, self.nq,
                          self.nkv, eps, hd=self.hd)
         sl = fb.slots.long()
         ok = sl >= 0
@@ -242,7 +247,7 @@ class Decoder:
         plain = not self.cfg.attn_output_gate and self.cos_sin.shape[1] == self.hd
         if plain and self.tq is None and self.kv.kv_format == "bf16" and ops.qkv_fused_ok(x, lw.qkv, self.kv.k[i]):
             kc, vc = self.kv.k[i], self.kv.v[i]
-            q = ops.qkv_fused(x, lw.qkv, lw.qkv_bias, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots,
+            q = ops.qkv_fused(x, lw.qkv, lw.qkv_bias, lw.q_norm, lw.k_norm, self.kv_cos[i], fb.positions, fb.slots,
                               kc, vc, self.nq, self.nkv, self.cfg.rms_eps, ag=ag)
             return self._attn_core(i, q, fb, plan)
         qkv = ops.linear(x, lw.qkv, bias=lw.qkv_bias, ag=ag)
@@ -291,7 +296,7 @@ class Decoder:
         if self.kv.kv_format == "int4g128":
             return self._attention_q4(i, qkv, lw, fb, T, tps, nsplit, ws, tq_pre)
         kc, vc = self.kv.k[i], self.kv.v[i]
-        q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.cos_sin, fb.positions, fb.slots, kc, vc,
+        q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.kv_cos[i], fb.positions, fb.slots, kc, vc,
                          self.nq, self.nkv, eps, hd=self.hd)
         return self._attn_core(i, q, fb, plan)
 
@@ -348,8 +353,8 @@ class Decoder:
         quant_kv = self.tq is not None or (self.kv.kv_format == "int4g128" and h.is_cuda and ops._TC_PREFILL)
         tq_pre = self._tq_prefill_pages(fb) if (quant_kv and not fb.is_decode) else None
         plan = (tps, nsplit, ws) if fb.is_decode else (0, 0, None)
-        if self.moe is None and not cfg.is_hybrid and comm.world > 1 and hasattr(comm, "use_rsag") and \
-                comm.use_rsag(T):
+        if self.moe is None and not cfg.is_hybrid and not cfg.sandwich_norms and cfg.act == "silu" and \
+                comm.world > 1 and hasattr(comm, "use_rsag") and comm.use_rsag(T):
             return self._forward_rsag(fb, h, plan, tq_pre)
         residual = torch.empty_like(h)
         x = ops.rmsnorm([h], w.layers[0].input_norm, eps, residual_out=residual)
@@ -367,12 +372,19 @@ class Decoder:
             else:
                 attn = self._qkv_attend(self.kvi[i], x, lw, fb, T, plan, tq_pre)
                 o_parts = self._row_parallel(attn.view(T, self.nq * self.hd), lw.o, "o")
+            if lw.attn_out_norm is not None:      # Gemma 3: normalise the sub-block output first
+                o_parts = [ops.rmsnorm(o_parts, lw.attn_out_norm, eps)]
             x = ops.rmsnorm(o_parts, lw.post_norm, eps, residual=residual, residual_out=residual)
             if self.moe is not None:
                 mlp_parts = self.moe.reduced(i, x)
+            elif cfg.act == "gelu_tanh":
+                act = ops.gelu_tanh_mul(ops.linear(x, lw.gate_up))
+                mlp_parts = self._row_parallel(act, lw.down, "mlp")
             else:
                 act = ops.linear(x, lw.gate_up, epilogue=ops.EPI_SWIGLU)
                 mlp_parts = self._row_parallel(act, lw.down, "mlp")
+            if lw.mlp_out_norm is not None:
+                mlp_parts = [ops.rmsnorm(mlp_parts, lw.mlp_out_norm, eps)]
             if _NVTX:
                 torch.cuda.nvtx.range_pop()
         rows = fb.logit_rows

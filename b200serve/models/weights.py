@@ -69,6 +69,8 @@ class LayerWeights:
     conv_w: torch.Tensor = None        # [conv_dim_local, K] fp32
     lin_A: torch.Tensor = None         # [nv_local] fp32, -exp(A_log)
     lin_dt: torch.Tensor = None        # [nv_local] fp32
+    attn_out_norm: torch.Tensor = None  # Gemma 3: norm of the attention output before its residual add
+    mlp_out_norm: torch.Tensor = None   # Gemma 3: norm of the MLP output before its residual add
 
 
 @dataclass
@@ -138,12 +140,14 @@ def shard_layer_dense(cfg: ModelConfig, full: dict, rank: int, size: int, dtype,
     o = full["o"]
     oc = o.shape[1] // size
     o = o[:, rank * oc:(rank + 1) * oc]
-    norms = {k_: full.get(k_) for k_ in ("input_norm", "post_norm", "q_norm", "k_norm")}
+    norms = {k_: full.get(k_) for k_ in ("input_norm", "post_norm", "q_norm", "k_norm", "attn_out_norm",
+                                          "mlp_out_norm")}
     if cfg.norm_offset:
         from b200serve.models.hybrid import offset_norm
         norms = {k_: (offset_norm(t) if t is not None else None) for k_, t in norms.items()}
     lw = LayerWeights(input_norm=norms["input_norm"], post_norm=norms["post_norm"], qkv=qkv, o=o, qkv_bias=bias,
-                      q_norm=norms["q_norm"], k_norm=norms["k_norm"])
+                      q_norm=norms["q_norm"], k_norm=norms["k_norm"], attn_out_norm=norms["attn_out_norm"],
+                      mlp_out_norm=norms["mlp_out_norm"])
     if not cfg.is_moe:
         I = cfg.intermediate_size
         assert I % size == 0
@@ -187,6 +191,8 @@ def build_weights(cfg: ModelConfig, layer_source, embed, lm_head, final_norm, tp
     if cfg.norm_offset:
         from b200serve.models.hybrid import offset_norm
         final_norm = offset_norm(final_norm)
+    if cfg.embed_scale:     # Gemma: the lookup table is pre-scaled; a tied lm_head keeps the plain one
+        embed = embed.float() * cfg.embed_scale
     return ModelWeights(
         embed=embed.to(device=device, dtype=dtype).contiguous(),
         final_norm=final_norm.to(device=device, dtype=dtype).contiguous(),
@@ -232,6 +238,8 @@ def random_weights(cfg: ModelConfig, seed=0, std=0.02, tp_rank=0, tp_size=1, ep_
             qrows = cfg.q_size * (2 if cfg.attn_output_gate else 1)
             d = {"q": n(qrows, H), "k": n(cfg.kv_size, H), "v": n(cfg.kv_size, H), "o": n(H, cfg.q_size),
                  "input_norm": one(H), "post_norm": one(H)}
+            if cfg.sandwich_norms:
+                d.update(attn_out_norm=one(H), mlp_out_norm=one(H))
             if cfg.attn_bias:
                 d.update(q_bias=torch.zeros(cfg.q_size, dtype=dtype, device=gen_dev),
                          k_bias=torch.zeros(cfg.kv_size, dtype=dtype, device=gen_dev),
@@ -265,6 +273,11 @@ def hf_layer_dict(get, cfg: ModelConfig, i: int) -> dict:
     """Collect layer ``i`` from an HF-named tensor getter (``get(name)`` -> tensor or None)."""
     pre = f"model.layers.{i}."
     d = {}
+    if cfg.sandwich_norms:      # Gemma 3 names its four norms differently
+        for k, name in (("attn_out_norm", "post_attention_layernorm.weight"),
+                        ("post_norm", "pre_feedforward_layernorm.weight"),
+                        ("mlp_out_norm", "post_feedforward_layernorm.weight")):
+            d[k] = get(pre + name)
     if cfg.family == "lfm2":
         from b200serve.models.hybrid import LFM2_KEYS
         for k, name in LFM2_KEYS.items():
@@ -277,6 +290,8 @@ def hf_layer_dict(get, cfg: ModelConfig, i: int) -> dict:
         for k, name in LIN_KEYS.items():
             d[k] = get(pre + name)
     for k, name in _HF_LAYER_KEYS.items():
+        if k in d:
+            continue
         t = get(pre + name)
         if t is not None:
             d[k] = t

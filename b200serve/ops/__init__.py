@@ -336,6 +336,22 @@ def silu_mul(gu, out=None):
     return r
 
 
+def gelu_tanh_mul(gu, out=None):
+    """act = gelu_tanh(gate) * up (GeGLU) on the 64-column interleaved [g|u] layout."""
+    I = gu.shape[-1] // 2
+    if _cuda(gu):
+        out = out if out is not None else torch.empty(*gu.shape[:-1], I, dtype=gu.dtype, device=gu.device)
+        ext().gelu_tanh_mul(gu, out)
+        return out
+    v = gu.view(*gu.shape[:-1], I // 64, 2, 64)
+    g, u = v[..., 0, :].reshape(*gu.shape[:-1], I), v[..., 1, :].reshape(*gu.shape[:-1], I)
+    r = (torch.nn.functional.gelu(g.float(), approximate="tanh").to(gu.dtype) * u)
+    if out is not None:
+        out.copy_(r)
+        return out
+    return r
+
+
 def embedding(ids, table, out=None):
     if _cuda(table):
         out = out if out is not None else torch.empty(ids.numel(), table.shape[1], dtype=table.dtype,
