@@ -276,3 +276,46 @@ def test_sliding_window_attention(hd, nq, nkv):
     refp = ops.paged_prefill_attention(qp.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), psl.cpu(), q_start.cpu(), cu.cpu(),
                                        scale, window=W)
     assert _rel(yp.cpu(), refp) < 1e-2
+
+
+def test_gelu_tanh_mul_matches_fp32():
+    gu = torch.randn(37, 2 * 512, device=dev).bfloat16()
+    out = ops.gelu_tanh_mul(gu)
+    ref = ops.gelu_tanh_mul(gu.cpu().float())
+    assert _rel(out.cpu(), ref) < 1e-2
+
+
+def test_gemma3_engine_gpu_matches_cpu():
+    """Tiny Gemma 3 (sliding-window + global layers, head_dim 256, GeGLU, sub-block norms)
+    on the GPU against the CPU fp32 path: prefill, then one batched decode step."""
+    from b200serve.core.config import EngineConfig
+    from b200serve.engine.b200_engine import B200Engine
+    from b200serve.models.config import ModelConfig
+    from b200serve.models.weights import random_weights
+    cfg = ModelConfig("tiny-gemma3", 2048, 512, 6, 4, 2, 256, 1024, rope_theta=1e6, qk_norm=True, max_position=2048,
+                      layer_types=("sliding_attention",) * 5 + ("full_attention",), sliding_window=64,
+                      norm_offset=True, embed_scale=512 ** 0.5, attn_scale=256 ** -0.5, act="gelu_tanh",
+                      rope_local_theta=1e4, sandwich_norms=True, family="gemma3_text", tie_embeddings=True)
+    prompts = [torch.randint(3, 2048, (n,), generator=torch.Generator().manual_seed(n)).tolist() for n in (40, 200)]
+    outs = {}
+    for device, dtype in (("cpu", torch.float32), ("cuda", torch.bfloat16)):
+        w = _moved(random_weights(cfg, seed=3, std=0.05, dtype=torch.float32, device="cpu"), device, dtype)
+        ec = EngineConfig(model="tiny-gemma3", device=device, dtype="float32" if device == "cpu" else "bfloat16",
+                          cuda_graphs=device == "cuda", max_seq=512, max_batch=4, kv_blocks=128)
+        eng = B200Engine(ec, weights=w, model_config=cfg)
+        eng.load()
+        try:
+            r, res, tables = eng.runner, [], []
+            for p in prompts:
+                bt = eng.scheduler.alloc.allocate((len(p) + 15) // 16 + 1)
+                tables.append(bt)
+                res.append(r.prefill([{"ids": p[:-1], "start": 0, "block_table": bt}])[0].float().cpu())
+            pos = [len(p) - 1 for p in prompts]
+            lg, _ = r.decode([p[-1] for p in prompts], pos, [bt[q // 16] * 16 + q % 16 for bt, q in zip(tables, pos)],
+                             tables, [q + 1 for q in pos], greedy=False)
+            res += [row.float().cpu() for row in lg]
+            outs[device] = res
+        finally:
+            eng.unload()
+    for a, b in zip(outs["cuda"], outs["cpu"]):
+        assert _rel(a, b) < 3e-2
