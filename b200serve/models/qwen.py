@@ -275,7 +275,7 @@ class Decoder:
         q_start = fb.positions if fb.is_decode else fb.q_start
         return ops.deltanet_layer(y, lw.conv_w, lw.lin_A, lw.lin_dt, lw.lin_norm, st.conv[i], st.rec[i], cu, q_start,
                                   fb.state_slots, cfg.lin_k_heads // tp, cfg.lin_v_heads // tp, cfg.lin_k_dim,
-                                  cfg.rms_eps)
+                                  cfg.rms_eps, max_q=0 if fb.is_decode else fb.max_q)
 
     def _attn_core(self, i, q, fb, plan):
         tps, nsplit, ws = plan

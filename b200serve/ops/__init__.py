@@ -210,23 +210,31 @@ def qkv_post(qkv, bias, q_norm, k_norm, cos_sin, positions, slots, k_cache, v_ca
 
 
 # ------------------------------------------------------------------ Gated DeltaNet
+DN_CHUNK_MIN = int(os.environ.get("B200_DN_CHUNK_MIN", "64"))
+
+
 def deltanet_layer(y, conv_w, A, dt_bias, norm_w, conv_state, rec_state, cu_q, q_start, slots, nk, nv, D,
-                   eps):
+                   eps, max_q=0):
     """Token mixing of a Gated DeltaNet layer after its fused input projection
     ``y`` [T, (2 nk + nv) D + nv D + 2 nv] = [q | k | v | z | b | a]: causal depthwise conv
     (state carried in ``conv_state`` [slots, conv_dim, K-1] fp32), SiLU, L2-normalised q/k,
     the gated delta-rule recurrence (state ``rec_state`` [slots, nv, D, D] fp32) and the
     gated RMSNorm with ``norm_w``. ``cu_q`` None means one token per sequence (decode); a
     sequence whose ``q_start`` is 0 starts from zero state. Returns [T, nv * D].
+    Prefill batches whose longest sequence has ``max_q`` >= DN_CHUNK_MIN tokens take the
+    chunked kernel (64-token chunks, the recurrence's sequential part shrinks 64-fold);
+    decode and short batches take the token-by-token scan.
     Reference behaviour: shaders/ssm_step.wgsl:1-12, conv1d.wgsl:28-82, l2norm.wgsl:14."""
     T = y.shape[0]
     conv_dim = (2 * nk + nv) * D
-    if _cuda(y, 2):
+    chunked = cu_q is not None and max_q >= DN_CHUNK_MIN
+    if _cuda(y, 3 if chunked else 2):
         xc = torch.empty(T, conv_dim, dtype=y.dtype, device=y.device)
         gb = torch.empty(T, nv, 2, dtype=torch.float32, device=y.device)
         out = torch.empty(T, nv * D, dtype=y.dtype, device=y.device)
+        o_raw = torch.empty(T, nv * D, dtype=torch.float32, device=y.device) if chunked else None
         ext().deltanet_layer(y, conv_w, A, dt_bias, norm_w, conv_state, rec_state, cu_q, q_start, slots, xc, gb,
-                             out, nk, nv, D, float(eps))
+                             out, nk, nv, D, float(eps), o_raw)
         return out
     return _deltanet_cpu(y, conv_w, A, dt_bias, norm_w, conv_state, rec_state, cu_q, q_start, slots, nk, nv, D,
                          eps)

@@ -111,7 +111,8 @@ void q4_dequant_pages(torch::Tensor block_ids, torch::Tensor codes, torch::Tenso
 void deltanet_layer(torch::Tensor y, torch::Tensor conv_w, torch::Tensor A, torch::Tensor dt_bias,
                     torch::Tensor norm_w, torch::Tensor conv_state, torch::Tensor rec_state,
                     c10::optional<torch::Tensor> cu_q, torch::Tensor q_start, torch::Tensor slots, torch::Tensor xc,
-                    torch::Tensor gb, torch::Tensor out, int64_t nk, int64_t nv, int64_t D, double eps);
+                    torch::Tensor gb, torch::Tensor out, int64_t nk, int64_t nv, int64_t D, double eps,
+                    c10::optional<torch::Tensor> o_raw);
 void sigmoid_gate_mul(torch::Tensor attn, torch::Tensor gate);
 void shortconv_layer(torch::Tensor y, torch::Tensor conv_w, torch::Tensor conv_state,
                      c10::optional<torch::Tensor> cu_q, torch::Tensor q_start, torch::Tensor slots,

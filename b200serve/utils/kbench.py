@@ -420,6 +420,40 @@ def decode_parts(layers=8, B=32, ctx=2304, tp=1):
     print(json.dumps(out))
 
 
+def deltanet_one(S=32, T_per=1, nk=16, nv=32, D=128, iters=3):
+    """Gated DeltaNet token mixing (prep + scan) of one layer of the Qwen3.5-9B shape:
+    S sequences with T_per new tokens each (T_per = 1 is a decode step). Decode reads and
+    writes each sequence's fp32 state (nv x D x D) once; reported as GB/s of state traffic."""
+    dev = "cuda"
+    T = S * T_per
+    conv_dim = (2 * nk + nv) * D
+    W = conv_dim + nv * D + 2 * nv
+    y = (torch.randn(T, W, device=dev) * 0.5).bfloat16()
+    conv_w = torch.randn(conv_dim, 4, device=dev) * 0.3
+    A = -torch.rand(nv, device=dev) * 4
+    dt = torch.randn(nv, device=dev) * 0.5
+    nw = torch.ones(D, device=dev).bfloat16()
+    cs = torch.zeros(S + 1, conv_dim, 3, device=dev)
+    rs = torch.zeros(S + 1, nv, D, D, device=dev)
+    slots = torch.arange(S, dtype=torch.int32, device=dev)
+    if T_per == 1:
+        cu, qs = None, torch.full((S,), 100, dtype=torch.int32, device=dev)
+    else:
+        cu = torch.arange(0, T + 1, T_per, dtype=torch.int32, device=dev)
+        qs = torch.zeros(S, dtype=torch.int32, device=dev)
+    run = lambda: ops.deltanet_layer(y, conv_w, A, dt, nw, cs, rs, cu, qs, slots, nk, nv, D, 1e-6)
+    for _ in range(iters):
+        run()
+    torch.cuda.synchronize()
+    ms = time_cuda(run)
+    state = S * nv * D * D * 4 * (2 if T_per == 1 else 1)
+    hbm, _, src = peaks()
+    print(json.dumps({"case": "deltanet_one", "S": S, "T_per": T_per, "ms": round(ms, 4),
+                      "us_per_token": round(ms * 1e3 / T_per, 2),
+                      "state_GBps": round(state / ms / 1e6, 1) if T_per == 1 else None,
+                      "frac_hbm": round(state / ms / 1e6 / hbm, 3) if T_per == 1 else None, "peaks": src}))
+
+
 if __name__ == "__main__":
     what = sys.argv[1] if len(sys.argv) > 1 else "all"
     ops.ext()
@@ -449,6 +483,9 @@ if __name__ == "__main__":
         sys.exit(0)
     if what == "decode_parts":
         decode_parts(*[int(v) for v in sys.argv[2:6]])
+        sys.exit(0)
+    if what == "deltanet_one":
+        deltanet_one(*[int(v) for v in sys.argv[2:4]])
         sys.exit(0)
     if what == "decode_step":
         decode_step(*[int(v) for v in sys.argv[2:5]])

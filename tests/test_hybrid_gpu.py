@@ -38,8 +38,10 @@ def _dn_inputs(T, nk, nv, D, slots_n):
     return y, conv_w, A, dt, nw, cs, rs
 
 
+@pytest.mark.parametrize("chunked", [False, True])
 @pytest.mark.parametrize("nk,nv,D", [(16, 32, 128), (2, 4, 32), (4, 4, 64)])
-def test_deltanet_prefill_and_decode_match_fp32(nk, nv, D):
+def test_deltanet_prefill_and_decode_match_fp32(nk, nv, D, chunked):
+    """Prefill through the token-by-token scan or the 64-token chunked kernel, then decode."""
     # prefill: three sequences, the second continues from a stored state (start > 0)
     lens, starts, slots = [37, 5, 130], [0, 64, 0], [2, 0, 5]
     T = sum(lens)
@@ -48,7 +50,8 @@ def test_deltanet_prefill_and_decode_match_fp32(nk, nv, D):
     qs = torch.tensor(starts, dtype=torch.int32, device=dev)
     sl = torch.tensor(slots, dtype=torch.int32, device=dev)
     cs_ref, rs_ref = cs.cpu().clone(), rs.cpu().clone()
-    out = ops.deltanet_layer(y, conv_w, A, dt, nw, cs, rs, cu, qs, sl, nk, nv, D, 1e-6)
+    out = ops.deltanet_layer(y, conv_w, A, dt, nw, cs, rs, cu, qs, sl, nk, nv, D, 1e-6,
+                             max_q=max(lens) if chunked else 0)
     ref = ops._deltanet_cpu(y.cpu().float(), conv_w.cpu(), A.cpu(), dt.cpu(), nw.cpu().float(), cs_ref, rs_ref,
                             cu.cpu(), qs.cpu(), sl.cpu(), nk, nv, D, 1e-6)
     torch.cuda.synchronize()
