@@ -178,7 +178,8 @@ BUILTIN = {
 }
 
 
-_FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "llama", "mistral", "qwen3_5_text", "lfm2", "gemma", "gemma3_text")
+_FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "llama", "mistral", "mixtral", "qwen3_5_text", "lfm2", "gemma",
+             "gemma3_text")
 
 
 def _rope_params(d: dict):
@@ -219,7 +220,10 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         local_theta = float(d["rope_local_base_freq"])
     max_pos = d.get("max_position_embeddings", 40960)
     sw = d.get("sliding_window") or 0
-    moe = mt == "qwen3_moe"
+    moe = mt in ("qwen3_moe", "mixtral")
+    if mt == "mixtral":       # expert count / width under Mixtral's names; routing = softmax, top-k, renormalise
+        d = dict(d, num_experts=d.get("num_local_experts", 8), moe_intermediate_size=d["intermediate_size"],
+                 norm_topk_prob=True)
     hybrid = {}
     if mt == "qwen3_5_text":
         n = d["num_hidden_layers"]
@@ -270,14 +274,14 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         attn_bias=(mt == "qwen2") or bool(d.get("attention_bias", False)),
         qk_norm=mt in ("qwen3", "qwen3_moe", "qwen3_5_text", "lfm2", "gemma3_text"),
         tie_embeddings=bool(d.get("tie_word_embeddings", False)),
-        num_experts=d.get("num_experts", 0) if moe else 0,
+        num_experts=(d.get("num_experts") or d.get("num_local_experts") or 0) if moe else 0,
         experts_per_tok=d.get("num_experts_per_tok", 0) if moe else 0,
         moe_intermediate_size=d.get("moe_intermediate_size", 0) if moe else 0,
         norm_topk_prob=d.get("norm_topk_prob", True),
         max_position=max_pos,
         bos_token_id=d.get("bos_token_id") or 1,
         eos_token_id=(d.get("eos_token_id") if isinstance(d.get("eos_token_id"), int) else 2),
-        family=mt, sliding_window=sw if mt in ("mistral", "gemma3_text") else 0, **hybrid,
+        family=mt, sliding_window=sw if mt in ("mistral", "mixtral", "gemma3_text") else 0, **hybrid,
     )
 
 

@@ -297,9 +297,21 @@ def hf_layer_dict(get, cfg: ModelConfig, i: int) -> dict:
             d[k] = t
     if cfg.is_moe:
         E = cfg.num_experts
-        d["exp_gate"] = torch.stack([get(pre + f"mlp.experts.{e}.gate_proj.weight") for e in range(E)])
-        d["exp_up"] = torch.stack([get(pre + f"mlp.experts.{e}.up_proj.weight") for e in range(E)])
-        d["exp_down"] = torch.stack([get(pre + f"mlp.experts.{e}.down_proj.weight") for e in range(E)])
+        fused = get(pre + "mlp.experts.gate_up_proj")
+        if fused is not None:          # transformers 5 layout: [E, 2 Ie, H] (gate rows, then up) and [E, H, Ie]
+            Ie = fused.shape[1] // 2
+            d["exp_gate"], d["exp_up"] = fused[:, :Ie], fused[:, Ie:]
+            d["exp_down"] = get(pre + "mlp.experts.down_proj")
+        elif get(pre + "block_sparse_moe.gate.weight") is not None:     # Mixtral checkpoints
+            bm = pre + "block_sparse_moe."
+            d["router"] = get(bm + "gate.weight")
+            d["exp_gate"] = torch.stack([get(bm + f"experts.{e}.w1.weight") for e in range(E)])
+            d["exp_up"] = torch.stack([get(bm + f"experts.{e}.w3.weight") for e in range(E)])
+            d["exp_down"] = torch.stack([get(bm + f"experts.{e}.w2.weight") for e in range(E)])
+        else:
+            d["exp_gate"] = torch.stack([get(pre + f"mlp.experts.{e}.gate_proj.weight") for e in range(E)])
+            d["exp_up"] = torch.stack([get(pre + f"mlp.experts.{e}.up_proj.weight") for e in range(E)])
+            d["exp_down"] = torch.stack([get(pre + f"mlp.experts.{e}.down_proj.weight") for e in range(E)])
     return d
 
 
