@@ -178,7 +178,7 @@ BUILTIN = {
 }
 
 
-_FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "llama", "mistral", "mixtral", "qwen3_5_text", "lfm2", "gemma",
+_FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "llama", "mistral", "mixtral", "phi3", "qwen3_5_text", "lfm2", "gemma",
              "gemma3_text")
 
 
@@ -206,6 +206,11 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         raise NotImplementedError(f"model_type {mt!r}: supported families are {', '.join(_FAMILIES)}")
     if mt in ("llama", "mistral") and d.get("mlp_bias"):
         raise NotImplementedError("llama mlp_bias=True")
+    if mt == "phi3":
+        rp_ = d.get("rope_parameters") or {}
+        kind = (d.get("rope_scaling") or rp_).get("rope_type") or (d.get("rope_scaling") or {}).get("type")
+        if kind not in (None, "default"):
+            raise NotImplementedError(f"phi3 rope scaling {kind!r} (longrope) is not supported")
     heads = d["num_attention_heads"]
     hd = d.get("head_dim") or d["hidden_size"] // heads
     theta, scaling = _rope_params(d)
@@ -237,6 +242,11 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
                       lin_k_dim=d.get("linear_key_head_dim", 128), lin_v_dim=d.get("linear_value_head_dim", 128),
                       conv_kernel=d.get("linear_conv_kernel_dim", 4), rotary_dim=int(hd_full * prf))
     inter = d.get("intermediate_size", 0)
+    if mt == "phi3":
+        prf = d.get("partial_rotary_factor") or (d.get("rope_parameters") or {}).get("partial_rotary_factor") or 1.0
+        hd_ = d.get("head_dim") or d["hidden_size"] // d["num_attention_heads"]
+        if prf < 1.0:
+            hybrid = dict(rotary_dim=int(hd_ * prf))
     if mt in ("gemma", "gemma3_text"):
         if d.get("attn_logit_softcapping") or d.get("final_logit_softcapping"):
             raise NotImplementedError("logit softcapping")
@@ -281,7 +291,7 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         max_position=max_pos,
         bos_token_id=d.get("bos_token_id") or 1,
         eos_token_id=(d.get("eos_token_id") if isinstance(d.get("eos_token_id"), int) else 2),
-        family=mt, sliding_window=sw if mt in ("mistral", "mixtral", "gemma3_text") else 0, **hybrid,
+        family=mt, sliding_window=sw if mt in ("mistral", "mixtral", "gemma3_text", "phi3") else 0, **hybrid,
     )
 
 

@@ -289,6 +289,12 @@ def hf_layer_dict(get, cfg: ModelConfig, i: int) -> dict:
         from b200serve.models.hybrid import LIN_KEYS
         for k, name in LIN_KEYS.items():
             d[k] = get(pre + name)
+    fused_qkv = get(pre + "self_attn.qkv_proj.weight")
+    if fused_qkv is not None:       # Phi-3: one [q | k | v] projection and one [gate | up] projection
+        q_, kv_ = cfg.q_size, cfg.kv_size
+        d.update(q=fused_qkv[:q_], k=fused_qkv[q_:q_ + kv_], v=fused_qkv[q_ + kv_:])
+        gu = get(pre + "mlp.gate_up_proj.weight")
+        d.update(gate=gu[:gu.shape[0] // 2], up=gu[gu.shape[0] // 2:])
     for k, name in _HF_LAYER_KEYS.items():
         if k in d:
             continue

@@ -114,3 +114,31 @@ def test_mistral_sliding_window_matches_hf():
     finally:
         eng.unload()
     assert req.output == hf
+
+
+def test_phi3_fused_projections_match_hf():
+    """Phi-3 stores one [q | k | v] and one [gate | up] projection per layer."""
+    d = dict(_BASE, rope_theta=10000.0, pad_token_id=0)
+    hf_cfg = transformers.Phi3Config(**d)
+    torch.manual_seed(0)
+    model = transformers.Phi3ForCausalLM(hf_cfg).eval()
+    cfg = from_hf_config(dict(json.loads(hf_cfg.to_json_string()), model_type="phi3"), "tiny-phi3")
+    sd = {k: v.detach().clone() for k, v in model.state_dict().items()}
+    w = load_hf_state_dict(cfg, sd, dtype=torch.float32, device="cpu")
+    prompt = torch.randint(3, 1000, (50,), generator=torch.Generator().manual_seed(1)).tolist()
+    with torch.no_grad():
+        ref_logits = model(torch.tensor([prompt])).logits[0, -1]
+        hf = model.generate(torch.tensor([prompt]), max_new_tokens=8, min_new_tokens=8, do_sample=False,
+                            pad_token_id=0)[0, len(prompt):].tolist()
+    eng = B200Engine(EngineConfig(model="tiny-phi3", device="cpu", dtype="float32", cuda_graphs=False, max_seq=128,
+                                  max_batch=2), weights=w, model_config=cfg)
+    eng.load()
+    try:
+        bt = eng.scheduler.alloc.allocate(4)
+        logits = eng.runner.prefill([{"ids": prompt, "start": 0, "block_table": bt}])
+        eng.scheduler.alloc.release(bt)
+        assert torch.allclose(logits[0], ref_logits, atol=1e-4, rtol=1e-4)
+        [req] = eng.generate([prompt], SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True))
+    finally:
+        eng.unload()
+    assert req.output == hf
