@@ -168,14 +168,15 @@ def _sampling_from_request(body: ChatCompletionRequest) -> dict:
     return samp
 
 
-def _produce(engine, messages, max_tokens, samp, q: _StreamQueue, enable_thinking):
-    """Producer thread: stream thinking/content pieces into ``q``."""
+def _produce(engine, messages, max_tokens, samp, q: _StreamQueue, enable_thinking, telemetry=False):
+    """Producer thread: stream thinking/content pieces (and telemetry frames) into ``q``."""
     tf = ThinkFilter(on_response=lambda t: q.put(("content", t)),
                      on_thinking=lambda t: q.put(("thinking", t)),
                      starts_in_think=bool(enable_thinking and getattr(engine, "stream_starts_in_think", True)))
     try:
+        kw = {"on_telemetry": lambda f: q.put(("telemetry", f))} if telemetry else {}
         engine.generate_streaming(messages, max_tokens=max_tokens, temperature=samp.get("temperature", 0.7),
-                                  on_token=tf.feed, enable_thinking=enable_thinking, sampling=samp)
+                                  on_token=tf.feed, enable_thinking=enable_thinking, sampling=samp, **kw)
         tf.flush()
         st = getattr(engine, "_last_gen_stats", None) or {}
         q.put(("usage", {"prompt_tokens": st.get("prompt_tokens", 0),
@@ -313,8 +314,8 @@ def create_app(engine=None, keystore: KeyStore = None):
         if body.stream:
             async def gen():
                 q = _StreamQueue()
-                th = threading.Thread(target=_produce, args=(eng, messages, max_tokens, samp, q, enable_thinking),
-                                      daemon=True)
+                th = threading.Thread(target=_produce, args=(eng, messages, max_tokens, samp, q, enable_thinking,
+                                                             bool(opts.get("telemetry"))), daemon=True)
                 th.start()
                 usage = {"prompt_tokens": 0, "completion_tokens": 0}
                 finish = "stop"
@@ -331,6 +332,8 @@ def create_app(engine=None, keystore: KeyStore = None):
                             yield _make_sse_chunk(chat_id, model, {"x_thinking": data})
                         elif kind == "content":
                             yield _make_sse_chunk(chat_id, model, {"content": data})
+                        elif kind == "telemetry":
+                            yield f"data: {json.dumps({'x_telemetry': data})}\n\n"
                         elif kind == "usage":
                             finish = data.pop("finish_reason", "stop")
                             usage = data

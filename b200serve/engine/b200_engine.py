@@ -322,7 +322,15 @@ class B200Engine(BaseEngine):
             return False
 
         t_start = time.perf_counter()
-        req = self.submit(Request(prompt=prompt, params=params, stop_ids=self.tokenizer.stop_ids, on_token=_cb))
+        cap = None
+        if on_telemetry is not None:
+            if self.world > 1:
+                raise NotImplementedError("forward telemetry runs on a single-rank engine")
+            from b200serve.core.forward_telemetry import TelemetryCapture
+            cap = TelemetryCapture(self.tokenizer)
+        req = Request(prompt=prompt, params=params, stop_ids=self.tokenizer.stop_ids, on_token=_cb)
+        req.telemetry = cap
+        req = self.submit(req)
         full, t_first, callback_error = "", None, None
         try:
             while True:
@@ -332,6 +340,9 @@ class B200Engine(BaseEngine):
                     if req.done_event.is_set() and q.empty():
                         break
                     continue
+                if cap is not None:
+                    for frame in cap.drain():
+                        on_telemetry(frame)
                 if delta:
                     if t_first is None:
                         t_first = time.perf_counter()
@@ -342,6 +353,9 @@ class B200Engine(BaseEngine):
             callback_error = e
             self.scheduler.abort(req)
             req.done_event.wait(30)
+        if cap is not None:
+            for frame in cap.drain():
+                on_telemetry(frame)
         t_end = time.perf_counter()
         n = len(req.output)
         wall = t_end - t_start

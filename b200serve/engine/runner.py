@@ -155,10 +155,16 @@ class ModelRunner:
         unpack_static(self, bucket)
         return bucket, pack[: bucket * W].numel() * 4
 
-    def decode(self, ids, pos, slots, block_tables, lens, greedy=True, state_slots=None):
-        """One decode step for B sequences. Returns (logits [B, V_local], tokens [B] or None)."""
+    def decode(self, ids, pos, slots, block_tables, lens, greedy=True, state_slots=None, telemetry=None):
+        """One decode step for B sequences. Returns (logits [B, V_local], tokens [B] or None).
+        ``telemetry`` [(row, capture)] runs the step eagerly and records per-layer frames."""
         B = len(ids)
         bucket, _ = self.load_decode_inputs(ids, pos, slots, block_tables, lens, state_slots)
+        if telemetry:
+            fb = self._decode_fb(bucket)
+            fb.telemetry = telemetry
+            logits = self.decoder.forward(fb, attn_plan=self.attn_plan(bucket))
+            return logits[:B], None
         with rng(f"decode b{bucket}"):
             if self.use_graphs:
                 key = (bucket, greedy)
@@ -308,10 +314,11 @@ class ModelRunner:
                 rows.append(cu[-1] - 1)
         T = len(ids)
         t = lambda x: torch.as_tensor(x, dtype=torch.int32).to(d, non_blocking=True)
+        watch = [(cu[i + 1] - 1, s["telemetry"]) for i, s in enumerate(seqs) if s.get("telemetry") is not None]
         fb = ForwardBatch(input_ids=t(ids), positions=t(pos), slots=t(slots), block_tables=bt.to(d),
                           seq_lens=t(lens), logit_rows=torch.as_tensor(rows, dtype=torch.long).to(d),
                           is_decode=False, cu_q=t(cu), q_start=t(qs), max_q=max(len(s["ids"]) for s in seqs),
-                          state_slots=t(sts) if self.lin_state is not None else None)
+                          state_slots=t(sts) if self.lin_state is not None else None, telemetry=watch or None)
         if T == 0:
             return None
         with rng(f"prefill T{T}"):

@@ -71,6 +71,7 @@ class Request:
     prefix_hit: int = 0
     seed: int = 0
     state_slot: int = -1             # recurrent-state slot (hybrid models) while running
+    telemetry: object = None         # TelemetryCapture: per-token forward frames (eager steps)
     done_event: threading.Event = field(default_factory=threading.Event)
 
     def __post_init__(self):
@@ -238,7 +239,8 @@ class Scheduler:
         waits for admission and the runner supports it (single rank, CUDA graphs)."""
         r = self.runner
         return (getattr(r, "use_graphs", False) and hasattr(r, "pipeline_step")
-                and not self.waiting and all(q.params.greedy and q.params.plain for q in batch))
+                and not self.waiting and all(q.params.greedy and q.params.plain and q.telemetry is None
+                                             for q in batch))
 
     def _pipelined_decode(self, batch) -> int:
         """Decode ``batch`` until it changes, keeping one step in flight: step N runs on the
@@ -335,11 +337,15 @@ class Scheduler:
         slots = [r.blocks[p // BLOCK] * BLOCK + p % BLOCK for r, p in zip(batch, pos)]
         lens = [p + 1 for p in pos]
         greedy = all(r.params.greedy and r.params.plain for r in batch)
-        logits, toks = self.runner.decode(ids, pos, slots, [r.blocks for r in batch], lens, greedy=greedy,
-                                          state_slots=[r.state_slot for r in batch])
+        watch = [(i, r.telemetry) for i, r in enumerate(batch) if r.telemetry is not None]
+        kw = {"telemetry": watch} if watch else {}
+        logits, toks = self.runner.decode(ids, pos, slots, [r.blocks for r in batch], lens,
+                                          greedy=greedy and not watch, state_slots=[r.state_slot for r in batch], **kw)
         if toks is None:
             toks = self._sample(logits, batch)
         toks = toks.tolist()
+        for i, cap in watch:
+            cap.finish_token(logits[i], toks[i])
         self.stats["decode_steps"] += 1
         for r, t in zip(batch, toks):
             r.num_computed = len(r.tokens)
@@ -366,9 +372,10 @@ class Scheduler:
                 continue
             if r not in self.running:
                 continue
+            last = r.num_computed + n == len(r.tokens)
             seqs.append({"ids": r.tokens[r.num_computed:r.num_computed + n], "start": r.num_computed,
-                         "block_table": r.blocks, "want_logits": r.num_computed + n == len(r.tokens),
-                         "state_slot": r.state_slot})
+                         "block_table": r.blocks, "want_logits": last, "state_slot": r.state_slot,
+                         "telemetry": r.telemetry if last else None})
             reqs.append((r, n))
             if remaining > 1:
                 budget -= n
@@ -387,6 +394,9 @@ class Scheduler:
         if not sample_reqs:
             return 0
         toks = self._sample(logits, sample_reqs).tolist()
+        for j, (r, t) in enumerate(zip(sample_reqs, toks)):
+            if r.telemetry is not None:
+                r.telemetry.finish_token(logits[j], t)
         for r, t in zip(sample_reqs, toks):
             self._accept_token(r, int(t))
             if r.state == "finished":
@@ -395,7 +405,8 @@ class Scheduler:
 
     # ------------------------------------------------------------ n-gram speculative decoding
     def _spec_ok(self, r: Request) -> bool:
-        return r.params.greedy and r.params.plain and ngram_draft(r.tokens, self.spec_ngram) != []
+        return (r.params.greedy and r.params.plain and r.telemetry is None
+                and ngram_draft(r.tokens, self.spec_ngram) != [])
 
     def _spec_step(self) -> int:
         """Verify n-gram drafts of greedy requests in one forward: each drafting request feeds
@@ -408,7 +419,7 @@ class Scheduler:
         for r in list(self.running):
             if r not in self.running:
                 continue
-            draft = ngram_draft(r.tokens, self.spec_ngram) if (r.params.greedy and r.params.plain) else []
+            draft = ngram_draft(r.tokens, self.spec_ngram) if self._spec_ok(r) else []
             room = min(r.params.max_tokens - len(r.output), self.max_seq - len(r.tokens)) - 1
             draft = draft[:max(0, room)]
             if not self._ensure_blocks(r, len(r.tokens) + len(draft)):

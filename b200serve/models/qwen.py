@@ -44,6 +44,7 @@ class ForwardBatch:
     q_start: torch.Tensor = None
     max_q: int = 0
     state_slots: torch.Tensor = None    # hybrid models: recurrent-state slot per sequence
+    telemetry: list = None              # [(row, TelemetryCapture)]: per-layer frames for these rows
 
 
 class NoComm:
@@ -258,6 +259,22 @@ class Decoder:
             ops.sigmoid_gate_mul(out.view(T, self.nq * self.hd), qkv[:, w0:w0 + self.nq * self.hd])
         return out
 
+    def _record(self, i, x, residual, parts, telemetry):
+        """Telemetry: residual-stream L2 norm after layer ``i`` (and MoE routes) for the
+        watched rows. Runs on single-rank eager forwards only."""
+        rows = torch.tensor([r for r, _ in telemetry], device=residual.device)
+        h = residual.index_select(0, rows).float()
+        for p in parts:
+            h = h + p.index_select(0, rows).float()
+        routes = None
+        if self.moe is not None:
+            from b200serve.models.moe import topk_softmax
+            logits = ops.linear(x.index_select(0, rows), self.w.layers[i].router, epilogue=ops.EPI_F32)
+            wts, ids = topk_softmax(logits, self.cfg.experts_per_tok, self.cfg.norm_topk_prob)
+            routes = [list(zip(a.tolist(), b.tolist())) for a, b in zip(ids.cpu(), wts.cpu())]
+        for j, (_, cap) in enumerate(telemetry):
+            cap.record_layer(h[j], moe=routes[j] if routes is not None else None)
+
     def _conv_mix(self, i, x, lw, fb):
         """LFM2 gated short convolution of layer ``i``: [B | C | x] = x W_in^T, then
         C * conv(B * x) with the causal depthwise conv state -> [T, H_local] (before out_proj)."""
@@ -385,6 +402,8 @@ class Decoder:
                 mlp_parts = self._row_parallel(act, lw.down, "mlp")
             if lw.mlp_out_norm is not None:
                 mlp_parts = [ops.rmsnorm(mlp_parts, lw.mlp_out_norm, eps)]
+            if fb.telemetry:
+                self._record(i, x, residual, mlp_parts, fb.telemetry)
             if _NVTX:
                 torch.cuda.nvtx.range_pop()
         rows = fb.logit_rows
