@@ -248,6 +248,8 @@ class EngineConfig:
                  valid cache is read instead of the checkpoint, otherwise it is written
     step_timeout_s  watchdog: a forward step running longer fails the requests it holds
                  (their streams end with an error) and marks the engine stalled (0 = off)
+    quantize     "" or "q4_k_m": quantise a bf16 checkpoint's projections to 4-bit blocks while
+                 loading (GPU only; the counterpart of loading an HF model in 4 bits)
     """
 
     model: str = "qwen3-8b"
@@ -274,6 +276,7 @@ class EngineConfig:
     spec_ngram: int = 0
     shard_cache: str = ""
     step_timeout_s: float = 600.0
+    quantize: str = ""
     extra: dict = field(default_factory=dict)
 
     @classmethod

@@ -97,6 +97,14 @@ class B200Engine(BaseEngine):
         dtype = _dtype(cfgE.dtype)
         say(f"b200: building {mc.name} ({mc.num_params() / 1e9:.2f}B params) tp={tp} on {dev}")
         self.weights = self._injected_weights or self._load_weights(mc, dtype, dev)
+        if cfgE.quantize:
+            if cfgE.quantize != "q4_k_m" or dev.type != "cuda":
+                raise ValueError("quantize='q4_k_m' needs a CUDA device")
+            if mc.is_moe or mc.is_hybrid or mc.attn_output_gate:
+                raise NotImplementedError("load-time 4-bit quantisation covers dense attention models")
+            from b200serve.models.gguf_gpu import quantize_model_q4_k_m
+            say("b200: quantising projections to Q4_K_M blocks")
+            quantize_model_q4_k_m(self.weights, mc)
         self.comm = pdist.make_comm(cfgE, dev, self.model_cfg) if tp > 1 else None
         nkv_local = max(1, mc.num_kv_heads // tp)
         num_blocks = self._size_kv(mc, nkv_local, dtype, dev)

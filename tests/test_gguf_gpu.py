@@ -69,3 +69,25 @@ def test_gpu_quantiser_close_to_cpu(kind, tt):
     # same quantiser on both sides; small differences from bf16 scale rounding
     assert np.linalg.norm(gpu - cpu) / np.linalg.norm(w) < 0.03
     assert np.linalg.norm(gpu - w) / np.linalg.norm(w) < {"q4_k": 0.15, "q6_k": 0.05, "q8_0": 0.02}[kind]
+
+
+def test_engine_load_time_q4_k_m_quantisation():
+    """EngineConfig.quantize='q4_k_m' turns a bf16 model's projections into 4-bit blocks while
+    loading; its prefill logits stay close to the bf16 model's."""
+    from b200serve.core.config import EngineConfig
+    from b200serve.engine.b200_engine import B200Engine
+    from b200serve.models.gguf import QuantGroup
+    prompt = list(range(3, 60))
+    out = {}
+    for q in ("", "q4_k_m"):
+        eng = B200Engine(EngineConfig(model="tiny-qwen2", max_seq=256, max_batch=2, kv_blocks=32, quantize=q))
+        eng.load()
+        try:
+            if q:
+                assert isinstance(eng.weights.layers[0].qkv, QuantGroup)
+            bt = eng.scheduler.alloc.allocate(4)
+            out[q] = eng.runner.prefill([{"ids": prompt, "start": 0, "block_table": bt}])[0].float().cpu()
+        finally:
+            eng.unload()
+    rel = ((out["q4_k_m"] - out[""]).norm() / out[""].norm()).item()
+    assert rel < 0.2
