@@ -64,6 +64,7 @@ class ModelConfig:
     lin_k_dim: int = 0
     lin_v_dim: int = 0
     conv_kernel: int = 0
+    shared_expert_size: int = 0      # Qwen2-MoE: a dense expert every token also takes, sigmoid-gated
     # Gemma: sqrt(H)-scaled embeddings, GeGLU, query_pre_attn_scalar, local RoPE base,
     # and (Gemma 3) norms on the attention and MLP outputs before their residual adds
     embed_scale: float = 0.0         # 0 = unscaled
@@ -178,8 +179,8 @@ BUILTIN = {
 }
 
 
-_FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "llama", "mistral", "mixtral", "phi3", "qwen3_5_text", "lfm2", "gemma",
-             "gemma3_text")
+_FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "qwen2_moe", "llama", "mistral", "mixtral", "phi3", "qwen3_5_text",
+             "lfm2", "gemma", "gemma3_text")
 
 
 def _rope_params(d: dict):
@@ -225,7 +226,11 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         local_theta = float(d["rope_local_base_freq"])
     max_pos = d.get("max_position_embeddings", 40960)
     sw = d.get("sliding_window") or 0
-    moe = mt in ("qwen3_moe", "mixtral")
+    moe = mt in ("qwen3_moe", "mixtral", "qwen2_moe")
+    if mt == "qwen2_moe":
+        if d.get("mlp_only_layers") or d.get("decoder_sparse_step", 1) != 1:
+            raise NotImplementedError("qwen2_moe with dense (mlp_only) layers")
+        d = dict(d, norm_topk_prob=bool(d.get("norm_topk_prob", False)))
     if mt == "mixtral":       # expert count / width under Mixtral's names; routing = softmax, top-k, renormalise
         d = dict(d, num_experts=d.get("num_local_experts", 8), moe_intermediate_size=d["intermediate_size"],
                  norm_topk_prob=True)
@@ -281,7 +286,8 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         num_kv_heads=d.get("num_key_value_heads") or heads, head_dim=hd,
         intermediate_size=inter, rms_eps=d.get("rms_norm_eps", d.get("norm_eps", 1e-6)),
         rope_theta=theta, rope_scaling=scaling,
-        attn_bias=(mt == "qwen2") or bool(d.get("attention_bias", False)),
+        attn_bias=(mt in ("qwen2", "qwen2_moe")) or bool(d.get("attention_bias", False)),
+        shared_expert_size=int(d.get("shared_expert_intermediate_size") or 0) if mt == "qwen2_moe" else 0,
         qk_norm=mt in ("qwen3", "qwen3_moe", "qwen3_5_text", "lfm2", "gemma3_text"),
         tie_embeddings=bool(d.get("tie_word_embeddings", False)),
         num_experts=(d.get("num_experts") or d.get("num_local_experts") or 0) if moe else 0,

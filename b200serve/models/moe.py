@@ -26,6 +26,10 @@ def shard_layer_moe(cfg, full, lw, ep_rank, ep_size, dtype, device):
     lw.experts_gate_up = torch.stack(gu).to(device=device, dtype=dtype).contiguous()
     lw.experts_down = torch.stack([pad_down(d) for d in full["exp_down"][sl]]).to(device=device,
                                                                                  dtype=dtype).contiguous()
+    if cfg.shared_expert_size:       # replicated on every rank; every rank adds it after the reduction
+        lw.shared_gate_up = interleave_gate_up(full["sh_gate"], full["sh_up"]).to(device=device, dtype=dtype)
+        lw.shared_down = pad_down(full["sh_down"]).to(device=device, dtype=dtype).contiguous()
+        lw.shared_gate = full["sh_g"].to(device=device, dtype=dtype).contiguous()
 
 
 def expert_hf_tensors(cfg, lw, pre) -> dict:
@@ -121,13 +125,21 @@ class MoEBlock:
     def reduced(self, layer: int, x: torch.Tensor):
         """Expert FFN output summed over the expert-parallel ranks, as the parts the next norm
         consumes: the fused combine-push on the NVLink communicator for decode-sized steps,
-        else the local combine followed by the communicator's all-reduce."""
+        else the local combine followed by the communicator's all-reduce. A shared expert
+        (Qwen2-MoE) is computed on every rank and joins as one more local part."""
         comm = self.comm
         if (x.is_cuda and comm is not None and hasattr(comm, "moe_combine_reduce")
                 and x.shape[0] <= getattr(comm, "max_tokens", 0)):
-            return self._cuda(layer, x, fused_reduce=True)
-        out = self(layer, x)
-        return comm.reduce_parts(out, "mlp") if comm is not None else [out]
+            parts = self._cuda(layer, x, fused_reduce=True)
+        else:
+            out = self(layer, x)
+            parts = comm.reduce_parts(out, "mlp") if comm is not None else [out]
+        lw = self.w.layers[layer]
+        if lw.shared_gate_up is not None:
+            sh = ops.linear(ops.linear(x, lw.shared_gate_up, epilogue=ops.EPI_SWIGLU), lw.shared_down)
+            g = ops.linear(x, lw.shared_gate, epilogue=ops.EPI_F32)
+            parts = list(parts) + [ops.row_sigmoid_scale(sh, g)]
+        return parts
 
     def __call__(self, layer: int, x: torch.Tensor) -> torch.Tensor:
         if x.is_cuda:

@@ -117,7 +117,8 @@ class Decoder:
         """Re-lay every GEMM weight tile-contiguous (ops.PackedWeight), in place, one at a time."""
         w = self.w
         for lw in w.layers:
-            for name in ("qkv", "o", "gate_up", "down", "router", "lin_in"):
+            for name in ("qkv", "o", "gate_up", "down", "router", "lin_in", "shared_gate_up", "shared_down",
+                         "shared_gate"):
                 t = getattr(lw, name)
                 if isinstance(t, torch.Tensor):
                     setattr(lw, name, ops.pack_weight(t))

@@ -63,6 +63,9 @@ class LayerWeights:
     router: torch.Tensor = None        # MoE: [E, H]
     experts_gate_up: torch.Tensor = None  # [E_local, 2*Ie_pad, H]
     experts_down: torch.Tensor = None     # [E_local, H, Ie_pad]
+    shared_gate_up: torch.Tensor = None   # Qwen2-MoE shared expert (replicated on every rank)
+    shared_down: torch.Tensor = None
+    shared_gate: torch.Tensor = None      # [1, H] sigmoid gate of the shared expert
     # Gated DeltaNet layer (Qwen3.5 hybrid); qkv is None there
     lin_in: torch.Tensor = None        # [q | k | v | z | b | a] rows of this rank's heads
     lin_norm: torch.Tensor = None      # [dv] gated RMSNorm weight
@@ -249,6 +252,9 @@ def random_weights(cfg: ModelConfig, seed=0, std=0.02, tp_rank=0, tp_size=1, ep_
             if cfg.is_moe:
                 E, Ie = cfg.num_experts, cfg.moe_intermediate_size
                 d.update(router=n(E, H), exp_gate=n(E, Ie, H), exp_up=n(E, Ie, H), exp_down=n(E, H, Ie))
+                if cfg.shared_expert_size:
+                    Is = cfg.shared_expert_size
+                    d.update(sh_gate=n(Is, H), sh_up=n(Is, H), sh_down=n(H, Is), sh_g=n(1, H))
             else:
                 I = cfg.intermediate_size
                 d.update(gate=n(I, H), up=n(I, H), down=n(H, I))
@@ -303,6 +309,11 @@ def hf_layer_dict(get, cfg: ModelConfig, i: int) -> dict:
             d[k] = t
     if cfg.is_moe:
         E = cfg.num_experts
+        if cfg.shared_expert_size:
+            d.update(sh_gate=get(pre + "mlp.shared_expert.gate_proj.weight"),
+                     sh_up=get(pre + "mlp.shared_expert.up_proj.weight"),
+                     sh_down=get(pre + "mlp.shared_expert.down_proj.weight"),
+                     sh_g=get(pre + "mlp.shared_expert_gate.weight"))
         fused = get(pre + "mlp.experts.gate_up_proj")
         if fused is not None:          # transformers 5 layout: [E, 2 Ie, H] (gate rows, then up) and [E, H, Ie]
             Ie = fused.shape[1] // 2

@@ -318,6 +318,15 @@ def shortconv_layer(y, conv_w, conv_state, cu_q, q_start, slots):
     return out
 
 
+def row_sigmoid_scale(x, g):
+    """x [T, H] *= sigmoid(g[t]) per row (g [T, 1] fp32), in place."""
+    if _cuda(x):
+        ext().row_sigmoid_scale(x, g.contiguous())
+        return x
+    x.copy_((x.float() * torch.sigmoid(g.float().view(-1, 1))).to(x.dtype))
+    return x
+
+
 def sigmoid_gate_mul(attn, gate):
     """attn [T, W] *= sigmoid(gate) in place; ``gate`` may be a strided column view."""
     if _cuda(attn):

@@ -36,9 +36,32 @@ __global__ void gelu_tanh_mul_kernel(const __nv_bfloat16* __restrict__ gu, __nv_
   }
 }
 
+// x[t, :] *= sigmoid(g[t]) (the sigmoid gate of a shared expert)
+__global__ void row_sigmoid_scale_kernel(__nv_bfloat16* __restrict__ x, const float* __restrict__ g, int T, int H) {
+  pdl_wait();
+  pdl_trigger();
+  const size_t n = (size_t)T * H;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const float s = 1.f / (1.f + __expf(-g[i / H]));
+    x[i] = __float2bfloat16_rn(__bfloat162float(x[i]) * s);
+  }
+}
+
 }  // namespace b200
 
 using namespace b200;
+
+void row_sigmoid_scale(torch::Tensor x, torch::Tensor g) {
+  TORCH_CHECK(x.is_contiguous() && x.scalar_type() == torch::kBFloat16 && g.scalar_type() == torch::kFloat32);
+  TORCH_CHECK(g.numel() == x.size(0));
+  const int T = x.size(0), H = x.size(1);
+  if (T == 0) return;
+  const long n = (long)T * H;
+  const int blocks = (int)std::min<long>((n + 255) / 256, 148L * 16);
+  launch_pdl(row_sigmoid_scale_kernel, dim3(blocks), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+             (__nv_bfloat16*)x.data_ptr(), g.data_ptr<float>(), T, H);
+  B200_CHECK_CUDA(cudaGetLastError());
+}
 
 void gelu_tanh_mul(torch::Tensor gu, torch::Tensor act) {
   const int I = act.size(-1);

@@ -66,3 +66,17 @@ def test_mixtral():
     torch.manual_seed(0)
     model = transformers.MixtralForCausalLM(c).eval()
     _run(model, json.loads(c.to_json_string()))
+
+
+def test_qwen2_moe_shared_expert():
+    """Qwen2-MoE: top-k without renormalisation plus a sigmoid-gated shared expert."""
+    c = transformers.Qwen2MoeConfig(vocab_size=1000, hidden_size=64, num_hidden_layers=2, num_attention_heads=4,
+                                    num_key_value_heads=2, intermediate_size=128, moe_intermediate_size=32,
+                                    shared_expert_intermediate_size=96, num_experts=8, num_experts_per_tok=2,
+                                    max_position_embeddings=256)
+    torch.manual_seed(0)
+    model = transformers.Qwen2MoeForCausalLM(c).eval()
+    d = json.loads(c.to_json_string())
+    cfg = from_hf_config(d)
+    assert cfg.shared_expert_size == 96 and not cfg.norm_topk_prob and cfg.attn_bias
+    _run(model, d)
