@@ -102,6 +102,8 @@ class B200Engine(BaseEngine):
                 raise ValueError("quantize='q4_k_m' needs a CUDA device")
             if mc.is_moe or mc.is_hybrid or mc.attn_output_gate:
                 raise NotImplementedError("load-time 4-bit quantisation covers dense attention models")
+            if (mc.intermediate_size // cfgE.tp_size) % 64 or mc.hidden_size % 256:
+                raise NotImplementedError("4-bit blocks need hidden % 256 == 0 and FFN width % 64 == 0")
             from b200serve.models.gguf_gpu import quantize_model_q4_k_m
             say("b200: quantising projections to Q4_K_M blocks")
             quantize_model_q4_k_m(self.weights, mc)

@@ -76,11 +76,14 @@ def test_engine_load_time_q4_k_m_quantisation():
     loading; its prefill logits stay close to the bf16 model's."""
     from b200serve.core.config import EngineConfig
     from b200serve.engine.b200_engine import B200Engine
+    from b200serve.models.config import ModelConfig
     from b200serve.models.gguf import QuantGroup
+    cfg = ModelConfig("tiny-q", 32000, 256, 2, 4, 2, 64, 512, attn_bias=True)   # 4-bit blocks: I % 64 == 0
     prompt = list(range(3, 60))
     out = {}
     for q in ("", "q4_k_m"):
-        eng = B200Engine(EngineConfig(model="tiny-qwen2", max_seq=256, max_batch=2, kv_blocks=32, quantize=q))
+        eng = B200Engine(EngineConfig(model="tiny-q", max_seq=256, max_batch=2, kv_blocks=32, quantize=q),
+                         model_config=cfg)
         eng.load()
         try:
             if q:
