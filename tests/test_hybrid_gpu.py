@@ -322,3 +322,11 @@ def test_gemma3_engine_gpu_matches_cpu():
             eng.unload()
     for a, b in zip(outs["cuda"], outs["cpu"]):
         assert _rel(a, b) < 3e-2
+
+
+def test_row_sigmoid_scale_matches_fp32():
+    x = torch.randn(23, 384, device=dev).bfloat16()
+    g = torch.randn(23, 1, device=dev)
+    ref = x.cpu().float() * torch.sigmoid(g.cpu())
+    ops.row_sigmoid_scale(x, g)
+    assert _rel(x.cpu(), ref) < 1e-2
