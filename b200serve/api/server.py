@@ -75,7 +75,10 @@ def _check_auth(request) -> bool:
 
 class ChatMessage(BaseModel):
     role: str = Field(..., examples=["user"])
-    content: Union[str, List[dict]] = Field(..., examples=["What is the capital of France?"])
+    content: Optional[Union[str, List[dict]]] = Field("", examples=["What is the capital of France?"])
+    tool_calls: Optional[List[dict]] = None     # an assistant turn that called tools
+    tool_call_id: Optional[str] = None          # a "tool" turn answering one call
+    name: Optional[str] = None
 
 
 class ChatCompletionRequest(BaseModel):
@@ -93,6 +96,8 @@ class ChatCompletionRequest(BaseModel):
     stream: Optional[bool] = False
     options: Optional[dict] = None
     web_tools: Optional[bool] = False
+    tools: Optional[List[dict]] = None          # OpenAI function tools
+    tool_choice: Optional[Union[str, dict]] = None
     grammar: Optional[str] = None
     response_format: Optional[dict] = None
     backend: Optional[Literal["b200", "ollama", "transformers", "llama_cpp", "claude_cli"]] = None
@@ -168,16 +173,28 @@ def _sampling_from_request(body: ChatCompletionRequest) -> dict:
     return samp
 
 
-def _produce(engine, messages, max_tokens, samp, q: _StreamQueue, enable_thinking, telemetry=False):
-    """Producer thread: stream thinking/content pieces (and telemetry frames) into ``q``."""
-    tf = ThinkFilter(on_response=lambda t: q.put(("content", t)),
+def _produce(engine, messages, max_tokens, samp, q: _StreamQueue, enable_thinking, telemetry=False, tools=None):
+    """Producer thread: stream thinking/content pieces (telemetry frames, tool calls) into ``q``."""
+    tcf = None
+    on_content = lambda t: q.put(("content", t))
+    if tools:
+        from b200serve.core.tool_calls import ToolCallFilter
+        tcf = ToolCallFilter(on_content)
+        on_content = tcf.feed
+    tf = ThinkFilter(on_response=on_content,
                      on_thinking=lambda t: q.put(("thinking", t)),
                      starts_in_think=bool(enable_thinking and getattr(engine, "stream_starts_in_think", True)))
     try:
         kw = {"on_telemetry": lambda f: q.put(("telemetry", f))} if telemetry else {}
+        if tools:
+            kw["tools"] = tools
         engine.generate_streaming(messages, max_tokens=max_tokens, temperature=samp.get("temperature", 0.7),
                                   on_token=tf.feed, enable_thinking=enable_thinking, sampling=samp, **kw)
         tf.flush()
+        if tcf is not None:
+            calls = tcf.finish()
+            if calls:
+                q.put(("tool_calls", calls))
         st = getattr(engine, "_last_gen_stats", None) or {}
         q.put(("usage", {"prompt_tokens": st.get("prompt_tokens", 0),
                          "completion_tokens": st.get("completion_tokens", 0),
@@ -296,7 +313,10 @@ def create_app(engine=None, keystore: KeyStore = None):
     @app.post("/v1/chat/completions")
     async def chat_completions(request: Request, body: ChatCompletionRequest):
         auth(request)
-        messages = [m.model_dump() for m in body.messages]
+        messages = [m.model_dump(exclude_none=True) for m in body.messages]
+        for m in messages:
+            m.setdefault("content", "")
+        tools = body.tools if (body.tools and body.tool_choice != "none") else None
         if not messages:
             raise HTTPException(status_code=400, detail="messages is required")
         opts = body.options or {}
@@ -315,7 +335,7 @@ def create_app(engine=None, keystore: KeyStore = None):
             async def gen():
                 q = _StreamQueue()
                 th = threading.Thread(target=_produce, args=(eng, messages, max_tokens, samp, q, enable_thinking,
-                                                             bool(opts.get("telemetry"))), daemon=True)
+                                                             bool(opts.get("telemetry")), tools), daemon=True)
                 th.start()
                 usage = {"prompt_tokens": 0, "completion_tokens": 0}
                 finish = "stop"
@@ -332,10 +352,15 @@ def create_app(engine=None, keystore: KeyStore = None):
                             yield _make_sse_chunk(chat_id, model, {"x_thinking": data})
                         elif kind == "content":
                             yield _make_sse_chunk(chat_id, model, {"content": data})
+                        elif kind == "tool_calls":
+                            deltas = [dict(c, index=i) for i, c in enumerate(data)]
+                            yield _make_sse_chunk(chat_id, model, {"tool_calls": deltas})
+                            finish = "tool_calls"
                         elif kind == "telemetry":
                             yield f"data: {json.dumps({'x_telemetry': data})}\n\n"
                         elif kind == "usage":
-                            finish = data.pop("finish_reason", "stop")
+                            reason = data.pop("finish_reason", "stop")
+                            finish = finish if finish == "tool_calls" else reason
                             usage = data
                         elif kind == "error":
                             yield f"data: {json.dumps({'error': data})}\n\n"
@@ -350,17 +375,26 @@ def create_app(engine=None, keystore: KeyStore = None):
             return StreamingResponse(gen(), media_type="text/event-stream",
                                      headers={"Cache-Control": "no-cache", "X-Accel-Buffering": "no"})
 
+        tkw = {"tools": tools} if tools else {}
         try:
             text = await asyncio.to_thread(
                 lambda: eng.generate_streaming(messages, max_tokens=max_tokens, temperature=samp["temperature"],
-                                               enable_thinking=enable_thinking, raw_output=True, sampling=samp))
+                                               enable_thinking=enable_thinking, raw_output=True, sampling=samp,
+                                               **tkw))
         finally:
             mq.request_finished()
         st = getattr(eng, "_last_gen_stats", None) or {}
         pt, ct = st.get("prompt_tokens", 0), st.get("completion_tokens", 0)
+        msg = {"role": "assistant", "content": text or ""}
+        finish = st.get("finish_reason", "stop")
+        if tools:
+            from b200serve.core.tool_calls import parse
+            visible, calls = parse(text or "")
+            if calls:
+                msg = {"role": "assistant", "content": visible or None, "tool_calls": calls}
+                finish = "tool_calls"
         return {"id": chat_id, "object": "chat.completion", "created": int(time.time()), "model": model,
-                "choices": [{"index": 0, "message": {"role": "assistant", "content": text or ""},
-                             "finish_reason": st.get("finish_reason", "stop")}],
+                "choices": [{"index": 0, "message": msg, "finish_reason": finish}],
                 "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct},
                 "x_backend": backend, "x_stats": st}
 

@@ -307,12 +307,13 @@ class B200Engine(BaseEngine):
     # ------------------------------------------------------------ BaseEngine
     def generate_streaming(self, messages, max_tokens, temperature, on_token=None, on_complete=None,
                            enable_thinking=True, grammar=None, response_format=None, raw_output=False,
-                           web_tools=False, reasoning_effort=None, on_telemetry=None, sampling=None) -> str:
+                           web_tools=False, reasoning_effort=None, on_telemetry=None, sampling=None,
+                           tools=None) -> str:
         self.load()
         params = SamplingParams.from_dict(sampling, temperature=temperature,
                                           max_tokens=max_tokens if max_tokens and max_tokens > 0 else 8192)
         prompt = self.tokenizer.apply_chat_template(messages, add_generation_prompt=True,
-                                                    enable_thinking=enable_thinking)
+                                                    enable_thinking=enable_thinking, tools=tools)
         prompt = prompt[-(self.config.max_seq - 1):]
         stop_strings = list(STOP_STRINGS) + list(params.stop)
         q = queue.Queue()

@@ -41,8 +41,12 @@ class SyntheticTokenizer:
         del words
         return out.decode("utf-8", errors="replace")
 
-    def apply_chat_template(self, messages, add_generation_prompt=True, enable_thinking=True, **_) -> list:
+    def apply_chat_template(self, messages, add_generation_prompt=True, enable_thinking=True, tools=None,
+                            **_) -> list:
         ids = []
+        if tools:
+            from b200serve.core.tool_calls import tools_system_block
+            messages = [{"role": "system", "content": tools_system_block(tools)}] + list(messages)
         for m in messages:
             content = m.get("content", "")
             if isinstance(content, list):
@@ -76,13 +80,17 @@ class HFTokenizer:
     def decode(self, ids, skip_special_tokens=True):
         return self.tok.decode(ids, skip_special_tokens=skip_special_tokens)
 
-    def apply_chat_template(self, messages, add_generation_prompt=True, enable_thinking=True, **_):
+    def apply_chat_template(self, messages, add_generation_prompt=True, enable_thinking=True, tools=None, **_):
+        kw = {"tools": tools} if tools else {}
         try:
-            return list(self.tok.apply_chat_template(messages, add_generation_prompt=add_generation_prompt,
-                                                     enable_thinking=enable_thinking, tokenize=True))
+            out = self.tok.apply_chat_template(messages, add_generation_prompt=add_generation_prompt,
+                                               enable_thinking=enable_thinking, tokenize=True, **kw)
         except TypeError:
-            return list(self.tok.apply_chat_template(messages, add_generation_prompt=add_generation_prompt,
-                                                     tokenize=True))
+            out = self.tok.apply_chat_template(messages, add_generation_prompt=add_generation_prompt, tokenize=True,
+                                               **kw)
+        if isinstance(out, dict) or hasattr(out, "input_ids"):    # BatchEncoding from newer tokenizers
+            out = out["input_ids"]
+        return list(out)
 
     @property
     def stop_ids(self) -> set:
