@@ -441,7 +441,8 @@ def deltanet_one(S=32, T_per=1, nk=16, nv=32, D=128, iters=3):
     else:
         cu = torch.arange(0, T + 1, T_per, dtype=torch.int32, device=dev)
         qs = torch.zeros(S, dtype=torch.int32, device=dev)
-    run = lambda: ops.deltanet_layer(y, conv_w, A, dt, nw, cs, rs, cu, qs, slots, nk, nv, D, 1e-6)
+    run = lambda: ops.deltanet_layer(y, conv_w, A, dt, nw, cs, rs, cu, qs, slots, nk, nv, D, 1e-6,
+                                     max_q=T_per if T_per > 1 else 0)
     for _ in range(iters):
         run()
     torch.cuda.synchronize()
