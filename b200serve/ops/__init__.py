@@ -218,7 +218,8 @@ def deltanet_layer(y, conv_w, A, dt_bias, norm_w, conv_state, rec_state, cu_q, q
     """Token mixing of a Gated DeltaNet layer after its fused input projection
     ``y`` [T, (2 nk + nv) D + nv D + 2 nv] = [q | k | v | z | b | a]: causal depthwise conv
     (state carried in ``conv_state`` [slots, conv_dim, K-1] fp32), SiLU, L2-normalised q/k,
-    the gated delta-rule recurrence (state ``rec_state`` [slots, nv, D, D] fp32) and the
+    the gated delta-rule recurrence (state ``rec_state`` [slots, nv, D, D] fp32, stored
+    transposed: [h][j][i] holds S[i][j]) and the
     gated RMSNorm with ``norm_w``. ``cu_q`` None means one token per sequence (decode); a
     sequence whose ``q_start`` is 0 starts from zero state. Returns [T, nv * D].
     Prefill batches whose longest sequence has ``max_q`` >= DN_CHUNK_MIN tokens take the
@@ -273,7 +274,9 @@ def _deltanet_cpu(y, conv_w, A, dt_bias, norm_w, conv_state, rec_state, cu_q, q_
         a = yt[:, conv_dim + nv * D + nv:conv_dim + nv * D + 2 * nv]
         beta = torch.sigmoid(b)
         decay = torch.exp(A.float() * F.softplus(a + dt_bias.float()))
-        S = rec_state[sl[s]].clone() if hist else torch.zeros(nv, D, D, dtype=torch.float32, device=y.device)
+        # the state is kept transposed (element [h][j][i] = S[i][j]): a column of S is contiguous
+        S = rec_state[sl[s]].transpose(1, 2).clone() if hist else torch.zeros(nv, D, D, dtype=torch.float32,
+                                                                                device=y.device)
         o = torch.empty(n, nv, D, dtype=torch.float32, device=y.device)
         for t in range(n):
             S = S * decay[t][:, None, None]
@@ -281,7 +284,7 @@ def _deltanet_cpu(y, conv_w, A, dt_bias, norm_w, conv_state, rec_state, cu_q, q_
             delta = (v[t] - kv) * beta[t][:, None]
             S = S + k[t][:, :, None] * delta[:, None, :]
             o[t] = (S * q[t][:, :, None]).sum(1)
-        rec_state[sl[s]] = S
+        rec_state[sl[s]] = S.transpose(1, 2)
         on = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + eps)
         out[t0:t1] = (norm_w.float() * on * F.silu(z)).reshape(n, nv * D).to(y.dtype)
     return out
