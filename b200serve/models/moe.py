@@ -126,7 +126,7 @@ class MoEBlock:
         """Expert FFN output summed over the expert-parallel ranks, as the parts the next norm
         consumes: the fused combine-push on the NVLink communicator for decode-sized steps,
         else the local combine followed by the communicator's all-reduce. A shared expert
-        (Qwen2-MoE) is computed on every rank and joins as one more local part."""
+        (Qwen2-MoE) is not part of this sum: see ``shared``."""
         comm = self.comm
         if (x.is_cuda and comm is not None and hasattr(comm, "moe_combine_reduce")
                 and x.shape[0] <= getattr(comm, "max_tokens", 0)):
@@ -134,12 +134,18 @@ class MoEBlock:
         else:
             out = self(layer, x)
             parts = comm.reduce_parts(out, "mlp") if comm is not None else [out]
-        lw = self.w.layers[layer]
-        if lw.shared_gate_up is not None:
-            sh = ops.linear(ops.linear(x, lw.shared_gate_up, epilogue=ops.EPI_SWIGLU), lw.shared_down)
-            g = ops.linear(x, lw.shared_gate, epilogue=ops.EPI_F32)
-            parts = list(parts) + [ops.row_sigmoid_scale(sh, g)]
         return parts
+
+    def shared(self, layer: int, x: torch.Tensor):
+        """The sigmoid-gated shared expert's output (Qwen2-MoE), or None. Its weights are
+        replicated, so every rank computes the same full output and adds it to its own copy
+        of the residual stream; it never enters the cross-rank sum."""
+        lw = self.w.layers[layer]
+        if lw.shared_gate_up is None:
+            return None
+        sh = ops.linear(ops.linear(x, lw.shared_gate_up, epilogue=ops.EPI_SWIGLU), lw.shared_down)
+        g = ops.linear(x, lw.shared_gate, epilogue=ops.EPI_F32)
+        return ops.row_sigmoid_scale(sh, g)
 
     def __call__(self, layer: int, x: torch.Tensor) -> torch.Tensor:
         if x.is_cuda:

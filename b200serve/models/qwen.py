@@ -395,6 +395,9 @@ class Decoder:
             x = ops.rmsnorm(o_parts, lw.post_norm, eps, residual=residual, residual_out=residual)
             if self.moe is not None:
                 mlp_parts = self.moe.reduced(i, x)
+                sh = self.moe.shared(i, x)
+                if sh is not None:
+                    residual.add_(sh)
             elif cfg.act == "gelu_tanh":
                 act = ops.gelu_tanh_mul(ops.linear(x, lw.gate_up))
                 mlp_parts = self._row_parallel(act, lw.down, "mlp")
