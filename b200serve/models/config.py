@@ -180,7 +180,7 @@ BUILTIN = {
 
 
 _FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "qwen2_moe", "llama", "mistral", "mixtral", "phi3", "qwen3_5_text",
-             "lfm2", "gemma", "gemma3_text")
+             "qwen3_next", "lfm2", "gemma", "gemma3_text")
 
 
 def _rope_params(d: dict):
@@ -226,7 +226,7 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         local_theta = float(d["rope_local_base_freq"])
     max_pos = d.get("max_position_embeddings", 40960)
     sw = d.get("sliding_window") or 0
-    moe = mt in ("qwen3_moe", "mixtral", "qwen2_moe")
+    moe = mt in ("qwen3_moe", "mixtral", "qwen2_moe", "qwen3_next")
     if mt == "qwen2_moe":
         if d.get("mlp_only_layers") or d.get("decoder_sparse_step", 1) != 1:
             raise NotImplementedError("qwen2_moe with dense (mlp_only) layers")
@@ -235,7 +235,9 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         d = dict(d, num_experts=d.get("num_local_experts", 8), moe_intermediate_size=d["intermediate_size"],
                  norm_topk_prob=True)
     hybrid = {}
-    if mt == "qwen3_5_text":
+    if mt == "qwen3_next" and (d.get("mlp_only_layers") or d.get("decoder_sparse_step", 1) != 1):
+        raise NotImplementedError("qwen3_next with dense (mlp_only) layers")
+    if mt in ("qwen3_5_text", "qwen3_next"):
         n = d["num_hidden_layers"]
         every = d.get("full_attention_interval", 4)
         lt = d.get("layer_types") or ["linear_attention" if (i + 1) % every else "full_attention" for i in range(n)]
@@ -287,8 +289,9 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         intermediate_size=inter, rms_eps=d.get("rms_norm_eps", d.get("norm_eps", 1e-6)),
         rope_theta=theta, rope_scaling=scaling,
         attn_bias=(mt in ("qwen2", "qwen2_moe")) or bool(d.get("attention_bias", False)),
-        shared_expert_size=int(d.get("shared_expert_intermediate_size") or 0) if mt == "qwen2_moe" else 0,
-        qk_norm=mt in ("qwen3", "qwen3_moe", "qwen3_5_text", "lfm2", "gemma3_text"),
+        shared_expert_size=int(d.get("shared_expert_intermediate_size") or 0) if mt in ("qwen2_moe", "qwen3_next")
+        else 0,
+        qk_norm=mt in ("qwen3", "qwen3_moe", "qwen3_5_text", "qwen3_next", "lfm2", "gemma3_text"),
         tie_embeddings=bool(d.get("tie_word_embeddings", False)),
         num_experts=(d.get("num_experts") or d.get("num_local_experts") or 0) if moe else 0,
         experts_per_tok=d.get("num_experts_per_tok", 0) if moe else 0,

@@ -39,6 +39,22 @@ def _heads(t, n_heads, dim, rank, size):
     return t.reshape(n_heads, dim, *t.shape[1:])[rank * per:(rank + 1) * per].reshape(per * dim, *t.shape[1:])
 
 
+def split_qwen3_next(cfg, qkvz: torch.Tensor, ba: torch.Tensor) -> dict:
+    """Qwen3-Next fuses the DeltaNet projections per key head: in_proj_qkvz rows are, for each
+    key head g, [q_g (dk) | k_g (dk) | v of its value heads | z of its value heads] and
+    in_proj_ba rows [b of its value heads | a of its value heads]. Returns the Qwen3.5
+    layout (lin_qkv = [all q | all k | all v], lin_z, lin_b, lin_a)."""
+    nk, nv, dk, dv = cfg.lin_k_heads, cfg.lin_v_heads, cfg.lin_k_dim, cfg.lin_v_dim
+    r = nv // nk
+    g = qkvz.reshape(nk, 2 * dk + 2 * r * dv, -1)
+    q, k = g[:, :dk], g[:, dk:2 * dk]
+    v, z = g[:, 2 * dk:2 * dk + r * dv], g[:, 2 * dk + r * dv:]
+    H = qkvz.shape[-1]
+    gb = ba.reshape(nk, 2 * r, -1)
+    return {"lin_qkv": torch.cat([q.reshape(-1, H), k.reshape(-1, H), v.reshape(-1, H)]),
+            "lin_z": z.reshape(-1, H), "lin_b": gb[:, :r].reshape(-1, H), "lin_a": gb[:, r:].reshape(-1, H)}
+
+
 def split_gated_q(q_proj: torch.Tensor, nq: int, hd: int):
     """[nq * 2 hd, H] interleaved per head -> (q [nq hd, H], gate [nq hd, H])."""
     v = q_proj.reshape(nq, 2, hd, -1)
@@ -74,10 +90,12 @@ def shard_layer_linear(cfg, full: dict, rank: int, size: int, dtype, device):
                       qkv=None, o=out)
     lw.lin_in = lin_in
     lw.lin_norm = full["lin_norm"]
-    I = cfg.intermediate_size
-    Ir = I // size
-    lw.gate_up = interleave_gate_up(full["gate"][rank * Ir:(rank + 1) * Ir], full["up"][rank * Ir:(rank + 1) * Ir])
-    lw.down = pad_down(full["down"][:, rank * Ir:(rank + 1) * Ir])
+    if not cfg.is_moe:
+        I = cfg.intermediate_size
+        Ir = I // size
+        lw.gate_up = interleave_gate_up(full["gate"][rank * Ir:(rank + 1) * Ir],
+                                        full["up"][rank * Ir:(rank + 1) * Ir])
+        lw.down = pad_down(full["down"][:, rank * Ir:(rank + 1) * Ir])
     for name, val in vars(lw).items():
         if isinstance(val, torch.Tensor):
             setattr(lw, name, val.to(device=device, dtype=dtype).contiguous())

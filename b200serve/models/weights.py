@@ -177,7 +177,10 @@ def build_weights(cfg: ModelConfig, layer_source, embed, lm_head, final_norm, tp
         full = layer_source(i)
         if cfg.is_linear(i):
             from b200serve.models.hybrid import shard_layer_linear
-            layers.append(shard_layer_linear(cfg, full, tp_rank, tp_size, dtype, device))
+            lw = shard_layer_linear(cfg, full, tp_rank, tp_size, dtype, device)
+            if cfg.is_moe:       # Qwen3-Next: experts after the DeltaNet mixer
+                shard_layer_moe(cfg, full, lw, ep_rank, ep_size, dtype, device)
+            layers.append(lw)
             del full
             continue
         if cfg.is_conv(i):
@@ -236,7 +239,15 @@ def random_weights(cfg: ModelConfig, seed=0, std=0.02, tp_rank=0, tp_size=1, ep_
                 from b200serve.models.hybrid import random_linear_layer
                 I = cfg.intermediate_size
                 d = random_linear_layer(cfg, n, lambda *sh: torch.ones(*sh, dtype=dtype, device=gen_dev), None)
-                d.update(input_norm=one(H), post_norm=one(H), gate=n(I, H), up=n(I, H), down=n(H, I))
+                d.update(input_norm=one(H), post_norm=one(H))
+                if cfg.is_moe:
+                    E, Ie = cfg.num_experts, cfg.moe_intermediate_size
+                    d.update(router=n(E, H), exp_gate=n(E, Ie, H), exp_up=n(E, Ie, H), exp_down=n(E, H, Ie))
+                    if cfg.shared_expert_size:
+                        Is = cfg.shared_expert_size
+                        d.update(sh_gate=n(Is, H), sh_up=n(Is, H), sh_down=n(H, Is), sh_g=n(1, H))
+                else:
+                    d.update(gate=n(I, H), up=n(I, H), down=n(H, I))
                 return d
             qrows = cfg.q_size * (2 if cfg.attn_output_gate else 1)
             d = {"q": n(qrows, H), "k": n(cfg.kv_size, H), "v": n(cfg.kv_size, H), "o": n(H, cfg.q_size),
@@ -292,9 +303,12 @@ def hf_layer_dict(get, cfg: ModelConfig, i: int) -> dict:
                 d[k] = t
         return d
     if cfg.is_linear(i):
-        from b200serve.models.hybrid import LIN_KEYS
+        from b200serve.models.hybrid import LIN_KEYS, split_qwen3_next
         for k, name in LIN_KEYS.items():
             d[k] = get(pre + name)
+        if d.get("lin_qkv") is None and get(pre + "linear_attn.in_proj_qkvz.weight") is not None:
+            d.update(split_qwen3_next(cfg, get(pre + "linear_attn.in_proj_qkvz.weight"),
+                                      get(pre + "linear_attn.in_proj_ba.weight")))
     fused_qkv = get(pre + "self_attn.qkv_proj.weight")
     if fused_qkv is not None:       # Phi-3: one [q | k | v] projection and one [gate | up] projection
         q_, kv_ = cfg.q_size, cfg.kv_size

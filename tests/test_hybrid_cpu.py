@@ -113,3 +113,45 @@ def test_chunked_prefill_and_batching_carry_the_state(tiny):
     finally:
         eng2.unload()
     assert single == batched
+
+
+def test_qwen3_next_matches_hf():
+    """Qwen3-Next: the same DeltaNet / gated-attention hybrid with per-key-head fused DeltaNet
+    projections, and MoE experts plus a sigmoid-gated shared expert in every layer."""
+    if not hasattr(transformers, "Qwen3NextForCausalLM"):
+        pytest.skip("transformers without Qwen3-Next")
+    c = transformers.Qwen3NextConfig(vocab_size=1000, hidden_size=128, num_hidden_layers=4, num_attention_heads=4,
+                                     num_key_value_heads=2, head_dim=64, intermediate_size=256, moe_intermediate_size=64,
+                                     shared_expert_intermediate_size=64, num_experts=8, num_experts_per_tok=2,
+                                     linear_num_key_heads=2, linear_num_value_heads=4, linear_key_head_dim=32,
+                                     linear_value_head_dim=32, max_position_embeddings=512, bos_token_id=1,
+                                     eos_token_id=2)
+    torch.manual_seed(0)
+    model = transformers.Qwen3NextForCausalLM(c).eval()
+    g = torch.Generator().manual_seed(7)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if name.endswith("layernorm.weight") or (name.endswith("norm.weight") and "linear_attn" not in name):
+                p.copy_(torch.randn(p.shape, generator=g) * 0.1)
+            elif name.endswith("A_log"):
+                p.copy_(torch.log(torch.rand(p.shape, generator=g) * 4 + 0.5))
+    cfg = from_hf_config(json.loads(c.to_json_string()), "tiny-qwen3-next")
+    assert cfg.is_moe and cfg.is_hybrid and cfg.shared_expert_size == 64
+    sd = {k: v.detach().clone() for k, v in model.state_dict().items()}
+    w = load_hf_state_dict(cfg, sd, dtype=torch.float32, device="cpu")
+    prompt = _prompt(50)
+    with torch.no_grad():
+        ref = model(torch.tensor([prompt])).logits[0, -1]
+        hf = model.generate(torch.tensor([prompt]), max_new_tokens=10, min_new_tokens=10, do_sample=False,
+                            pad_token_id=0)[0, len(prompt):].tolist()
+    eng = _engine(cfg, w)
+    eng.load()
+    try:
+        bt = eng.scheduler.alloc.allocate(5)
+        logits = eng.runner.prefill([{"ids": prompt, "start": 0, "block_table": bt, "state_slot": 0}])
+        eng.scheduler.alloc.release(bt)
+        assert torch.allclose(logits[0], ref, atol=1e-4, rtol=1e-4), (logits[0] - ref).abs().max()
+        [req] = eng.generate([prompt], SamplingParams(temperature=0.0, max_tokens=10, ignore_eos=True))
+    finally:
+        eng.unload()
+    assert req.output == hf
