@@ -330,3 +330,36 @@ def test_row_sigmoid_scale_matches_fp32():
     ref = x.cpu().float() * torch.sigmoid(g.cpu())
     ops.row_sigmoid_scale(x, g)
     assert _rel(x.cpu(), ref) < 1e-2
+
+
+def test_qwen3_next_engine_gpu_matches_cpu():
+    """Tiny Qwen3-Next shape (DeltaNet + gated attention, MoE with a shared expert in every
+    layer) on the GPU against the CPU fp32 path: prefill then one batched decode step."""
+    from b200serve.core.config import EngineConfig
+    from b200serve.engine.b200_engine import B200Engine
+    from b200serve.models.weights import random_weights
+    cfg = _hybrid_cfg(name="tiny-next", num_experts=8, experts_per_tok=2, moe_intermediate_size=128,
+                      shared_expert_size=256, family="qwen3_next")
+    prompts = [torch.randint(3, 2048, (n,), generator=torch.Generator().manual_seed(n)).tolist() for n in (30, 100)]
+    outs = {}
+    for device, dtype in (("cpu", torch.float32), ("cuda", torch.bfloat16)):
+        w = _moved(random_weights(cfg, seed=4, std=0.05, dtype=torch.float32, device="cpu"), device, dtype)
+        ec = EngineConfig(model="tiny-next", device=device, dtype="float32" if device == "cpu" else "bfloat16",
+                          cuda_graphs=device == "cuda", max_seq=512, max_batch=4, kv_blocks=128)
+        eng = B200Engine(ec, weights=w, model_config=cfg)
+        eng.load()
+        try:
+            r, res, tables = eng.runner, [], []
+            for i, p in enumerate(prompts):
+                bt = eng.scheduler.alloc.allocate((len(p) + 15) // 16 + 1)
+                tables.append(bt)
+                res.append(r.prefill([{"ids": p[:-1], "start": 0, "block_table": bt, "state_slot": i}])[0].float().cpu())
+            pos = [len(p) - 1 for p in prompts]
+            lg, _ = r.decode([p[-1] for p in prompts], pos, [bt[q // 16] * 16 + q % 16 for bt, q in zip(tables, pos)],
+                             tables, [q + 1 for q in pos], greedy=False, state_slots=[0, 1])
+            res += [row.float().cpu() for row in lg]
+            outs[device] = res
+        finally:
+            eng.unload()
+    for a, b in zip(outs["cuda"], outs["cpu"]):
+        assert _rel(a, b) < 3e-2
