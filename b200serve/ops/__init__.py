@@ -211,6 +211,7 @@ def qkv_post(qkv, bias, q_norm, k_norm, cos_sin, positions, slots, k_cache, v_ca
 
 # ------------------------------------------------------------------ Gated DeltaNet
 DN_CHUNK_MIN = int(os.environ.get("B200_DN_CHUNK_MIN", "64"))
+DN_CHUNK_MAX_CTAS = int(os.environ.get("B200_DN_CHUNK_MAX_CTAS", "148"))
 
 
 def deltanet_layer(y, conv_w, A, dt_bias, norm_w, conv_state, rec_state, cu_q, q_start, slots, nk, nv, D,
@@ -218,17 +219,20 @@ def deltanet_layer(y, conv_w, A, dt_bias, norm_w, conv_state, rec_state, cu_q, q
     """Token mixing of a Gated DeltaNet layer after its fused input projection
     ``y`` [T, (2 nk + nv) D + nv D + 2 nv] = [q | k | v | z | b | a]: causal depthwise conv
     (state carried in ``conv_state`` [slots, conv_dim, K-1] fp32), SiLU, L2-normalised q/k,
-    the gated delta-rule recurrence (state ``rec_state`` [slots, nv, D, D] fp32, stored
-    transposed: [h][j][i] holds S[i][j]) and the
+    the gated delta-rule recurrence (state ``rec_state`` [slots, nv, D, D] fp32) and the
     gated RMSNorm with ``norm_w``. ``cu_q`` None means one token per sequence (decode); a
     sequence whose ``q_start`` is 0 starts from zero state. Returns [T, nv * D].
-    Prefill batches whose longest sequence has ``max_q`` >= DN_CHUNK_MIN tokens take the
-    chunked kernel (64-token chunks, the recurrence's sequential part shrinks 64-fold);
-    decode and short batches take the token-by-token scan.
+    Prefill batches whose longest sequence has ``max_q`` >= DN_CHUNK_MIN tokens, and whose
+    chunk grid fits one wave of the GPU, take the chunked kernel (64-token chunks, the
+    recurrence's sequential part shrinks 64-fold); decode, short and many-sequence batches
+    take the token-by-token scan.
     Reference behaviour: shaders/ssm_step.wgsl:1-12, conv1d.wgsl:28-82, l2norm.wgsl:14."""
     T = y.shape[0]
     conv_dim = (2 * nk + nv) * D
-    chunked = cu_q is not None and max_q >= DN_CHUNK_MIN
+    # the chunk kernel pays off while its (sequence, head, column group) CTAs fit one wave; with
+    # more sequences the token-by-token scan's per-sequence parallelism wins (measured on B200)
+    n_seq = cu_q.numel() - 1 if cu_q is not None else T
+    chunked = cu_q is not None and max_q >= DN_CHUNK_MIN and n_seq * nv * max(1, D // 32) <= DN_CHUNK_MAX_CTAS
     if _cuda(y, 3 if chunked else 2):
         xc = torch.empty(T, conv_dim, dtype=y.dtype, device=y.device)
         gb = torch.empty(T, nv, 2, dtype=torch.float32, device=y.device)
@@ -274,9 +278,7 @@ def _deltanet_cpu(y, conv_w, A, dt_bias, norm_w, conv_state, rec_state, cu_q, q_
         a = yt[:, conv_dim + nv * D + nv:conv_dim + nv * D + 2 * nv]
         beta = torch.sigmoid(b)
         decay = torch.exp(A.float() * F.softplus(a + dt_bias.float()))
-        # the state is kept transposed (element [h][j][i] = S[i][j]): a column of S is contiguous
-        S = rec_state[sl[s]].transpose(1, 2).clone() if hist else torch.zeros(nv, D, D, dtype=torch.float32,
-                                                                                device=y.device)
+        S = rec_state[sl[s]].clone() if hist else torch.zeros(nv, D, D, dtype=torch.float32, device=y.device)
         o = torch.empty(n, nv, D, dtype=torch.float32, device=y.device)
         for t in range(n):
             S = S * decay[t][:, None, None]
@@ -284,7 +286,7 @@ def _deltanet_cpu(y, conv_w, A, dt_bias, norm_w, conv_state, rec_state, cu_q, q_
             delta = (v[t] - kv) * beta[t][:, None]
             S = S + k[t][:, :, None] * delta[:, None, :]
             o[t] = (S * q[t][:, :, None]).sum(1)
-        rec_state[sl[s]] = S.transpose(1, 2)
+        rec_state[sl[s]] = S
         on = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + eps)
         out[t0:t1] = (norm_w.float() * on * F.silu(z)).reshape(n, nv * D).to(y.dtype)
     return out

@@ -14,9 +14,10 @@
 //            position 0), SiLU, L2-normalisation of the q and k heads; the v-head
 //            warps also turn (a, b) into the log decay g = A softplus(a + dt) and
 //            beta = sigmoid(b).
-//  dn_scan   one CTA of P*D threads per (sequence, v head): P consecutive threads
-//            keep column j of the fp32 state S [D x D] in registers (D/P rows each)
-//            and run the recurrence over the sequence's tokens in order,
+//  dn_scan   one CTA of 2D threads per (sequence, v head): the thread pair
+//            (2j, 2j+1) keeps column j of the fp32 state S [D x D] in registers
+//            (D/2 rows each) and runs the recurrence over the sequence's tokens
+//            in order,
 //               S <- decay S;  d = beta (v - S^T k);  S <- S + k d^T;  o = S^T q,
 //            then the gated RMSNorm  out = w * norm(o) * silu(z)  over the head.
 //            It also rolls the conv state forward (last K-1 inputs of the
@@ -25,8 +26,7 @@
 // Sequences: decode passes cu_q = nullptr (token t is sequence t); prefill passes
 // the token offsets cu_q [S+1]. q_start[s] is the absolute position of sequence s's
 // first token in this batch; state_slots[s] indexes the state buffers
-// (conv [slots][conv_dim][K-1] fp32, rec [slots][nv][D][D] fp32 holding S^T: element
-// [j][i] is S[i][j], so one column of S is contiguous).
+// (conv [slots][conv_dim][K-1] fp32, rec [slots][nv][D][D] fp32).
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 
@@ -109,24 +109,20 @@ __global__ void __launch_bounds__(256) dn_prep_kernel(
   }
 }
 
-template <int D, int K, int P>
-__global__ void __launch_bounds__(P * D) dn_scan_kernel(
+template <int D, int K>
+__global__ void __launch_bounds__(2 * D) dn_scan_kernel(
     const __nv_bfloat16* __restrict__ y, int ystride, const __nv_bfloat16* __restrict__ xc,
     const float* __restrict__ gb, const __nv_bfloat16* __restrict__ norm_w, float* __restrict__ conv_state,
     float* __restrict__ rec_state, const int* __restrict__ cu_q, const int* __restrict__ q_start,
     const int* __restrict__ slots, __nv_bfloat16* __restrict__ out, int nk, int nv, float eps) {
-  // P consecutive threads own one column j of S (the state is stored column-major, S^T), each
-  // R = D / P contiguous rows of it: loads are float4 and a warp reads 32/P whole columns.
-  constexpr int R = D / P;
-  constexpr int NW = P * D / 32;
-  static_assert(R % 4 == 0 && (P & (P - 1)) == 0 && P <= 32, "bad scan split");
+  constexpr int R = D / 2;         // state rows per thread
+  constexpr int NW = 2 * D / 32;   // warps
   __shared__ float qs[2][D], ks[2][D];
   __shared__ float red[2][NW];
   pdl_wait();
   pdl_trigger();
   const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
-  const int j = tid / P, part = tid % P, i0 = part * R;
-  const bool lead = part == 0;
+  const int j = tid >> 1, half = tid & 1, i0 = half * R;
   const int lane = tid & 31, warp = tid >> 5;
   const int ratio = nv / nk, kh = h / ratio;
   const int conv_dim = (2 * nk + nv) * D;
@@ -135,21 +131,16 @@ __global__ void __launch_bounds__(P * D) dn_scan_kernel(
   const int slot = slots[s];
   const bool hist = q_start[s] > 0;
   const float scale = rsqrtf((float)D);
-  float* col = rec_state + ((size_t)slot * nv + h) * D * D + (size_t)j * D + i0;   // S[i0.., j]
-  float Sc[R];
+  float* rs = rec_state + ((size_t)slot * nv + h) * D * D;
+  float Sc[R];  // Sc[i] = S[i0 + i][j]
 #pragma unroll
-  for (int i = 0; i < R; i += 4) {
-    const float4 v4 = hist ? *reinterpret_cast<const float4*>(col + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    Sc[i] = v4.x; Sc[i + 1] = v4.y; Sc[i + 2] = v4.z; Sc[i + 3] = v4.w;
-  }
+  for (int i = 0; i < R; ++i) Sc[i] = hist ? rs[(size_t)(i0 + i) * D + j] : 0.f;
   const float wj = __bfloat162float(norm_w[j]);
   for (int tt = 0; tt < n; ++tt) {
     const int t = t0 + tt, buf = tt & 1;
     const __nv_bfloat16* xr = xc + (size_t)t * conv_dim;
-    for (int e = tid; e < 2 * D; e += P * D) {
-      if (e < D) qs[buf][e] = __bfloat162float(xr[kh * D + e]) * scale;
-      else ks[buf][e - D] = __bfloat162float(xr[nk * D + kh * D + e - D]);
-    }
+    if (tid < D) qs[buf][tid] = __bfloat162float(xr[kh * D + tid]) * scale;
+    else ks[buf][tid - D] = __bfloat162float(xr[nk * D + kh * D + tid - D]);
     const float v = __bfloat162float(xr[2 * nk * D + h * D + j]);
     const float z = __bfloat162float(y[(size_t)t * ystride + conv_dim + h * D + j]);
     const float decay = __expf(gb[((size_t)t * nv + h) * 2 + 0]), beta = gb[((size_t)t * nv + h) * 2 + 1];
@@ -166,8 +157,7 @@ __global__ void __launch_bounds__(P * D) dn_scan_kernel(
       a3 += Sc[i + 3] * kk[i + 3];
     }
     float acc = (a0 + a1) + (a2 + a3);
-#pragma unroll
-    for (int o = 1; o < P; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
     const float delta = beta * (v - acc);
     float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
 #pragma unroll
@@ -182,10 +172,9 @@ __global__ void __launch_bounds__(P * D) dn_scan_kernel(
       o3 += Sc[i + 3] * qq[i + 3];
     }
     float of = (o0 + o1) + (o2 + o3);
-#pragma unroll
-    for (int o = 1; o < P; o <<= 1) of += __shfl_xor_sync(0xffffffffu, of, o);
+    of += __shfl_xor_sync(0xffffffffu, of, 1);
     const float o = bf16r(of);
-    const float ss = warp_sum(lead ? o * o : 0.f);
+    const float ss = warp_sum(half ? 0.f : o * o);
     if (lane == 0) red[buf][warp] = ss;
     __syncthreads();
     float tot = 0.f;
@@ -193,12 +182,11 @@ __global__ void __launch_bounds__(P * D) dn_scan_kernel(
     for (int w = 0; w < NW; ++w) tot += red[buf][w];
     const float normed = bf16r(o * rsqrtf(tot / (float)D + eps));
     const float res = bf16r(wj * normed) * silu(z);
-    if (lead) out[(size_t)t * nv * D + h * D + j] = __float2bfloat16_rn(res);
+    if (!half) out[(size_t)t * nv * D + h * D + j] = __float2bfloat16_rn(res);
   }
 #pragma unroll
-  for (int i = 0; i < R; i += 4)
-    *reinterpret_cast<float4*>(col + i) = make_float4(Sc[i], Sc[i + 1], Sc[i + 2], Sc[i + 3]);
-  if (!lead) return;
+  for (int i = 0; i < R; ++i) rs[(size_t)(i0 + i) * D + j] = Sc[i];
+  if (half) return;
   // roll the conv state: the last K-1 inputs of (old state ++ this batch's tokens)
   auto roll = [&](int c) {
     float* cs = conv_state + ((size_t)slot * conv_dim + c) * (K - 1);
@@ -232,7 +220,6 @@ __global__ void __launch_bounds__(P * D) dn_scan_kernel(
 // k and q, so the CW-column groups split the work; A and q.k are recomputed per group. The
 // sequential part is a 64-step forward substitution done warp-locally (each warp owns 4
 // columns). fp32 throughout; the raw o (before the gated RMSNorm) goes to o_raw.
-constexpr int kScanP = 8;   // threads per state column in dn_scan
 constexpr int kDnC = 64;    // chunk length
 constexpr int kDnCW = 32;   // state columns per CTA
 
@@ -279,9 +266,9 @@ __global__ void __launch_bounds__(256) dn_chunk_kernel(
   const bool hist = q_start[s] > 0;
   const float scale = rsqrtf((float)D);
   float* rs = rec_state + ((size_t)slot * nv + h) * D * D;
-  for (int e = tid; e < D * kDnCW; e += 256) {     // e = j * D + i: contiguous reads of S^T
-    const int j = e / D, i = e % D;
-    Ss[i * kDnCW + j] = hist ? rs[(size_t)(c0 + j) * D + i] : 0.f;
+  for (int e = tid; e < D * kDnCW; e += 256) {
+    const int i = e / kDnCW, j = e % kDnCW;
+    Ss[e] = hist ? rs[(size_t)i * D + c0 + j] : 0.f;
   }
   for (int cs = 0; cs < n; cs += kDnC) {
     const int nc = min(kDnC, n - cs);
@@ -416,8 +403,8 @@ __global__ void __launch_bounds__(256) dn_chunk_kernel(
   }
   __syncthreads();
   for (int e = tid; e < D * kDnCW; e += 256) {
-    const int j = e / D, i = e % D;
-    rs[(size_t)(c0 + j) * D + i] = Ss[i * kDnCW + j];
+    const int i = e / kDnCW, j = e % kDnCW;
+    rs[(size_t)i * D + c0 + j] = Ss[e];
   }
   // column group 0 rolls the conv state of this head's channels (as dn_scan does)
   if (blockIdx.z == 0 && tid < D) {
@@ -521,8 +508,7 @@ void deltanet_layer(torch::Tensor y, torch::Tensor conv_w, torch::Tensor A, torc
              (const __nv_bfloat16*)y.data_ptr(), ys, (const float*)conv_w.data_ptr(), (const float*)A.data_ptr(), \
              (const float*)dt_bias.data_ptr(), (const float*)conv_state.data_ptr(), cu, q_start.data_ptr<int>(),  \
              slots.data_ptr<int>(), (__nv_bfloat16*)xc.data_ptr(), gb.data_ptr<float>(), T, S, (int)nk, (int)nv);  \
-  launch_pdl(dn_scan_kernel<DV, 4, kScanP>, dim3(S, nv), dim3(kScanP * DV), 0, stream,                           \
-             (const __nv_bfloat16*)y.data_ptr(), ys,                                                           \
+  launch_pdl(dn_scan_kernel<DV, 4>, dim3(S, nv), dim3(2 * DV), 0, stream, (const __nv_bfloat16*)y.data_ptr(), ys, \
              (const __nv_bfloat16*)xc.data_ptr(), (const float*)gb.data_ptr(),                                  \
              (const __nv_bfloat16*)norm_w.data_ptr(), conv_state.data_ptr<float>(), rec_state.data_ptr<float>(),  \
              cu, q_start.data_ptr<int>(), slots.data_ptr<int>(), (__nv_bfloat16*)out.data_ptr(), (int)nk,        \
