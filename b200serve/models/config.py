@@ -198,8 +198,16 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
     if d.get("model_type") in ("qwen3_5", "gemma3") or "text_config" in d:
         # the multimodal checkpoint wraps the text decoder; its language model is served alone
         inner = {"qwen3_5": "qwen3_5_text", "gemma3": "gemma3_text"}.get(d.get("model_type"), None)
+        outer_tie = d.get("tie_word_embeddings")
         d = dict(d["text_config"])
         d["model_type"] = inner or d.get("model_type", "qwen2")
+        if outer_tie is not None and "tie_word_embeddings" not in d:
+            d["tie_word_embeddings"] = outer_tie
+    # Qwen-VL text decoders: for text-only input their multimodal RoPE (equal positions in
+    # every section) is plain RoPE, so they run as the matching text family
+    d = dict(d, model_type={"qwen2_vl": "qwen2", "qwen2_vl_text": "qwen2", "qwen2_5_vl": "qwen2",
+                            "qwen2_5_vl_text": "qwen2", "qwen3_vl_text": "qwen3", "qwen3_vl": "qwen3",
+                            "qwen3_vl_moe_text": "qwen3_moe"}.get(d.get("model_type"), d.get("model_type")))
     if d.get("model_type") == "gemma2":
         raise NotImplementedError("gemma2 (attention logit softcapping) is not supported")
     mt = d.get("model_type", "qwen2")

@@ -142,3 +142,36 @@ def test_phi3_fused_projections_match_hf():
     finally:
         eng.unload()
     assert req.output == hf
+
+
+def test_vl_checkpoints_serve_their_text_decoder():
+    """A Qwen3-VL checkpoint (text_config + ``model.language_model.`` weights) loads as its
+    Qwen3 text decoder and matches the plain Qwen3 model built from the same weights."""
+    from b200serve.models.config import BUILTIN
+    vl = transformers.Qwen3VLConfig(text_config=dict(vocab_size=1000, hidden_size=128, num_hidden_layers=2,
+                                                     num_attention_heads=4, num_key_value_heads=2, head_dim=32,
+                                                     intermediate_size=256, max_position_embeddings=512,
+                                                     rope_theta=1e6))
+    cfg = from_hf_config(json.loads(vl.to_json_string()), "tiny-vl")
+    assert cfg.qk_norm and not cfg.attn_bias and cfg.num_layers == 2 and cfg.rope_theta == 1e6
+    q3 = transformers.Qwen3Config(vocab_size=1000, hidden_size=128, num_hidden_layers=2, num_attention_heads=4,
+                                  num_key_value_heads=2, head_dim=32, intermediate_size=256,
+                                  max_position_embeddings=512, rope_theta=1e6, tie_word_embeddings=cfg.tie_embeddings)
+    torch.manual_seed(0)
+    model = transformers.Qwen3ForCausalLM(q3).eval()
+    sd = {}
+    for k, v in model.state_dict().items():      # the VL layout nests the decoder one level deeper
+        sd[k.replace("model.", "model.language_model.", 1) if k.startswith("model.") else k] = v.detach().clone()
+    w = load_hf_state_dict(cfg, sd, dtype=torch.float32, device="cpu")
+    prompt = list(range(3, 40))
+    with torch.no_grad():
+        ref = model(torch.tensor([prompt])).logits[0, -1]
+    eng = B200Engine(EngineConfig(model="tiny-vl", device="cpu", dtype="float32", cuda_graphs=False, max_seq=128,
+                                  max_batch=2), weights=w, model_config=cfg)
+    eng.load()
+    try:
+        bt = eng.scheduler.alloc.allocate(3)
+        logits = eng.runner.prefill([{"ids": prompt, "start": 0, "block_table": bt}])
+        assert torch.allclose(logits[0], ref, atol=1e-4, rtol=1e-4)
+    finally:
+        eng.unload()
