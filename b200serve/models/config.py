@@ -180,7 +180,7 @@ BUILTIN = {
 
 
 _FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "qwen2_moe", "llama", "mistral", "mixtral", "phi3", "qwen3_5_text",
-             "qwen3_next", "lfm2", "gemma", "gemma3_text")
+             "qwen3_5_moe_text", "qwen3_next", "lfm2", "gemma", "gemma3_text")
 
 
 def _rope_params(d: dict):
@@ -195,9 +195,10 @@ def _rope_params(d: dict):
 
 
 def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
-    if d.get("model_type") in ("qwen3_5", "gemma3") or "text_config" in d:
+    if d.get("model_type") in ("qwen3_5", "qwen3_5_moe", "gemma3") or "text_config" in d:
         # the multimodal checkpoint wraps the text decoder; its language model is served alone
-        inner = {"qwen3_5": "qwen3_5_text", "gemma3": "gemma3_text"}.get(d.get("model_type"), None)
+        inner = {"qwen3_5": "qwen3_5_text", "qwen3_5_moe": "qwen3_5_moe_text",
+                 "gemma3": "gemma3_text"}.get(d.get("model_type"), None)
         outer_tie = d.get("tie_word_embeddings")
         d = dict(d["text_config"])
         d["model_type"] = inner or d.get("model_type", "qwen2")
@@ -234,7 +235,9 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         local_theta = float(d["rope_local_base_freq"])
     max_pos = d.get("max_position_embeddings", 40960)
     sw = d.get("sliding_window") or 0
-    moe = mt in ("qwen3_moe", "mixtral", "qwen2_moe", "qwen3_next")
+    moe = mt in ("qwen3_moe", "mixtral", "qwen2_moe", "qwen3_next", "qwen3_5_moe_text")
+    if mt == "qwen3_5_moe_text":      # routes always renormalise over the top-k
+        d = dict(d, norm_topk_prob=True)
     if mt == "qwen2_moe":
         if d.get("mlp_only_layers") or d.get("decoder_sparse_step", 1) != 1:
             raise NotImplementedError("qwen2_moe with dense (mlp_only) layers")
@@ -245,7 +248,7 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
     hybrid = {}
     if mt == "qwen3_next" and (d.get("mlp_only_layers") or d.get("decoder_sparse_step", 1) != 1):
         raise NotImplementedError("qwen3_next with dense (mlp_only) layers")
-    if mt in ("qwen3_5_text", "qwen3_next"):
+    if mt in ("qwen3_5_text", "qwen3_next", "qwen3_5_moe_text"):
         n = d["num_hidden_layers"]
         every = d.get("full_attention_interval", 4)
         lt = d.get("layer_types") or ["linear_attention" if (i + 1) % every else "full_attention" for i in range(n)]
@@ -297,9 +300,9 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         intermediate_size=inter, rms_eps=d.get("rms_norm_eps", d.get("norm_eps", 1e-6)),
         rope_theta=theta, rope_scaling=scaling,
         attn_bias=(mt in ("qwen2", "qwen2_moe")) or bool(d.get("attention_bias", False)),
-        shared_expert_size=int(d.get("shared_expert_intermediate_size") or 0) if mt in ("qwen2_moe", "qwen3_next")
-        else 0,
-        qk_norm=mt in ("qwen3", "qwen3_moe", "qwen3_5_text", "qwen3_next", "lfm2", "gemma3_text"),
+        shared_expert_size=int(d.get("shared_expert_intermediate_size") or 0)
+        if mt in ("qwen2_moe", "qwen3_next", "qwen3_5_moe_text") else 0,
+        qk_norm=mt in ("qwen3", "qwen3_moe", "qwen3_5_text", "qwen3_next", "qwen3_5_moe_text", "lfm2", "gemma3_text"),
         tie_embeddings=bool(d.get("tie_word_embeddings", False)),
         num_experts=(d.get("num_experts") or d.get("num_local_experts") or 0) if moe else 0,
         experts_per_tok=d.get("num_experts_per_tok", 0) if moe else 0,

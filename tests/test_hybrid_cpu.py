@@ -155,3 +155,37 @@ def test_qwen3_next_matches_hf():
     finally:
         eng.unload()
     assert req.output == hf
+
+
+def test_qwen3_5_moe_matches_hf():
+    """Qwen3.5-MoE: the Qwen3.5 hybrid with routed experts plus a shared expert."""
+    if not hasattr(transformers, "Qwen3_5MoeForCausalLM"):
+        pytest.skip("transformers without Qwen3.5-MoE")
+    c = transformers.Qwen3_5MoeTextConfig(vocab_size=1000, hidden_size=128, num_hidden_layers=4,
+                                          num_attention_heads=4, num_key_value_heads=2, head_dim=64,
+                                          moe_intermediate_size=64, shared_expert_intermediate_size=64,
+                                          num_experts=8, num_experts_per_tok=2, linear_num_key_heads=2,
+                                          linear_num_value_heads=4, linear_key_head_dim=32, linear_value_head_dim=32,
+                                          max_position_embeddings=512, bos_token_id=1, eos_token_id=2)
+    torch.manual_seed(0)
+    model = transformers.Qwen3_5MoeForCausalLM(c).eval()
+    g = torch.Generator().manual_seed(8)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if name.endswith("layernorm.weight") or (name.endswith("norm.weight") and "linear_attn" not in name):
+                p.copy_(torch.randn(p.shape, generator=g) * 0.1)
+    cfg = from_hf_config(json.loads(c.to_json_string()), "tiny-q35moe")
+    assert cfg.is_moe and cfg.is_hybrid and cfg.norm_topk_prob and cfg.shared_expert_size == 64
+    sd = {k: v.detach().clone() for k, v in model.state_dict().items()}
+    w = load_hf_state_dict(cfg, sd, dtype=torch.float32, device="cpu")
+    prompt = _prompt(45)
+    with torch.no_grad():
+        ref = model(torch.tensor([prompt])).logits[0, -1]
+    eng = _engine(cfg, w)
+    eng.load()
+    try:
+        bt = eng.scheduler.alloc.allocate(4)
+        logits = eng.runner.prefill([{"ids": prompt, "start": 0, "block_table": bt, "state_slot": 0}])
+        assert torch.allclose(logits[0], ref, atol=1e-4, rtol=1e-4), (logits[0] - ref).abs().max()
+    finally:
+        eng.unload()
