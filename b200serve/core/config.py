@@ -238,7 +238,8 @@ class EngineConfig:
                  "turboquant" (WHT + Lloyd-Max codes, ``kv_key_bits``/``kv_value_bits``)
     kv_block     tokens per KV page
     max_batch    most sequences decoded together (CUDA-graph buckets up to this)
-    max_seq      longest sequence (prompt + completion) accepted
+    max_seq      longest sequence (prompt + completion) accepted; 0 = the largest context
+                 tier whose KV fits (core/ctx_planner.py)
     kv_blocks    KV pages to allocate (0 = size from ``kv_mem_fraction`` of free memory)
     comm         "fused" (in-kernel NVLink P2P) or "nccl" (library collectives)
     spec_ngram   draft tokens per step for n-gram speculative decoding of greedy

@@ -94,6 +94,8 @@ class B200Engine(BaseEngine):
         self.device = dev
         mc = self._injected_model_cfg or get_model_config(cfgE.model, cfgE.num_layers_override)
         self.model_cfg = mc
+        if cfgE.max_seq <= 0:
+            self._plan_max_seq(mc, dev)
         dtype = _dtype(cfgE.dtype)
         say(f"b200: building {mc.name} ({mc.num_params() / 1e9:.2f}B params) tp={tp} on {dev}")
         self.weights = self._injected_weights or self._load_weights(mc, dtype, dev)
@@ -129,6 +131,25 @@ class B200Engine(BaseEngine):
         inference._tokenizer = self.tokenizer
         self._loaded_model = cfgE.model
         say(f"b200: ready, {num_blocks} KV pages ({num_blocks * BLOCK} tokens)")
+
+    def _plan_max_seq(self, mc, dev):
+        """max_seq = 0: the longest context tier whose KV fits next to the weights."""
+        from b200serve.core.ctx_planner import plan_context
+        cfgE = self.config
+        if dev.type == "cuda":
+            free, _ = torch.cuda.mem_get_info(dev)
+            free -= int(mc.num_params() * 2 / cfgE.tp_size)       # bf16 weights still to load
+        else:
+            free = 16 << 30
+        state = 0
+        if mc.is_hybrid:
+            from b200serve.models.hybrid import LinearState
+            state = LinearState.bytes_per_slot(mc, cfgE.tp_size)
+        ctx = plan_context(mc, free, cfgE.max_batch, cfgE.tp_size, cfgE.kv_format, state_bytes_per_seq=state)
+        if ctx == 0:
+            raise RuntimeError("not even a 4096-token context fits; lower max_batch or use a smaller KV format")
+        cfgE.max_seq = ctx
+        _log.info(f"b200: planned context {ctx} tokens for {cfgE.max_batch} sequences")
 
     def _model_path(self):
         m = self.config.model
