@@ -65,6 +65,8 @@ class ModelConfig:
     lin_v_dim: int = 0
     conv_kernel: int = 0
     shared_expert_size: int = 0      # Qwen2-MoE: a dense expert every token also takes, sigmoid-gated
+    residual_scale: float = 0.0      # Granite: sub-block outputs scaled before the residual add (0 = 1)
+    logits_scale: float = 0.0        # Granite: logits divided by this (0 = 1)
     # Gemma: sqrt(H)-scaled embeddings, GeGLU, query_pre_attn_scalar, local RoPE base,
     # and (Gemma 3) norms on the attention and MLP outputs before their residual adds
     embed_scale: float = 0.0         # 0 = unscaled
@@ -179,7 +181,8 @@ BUILTIN = {
 }
 
 
-_FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "qwen2_moe", "llama", "mistral", "mixtral", "phi3", "qwen3_5_text",
+_FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "qwen2_moe", "llama", "mistral", "granite", "mixtral", "phi3",
+             "qwen3_5_text",
              "qwen3_5_moe_text", "qwen3_next", "lfm2", "gemma", "gemma3_text")
 
 
@@ -214,7 +217,7 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
     mt = d.get("model_type", "qwen2")
     if mt not in _FAMILIES:
         raise NotImplementedError(f"model_type {mt!r}: supported families are {', '.join(_FAMILIES)}")
-    if mt in ("llama", "mistral") and d.get("mlp_bias"):
+    if mt in ("llama", "mistral", "granite") and d.get("mlp_bias"):
         raise NotImplementedError("llama mlp_bias=True")
     if mt == "phi3":
         rp_ = d.get("rope_parameters") or {}
@@ -281,6 +284,11 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
             lt = d.get("layer_types") or ["full_attention" if (i + 1) % every == 0 else "sliding_attention"
                                           for i in range(n)]
             hybrid.update(layer_types=tuple(lt), sandwich_norms=True, rope_local_theta=local_theta)
+    if mt == "granite":       # every multiplier folds into the weights at load
+        hybrid = dict(embed_scale=float(d.get("embedding_multiplier", 1.0)),
+                      attn_scale=float(d.get("attention_multiplier", 0.0)),
+                      residual_scale=float(d.get("residual_multiplier", 1.0)),
+                      logits_scale=float(d.get("logits_scaling", 1.0)))
     if mt == "lfm2":
         n = d["num_hidden_layers"]
         full = d.get("full_attn_idxs")

@@ -197,8 +197,16 @@ def build_weights(cfg: ModelConfig, layer_source, embed, lm_head, final_norm, tp
     if cfg.norm_offset:
         from b200serve.models.hybrid import offset_norm
         final_norm = offset_norm(final_norm)
-    if cfg.embed_scale:     # Gemma: the lookup table is pre-scaled; a tied lm_head keeps the plain one
-        embed = embed.float() * cfg.embed_scale
+    if cfg.embed_scale and cfg.embed_scale != 1.0:   # Gemma, Granite: the lookup table is pre-scaled;
+        embed = embed.float() * cfg.embed_scale           # a tied lm_head keeps the plain one
+    if cfg.logits_scale and cfg.logits_scale != 1.0:     # Granite: logits / logits_scaling
+        lm_head = lm_head.float() / cfg.logits_scale
+    if cfg.residual_scale and cfg.residual_scale != 1.0:  # Granite: both row-parallel outputs scaled
+        for lw in layers:
+            for name in ("o", "down"):
+                t = getattr(lw, name)
+                if isinstance(t, torch.Tensor):
+                    setattr(lw, name, (t.float() * cfg.residual_scale).to(t.dtype))
     return ModelWeights(
         embed=embed.to(device=device, dtype=dtype).contiguous(),
         final_norm=final_norm.to(device=device, dtype=dtype).contiguous(),

@@ -175,3 +175,27 @@ def test_vl_checkpoints_serve_their_text_decoder():
         assert torch.allclose(logits[0], ref, atol=1e-4, rtol=1e-4)
     finally:
         eng.unload()
+
+
+def test_granite_multipliers_match_hf():
+    """Granite: embedding, attention, residual and logits multipliers folded into the weights."""
+    d = dict(_BASE, rope_theta=10000.0, embedding_multiplier=12.0, attention_multiplier=0.0078125,
+             residual_multiplier=0.22, logits_scaling=8.0)
+    hf_cfg = transformers.GraniteConfig(**d)
+    torch.manual_seed(0)
+    model = transformers.GraniteForCausalLM(hf_cfg).eval()
+    cfg = from_hf_config(dict(json.loads(hf_cfg.to_json_string()), model_type="granite"), "tiny-granite")
+    sd = {k: v.detach().clone() for k, v in model.state_dict().items()}
+    w = load_hf_state_dict(cfg, sd, dtype=torch.float32, device="cpu")
+    prompt = torch.randint(3, 1000, (40,), generator=torch.Generator().manual_seed(1)).tolist()
+    with torch.no_grad():
+        ref = model(torch.tensor([prompt])).logits[0, -1]
+    eng = B200Engine(EngineConfig(model="tiny-granite", device="cpu", dtype="float32", cuda_graphs=False,
+                                  max_seq=128, max_batch=2), weights=w, model_config=cfg)
+    eng.load()
+    try:
+        bt = eng.scheduler.alloc.allocate(3)
+        logits = eng.runner.prefill([{"ids": prompt, "start": 0, "block_table": bt}])
+        assert torch.allclose(logits[0], ref, atol=1e-4, rtol=1e-4), (logits[0] - ref).abs().max()
+    finally:
+        eng.unload()
