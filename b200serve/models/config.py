@@ -65,6 +65,8 @@ class ModelConfig:
     lin_v_dim: int = 0
     conv_kernel: int = 0
     shared_expert_size: int = 0      # Qwen2-MoE: a dense expert every token also takes, sigmoid-gated
+    attn_softcap: float = 0.0        # Gemma 2: attention scores -> c tanh(score / c) (0 = off)
+    final_softcap: float = 0.0       # Gemma 2: logits -> c tanh(logit / c) (0 = off)
     residual_scale: float = 0.0      # Granite: sub-block outputs scaled before the residual add (0 = 1)
     logits_scale: float = 0.0        # Granite: logits divided by this (0 = 1)
     # Gemma: sqrt(H)-scaled embeddings, GeGLU, query_pre_attn_scalar, local RoPE base,
@@ -182,7 +184,7 @@ BUILTIN = {
 
 
 _FAMILIES = ("qwen2", "qwen3", "qwen3_moe", "qwen2_moe", "llama", "mistral", "granite", "mixtral", "phi3",
-             "qwen3_5_text",
+             "gemma2", "qwen3_5_text",
              "qwen3_5_moe_text", "qwen3_next", "lfm2", "gemma", "gemma3_text")
 
 
@@ -212,8 +214,7 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
     d = dict(d, model_type={"qwen2_vl": "qwen2", "qwen2_vl_text": "qwen2", "qwen2_5_vl": "qwen2",
                             "qwen2_5_vl_text": "qwen2", "qwen3_vl_text": "qwen3", "qwen3_vl": "qwen3",
                             "qwen3_vl_moe_text": "qwen3_moe"}.get(d.get("model_type"), d.get("model_type")))
-    if d.get("model_type") == "gemma2":
-        raise NotImplementedError("gemma2 (attention logit softcapping) is not supported")
+
     mt = d.get("model_type", "qwen2")
     if mt not in _FAMILIES:
         raise NotImplementedError(f"model_type {mt!r}: supported families are {', '.join(_FAMILIES)}")
@@ -268,9 +269,7 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         hd_ = d.get("head_dim") or d["hidden_size"] // d["num_attention_heads"]
         if prf < 1.0:
             hybrid = dict(rotary_dim=int(hd_ * prf))
-    if mt in ("gemma", "gemma3_text"):
-        if d.get("attn_logit_softcapping") or d.get("final_logit_softcapping"):
-            raise NotImplementedError("logit softcapping")
+    if mt in ("gemma", "gemma2", "gemma3_text"):
         act = d.get("hidden_activation") or d.get("hidden_act") or "gelu_pytorch_tanh"
         if act not in ("gelu_pytorch_tanh", "gelu"):
             raise NotImplementedError(f"activation {act}")
@@ -278,11 +277,15 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         hd_ = d.get("head_dim") or d["hidden_size"] // heads_
         hybrid = dict(norm_offset=True, embed_scale=float(d["hidden_size"]) ** 0.5, act="gelu_tanh",
                       attn_scale=float(d.get("query_pre_attn_scalar") or hd_) ** -0.5)
-        if mt == "gemma3_text":
+        hybrid.update(attn_softcap=float(d.get("attn_logit_softcapping") or 0.0),
+                      final_softcap=float(d.get("final_logit_softcapping") or 0.0))
+        if mt in ("gemma2", "gemma3_text"):
             n = d["num_hidden_layers"]
             every = d.get("sliding_window_pattern", 6)
             lt = d.get("layer_types") or ["full_attention" if (i + 1) % every == 0 else "sliding_attention"
                                           for i in range(n)]
+            if mt == "gemma2" and not d.get("layer_types"):    # Gemma 2 alternates local and global layers
+                lt = ["sliding_attention" if i % 2 == 0 else "full_attention" for i in range(n)]
             hybrid.update(layer_types=tuple(lt), sandwich_norms=True, rope_local_theta=local_theta)
     if mt == "granite":       # every multiplier folds into the weights at load
         hybrid = dict(embed_scale=float(d.get("embedding_multiplier", 1.0)),
@@ -319,7 +322,7 @@ def from_hf_config(d: dict, name: str = "hf") -> ModelConfig:
         max_position=max_pos,
         bos_token_id=d.get("bos_token_id") or 1,
         eos_token_id=(d.get("eos_token_id") if isinstance(d.get("eos_token_id"), int) else 2),
-        family=mt, sliding_window=sw if mt in ("mistral", "mixtral", "gemma3_text", "phi3") else 0, **hybrid,
+        family=mt, sliding_window=sw if mt in ("mistral", "mixtral", "gemma2", "gemma3_text", "phi3") else 0, **hybrid,
     )
 
 

@@ -96,8 +96,8 @@ class Decoder:
             n += 1 if cfg.has_kv(i) else 0
         # sliding-window length per K/V layer index (0 = full attention)
         self.kv_window = [cfg.window(i) for i in range(cfg.num_layers) if cfg.has_kv(i)]
-        if any(self.kv_window) and getattr(kv_cache, "kv_format", "bf16") != "bf16":
-            raise NotImplementedError("sliding-window attention runs with the bf16 KV cache")
+        if (any(self.kv_window) or cfg.attn_softcap) and getattr(kv_cache, "kv_format", "bf16") != "bf16":
+            raise NotImplementedError("sliding-window / softcapped attention runs with the bf16 KV cache")
         self.lin_state = None
         if cfg.is_hybrid and getattr(kv_cache, "kv_format", "bf16") != "bf16":
             raise NotImplementedError("hybrid (DeltaNet / short-conv) models run with the bf16 KV cache")
@@ -299,11 +299,12 @@ class Decoder:
         tps, nsplit, ws = plan
         kc, vc = self.kv.k[i], self.kv.v[i]
         win = self.kv_window[i]
+        cap = self.cfg.attn_softcap
         if fb.is_decode:
             return ops.paged_decode_attention(q, kc, vc, fb.block_tables, fb.seq_lens, self.scale, tps, nsplit, ws,
-                                              window=win)
+                                              window=win, softcap=cap)
         return ops.paged_prefill_attention(q, kc, vc, fb.block_tables, fb.seq_lens, fb.q_start, fb.cu_q,
-                                           self.scale, max_q=fb.max_q, window=win)
+                                           self.scale, max_q=fb.max_q, window=win, softcap=cap)
 
     def _attend(self, i, qkv, lw, fb, T, plan, tq_pre):
         """QKV post-processing, KV write and attention of layer ``i`` -> [T, nq, hd]."""
@@ -414,4 +415,7 @@ class Decoder:
         x = ops.rmsnorm(mlp_parts, w.final_norm, eps, residual=residual)
         if rows is not None:
             x = x.index_select(0, rows)
-        return ops.linear(x, w.lm_head, epilogue=ops.EPI_F32)
+        logits = ops.linear(x, w.lm_head, epilogue=ops.EPI_F32)
+        if cfg.final_softcap:
+            ops.softcap_(logits, cfg.final_softcap)
+        return logits

@@ -358,6 +358,15 @@ def silu_mul(gu, out=None):
     return r
 
 
+def softcap_(x, cap):
+    """x = cap * tanh(x / cap) in place (fp32 logits)."""
+    if _cuda(x):
+        ext().softcap_(x, float(cap))
+        return x
+    x.copy_(cap * torch.tanh(x / cap))
+    return x
+
+
 def gelu_tanh_mul(gu, out=None):
     """act = gelu_tanh(gate) * up (GeGLU) on the 64-column interleaved [g|u] layout."""
     I = gu.shape[-1] // 2
@@ -642,9 +651,10 @@ _TC_PREFILL = os.environ.get("B200_TC_PREFILL", "1") != "0"         # tcgen05 pr
 
 
 def paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, scale, tps=256, nsplit=1,
-                           workspace=None, out=None, window=0):
+                           workspace=None, out=None, window=0, softcap=0.0):
     """One query token per sequence. q [B, nq, hd]; seq_lens include the new token.
-    ``window`` > 0: sliding-window attention over the last ``window`` keys."""
+    ``window`` > 0: sliding-window attention over the last ``window`` keys; ``softcap`` > 0:
+    scores become softcap * tanh(score / softcap) before the softmax."""
     if _cuda(q, 2 if nsplit > 1 else 1):
         out = out if out is not None else torch.empty_like(q)
         if nsplit > 1:
@@ -654,12 +664,12 @@ def paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, scale, t
             acc = ml = torch.empty(0, dtype=torch.float32, device=q.device)
         B, nq, hd = q.shape
         G = nq // k_cache.shape[1]
-        if hd == 128 and G in (1, 2, 4, 8, 16) and not _FORCE_SIMT_DECODE and not window:
+        if hd == 128 and G in (1, 2, 4, 8, 16) and not _FORCE_SIMT_DECODE and not window and not softcap:
             ext().paged_decode_attention_tc(q, k_cache, v_cache, block_tables, seq_lens, out, acc, ml,
                                             float(scale), int(tps), int(nsplit))
         else:
             ext().paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, out, acc, ml,
-                                         float(scale), int(tps), int(nsplit), int(window))
+                                         float(scale), int(tps), int(nsplit), int(window), float(softcap))
         return out
     B, nq, hd = q.shape
     nkv = k_cache.shape[1]
@@ -674,6 +684,8 @@ def paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, scale, t
         v = v_cache[blocks].permute(1, 0, 2, 3).reshape(nkv, nb * 16, hd)[:, :L].float()
         qq = q[b].float().view(nkv, nq // nkv, hd)
         s = torch.einsum("kgd,ktd->kgt", qq, k) * scale
+        if softcap:
+            s = softcap * torch.tanh(s / softcap)
         if window:
             s[..., :max(0, L - window)] = float("-inf")
         p = torch.softmax(s, -1)
@@ -685,7 +697,7 @@ def paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, scale, t
 
 
 def paged_prefill_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, cu_q, scale, out=None,
-                            max_q=None, window=0):
+                            max_q=None, window=0, softcap=0.0):
     """Causal attention for chunks of new tokens against the paged cache.
 
     q [T, nq, hd] holds the new tokens of all sequences back to back; sequence i
@@ -698,12 +710,12 @@ def paged_prefill_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start
         mq = int(max_q if max_q is not None else q.shape[0])
         G = q.shape[1] // k_cache.shape[1]
         if (_TC_PREFILL and q.shape[2] == 128 and k_cache.dtype == torch.bfloat16 and G in (1, 2, 4, 8)
-                and q.is_contiguous() and not window):
+                and q.is_contiguous() and not window and not softcap):
             ext().paged_prefill_attention_tc(q, k_cache, v_cache, block_tables, seq_lens, q_start, cu_q, out,
                                              float(scale), mq)
         else:
             ext().paged_prefill_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start, cu_q, out,
-                                          float(scale), mq, int(window))
+                                          float(scale), mq, int(window), float(softcap))
         return out
     T, nq, hd = q.shape
     nkv = k_cache.shape[1]
@@ -723,6 +735,8 @@ def paged_prefill_attention(q, k_cache, v_cache, block_tables, seq_lens, q_start
         v = v.repeat_interleave(g, 0)
         qq = q[a:b_].float().permute(1, 0, 2)  # [nq, n, hd]
         s = torch.einsum("hnd,htd->hnt", qq, k) * scale
+        if softcap:
+            s = softcap * torch.tanh(s / softcap)
         pos = torch.arange(s0, s0 + (b_ - a))[:, None]
         mask = torch.arange(L)[None, :] > pos
         if window:

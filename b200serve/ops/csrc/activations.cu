@@ -47,9 +47,27 @@ __global__ void row_sigmoid_scale_kernel(__nv_bfloat16* __restrict__ x, const fl
   }
 }
 
+// x = cap * tanh(x / cap) in place (fp32 logits; Gemma 2's final logit softcapping)
+__global__ void softcap_kernel(float* __restrict__ x, size_t n, float cap) {
+  pdl_wait();
+  pdl_trigger();
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    x[i] = cap * tanhf(x[i] / cap);
+}
+
 }  // namespace b200
 
 using namespace b200;
+
+void softcap_(torch::Tensor x, double cap) {
+  TORCH_CHECK(x.is_contiguous() && x.scalar_type() == torch::kFloat32);
+  const size_t n = x.numel();
+  if (n == 0) return;
+  const int blocks = (int)std::min<size_t>((n + 255) / 256, 148 * 16);
+  launch_pdl(softcap_kernel, dim3(blocks), dim3(256), 0, at::cuda::getCurrentCUDAStream(), x.data_ptr<float>(), n,
+             (float)cap);
+  B200_CHECK_CUDA(cudaGetLastError());
+}
 
 void row_sigmoid_scale(torch::Tensor x, torch::Tensor g) {
   TORCH_CHECK(x.is_contiguous() && x.scalar_type() == torch::kBFloat16 && g.scalar_type() == torch::kFloat32);

@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
     const __nv_bfloat16* __restrict__ v_cache, const int* __restrict__ block_tables,
     const int* __restrict__ seq_lens, int max_blocks, int nkv, float scale_log2, int tps,
     float* __restrict__ part_acc, float* __restrict__ part_ml, __nv_bfloat16* __restrict__ out, int nsplit,
-    int window = 0) {
+    int window = 0, float softcap = 0.f) {
   constexpr int E = HD / 32;          // value dims per lane
   __shared__ float q_s[G][HD];
   __shared__ __align__(16) float p_s[kAttnWarps][kPage][G < 4 ? 4 : G];
@@ -122,6 +122,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       s[g] += __shfl_xor_sync(0xffffffffu, s[g], 16);
+      if (softcap > 0.f) {   // logit softcapping c tanh(x / c) on the natural-scale score
+        const float x = s[g] * 0.69314718055994531f;
+        s[g] = softcap * tanhf(x / softcap) * 1.4426950408889634f;
+      }
       if (!valid) s[g] = -INFINITY;
     }
 #pragma unroll
@@ -264,7 +268,7 @@ using namespace b200;
 void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                             torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
                             torch::Tensor part_acc, torch::Tensor part_ml, double scale, int64_t tps,
-                            int64_t nsplit, int64_t window) {
+                            int64_t nsplit, int64_t window, double softcap) {
   const int B = q.size(0), nq = q.size(1), HD = q.size(2);
   const int nkv = k_cache.size(1);
   const int G = nq / nkv;
@@ -287,7 +291,7 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tenso
 #define B200_DEC(HDV, GV)                                                                                    \
   launch_pdl(paged_decode_kernel<HDV, GV>, grid, dim3(kAttnWarps * 32), 0, stream, qp, kp, vp,                \
              (const int*)block_tables.data_ptr<int>(), (const int*)seq_lens.data_ptr<int>(),                  \
-             (int)block_tables.size(1), nkv, sl2, (int)tps, pa, pm, op, (int)nsplit, (int)window)
+             (int)block_tables.size(1), nkv, sl2, (int)tps, pa, pm, op, (int)nsplit, (int)window, (float)softcap)
   if (HD == 256 && G == 4) B200_DEC(256, 4);
   else if (HD == 256 && G == 2) B200_DEC(256, 2);
   else if (HD == 256 && G == 1) B200_DEC(256, 1);

@@ -45,7 +45,8 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(
     const __nv_bfloat16* __restrict__ v_cache, const int* __restrict__ block_tables, int max_blocks,
     const int* __restrict__ seq_lens, const int* __restrict__ q_start, const int* __restrict__ cu_q,
     __nv_bfloat16* __restrict__ out, int nq, int nkv, float scale_log2, const uint8_t* __restrict__ kq,
-    const uint8_t* __restrict__ vq, const __half* __restrict__ ksc, const __half* __restrict__ vsc, int window) {
+    const uint8_t* __restrict__ vq, const __half* __restrict__ ksc, const __half* __restrict__ vsc, int window,
+    float softcap) {
   constexpr int LD = HD + 8;  // padded smem row (bf16) -> conflict-free 32-bit fragment loads
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);          // [2][64][LD]
@@ -187,8 +188,13 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(
         const bool valid_k = kpos < kv_end;
         const bool in_a = kpos <= qpos_a && (window == 0 || kpos > qpos_a - window);
         const bool in_b = kpos <= qpos_b && (window == 0 || kpos > qpos_b - window);
-        s[j][e] = (valid_k && in_a) ? s[j][e] * scale_log2 : -INFINITY;
-        s[j][2 + e] = (valid_k && in_b) ? s[j][2 + e] * scale_log2 : -INFINITY;
+        float xa = s[j][e] * scale_log2, xb = s[j][2 + e] * scale_log2;
+        if (softcap > 0.f) {   // c tanh(x / c) on the natural-scale score, back to log2 units
+          xa = softcap * tanhf(xa * 0.69314718055994531f / softcap) * 1.4426950408889634f;
+          xb = softcap * tanhf(xb * 0.69314718055994531f / softcap) * 1.4426950408889634f;
+        }
+        s[j][e] = (valid_k && in_a) ? xa : -INFINITY;
+        s[j][2 + e] = (valid_k && in_b) ? xb : -INFINITY;
         mx_a = fmaxf(mx_a, s[j][e]);
         mx_b = fmaxf(mx_b, s[j][2 + e]);
       }
@@ -292,7 +298,7 @@ using namespace b200;
 static void prefill_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                          torch::Tensor seq_lens, torch::Tensor q_start, torch::Tensor cu_q, torch::Tensor out,
                          double scale, int64_t max_q, int kvq, const uint8_t* kq, const uint8_t* vq,
-                         const __half* ksc, const __half* vsc, int window = 0) {
+                         const __half* ksc, const __half* vsc, int window = 0, float softcap = 0.f) {
   const int T = q.size(0), nq = q.size(1), HD = q.size(2);
   const int nkv = k_cache.size(1);
   const int nseq = seq_lens.size(0);
@@ -315,7 +321,7 @@ static void prefill_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v
         reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()), (const int*)block_tables.data_ptr<int>(),   \
         (int)block_tables.size(1), (const int*)seq_lens.data_ptr<int>(), (const int*)q_start.data_ptr<int>(),    \
         (const int*)cu_q.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nq, nkv, sl2,       \
-        kq, vq, ksc, vsc, window);                                                                              \
+        kq, vq, ksc, vsc, window, softcap);                                                                     \
   }
   if (kvq) {
     TORCH_CHECK(HD == 128, "int4 KV cache needs head_dim 128");
@@ -330,9 +336,10 @@ static void prefill_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v
 
 void paged_prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                              torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor q_start,
-                             torch::Tensor cu_q, torch::Tensor out, double scale, int64_t max_q, int64_t window) {
+                             torch::Tensor cu_q, torch::Tensor out, double scale, int64_t max_q, int64_t window,
+                             double softcap) {
   prefill_impl(q, k_cache, v_cache, block_tables, seq_lens, q_start, cu_q, out, scale, max_q, 0, nullptr, nullptr,
-               nullptr, nullptr, (int)window);
+               nullptr, nullptr, (int)window, (float)softcap);
 }
 
 // int4g128 cache: k_codes/v_codes [blocks][nkv][16][64] uint8, k_scale/v_scale [blocks][nkv][16] fp16.

@@ -23,15 +23,17 @@ void qkv_post(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optiona
               int64_t nkv, double eps);
 void silu_mul(torch::Tensor gu, torch::Tensor act);
 void gelu_tanh_mul(torch::Tensor gu, torch::Tensor act);
+void softcap_(torch::Tensor x, double cap);
 void row_sigmoid_scale(torch::Tensor x, torch::Tensor g);
 void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
 void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                             torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
                             torch::Tensor part_acc, torch::Tensor part_ml, double scale, int64_t tps,
-                            int64_t nsplit, int64_t window);
+                            int64_t nsplit, int64_t window, double softcap);
 void paged_prefill_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                              torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor q_start,
-                             torch::Tensor cu_q, torch::Tensor out, double scale, int64_t max_q, int64_t window);
+                             torch::Tensor cu_q, torch::Tensor out, double scale, int64_t max_q, int64_t window,
+                             double softcap);
 void paged_decode_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                                torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
                                torch::Tensor part_acc, torch::Tensor part_ml, double scale, int64_t tps,
@@ -138,6 +140,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flag_pingpong", &flag_pingpong);
   m.def("silu_mul", &silu_mul);
   m.def("gelu_tanh_mul", &gelu_tanh_mul);
+  m.def("softcap_", &softcap_);
   m.def("row_sigmoid_scale", &row_sigmoid_scale);
   m.def("embedding", &embedding);
   m.def("paged_decode_attention", &paged_decode_attention);

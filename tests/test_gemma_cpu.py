@@ -68,3 +68,17 @@ def test_gemma1_matches_hf():
     cfg = from_hf_config(json.loads(c.to_json_string()), "tiny-gemma")
     assert cfg.act == "gelu_tanh" and not cfg.sandwich_norms
     _check(model, cfg)
+
+
+def test_gemma2_softcaps_match_hf():
+    c = transformers.Gemma2Config(vocab_size=1000, hidden_size=128, intermediate_size=256, num_hidden_layers=4,
+                                  num_attention_heads=4, num_key_value_heads=2, head_dim=32, sliding_window=16,
+                                  max_position_embeddings=512, attn_logit_softcapping=5.0,
+                                  final_logit_softcapping=3.0)
+    c._attn_implementation = "eager"
+    torch.manual_seed(0)
+    model = transformers.Gemma2ForCausalLM(c).eval()
+    _perturb(model, 9)
+    cfg = from_hf_config(json.loads(c.to_json_string()), "tiny-gemma2")
+    assert cfg.attn_softcap == 5.0 and cfg.final_softcap == 3.0 and cfg.window(0) == 16 and cfg.window(1) == 0
+    _check(model, cfg)

@@ -363,3 +363,30 @@ def test_qwen3_next_engine_gpu_matches_cpu():
             eng.unload()
     for a, b in zip(outs["cuda"], outs["cpu"]):
         assert _rel(a, b) < 6e-2       # bf16 through DeltaNet and routed experts (measured 0.034)
+
+
+def test_softcapped_windowed_attention_and_logits():
+    hd, nq, nkv, W, cap = 256, 8, 4, 40, 5.0
+    lens = [7, 90, 300]
+    kc, vc, bt = _make_paged(3, lens, nkv, hd, 256)
+    q = (torch.randn(3, nq, hd, device=dev) * 3).bfloat16()
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    scale = 1 / math.sqrt(hd)
+    ws = ops.AttnWorkspace(dev, 3, nkv, nq // nkv, hd, 4)
+    y = ops.paged_decode_attention(q, kc, vc, bt, sl, scale, 128, 3, ws, window=W, softcap=cap)
+    ref = ops.paged_decode_attention(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), sl.cpu(), scale, window=W, softcap=cap)
+    assert _rel(y.cpu(), ref) < 1e-2
+    chunks = [(0, 100), (37, 50)]
+    plens = [s + n for s, n in chunks]
+    kc, vc, bt = _make_paged(2, plens, nkv, hd, 256)
+    qp = (torch.randn(150, nq, hd, device=dev) * 3).bfloat16()
+    cu = torch.tensor([0, 100, 150], dtype=torch.int32, device=dev)
+    q_start = torch.tensor([0, 37], dtype=torch.int32, device=dev)
+    psl = torch.tensor(plens, dtype=torch.int32, device=dev)
+    yp = ops.paged_prefill_attention(qp, kc, vc, bt, psl, q_start, cu, scale, max_q=100, window=W, softcap=cap)
+    refp = ops.paged_prefill_attention(qp.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), psl.cpu(), q_start.cpu(), cu.cpu(),
+                                       scale, window=W, softcap=cap)
+    assert _rel(yp.cpu(), refp) < 1e-2
+    lg = torch.randn(5, 1000, device=dev) * 20
+    ref_lg = 30.0 * torch.tanh(lg.cpu() / 30.0)
+    assert _rel(ops.softcap_(lg, 30.0).cpu(), ref_lg) < 1e-5
