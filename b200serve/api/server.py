@@ -196,6 +196,8 @@ def _produce(engine, messages, max_tokens, samp, q: _StreamQueue, enable_thinkin
             if calls:
                 q.put(("tool_calls", calls))
         st = getattr(engine, "_last_gen_stats", None) or {}
+        if st.get("context_fit"):
+            q.put(("context_fit", st["context_fit"]))
         q.put(("usage", {"prompt_tokens": st.get("prompt_tokens", 0),
                          "completion_tokens": st.get("completion_tokens", 0),
                          "finish_reason": st.get("finish_reason", "stop"),
@@ -356,6 +358,8 @@ def create_app(engine=None, keystore: KeyStore = None):
                             deltas = [dict(c, index=i) for i, c in enumerate(data)]
                             yield _make_sse_chunk(chat_id, model, {"tool_calls": deltas})
                             finish = "tool_calls"
+                        elif kind == "context_fit":
+                            yield f"data: {json.dumps({'x_context_fit': data})}\n\n"
                         elif kind == "telemetry":
                             yield f"data: {json.dumps({'x_telemetry': data})}\n\n"
                         elif kind == "usage":
@@ -376,14 +380,21 @@ def create_app(engine=None, keystore: KeyStore = None):
                                      headers={"Cache-Control": "no-cache", "X-Accel-Buffering": "no"})
 
         tkw = {"tools": tools} if tools else {}
+
+        def _run():
+            # the stats are read in the thread that generated: concurrent requests each see their own
+            out = eng.generate_streaming(messages, max_tokens=max_tokens, temperature=samp["temperature"],
+                                         enable_thinking=enable_thinking, raw_output=True, sampling=samp, **tkw)
+            return out, dict(getattr(eng, "_last_gen_stats", None) or {})
+
         try:
-            text = await asyncio.to_thread(
-                lambda: eng.generate_streaming(messages, max_tokens=max_tokens, temperature=samp["temperature"],
-                                               enable_thinking=enable_thinking, raw_output=True, sampling=samp,
-                                               **tkw))
+            text, st = await asyncio.to_thread(_run)
+        except ValueError as e:
+            raise HTTPException(status_code=400, detail=str(e))
         finally:
             mq.request_finished()
-        st = getattr(eng, "_last_gen_stats", None) or {}
+        if fit["compacted"] or fit["trimmed"]:
+            st.setdefault("context_fit", fit)
         pt, ct = st.get("prompt_tokens", 0), st.get("completion_tokens", 0)
         msg = {"role": "assistant", "content": text or ""}
         finish = st.get("finish_reason", "stop")
@@ -393,10 +404,13 @@ def create_app(engine=None, keystore: KeyStore = None):
             if calls:
                 msg = {"role": "assistant", "content": visible or None, "tool_calls": calls}
                 finish = "tool_calls"
-        return {"id": chat_id, "object": "chat.completion", "created": int(time.time()), "model": model,
+        resp = {"id": chat_id, "object": "chat.completion", "created": int(time.time()), "model": model,
                 "choices": [{"index": 0, "message": msg, "finish_reason": finish}],
                 "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct},
                 "x_backend": backend, "x_stats": st}
+        if st.get("context_fit"):
+            resp["x_context_fit"] = st["context_fit"]
+        return resp
 
     from b200serve.api.chat_jobs import register_chat_job_routes
     register_chat_job_routes(app, auth, _get_engine)

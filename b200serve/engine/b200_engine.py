@@ -60,12 +60,28 @@ class B200Engine(BaseEngine):
         self._stop = threading.Event()
         self._wake = threading.Condition()
         self._error = None
-        self._last_gen_stats = None
+        self._stats_tls = threading.local()
+        self._shared_stats = None
         self.rank = 0
         self.world = 1
         self._step_t0 = None        # start of the step in progress (watchdog)
         self.stalled = False
         self._watch = None
+
+    # ------------------------------------------------------------ per-request stats
+    @property
+    def _last_gen_stats(self):
+        """Stats of the last generate_streaming call made by THIS thread (the reference's
+        attribute name and keys). Concurrent requests each run in their own thread, so one
+        request never reads another's usage or finish_reason; a thread that has not generated
+        sees the most recent call of any thread."""
+        mine = getattr(self._stats_tls, "stats", None)
+        return mine if mine is not None else self._shared_stats
+
+    @_last_gen_stats.setter
+    def _last_gen_stats(self, value):
+        self._stats_tls.stats = value
+        self._shared_stats = value
 
     # ------------------------------------------------------------ lifecycle
     def is_loaded(self) -> bool:
@@ -326,6 +342,30 @@ class B200Engine(BaseEngine):
         return reqs
 
     # ------------------------------------------------------------ BaseEngine
+    def _fit_prompt(self, messages, max_tokens, enable_thinking, tools):
+        """Chat template -> token ids that fit the context with room for ``max_tokens``.
+
+        A conversation that does not fit is compacted and trimmed by ``ensure_context_fit``
+        (the reference's pre-flight, core/inference.py ensure_context_fit) and the result is
+        reported as the ``context_fit`` stat (the API's ``x_context_fit``). A prompt that still
+        leaves no room for one completion token raises ValueError: the head of the prompt
+        (the system prompt) is never dropped silently."""
+        ctx = self.config.max_seq
+        tmpl = lambda msgs: self.tokenizer.apply_chat_template(msgs, add_generation_prompt=True,
+                                                               enable_thinking=enable_thinking, tools=tools)
+        prompt = tmpl(messages)
+        fit = None
+        if len(prompt) + min(max_tokens, ctx // 4) > ctx:
+            from b200serve.core.inference import ensure_context_fit
+            messages, fit = ensure_context_fit(messages, ctx, min(max_tokens, ctx // 4),
+                                               count_fn=self.count_tokens)
+            prompt = tmpl(messages)
+            fit = dict(fit, prompt_tokens=len(prompt))
+        if len(prompt) >= ctx:
+            raise ValueError(f"prompt of {len(prompt)} tokens does not fit the {ctx}-token context "
+                             f"even after compaction; shorten the conversation")
+        return prompt, fit
+
     def generate_streaming(self, messages, max_tokens, temperature, on_token=None, on_complete=None,
                            enable_thinking=True, grammar=None, response_format=None, raw_output=False,
                            web_tools=False, reasoning_effort=None, on_telemetry=None, sampling=None,
@@ -333,24 +373,31 @@ class B200Engine(BaseEngine):
         self.load()
         params = SamplingParams.from_dict(sampling, temperature=temperature,
                                           max_tokens=max_tokens if max_tokens and max_tokens > 0 else 8192)
-        prompt = self.tokenizer.apply_chat_template(messages, add_generation_prompt=True,
-                                                    enable_thinking=enable_thinking, tools=tools)
-        prompt = prompt[-(self.config.max_seq - 1):]
-        stop_strings = list(STOP_STRINGS) + list(params.stop)
+        prompt, fit = self._fit_prompt(messages, params.max_tokens, enable_thinking, tools)
+        if len(prompt) + params.max_tokens > self.config.max_seq:
+            params.max_tokens = self.config.max_seq - len(prompt)
+        # the reference halts at once on a faked conversational turn (STOP_STRINGS, applied by
+        # core/engine_transformers.py:1255 through StopStringCriteria) and on the request's stops
+        stop_strings = [s for s in list(STOP_STRINGS) + list(params.stop) if s]
+        hold = max((len(s) for s in stop_strings), default=0) + 8
         q = queue.Queue()
         dec = IncrementalDecoder(self.tokenizer)
         text_so_far = [""]
+        stopped_by = [None]
 
         def _cb(req, tok):
             delta = dec.push(tok)
             if tok in req.stop_ids:
                 delta = ""
             q.put(("tok", delta))
-            if delta:
+            if delta and stop_strings:
                 text_so_far[0] += delta
-                tail = text_so_far[0][-64:]
-                if any(s in tail for s in params.stop):
-                    return True
+                tail = text_so_far[0][-(len(delta) + hold):]
+                for s_ in stop_strings:
+                    if s_ in tail:
+                        stopped_by[0] = s_
+                        return True
+                text_so_far[0] = text_so_far[0][-4 * hold:]
             return False
 
         t_start = time.perf_counter()
@@ -400,6 +447,10 @@ class B200Engine(BaseEngine):
             "ttft": round(ttft, 3), "decode_tok_per_sec": round(max(n - 1, 0) / dec_time, 1) if dec_time > 0 else 0,
             "prefix_hit_tokens": req.prefix_hit,
         }
+        if stopped_by[0] is not None:
+            self._last_gen_stats["stop_string"] = stopped_by[0]
+        if fit is not None:
+            self._last_gen_stats["context_fit"] = fit
         if callback_error is not None:
             raise callback_error
         if self._error is not None and req.finish_reason == "error":

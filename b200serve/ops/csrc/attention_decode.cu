@@ -325,6 +325,7 @@ void paged_decode_combine(torch::Tensor part_acc, torch::Tensor part_ml, torch::
   const int blocks = (B * nq * 32 + threads - 1) / threads;
   auto stream = at::cuda::getCurrentCUDAStream();
   auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  TORCH_CHECK(HD == 128 || HD == 64, "paged_decode_combine supports head_dim 64 and 128, got ", HD);
   if (HD == 128)
     launch_pdl(paged_decode_combine_kernel<128>, dim3(blocks), dim3(threads), 0, stream,
                (const float*)part_acc.data_ptr<float>(), (const float*)part_ml.data_ptr<float>(),
@@ -377,10 +378,11 @@ extern "C" __attribute__((visibility("default"))) int b200_paged_decode_attentio
   const int G = nq / nkv;
   const long need_acc = (long)B * nkv * nsplit * G * head_dim;
   const long need_ml = (long)B * nkv * nsplit * G * 2;
-  if (need_acc > (long)B200_NOALLOC_MAX_ACC_FLOATS)
+  // one split writes straight to `out` and uses no scratch, so only split calls have a limit
+  if (nsplit > 1 && need_acc > (long)B200_NOALLOC_MAX_ACC_FLOATS)
     return noalloc_fail(2, "scratch limit: needs %ld accumulator floats, maximum is %ld", need_acc,
                         (long)B200_NOALLOC_MAX_ACC_FLOATS);
-  if (need_ml > (long)B200_NOALLOC_MAX_ML_FLOATS)
+  if (nsplit > 1 && need_ml > (long)B200_NOALLOC_MAX_ML_FLOATS)
     return noalloc_fail(2, "scratch limit: needs %ld max/sum floats, maximum is %ld", need_ml,
                         (long)B200_NOALLOC_MAX_ML_FLOATS);
   int dev = 0;

@@ -92,7 +92,9 @@ void rmsnorm_rs_ag(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor
                    int64_t epoch_ptr, int64_t err_ptr, torch::Tensor dst_ptrs, torch::Tensor ag_flag_ptrs,
                    int64_t row0, int64_t T, torch::Tensor done);
 
-void flag_wait(int64_t flags_ptr, int64_t n, int64_t epoch_ptr, int64_t err_ptr);
+void flag_wait(int64_t flags_ptr, int64_t n, int64_t epoch_ptr, int64_t err_ptr, double timeout_ms);
+void set_flag_wait_ms(double ms);
+double get_flag_wait_ms();
 void flag_pingpong(int64_t mine_ptr, int64_t peer_ptr, int64_t iters, int64_t initiator, int64_t mode,
                    torch::Tensor out);
 
@@ -136,7 +138,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("host_error_word", &host_error_word);
   m.def("read_host_word", &read_host_word);
   m.def("epoch_inc", &epoch_inc);
-  m.def("flag_wait", &flag_wait);
+  m.def("flag_wait", &flag_wait, py::arg("flags_ptr"), py::arg("n"), py::arg("epoch_ptr"), py::arg("err_ptr"),
+        py::arg("timeout_ms") = -1.0);
+  m.def("set_flag_wait_ms", &set_flag_wait_ms);
+  m.def("get_flag_wait_ms", &get_flag_wait_ms);
   m.def("flag_pingpong", &flag_pingpong);
   m.def("silu_mul", &silu_mul);
   m.def("gelu_tanh_mul", &gelu_tanh_mul);

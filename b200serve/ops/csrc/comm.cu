@@ -16,6 +16,8 @@
 // finished reading site (stream order), so no slot is overwritten while read.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
+#include <algorithm>
+#include <cstdlib>
 #include "common.cuh"
 
 namespace b200 {
@@ -26,14 +28,15 @@ __global__ void epoch_inc_kernel(int* epoch) {
   if (threadIdx.x == 0) *epoch += 1;
 }
 
-// One thread waits (bounded, 2 s) until flags[0..n) all hold *epoch: orders a consumer that
-// cannot wait by itself (a library kernel) after the peers' all-gather pushes.
-__global__ void flag_wait_kernel(const int* flags, int n, const int* epoch, int* err) {
+// One thread waits (bounded by wait_ns) until flags[0..n) all hold *epoch: orders a consumer
+// that cannot wait by itself (a library kernel) after the peers' all-gather pushes. On expiry
+// it records 140 + r in *err and returns, so the context stays usable.
+__global__ void flag_wait_kernel(const int* flags, int n, const int* epoch, int* err, uint64_t wait_ns) {
   pdl_wait();
   pdl_trigger();
   if (threadIdx.x != 0) return;
   const int e = *epoch;
-  const uint64_t deadline = globaltimer_ns() + 2000000000ull;
+  const uint64_t deadline = globaltimer_ns() + wait_ns;
   for (int r = 0; r < n; ++r) {
     uint32_t it = 0;
     while (true) {
@@ -85,9 +88,28 @@ __global__ void flag_pingpong_kernel(volatile int* mine, int* peer, int iters, i
   *out = (long long)(globaltimer_ns() - t0);
 }
 
+static uint64_t g_flag_wait_ns = 0;
+
+uint64_t flag_wait_ns() {
+  if (g_flag_wait_ns == 0) {
+    const char* e = getenv("B200_FLAG_WAIT_MS");
+    const long ms = e ? atol(e) : 2000;
+    g_flag_wait_ns = (uint64_t)std::max(1L, ms) * 1000000ull;
+  }
+  return g_flag_wait_ns;
+}
+
 }  // namespace b200
 
 using namespace b200;
+
+// Deadline of the cross-GPU flag waits for kernels launched (or graphs captured) from now on.
+void set_flag_wait_ms(double ms) {
+  TORCH_CHECK(ms > 0, "flag wait deadline must be positive");
+  g_flag_wait_ns = (uint64_t)(ms * 1e6);
+}
+
+double get_flag_wait_ms() { return (double)flag_wait_ns() / 1e6; }
 
 void flag_pingpong(int64_t mine_ptr, int64_t peer_ptr, int64_t iters, int64_t initiator, int64_t mode,
                    torch::Tensor out) {
@@ -97,10 +119,12 @@ void flag_pingpong(int64_t mine_ptr, int64_t peer_ptr, int64_t iters, int64_t in
   B200_CHECK_CUDA(cudaGetLastError());
 }
 
-void flag_wait(int64_t flags_ptr, int64_t n, int64_t epoch_ptr, int64_t err_ptr) {
+// timeout_ms <= 0: the process-wide deadline (flag_wait_ns)
+void flag_wait(int64_t flags_ptr, int64_t n, int64_t epoch_ptr, int64_t err_ptr, double timeout_ms) {
+  const uint64_t ns = timeout_ms > 0 ? (uint64_t)(timeout_ms * 1e6) : flag_wait_ns();
   launch_pdl(flag_wait_kernel, dim3(1), dim3(32), 0, at::cuda::getCurrentCUDAStream(),
              reinterpret_cast<const int*>(flags_ptr), (int)n, reinterpret_cast<const int*>(epoch_ptr),
-             reinterpret_cast<int*>(err_ptr));
+             reinterpret_cast<int*>(err_ptr), ns);
 }
 
 int64_t ipc_malloc(int64_t bytes) {

@@ -88,6 +88,11 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 bool pdl_enabled();
 
+// Deadline (ns) of every cross-GPU flag wait, passed to the kernels as an argument (so a CUDA
+// graph keeps the value it was captured with). Default 2 s; B200_FLAG_WAIT_MS or
+// set_flag_wait_ms() change it.
+uint64_t flag_wait_ns();
+
 template <typename... KArgs, typename... Args>
 inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                        Args&&... args) {

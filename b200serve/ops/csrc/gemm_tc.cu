@@ -242,6 +242,7 @@ static void gemm_tc_impl(torch::Tensor act, torch::Tensor w, torch::Tensor out, 
   p.ag_flags = ag_flags;
   p.ag_n = ag_n;
   p.ag_epoch = ag_epoch;
+  p.ag_wait_ns = flag_wait_ns();
   if (qkv) {
     p.qkv_nq = qkv->qkv_nq; p.qkv_nkv = qkv->qkv_nkv; p.q_norm = qkv->q_norm; p.k_norm = qkv->k_norm;
     p.cos_sin = qkv->cos_sin; p.positions = qkv->positions; p.slots = qkv->slots; p.q_out = qkv->q_out;

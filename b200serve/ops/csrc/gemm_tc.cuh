@@ -63,6 +63,7 @@ struct GemmParams {
   const int* ag_flags;
   int ag_n;
   const int* ag_epoch;
+  unsigned long long ag_wait_ns;  // deadline of the all-gather flag wait
   const uint8_t* w_ptr;         // packed weight base (L2 prefetch), or null
   int l2_prefetch_blocks;       // weight tiles per CTA prefetched into L2 before the dependency wait
   void* out;                    // bf16 or fp32, row stride ldo (elements)
@@ -292,11 +293,11 @@ __device__ __forceinline__ int w_y(const GemmParams& p, int w_tile, int kb) {
   return p.w_packed ? (w_tile * p.kb_total + kb) * 128 : w_tile * 128;
 }
 
-// All-gather -> GEMM: spin (bounded, 2 s) until every rank published this step's epoch for the
-// gathered activation rows, then order the async proxy (TMA) after those acquires.
+// All-gather -> GEMM: spin (bounded by ag_wait_ns) until every rank published this step's epoch
+// for the gathered activation rows, then order the async proxy (TMA) after those acquires.
 __device__ __forceinline__ bool wait_ag_flags(const GemmParams& p, volatile int* abort_flag, int* err) {
   const int e = *p.ag_epoch;
-  const uint64_t deadline = globaltimer_ns() + 2000000000ull;
+  const uint64_t deadline = globaltimer_ns() + p.ag_wait_ns;
   for (int r = 0; r < p.ag_n; ++r) {
     uint32_t it = 0;
     while (true) {

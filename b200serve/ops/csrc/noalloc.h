@@ -26,6 +26,11 @@ extern "C" {
 //   block_tables [B, max_blocks] int32            seq_lens [B] int32 (tokens incl. the new one)
 //   out          [B, nq, head_dim] bf16 (written)
 //   tokens_per_split: multiple of 16; nsplit: number of KV splits (grid size)
+// Caller preconditions (seq_lens lives on the device, so the entry point cannot check them):
+//   * seq_lens[b] <= max_blocks * 16 for every b: keys past the block table are never read;
+//   * seq_lens[b] <= nsplit * tokens_per_split: split s covers keys [s*tps, (s+1)*tps), so keys
+//     past the last split are dropped and the result is wrong although the call returns 0.
+// With nsplit == 1 the kernel writes `out` directly and uses no scratch (no size limit).
 // Returns 0 on success, otherwise a nonzero code with a message available from
 // b200_noalloc_last_error(). Every call on a device shares the same scratch
 // array and leaves its contents behind; no state is carried between calls

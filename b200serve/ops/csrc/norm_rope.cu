@@ -27,12 +27,13 @@ struct AgArgs {
 // y = rmsnorm(sum(parts) [+ residual_in]) * w ; residual_out = the pre-norm sum.
 // One CTA per row, 8 bf16 per thread per step, at most 4 steps (H <= 32768 with 1024 threads).
 // Wait (one thread per CTA) until every rank has published this step's epoch
-// for the site; bounded by a 2 s deadline, after which an error code is
+// for the site; bounded by `wait_ns`, after which an error code is
 // recorded and the CTA proceeds (the host raises on the error word).
-__device__ __forceinline__ void wait_peer_flags(const int* flags, const int* epoch, int n, int* err) {
+__device__ __forceinline__ void wait_peer_flags(const int* flags, const int* epoch, int n, int* err,
+                                                uint64_t wait_ns) {
   if (threadIdx.x == 0) {
     const int e = *epoch;
-    const uint64_t deadline = globaltimer_ns() + 2000000000ull;
+    const uint64_t deadline = globaltimer_ns() + wait_ns;
     for (int r = 0; r < n; ++r) {
       uint32_t it = 0;
       while (true) {
@@ -56,11 +57,11 @@ template <int VPT>
 __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
     PartPtrs parts, int nparts, const __nv_bfloat16* residual_in, __nv_bfloat16* residual_out,
     const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H, float eps,
-    const int* wait_flags, const int* epoch, int* err, const AgArgs ag) {
+    const int* wait_flags, const int* epoch, int* err, const AgArgs ag, uint64_t wait_ns) {
   __shared__ float red[32];
   pdl_wait();
   pdl_trigger();
-  if (wait_flags) wait_peer_flags(wait_flags, epoch, nparts, err);
+  if (wait_flags) wait_peer_flags(wait_flags, epoch, nparts, err, wait_ns);
   const int row = blockIdx.x;
   const size_t base = (size_t)row * H;
   float v[VPT][8];
@@ -301,10 +302,10 @@ void rmsnorm_fused_impl(std::vector<torch::Tensor> parts, c10::optional<torch::T
   auto wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   switch (vpt) {
-    case 1: launch_pdl(rmsnorm_fused_kernel<1>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag); break;
-    case 2: launch_pdl(rmsnorm_fused_kernel<2>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag); break;
+    case 1: launch_pdl(rmsnorm_fused_kernel<1>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns()); break;
+    case 2: launch_pdl(rmsnorm_fused_kernel<2>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns()); break;
     case 3:
-    case 4: launch_pdl(rmsnorm_fused_kernel<4>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag); break;
+    case 4: launch_pdl(rmsnorm_fused_kernel<4>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns()); break;
     default: TORCH_CHECK(false, "hidden size too large");
   }
   B200_CHECK_CUDA(cudaGetLastError());

@@ -30,6 +30,15 @@ class CollectiveTimeout(RuntimeError):
     """A fused collective's bounded wait expired (a peer rank did not publish)."""
 
 
+def check_error_word(host_ptr: int, rank: int = 0):
+    """Read (and clear) a host-mapped error word written by the kernels' bounded waits;
+    raise CollectiveTimeout when one of them gave up. Codes: 100+r / 120+r / 140+r = the
+    norm, the all-gather GEMM or the flag-wait kernel stopped waiting for rank r."""
+    code = ops.ext().read_host_word(host_ptr, 0, True)
+    if code:
+        raise CollectiveTimeout(f"fused collective wait expired on rank {rank} (code {code})")
+
+
 def fused_available() -> bool:
     try:
         return hasattr(ops.ext(), "gemm_tc_push")
@@ -229,9 +238,7 @@ class FusedComm:
         self.nccl.barrier()
 
     def check(self):
-        code = ops.ext().read_host_word(self.err_host, 0, True)
-        if code:
-            raise CollectiveTimeout(f"fused all-reduce wait expired on rank {self.rank} (code {code})")
+        check_error_word(self.err_host, self.rank)
 
     def close(self):
         e = ops.ext()

@@ -1,6 +1,6 @@
 #!/usr/bin/env python
 """Headline benchmark: decode tok/s + p50 TTFT of the Qwen3-8B shape in bf16,
-tensor-parallel over N GPUs of one node.
+tensor-parallel over N GPUs of one node (Qwen3-8B shape, batch 32, 2048-token prompts).
 
   python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
   (N > 1: launched by torch.distributed.run, one rank per GPU)

@@ -1,4 +1,4 @@
-"""tiny Qwen2 (2 layers, hidden 256, 4/2 heads, FFN 688,
+"""Tiny Qwen2 oracle config: tiny Qwen2 (2 layers, hidden 256, 4/2 heads, FFN 688,
 vocab 32000, N(0, 0.02) init from seed 0), 64-token prompt, greedy 32 tokens.
 The engine's CPU path must reproduce HF transformers fp32 token for token."""
 

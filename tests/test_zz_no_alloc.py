@@ -88,3 +88,68 @@ def test_noalloc_rejects_sizes_beyond_the_limit():
     rc, msg = _call(f, err, q, kc, vc, bt, sl, out, 0.088, 16, 4096)
     assert rc != 0
     assert "scratch limit" in msg
+
+
+def _fp32_reference(q, kc, vc, bt, sl, scale):
+    """Plain fp32 PyTorch attention of one query token per sequence over its gathered pages."""
+    B, nq, hd = q.shape
+    nkv = kc.shape[1]
+    G = nq // nkv
+    out = torch.empty(B, nq, hd, dtype=torch.float32, device=q.device)
+    for b in range(B):
+        L = int(sl[b])
+        n = (L + 15) // 16
+        pages = bt[b, :n].long()
+        k = kc[pages].float().permute(1, 0, 2, 3).reshape(nkv, n * 16, hd)[:, :L]
+        v = vc[pages].float().permute(1, 0, 2, 3).reshape(nkv, n * 16, hd)[:, :L]
+        qb = q[b].float().view(nkv, G, hd)
+        p = torch.softmax(torch.einsum("hgd,hld->hgl", qb, k) * scale, -1)
+        out[b] = torch.einsum("hgl,hld->hgd", p, v).reshape(nq, hd)
+    return out
+
+
+@pytest.mark.parametrize("B,lens,nq,nkv,hd,tps,nsplit", [
+    (4, [1, 300, 1000, 77], 32, 8, 128, 64, 16),     # split-KV through the shared scratch
+    (3, [900, 17, 512], 32, 8, 128, 1024, 1),        # one split: direct write, no scratch
+    (5, [33, 700, 129, 1, 256], 16, 8, 64, 128, 6),  # head_dim 64, group 2, split
+])
+def test_noalloc_matches_fp32_reference(B, lens, nq, nkv, hd, tps, nsplit):
+    f, err = _fn()
+    for seed in (10, 11):                            # two calls in a row
+        q, kc, vc, bt, sl = _case(B, lens, nq, nkv, hd, seed)
+        scale = 1.0 / math.sqrt(hd)
+        out = torch.full_like(q, float("nan"))
+        rc, msg = _call(f, err, q, kc, vc, bt, sl, out, scale, tps, nsplit)
+        assert rc == 0, msg
+        torch.cuda.synchronize()
+        ref = _fp32_reference(q, kc, vc, bt, sl, scale)
+        rel = ((out.float() - ref).norm() / ref.norm()).item()
+        assert rel < 1e-2, rel
+
+
+def test_noalloc_single_split_has_no_scratch_limit():
+    f, err = _fn()
+    # 512 x 32 heads x 128 dims of partials would exceed the limit, but one split needs none
+    B = 512
+    q, kc, vc, bt, sl = _case(B, [32] * B, 32, 8, 128, 3)
+    out = torch.full_like(q, float("nan"))
+    rc, msg = _call(f, err, q, kc, vc, bt, sl, out, 1.0 / math.sqrt(128), 32, 1)
+    assert rc == 0, msg
+    torch.cuda.synchronize()
+    ref = _fp32_reference(q[:8], kc, vc, bt[:8], sl[:8], 1.0 / math.sqrt(128))
+    rel = ((out[:8].float() - ref).norm() / ref.norm()).item()
+    assert rel < 1e-2, rel
+
+
+def test_noalloc_empty_batch_and_unsupported_shape():
+    f, err = _fn()
+    q, kc, vc, bt, sl = _case(2, [64, 64], 32, 8, 128, 4)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = f(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), bt.data_ptr(), sl.data_ptr(), out.data_ptr(), 0, 32, 8, 128,
+           bt.shape[1], 0.088, 64, 1, stream)
+    assert rc == 0, err().decode()
+    q2, kc2, vc2, bt2, sl2 = _case(2, [64, 64], 8, 2, 256, 5)
+    out2 = torch.empty_like(q2)
+    rc, msg = _call(f, err, q2, kc2, vc2, bt2, sl2, out2, 0.0625, 64, 1)
+    assert rc == 5 and "unsupported head_dim" in msg
