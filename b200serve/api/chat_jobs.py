@@ -9,23 +9,25 @@ Same routes and observable behaviour as the reference's chat jobs (api/chat_jobs
 A client (a phone that went to sleep, a closed browser tab) can drop the event stream and
 re-attach later without losing the generation.
 
-The job runs the engine's streaming generation in its own thread and keeps the chunks in a
-bounded ring (the newest 400, trimmed by 200), each with a serial number; listeners resume
-from the last serial they saw.
+The job runs the engine's streaming generation in its own thread. What it produces goes to
+an append-only event log (numbered events, newest 512 retained) plus the job's accumulated
+text; the SSE payloads are rendered when a reader takes the events. A reader resumes after
+the last event number it saw, and one that fell out of the retention window gets a fresh
+snapshot instead of a gap.
 """
 
 
 import json
+import secrets
 import threading
 import time
-import uuid
+from collections import deque
+from enum import Enum
 from typing import List, Optional
 
 from pydantic import BaseModel
 
 from b200serve.core.inference import ThinkFilter
-
-_RING_MAX, _RING_TRIM = 400, 200
 
 
 class ChatJobRequest(BaseModel):
@@ -40,85 +42,133 @@ class ChatJobRequest(BaseModel):
     options: Optional[dict] = None
 
 
+class JobState(str, Enum):
+    RUNNING = "running"
+    DONE = "done"
+    ERROR = "error"
+    STOPPED = "stopped"
+
+    @property
+    def final(self) -> bool:
+        return self is not JobState.RUNNING
+
+
+class EventLog:
+    """Append-only log of (kind, data) events numbered 1, 2, 3, ... that retains the newest
+    ``retain`` events. A reader asks for everything after the number it saw last; a reader
+    that fell out of the retention window is told so and restarts from a snapshot (the job's
+    accumulated text is never trimmed, only the event history is)."""
+
+    def __init__(self, retain: int = 512):
+        self._events = deque(maxlen=retain)
+        self.last = 0                      # number of the newest event
+
+    def append(self, kind: str, data):
+        self.last += 1
+        self._events.append((self.last, kind, data))
+
+    @property
+    def oldest(self) -> int:
+        return self._events[0][0] if self._events else self.last + 1
+
+    def after(self, seen: int):
+        """(events after ``seen``, whether the reader missed events that were dropped)."""
+        missed = seen + 1 < self.oldest and seen < self.last
+        return [e for e in self._events if e[0] > seen], missed
+
+
 class _Stopped(Exception):
     pass
 
 
 class ChatJob:
-    def __init__(self, req: ChatJobRequest):
-        self.id = uuid.uuid4().hex[:12]
-        self.created = time.time()
+    """One background generation: accumulated text/thinking, usage, state, event log."""
+
+    def __init__(self, req: ChatJobRequest, retain: int = 512):
+        self.id = secrets.token_hex(6)
         self.req = req
-        self.status = "running"          # running | done | error | stopped
-        self.text = ""
-        self.thinking = ""
+        self.created = time.time()
+        self.ended: Optional[float] = None
+        self.state = JobState.RUNNING
+        self._text: list = []
+        self._thinking: list = []
         self.usage: dict = {}
         self.error = ""
-        self.finished_at: Optional[float] = None
-        self._cond = threading.Condition()
-        self._ring: list = []            # (serial, payload)
-        self._serial = 0
+        self.log = EventLog(retain)
+        self._cv = threading.Condition()
         self.stop_event = threading.Event()
+
+    # -- producer side
+    def record(self, kind: str, data):
+        with self._cv:
+            if kind == "content":
+                self._text.append(data)
+            elif kind == "thinking":
+                self._thinking.append(data)
+            elif kind == "usage":
+                self.usage = data
+            self.log.append(kind, data)
+            self._cv.notify_all()
+
+    def end(self, state: JobState, error: str = ""):
+        with self._cv:
+            if self.state.final:
+                return
+            self.state, self.ended = state, time.time()
+            if error:
+                self.error = error
+            self._cv.notify_all()
+
+    # -- reader side
+    @property
+    def status(self) -> str:
+        return self.state.value
 
     @property
     def terminal(self) -> bool:
-        return self.status in ("done", "error", "stopped")
-
-    def push(self, payload: dict):
-        with self._cond:
-            delta = ((payload.get("choices") or [{}])[0].get("delta") or {})
-            if delta.get("content"):
-                self.text += delta["content"]
-            th = delta.get("x_thinking") or payload.get("x_thinking")
-            if th:
-                self.thinking += th
-            if payload.get("x_usage"):
-                self.usage = payload["x_usage"]
-            self._serial += 1
-            self._ring.append((self._serial, payload))
-            if len(self._ring) > _RING_MAX:
-                del self._ring[:_RING_TRIM]
-            self._cond.notify_all()
-
-    def finish(self, status: str, error: str = ""):
-        with self._cond:
-            self.status = status
-            self.error = error or self.error
-            self.finished_at = time.time()
-            self._cond.notify_all()
+        return self.state.final
 
     def snapshot(self) -> dict:
-        with self._cond:
-            return {"job_id": self.id, "status": self.status, "created": self.created,
-                    "finished_at": self.finished_at, "session_id": self.req.session_id, "model": self.req.model,
-                    "text": self.text, "thinking": self.thinking, "usage": self.usage, "error": self.error}
+        with self._cv:
+            return {"job_id": self.id, "status": self.state.value, "created": self.created,
+                    "finished_at": self.ended, "session_id": self.req.session_id, "model": self.req.model,
+                    "text": "".join(self._text), "thinking": "".join(self._thinking), "usage": self.usage,
+                    "error": self.error}
 
-    def events_after(self, serial: int, timeout: float):
-        """(new payloads, last serial, terminal-and-drained) after ``serial``; waits up to
-        ``timeout`` s for something new while the job runs."""
-        with self._cond:
-            if self._serial == serial and not self.terminal:
-                self._cond.wait(timeout=timeout)
-            out = [(s, p) for s, p in self._ring if s > serial]
-            last = out[-1][0] if out else serial
-            return [p for _, p in out], last, self.terminal and last == self._serial
+    def wait_events(self, seen: int, timeout: float):
+        """Block up to ``timeout`` s for events after ``seen``. Returns (events, missed,
+        finished): finished is True once the job ended and the reader has every event."""
+        with self._cv:
+            if self.log.last == seen and not self.state.final:
+                self._cv.wait(timeout=timeout)
+            events, missed = self.log.after(seen)
+            newest = events[-1][0] if events else seen
+            return events, missed, self.state.final and newest == self.log.last
 
 
-def _chunk(job: ChatJob, delta: dict, finish=None, extra=None) -> dict:
-    ev = {"id": f"chatjob-{job.id}", "object": "chat.completion.chunk", "created": int(time.time()),
-          "model": job.req.model or "", "choices": [{"index": 0, "delta": delta, "finish_reason": finish}]}
-    if extra:
-        ev.update(extra)
-    return ev
+def render_event(job: ChatJob, kind: str, data) -> dict:
+    """An event as the SSE payload of the chat-completions stream format."""
+    if kind == "error":
+        return {"error": data}
+    base = {"id": f"chatjob-{job.id}", "object": "chat.completion.chunk", "created": int(time.time()),
+            "model": job.req.model or ""}
+    if kind == "usage":
+        finish = data.get("finish_reason", "stop")
+        usage = {k: v for k, v in data.items() if k != "finish_reason"}
+        return dict(base, choices=[{"index": 0, "delta": {}, "finish_reason": finish}], x_usage=usage)
+    delta = {"x_thinking": data} if kind == "thinking" else {"content": data}
+    return dict(base, choices=[{"index": 0, "delta": delta, "finish_reason": None}])
 
 
 def _run(job: ChatJob, engine, samp: dict, max_tokens: int, enable_thinking: bool):
-    def emit(kind, text):
-        if job.stop_event.is_set():
-            raise _Stopped()
-        job.push(_chunk(job, {"x_thinking": text} if kind == "thinking" else {"content": text}))
+    def emit(kind):
+        def put(text):
+            if job.stop_event.is_set():
+                raise _Stopped()          # raised inside the engine callback: generation aborts
+            job.record(kind, text)
+        return put
 
-    tf = ThinkFilter(on_response=lambda t: emit("content", t), on_thinking=lambda t: emit("thinking", t),
+    tf = ThinkFilter(on_response=emit("content"), on_thinking=emit("thinking"),
                      starts_in_think=bool(enable_thinking and getattr(engine, "stream_starts_in_think", True)))
     try:
         engine.generate_streaming(job.req.messages, max_tokens=max_tokens, temperature=samp.get("temperature", 0.7),
@@ -126,14 +176,14 @@ def _run(job: ChatJob, engine, samp: dict, max_tokens: int, enable_thinking: boo
         tf.flush()
         st = getattr(engine, "_last_gen_stats", None) or {}
         pt, ct = st.get("prompt_tokens", 0), st.get("completion_tokens", 0)
-        job.push(_chunk(job, {}, finish=st.get("finish_reason", "stop"),
-                        extra={"x_usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct}}))
-        job.finish("done")
+        job.record("usage", {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct,
+                             "finish_reason": st.get("finish_reason", "stop")})
+        job.end(JobState.DONE)
     except _Stopped:
-        job.finish("stopped")
+        job.end(JobState.STOPPED)
     except Exception as e:  # reported in the snapshot and the x_job_end event
-        job.push({"error": str(e)[:500]})
-        job.finish("error", str(e)[:500])
+        job.record("error", str(e)[:500])
+        job.end(JobState.ERROR, str(e)[:500])
 
 
 class JobStore:
@@ -202,20 +252,27 @@ def register_chat_job_routes(app, auth, get_engine, store: JobStore = None):
         job = _get(job_id)
 
         def gen():
-            with job._cond:
+            with job._cv:
                 snap = job.snapshot()
-                last = job._serial
+                seen = job.log.last
             yield "data: " + json.dumps({"x_snapshot": snap}) + "\n\n"
             if snap["status"] != "running":
                 yield "data: [DONE]\n\n"
                 return
             while True:
-                out, last, done = job.events_after(last, 15.0)
-                for p in out:
-                    yield "data: " + json.dumps(p) + "\n\n"
-                if not out:
+                events, missed, finished = job.wait_events(seen, 15.0)
+                if missed:                       # fell behind the retention window: resync
+                    with job._cv:
+                        snap = job.snapshot()
+                        seen = job.log.last
+                    yield "data: " + json.dumps({"x_snapshot": snap}) + "\n\n"
+                    events = []
+                for n, kind, data in events:
+                    seen = n
+                    yield "data: " + json.dumps(render_event(job, kind, data)) + "\n\n"
+                if not events and not missed:
                     yield ": ping\n\n"
-                if done:
+                if finished:
                     end = {"status": job.status, "error": job.error, "usage": job.usage}
                     yield "data: " + json.dumps({"x_job_end": end}) + "\n\n"
                     yield "data: [DONE]\n\n"

@@ -141,131 +141,179 @@ class TurboQuantCodec:
         return (enc["norms"].float()[:, None] * fast_wht(u)).to(self.dtype)
 
 
-# ------------------------------------------------------------------ HF cache wrapper
-def _cache_base():
+# ------------------------------------------------------------------ transformers cache
+PAGE = 16   # tokens coded together, the engine's KV page size
+
+
+def _cache_bases():
     try:
-        from transformers.cache_utils import Cache
-        return Cache
-    except Exception:  # transformers absent: a plain base keeps the module importable
-        return object
+        from transformers.cache_utils import Cache, CacheLayerMixin, DynamicLayer
+        return Cache, CacheLayerMixin, DynamicLayer
+    except Exception:  # transformers absent: plain bases keep the module importable
+        class _Plain:
+            def __init__(self, *a, **k):
+                self.is_initialized = False
+        return _Plain, _Plain, _Plain
 
 
-class TurboQuantCache(_cache_base()):
-    """Wraps a transformers cache and keeps every token older than
-    ``residual_length`` in TurboQuant form (keys with QJL, values without);
-    boundary layers (first/last ``boundary_layers``) stay full precision.
-    update() returns full K/V for attention, decoding the compressed part.
-    Other attributes proxy to the inner cache (hybrid SSM states keep working)."""
+_Cache, _LayerBase, _DynamicLayer = _cache_bases()
 
-    _OWN = frozenset({"key_bits", "value_bits", "residual_length", "boundary_layers", "num_layers", "layers",
-                      "layer_class_to_replicate", "offloading", "only_non_sliding", "prefetch_stream"})
 
-    def __init__(self, inner, key_bits=3, value_bits=2, residual_length=128, boundary_layers=2, num_layers=None):
-        object.__setattr__(self, "_inner", inner)
-        self.key_bits, self.value_bits = key_bits, value_bits
-        self.residual_length, self.boundary_layers, self.num_layers = residual_length, boundary_layers, num_layers
-        self._codecs = {}
-        self._store = {}
-        self._max_layer = 0
-        self.layers = getattr(inner, "layers", [])
-        self.layer_class_to_replicate = getattr(inner, "layer_class_to_replicate", None)
-        self.offloading = getattr(inner, "offloading", False)
+class TurboQuantLayer(_LayerBase):
+    """K/V of one full-attention layer for transformers models, stored as
+      * TurboQuant pages of ``PAGE`` tokens (keys with QJL signs, values without), for every
+        token older than the newest ``window`` tokens, and
+      * the newest ``window`` .. ``window + PAGE - 1`` tokens in full precision.
+    A page is coded once when it leaves the window and decoded once right then; the decoded
+    copy only grows by appending, so a decode step does O(new tokens) codec work.
+    update() returns the full key/value sequence (decoded pages, then the exact window)."""
 
-    def __getattr__(self, name):
-        return getattr(object.__getattribute__(self, "_inner"), name)
+    is_sliding = False
 
-    def __setattr__(self, name, value):
-        if name.startswith("_") or name in self._OWN:
-            object.__setattr__(self, name, value)
-        else:
-            setattr(self._inner, name, value)
+    def __init__(self, key_bits: int = 3, value_bits: int = 2, window: int = 128):
+        super().__init__()
+        self.key_bits, self.value_bits, self.window = key_bits, value_bits, window
+        self.pages = []            # [(enc_k, enc_v)] per coded page, each [B, H, PAGE, ...]
+        self.keys = self.values = None            # exact window [B, H, n, d]
+        self.dec_keys = self.dec_values = None    # decoded pages  [B, H, PAGE * len(pages), d]
+        self._kc = self._vc = None
+        self.is_initialized = False
 
-    def __len__(self):
-        return len(self._inner)
+    def lazy_initialization(self, key_states, value_states):
+        self.dtype, self.device = key_states.dtype, key_states.device
+        B, H, _, d = key_states.shape
+        self.keys = key_states.new_zeros(B, H, 0, d)
+        self.values = value_states.new_zeros(B, H, 0, value_states.shape[-1])
+        self.dec_keys, self.dec_values = self.keys.clone(), self.values.clone()
+        self._kc = TurboQuantCodec(d, self.key_bits, device=self.device)
+        self._vc = TurboQuantCodec(value_states.shape[-1], self.value_bits, device=self.device)
+        self.is_initialized = True
 
-    def __bool__(self):
-        return bool(self._inner)
+    def _code_oldest_page(self):
+        B, H, _, d = self.keys.shape
+        dv = self.values.shape[-1]
+        k, v = self.keys[:, :, :PAGE], self.values[:, :, :PAGE]
+        ek = self._kc.encode(k.reshape(-1, d), True)
+        ev = self._vc.encode(v.reshape(-1, dv), False)
+        self.pages.append(({n: t.reshape(B, H, PAGE, *t.shape[1:]) for n, t in ek.items()},
+                           {n: t.reshape(B, H, PAGE, *t.shape[1:]) for n, t in ev.items()}))
+        dk = self._kc.decode(ek).reshape(B, H, PAGE, d).to(self.dtype)
+        dvv = self._vc.decode(ev).reshape(B, H, PAGE, dv).to(self.dtype)
+        self.dec_keys = torch.cat([self.dec_keys, dk], 2)
+        self.dec_values = torch.cat([self.dec_values, dvv], 2)
+        self.keys, self.values = self.keys[:, :, PAGE:], self.values[:, :, PAGE:]
 
-    def _boundary(self, i):
-        if self.boundary_layers <= 0:
-            return False
-        self._max_layer = max(self._max_layer, i)
-        total = self.num_layers or (self._max_layer + 1)
-        return i < self.boundary_layers or i >= total - self.boundary_layers
+    def update(self, key_states, value_states, *args, **kwargs):
+        if not self.is_initialized:
+            self.lazy_initialization(key_states, value_states)
+        self.keys = torch.cat([self.keys, key_states], 2)
+        self.values = torch.cat([self.values, value_states], 2)
+        while self.keys.shape[2] >= self.window + PAGE:
+            self._code_oldest_page()
+        if not self.pages:
+            return self.keys, self.values
+        return torch.cat([self.dec_keys, self.keys], 2), torch.cat([self.dec_values, self.values], 2)
 
-    def _codec(self, kind, d, device):
-        key = (kind, d)
-        if key not in self._codecs:
-            self._codecs[key] = TurboQuantCodec(d, self.key_bits if kind == "k" else self.value_bits, device=device)
-        c = self._codecs[key]
-        if c.device != device:
-            c.to(device)
-        return c
+    @property
+    def coded_tokens(self) -> int:
+        return PAGE * len(self.pages)
 
-    def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
-        keys, values = self._inner.update(key_states, value_states, layer_idx, cache_kwargs)
-        if self._boundary(layer_idx) or keys.ndim != 4:
-            return keys, values
-        layers = getattr(self._inner, "layers", None)
-        if layers is not None and layer_idx < len(layers) and getattr(layers[layer_idx], "is_sliding", False):
-            return keys, values
-        B, H, T, d = keys.shape
-        if d < 8 or d & (d - 1):
-            return keys, values
-        if T > self.residual_length:
-            n = T - self.residual_length
-            kc, vc = self._codec("k", d, keys.device), self._codec("v", d, keys.device)
-            ek = kc.encode(keys[:, :, :n].reshape(-1, d), True)
-            ev = vc.encode(values[:, :, :n].reshape(-1, d), False)
-            ek = {k: v.reshape(B, H, n, *v.shape[1:]) for k, v in ek.items()}
-            ev = {k: v.reshape(B, H, n, *v.shape[1:]) for k, v in ev.items()}
-            prev = self._store.get(layer_idx)
-            if prev is not None:
-                ek = {k: torch.cat([prev["k"][k], ek[k]], 2) for k in ek}
-                ev = {k: torch.cat([prev["v"][k], ev[k]], 2) for k in ev}
-            self._store[layer_idx] = {"k": ek, "v": ev}
-            k_recent, v_recent = keys[:, :, n:], values[:, :, n:]
-            if not self._truncate(layer_idx, k_recent, v_recent):
-                raise RuntimeError("TurboQuantCache: cannot truncate the inner cache of "
-                                   f"{type(self._inner).__name__}; disable TurboQuant KV for this model")
-            keys, values = k_recent, v_recent
-        st = self._store.get(layer_idx)
-        if st is None:
-            return keys, values
-        kc, vc = self._codec("k", d, keys.device), self._codec("v", d, keys.device)
-        n_old = st["k"]["norms"].shape[2]
-        flat = lambda e: {k: v.reshape(-1, *v.shape[3:]) for k, v in e.items()}
-        k_old = kc.decode(flat(st["k"])).reshape(B, H, n_old, d).to(keys.dtype)
-        v_old = vc.decode(flat(st["v"])).reshape(B, H, n_old, d).to(values.dtype)
-        return torch.cat([k_old, keys], 2), torch.cat([v_old, values], 2)
+    def get_seq_length(self) -> int:
+        return 0 if not self.is_initialized else self.coded_tokens + self.keys.shape[2]
 
-    def _truncate(self, i, k, v) -> bool:
-        layers = getattr(self._inner, "layers", None)
-        if layers is not None and i < len(layers) and getattr(layers[i], "keys", None) is not None:
-            layers[i].keys, layers[i].values = k, v
-            return True
-        kcache = getattr(self._inner, "key_cache", None)
-        if isinstance(kcache, list) and i < len(kcache):
-            kcache[i] = k
-            self._inner.value_cache[i] = v
-            return self._inner.key_cache[i].shape[2] == k.shape[2]
-        return False
+    def get_mask_sizes(self, query_length: int):
+        return self.get_seq_length() + query_length, 0
 
-    def get_seq_length(self, layer_idx=0):
-        st = self._store.get(layer_idx)
-        return self._inner.get_seq_length(layer_idx) + (st["k"]["norms"].shape[2] if st else 0)
+    def get_max_cache_shape(self) -> int:
+        return -1
 
     def reset(self):
-        self._inner.reset()
-        self._store.clear()
+        self.pages = []
+        if self.is_initialized:
+            self.keys, self.values = self.keys[:, :, :0], self.values[:, :, :0]
+            self.dec_keys, self.dec_values = self.dec_keys[:, :, :0], self.dec_values[:, :, :0]
+
+    def crop(self, max_length: int):
+        n = self.get_seq_length()
+        if max_length < 0:
+            max_length = n - abs(max_length)
+        if n <= max_length:
+            return
+        keep_pages = min(len(self.pages), max_length // PAGE)
+        if keep_pages < len(self.pages):
+            # decoded pages past the cut become exact-window tokens again (at decoded precision)
+            start = keep_pages * PAGE
+            self.keys = torch.cat([self.dec_keys[:, :, start:], self.keys], 2)
+            self.values = torch.cat([self.dec_values[:, :, start:], self.values], 2)
+            self.pages = self.pages[:keep_pages]
+            self.dec_keys, self.dec_values = self.dec_keys[:, :, :start], self.dec_values[:, :, :start]
+        w = max_length - self.coded_tokens
+        self.keys, self.values = self.keys[:, :, :w], self.values[:, :, :w]
+
+    def _select(self, fn):
+        self.keys, self.values = fn(self.keys), fn(self.values)
+        self.dec_keys, self.dec_values = fn(self.dec_keys), fn(self.dec_values)
+        self.pages = [({n: fn(t) for n, t in ek.items()}, {n: fn(t) for n, t in ev.items()})
+                      for ek, ev in self.pages]
+
+    def batch_repeat_interleave(self, repeats: int):
+        if self.is_initialized:
+            self._select(lambda t: t.repeat_interleave(repeats, dim=0))
+
+    def batch_select_indices(self, indices):
+        if self.is_initialized:
+            self._select(lambda t: t[indices, ...])
 
     def reorder_cache(self, beam_idx):
-        return self._inner.reorder_cache(beam_idx)
-
-    def get_max_cache_shape(self, layer_idx=0):
-        return self._inner.get_max_cache_shape(layer_idx)
+        self.batch_select_indices(beam_idx)
 
 
-def wrap_cache_with_turboquant(cache, num_layers=None, key_bits=3, value_bits=2, residual_length=128,
+class TurboQuantCache(_Cache):
+    """A transformers cache whose full-attention layers keep old tokens in TurboQuant form.
+
+    Layer ``i`` is a ``TurboQuantLayer`` unless it is one of the first or last
+    ``boundary_layers`` of ``num_layers`` (those stay exact) or ``base`` supplies a layer of
+    another kind for it (sliding-window or linear-attention state), which is kept as is.
+    Layers are created on first use. The options match the reference's (key/value bits,
+    full-precision window ``residual_length``, boundary layers; core/turboquant_cache.py)."""
+
+    def __init__(self, key_bits=3, value_bits=2, residual_length=128, boundary_layers=2, num_layers=None,
+                 base=None):
+        super().__init__(layers=[])
+        self.key_bits, self.value_bits = key_bits, value_bits
+        self.residual_length, self.boundary_layers, self.num_layers = residual_length, boundary_layers, num_layers
+        self._base_layers = list(getattr(base, "layers", None) or [])
+
+    def _exact(self, i: int) -> bool:
+        b = self.boundary_layers
+        if b <= 0:
+            return False
+        return i < b or (self.num_layers is not None and i >= self.num_layers - b)
+
+    def _make_layer(self, i: int):
+        if i < len(self._base_layers):
+            given = self._base_layers[i]
+            if type(given) is not _DynamicLayer or getattr(given, "is_sliding", False):
+                return given                     # sliding / recurrent state: not ours to code
+        if self._exact(i):
+            return _DynamicLayer()
+        return TurboQuantLayer(self.key_bits, self.value_bits, self.residual_length)
+
+    def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
+        while len(self.layers) <= layer_idx:
+            self.layers.append(self._make_layer(len(self.layers)))
+        layer = self.layers[layer_idx]
+        d = key_states.shape[-1]
+        if isinstance(layer, TurboQuantLayer) and (key_states.ndim != 4 or d < 8 or d & (d - 1)):
+            # the codec's Walsh-Hadamard transform needs a power-of-two head size
+            layer = self.layers[layer_idx] = _DynamicLayer()
+        return layer.update(key_states, value_states, cache_kwargs)
+
+    def get_seq_length(self, layer_idx=0):
+        return self.layers[layer_idx].get_seq_length() if layer_idx < len(self.layers) else 0
+
+
+def wrap_cache_with_turboquant(cache=None, num_layers=None, key_bits=3, value_bits=2, residual_length=128,
                                boundary_layers=2):
-    return TurboQuantCache(cache, key_bits, value_bits, residual_length, boundary_layers, num_layers)
+    """A TurboQuantCache that keeps the non-attention layers of ``cache`` (if any)."""
+    return TurboQuantCache(key_bits, value_bits, residual_length, boundary_layers, num_layers, base=cache)

@@ -95,7 +95,13 @@ def rmsnorm(parts, weight, eps, residual=None, residual_out=None, out=None):
     if _cuda(x0):
         out = out if out is not None else torch.empty_like(x0)
         flags = getattr(parts, "flags_ptr", None)
-        if flags is not None:   # parts pushed by peers: wait for their flags first
+        if getattr(parts, "lamport", False):
+            # flag-free receive slots: poll the data; skip the wait for the push GEMM's grid only
+            # when that GEMM was the launch right before this one
+            direct = launch_count() == parts.launch_mark + 1     # +1: this norm, counted above
+            ext().rmsnorm_lamport(list(parts), residual, residual_out, weight, out, float(eps), parts.err_ptr,
+                                  direct)
+        elif flags is not None:   # parts pushed by peers: wait for their flags first
             ext().rmsnorm_fused_wait(list(parts), residual, residual_out, weight, out, float(eps), flags,
                                      parts.epoch_ptr, parts.err_ptr)
         else:

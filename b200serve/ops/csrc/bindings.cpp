@@ -6,9 +6,12 @@ void rmsnorm_fused(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor
 void rmsnorm_fused_wait(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
                         c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps,
                         int64_t flags_ptr, int64_t epoch_ptr, int64_t err_ptr);
+void rmsnorm_lamport(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
+                     c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps,
+                     int64_t err_ptr, bool skip_prior_wait);
 void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, int64_t ldo, torch::Tensor flag_ptrs,
                   int64_t epoch_ptr, torch::Tensor tile_done, c10::optional<torch::Tensor> bias, torch::Tensor ws,
-                  torch::Tensor counters, int64_t err_ptr, int64_t packed_n, int64_t rs_rows);
+                  torch::Tensor counters, int64_t err_ptr, int64_t packed_n, int64_t rs_rows, int64_t lamport);
 int64_t ipc_malloc(int64_t bytes);
 void ipc_free(int64_t ptr);
 torch::Tensor ipc_handle(int64_t ptr);
@@ -130,6 +133,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_fused_wait", &rmsnorm_fused_wait);
   m.def("rmsnorm_rs_ag", &rmsnorm_rs_ag);
   m.def("gemm_tc_push", &gemm_tc_push);
+  m.def("rmsnorm_lamport", &rmsnorm_lamport);
   m.def("ipc_malloc", &ipc_malloc);
   m.def("ipc_free", &ipc_free);
   m.def("ipc_handle", &ipc_handle);

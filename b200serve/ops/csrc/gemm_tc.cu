@@ -305,7 +305,7 @@ void gemm_tc_qkv(torch::Tensor act, torch::Tensor w, int64_t packed_n, c10::opti
 // whole output is pushed. dst_ptrs/flag_ptrs: int64 [world] device addresses.
 void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, int64_t ldo, torch::Tensor flag_ptrs,
                   int64_t epoch_ptr, torch::Tensor tile_done, c10::optional<torch::Tensor> bias, torch::Tensor ws,
-                  torch::Tensor counters, int64_t err_ptr, int64_t packed_n, int64_t rs_rows) {
+                  torch::Tensor counters, int64_t err_ptr, int64_t packed_n, int64_t rs_rows, int64_t lamport) {
   TORCH_CHECK(act.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16);
   const bool packed = packed_n > 0;
   const int M = act.size(0), K = act.size(1), N = packed ? (int)packed_n : w.size(0);
@@ -343,6 +343,8 @@ void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, in
   p.epoch = reinterpret_cast<const int*>(epoch_ptr);
   p.tile_done = tile_done.data_ptr<int>();
   p.rs_rows = (int)rs_rows;
+  p.lamport = lamport ? 1 : 0;
+  TORCH_CHECK(!(lamport && rs_rows), "the flag-free push is an all-reduce (rs_rows must be 0)");
   TORCH_CHECK(rs_rows == 0 || (int64_t)rs_rows * world >= M, "reduce-scatter rows do not cover the tokens");
   p.err = err_ptr ? reinterpret_cast<int*>(err_ptr) : gemm_err_word();
   p.w_packed = packed ? 1 : 0;

@@ -80,6 +80,11 @@ struct GemmParams {
   int* push_flag[kMaxPeers];            // flag word on rank r for (site, this rank)
   const int* epoch;                     // this step's epoch (device)
   int* tile_done;                       // local counter of pushed tiles, zero on entry and exit
+  // EPI_PUSH without flags: the receive slots hold the sentinel bf16 pattern 0xFFFF until data
+  // lands, and the consumer polls the data itself (no system fence, no tile counter, no flag
+  // stores). The kernel lets its dependent launch only after its own prerequisites completed,
+  // so a consumer that skips griddepcontrol.wait still runs after everything before this GEMM.
+  int lamport;
   // optional per-CTA timeline (globaltimer ns): [cta][8] = entry, setup done, first TMA issued,
   // first stage landed, last MMA committed, epilogue done, exit (thread 0), exit (thread 32)
   unsigned long long* trace;
@@ -146,7 +151,12 @@ __device__ __forceinline__ void epilogue_store(const GemmParams& p, float* v, in
       const int col = n_tile * 128 + row;
       const float b = (p.bias && col < p.N) ? __bfloat162float(p.bias[col]) : 0.f;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) xs[j * 136 + row] = __float2bfloat16_rn(v[j] + b);
+      for (int j = 0; j < 16; ++j) {
+        __nv_bfloat16 h = __float2bfloat16_rn(v[j] + b);
+        // 0xFFFF marks an empty receive slot; a NaN with that payload is stored as 0x7FFF
+        if (__bfloat16_as_ushort(h) == 0xFFFFu) h = __ushort_as_bfloat16((unsigned short)0x7FFFu);
+        xs[j * 136 + row] = h;
+      }
     }
     epi_bar();
     const int tid = threadIdx.x - 64;                                    // 0..127 over the epilogue warps
@@ -414,8 +424,11 @@ __global__ void __launch_bounds__(192, 2)
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   if (threadIdx.x == 0) trace_mark(p, 1);
-  pdl_trigger();
-  if (warp != 0) pdl_wait();
+  if (!p.lamport) pdl_trigger();
+  if (warp != 0) {
+    pdl_wait();
+    if (p.lamport) pdl_trigger();   // the dependent may start only after our prerequisites completed
+  }
 
   if (warp == 0) {
     if (lane == 0) {
@@ -539,7 +552,9 @@ __global__ void __launch_bounds__(192, 2)
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&tempty[acc]);
-        if constexpr (EPI == EPI_PUSH) publish_tile(p, last_flag);
+        if constexpr (EPI == EPI_PUSH) {
+          if (!p.lamport) publish_tile(p, last_flag);
+        }
       } else if (p.cluster_red) {
         // partial tile -> this CTA's shared memory (the drained stage ring), reduced after the
         // cluster barrier below
@@ -575,6 +590,9 @@ __global__ void __launch_bounds__(192, 2)
         const bool last = *last_flag != 0;
         epi_bar();  // everyone has read last_flag before it is rewritten
         if (last) {
+          // every split of this tile has arrived: reset its counter before the epilogue's stores
+          // (a flag-free consumer may let the next GEMM start as soon as those stores land)
+          if (threadIdx.x == 64) p.counters[x.tile] = 0;
           __threadfence();
           for (int c0 = 0; c0 < BN; c0 += 16) {
             float v[16];
@@ -598,8 +616,9 @@ __global__ void __launch_bounds__(192, 2)
             }
             epilogue_store<EPI>(p, v, row, x.n_tile, x.a_row0 + c0, t_end, xchg, quad, lane);
           }
-          if (threadIdx.x == 64) p.counters[x.tile] = 0;
-          if constexpr (EPI == EPI_PUSH) publish_tile(p, last_flag);
+          if constexpr (EPI == EPI_PUSH) {
+            if (!p.lamport) publish_tile(p, last_flag);
+          }
         }
       }
       acc_phase[acc] ^= 1;

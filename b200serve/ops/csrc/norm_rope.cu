@@ -53,15 +53,56 @@ __device__ __forceinline__ void wait_peer_flags(const int* flags, const int* epo
   __syncthreads();
 }
 
+// Flag-free receive slots: a 16-byte vector of 8 bf16 is complete once none of its elements
+// holds the empty-slot pattern 0xFFFF (producers never store that pattern).
+__device__ __forceinline__ bool lamport_empty(const uint4& v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  bool e = false;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) e |= (w[i] & 0xFFFFu) == 0xFFFFu || (w[i] >> 16) == 0xFFFFu;
+  return e;
+}
+
+// Poll one vector of a flag-free slot until a peer's store has landed (bounded: after
+// `wait_ns` an error code is recorded, `gave_up` is set and zeros are returned without further
+// spinning), then put the empty pattern back for the slot's next use.
+__device__ __forceinline__ uint4 lamport_take(const __nv_bfloat16* ptr, uint64_t wait_ns, int* err, bool& gave_up) {
+  uint4 v;
+  uint64_t deadline = 0;
+  for (uint32_t it = 1;; ++it) {
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(ptr) : "memory");
+    if (!lamport_empty(v)) break;
+    if (gave_up) { v = make_uint4(0, 0, 0, 0); break; }
+    if ((it & 255u) == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (deadline == 0) {
+        deadline = now + wait_ns;
+      } else if (now > deadline) {
+        if (err) atomicExch(err, 160);
+        gave_up = true;
+        v = make_uint4(0, 0, 0, 0);
+        break;
+      }
+    }
+  }
+  asm volatile("st.global.v4.u32 [%0], {%1, %1, %1, %1};" ::"l"(ptr), "r"(0xFFFFFFFFu) : "memory");
+  return v;
+}
+
 template <int VPT>
 __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
     PartPtrs parts, int nparts, const __nv_bfloat16* residual_in, __nv_bfloat16* residual_out,
     const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H, float eps,
-    const int* wait_flags, const int* epoch, int* err, const AgArgs ag, uint64_t wait_ns) {
+    const int* wait_flags, const int* epoch, int* err, const AgArgs ag, uint64_t wait_ns, int lamport) {
   __shared__ float red[32];
-  pdl_wait();
+  // lamport == 2: the partials come from a flag-free push GEMM launched right before this kernel,
+  // which let it start only after that GEMM's own prerequisites completed; the partials are
+  // polled, so the wait for the GEMM's grid to drain is skipped
+  if (lamport != 2) pdl_wait();
   pdl_trigger();
   if (wait_flags) wait_peer_flags(wait_flags, epoch, nparts, err, wait_ns);
+  bool gave_up = false;
   const int row = blockIdx.x;
   const size_t base = (size_t)row * H;
   float v[VPT][8];
@@ -72,11 +113,13 @@ __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
     if (col < H) {
       float acc[8];
       // partials may have been written by other GPUs: read through L2, not L1
-      uint4 a4 = __ldcg(reinterpret_cast<const uint4*>(parts.p[0] + base + col));
+      uint4 a4 = lamport ? lamport_take(parts.p[0] + base + col, wait_ns, err, gave_up)
+                         : __ldcg(reinterpret_cast<const uint4*>(parts.p[0] + base + col));
       unpack8(*reinterpret_cast<bf16x8*>(&a4), acc);
       for (int k = 1; k < nparts; ++k) {
         float t[8];
-        uint4 t4 = __ldcg(reinterpret_cast<const uint4*>(parts.p[k] + base + col));
+        uint4 t4 = lamport ? lamport_take(parts.p[k] + base + col, wait_ns, err, gave_up)
+                           : __ldcg(reinterpret_cast<const uint4*>(parts.p[k] + base + col));
         unpack8(*reinterpret_cast<bf16x8*>(&t4), t);
 #pragma unroll
         for (int i = 0; i < 8; ++i) acc[i] += t[i];
@@ -283,7 +326,7 @@ using namespace b200;
 
 void rmsnorm_fused_impl(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
                         c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps,
-                        const int* wait_flags, const int* epoch, int* err, const AgArgs& ag) {
+                        const int* wait_flags, const int* epoch, int* err, const AgArgs& ag, int lamport = 0) {
   TORCH_CHECK(!parts.empty() && parts.size() <= 8, "1..8 partial inputs");
   const int H = parts[0].size(-1);
   const int T = parts[0].numel() / H;
@@ -302,10 +345,10 @@ void rmsnorm_fused_impl(std::vector<torch::Tensor> parts, c10::optional<torch::T
   auto wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   switch (vpt) {
-    case 1: launch_pdl(rmsnorm_fused_kernel<1>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns()); break;
-    case 2: launch_pdl(rmsnorm_fused_kernel<2>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns()); break;
+    case 1: launch_pdl(rmsnorm_fused_kernel<1>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport); break;
+    case 2: launch_pdl(rmsnorm_fused_kernel<2>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport); break;
     case 3:
-    case 4: launch_pdl(rmsnorm_fused_kernel<4>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns()); break;
+    case 4: launch_pdl(rmsnorm_fused_kernel<4>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport); break;
     default: TORCH_CHECK(false, "hidden size too large");
   }
   B200_CHECK_CUDA(cudaGetLastError());
@@ -323,6 +366,16 @@ void rmsnorm_fused_wait(std::vector<torch::Tensor> parts, c10::optional<torch::T
                         int64_t flags_ptr, int64_t epoch_ptr, int64_t err_ptr) {
   rmsnorm_fused_impl(parts, residual_in, residual_out, w, out, eps, reinterpret_cast<const int*>(flags_ptr),
                      reinterpret_cast<const int*>(epoch_ptr), reinterpret_cast<int*>(err_ptr), AgArgs{});
+}
+
+// Consumer of a flag-free all-reduce site: parts are this rank's receive slots (one per source
+// rank, filled with 0xFFFF while empty); every vector is polled until it has landed, summed in
+// rank order and reset to empty. skip_prior_wait: the push GEMM was the launch right before.
+void rmsnorm_lamport(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
+                     c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps,
+                     int64_t err_ptr, bool skip_prior_wait) {
+  rmsnorm_fused_impl(parts, residual_in, residual_out, w, out, eps, nullptr, nullptr,
+                     reinterpret_cast<int*>(err_ptr), AgArgs{}, skip_prior_wait ? 2 : 1);
 }
 
 // Reduce-scatter consumer + all-gather producer: waits for the partial rows of this rank's

@@ -54,6 +54,23 @@ class FusedParts(list):
         self.flags_ptr, self.epoch_ptr, self.err_ptr = flags_ptr, epoch_ptr, err_ptr
 
 
+class LamportParts(list):
+    """The local receive slots of one flag-free site (one view per source rank). The consumer
+    polls the data itself; ``launch_mark`` is the launch count right after the push GEMM, so the
+    norm can tell whether it directly follows that GEMM."""
+
+    lamport = True
+
+    def __init__(self, views, err_ptr, launch_mark):
+        super().__init__(views)
+        self.err_ptr, self.launch_mark = err_ptr, launch_mark
+
+
+def _lamport_default() -> bool:
+    import os
+    return os.environ.get("B200_TP_LAMPORT", "1") != "0"
+
+
 class FusedComm:
     kind = "fused-p2p"
 
@@ -76,7 +93,12 @@ class FusedComm:
         self.ag_off = (data_bytes + 4095) // 4096 * 4096
         ag_bytes = 2 * self.max_step * H * 2                  # gathered rows, [2 parities][max_step][H]
         self.flag_off = (self.ag_off + ag_bytes + 4095) // 4096 * 4096
-        total = self.flag_off + self.n_sites * self.world * 4
+        # flag-free all-reduce slots: [3 rotations][world][max_tokens][H] bf16, 0xFFFF while empty
+        self.lam_elems = self.max_tokens * H
+        self.lam_off = (self.flag_off + self.n_sites * self.world * 4 + 4095) // 4096 * 4096
+        self.lam_bytes = 3 * self.world * self.lam_elems * 2
+        total = self.lam_off + self.lam_bytes
+        self.lamport = _lamport_default()
         e = ops.ext()
         self.base = e.ipc_malloc(total)
         handle = e.ipc_handle(self.base)
@@ -92,6 +114,7 @@ class FusedComm:
         self.tile_done = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.ag_done = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._ag_ptrs = {}
+        self.reset_lamport()
         self.err = e.host_error_word()       # [host ptr, device ptr]
         self.err_host, self.err_dev = int(self.err[0]), int(self.err[1])
         self.ws = ops.GemmWorkspace(self.device, max_elems=8 << 20, max_tiles=1 << 14)
@@ -106,6 +129,23 @@ class FusedComm:
 
     def _flag_ptr(self, rank_base: int, site: int, src_rank: int) -> int:
         return rank_base + self.flag_off + (site * self.world + src_rank) * 4
+
+    def reset_lamport(self):
+        """Mark every flag-free slot of this rank empty (at start-up and after a failed step, whose
+        consumers may not have emptied the slots they were reading)."""
+        region = _tensor_from_ptr(self.base + self.lam_off, self.lam_bytes // 2, self.device)
+        region.view(torch.int16).fill_(-1)
+        torch.cuda.synchronize(self.device)
+
+    def _lam_ptr(self, rank_base: int, rot: int, src_rank: int) -> int:
+        return rank_base + self.lam_off + (rot * self.world + src_rank) * self.lam_elems * 2
+
+    def _lam_views(self, rot: int, T: int):
+        key = ("lam", rot, T)
+        if key not in self._views:
+            self._views[key] = [_tensor_from_ptr(self._lam_ptr(self.base, rot, r), T * self.H, self.device)
+                                .view(T, self.H) for r in range(self.world)]
+        return self._views[key]
 
     def _local_views(self, slot: int, T: int):
         key = (slot, T)
@@ -146,8 +186,18 @@ class FusedComm:
         dst, flg = self._push_ptrs(site)
         ops._cuda(x)
         packed_n = w.N if isinstance(w, ops.PackedWeight) else 0
+        if self.lamport:
+            rot = site % 3
+            key = ("lamdst", rot)
+            if key not in self._ptrs:
+                self._ptrs[key] = torch.tensor([self._lam_ptr(self.peer[r], rot, self.rank)
+                                                for r in range(self.world)], dtype=torch.int64)
+            ops.ext().gemm_tc_push(x, w.data if packed_n else w, self._ptrs[key], self.H, flg,
+                                   self.epoch.data_ptr(), self.tile_done, None, self.ws.ws, self.ws.counters,
+                                   self.err_dev, packed_n, 0, 1)
+            return LamportParts(self._lam_views(rot, T), self.err_dev, ops.launch_count())
         ops.ext().gemm_tc_push(x, w.data if packed_n else w, dst, self.H, flg, self.epoch.data_ptr(), self.tile_done,
-                               None, self.ws.ws, self.ws.counters, self.err_dev, packed_n, 0)
+                               None, self.ws.ws, self.ws.counters, self.err_dev, packed_n, 0, 0)
         return FusedParts(self._local_views(site % 2, T), self._flag_ptr(self.base, site, 0),
                           self.epoch.data_ptr(), self.err_dev)
 
@@ -181,7 +231,7 @@ class FusedComm:
         ops._cuda(x)
         packed_n = w.N if isinstance(w, ops.PackedWeight) else 0
         ops.ext().gemm_tc_push(x, w.data if packed_n else w, dst, self.H, flg, self.epoch.data_ptr(),
-                               self.tile_done, None, self.ws.ws, self.ws.counters, self.err_dev, packed_n, Tw)
+                               self.tile_done, None, self.ws.ws, self.ws.counters, self.err_dev, packed_n, Tw, 0)
         return RSParts(self._local_views(site % 2, Tw), T, self._flag_ptr(self.base, site, 0),
                        self.epoch.data_ptr(), self.err_dev)
 
@@ -238,7 +288,11 @@ class FusedComm:
         self.nccl.barrier()
 
     def check(self):
-        check_error_word(self.err_host, self.rank)
+        try:
+            check_error_word(self.err_host, self.rank)
+        except CollectiveTimeout:
+            self.reset_lamport()
+            raise
 
     def close(self):
         e = ops.ext()

@@ -2,6 +2,8 @@
 
 One site of the decode step: row-parallel GEMM [T, K/world] x [K/world, H] whose
 outputs are summed over ranks, then add+RMSNorm. Compares
+  lamport: push-GEMM storing tiles into every rank's flag-free slot (empty = 0xFFFF) +
+         a RMSNorm that polls the data itself,
   fused: push-GEMM (epilogue stores tiles into every rank's slot over NVLink) +
          flag-waiting RMSNorm,
   nccl:  GEMM + NCCL all-reduce + RMSNorm,
@@ -87,7 +89,15 @@ def main():
             res = torch.randn(T, H, device="cuda").bfloat16()
             out = torch.empty(T, H, device="cuda").bfloat16()
 
+            def lamport():
+                comm.lamport = True
+                comm.begin_step()
+                for _ in range(8):
+                    parts = comm.linear_reduce(x, w, "o")
+                    ops.rmsnorm(parts, nw, 1e-6, residual=res, out=out)
+
             def fused():
+                comm.lamport = False
                 comm.begin_step()
                 for _ in range(8):   # 8 sites per replay, as in 4 layers of a decode step
                     parts = comm.linear_reduce(x, w, "o")
@@ -115,7 +125,8 @@ def main():
                     ops.rmsnorm([y], nw, 1e-6, residual=res, out=out)
 
             row = {"site": name, "T": T, "world": world, "K_shard": K}
-            for label, fn in (("fused", fused), ("rsag", rsag), ("nccl", nccl), ("local", local)):
+            for label, fn in (("lamport", lamport), ("fused", fused), ("rsag", rsag), ("nccl", nccl),
+                              ("local", local)):
                 for _ in range(3):
                     fn()
                 torch.cuda.synchronize()
@@ -143,6 +154,7 @@ def main():
             rs_bytes = 2 * (world - 1) * (-(-T // world)) * H * 2
             row["rsag_roofline_us"] = round(max(wbytes / (hbm * 1e3), rs_bytes / (NVLINK_GBPS * 1e3)), 2)
             row["fused_frac_of_roofline"] = round(roof_us / row["fused_us"], 3)
+            row["lamport_frac_of_roofline"] = round(roof_us / row["lamport_us"], 3)
             row["speedup_vs_nccl"] = round(row["nccl_us"] / row["fused_us"], 3)
             row["peaks"] = src
             results.append(row)

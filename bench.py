@@ -93,6 +93,7 @@ def run_ours(a):
     if world > 1:
         init_distributed("nccl", timeout_s=600)
     torch.cuda.set_device(lrank)
+    match = _tp_path_check(a.model, world, rank) if (world > 1 and a.comm == "fused") else None
     B, P, K, W = a.batch, a.prompt, a.steps, a.warmup
     max_seq = ((P + K + W + 64) + 15) // 16 * 16
     moe = a.model == "qwen3-30b-a3b"
@@ -141,7 +142,7 @@ def run_ours(a):
     tps = B * K / (ms / 1e3)
     from b200serve.engine.runner import PACK
     pack_bytes = inner.bucket(B) * (PACK + inner.max_blocks) * 4
-    emit({
+    line = {
         "metric": METRIC, "value": round(tps, 1), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16",
@@ -159,7 +160,53 @@ def run_ours(a):
                 "ttft_p50_ms": round(statistics.median(ttfts) * 1e3, 2), "wall_s": round(t1 - t0, 3)},
         "gpu_launches": res["launches_per_step"] * K,
         "impl": "ours",
-    })
+    }
+    if match is not None:
+        line["tokens_match"] = match["match"]
+        line["tokens_match_check"] = match["what"]
+    emit(line)
+
+
+def _tp_path_check(model, world, rank):
+    """Multi-GPU correctness next to the timing: a 2-layer model of the same shape (same seed,
+    same random-init weights per rank) decodes greedily through the NCCL path and through the
+    fused in-kernel collectives; the first 4 tokens of every sequence must agree. (The paths
+    round the cross-rank sum differently, so later near-ties may legitimately part.)"""
+    import torch
+    import torch.distributed as dist
+    from b200serve.core.config import EngineConfig
+    from b200serve.engine.b200_engine import B200Engine
+    from b200serve.engine.sampler import SamplingParams
+    from b200serve.parallel.worker import worker_loop
+    moe = model == "qwen3-30b-a3b"
+    outs = {}
+    for kind in ("nccl", "fused"):
+        cfg = EngineConfig(model=model, num_layers_override=2, tp_size=world, ep_size=world if moe else 1,
+                           comm=kind, max_batch=8, max_seq=512, kv_blocks=256, cuda_graphs=True)
+        eng = B200Engine(cfg)
+        eng.load()
+        if rank == 0:
+            g = torch.Generator().manual_seed(5)
+            prompts = [torch.randint(0, 150000, (n,), generator=g).tolist() for n in (64, 200, 17, 5)]
+            reqs = eng.generate(prompts, SamplingParams(temperature=0.0, max_tokens=6, ignore_eos=True),
+                                timeout=600)
+            outs[kind] = [r.output[:4] for r in reqs]
+            eng.stop_loop()
+        else:
+            worker_loop(eng.runner.inner, eng.comm)
+        eng.runner.inner.release_graphs()
+        dist.barrier()
+        if hasattr(eng.comm, "close"):
+            eng.comm.close()
+        eng.runner = eng.scheduler = eng.kv = eng.weights = eng.comm = None
+        del eng
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        dist.barrier()
+    if rank != 0:
+        return None
+    return {"match": outs["nccl"] == outs["fused"],
+            "what": f"first 4 greedy tokens of 4 sequences, 2-layer {model} shape, fused vs NCCL collectives"}
 
 
 def _device_loop(runner, inner, eng, B, P, K, W, vocab):

@@ -39,7 +39,8 @@ def _fused_worker(rank, world, port, q):
     torch.cuda.set_device(rank)
     cfg = BUILTIN["qwen3-8b"]
     comm = FusedComm(dist.group.WORLD, torch.device("cuda", rank), cfg, EngineConfig(max_batch=32))
-    g = torch.Generator(device="cuda").manual_seed(100 + rank)
+    g = torch.Generator(device="cuda").manual_seed(100 + rank)     # this rank's shard
+    gs = torch.Generator(device="cuda").manual_seed(7)              # replicated tensors
     errs = []
     for step in range(6):
         comm.begin_step()
@@ -47,14 +48,24 @@ def _fused_worker(rank, world, port, q):
             T = [32, 7, 1][site]
             x = torch.randn(T, 1536, device="cuda", generator=g).bfloat16()
             w = ops.pack_weight((torch.randn(4096, 1536, device="cuda", generator=g) * 0.03).bfloat16())
-            res = torch.randn(T, 4096, device="cuda", generator=g).bfloat16()
-            nw = torch.randn(4096, device="cuda", generator=g).bfloat16()
+            res = torch.randn(T, 4096, device="cuda", generator=gs).bfloat16()
+            nw = torch.randn(4096, device="cuda", generator=gs).bfloat16()
+            comm.lamport = step % 3 != 2          # flag-free slots on most steps, flags on the rest
             parts = comm.linear_reduce(x, w, "o")
-            out = ops.rmsnorm(parts, nw, 1e-6, residual=res)
-            y = ops.linear(x, w)
+            if site == 1:                          # another launch between the GEMM and its norm
+                y = ops.linear(x, w)
+                out = ops.rmsnorm(parts, nw, 1e-6, residual=res)
+            else:                                  # the norm directly follows the push GEMM
+                out = ops.rmsnorm(parts, nw, 1e-6, residual=res)
+                y = ops.linear(x, w)
             dist.all_reduce(y)
             ref = ops.rmsnorm([y], nw, 1e-6, residual=res)
             errs.append(((out.float() - ref.float()).norm() / ref.float().norm()).item())
+            # every rank sums the partials in rank order: the outputs agree bit for bit
+            outs = [torch.empty_like(out) for _ in range(world)]
+            dist.all_gather(outs, out)
+            if not all(torch.equal(outs[0], o) for o in outs):
+                errs.append(1.0)
     torch.cuda.synchronize()
     comm.check()
     comm.close()
