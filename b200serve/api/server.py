@@ -1,8 +1,9 @@
 """OpenAI-compatible HTTP API (reference: api/server.py).
 
-Routes: /health, /metrics, /v1/queue, /v1/models, /v1/tokenize, /v1/engine
-(GET, POST switch, POST /reload), /v1/chat/completions (streaming SSE and
-plain JSON). SSE chunks carry the reference's extensions: ``x_thinking``
+Routes: /health, /metrics (Prometheus text: counters, TTFT / decode-rate / latency
+histograms, scheduler and queue gauges, per-GPU memory), /v1/queue, /v1/models,
+/v1/tokenize, /v1/embeddings, /v1/engine (GET, POST switch, POST /reload),
+/v1/chat/completions (streaming SSE and plain JSON), /v1/chat/jobs*, /v1/sessions*. SSE chunks carry the reference's extensions: ``x_thinking``
 deltas for reasoning text, ``x_context_fit`` when the pre-flight fit compacted
 or trimmed the conversation, and ``x_usage`` / ``x_backend`` on the final chunk.
 
@@ -56,21 +57,36 @@ def _get_engine():
         return _engine
 
 
-def _check_auth(request) -> bool:
+def _auth_status(request) -> str:
+    """"ok", "denied" (no or wrong key) or "limited" (too many failures from this address in
+    the last minute). A correct key is always accepted, even from a limited address: the
+    limit only stops further guesses (reference behaviour, api/server.py:104-139)."""
     if _keystore is None or not _keystore.configured():
-        return True
+        return "ok"
     ip = request.client.host if request.client else "unknown"
     now = time.time()
     fails = [t for t in _auth_failures.get(ip, []) if now - t < _AUTH_FAIL_WINDOW]
     auth = request.headers.get("Authorization", "")
     token = auth[7:] if auth.startswith("Bearer ") else request.headers.get("X-API-Key", "")
-    if token and _keystore.match(token) is not None:
+    hit = _keystore.match(token) if token else None
+    if hit is not None:
         _auth_failures[ip] = fails
-        return True
-    if len(fails) < _AUTH_FAIL_MAX:
-        fails.append(now)
+        try:
+            request.state.api_key_id = hit.get("id", "")
+        except AttributeError:
+            pass
+        return "ok"
+    if len(fails) >= _AUTH_FAIL_MAX:
+        _auth_failures[ip] = fails
+        _log.warning("rate-limited auth from %s (%d failures)", ip, len(fails))
+        return "limited"
+    fails.append(now)
     _auth_failures[ip] = fails
-    return False
+    return "denied"
+
+
+def _check_auth(request) -> bool:
+    return _auth_status(request) == "ok"
 
 
 class ChatMessage(BaseModel):
@@ -101,6 +117,12 @@ class ChatCompletionRequest(BaseModel):
     grammar: Optional[str] = None
     response_format: Optional[dict] = None
     backend: Optional[Literal["b200", "ollama", "transformers", "llama_cpp", "claude_cli"]] = None
+
+
+class EmbeddingRequest(BaseModel):
+    input: Union[str, List[str]]
+    model: Optional[str] = None
+    encoding_format: Optional[str] = None
 
 
 class TokenizeRequest(BaseModel):
@@ -228,8 +250,17 @@ def create_app(engine=None, keystore: KeyStore = None):
     mq = get_model_queue()
     mq.register_engine_unload(lambda: _engine.unload() if _engine is not None else None)
 
+    from b200serve.core.metrics import get_metrics
+    metrics_reg = get_metrics()
+
     def auth(request):
-        if not _check_auth(request):
+        st = _auth_status(request)
+        if st == "limited":
+            metrics_reg.count("auth_rate_limited_total")
+            raise HTTPException(status_code=429, detail="Too many failed authentication attempts; retry later",
+                                headers={"Retry-After": str(int(_AUTH_FAIL_WINDOW))})
+        if st != "ok":
+            metrics_reg.count("auth_rejected_total")
             raise HTTPException(status_code=401, detail="Invalid API key")
 
     @app.get("/health")
@@ -244,9 +275,28 @@ def create_app(engine=None, keystore: KeyStore = None):
     async def metrics(request: Request):
         auth(request)
         m = _engine.metrics() if _engine is not None and _engine.is_loaded() else {}
-        lines = [f"b200serve_{k} {v}" for k, v in m.items() if isinstance(v, (int, float))]
-        lines += [f"b200serve_queue_{k} {v}" for k, v in mq.stats.items() if isinstance(v, (int, float))]
-        return PlainTextResponse("\n".join(lines) + "\n")
+        gauges = {f"scheduler_{k}": v for k, v in m.items()}
+        gauges.update({f"queue_{k}": v for k, v in mq.stats.items()})
+        text = await asyncio.to_thread(metrics_reg.render, "b200serve", gauges)
+        return PlainTextResponse(text)
+
+    @app.post("/v1/embeddings")
+    async def embeddings(request: Request, body: EmbeddingRequest):
+        """Mean-pooled final hidden state of each input through the serving engine."""
+        auth(request)
+        texts = [body.input] if isinstance(body.input, str) else list(body.input)
+        if not texts:
+            raise HTTPException(status_code=400, detail="input is required")
+        eng = await asyncio.to_thread(_get_engine)
+        if not hasattr(eng, "embed"):
+            raise HTTPException(status_code=503, detail="the active engine does not produce embeddings")
+        try:
+            vecs, counts = await asyncio.to_thread(eng.embed, texts)
+        except ValueError as e:
+            raise HTTPException(status_code=400, detail=str(e))
+        data = [{"object": "embedding", "index": i, "embedding": v} for i, v in enumerate(vecs)]
+        return {"object": "list", "data": data, "model": body.model or cfgmod.get_active_model_name(),
+                "usage": {"prompt_tokens": sum(counts), "total_tokens": sum(counts)}}
 
     @app.get("/v1/queue")
     async def queue_status(request: Request):
@@ -366,6 +416,7 @@ def create_app(engine=None, keystore: KeyStore = None):
                             reason = data.pop("finish_reason", "stop")
                             finish = finish if finish == "tool_calls" else reason
                             usage = data
+                            metrics_reg.record_request(dict(data))
                         elif kind == "error":
                             yield f"data: {json.dumps({'error': data})}\n\n"
                     usage["total_tokens"] = usage.get("prompt_tokens", 0) + usage.get("completion_tokens", 0)
@@ -390,9 +441,11 @@ def create_app(engine=None, keystore: KeyStore = None):
         try:
             text, st = await asyncio.to_thread(_run)
         except ValueError as e:
+            metrics_reg.record_request({}, ok=False)
             raise HTTPException(status_code=400, detail=str(e))
         finally:
             mq.request_finished()
+        metrics_reg.record_request(st)
         if fit["compacted"] or fit["trimmed"]:
             st.setdefault("context_fit", fit)
         pt, ct = st.get("prompt_tokens", 0), st.get("completion_tokens", 0)
@@ -413,7 +466,9 @@ def create_app(engine=None, keystore: KeyStore = None):
         return resp
 
     from b200serve.api.chat_jobs import register_chat_job_routes
+    from b200serve.api.session_api import register_session_routes
     register_chat_job_routes(app, auth, _get_engine)
+    register_session_routes(app, auth)
     return app
 
 

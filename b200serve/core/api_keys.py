@@ -63,6 +63,24 @@ class KeyStore:
             self._save()
             return len(self._keys) != n
 
+    def rotate(self, key_id: str) -> str:
+        """Replace key ``key_id`` with a fresh one of the same name; the old key stops working.
+        Returns the new plaintext key (shown once). KeyError for an unknown id."""
+        with self._lock:
+            old = next((k for k in self._keys if k["id"] == key_id), None)
+            if old is None or key_id == "env":
+                raise KeyError(key_id)
+            key = "ak-" + secrets.token_urlsafe(24)
+            entry = self._entry(key, old.get("name", "device"))
+            entry["rotated_from"] = key_id
+            self._keys = [k for k in self._keys if k["id"] != key_id] + [entry]
+            self._save()
+        return key
+
+    def list(self) -> list:
+        """Key metadata without salts or hashes."""
+        return [{"id": k["id"], "name": k.get("name"), "created": k.get("created")} for k in self._keys]
+
     def match(self, token: str):
         hit = None
         for k in self._keys:

@@ -341,6 +341,25 @@ class B200Engine(BaseEngine):
                 raise TimeoutError(f"{r.rid} did not finish")
         return reqs
 
+    def embed(self, texts, timeout: float = 600.0):
+        """Mean-pooled final hidden states (after the final RMSNorm) of each text, computed by
+        this engine's model in its scheduler loop. Returns (vectors, token counts)."""
+        self.load()
+        self.start_loop()
+        reqs = []
+        for t in texts:
+            ids = self.tokenizer.encode(t if isinstance(t, str) else str(t), add_special_tokens=False) or [0]
+            ids = ids[: self.config.max_seq - 1]
+            reqs.append(self.scheduler.add_embedding(Request(prompt=ids, params=SamplingParams(max_tokens=1))))
+        with self._wake:
+            self._wake.notify_all()
+        for r in reqs:
+            if not r.done_event.wait(timeout):
+                raise TimeoutError("embedding request did not finish")
+            if r.embedding is None:
+                raise RuntimeError("embedding failed: " + str(self._error or "engine error"))
+        return [r.embedding for r in reqs], [len(r.tokens) for r in reqs]
+
     # ------------------------------------------------------------ BaseEngine
     def _fit_prompt(self, messages, max_tokens, enable_thinking, tools):
         """Chat template -> token ids that fit the context with room for ``max_tokens``.

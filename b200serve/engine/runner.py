@@ -308,7 +308,7 @@ class ModelRunner:
             lens.append(st + n)
             sts.append(s.get("state_slot", self.scratch_slot))
             bt[i, : len(table)] = torch.as_tensor(table, dtype=torch.int32)
-            if s.get("all_logits"):
+            if s.get("all_logits") or s.get("hidden"):
                 rows += list(range(cu[-2], cu[-1]))
             elif s.get("want_logits", True):
                 rows.append(cu[-1] - 1)
@@ -318,7 +318,8 @@ class ModelRunner:
         fb = ForwardBatch(input_ids=t(ids), positions=t(pos), slots=t(slots), block_tables=bt.to(d),
                           seq_lens=t(lens), logit_rows=torch.as_tensor(rows, dtype=torch.long).to(d),
                           is_decode=False, cu_q=t(cu), q_start=t(qs), max_q=max(len(s["ids"]) for s in seqs),
-                          state_slots=t(sts) if self.lin_state is not None else None, telemetry=watch or None)
+                          state_slots=t(sts) if self.lin_state is not None else None, telemetry=watch or None,
+                          hidden=any(s.get("hidden") for s in seqs))
         if T == 0:
             return None
         with rng(f"prefill T{T}"):

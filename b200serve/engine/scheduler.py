@@ -72,6 +72,7 @@ class Request:
     seed: int = 0
     state_slot: int = -1             # recurrent-state slot (hybrid models) while running
     telemetry: object = None         # TelemetryCapture: per-token forward frames (eager steps)
+    embedding: list = None           # embedding requests: the mean-pooled final hidden state
     done_event: threading.Event = field(default_factory=threading.Event)
 
     def __post_init__(self):
@@ -97,6 +98,7 @@ class Scheduler:
         self.max_seq = max_seq
         self.waiting = []
         self.running = []
+        self.embed_waiting = []
         self.lock = threading.Lock()
         self.pipeline = True
         # hybrid (DeltaNet) models keep a recurrent state per running request
@@ -126,8 +128,56 @@ class Scheduler:
     def abort(self, req: Request):
         req.aborted = True
 
+    def add_embedding(self, req: Request) -> Request:
+        """Queue a prompt whose mean-pooled final hidden state is wanted (no generation)."""
+        if not req.tokens or len(req.tokens) >= self.max_seq:
+            raise ValueError(f"embedding input of {len(req.tokens)} tokens: must be 1..{self.max_seq - 1}")
+        with self.lock:
+            self.embed_waiting.append(req)
+        return req
+
     def has_work(self) -> bool:
-        return bool(self.waiting or self.running)
+        return bool(self.waiting or self.running or self.embed_waiting)
+
+    def _embed_step(self) -> int:
+        """One prefill of queued embedding inputs (up to ``prefill_chunk`` tokens; hybrid models one
+        input at a time, since they share the scratch state slot). Pages are borrowed for the
+        forward and returned right after; the outputs are mean-pooled per input."""
+        with self.lock:
+            batch, total = [], 0
+            for r in list(self.embed_waiting):
+                if batch and (total + len(r.tokens) > self.prefill_chunk or self.free_states is not None):
+                    break
+                batch.append(r)
+                total += len(r.tokens)
+            for r in batch:
+                self.embed_waiting.remove(r)
+        seqs, held = [], []
+        for r in batch:
+            try:
+                table = self.alloc.allocate((len(r.tokens) + BLOCK - 1) // BLOCK)
+            except MemoryError:                     # no free pages now: retry after decode frees some
+                with self.lock:
+                    self.embed_waiting.insert(0, r)
+                continue
+            held.append((r, table))
+            seqs.append({"ids": list(r.tokens), "start": 0, "block_table": table, "hidden": True})
+        if not seqs:
+            return 0
+        try:
+            hid = self.runner.prefill(seqs)
+            off = 0
+            for (r, table) in held:
+                n = len(r.tokens)
+                r.embedding = hid[off:off + n].float().mean(0).cpu().tolist()
+                off += n
+                r.state, r.finish_reason = "finished", "stop"
+                r.finish_time = time.perf_counter()
+        finally:
+            for r, table in held:
+                self.alloc.release(table)
+                r.done_event.set()
+        return 0
 
     def metrics(self) -> dict:
         return {**self.stats, "running": len(self.running), "waiting": len(self.waiting),
@@ -302,6 +352,8 @@ class Scheduler:
 
     def step(self) -> int:
         """Run one forward pass. Returns the number of tokens sampled."""
+        if self.embed_waiting:
+            self._embed_step()
         self._admit()
         for r in [r for r in self.running if r.aborted]:
             self.running.remove(r)

@@ -45,6 +45,7 @@ class ForwardBatch:
     max_q: int = 0
     state_slots: torch.Tensor = None    # hybrid models: recurrent-state slot per sequence
     telemetry: list = None              # [(row, TelemetryCapture)]: per-layer frames for these rows
+    hidden: bool = False                # return the final-normed hidden states of logit_rows, no lm_head
 
 
 class NoComm:
@@ -344,10 +345,12 @@ class Decoder:
             parts = comm.rs_linear(act, lw.down, "mlp")
         x, ag = comm.norm_ag(parts, w.final_norm, eps, residual)
         rows = fb.logit_rows
-        if rows is not None:
+        if rows is not None or fb.hidden:
             if ag is not None:
                 ag.wait()
-            x, ag = x.index_select(0, rows), None
+            x, ag = (x.index_select(0, rows) if rows is not None else x), None
+        if fb.hidden:
+            return x
         return ops.linear(x, w.lm_head, epilogue=ops.EPI_F32, ag=ag)
 
     def _row_parallel(self, x, w, tag):
@@ -415,6 +418,8 @@ class Decoder:
         x = ops.rmsnorm(mlp_parts, w.final_norm, eps, residual=residual)
         if rows is not None:
             x = x.index_select(0, rows)
+        if fb.hidden:
+            return x
         logits = ops.linear(x, w.lm_head, epilogue=ops.EPI_F32)
         if cfg.final_softcap:
             ops.softcap_(logits, cfg.final_softcap)

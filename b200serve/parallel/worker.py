@@ -48,13 +48,15 @@ class BroadcastRunner:
     def prefill(self, seqs):
         flat = [len(seqs)]
         for s in seqs:
-            want = 2 if s.get("all_logits") else int(s.get("want_logits", True))
+            want = 3 if s.get("hidden") else 2 if s.get("all_logits") else int(s.get("want_logits", True))
             flat += [len(s["ids"]), s["start"], want, len(s["block_table"]),
                      s.get("state_slot", self.inner.scratch_slot)]
             flat += list(s["ids"]) + list(s["block_table"])
         payload = torch.as_tensor(flat, dtype=torch.int32).to(self.device)
         self._send([OP_PREFILL, payload.numel()], payload)
         logits = self.inner.prefill(seqs)
+        if any(s.get("hidden") for s in seqs):
+            return logits            # hidden states are replicated on every rank
         return self.comm.gather_vocab(logits)
 
     def decode_loop(self, ids, pos, slots, block_tables, lens, warmup, steps, state_slots=None):
@@ -131,7 +133,7 @@ def _unpack_prefill(flat):
         bt = flat[i:i + nb]
         i += nb
         seqs.append({"ids": ids, "start": start, "want_logits": bool(want), "all_logits": want == 2,
-                     "block_table": bt, "state_slot": st})
+                     "hidden": want == 3, "block_table": bt, "state_slot": st})
     return seqs
 
 
@@ -173,7 +175,9 @@ def worker_loop(runner, comm):
         elif op == OP_PREFILL:
             payload = torch.empty(h[1], dtype=torch.int32, device=runner.device)
             comm.broadcast(payload, 0)
-            logits = runner.prefill(_unpack_prefill(payload.tolist()))
-            comm.gather_vocab(logits)
+            seqs = _unpack_prefill(payload.tolist())
+            logits = runner.prefill(seqs)
+            if not any(s["hidden"] for s in seqs):
+                comm.gather_vocab(logits)
         else:
             raise RuntimeError(f"unknown step op {op}")

@@ -131,6 +131,11 @@ def run_ours(a):
     e2e_tokens = sum(len(r.output) - 1 for r in reqs)
     e2e_tps = e2e_tokens / (last - first_all)
 
+    # batch-1 TTFT: one 2048-token request alone through the same API (the reference's case)
+    one = SamplingParams(temperature=0.0, max_tokens=2, ignore_eos=True)
+    eng.generate(_prompts(1, P, vocab, seed=4), one)
+    ttft_b1 = statistics.median([eng.generate(_prompts(1, P, vocab, seed=5 + i), one)[0].ttft for i in range(3)])
+
     # device-timed decode loop (mirrored on every rank)
     sampler = ClockSampler(gpus=list(range(world))).start()
     res = _device_loop(runner, inner, eng, B, P, K, W, vocab)
@@ -154,6 +159,7 @@ def run_ours(a):
                    "comm": eng.comm.kind if eng.comm else "none",
                    "l2": "inputs larger than L2: every step streams the layer weights and the KV cache (GBs)"},
         "ttft_p50_ms": round(statistics.median(ttfts) * 1e3, 2),
+        "ttft_b1_ms": round(ttft_b1 * 1e3, 2),
         "clocks": clocks,
         "e2e": {"value": round(e2e_tps, 1), "unit": "tok/s", "api": "B200Engine.generate",
                 "h2d_bytes_per_step": pack_bytes, "d2h_bytes_per_step": B * 4,

@@ -83,7 +83,7 @@ def test_misc_routes(client):
     e = client.get("/v1/engine").json()
     assert e["loaded"] and e["config"]["model"] == "tiny-qwen2"
     assert client.get("/health").json()["checks"]["engine"]["ok"]
-    assert "b200serve_generated" in client.get("/metrics").text
+    assert "b200serve_scheduler_generated" in client.get("/metrics").text
 
 
 def test_auth(tmp_path):
