@@ -378,10 +378,17 @@ def create_app(engine=None, keystore: KeyStore = None):
         samp = _sampling_from_request(body)
         eng = await asyncio.to_thread(_get_engine)
         max_tokens = body.max_tokens or max(1, eng.get_context_size() // 2)
+        if opts.get("rag"):
+            from b200serve.api.knowledge_api import get_knowledge
+            kb = await asyncio.to_thread(get_knowledge, eng)
+            messages = await asyncio.to_thread(kb.augment, messages, None, int(opts["rag"]))
         messages, fit = ensure_context_fit(messages, eng.get_context_size(), max_tokens,
                                            count_fn=eng.count_tokens)
         mq.request_started()
         chat_id = f"chatcmpl-{uuid.uuid4().hex[:12]}"
+
+        if body.web_tools:
+            return await _tool_round_response(eng, messages, max_tokens, samp, body, chat_id, model, backend)
 
         if body.stream:
             async def gen():
@@ -465,10 +472,82 @@ def create_app(engine=None, keystore: KeyStore = None):
             resp["x_context_fit"] = st["context_fit"]
         return resp
 
+    async def _tool_round_response(eng, messages, max_tokens, samp, body, chat_id, model, backend):
+        """web_tools: the server runs the model's tool calls itself (rounds), then answers."""
+        from b200serve.api.chat_tools import run_tool_rounds
+        if not body.stream:
+            try:
+                text, st, n = await asyncio.to_thread(run_tool_rounds, eng, messages, max_tokens,
+                                                      samp.get("temperature", 0.7))
+            finally:
+                mq.request_finished()
+            metrics_reg.record_request(st)
+            pt, ct = st.get("prompt_tokens", 0), st.get("completion_tokens", 0)
+            return {"id": chat_id, "object": "chat.completion", "created": int(time.time()), "model": model,
+                    "choices": [{"index": 0, "message": {"role": "assistant", "content": text},
+                                 "finish_reason": st.get("finish_reason", "stop")}],
+                    "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct},
+                    "x_backend": backend, "x_tool_calls": n, "x_stats": st}
+
+        q = _StreamQueue()
+
+        def work():
+            try:
+                text, st, n = run_tool_rounds(eng, messages, max_tokens, samp.get("temperature", 0.7),
+                                              on_tool=lambda d: q.put(("tool", d)))
+                q.put(("content", text))
+                q.put(("usage", {"prompt_tokens": st.get("prompt_tokens", 0),
+                                 "completion_tokens": st.get("completion_tokens", 0), "tool_calls": n,
+                                 "finish_reason": st.get("finish_reason", "stop")}))
+            except _StreamAbandoned:
+                pass
+            except Exception as e:
+                try:
+                    q.put(("error", str(e)))
+                except _StreamAbandoned:
+                    pass
+            finally:
+                q.finish()
+
+        async def gen():
+            threading.Thread(target=work, daemon=True).start()
+            loop = asyncio.get_running_loop()
+            usage, finish = {}, "stop"
+            try:
+                while True:
+                    item = await loop.run_in_executor(None, q.get)
+                    if item is _SENTINEL:
+                        break
+                    kind, data = item
+                    if kind == "tool":
+                        yield f"data: {json.dumps({'x_tool': data})}\n\n"
+                    elif kind == "content":
+                        yield _make_sse_chunk(chat_id, model, {"content": data})
+                    elif kind == "usage":
+                        finish = data.pop("finish_reason", "stop")
+                        usage = data
+                        metrics_reg.record_request(dict(data))
+                    elif kind == "error":
+                        yield f"data: {json.dumps({'error': data})}\n\n"
+                usage["total_tokens"] = usage.get("prompt_tokens", 0) + usage.get("completion_tokens", 0)
+                yield _make_sse_chunk(chat_id, model, {}, finish_reason=finish,
+                                      extra={"x_usage": usage, "x_backend": backend})
+                yield "data: [DONE]\n\n"
+            finally:
+                q.abandon()
+                mq.request_finished()
+
+        return StreamingResponse(gen(), media_type="text/event-stream",
+                                 headers={"Cache-Control": "no-cache", "X-Accel-Buffering": "no"})
+
     from b200serve.api.chat_jobs import register_chat_job_routes
     from b200serve.api.session_api import register_session_routes
     register_chat_job_routes(app, auth, _get_engine)
     register_session_routes(app, auth)
+    from b200serve.api.agent_api import register_agent_routes
+    from b200serve.api.knowledge_api import register_knowledge_routes
+    register_agent_routes(app, auth, _get_engine)
+    register_knowledge_routes(app, auth, _get_engine)
     return app
 
 
