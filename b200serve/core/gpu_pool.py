@@ -77,6 +77,94 @@ class GPUPool:
     def status(self) -> list:
         return [vars(d) for d in self.devices()]
 
+    def refresh(self, index: int):
+        """One device's live reading, or None when it cannot be queried."""
+        for d in self.devices():
+            if d.index == index:
+                return d
+        return None
+
+    def measure_baseline(self, index: int = 0) -> float:
+        """MB in use on the device by anything other than this process's PyTorch allocator
+        (the driver context, other processes): the headroom an allocation must leave."""
+        d = self.refresh(index)
+        if d is None:
+            return 0.0
+        mine = 0
+        try:
+            import torch
+            if torch.cuda.is_available() and index < torch.cuda.device_count():
+                mine = torch.cuda.memory_reserved(index) >> 20
+        except Exception:
+            pass
+        return float(max(0, d.used_mb - mine))
+
+    def wait_for_memory(self, need_mb: float, index: int = 0, timeout_s: float = 30.0, poll_s: float = 0.5,
+                        clock=None, sleep=None) -> bool:
+        """Block until device ``index`` has ``need_mb`` free (True) or ``timeout_s`` passes
+        (False). Memory freed by a process that just exited can take seconds to come back;
+        loading before then fails (reference: core/gpu_pool.py:725)."""
+        import time as _t
+        clock, sleep = clock or _t.monotonic, sleep or _t.sleep
+        deadline = clock() + timeout_s
+        while True:
+            d = self.refresh(index)
+            if d is not None and d.free_mb >= need_mb:
+                return True
+            if clock() >= deadline:
+                return False
+            sleep(poll_s)
+
+    def wait_settled(self, indices=None, tolerance_mb: int = 256, polls: int = 3, timeout_s: float = 30.0,
+                     poll_s: float = 0.5, clock=None, sleep=None) -> dict:
+        """Poll until every listed device's free memory has varied by at most ``tolerance_mb``
+        over the last ``polls`` readings (a release or an allocation in flight has finished).
+        Returns {index: settled free MB} (the last reading for devices that never settled)."""
+        import time as _t
+        clock, sleep = clock or _t.monotonic, sleep or _t.sleep
+        hist = {}
+        deadline = clock() + timeout_s
+        while True:
+            devs = {d.index: d for d in self.devices()}
+            want = list(devs) if indices is None else list(indices)
+            for i in want:
+                if i in devs:
+                    hist.setdefault(i, []).append(devs[i].free_mb)
+            done = all(len(hist.get(i, [])) >= polls and
+                       max(hist[i][-polls:]) - min(hist[i][-polls:]) <= tolerance_mb for i in want)
+            if done or clock() >= deadline:
+                return {i: hist[i][-1] for i in want if hist.get(i)}
+            sleep(poll_s)
+
+    def estimate_allocation(self, model_cfg, tp_size: int = 1, max_tokens: int = 0, kv_format: str = "bf16",
+                            weight_bytes: float = 2.0, shares=None, workspace_mb: float = 1024.0,
+                            indices=None) -> list:
+        """Per-device MB for a tensor-parallel placement: weights (the sharded part, lm_head
+        included, split by ``shares``, default even; the input embedding replicated), KV for ``max_tokens`` over
+        the device's KV heads, activation/graph workspace, and the device's measured baseline.
+        Returns [{index, weights_mb, kv_mb, workspace_mb, reserve_mb, total_mb, free_mb, fits}]."""
+        shares = list(shares) if shares else [1.0 / tp_size] * tp_size
+        if len(shares) != tp_size or abs(sum(shares) - 1.0) > 1e-6:
+            raise ValueError("shares must give one fraction per rank, summing to 1")
+        base = estimate_model_memory(model_cfg, 1, max_tokens, kv_format, weight_bytes)
+        c = model_cfg
+        emb = c.vocab_size * c.hidden_size * weight_bytes / 2 ** 20      # replicated input embedding
+        sharded = base["weights_mb"] - emb
+        devs = {d.index: d for d in self.devices()}
+        idx = list(indices) if indices is not None else sorted(devs)[:tp_size]
+        out = []
+        for r, frac in enumerate(shares):
+            i = idx[r] if r < len(idx) else r
+            w = sharded * frac + emb
+            kv = base["kv_mb"] * frac
+            reserve = self.measure_baseline(i) if i in devs else 0.0
+            total = w + kv + workspace_mb + reserve
+            free = devs[i].free_mb if i in devs else 0
+            out.append({"index": i, "weights_mb": round(w, 1), "kv_mb": round(kv, 1),
+                        "workspace_mb": workspace_mb, "reserve_mb": round(reserve, 1), "total_mb": round(total, 1),
+                        "free_mb": free, "fits": free >= total - reserve})
+        return out
+
 
 def estimate_model_memory(model_cfg, tp_size=1, max_tokens=0, kv_format="bf16", weight_bytes=2.0) -> dict:
     """Per-rank MB for weights (TP-sharded, embedding replicated) and KV for max_tokens."""

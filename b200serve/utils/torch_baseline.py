@@ -87,7 +87,7 @@ class TorchDecoder:
             v = qkv[:, :, nq + nkv:]
             self.k[li][bidx, :, pos] = k            # [B, T, nkv, hd] into [B, nkv, L, hd]
             self.v[li][bidx, :, pos] = v
-            a = F.scaled_dot_product_attention(q.transpose(1, 2), self.k[li], self.v[li], attn_mask=mask,
+            a = F.scaled_dot_product_attention(q.transpose(1, 2), self.k[li][:B], self.v[li][:B], attn_mask=mask,
                                                enable_gqa=True)
             o = F.linear(a.transpose(1, 2).reshape(B, T, nq * hd), lw["o"])
             h = h + self._allreduce(o)

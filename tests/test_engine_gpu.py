@@ -77,3 +77,31 @@ def test_sampling_seeded_and_prefix_cache():
         assert r2.prefix_hit >= 96          # six full pages reused from the first request
     finally:
         e.unload()
+
+
+def test_embeddings_gpu_vs_cpu():
+    """/v1/embeddings' engine path (mean-pooled final hidden states) through the CUDA kernels
+    agrees with the fp32 CPU path of the same weights."""
+    cfg = BUILTIN["tiny-qwen2"]
+    w_cpu = random_weights(cfg, seed=0, dtype=torch.float32)
+    w_gpu = random_weights(cfg, seed=0, dtype=torch.bfloat16, device="cpu")     # same draws as the CPU copy
+    for lw in w_gpu.layers:
+        for k, v in vars(lw).items():
+            if isinstance(v, torch.Tensor):
+                setattr(lw, k, v.cuda())
+    w_gpu.embed, w_gpu.lm_head, w_gpu.final_norm = w_gpu.embed.cuda(), w_gpu.lm_head.cuda(), w_gpu.final_norm.cuda()
+    ec, eg = _eng(w_cpu, "cpu", "float32", graphs=False), _eng(w_gpu, "cuda", "bfloat16")
+    try:
+        texts = ["the quick brown fox", "jumps over the lazy dog " * 20, "x"]
+        vc, nc = ec.embed(texts)
+        vg, ng = eg.embed(texts)
+        assert nc == ng
+        a, b = torch.tensor(vc), torch.tensor(vg)
+        cos = torch.nn.functional.cosine_similarity(a, b, dim=-1)
+        assert cos.min().item() > 0.995, cos
+        # generation still works after an embedding step on the same engine
+        [r] = eg.generate([_prompt(16)], SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True), timeout=120)
+        assert len(r.output) == 4 and ops.gemm_error_flag() == 0
+    finally:
+        ec.unload()
+        eg.unload()
