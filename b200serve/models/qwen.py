@@ -253,6 +253,14 @@ class Decoder:
             q = ops.qkv_fused(x, lw.qkv, lw.qkv_bias, lw.q_norm, lw.k_norm, self.kv_cos[i], fb.positions, fb.slots,
                               kc, vc, self.nq, self.nkv, self.cfg.rms_eps, ag=ag)
             return self._attn_core(i, q, fb, plan)
+        if (plain and ag is None and fb.is_decode and self.tq is None and self.kv.kv_format == "bf16"
+                and getattr(self, "_partial_ok", False) and x.is_cuda):
+            pp = ops.linear_partial(x, lw.qkv)
+            if pp is not None:
+                q = ops.qkv_post_partial(pp, lw.qkv_bias, lw.q_norm, lw.k_norm, self.kv_cos[i], fb.positions,
+                                         fb.slots, self.kv.k[i], self.kv.v[i], self.nq, self.nkv, self.cfg.rms_eps,
+                                         self.hd)
+                return self._attn_core(i, q, fb, plan)
         qkv = ops.linear(x, lw.qkv, bias=lw.qkv_bias, ag=ag)
         out = self._attend(i, qkv, lw, fb, T, plan, tq_pre)
         if self.cfg.attn_output_gate:
@@ -354,7 +362,12 @@ class Decoder:
         return ops.linear(x, w.lm_head, epilogue=ops.EPI_F32, ag=ag)
 
     def _row_parallel(self, x, w, tag):
-        """Row-parallel linear whose output is summed over tensor-parallel ranks."""
+        """Row-parallel linear whose output is summed over tensor-parallel ranks. On one rank a
+        decode batch leaves the output as stream-K partial sums that the next norm adds up."""
+        if getattr(self.comm, "world", 1) == 1 and getattr(self, "_partial_ok", False):
+            pp = ops.linear_partial(x, w)
+            if pp is not None:
+                return pp
         if hasattr(self.comm, "linear_reduce"):
             return self.comm.linear_reduce(x, w, tag)
         return self.comm.reduce_parts(ops.linear(x, w), tag)
@@ -366,6 +379,8 @@ class Decoder:
         eps = cfg.rms_eps
         T = fb.input_ids.shape[0]
         comm = self.comm
+        # telemetry reads every layer's output rows directly, so those steps keep dense outputs
+        self._partial_ok = not fb.telemetry
         if hasattr(comm, "begin_step"):
             comm.begin_step()
         h = ops.embedding(fb.input_ids, w.embed)

@@ -95,7 +95,9 @@ def rmsnorm(parts, weight, eps, residual=None, residual_out=None, out=None):
     if _cuda(x0):
         out = out if out is not None else torch.empty_like(x0)
         flags = getattr(parts, "flags_ptr", None)
-        if getattr(parts, "lamport", False):
+        if isinstance(parts, PartialParts):
+            ext().rmsnorm_partial(parts[0], parts.part, *parts.plan, residual, residual_out, weight, out, float(eps))
+        elif getattr(parts, "lamport", False):
             # flag-free receive slots: poll the data; skip the wait for the push GEMM's grid only
             # when that GEMM was the launch right before this one
             direct = launch_count() == parts.launch_mark + 1     # +1: this norm, counted above
@@ -403,6 +405,64 @@ def embedding(ids, table, out=None):
 
 
 # ------------------------------------------------------------------ GEMM
+class PartialParts(list):
+    """Output of a decode GEMM left as fp32 stream-K partial sums (gemm_tc_partial): the row
+    kernel that consumes it (rmsnorm, qkv_post_partial) adds the slots up. Element 0 is a
+    [T, N] bf16 view that only carries the shape; ``part`` and ``plan`` (kb, ctas, total) say
+    where the slots are."""
+
+    def __init__(self, like, part, plan):
+        super().__init__([like])
+        self.part, self.plan = part, plan
+
+
+_PARTIAL = os.environ.get("B200_GEMM_PARTIAL", "1") != "0"
+_partial_bufs = {}
+_num_sms = {}
+
+
+def _partial_buffer(device, floats: int = 4 << 20):
+    """Two fp32 buffers per device used in turn, so a consumer still reading one never races
+    the next partial GEMM."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    if key not in _partial_bufs:
+        _partial_bufs[key] = [[torch.empty(floats, dtype=torch.float32, device=device) for _ in range(2)], 0]
+    bufs = _partial_bufs[key]
+    bufs[1] ^= 1
+    return bufs[0][bufs[1]]
+
+
+def linear_partial(x, w):
+    """x @ w^T for a decode batch (1..64 rows) as stream-K partial sums (PartialParts), or None
+    when this path does not apply (CPU, plain weight, larger batch, disabled by
+    B200_GEMM_PARTIAL=0, or a partial set larger than the buffer)."""
+    if not (_PARTIAL and x.is_cuda and isinstance(w, PackedWeight) and 1 <= x.shape[0] <= 64):
+        return None
+    M, K = x.shape
+    dev = x.device
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    if key not in _num_sms:
+        _num_sms[key] = torch.cuda.get_device_properties(key).multi_processor_count
+    kb, ctas, total, slots = ext().gemm_partial_plan(M, w.N, K, _num_sms[key])
+    buf = _partial_buffer(dev)
+    if slots * M * w.N > buf.numel():
+        return None
+    _cuda(x)
+    ext().gemm_tc_partial(x.contiguous() if x.stride(1) != 1 else x, w.data, w.N, buf)
+    like = buf.view(torch.bfloat16)[: M * w.N].view(M, w.N)
+    return PartialParts(like, buf, (kb, ctas, total))
+
+
+def qkv_post_partial(pp, bias, q_norm, k_norm, cos_sin, positions, slots, k_cache, v_cache, nq, nkv, eps, hd):
+    """qkv_post over a QKV projection left as partial sums (bf16 KV cache)."""
+    T = pp[0].shape[0]
+    q_out = torch.empty(T, nq, hd, dtype=torch.bfloat16, device=pp.part.device)
+    _cuda(q_out)
+    ext().qkv_post_partial(pp[0], pp.part, *pp.plan, bias, q_norm, k_norm, cos_sin, positions, slots, q_out,
+                           k_cache, v_cache, None, None, nq, nkv, float(eps))
+    return q_out
+
+
 class GemmWorkspace:
     """fp32 split-K workspace and per-tile counters shared by the GEMMs of one stream.
 

@@ -9,6 +9,17 @@ void rmsnorm_fused_wait(std::vector<torch::Tensor> parts, c10::optional<torch::T
 void rmsnorm_lamport(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
                      c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps,
                      int64_t err_ptr, bool skip_prior_wait);
+std::vector<int64_t> gemm_partial_plan(int64_t M, int64_t N, int64_t K, int64_t num_sms);
+std::vector<int64_t> gemm_tc_partial(torch::Tensor act, torch::Tensor w, int64_t packed_n, torch::Tensor part);
+void rmsnorm_partial(torch::Tensor like, torch::Tensor part, int64_t kb, int64_t ctas, int64_t total,
+                     c10::optional<torch::Tensor> residual_in, c10::optional<torch::Tensor> residual_out,
+                     torch::Tensor w, torch::Tensor out, double eps);
+void qkv_post_partial(torch::Tensor like, torch::Tensor part, int64_t kb, int64_t ctas, int64_t total,
+                      c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
+                      c10::optional<torch::Tensor> kn_w, torch::Tensor cos_sin, torch::Tensor positions,
+                      torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache,
+                      c10::optional<torch::Tensor> k_scale, c10::optional<torch::Tensor> v_scale, int64_t nq,
+                      int64_t nkv, double eps);
 void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, int64_t ldo, torch::Tensor flag_ptrs,
                   int64_t epoch_ptr, torch::Tensor tile_done, c10::optional<torch::Tensor> bias, torch::Tensor ws,
                   torch::Tensor counters, int64_t err_ptr, int64_t packed_n, int64_t rs_rows, int64_t lamport);
@@ -133,6 +144,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_fused_wait", &rmsnorm_fused_wait);
   m.def("rmsnorm_rs_ag", &rmsnorm_rs_ag);
   m.def("gemm_tc_push", &gemm_tc_push);
+  m.def("gemm_partial_plan", &gemm_partial_plan);
+  m.def("gemm_tc_partial", &gemm_tc_partial);
+  m.def("rmsnorm_partial", &rmsnorm_partial);
+  m.def("qkv_post_partial", &qkv_post_partial);
   m.def("rmsnorm_lamport", &rmsnorm_lamport);
   m.def("ipc_malloc", &ipc_malloc);
   m.def("ipc_free", &ipc_free);

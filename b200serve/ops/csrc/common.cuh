@@ -74,6 +74,53 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// fp32 partial sums of a stream-K GEMM (EPI_PARTIAL) that a row kernel reduces: slot s of
+// column c holds part[s][row][c]. CTA g of `ctas` streamed the flattened k-blocks
+// [g*total/ctas, (g+1)*total/ctas) of the 128-wide column tiles (`kb` k-blocks per tile,
+// total = tiles*kb); tile t's slots are the CTAs from the one holding k-block t*kb to the one
+// holding k-block (t+1)*kb - 1, in that order.
+struct PartialIn {
+  const float* part;      // nullptr: not in use
+  int kb, ctas;
+  long long total;
+  int rows, cols;
+};
+
+__device__ __forceinline__ int partial_slots(const PartialIn& pi, int col) {
+  const long long t = col / 128;
+  const long long first = ((t * pi.kb + 1) * pi.ctas + pi.total - 1) / pi.total - 1;
+  const long long last = ((t + 1) * pi.kb * pi.ctas + pi.total - 1) / pi.total - 1;
+  return (int)(last - first + 1);
+}
+
+// Sum of the slots for NE consecutive columns of one tile (NE even; 8-byte aligned, 16-byte
+// when NE is a multiple of 4), in slot order, rounded to bf16 as a bf16 GEMM output would be.
+template <int NE>
+__device__ __forceinline__ void partial_sum(const PartialIn& pi, int row, int col, float* acc) {
+  const int n = partial_slots(pi, col);
+  const float* src = pi.part + (size_t)row * pi.cols + col;
+  const size_t slot = (size_t)pi.rows * pi.cols;
+#pragma unroll
+  for (int i = 0; i < NE; ++i) acc[i] = 0.f;
+  for (int s = 0; s < n; ++s) {
+    if constexpr (NE % 4 == 0) {
+#pragma unroll
+      for (int i = 0; i < NE; i += 4) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(src + s * slot + i));
+        acc[i] += v.x; acc[i + 1] += v.y; acc[i + 2] += v.z; acc[i + 3] += v.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < NE; i += 2) {
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(src + s * slot + i));
+        acc[i] += v.x; acc[i + 1] += v.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < NE; ++i) acc[i] = __bfloat162float(__float2bfloat16_rn(acc[i]));
+}
+
 }  // namespace b200
 
 namespace b200 {

@@ -354,6 +354,53 @@ void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, in
   launch_by_bn(BN, EPI_PUSH, tw, ta, p, grid, at::cuda::getCurrentCUDAStream());
 }
 
+// Decode-sized GEMM (M <= 64) as stream-K with consumer-side reduction: every CTA streams an
+// equal share of the flattened (n tile, k block) space and stores the fp32 partial of each
+// piece to part[slot][M][N]; the row kernel that consumes the output (RMSNorm, qkv_post) sums
+// the slots (PartialIn). No split-K counters and no fixup pass. Returns {kb, ctas, total,
+// slots}; part must hold slots * M * N floats (gemm_partial_slots gives the size up front).
+std::vector<int64_t> gemm_partial_plan(int64_t M, int64_t N, int64_t K, int64_t num_sms) {
+  const int64_t kb = (K + 63) / 64, tiles = (N + 127) / 128, total = tiles * kb;
+  // at least 4 k-blocks (64 KB of weights) per CTA, so every piece amortises its pipeline start
+  const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>(num_sms, total / 4));
+  const int64_t slots = (kb * ctas + total - 1) / total + 1;
+  return {kb, ctas, total, slots};
+}
+
+std::vector<int64_t> gemm_tc_partial(torch::Tensor act, torch::Tensor w, int64_t packed_n, torch::Tensor part) {
+  TORCH_CHECK(act.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16);
+  TORCH_CHECK(act.dim() == 2 && act.stride(1) == 1 && w.is_contiguous());
+  TORCH_CHECK(part.scalar_type() == at::kFloat && part.is_contiguous(), "partials: contiguous fp32");
+  const bool packed = packed_n > 0;
+  const int M = act.size(0), K = act.size(1), N = packed ? (int)packed_n : w.size(0);
+  TORCH_CHECK(M >= 1 && M <= 64, "the stream-K partial GEMM serves decode sizes (1..64 tokens)");
+  TORCH_CHECK(K % 8 == 0 && N % 8 == 0, "K and N must be multiples of 8");
+  if (g_num_sms == 0) {
+    int dev;
+    B200_CHECK_CUDA(cudaGetDevice(&dev));
+    B200_CHECK_CUDA(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
+  }
+  auto plan = gemm_partial_plan(M, N, K, g_num_sms);
+  const int BN = M <= 16 ? 16 : M <= 32 ? 32 : 64;
+  TORCH_CHECK(part.numel() >= plan[3] * M * N, "partial buffer too small: need ", plan[3] * M * N, " floats");
+  GemmParams p{};
+  p.M = M; p.N = N; p.K = K;
+  p.m_tiles = 1; p.n_tiles = (N + 127) / 128; p.splits = 1;
+  p.kb_total = (int)plan[0]; p.kb_per_split = p.kb_total;
+  p.units = (int)plan[1];
+  p.streamk = 1;
+  p.sk_total = plan[2];
+  p.part = part.data_ptr<float>();
+  p.err = gemm_err_word();
+  p.w_packed = packed ? 1 : 0;
+  p.w_ptr = packed ? reinterpret_cast<const uint8_t*>(w.data_ptr()) : nullptr;
+  p.trace = next_trace();
+  CUtensorMap tw = weight_tmap(w, N, K, packed);
+  CUtensorMap ta = make_tmap_bf16(act.data_ptr(), M, K, act.stride(0), BN);
+  launch_by_bn(BN, EPI_PARTIAL, tw, ta, p, (int)plan[1], at::cuda::getCurrentCUDAStream());
+  return plan;
+}
+
 // Grouped expert GEMM: act [R, K] rows sorted by expert, offsets [E+1] (device), w packed
 // [E][n_tiles][k_blocks][128][64] (logical per-expert [N, K]); out [R, N] bf16 or [R, N/2] (SwiGLU).
 // max_rows bounds the rows of one expert (sizes the m-tile grid without reading offsets on the host).

@@ -28,7 +28,7 @@
 
 namespace b200 {
 
-enum GemmEpi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_PUSH = 3, EPI_QKV = 4 };
+enum GemmEpi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_PUSH = 3, EPI_QKV = 4, EPI_PARTIAL = 5 };
 
 constexpr int kMaxPeers = 8;
 
@@ -85,6 +85,13 @@ struct GemmParams {
   // stores). The kernel lets its dependent launch only after its own prerequisites completed,
   // so a consumer that skips griddepcontrol.wait still runs after everything before this GEMM.
   int lamport;
+  // stream-K with partial sums reduced by the consumer (EPI_PARTIAL, m_tiles == 1): CTA c streams the
+  // flattened k-blocks [c*sk_total/G, (c+1)*sk_total/G) of the n tiles (sk_total = n_tiles*kb_total,
+  // G = gridDim.x), cut at tile boundaries; each piece's fp32 partial goes to
+  // part[slot][M][N] with slot = c - (first CTA touching the tile). No counters, no fixup pass.
+  int streamk;
+  long long sk_total;
+  float* part;
   // optional per-CTA timeline (globaltimer ns): [cta][8] = entry, setup done, first TMA issued,
   // first stage landed, last MMA committed, epilogue done, exit (thread 0), exit (thread 32)
   unsigned long long* trace;
@@ -296,6 +303,54 @@ __device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int BN) 
   return x;
 }
 
+// One piece of work of a CTA: a (tile, k-range) with the partial-sum slot (stream-K) or the split.
+struct Work {
+  Unit x;
+  int kb0, kb1, slot;
+};
+
+__device__ __forceinline__ long long sk_begin(const GemmParams& p, long long c) {
+  return c * p.sk_total / (long long)gridDim.x;
+}
+// first CTA whose range touches tile t: the largest c with sk_begin(c) <= t * kb_total
+__device__ __forceinline__ int sk_first_cta(const GemmParams& p, int t) {
+  const long long x = ((long long)t * p.kb_total + 1) * (long long)gridDim.x;
+  return (int)((x + p.sk_total - 1) / p.sk_total) - 1;
+}
+
+// The sequence of work pieces of this CTA; every role (producer, MMA issuer, epilogue) walks
+// the same sequence, so they agree on stage and accumulator order.
+struct WorkIter {
+  int u;
+  long long g, g_end;
+  __device__ __forceinline__ explicit WorkIter(const GemmParams& p) {
+    u = blockIdx.x;
+    g = p.streamk ? sk_begin(p, blockIdx.x) : 0;
+    g_end = p.streamk ? sk_begin(p, (long long)blockIdx.x + 1) : 0;
+  }
+  __device__ __forceinline__ bool next(const GemmParams& p, int BN, Work& w) {
+    if (p.streamk) {
+      if (g >= g_end) return false;
+      const int t = (int)(g / p.kb_total);
+      const long long seg_end = min(g_end, (long long)(t + 1) * p.kb_total);
+      w.x.n_tile = t; w.x.m_tile = 0; w.x.split = 0; w.x.tile = t;
+      w.x.a_row0 = 0; w.x.m_lim = p.M; w.x.w_tile_base = t; w.x.empty = false;
+      w.kb0 = (int)(g - (long long)t * p.kb_total);
+      w.kb1 = (int)(seg_end - (long long)t * p.kb_total);
+      w.slot = (int)blockIdx.x - sk_first_cta(p, t);
+      g = seg_end;
+      return true;
+    }
+    if (u >= p.units) return false;
+    w.x = decode_unit(p, u, BN);
+    w.kb0 = w.x.split * p.kb_per_split;
+    w.kb1 = min(p.kb_total, w.kb0 + p.kb_per_split);
+    w.slot = w.x.split;
+    u += gridDim.x;
+    return true;
+  }
+};
+
 // TMA coordinates of the weight tile (n_tile, k block kb) in the plain [N, K]
 // layout or the tile-contiguous packed layout (each 128x64 tile one 16 KB run).
 __device__ __forceinline__ int w_x(const GemmParams& p, int kb) { return p.w_packed ? 0 : kb * 64; }
@@ -438,32 +493,35 @@ __global__ void __launch_bounds__(192, 2)
       uint32_t phase = 0;
       // Weights never depend on the previous kernel: stream the first stages of W
       // while that kernel finishes, then wait for it before loading activations.
+      WorkIter it(p);
+      Work w;
+      bool have = it.next(p, BN, w);
       int pre = 0;
-      if ((int)blockIdx.x < p.units && !p.grouped) {
-        const Unit x = decode_unit(p, blockIdx.x, BN);
-        const int kb0 = x.split * p.kb_per_split, kb1 = min(p.kb_total, kb0 + p.kb_per_split);
-        pre = min(kb1 - kb0, STAGES);
+      if (have && !p.grouped && !w.x.empty) {
+        pre = min(w.kb1 - w.kb0, STAGES);
         for (int i = 0; i < pre; ++i) {
           tc::mbar_arrive_expect_tx(&full[i], Cfg::STAGE_BYTES);
-          tc::tma_load_2d(s_w + i * Cfg::W_BYTES, &tm_w, &full[i], w_x(p, kb0 + i), w_y(p, x.w_tile_base, kb0 + i), pol_w);
+          tc::tma_load_2d(s_w + i * Cfg::W_BYTES, &tm_w, &full[i], w_x(p, w.kb0 + i),
+                          w_y(p, w.x.w_tile_base, w.kb0 + i), pol_w);
         }
-        // Stream further weight tiles of this CTA's units into L2 while the previous kernel
+        // Stream further weight tiles of this CTA's work into L2 while the previous kernel
         // finishes (tile-packed weights: each 128 x 64 tile is one contiguous 16 KB run).
         if (p.w_ptr && p.l2_prefetch_blocks > 0) {
           int budget = p.l2_prefetch_blocks;
-          for (int u = blockIdx.x; u < p.units && budget > 0; u += gridDim.x) {
-            const Unit y = decode_unit(p, u, BN);
-            const int a0 = y.split * p.kb_per_split + (u == (int)blockIdx.x ? pre : 0);
-            const int a1 = min(p.kb_total, y.split * p.kb_per_split + p.kb_per_split);
-            for (int kb = a0; kb < a1 && budget > 0; ++kb, --budget)
-              tc::prefetch_l2(p.w_ptr + ((size_t)y.w_tile_base * p.kb_total + kb) * (size_t)Cfg::W_BYTES,
+          WorkIter it2(p);
+          Work y;
+          bool first_piece = true;
+          while (budget > 0 && it2.next(p, BN, y)) {
+            for (int kb = y.kb0 + (first_piece ? pre : 0); kb < y.kb1 && budget > 0; ++kb, --budget)
+              tc::prefetch_l2(p.w_ptr + ((size_t)y.x.w_tile_base * p.kb_total + kb) * (size_t)Cfg::W_BYTES,
                               Cfg::W_BYTES);
+            first_piece = false;
           }
         }
         pdl_wait();
         if (p.ag_flags) wait_ag_flags(p, abort_flag, err);
         for (int i = 0; i < pre; ++i)
-          tc::tma_load_2d(s_a + i * Cfg::A_BYTES, &tm_a, &full[i], (kb0 + i) * 64, x.a_row0, pol_a);
+          tc::tma_load_2d(s_a + i * Cfg::A_BYTES, &tm_a, &full[i], (w.kb0 + i) * 64, w.x.a_row0, pol_a);
         trace_mark(p, 2);
         stage = pre % STAGES;
         phase = pre == STAGES ? 1 : 0;
@@ -471,15 +529,16 @@ __global__ void __launch_bounds__(192, 2)
         pdl_wait();
         if (p.ag_flags) wait_ag_flags(p, abort_flag, err);
       }
-      for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
-        const Unit x = decode_unit(p, u, BN);
-        if (x.empty) continue;
-        const int kb0 = x.split * p.kb_per_split, kb1 = min(p.kb_total, kb0 + p.kb_per_split);
-        for (int kb = kb0 + (u == (int)blockIdx.x ? pre : 0); kb < kb1; ++kb) {
+      bool first_piece = true;
+      for (; have && !*abort_flag; have = it.next(p, BN, w)) {
+        const int kb_start = w.kb0 + (first_piece ? pre : 0);
+        first_piece = false;
+        if (w.x.empty) continue;
+        for (int kb = kb_start; kb < w.kb1; ++kb) {
           if (!tc::mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, err, 1)) break;
           tc::mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-          tc::tma_load_2d(s_w + stage * Cfg::W_BYTES, &tm_w, &full[stage], w_x(p, kb), w_y(p, x.w_tile_base, kb), pol_w);
-          tc::tma_load_2d(s_a + stage * Cfg::A_BYTES, &tm_a, &full[stage], kb * 64, x.a_row0, pol_a);
+          tc::tma_load_2d(s_w + stage * Cfg::W_BYTES, &tm_w, &full[stage], w_x(p, kb), w_y(p, w.x.w_tile_base, kb), pol_w);
+          tc::tma_load_2d(s_a + stage * Cfg::A_BYTES, &tm_a, &full[stage], kb * 64, w.x.a_row0, pol_a);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
@@ -493,10 +552,11 @@ __global__ void __launch_bounds__(192, 2)
       uint32_t acc_phase[2] = {0, 0};
       int acc = 0;
       bool first = true;
-      for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
-        const Unit x = decode_unit(p, u, BN);
-        if (x.empty) continue;
-        const int kb0 = x.split * p.kb_per_split, kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+      WorkIter it(p);
+      Work w;
+      while (!*abort_flag && it.next(p, BN, w)) {
+        if (w.x.empty) continue;
+        const int kb0 = w.kb0, kb1 = w.kb1;
         if (!tc::mbar_wait_bounded(&tempty[acc], acc_phase[acc] ^ 1, abort_flag, err, 2)) break;
         if (first) {
           tc::mbar_wait_bounded(&full[stage], phase, abort_flag, err, 3);
@@ -536,14 +596,32 @@ __global__ void __launch_bounds__(192, 2)
     uint32_t acc_phase[2] = {0, 0};
     int acc = 0;
     const int total_tiles = p.units / p.splits;
-    for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
-      const Unit x = decode_unit(p, u, BN);
+    WorkIter it(p);
+    Work w;
+    while (!*abort_flag && it.next(p, BN, w)) {
+      const Unit& x = w.x;
       if (x.empty) continue;
       const int t_end = x.a_row0 + min(x.m_lim, BN);
       if (!tc::mbar_wait_bounded(&tfull[acc], acc_phase[acc], abort_flag, err, 4)) break;
       tc::tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
-      if (p.splits == 1) {
+      if constexpr (EPI == EPI_PARTIAL) {
+        // fp32 partial of this piece -> part[slot][t][col] (consecutive lanes: consecutive columns)
+        float* dst = p.part + (size_t)w.slot * p.M * p.N;
+        const int col = x.n_tile * 128 + row;
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tc::tmem_ld16(t_row + c0, v);
+          if (col < p.N) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (x.a_row0 + c0 + j < t_end) dst[(size_t)(x.a_row0 + c0 + j) * p.N + col] = v[j];
+          }
+        }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+      } else if (p.splits == 1) {
         for (int c0 = 0; c0 < BN; c0 += 16) {
           float v[16];
           tc::tmem_ld16(t_row + c0, v);

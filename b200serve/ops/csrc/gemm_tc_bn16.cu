@@ -12,6 +12,7 @@ void launch_gemm_bn<16>(int epi, const CUtensorMap& tw, const CUtensorMap& ta, c
     case EPI_SWIGLU: launch_gemm<16, EPI_SWIGLU>(tw, ta, p, grid, stream); break;
     case EPI_PUSH: launch_gemm<16, EPI_PUSH>(tw, ta, p, grid, stream); break;
     case EPI_QKV: launch_gemm<16, EPI_QKV>(tw, ta, p, grid, stream); break;
+    case EPI_PARTIAL: launch_gemm<16, EPI_PARTIAL>(tw, ta, p, grid, stream); break;
     default: TORCH_CHECK(false, "bad epilogue");
   }
 }

@@ -94,7 +94,8 @@ template <int VPT>
 __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
     PartPtrs parts, int nparts, const __nv_bfloat16* residual_in, __nv_bfloat16* residual_out,
     const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H, float eps,
-    const int* wait_flags, const int* epoch, int* err, const AgArgs ag, uint64_t wait_ns, int lamport) {
+    const int* wait_flags, const int* epoch, int* err, const AgArgs ag, uint64_t wait_ns, int lamport,
+    const PartialIn pin) {
   __shared__ float red[32];
   // lamport == 2: the partials come from a flag-free push GEMM launched right before this kernel,
   // which let it start only after that GEMM's own prerequisites completed; the partials are
@@ -112,6 +113,10 @@ __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
     const int col = (threadIdx.x + s * blockDim.x) * 8;
     if (col < H) {
       float acc[8];
+      if (pin.part) {
+        // the GEMM's fp32 stream-K partials of this row (one "part"), summed here
+        partial_sum<8>(pin, row, col, acc);
+      } else {
       // partials may have been written by other GPUs: read through L2, not L1
       uint4 a4 = lamport ? lamport_take(parts.p[0] + base + col, wait_ns, err, gave_up)
                          : __ldcg(reinterpret_cast<const uint4*>(parts.p[0] + base + col));
@@ -123,6 +128,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
         unpack8(*reinterpret_cast<bf16x8*>(&t4), t);
 #pragma unroll
         for (int i = 0; i < 8; ++i) acc[i] += t[i];
+      }
       }
       if (residual_in) {
         float r[8];
@@ -190,7 +196,8 @@ __global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __n
                                 const float* __restrict__ cos_sin, const int* __restrict__ positions,
                                 const int* __restrict__ slots, __nv_bfloat16* __restrict__ q_out,
                                 void* __restrict__ k_cache, void* __restrict__ v_cache, __half* __restrict__ k_scale,
-                                __half* __restrict__ v_scale, int T, int nq, int nkv, float eps, int width, int rot) {
+                                __half* __restrict__ v_scale, int T, int nq, int nkv, float eps, int width, int rot,
+                                const PartialIn pin) {
   constexpr int E = HD / 32;
   pdl_wait();
   pdl_trigger();
@@ -201,9 +208,10 @@ __global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __n
   const int t = warp / nslots, h = warp % nslots;
   const __nv_bfloat16* src = qkv + (size_t)t * width + h * HD + lane * E;
   float x[E];
+  if (pin.part) partial_sum<E>(pin, t, h * HD + lane * E, x);
 #pragma unroll
   for (int i = 0; i < E; ++i) {
-    x[i] = __bfloat162float(src[i]);
+    if (!pin.part) x[i] = __bfloat162float(src[i]);
     if (bias) x[i] = __bfloat162float(__float2bfloat16_rn(x[i] + __bfloat162float(bias[h * HD + lane * E + i])));
   }
   const bool is_q = h < nq, is_k = !is_q && h < nq + nkv;
@@ -326,7 +334,8 @@ using namespace b200;
 
 void rmsnorm_fused_impl(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
                         c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps,
-                        const int* wait_flags, const int* epoch, int* err, const AgArgs& ag, int lamport = 0) {
+                        const int* wait_flags, const int* epoch, int* err, const AgArgs& ag, int lamport = 0,
+                        const PartialIn& pin = PartialIn{}) {
   TORCH_CHECK(!parts.empty() && parts.size() <= 8, "1..8 partial inputs");
   const int H = parts[0].size(-1);
   const int T = parts[0].numel() / H;
@@ -345,10 +354,10 @@ void rmsnorm_fused_impl(std::vector<torch::Tensor> parts, c10::optional<torch::T
   auto wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   switch (vpt) {
-    case 1: launch_pdl(rmsnorm_fused_kernel<1>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport); break;
-    case 2: launch_pdl(rmsnorm_fused_kernel<2>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport); break;
+    case 1: launch_pdl(rmsnorm_fused_kernel<1>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport, pin); break;
+    case 2: launch_pdl(rmsnorm_fused_kernel<2>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport, pin); break;
     case 3:
-    case 4: launch_pdl(rmsnorm_fused_kernel<4>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport); break;
+    case 4: launch_pdl(rmsnorm_fused_kernel<4>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport, pin); break;
     default: TORCH_CHECK(false, "hidden size too large");
   }
   B200_CHECK_CUDA(cudaGetLastError());
@@ -366,6 +375,16 @@ void rmsnorm_fused_wait(std::vector<torch::Tensor> parts, c10::optional<torch::T
                         int64_t flags_ptr, int64_t epoch_ptr, int64_t err_ptr) {
   rmsnorm_fused_impl(parts, residual_in, residual_out, w, out, eps, reinterpret_cast<const int*>(flags_ptr),
                      reinterpret_cast<const int*>(epoch_ptr), reinterpret_cast<int*>(err_ptr), AgArgs{});
+}
+
+// out = RMSNorm(sum of a stream-K GEMM's fp32 partials + residual) * w (see PartialIn);
+// `like` is a bf16 [T, H] tensor that gives the row geometry (its data is not read).
+void rmsnorm_partial(torch::Tensor like, torch::Tensor part, int64_t kb, int64_t ctas, int64_t total,
+                     c10::optional<torch::Tensor> residual_in, c10::optional<torch::Tensor> residual_out,
+                     torch::Tensor w, torch::Tensor out, double eps) {
+  TORCH_CHECK(part.scalar_type() == at::kFloat && part.is_contiguous(), "partials: contiguous fp32");
+  PartialIn pin{part.data_ptr<float>(), (int)kb, (int)ctas, (long long)total, (int)like.size(0), (int)like.size(1)};
+  rmsnorm_fused_impl({like}, residual_in, residual_out, w, out, eps, nullptr, nullptr, nullptr, AgArgs{}, 0, pin);
 }
 
 // Consumer of a flag-free all-reduce site: parts are this rank's receive slots (one per source
@@ -407,7 +426,8 @@ void rmsnorm_rs_ag(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor
 void qkv_post_impl(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
                    c10::optional<torch::Tensor> kn_w, torch::Tensor cos_sin, torch::Tensor positions,
                    torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache,
-                   __half* k_scale, __half* v_scale, int64_t nq, int64_t nkv, double eps, int kvq) {
+                   __half* k_scale, __half* v_scale, int64_t nq, int64_t nkv, double eps, int kvq,
+                   const PartialIn& pin = PartialIn{}) {
   const int T = qkv.size(0);
   const int HD = q_out.size(2), rot = cos_sin.size(1);
   const int width = (int)qkv.stride(0);
@@ -428,7 +448,7 @@ void qkv_post_impl(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::op
       qn_w ? reinterpret_cast<const __nv_bfloat16*>(qn_w->data_ptr()) : nullptr,                            \
       kn_w ? reinterpret_cast<const __nv_bfloat16*>(kn_w->data_ptr()) : nullptr, cos_sin.data_ptr<float>(), \
       positions.data_ptr<int>(), slots.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), \
-      k_cache.data_ptr(), v_cache.data_ptr(), k_scale, v_scale, T, (int)nq, (int)nkv, (float)eps, width, rot)
+      k_cache.data_ptr(), v_cache.data_ptr(), k_scale, v_scale, T, (int)nq, (int)nkv, (float)eps, width, rot, pin)
   if (HD == 128) { if (kvq) B200_QKV((qkv_post_kernel<128, 1>)); else B200_QKV((qkv_post_kernel<128, 0>)); }
   else if (HD == 64 && !kvq) B200_QKV((qkv_post_kernel<64, 0>));
   else if (HD == 256 && !kvq) B200_QKV((qkv_post_kernel<256, 0>));
@@ -443,6 +463,23 @@ void qkv_post(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optiona
               int64_t nkv, double eps) {
   qkv_post_impl(qkv, bias, qn_w, kn_w, cos_sin, positions, slots, q_out, k_cache, v_cache, nullptr, nullptr, nq, nkv,
                 eps, 0);
+}
+
+// qkv_post whose input rows are the fp32 stream-K partials of the QKV GEMM (see PartialIn);
+// `like` [T, width] bf16 only gives the geometry. Scales given: int4g128 KV cache.
+void qkv_post_partial(torch::Tensor like, torch::Tensor part, int64_t kb, int64_t ctas, int64_t total,
+                      c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
+                      c10::optional<torch::Tensor> kn_w, torch::Tensor cos_sin, torch::Tensor positions,
+                      torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache,
+                      c10::optional<torch::Tensor> k_scale, c10::optional<torch::Tensor> v_scale, int64_t nq,
+                      int64_t nkv, double eps) {
+  TORCH_CHECK(part.scalar_type() == at::kFloat && part.is_contiguous(), "partials: contiguous fp32");
+  TORCH_CHECK(like.stride(0) == like.size(1), "partials have the row stride of a dense [T, width] output");
+  PartialIn pin{part.data_ptr<float>(), (int)kb, (int)ctas, (long long)total, (int)like.size(0), (int)like.size(1)};
+  const bool q4 = k_scale.has_value();
+  qkv_post_impl(like, bias, qn_w, kn_w, cos_sin, positions, slots, q_out, k_cache, v_cache,
+                q4 ? reinterpret_cast<__half*>(k_scale->data_ptr()) : nullptr,
+                q4 ? reinterpret_cast<__half*>(v_scale->data_ptr()) : nullptr, nq, nkv, eps, q4 ? 1 : 0, pin);
 }
 
 // Same, writing K/V into an int4g128 cache (codes + fp16 scales).

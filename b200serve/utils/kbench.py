@@ -372,6 +372,35 @@ def decode_parts(layers=8, B=32, ctx=2304, tp=1):
             ops.linear(x, lw.gate_up, epilogue=ops.EPI_SWIGLU)
             ops.linear(act, lw.down)
 
+    def gemms_partial():
+        # the decode path on one rank: QKV, o_proj and down as stream-K partials, each summed by
+        # its consumer kernel (qkv_post, RMSNorm), gate_up with its SwiGLU epilogue
+        for i, lw in enumerate(w.layers):
+            pp = ops.linear_partial(x, lw.qkv)
+            ops.qkv_post_partial(pp, None, lw.q_norm, lw.k_norm, dec.cos_sin, fb.positions, fb.slots, kv.k[i],
+                                 kv.v[i], nq, nkv, cfg.rms_eps, hd)
+            ops.rmsnorm(ops.linear_partial(a, lw.o), lw.post_norm, cfg.rms_eps, residual=res, residual_out=res)
+            ops.linear(x, lw.gate_up, epilogue=ops.EPI_SWIGLU)
+            ops.rmsnorm(ops.linear_partial(act, lw.down), lw.input_norm, cfg.rms_eps, residual=res,
+                        residual_out=res)
+
+    def gemms_dense():
+        # the same chain with the split-K fixup inside each GEMM
+        for i, lw in enumerate(w.layers):
+            ops.qkv_post(ops.linear(x, lw.qkv), None, lw.q_norm, lw.k_norm, dec.cos_sin, fb.positions, fb.slots,
+                         kv.k[i], kv.v[i], nq, nkv, cfg.rms_eps)
+            ops.rmsnorm([ops.linear(a, lw.o)], lw.post_norm, cfg.rms_eps, residual=res, residual_out=res)
+            ops.linear(x, lw.gate_up, epilogue=ops.EPI_SWIGLU)
+            ops.rmsnorm([ops.linear(act, lw.down)], lw.input_norm, cfg.rms_eps, residual=res, residual_out=res)
+
+    def full_dense():
+        prev = ops._PARTIAL
+        ops._PARTIAL = False
+        try:
+            dec.forward(fb, attn_plan=plan)
+        finally:
+            ops._PARTIAL = prev
+
     def attn():
         for i in range(layers):
             ops.paged_decode_attention(q, kv.k[i], kv.v[i], tables, fb.seq_lens, dec.scale, plan[0], plan[1], ws)
@@ -385,9 +414,12 @@ def decode_parts(layers=8, B=32, ctx=2304, tp=1):
 
     wbytes = sum(t.N * t.K * 2 for lw in w.layers for t in (lw.qkv, lw.o, lw.gate_up, lw.down)) / layers
     kvbytes = B * (ctx + 1) * nkv * hd * 2 * 2
-    ideal = {"full": (wbytes + kvbytes) / hbm / 1e3, "gemms": wbytes / hbm / 1e3, "attn": kvbytes / hbm / 1e3}
+    ideal = {"full": (wbytes + kvbytes) / hbm / 1e3, "full_dense": (wbytes + kvbytes) / hbm / 1e3,
+             "gemms": wbytes / hbm / 1e3, "gemms_partial": wbytes / hbm / 1e3, "gemms_dense": wbytes / hbm / 1e3,
+             "attn": kvbytes / hbm / 1e3}
     out = {"case": "decode_parts", "layers": layers, "B": B, "ctx": ctx, "tp": tp, "peaks": src}
-    for name, fn in (("full", full), ("gemms", gemms), ("attn", attn), ("small", small)):
+    for name, fn in (("full", full), ("full_dense", full_dense), ("gemms", gemms), ("gemms_partial", gemms_partial),
+                     ("gemms_dense", gemms_dense), ("attn", attn), ("small", small)):
         for _ in range(2):
             fn()
         torch.cuda.synchronize()

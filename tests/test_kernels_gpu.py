@@ -444,3 +444,45 @@ def test_int4g128_kv_write_and_attention():
     refp = ops.paged_prefill_attention(q.cpu(), kd.cpu(), vd.cpu(), bt.cpu(), lens.cpu(), q0.cpu(), cu.cpu(),
                                        1 / math.sqrt(hd))
     assert _rel(outp.cpu(), refp) < 2e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (7, 768, 512), (32, 4096, 12288), (32, 4096, 4096),
+                                   (64, 6144, 4096), (16, 200, 1024), (3, 128, 64)])
+def test_stream_k_partial_gemm_into_rmsnorm(M, N, K):
+    """Stream-K GEMM whose fp32 partial sums the RMSNorm adds up (decode o_proj / down) vs an
+    fp32 reference of GEMM + residual add + RMSNorm; the pre-norm sum equals the dense GEMM's."""
+    x = torch.randn(M, K, device=dev).bfloat16()
+    w = ops.pack_weight((torch.randn(N, K, device=dev) * 0.03).bfloat16())
+    res = torch.randn(M, N, device=dev).bfloat16()
+    nw = (torch.rand(N, device=dev) + 0.5).bfloat16()
+    pp = ops.linear_partial(x, w)
+    assert isinstance(pp, ops.PartialParts)
+    kb, ctas, total = pp.plan
+    assert ctas <= 148 and total == ((N + 127) // 128) * ((K + 63) // 64)
+    res_out = torch.empty_like(res)
+    y = ops.rmsnorm(pp, nw, 1e-6, residual=res, residual_out=res_out)
+    # fp32 reference: matmul on the unpacked weight, residual add, RMSNorm
+    yd = x.float() @ w.unpacked().float().t() + res.float()
+    ref = yd * torch.rsqrt(yd.pow(2).mean(-1, keepdim=True) + 1e-6) * nw.float()
+    assert _rel(res_out, yd) < 1e-2
+    assert _rel(y, ref) < 1e-2
+    assert ops.gemm_error_flag() == 0
+
+
+def test_stream_k_partial_qkv_post_matches_dense():
+    T, H, nq, nkv, hd, nb = 32, 2048, 16, 4, 128, 16
+    x = torch.randn(T, H, device=dev).bfloat16()
+    w = ops.pack_weight((torch.randn((nq + 2 * nkv) * hd, H, device=dev) * 0.03).bfloat16())
+    b = torch.randn((nq + 2 * nkv) * hd, device=dev).bfloat16()
+    qn, kn = torch.randn(hd, device=dev).bfloat16(), torch.randn(hd, device=dev).bfloat16()
+    cs = ops.rope_cos_sin(hd, 4096, 1e6, dev)
+    pos = torch.randint(0, 4000, (T,), device=dev, dtype=torch.int32)
+    slots = torch.randperm(nb * 16, device=dev)[:T].int()
+    kc = torch.zeros(nb, nkv, 16, hd, device=dev).bfloat16()
+    vc = torch.zeros_like(kc)
+    kc2, vc2 = kc.clone(), vc.clone()
+    pp = ops.linear_partial(x, w)
+    q = ops.qkv_post_partial(pp, b, qn, kn, cs, pos, slots, kc, vc, nq, nkv, 1e-6, hd)
+    q2 = ops.qkv_post(ops.linear(x, w, bias=b), None, qn, kn, cs, pos, slots, kc2, vc2, nq, nkv, 1e-6)
+    assert _rel(q, q2) < 1e-2 and _rel(kc, kc2) < 1e-2 and _rel(vc, vc2) < 1e-2
+    assert ops.gemm_error_flag() == 0
