@@ -167,6 +167,9 @@ BUILTIN = {
     "qwen3-8b": ModelConfig("qwen3-8b", 151936, 4096, 36, 32, 8, 128, 12288, qk_norm=True),
     "qwen3-30b-a3b": ModelConfig("qwen3-30b-a3b", 151936, 2048, 48, 32, 4, 128, 6144, qk_norm=True,
                                  num_experts=128, experts_per_tok=8, moe_intermediate_size=768),
+    # CPU-sized MoE for tests: 16 experts, top-4 (expert-parallel paths on gloo / 2 GPUs)
+    "tiny-qwen3-moe": ModelConfig("tiny-qwen3-moe", 32000, 256, 2, 4, 2, 64, 512, qk_norm=True,
+                                  num_experts=16, experts_per_tok=4, moe_intermediate_size=128),
     # CPU-sized hybrid for tests: 3 Gated DeltaNet layers + 1 gated attention layer
     "tiny-qwen35": ModelConfig("tiny-qwen35", 32000, 256, 4, 4, 2, 64, 512, rope_theta=1e4, qk_norm=True,
                                max_position=4096, rotary_dim=16,

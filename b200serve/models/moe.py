@@ -136,6 +136,41 @@ class MoEBlock:
             parts = comm.reduce_parts(out, "mlp") if comm is not None else [out]
         return parts
 
+    def route(self, layer: int, x: torch.Tensor):
+        """Router GEMM + top-k softmax of rows ``x``: (weights [T, k] fp32, expert ids [T, k] int32)."""
+        lw = self.w.layers[layer]
+        logits = ops.linear(x, lw.router, epilogue=ops.EPI_F32)
+        return topk_softmax(logits, self.cfg.experts_per_tok, self.cfg.norm_topk_prob)
+
+    def pair_outputs(self, layer: int, x: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor) -> torch.Tensor:
+        """[T, k, H]: row (t, j) = wts[t, j] * expert_{ids[t, j]}(x[t]) for the pairs whose expert
+        is on this rank, zeros for the others (each pair is computed by exactly one rank)."""
+        lw = self.w.layers[layer]
+        T, k = ids.shape
+        out = torch.zeros(T, k, x.shape[1], dtype=x.dtype, device=x.device)
+        loc = ids.long() - self.e0
+        for e in range(self.per):
+            t_idx, j_idx = torch.nonzero(loc == e, as_tuple=True)
+            if t_idx.numel() == 0:
+                continue
+            xe = x.index_select(0, t_idx)
+            if x.is_cuda:
+                gu, n_gu, dn, n_dn = self.packed[layer]
+                we_gu = ops.PackedWeight.from_packed(gu.view(self.per, -1, 64)[e], n_gu, x.shape[1])
+                we_dn = ops.PackedWeight.from_packed(dn.view(self.per, -1, 64)[e], n_dn, n_gu // 2)
+                ye = ops.linear(ops.linear(xe, we_gu, epilogue=ops.EPI_SWIGLU), we_dn)
+            else:
+                ye = ops.linear(ops.linear(xe, lw.experts_gate_up[e], epilogue=ops.EPI_SWIGLU), lw.experts_down[e])
+            out[t_idx, j_idx] = (ye.float() * wts[t_idx, j_idx, None]).to(x.dtype)
+        return out
+
+    def a2a(self, layer: int, x_own: torch.Tensor, T: int):
+        """Expert FFN of this rank's token shard (``T`` tokens in the whole step) through the
+        communicator's all-to-all dispatch and combine; returns the parts the owner's next norm
+        sums."""
+        wts, ids = self.route(layer, x_own)
+        return self.comm.ep_moe(self, layer, x_own, ids, wts, T)
+
     def shared(self, layer: int, x: torch.Tensor):
         """The sigmoid-gated shared expert's output (Qwen2-MoE), or None. Its weights are
         replicated, so every rank computes the same full output and adds it to its own copy

@@ -328,6 +328,54 @@ class Decoder:
                          self.nq, self.nkv, eps, hd=self.hd)
         return self._attn_core(i, q, fb, plan)
 
+    def _use_ep_a2a(self, T: int) -> bool:
+        """Token-sharded expert parallelism (all-to-all) for this step? B200_EP_MODE = a2a (always),
+        replicated (never) or auto: steps larger than the fused communicator's decode size."""
+        import os
+        comm, cfg = self.comm, self.cfg
+        if comm.world == 1 or not hasattr(comm, "ep_moe") or cfg.is_hybrid or cfg.sandwich_norms:
+            return False
+        mode = os.environ.get("B200_EP_MODE", "auto")
+        if mode == "a2a":
+            return True
+        if mode == "replicated":
+            return False
+        return T > getattr(comm, "max_tokens", 64)
+
+    def _forward_ep(self, fb, h, plan, tq_pre):
+        """MoE forward on a token-sharded residual stream: attention as in the tensor-parallel
+        forward (o_proj reduce-scattered to the token owners, the input norm all-gathered), and
+        the expert FFN as an all-to-all: each owner routes its rows, every (token, expert) pair
+        goes to the rank holding the expert, and the weighted expert outputs come back to the
+        owner, whose next norm sums the k pair rows (MoEBlock.a2a, comm.ep_moe)."""
+        cfg, w, comm = self.cfg, self.w, self.comm
+        eps = cfg.rms_eps
+        T = h.shape[0]
+        Tw, row0, cnt = comm.shard(T)
+        residual = torch.zeros(Tw, h.shape[1], dtype=h.dtype, device=h.device)
+        residual[:cnt] = h[row0:row0 + cnt]
+        x, ag = ops.rmsnorm([h], w.layers[0].input_norm, eps), None
+        parts = None
+        for i, lw in enumerate(w.layers):
+            if i > 0:
+                x, ag = comm.norm_ag(parts, lw.input_norm, eps, residual)
+            attn = self._qkv_attend(i, x, lw, fb, T, plan, tq_pre, ag)
+            parts = comm.rs_linear(attn.view(T, self.nq * self.hd), lw.o, "o")
+            x_own = ops.rmsnorm(parts, lw.post_norm, eps, residual=residual, residual_out=residual)
+            sh = self.moe.shared(i, x_own)
+            if sh is not None:
+                residual.add_(sh)
+            parts = self.moe.a2a(i, x_own, T)
+        x, ag = comm.norm_ag(parts, w.final_norm, eps, residual)
+        rows = fb.logit_rows
+        if rows is not None or fb.hidden:
+            if ag is not None:
+                ag.wait()
+            x, ag = (x.index_select(0, rows) if rows is not None else x), None
+        if fb.hidden:
+            return x
+        return ops.linear(x, w.lm_head, epilogue=ops.EPI_F32, ag=ag)
+
     def _forward_rsag(self, fb, h, plan, tq_pre):
         """Tensor-parallel forward on a token-sharded residual stream (sequence parallelism for
         the norms): each row-parallel GEMM reduce-scatters its output to the token owners
@@ -390,6 +438,8 @@ class Decoder:
         quant_kv = self.tq is not None or (self.kv.kv_format == "int4g128" and h.is_cuda and ops._TC_PREFILL)
         tq_pre = self._tq_prefill_pages(fb) if (quant_kv and not fb.is_decode) else None
         plan = (tps, nsplit, ws) if fb.is_decode else (0, 0, None)
+        if self.moe is not None and self._use_ep_a2a(T):
+            return self._forward_ep(fb, h, plan, tq_pre)
         if self.moe is None and not cfg.is_hybrid and not cfg.sandwich_norms and cfg.act == "silu" and \
                 comm.world > 1 and hasattr(comm, "use_rsag") and comm.use_rsag(T):
             return self._forward_rsag(fb, h, plan, tq_pre)

@@ -432,10 +432,47 @@ def _partial_buffer(device, floats: int = 4 << 20):
     return bufs[0][bufs[1]]
 
 
+_NO_PUSH = torch.zeros(0, dtype=torch.int64)
+_dequant_scratch = {}
+
+
+def _quant_parts(w):
+    parts = list(w) if isinstance(w, list) else [w]
+    return parts if parts and all(isinstance(p, QuantWeight) for p in parts) else None
+
+
+def qlinear_partial(x, w):
+    """GGUF projection(s) for a decode batch (1..16 rows) as fp32 partial sums: every part of a
+    QuantGroup writes its columns of one [S][M][sum N] slot set (gguf_gemv, K split S), which the
+    consuming row kernel sums (S slots per 128-column tile). None when the path does not apply."""
+    parts = _quant_parts(w)
+    M = x.shape[0]
+    if parts is None or not (x.is_cuda and 1 <= M <= 16) or len({p.K for p in parts}) != 1:
+        return None
+    if any(p.K % 256 or p.N % 16 for p in parts):
+        return None
+    ntot, K = sum(p.N for p in parts), parts[0].K
+    S = min(ext().gguf_gemv_splits(p.N, K) for p in parts)
+    buf = _partial_buffer(x.device)
+    if S * M * ntot > buf.numel():
+        return None
+    xc = x if (x.stride(1) == 1 and x.stride(0) % 8 == 0) else x.contiguous()
+    col = 0
+    for p in parts:
+        _cuda(x)
+        ext().gguf_gemv(xc, p.codes, p.meta, p.N, p.bits, p.group, 2, S, buf, ntot, col, _NO_PUSH, 0)
+        col += p.N
+    tiles = (ntot + 127) // 128
+    like = buf.view(torch.bfloat16)[: M * ntot].view(M, ntot)
+    return PartialParts(like, buf, (S, S * tiles, S * tiles))
+
+
 def linear_partial(x, w):
-    """x @ w^T for a decode batch (1..64 rows) as stream-K partial sums (PartialParts), or None
-    when this path does not apply (CPU, plain weight, larger batch, disabled by
-    B200_GEMM_PARTIAL=0, or a partial set larger than the buffer)."""
+    """x @ w^T for a decode batch (1..64 rows; GGUF weights 1..16) as stream-K partial sums
+    (PartialParts), or None when this path does not apply (CPU, plain weight, larger batch,
+    disabled by B200_GEMM_PARTIAL=0, or a partial set larger than the buffer)."""
+    if _PARTIAL and _quant_parts(w) is not None:
+        return qlinear_partial(x, w)
     if not (_PARTIAL and x.is_cuda and isinstance(w, PackedWeight) and 1 <= x.shape[0] <= 64):
         return None
     M, K = x.shape
@@ -501,6 +538,14 @@ class PackedWeight:
         self.dtype = w.dtype
         self.device = w.device
 
+    @classmethod
+    def from_packed(cls, data: torch.Tensor, N: int, K: int) -> "PackedWeight":
+        """Wrap data already in the tile-packed layout (no copy)."""
+        self = cls.__new__(cls)
+        self.N, self.K, self.data = N, K, data
+        self.shape, self.dtype, self.device = (N, K), data.dtype, data.device
+        return self
+
     def unpacked(self) -> torch.Tensor:
         Np, Kp = (self.N + 127) // 128 * 128, (self.K + 63) // 64 * 64
         return self.data.view(Np // 128, Kp // 64, 128, 64).permute(0, 2, 1, 3).reshape(Np, Kp)[:self.N, :self.K]
@@ -528,6 +573,20 @@ class QuantWeight:
 
     def element_size(self):
         return 4
+
+    def dequantize_packed(self) -> "PackedWeight":
+        """bf16 tile-packed copy for the tcgen05 GEMM (prefill-sized batches), written by a CUDA
+        kernel into a per-device scratch buffer that the next call reuses: consume it before
+        dequantising another weight on the same stream."""
+        key = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        need = self.N * self.K
+        buf = _dequant_scratch.get(key)
+        if buf is None or buf.numel() < need:
+            buf = torch.empty(need, dtype=torch.bfloat16, device=self.device)
+            _dequant_scratch[key] = buf
+        _cuda(self.codes)
+        ext().gguf_dequant_packed(self.codes, self.meta, self.N, self.K, self.bits, self.group, buf)
+        return PackedWeight.from_packed(buf[:need].view(-1, 64), self.N, self.K)
 
     def dequantize(self) -> torch.Tensor:
         """bf16 [N, K] (used for prefill-sized batches and tests)."""
@@ -615,6 +674,14 @@ def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspac
                          ag.epoch_ptr)
         return out
     if isinstance(w, list):                         # QuantGroup: parts share the input
+        if epilogue == EPI_SWIGLU and x.is_cuda and len(w) == 2 and w[0].N == w[1].N:
+            pp = qlinear_partial(x, w)             # gate | up as partials, SwiGLU while summing
+            if pp is not None:
+                I = w[0].N
+                out = out if out is not None else torch.empty(M, I, dtype=x.dtype, device=x.device)
+                _cuda(x)
+                ext().silu_mul_partial(pp.part, pp.plan[0], M, I, out)
+                return out
         if epilogue == EPI_SWIGLU:
             g, u = (linear(x, p) for p in w)
             return silu_mul(_interleave64(g, u), out=out)
@@ -631,6 +698,19 @@ def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspac
     N = w.shape[0]
     packed_n = 0
     if isinstance(w, QuantWeight):
+        if (x.is_cuda and M <= 16 and epilogue in (EPI_BF16, EPI_F32) and bias is None and residual is None
+                and w.K % 256 == 0 and w.N % 16 == 0):
+            f32 = epilogue == EPI_F32
+            y = out if (out is not None and out.is_contiguous() and
+                        out.dtype == (torch.float32 if f32 else x.dtype)) else \
+                torch.empty(M, w.N, dtype=torch.float32 if f32 else x.dtype, device=x.device)
+            _cuda(x)
+            ext().gguf_gemv(x if x.stride(1) == 1 and x.stride(0) % 8 == 0 else x.contiguous(), w.codes, w.meta,
+                            w.N, w.bits, w.group, 1 if f32 else 0, 1, y, w.N, 0, _NO_PUSH, 0)
+            if out is not None and y is not out:
+                out.copy_(y)
+                return out
+            return y
         if x.is_cuda and M <= 32 and epilogue in (EPI_BF16, EPI_F32) and bias is None and residual is None:
             y = torch.empty(M, N, dtype=x.dtype, device=x.device)
             _cuda(x)
@@ -641,9 +721,12 @@ def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspac
                 out.copy_(y)
                 return out
             return y
-        w = w.dequantize() if x.is_cuda else w.dequantize().cpu()
-        if x.is_cuda:
-            w = PackedWeight(w)
+        if x.is_cuda and w.N % 128 == 0 and w.K % 256 == 0:
+            w = w.dequantize_packed()                  # CUDA kernel into a reused scratch buffer
+        else:
+            w = w.dequantize() if x.is_cuda else w.dequantize().cpu()
+            if x.is_cuda:
+                w = PackedWeight(w)
     if isinstance(w, PackedWeight):
         packed_n = w.N
         if not x.is_cuda:

@@ -20,9 +20,16 @@ void qkv_post_partial(torch::Tensor like, torch::Tensor part, int64_t kb, int64_
                       torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache,
                       c10::optional<torch::Tensor> k_scale, c10::optional<torch::Tensor> v_scale, int64_t nq,
                       int64_t nkv, double eps);
+int64_t gguf_gemv_splits(int64_t N, int64_t K);
+void gguf_gemv(torch::Tensor x, torch::Tensor codes, torch::Tensor meta, int64_t N, int64_t bits, int64_t group,
+               int64_t mode, int64_t S, torch::Tensor out, int64_t ldo, int64_t col0, torch::Tensor push_ptrs,
+               int64_t mc_ptr);
+void silu_mul_partial(torch::Tensor part, int64_t S, int64_t M, int64_t I, torch::Tensor out);
+void gguf_dequant_packed(torch::Tensor codes, torch::Tensor meta, int64_t N, int64_t K, int64_t bits, int64_t group,
+                         torch::Tensor out);
 void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, int64_t ldo, torch::Tensor flag_ptrs,
                   int64_t epoch_ptr, torch::Tensor tile_done, c10::optional<torch::Tensor> bias, torch::Tensor ws,
-                  torch::Tensor counters, int64_t err_ptr, int64_t packed_n, int64_t rs_rows, int64_t lamport);
+                  torch::Tensor counters, int64_t err_ptr, int64_t packed_n, int64_t rs_rows, int64_t lamport, int64_t mc_ptr);
 int64_t ipc_malloc(int64_t bytes);
 void ipc_free(int64_t ptr);
 torch::Tensor ipc_handle(int64_t ptr);
@@ -143,8 +150,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qkv_post", &qkv_post);
   m.def("rmsnorm_fused_wait", &rmsnorm_fused_wait);
   m.def("rmsnorm_rs_ag", &rmsnorm_rs_ag);
-  m.def("gemm_tc_push", &gemm_tc_push);
+  m.def("gemm_tc_push", &gemm_tc_push, py::arg("act"), py::arg("w"), py::arg("dst_ptrs"), py::arg("ldo"),
+        py::arg("flag_ptrs"), py::arg("epoch_ptr"), py::arg("tile_done"), py::arg("bias"), py::arg("ws"),
+        py::arg("counters"), py::arg("err_ptr"), py::arg("packed_n"), py::arg("rs_rows"), py::arg("lamport") = 0,
+        py::arg("mc_ptr") = 0);
   m.def("gemm_partial_plan", &gemm_partial_plan);
+  m.def("gguf_gemv_splits", &gguf_gemv_splits);
+  m.def("gguf_gemv", &gguf_gemv);
+  m.def("gguf_dequant_packed", &gguf_dequant_packed);
+  m.def("silu_mul_partial", &silu_mul_partial);
   m.def("gemm_tc_partial", &gemm_tc_partial);
   m.def("rmsnorm_partial", &rmsnorm_partial);
   m.def("qkv_post_partial", &qkv_post_partial);

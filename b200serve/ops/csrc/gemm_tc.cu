@@ -305,7 +305,8 @@ void gemm_tc_qkv(torch::Tensor act, torch::Tensor w, int64_t packed_n, c10::opti
 // whole output is pushed. dst_ptrs/flag_ptrs: int64 [world] device addresses.
 void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, int64_t ldo, torch::Tensor flag_ptrs,
                   int64_t epoch_ptr, torch::Tensor tile_done, c10::optional<torch::Tensor> bias, torch::Tensor ws,
-                  torch::Tensor counters, int64_t err_ptr, int64_t packed_n, int64_t rs_rows, int64_t lamport) {
+                  torch::Tensor counters, int64_t err_ptr, int64_t packed_n, int64_t rs_rows, int64_t lamport,
+                  int64_t mc_ptr) {
   TORCH_CHECK(act.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16);
   const bool packed = packed_n > 0;
   const int M = act.size(0), K = act.size(1), N = packed ? (int)packed_n : w.size(0);
@@ -344,6 +345,9 @@ void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, in
   p.tile_done = tile_done.data_ptr<int>();
   p.rs_rows = (int)rs_rows;
   p.lamport = lamport ? 1 : 0;
+  p.mc_dst = reinterpret_cast<__nv_bfloat16*>(mc_ptr);
+  TORCH_CHECK(!mc_ptr || (lamport && (mc_ptr % 16) == 0 && (ldo % 8) == 0),
+              "multicast push: flag-free mode, 16-byte aligned slot and row stride");
   TORCH_CHECK(!(lamport && rs_rows), "the flag-free push is an all-reduce (rs_rows must be 0)");
   TORCH_CHECK(rs_rows == 0 || (int64_t)rs_rows * world >= M, "reduce-scatter rows do not cover the tokens");
   p.err = err_ptr ? reinterpret_cast<int*>(err_ptr) : gemm_err_word();

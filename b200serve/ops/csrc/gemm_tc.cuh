@@ -85,6 +85,9 @@ struct GemmParams {
   // stores). The kernel lets its dependent launch only after its own prerequisites completed,
   // so a consumer that skips griddepcontrol.wait still runs after everything before this GEMM.
   int lamport;
+  // flag-free push through an NVLink multicast object (NVLS): one multimem.st per 16 bytes reaches
+  // this rank's slot on every GPU of the group (row stride ldo); null = one P2P store per rank
+  __nv_bfloat16* mc_dst;
   // stream-K with partial sums reduced by the consumer (EPI_PARTIAL, m_tiles == 1): CTA c streams the
   // flattened k-blocks [c*sk_total/G, (c+1)*sk_total/G) of the n tiles (sk_total = n_tiles*kb_total,
   // G = gridDim.x), cut at tile boundaries; each piece's fp32 partial goes to
@@ -174,7 +177,11 @@ __device__ __forceinline__ void epilogue_store(const GemmParams& p, float* v, in
       const int t = t0 + tok, col = n_tile * 128 + chunk * 8;
       if (t < t_end && col < p.N) {
         const uint4 val = *reinterpret_cast<const uint4*>(xs + tok * 136 + chunk * 8);
-        if (p.rs_rows > 0) {
+        if (p.mc_dst) {
+          __nv_bfloat16* d = p.mc_dst + (size_t)t * p.ldo + col;
+          asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};"
+                       ::"l"(d), "r"(val.x), "r"(val.y), "r"(val.z), "r"(val.w) : "memory");
+        } else if (p.rs_rows > 0) {
           const int owner = t / p.rs_rows;
           *reinterpret_cast<uint4*>(p.push_dst[owner] + (size_t)(t - owner * p.rs_rows) * p.ldo + col) = val;
         } else {

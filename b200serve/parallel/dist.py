@@ -113,6 +113,27 @@ class NcclComm:
         dist.all_reduce(t, group=self.group)
         return [t]
 
+    # ---- expert parallelism on a token-sharded stream: all-to-all dispatch and combine ----
+    def ep_moe(self, moe, layer: int, x_own: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor, T: int):
+        """Expert FFN of this rank's own rows, experts spread over the ranks (library collectives:
+        the reference the fused NVLink path is checked against). Every (token, expert) pair is
+        computed by the rank owning the expert; its routing-weighted output comes back to the
+        token's owner as pair row (t, j). Returns the k pair rows as parts [k][Tw, H], which the
+        owner's norm sums in j order."""
+        Tw, H = x_own.shape
+        k = ids.shape[1]
+        xs = [torch.empty_like(x_own) for _ in range(self.world)]
+        idl = [torch.empty_like(ids) for _ in range(self.world)]
+        wl = [torch.empty_like(wts) for _ in range(self.world)]
+        dist.all_gather(xs, x_own.contiguous(), group=self.group)
+        dist.all_gather(idl, ids.contiguous(), group=self.group)
+        dist.all_gather(wl, wts.contiguous(), group=self.group)
+        x_all, id_all, w_all = torch.cat(xs), torch.cat(idl), torch.cat(wl)
+        contrib = moe.pair_outputs(layer, x_all, id_all, w_all)          # [world*Tw, k, H], zeros elsewhere
+        dist.all_reduce(contrib, group=self.group)                       # one rank owns each pair
+        mine = contrib[self.rank * Tw:(self.rank + 1) * Tw]
+        return RSParts([mine[:, j].contiguous() for j in range(k)], T)
+
     def all_gather_small(self, t: torch.Tensor) -> torch.Tensor:
         flat = torch.empty(self.world * t.numel(), dtype=t.dtype, device=t.device)
         dist.all_gather_into_tensor(flat, t.contiguous().view(-1), group=self.group)

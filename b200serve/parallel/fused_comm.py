@@ -71,6 +71,27 @@ def _lamport_default() -> bool:
     return os.environ.get("B200_TP_LAMPORT", "1") != "0"
 
 
+def _nvls_default() -> bool:
+    import os
+    return os.environ.get("B200_TP_NVLS", "1") != "0"
+
+
+def _multicast_slots(nbytes: int, device, group):
+    """(tensor, local ptr, multicast ptr) of a symmetric buffer bound to an NVLink multicast object
+    (NVLS through the NVSwitch), or None when the box or the driver offers none."""
+    try:
+        import torch.distributed._symmetric_memory as symm
+        if hasattr(symm, "enable_symm_mem_for_group"):
+            symm.enable_symm_mem_for_group(group.group_name)
+        t = symm.empty(nbytes, dtype=torch.uint8, device=device)
+        h = symm.rendezvous(t, group)
+        if not getattr(h, "has_multicast_support", False) or not h.multicast_ptr:
+            return None
+        return t, h, int(t.data_ptr()), int(h.multicast_ptr)
+    except Exception:  # no symmetric memory / multicast here: the P2P slots serve
+        return None
+
+
 class FusedComm:
     kind = "fused-p2p"
 
@@ -114,6 +135,11 @@ class FusedComm:
         self.tile_done = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.ag_done = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._ag_ptrs = {}
+        # NVLS: the flag-free slots in a symmetric buffer with a multicast mapping, so one
+        # multimem store per 16 bytes reaches every GPU (same layout as the P2P slots)
+        self.mc = _multicast_slots(self.lam_bytes, self.device, group) if (self.world > 1 and _nvls_default()) else None
+        self.use_mc = self.mc is not None
+        self.kind = "fused-nvls" if self.use_mc else "fused-p2p"
         self.reset_lamport()
         self.err = e.host_error_word()       # [host ptr, device ptr]
         self.err_host, self.err_dev = int(self.err[0]), int(self.err[1])
@@ -135,15 +161,22 @@ class FusedComm:
         consumers may not have emptied the slots they were reading)."""
         region = _tensor_from_ptr(self.base + self.lam_off, self.lam_bytes // 2, self.device)
         region.view(torch.int16).fill_(-1)
+        if getattr(self, "mc", None) is not None:
+            self.mc[0].fill_(0xFF)
         torch.cuda.synchronize(self.device)
 
     def _lam_ptr(self, rank_base: int, rot: int, src_rank: int) -> int:
         return rank_base + self.lam_off + (rot * self.world + src_rank) * self.lam_elems * 2
 
+    def _lam_local(self, rot: int, src_rank: int) -> int:
+        if self.use_mc:
+            return self.mc[2] + (rot * self.world + src_rank) * self.lam_elems * 2
+        return self._lam_ptr(self.base, rot, src_rank)
+
     def _lam_views(self, rot: int, T: int):
-        key = ("lam", rot, T)
+        key = ("lam", rot, T, self.use_mc)
         if key not in self._views:
-            self._views[key] = [_tensor_from_ptr(self._lam_ptr(self.base, rot, r), T * self.H, self.device)
+            self._views[key] = [_tensor_from_ptr(self._lam_local(rot, r), T * self.H, self.device)
                                 .view(T, self.H) for r in range(self.world)]
         return self._views[key]
 
@@ -176,8 +209,28 @@ class FusedComm:
     def linear_reduce(self, x: torch.Tensor, w: torch.Tensor, tag: str):
         """Row-parallel GEMM + all-reduce. Returns the parts the next RMSNorm sums."""
         T = x.shape[0]
+        if (isinstance(w, ops.QuantWeight) and self.lamport and T <= 16 and x.is_cuda
+                and w.N == self.H and w.K % 256 == 0):
+            # GGUF row-parallel projection: the warp-task GEMV stores its bf16 tiles straight into
+            # every rank's flag-free slot (P2P or one multicast store)
+            site = self.site
+            self.site += 1
+            assert site < self.n_sites, "more fused sites than allocated"
+            rot = site % 3
+            key = ("lamdst", rot)
+            if key not in self._ptrs:
+                self._ptrs[key] = torch.tensor([self._lam_ptr(self.peer[r], rot, self.rank)
+                                                for r in range(self.world)], dtype=torch.int64)
+            mc = self.mc[3] + (rot * self.world + self.rank) * self.lam_elems * 2 if self.use_mc else 0
+            dst = self._ptrs[key]
+            if self.use_mc:
+                dst = torch.tensor([self._lam_local(rot, self.rank)], dtype=torch.int64)   # unused with mc
+            xc = x if (x.stride(1) == 1 and x.stride(0) % 8 == 0) else x.contiguous()
+            ops._cuda(x)
+            ops.ext().gguf_gemv(xc, w.codes, w.meta, w.N, w.bits, w.group, 4, 1, xc, self.H, 0, dst, mc)
+            return LamportParts(self._lam_views(rot, T), self.err_dev, ops.launch_count())
         if T > self.max_tokens or not isinstance(w, (torch.Tensor, ops.PackedWeight)):
-            # large chunks (NVLS all-reduce is bandwidth-optimal) and quantised weights take NCCL
+            # large chunks (NVLS all-reduce is bandwidth-optimal) and other quantised shapes take NCCL
             y = ops.linear(x, w)
             return self.nccl.reduce_parts(y, tag)
         site = self.site
@@ -192,9 +245,10 @@ class FusedComm:
             if key not in self._ptrs:
                 self._ptrs[key] = torch.tensor([self._lam_ptr(self.peer[r], rot, self.rank)
                                                 for r in range(self.world)], dtype=torch.int64)
+            mc = self.mc[3] + (rot * self.world + self.rank) * self.lam_elems * 2 if self.use_mc else 0
             ops.ext().gemm_tc_push(x, w.data if packed_n else w, self._ptrs[key], self.H, flg,
                                    self.epoch.data_ptr(), self.tile_done, None, self.ws.ws, self.ws.counters,
-                                   self.err_dev, packed_n, 0, 1)
+                                   self.err_dev, packed_n, 0, 1, mc)
             return LamportParts(self._lam_views(rot, T), self.err_dev, ops.launch_count())
         ops.ext().gemm_tc_push(x, w.data if packed_n else w, dst, self.H, flg, self.epoch.data_ptr(), self.tile_done,
                                None, self.ws.ws, self.ws.counters, self.err_dev, packed_n, 0, 0)

@@ -89,15 +89,22 @@ def main():
             res = torch.randn(T, H, device="cuda").bfloat16()
             out = torch.empty(T, H, device="cuda").bfloat16()
 
+            def lamport_nvls():
+                comm.lamport, comm.use_mc = True, comm.mc is not None
+                comm.begin_step()
+                for _ in range(8):
+                    parts = comm.linear_reduce(x, w, "o")
+                    ops.rmsnorm(parts, nw, 1e-6, residual=res, out=out)
+
             def lamport():
-                comm.lamport = True
+                comm.lamport, comm.use_mc = True, False
                 comm.begin_step()
                 for _ in range(8):
                     parts = comm.linear_reduce(x, w, "o")
                     ops.rmsnorm(parts, nw, 1e-6, residual=res, out=out)
 
             def fused():
-                comm.lamport = False
+                comm.lamport, comm.use_mc = False, False
                 comm.begin_step()
                 for _ in range(8):   # 8 sites per replay, as in 4 layers of a decode step
                     parts = comm.linear_reduce(x, w, "o")
@@ -125,8 +132,10 @@ def main():
                     ops.rmsnorm([y], nw, 1e-6, residual=res, out=out)
 
             row = {"site": name, "T": T, "world": world, "K_shard": K}
-            for label, fn in (("lamport", lamport), ("fused", fused), ("rsag", rsag), ("nccl", nccl),
-                              ("local", local)):
+            variants = [("lamport", lamport), ("fused", fused), ("rsag", rsag), ("nccl", nccl), ("local", local)]
+            if comm.mc is not None:
+                variants.insert(0, ("lamport_nvls", lamport_nvls))
+            for label, fn in variants:
                 for _ in range(3):
                     fn()
                 torch.cuda.synchronize()
@@ -155,6 +164,11 @@ def main():
             row["rsag_roofline_us"] = round(max(wbytes / (hbm * 1e3), rs_bytes / (NVLINK_GBPS * 1e3)), 2)
             row["fused_frac_of_roofline"] = round(roof_us / row["fused_us"], 3)
             row["lamport_frac_of_roofline"] = round(roof_us / row["lamport_us"], 3)
+            if "lamport_nvls_us" in row:
+                # NVLS: every tile crosses the sender's NVLink once; the switch fans it out
+                mc_roof = max(wbytes / (hbm * 1e3), T * H * 2 / (NVLINK_GBPS * 1e3))
+                row["nvls_roofline_us"] = round(mc_roof, 2)
+                row["lamport_nvls_frac_of_roofline"] = round(mc_roof / row["lamport_nvls_us"], 3)
             row["speedup_vs_nccl"] = round(row["nccl_us"] / row["fused_us"], 3)
             row["peaks"] = src
             results.append(row)

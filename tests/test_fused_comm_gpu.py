@@ -51,6 +51,7 @@ def _fused_worker(rank, world, port, q):
             res = torch.randn(T, 4096, device="cuda", generator=gs).bfloat16()
             nw = torch.randn(4096, device="cuda", generator=gs).bfloat16()
             comm.lamport = step % 3 != 2          # flag-free slots on most steps, flags on the rest
+            comm.use_mc = comm.mc is not None and step % 2 == 0    # NVLS multicast push when offered
             parts = comm.linear_reduce(x, w, "o")
             if site == 1:                          # another launch between the GEMM and its norm
                 y = ops.linear(x, w)
@@ -70,6 +71,8 @@ def _fused_worker(rank, world, port, q):
     comm.check()
     comm.close()
     q.put((rank, max(errs)))
+    if rank == 0:
+        print("multicast slots:", comm.mc is not None, flush=True)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -181,6 +184,8 @@ def _rsag_worker(rank, world, port, q):
     comm.check()
     comm.close()
     q.put((rank, max(errs)))
+    if rank == 0:
+        print("multicast slots:", comm.mc is not None, flush=True)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -247,6 +252,8 @@ def _moe_combine_worker(rank, world, port, q):
     comm.check()
     comm.close()
     q.put((rank, max(errs)))
+    if rank == 0:
+        print("multicast slots:", comm.mc is not None, flush=True)
     dist.barrier()
     dist.destroy_process_group()
 

@@ -94,3 +94,59 @@ def test_engine_load_time_q4_k_m_quantisation():
             eng.unload()
     rel = ((out["q4_k_m"] - out[""]).norm() / out[""].norm()).item()
     assert rel < 0.35       # 4-bit blocks on random N(0, 0.02) weights; unrelated logits give ~1.4
+
+
+# ---------------------------------------------------------------- warp-task GEMV and packed dequant
+def _quant_pair(N, K, seed=0):
+    """A random weight quantised to Q4_K and Q6_K (as QuantWeights) and its fp32 dequantisation."""
+    import numpy as np
+    from b200serve.models import gguf as G
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    out = {}
+    for t in (G.GGML_Q4_K, G.GGML_Q6_K, G.GGML_Q8_0):
+        raw = np.frombuffer(G.quantize(w, t), dtype=np.uint8)
+        qw = G._repack(raw, t, N, K, "cuda")
+        ref = torch.from_numpy(np.asarray(G.dequantize(raw, t, (N, K)), dtype=np.float32))
+        out[t] = (qw, ref)
+    return out
+
+
+@pytest.mark.parametrize("M", [1, 5, 8, 13, 16])
+def test_gguf_gemv_modes_vs_fp32(M):
+    from b200serve import ops
+    N, K = 384, 1024
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    for qw, ref in _quant_pair(N, K).values():
+        y_ref = x.float().cpu() @ ref.t()
+        y = ops.linear(x, qw)                                       # S = 1, bf16
+        assert ((y.float().cpu() - y_ref).norm() / y_ref.norm()).item() < 1e-2
+        y32 = ops.linear(x, qw, epilogue=ops.EPI_F32)               # S = 1, fp32 (logits)
+        assert y32.dtype == torch.float32 and ((y32.cpu() - y_ref).norm() / y_ref.norm()).item() < 1e-2
+        pp = ops.qlinear_partial(x, qw)                             # K split, summed by the norm
+        nw = torch.ones(N, device="cuda").bfloat16()
+        yn = ops.rmsnorm(pp, nw, 1e-6)
+        r = y_ref * torch.rsqrt(y_ref.pow(2).mean(-1, keepdim=True) + 1e-6)
+        assert ((yn.float().cpu() - r).norm() / r.norm()).item() < 2e-2
+
+
+def test_gguf_group_partial_swiglu_and_packed_dequant():
+    from b200serve import ops
+    from b200serve.models import gguf as G
+    N, K, M = 256, 2048, 8
+    pairs = _quant_pair(N, K, seed=3)
+    g, gref = pairs[G.GGML_Q4_K]
+    u, uref = _quant_pair(N, K, seed=4)[G.GGML_Q4_K]
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    act = ops.linear(x, G.QuantGroup([g, u]), epilogue=ops.EPI_SWIGLU)
+    gf, uf = x.float().cpu() @ gref.t(), x.float().cpu() @ uref.t()
+    ref = torch.nn.functional.silu(gf) * uf
+    assert ((act.float().cpu() - ref).norm() / ref.norm()).item() < 2e-2
+    # prefill-sized batch: CUDA dequantisation into the packed layout + tcgen05 GEMM
+    xb = torch.randn(300, K, device="cuda").bfloat16()
+    for qw, wref in pairs.values():
+        yb = ops.linear(xb, qw)
+        yr = xb.float().cpu() @ wref.t()
+        assert ((yb.float().cpu() - yr).norm() / yr.norm()).item() < 1e-2
+        pw = qw.dequantize_packed()
+        assert torch.equal(pw.unpacked().cpu(), qw.dequantize().cpu())

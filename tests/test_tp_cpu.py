@@ -92,3 +92,54 @@ def test_tp_hybrid_matches_single_rank():
     """Qwen3.5-style hybrid at TP2: DeltaNet key/value heads and the recurrent state are split
     across ranks, and the gated attention layer shards its q, gate and KV heads."""
     assert _run_tp(2, True, model="tiny-qwen35") == _single(True, model="tiny-qwen35")
+
+
+def _ep_worker(rank, world, port, out_q, mode):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), B200_EP_MODE=mode)
+    torch.set_num_threads(1)
+    from b200serve.core.config import EngineConfig
+    from b200serve.engine.b200_engine import B200Engine
+    from b200serve.engine.sampler import SamplingParams
+    from b200serve.parallel.worker import worker_loop
+    cfg = EngineConfig(model="tiny-qwen3-moe", device="cpu", dtype="float32", cuda_graphs=False, max_seq=256,
+                       max_batch=4, tp_size=world, ep_size=world, comm="nccl")
+    eng = B200Engine(cfg)
+    eng.load()
+    if rank == 0:
+        sp = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True)
+        reqs = eng.generate(_prompts(), sp, timeout=300)
+        # logits of one prefill through the same path, for a numeric comparison
+        seqs = [{"ids": _prompts()[1], "start": 0, "block_table": eng.scheduler.alloc.allocate(4)}]
+        logits = eng.runner.prefill(seqs)
+        out_q.put(([r.output for r in reqs], logits.float()))
+        eng.stop_loop()
+    else:
+        worker_loop(eng.runner.inner, eng.comm)
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+
+
+def _run_ep(world, mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, q, mode)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = q.get(timeout=600)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return out
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_expert_parallel_all_to_all_matches_replicated(world):
+    """Token-sharded MoE (all-to-all dispatch and combine on gloo ranks) reproduces the
+    replicated-token expert-parallel forward and the single-rank model."""
+    toks_a2a, lg_a2a = _run_ep(world, "a2a")
+    toks_rep, lg_rep = _run_ep(world, "replicated")
+    assert toks_a2a == toks_rep
+    assert torch.allclose(lg_a2a, lg_rep, atol=1e-4, rtol=1e-4)
+    assert toks_a2a == [t[:8] for t in _single(True, model="tiny-qwen3-moe")]
