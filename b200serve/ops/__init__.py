@@ -105,7 +105,7 @@ def rmsnorm(parts, weight, eps, residual=None, residual_out=None, out=None):
                                   direct)
         elif flags is not None:   # parts pushed by peers: wait for their flags first
             ext().rmsnorm_fused_wait(list(parts), residual, residual_out, weight, out, float(eps), flags,
-                                     parts.epoch_ptr, parts.err_ptr)
+                                     parts.epoch_ptr, parts.err_ptr, getattr(parts, 'n_flags', len(parts)))
         else:
             ext().rmsnorm_fused(list(parts), residual, residual_out, weight, out, float(eps))
         return out

@@ -5,7 +5,7 @@ void rmsnorm_fused(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor
                    c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps);
 void rmsnorm_fused_wait(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
                         c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps,
-                        int64_t flags_ptr, int64_t epoch_ptr, int64_t err_ptr);
+                        int64_t flags_ptr, int64_t epoch_ptr, int64_t err_ptr, int64_t n_flags);
 void rmsnorm_lamport(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
                      c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps,
                      int64_t err_ptr, bool skip_prior_wait);
@@ -27,6 +27,17 @@ void gguf_gemv(torch::Tensor x, torch::Tensor codes, torch::Tensor meta, int64_t
 void silu_mul_partial(torch::Tensor part, int64_t S, int64_t M, int64_t I, torch::Tensor out);
 void gguf_dequant_packed(torch::Tensor codes, torch::Tensor meta, int64_t N, int64_t K, int64_t bits, int64_t group,
                          torch::Tensor out);
+void gemm_grouped_ep(torch::Tensor act, torch::Tensor w_packed, int64_t N, int64_t E, torch::Tensor offsets,
+                     int64_t max_rows, torch::Tensor out, torch::Tensor ws, torch::Tensor counters, int64_t epi,
+                     int64_t ag_flags_ptr, int64_t ag_n, int64_t ag_epoch_ptr, torch::Tensor comb_meta,
+                     int64_t comb_k, int64_t comb_rows, torch::Tensor comb_dst_ptrs, int64_t ldo,
+                     torch::Tensor flag_ptrs, torch::Tensor tile_done, int64_t push_tiles, int64_t err_ptr);
+void ep_count(torch::Tensor ids, int64_t valid, int64_t per, int64_t me, torch::Tensor pos, torch::Tensor cnt_ptrs,
+              torch::Tensor flag_ptrs, int64_t epoch_ptr);
+void ep_dispatch(torch::Tensor x, torch::Tensor ids, torch::Tensor wts, torch::Tensor pos, int64_t valid, int64_t per,
+                 int64_t me, int64_t cnt_all_ptr, int64_t wait_flags_ptr, torch::Tensor cnt_ptrs,
+                 torch::Tensor rows_ptrs, torch::Tensor meta_ptrs, torch::Tensor dflag_ptrs, int64_t epoch_ptr,
+                 torch::Tensor done, int64_t err_ptr);
 void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, int64_t ldo, torch::Tensor flag_ptrs,
                   int64_t epoch_ptr, torch::Tensor tile_done, c10::optional<torch::Tensor> bias, torch::Tensor ws,
                   torch::Tensor counters, int64_t err_ptr, int64_t packed_n, int64_t rs_rows, int64_t lamport, int64_t mc_ptr);
@@ -111,8 +122,9 @@ void gemm_tc_ag(torch::Tensor act, torch::Tensor w, torch::Tensor out, c10::opti
 void rmsnorm_rs_ag(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
                    c10::optional<torch::Tensor> residual_out, torch::Tensor w, double eps, int64_t flags_ptr,
                    int64_t epoch_ptr, int64_t err_ptr, torch::Tensor dst_ptrs, torch::Tensor ag_flag_ptrs,
-                   int64_t row0, int64_t T, torch::Tensor done);
+                   int64_t row0, int64_t T, torch::Tensor done, int64_t n_flags);
 
+void publish_flags(torch::Tensor flag_ptrs, int64_t epoch_ptr);
 void flag_wait(int64_t flags_ptr, int64_t n, int64_t epoch_ptr, int64_t err_ptr, double timeout_ms);
 void set_flag_wait_ms(double ms);
 double get_flag_wait_ms();
@@ -157,6 +169,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_partial_plan", &gemm_partial_plan);
   m.def("gguf_gemv_splits", &gguf_gemv_splits);
   m.def("gguf_gemv", &gguf_gemv);
+  m.def("gemm_grouped_ep", &gemm_grouped_ep);
+  m.def("ep_count", &ep_count);
+  m.def("ep_dispatch", &ep_dispatch);
   m.def("gguf_dequant_packed", &gguf_dequant_packed);
   m.def("silu_mul_partial", &silu_mul_partial);
   m.def("gemm_tc_partial", &gemm_tc_partial);
@@ -174,6 +189,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flag_wait", &flag_wait, py::arg("flags_ptr"), py::arg("n"), py::arg("epoch_ptr"), py::arg("err_ptr"),
         py::arg("timeout_ms") = -1.0);
   m.def("set_flag_wait_ms", &set_flag_wait_ms);
+  m.def("publish_flags", &publish_flags);
   m.def("get_flag_wait_ms", &get_flag_wait_ms);
   m.def("flag_pingpong", &flag_pingpong);
   m.def("silu_mul", &silu_mul);

@@ -22,6 +22,10 @@
 
 namespace b200 {
 
+struct FlagPtrs {
+  int* p[8];
+};
+
 __global__ void epoch_inc_kernel(int* epoch) {
   pdl_wait();
   pdl_trigger();
@@ -50,6 +54,18 @@ __global__ void flag_wait_kernel(const int* flags, int n, const int* epoch, int*
     }
   }
   asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
+// Raise flag[r] = *epoch on every rank (a producer with nothing to send still releases its
+// consumers); one system fence first.
+__global__ void publish_flags_kernel(const FlagPtrs f, int world, const int* epoch) {
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x != 0) return;
+  __threadfence_system();
+  const int e = *epoch;
+  for (int r = 0; r < world; ++r)
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(f.p[r]), "r"(e) : "memory");
 }
 
 // Cross-GPU flag round trip (diagnostics): the initiator stores i into the peer's flag and waits
@@ -125,6 +141,15 @@ void flag_wait(int64_t flags_ptr, int64_t n, int64_t epoch_ptr, int64_t err_ptr,
   launch_pdl(flag_wait_kernel, dim3(1), dim3(32), 0, at::cuda::getCurrentCUDAStream(),
              reinterpret_cast<const int*>(flags_ptr), (int)n, reinterpret_cast<const int*>(epoch_ptr),
              reinterpret_cast<int*>(err_ptr), ns);
+}
+
+void publish_flags(torch::Tensor flag_ptrs, int64_t epoch_ptr) {
+  const int world = flag_ptrs.numel();
+  TORCH_CHECK(world >= 1 && world <= 8 && flag_ptrs.device().is_cpu(), "flag pointers: host int64 [world]");
+  FlagPtrs f{};
+  for (int r = 0; r < world; ++r) f.p[r] = reinterpret_cast<int*>(flag_ptrs.data_ptr<int64_t>()[r]);
+  launch_pdl(publish_flags_kernel, dim3(1), dim3(32), 0, at::cuda::getCurrentCUDAStream(), f, world,
+             reinterpret_cast<const int*>(epoch_ptr));
 }
 
 int64_t ipc_malloc(int64_t bytes) {

@@ -215,6 +215,12 @@ static void gemm_tc_impl(torch::Tensor act, torch::Tensor w, torch::Tensor out, 
     }
   }
   p.units = p.m_tiles * p.n_tiles * p.splits;
+  static int raster = -1;
+  if (raster < 0) {
+    const char* e = getenv("B200_GEMM_RASTER");
+    raster = e ? atoi(e) : 8;
+  }
+  if (p.splits == 1 && p.m_tiles > 1 && raster > 1) p.raster = raster;
   const int grid = p.cluster_red ? p.units : std::min(p.units, g_num_sms);
   p.out = out.data_ptr();
   p.ldo = out.stride(0);
@@ -435,6 +441,73 @@ void gemm_grouped(torch::Tensor act, torch::Tensor w_packed, int64_t N, int64_t 
   p.out = out.data_ptr();
   p.ldo = out.stride(0);
   p.err = gemm_err_word();
+  TORCH_CHECK(w_packed.size(1) == 64 && w_packed.size(0) == E * p.n_tiles * p.kb_total * 128, "bad packed expert weight");
+  CUtensorMap tw = make_tmap_bf16(w_packed.data_ptr(), w_packed.size(0), 64, 64, 128);
+  CUtensorMap ta = make_tmap_bf16(act.data_ptr(), R, K, act.stride(0), BN);
+  const int grid = std::min(p.units, g_num_sms);
+  launch_by_bn(BN, (int)epi, tw, ta, p, grid, at::cuda::getCurrentCUDAStream());
+}
+
+// Grouped expert GEMM of the expert-parallel all-to-all: like gemm_grouped, plus
+//  * ag_flags_ptr/ag_n (0 = none): the activation rows arrive from peers; the producer waits
+//    until those flags hold the step epoch before loading any row;
+//  * comb_meta (empty = none): EPI_PUSH combine epilogue (GemmParams::comb_meta) into the home
+//    ranks' slots comb_dst_ptrs[rank] (row stride ldo), then the site flags flag_ptrs[rank]
+//    raised once all push_tiles tiles are stored.
+void gemm_grouped_ep(torch::Tensor act, torch::Tensor w_packed, int64_t N, int64_t E, torch::Tensor offsets,
+                     int64_t max_rows, torch::Tensor out, torch::Tensor ws, torch::Tensor counters, int64_t epi,
+                     int64_t ag_flags_ptr, int64_t ag_n, int64_t ag_epoch_ptr, torch::Tensor comb_meta,
+                     int64_t comb_k, int64_t comb_rows, torch::Tensor comb_dst_ptrs, int64_t ldo,
+                     torch::Tensor flag_ptrs, torch::Tensor tile_done, int64_t push_tiles, int64_t err_ptr) {
+  TORCH_CHECK(act.scalar_type() == at::kBFloat16 && w_packed.scalar_type() == at::kBFloat16);
+  const bool comb = comb_meta.numel() > 0;
+  TORCH_CHECK(comb ? epi == EPI_PUSH : (epi == EPI_BF16 || epi == EPI_SWIGLU), "bad epilogue for the grouped GEMM");
+  const int R = act.size(0), K = act.size(1);
+  if (R == 0 || E == 0 || max_rows == 0) return;
+  if (g_num_sms == 0) {
+    int dev;
+    B200_CHECK_CUDA(cudaGetDevice(&dev));
+    B200_CHECK_CUDA(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
+  }
+  const int BN = max_rows <= 16 ? 16 : max_rows <= 32 ? 32 : max_rows <= 64 ? 64 : max_rows <= 128 ? 128 : 256;
+  GemmParams p{};
+  p.M = R; p.N = N; p.K = K;
+  p.n_tiles = (N + 127) / 128;
+  p.m_tiles = (max_rows + BN - 1) / BN;
+  p.kb_total = (K + 63) / 64;
+  p.splits = 1;
+  p.kb_per_split = p.kb_total;
+  p.units = E * p.m_tiles * p.n_tiles;
+  p.grouped = 1;
+  p.g_offsets = offsets.data_ptr<int>();
+  p.g_E = E;
+  p.w_packed = 1;
+  p.err = err_ptr ? reinterpret_cast<int*>(err_ptr) : gemm_err_word();
+  p.ag_flags = ag_flags_ptr ? reinterpret_cast<const int*>(ag_flags_ptr) : nullptr;
+  p.ag_n = (int)ag_n;
+  p.ag_epoch = reinterpret_cast<const int*>(ag_epoch_ptr);
+  p.ag_wait_ns = flag_wait_ns();
+  if (comb) {
+    const int world = comb_dst_ptrs.numel();
+    TORCH_CHECK(world >= 1 && world <= kMaxPeers && flag_ptrs.numel() == world && comb_k >= 1 && push_tiles > 0,
+                "combine: pointers, k and tile count");
+    TORCH_CHECK(comb_meta.scalar_type() == at::kInt && comb_meta.numel() >= (int64_t)R * 4, "combine metadata");
+    p.comb_meta = reinterpret_cast<const int4*>(comb_meta.data_ptr<int>());
+    p.comb_k = (int)comb_k;
+    p.comb_rows = (int)comb_rows;
+    p.push_tiles = (int)push_tiles;
+    p.world = world;
+    for (int r = 0; r < world; ++r) {
+      p.push_dst[r] = reinterpret_cast<__nv_bfloat16*>(comb_dst_ptrs.data_ptr<int64_t>()[r]);
+      p.push_flag[r] = reinterpret_cast<int*>(flag_ptrs.data_ptr<int64_t>()[r]);
+    }
+    p.epoch = reinterpret_cast<const int*>(ag_epoch_ptr);
+    p.tile_done = tile_done.data_ptr<int>();
+    p.ldo = (int)ldo;
+  } else {
+    p.out = out.data_ptr();
+    p.ldo = out.stride(0);
+  }
   TORCH_CHECK(w_packed.size(1) == 64 && w_packed.size(0) == E * p.n_tiles * p.kb_total * 128, "bad packed expert weight");
   CUtensorMap tw = make_tmap_bf16(w_packed.data_ptr(), w_packed.size(0), 64, 64, 128);
   CUtensorMap ta = make_tmap_bf16(act.data_ptr(), R, K, act.stride(0), BN);

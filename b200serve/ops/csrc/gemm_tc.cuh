@@ -88,6 +88,12 @@ struct GemmParams {
   // flag-free push through an NVLink multicast object (NVLS): one multimem.st per 16 bytes reaches
   // this rank's slot on every GPU of the group (row stride ldo); null = one P2P store per rank
   __nv_bfloat16* mc_dst;
+  // EPI_PUSH as the expert-parallel combine: output row r carries comb_meta[r] = (home rank,
+  // pair p = t * comb_k + j, routing weight bits); the row is scaled by the weight and stored at
+  // row j * comb_rows + t of the home rank's slot (push_dst[home]). push_tiles: number of tiles
+  // that publish (the grouped GEMM's non-empty tiles); 0 = m_tiles * n_tiles.
+  const int4* comb_meta;
+  int comb_k, comb_rows, push_tiles;
   // stream-K with partial sums reduced by the consumer (EPI_PARTIAL, m_tiles == 1): CTA c streams the
   // flattened k-blocks [c*sk_total/G, (c+1)*sk_total/G) of the n tiles (sk_total = n_tiles*kb_total,
   // G = gridDim.x), cut at tile boundaries; each piece's fp32 partial goes to
@@ -95,6 +101,10 @@ struct GemmParams {
   int streamk;
   long long sk_total;
   float* part;
+  // > 1: raster the (m tile, n tile) grid in bands of `raster` m tiles (prefill): consecutive
+  // units walk down a band for one n tile, so a wave of CTAs shares its activation and weight
+  // tiles in L2 instead of sweeping every weight tile once per m tile
+  int raster;
   // optional per-CTA timeline (globaltimer ns): [cta][8] = entry, setup done, first TMA issued,
   // first stage landed, last MMA committed, epilogue done, exit (thread 0), exit (thread 32)
   unsigned long long* trace;
@@ -162,7 +172,8 @@ __device__ __forceinline__ void epilogue_store(const GemmParams& p, float* v, in
       const float b = (p.bias && col < p.N) ? __bfloat162float(p.bias[col]) : 0.f;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        __nv_bfloat16 h = __float2bfloat16_rn(v[j] + b);
+        const float scale = p.comb_meta ? (t0 + j < t_end ? __int_as_float(p.comb_meta[t0 + j].z) : 0.f) : 1.f;
+        __nv_bfloat16 h = __float2bfloat16_rn((v[j] + b) * scale);
         // 0xFFFF marks an empty receive slot; a NaN with that payload is stored as 0x7FFF
         if (__bfloat16_as_ushort(h) == 0xFFFFu) h = __ushort_as_bfloat16((unsigned short)0x7FFFu);
         xs[j * 136 + row] = h;
@@ -177,7 +188,12 @@ __device__ __forceinline__ void epilogue_store(const GemmParams& p, float* v, in
       const int t = t0 + tok, col = n_tile * 128 + chunk * 8;
       if (t < t_end && col < p.N) {
         const uint4 val = *reinterpret_cast<const uint4*>(xs + tok * 136 + chunk * 8);
-        if (p.mc_dst) {
+        if (p.comb_meta) {
+          const int4 m = p.comb_meta[t];
+          const int home = m.x, pair = m.y;
+          const size_t r = (size_t)(pair % p.comb_k) * p.comb_rows + pair / p.comb_k;
+          *reinterpret_cast<uint4*>(p.push_dst[home] + r * p.ldo + col) = val;
+        } else if (p.mc_dst) {
           __nv_bfloat16* d = p.mc_dst + (size_t)t * p.ldo + col;
           asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};"
                        ::"l"(d), "r"(val.x), "r"(val.y), "r"(val.z), "r"(val.w) : "memory");
@@ -292,7 +308,17 @@ __device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u, int BN) 
   x.tile = u / p.splits;
   x.n_tile = x.tile % p.n_tiles;
   const int rest = x.tile / p.n_tiles;
-  if (!p.grouped) {
+  if (!p.grouped && p.raster > 1) {
+    const int band = p.raster * p.n_tiles;                 // tiles per band of `raster` m tiles
+    const int b = x.tile / band, in = x.tile % band;
+    const int rows = min(p.raster, p.m_tiles - b * p.raster);
+    x.m_tile = b * p.raster + in % rows;
+    x.n_tile = in / rows;
+    x.a_row0 = x.m_tile * BN;
+    x.m_lim = p.M - x.a_row0;
+    x.w_tile_base = x.n_tile;
+    x.empty = false;
+  } else if (!p.grouped) {
     x.m_tile = rest;
     x.a_row0 = x.m_tile * BN;
     x.m_lim = p.M - x.a_row0;
@@ -394,7 +420,7 @@ __device__ __forceinline__ void publish_tile(const GemmParams& p, int* scratch) 
   __threadfence_system();
   epi_bar();
   if (threadIdx.x == 64) {
-    const int total = p.m_tiles * p.n_tiles;
+    const int total = p.push_tiles > 0 ? p.push_tiles : p.m_tiles * p.n_tiles;
     const int old = atomicAdd(p.tile_done, 1);
     if (old == total - 1) {
       *p.tile_done = 0;

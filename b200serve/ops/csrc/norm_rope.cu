@@ -95,14 +95,14 @@ __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
     PartPtrs parts, int nparts, const __nv_bfloat16* residual_in, __nv_bfloat16* residual_out,
     const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H, float eps,
     const int* wait_flags, const int* epoch, int* err, const AgArgs ag, uint64_t wait_ns, int lamport,
-    const PartialIn pin) {
+    const PartialIn pin, int nflags) {
   __shared__ float red[32];
   // lamport == 2: the partials come from a flag-free push GEMM launched right before this kernel,
   // which let it start only after that GEMM's own prerequisites completed; the partials are
   // polled, so the wait for the GEMM's grid to drain is skipped
   if (lamport != 2) pdl_wait();
   pdl_trigger();
-  if (wait_flags) wait_peer_flags(wait_flags, epoch, nparts, err, wait_ns);
+  if (wait_flags) wait_peer_flags(wait_flags, epoch, nflags, err, wait_ns);
   bool gave_up = false;
   const int row = blockIdx.x;
   const size_t base = (size_t)row * H;
@@ -335,7 +335,7 @@ using namespace b200;
 void rmsnorm_fused_impl(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
                         c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps,
                         const int* wait_flags, const int* epoch, int* err, const AgArgs& ag, int lamport = 0,
-                        const PartialIn& pin = PartialIn{}) {
+                        const PartialIn& pin = PartialIn{}, int nflags = -1) {
   TORCH_CHECK(!parts.empty() && parts.size() <= 8, "1..8 partial inputs");
   const int H = parts[0].size(-1);
   const int T = parts[0].numel() / H;
@@ -354,10 +354,10 @@ void rmsnorm_fused_impl(std::vector<torch::Tensor> parts, c10::optional<torch::T
   auto wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   switch (vpt) {
-    case 1: launch_pdl(rmsnorm_fused_kernel<1>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport, pin); break;
-    case 2: launch_pdl(rmsnorm_fused_kernel<2>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport, pin); break;
+    case 1: launch_pdl(rmsnorm_fused_kernel<1>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport, pin, nflags < 0 ? (int)parts.size() : nflags); break;
+    case 2: launch_pdl(rmsnorm_fused_kernel<2>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport, pin, nflags < 0 ? (int)parts.size() : nflags); break;
     case 3:
-    case 4: launch_pdl(rmsnorm_fused_kernel<4>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport, pin); break;
+    case 4: launch_pdl(rmsnorm_fused_kernel<4>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport, pin, nflags < 0 ? (int)parts.size() : nflags); break;
     default: TORCH_CHECK(false, "hidden size too large");
   }
   B200_CHECK_CUDA(cudaGetLastError());
@@ -372,9 +372,10 @@ void rmsnorm_fused(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor
 // (flags_ptr: this rank's [world] flag words of the site; one per part).
 void rmsnorm_fused_wait(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
                         c10::optional<torch::Tensor> residual_out, torch::Tensor w, torch::Tensor out, double eps,
-                        int64_t flags_ptr, int64_t epoch_ptr, int64_t err_ptr) {
+                        int64_t flags_ptr, int64_t epoch_ptr, int64_t err_ptr, int64_t n_flags) {
   rmsnorm_fused_impl(parts, residual_in, residual_out, w, out, eps, reinterpret_cast<const int*>(flags_ptr),
-                     reinterpret_cast<const int*>(epoch_ptr), reinterpret_cast<int*>(err_ptr), AgArgs{});
+                     reinterpret_cast<const int*>(epoch_ptr), reinterpret_cast<int*>(err_ptr), AgArgs{}, 0,
+                     PartialIn{}, (int)n_flags);
 }
 
 // out = RMSNorm(sum of a stream-K GEMM's fp32 partials + residual) * w (see PartialIn);
@@ -404,7 +405,7 @@ void rmsnorm_lamport(std::vector<torch::Tensor> parts, c10::optional<torch::Tens
 void rmsnorm_rs_ag(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor> residual_in,
                    c10::optional<torch::Tensor> residual_out, torch::Tensor w, double eps, int64_t flags_ptr,
                    int64_t epoch_ptr, int64_t err_ptr, torch::Tensor dst_ptrs, torch::Tensor ag_flag_ptrs,
-                   int64_t row0, int64_t T, torch::Tensor done) {
+                   int64_t row0, int64_t T, torch::Tensor done, int64_t n_flags) {
   const int world = dst_ptrs.numel();
   TORCH_CHECK(world >= 1 && world <= 8 && ag_flag_ptrs.numel() == world && dst_ptrs.device().is_cpu() &&
                   ag_flag_ptrs.device().is_cpu(), "dst/flag pointer lists: host int64 [world]");
@@ -420,7 +421,8 @@ void rmsnorm_rs_ag(std::vector<torch::Tensor> parts, c10::optional<torch::Tensor
   }
   rmsnorm_fused_impl(parts, residual_in, residual_out, w, parts[0], eps,
                      flags_ptr ? reinterpret_cast<const int*>(flags_ptr) : nullptr,
-                     reinterpret_cast<const int*>(epoch_ptr), reinterpret_cast<int*>(err_ptr), ag);
+                     reinterpret_cast<const int*>(epoch_ptr), reinterpret_cast<int*>(err_ptr), ag, 0, PartialIn{},
+                     (int)n_flags);
 }
 
 void qkv_post_impl(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,

@@ -58,10 +58,11 @@ class RSParts(list):
     """Partials of this rank's token shard after a reduce-scatter (``T`` tokens in the step).
     ``flags_ptr`` (fused path): flags the consumer waits for before reading the partials."""
 
-    def __init__(self, views, T, flags_ptr=None, epoch_ptr=None, err_ptr=None):
+    def __init__(self, views, T, flags_ptr=None, epoch_ptr=None, err_ptr=None, n_flags=None):
         super().__init__(views)
         self.T = T
         self.flags_ptr, self.epoch_ptr, self.err_ptr = flags_ptr, epoch_ptr, err_ptr
+        self.n_flags = len(views) if n_flags is None else n_flags     # flags to wait for (one per rank)
 
 
 class NcclComm:

@@ -107,7 +107,8 @@ class FusedComm:
         # largest step (a prefill chunk plus the decode tokens riding along) for the
         # reduce-scatter / all-gather path
         self.max_step = max(self.max_tokens, int(getattr(cfgE, "prefill_chunk", 0) or 0) + cfgE.max_batch)
-        self.n_sites = 4 * model_cfg.num_layers + 8
+        # MoE steps on a token-sharded stream use five sites per layer (RS, AG, counts, dispatch, combine)
+        self.n_sites = (6 if model_cfg.is_moe else 4) * model_cfg.num_layers + 8
         self.slot_rows = max(self.max_tokens, -(-self.max_step // self.world))
         self.slot_elems = self.slot_rows * H
         data_bytes = 2 * self.world * self.slot_elems * 2
@@ -119,6 +120,20 @@ class FusedComm:
         self.lam_off = (self.flag_off + self.n_sites * self.world * 4 + 4095) // 4096 * 4096
         self.lam_bytes = 3 * self.world * self.lam_elems * 2
         total = self.lam_off + self.lam_bytes
+        # expert-parallel all-to-all (MoE): count matrices of every rank, expert-sorted receive rows
+        # and their (home rank, pair, weight) metadata, and the k combine slots of the owned rows
+        self.ep = None
+        if model_cfg.is_moe and self.world > 1:
+            k, per = model_cfg.experts_per_tok, model_cfg.num_experts // self.world
+            rcap = self.world * self.slot_rows * k
+            lay = {}
+            off = (total + 4095) // 4096 * 4096
+            for name, nbytes in (("cnt", self.world * self.world * per * 4), ("rows", rcap * H * 2),
+                                 ("meta", rcap * 16), ("comb", k * self.slot_rows * H * 2)):
+                lay[name] = off
+                off = (off + nbytes + 4095) // 4096 * 4096
+            self.ep = {"k": k, "per": per, "rcap": rcap, "off": lay}
+            total = off
         self.lamport = _lamport_default()
         e = ops.ext()
         self.base = e.ipc_malloc(total)
@@ -132,6 +147,7 @@ class FusedComm:
             else:
                 self.peer.append(e.ipc_open(torch.tensor(handles[r], dtype=torch.uint8)))
         self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.ep_done = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.tile_done = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.ag_done = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._ag_ptrs = {}
@@ -311,9 +327,84 @@ class FusedComm:
         dst, flg = self._ag_ptrs[key]
         ops._cuda(residual)
         ops.ext().rmsnorm_rs_ag(list(parts), residual, residual, weight, float(eps), parts.flags_ptr,
-                                self.epoch.data_ptr(), self.err_dev, dst, flg, row0, T, self.ag_done)
+                                self.epoch.data_ptr(), self.err_dev, dst, flg, row0, T, self.ag_done,
+                                getattr(parts, "n_flags", len(parts)))
         full = _tensor_from_ptr(self._ag_base(self.base, par), T * self.H, self.device).view(T, self.H)
         return full, ops.AGWait(self._flag_ptr(self.base, site, 0), self.world, self.epoch.data_ptr(), self.err_dev)
+
+    # ------------------------------------------------------------ expert-parallel all-to-all
+    def _ep_ptr(self, rank_base: int, name: str) -> int:
+        return rank_base + self.ep["off"][name]
+
+    def ep_moe(self, moe, layer: int, x_own: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor, T: int):
+        """Expert FFN of this rank's token rows over NVLink: counts broadcast to every rank (one
+        host read of the small count matrix sizes the grouped GEMMs), each (token, expert) pair's
+        row pushed into its expert-sorted slot on the expert's owner, the owner's grouped
+        SwiGLU GEMM waiting for the rows inside the kernel, and the grouped down GEMM's epilogue
+        pushing routing-weighted rows back to the home rank's k combine slots. Returns those slots
+        as the parts of the next norm, which waits for one flag per rank."""
+        if self.ep is None or not x_own.is_cuda:
+            return self.nccl.ep_moe(moe, layer, x_own, ids, wts, T)
+        e = ops.ext()
+        Tw, H = x_own.shape
+        k, per, world, me = ids.shape[1], self.ep["per"], self.world, self.rank
+        assert k == self.ep["k"] and Tw <= self.slot_rows
+        _, _, valid = self.shard(T)
+        ids_c, wts_c = ids.contiguous(), wts.float().contiguous()
+        epoch = self.epoch.data_ptr()
+        peers = range(world)
+        i64 = lambda v: torch.tensor(v, dtype=torch.int64)
+        # 1. counts -> every rank
+        s1 = self._next_site()
+        pos = torch.empty(max(1, Tw * k), dtype=torch.int32, device=self.device)
+        e.ep_count(ids_c, valid, per, me, pos, i64([self._ep_ptr(self.peer[r], "cnt") for r in peers]),
+                   i64([self._flag_ptr(self.peer[r], s1, me) for r in peers]), epoch)
+        e.flag_wait(self._flag_ptr(self.base, s1, 0), world, epoch, self.err_dev)
+        cnt_t = _tensor_from_ptr(self._ep_ptr(self.base, "cnt"), world * world * per * 2, self.device)
+        cnt = cnt_t.view(torch.int32).view(world, world, per).cpu()           # host read: sizes the GEMMs
+        self.check()
+        mine = cnt[:, me, :].sum(0)                                           # rows per local expert
+        offsets = torch.zeros(per + 1, dtype=torch.int32)
+        offsets[1:] = torch.cumsum(mine, 0)
+        R, max_rows = int(offsets[-1]), int(mine.max())
+        offsets = offsets.to(self.device)
+        # 2. dispatch rows to their experts' owners
+        s2 = self._next_site()
+        e.ep_dispatch(x_own.contiguous(), ids_c, wts_c, pos, valid, per, me, self._ep_ptr(self.base, "cnt"),
+                      self._flag_ptr(self.base, s1, 0), i64([self._ep_ptr(self.peer[r], "cnt") for r in peers]),
+                      i64([self._ep_ptr(self.peer[r], "rows") for r in peers]),
+                      i64([self._ep_ptr(self.peer[r], "meta") for r in peers]),
+                      i64([self._flag_ptr(self.peer[r], s2, me) for r in peers]), epoch, self.ep_done, self.err_dev)
+        ops._launches[0] += 3
+        s3 = self._next_site()
+        flg3 = i64([self._flag_ptr(self.peer[r], s3, me) for r in peers])
+        comb_rows = self.slot_rows
+        if R == 0:
+            # nothing routed here: wait for the (empty) dispatch, then release the combine consumers
+            e.flag_wait(self._flag_ptr(self.base, s2, 0), world, epoch, self.err_dev)
+            e.publish_flags(flg3, epoch)
+        else:
+            gu, n_gu, dn, n_dn = moe.packed[layer]
+            rows = _tensor_from_ptr(self._ep_ptr(self.base, "rows"), R * H, self.device).view(R, H)
+            act = torch.empty(R, n_gu // 2, dtype=x_own.dtype, device=self.device)
+            empty = torch.empty(0, dtype=torch.int32)
+            e.gemm_grouped_ep(rows, gu, n_gu, per, offsets, max_rows, act, self.ws.ws, self.ws.counters,
+                              ops.EPI_SWIGLU, self._flag_ptr(self.base, s2, 0), world, epoch, empty, 0, 0,
+                              torch.empty(0, dtype=torch.int64), 0, torch.empty(0, dtype=torch.int64),
+                              self.tile_done, 0, self.err_dev)
+            bn = 16 if max_rows <= 16 else 32 if max_rows <= 32 else 64 if max_rows <= 64 else \
+                128 if max_rows <= 128 else 256
+            tiles = int(sum((int(c) + bn - 1) // bn for c in mine)) * ((n_dn + 127) // 128)
+            meta = _tensor_from_ptr(self._ep_ptr(self.base, "meta"), R * 8, self.device).view(torch.int32)
+            e.gemm_grouped_ep(act, dn, n_dn, per, offsets, max_rows, act, self.ws.ws, self.ws.counters,
+                              ops.EPI_PUSH, 0, 0, epoch, meta, k, comb_rows,
+                              i64([self._ep_ptr(self.peer[r], "comb") for r in peers]), H, flg3, self.tile_done,
+                              tiles, self.err_dev)
+            ops._launches[0] += 2
+        views = [_tensor_from_ptr(self._ep_ptr(self.base, "comb") + j * comb_rows * H * 2, Tw * H, self.device)
+                 .view(Tw, H) for j in range(k)]
+        from b200serve.parallel.dist import RSParts
+        return RSParts(views, T, self._flag_ptr(self.base, s3, 0), epoch, self.err_dev, n_flags=world)
 
     def moe_combine_reduce(self, y, wts, pos, k, T):
         """Expert-parallel combine fused with the cross-rank sum: the combine kernel pushes each

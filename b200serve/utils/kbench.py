@@ -200,6 +200,49 @@ def gguf_one(M=8, N=6144, K=4096, iters=5):
                       "GBps_quant": round(wbytes / ms / 1e6, 1), "bf16_gemm_ms": round(ms_bf16, 4)}))
 
 
+def gguf_gemv_suite(M=8):
+    """Decode GEMV over the Qwen3-8B shapes in the Q4_K_M mix (Q4_K q/k/o/gate/up, Q6_K v/down,
+    Q8_0 lm_head), warp-task kernel vs the CTA-staged mma.sync kernel, as GB/s of quantised bytes
+    and the fraction of the measured copy bandwidth. Weights of ~1 GB per case rotate so every
+    launch streams from HBM."""
+    from b200serve.models.gguf_gpu import to_quant_weight
+    hbm, _, src = peaks()
+    cases = [("q_proj", 4096, 4096, "q4_k"), ("gate", 12288, 4096, "q4_k"), ("o_proj", 4096, 4096, "q4_k"),
+             ("down", 4096, 12288, "q6_k"), ("v_proj", 1024, 4096, "q6_k"), ("lm_head", 151936, 4096, "q8_0")]
+    x = torch.randn(M, 4096, device="cuda").bfloat16()
+    for name, N, K, kind in cases:
+        wq = to_quant_weight(torch.randn(N, K, device="cuda") * 0.02, kind)
+        nbytes = wq.codes.numel() * 4 + wq.meta.numel() * 4
+        reps = max(1, min(8, (1 << 30) // nbytes))
+        ws = [wq] + [to_quant_weight(torch.randn(N, K, device="cuda") * 0.02, kind) for _ in range(reps - 1)]
+        xk = torch.randn(M, K, device="cuda").bfloat16()
+        row = {"case": "gguf_gemv", "shape": name, "M": M, "N": N, "K": K, "type": kind, "MB": round(nbytes / 1e6, 2)}
+        i = [0]
+
+        def gemv():
+            ops.linear(xk, ws[i[0] % reps])
+            i[0] += 1
+
+        def partial():
+            ops.qlinear_partial(xk, ws[i[0] % reps])
+            i[0] += 1
+
+        def old():
+            w = ws[i[0] % reps]
+            y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+            ops.ext().gguf_gemm(xk, w.codes, w.meta, N, w.bits, w.group, y)
+            i[0] += 1
+
+        for label, fn in (("gemv", gemv), ("gemv_partial", partial), ("cta_staged", old)):
+            ms = time_cuda(fn, iters=20, warmup=3)
+            row[label + "_us"] = round(ms * 1e3, 2)
+            row[label + "_hbm_frac"] = round(nbytes / (ms * 1e-3) / (hbm * 1e9), 3)
+        row["peaks"] = src
+        print(json.dumps(row), flush=True)
+        del ws
+        torch.cuda.empty_cache()
+
+
 def sample_one(B=32, V=151936, iters=5):
     logits = torch.randn(B, V, device="cuda") * 3
     args = ([0.7] * B, [40] * B, [0.9] * B, [0.0] * B, [1] * B, [0] * B)
@@ -507,6 +550,9 @@ if __name__ == "__main__":
         sys.exit(0)
     if what == "gguf_one":
         gguf_one(*[int(v) for v in sys.argv[2:5]])
+        sys.exit(0)
+    if what == "gguf_gemv":
+        gguf_gemv_suite(*[int(v) for v in sys.argv[2:3]])
         sys.exit(0)
     if what == "sample_one":
         sample_one(*[int(v) for v in sys.argv[2:4]])

@@ -105,3 +105,27 @@ def test_embeddings_gpu_vs_cpu():
     finally:
         ec.unload()
         eg.unload()
+
+
+def test_bitwise_deterministic_prefill_and_decode():
+    """Every reduction of the engine sums in a fixed order (split-K fixup and stream-K slots in
+    split order, split-KV attention in split order, tensor-parallel slots in rank order), so two
+    runs of the same batch give bit-identical logits and tokens."""
+    cfg = BUILTIN["tiny-qwen2"]
+    w = random_weights(cfg, seed=0, dtype=torch.bfloat16, device="cuda")
+    eng = _eng(w, "cuda", "bfloat16")
+    eng.load()
+    try:
+        outs, logits = [], []
+        for _ in range(2):
+            table = eng.scheduler.alloc.allocate(8)
+            logits.append(eng.runner.prefill([{"ids": _prompt(100), "start": 0, "block_table": table}]).clone())
+            eng.scheduler.alloc.release(table)
+            reqs = eng.generate([_prompt(37, 1), _prompt(64, 2), _prompt(5, 3)],
+                                SamplingParams(temperature=0.8, top_p=0.9, seed=11, max_tokens=12, ignore_eos=True),
+                                timeout=120)
+            outs.append([r.output for r in reqs])
+        assert torch.equal(logits[0], logits[1])
+        assert outs[0] == outs[1]
+    finally:
+        eng.unload()

@@ -92,7 +92,8 @@ def test_fused_allreduce_matches_nccl():
     assert max(res.values()) < 2e-2, res
 
 
-def _tp_worker(rank, world, port, comm_kind, q, model="qwen3-8b"):
+def _tp_worker(rank, world, port, comm_kind, q, model="qwen3-8b", env=None):
+    os.environ.update(env or {})
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     from b200serve.core.config import EngineConfig
@@ -118,11 +119,11 @@ def _tp_worker(rank, world, port, comm_kind, q, model="qwen3-8b"):
     dist.destroy_process_group()
 
 
-def _run_tp(kind, model="qwen3-8b"):
+def _run_tp(kind, model="qwen3-8b", env=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_tp_worker, args=(r, 2, port, kind, q, model)) for r in range(2)]
+    ps = [ctx.Process(target=_tp_worker, args=(r, 2, port, kind, q, model, env)) for r in range(2)]
     for p in ps:
         p.start()
     out = q.get(timeout=600)
@@ -280,4 +281,14 @@ def test_ep2_moe_fused_combine_engine():
     prefill token and the first decode token (random-init MoE routing amplifies rounding
     differences in later steps)."""
     a, b = _run_tp("fused", "qwen3-30b-a3b"), _run_tp("nccl", "qwen3-30b-a3b")
+    assert [x[:2] for x in a] == [x[:2] for x in b]
+
+
+@needs2
+def test_ep2_all_to_all_matches_replicated():
+    """Token-sharded expert parallelism over NVLink (count broadcast, rows pushed into the
+    owners' expert-sorted buffers, grouped GEMM waiting for them in-kernel, weighted rows pushed
+    back by the down GEMM's epilogue) against the replicated-token path, on every step."""
+    a = _run_tp("fused", "qwen3-30b-a3b", {"B200_EP_MODE": "a2a"})
+    b = _run_tp("fused", "qwen3-30b-a3b", {"B200_EP_MODE": "replicated"})
     assert [x[:2] for x in a] == [x[:2] for x in b]
