@@ -15,7 +15,7 @@ import sys
 import torch
 
 from b200serve import ops
-from b200serve.utils.timing import time_cuda
+from b200serve.utils.timing import time_cuda, time_graph
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
@@ -213,7 +213,7 @@ def gguf_gemv_suite(M=8):
     for name, N, K, kind in cases:
         wq = to_quant_weight(torch.randn(N, K, device="cuda") * 0.02, kind)
         nbytes = wq.codes.numel() * 4 + wq.meta.numel() * 4
-        reps = max(1, min(8, (1 << 30) // nbytes))
+        reps = max(2, -(-(320 << 20) // nbytes))          # rotate over > 2.5x the L2
         ws = [wq] + [to_quant_weight(torch.randn(N, K, device="cuda") * 0.02, kind) for _ in range(reps - 1)]
         xk = torch.randn(M, K, device="cuda").bfloat16()
         row = {"case": "gguf_gemv", "shape": name, "M": M, "N": N, "K": K, "type": kind, "MB": round(nbytes / 1e6, 2)}
@@ -234,13 +234,31 @@ def gguf_gemv_suite(M=8):
             i[0] += 1
 
         for label, fn in (("gemv", gemv), ("gemv_partial", partial), ("cta_staged", old)):
-            ms = time_cuda(fn, iters=20, warmup=3)
+            # back-to-back launches in one CUDA graph: the device time of the kernel alone
+            ms = time_graph(fn, calls=2 * reps)
             row[label + "_us"] = round(ms * 1e3, 2)
             row[label + "_hbm_frac"] = round(nbytes / (ms * 1e-3) / (hbm * 1e9), 3)
         row["peaks"] = src
         print(json.dumps(row), flush=True)
         del ws
         torch.cuda.empty_cache()
+
+
+def gguf_one(N=4096, K=4096, M=8, kind="q4_k"):
+    """A few launches of each GGUF decode kernel on one shape (a small case for a profiler):
+    three warm-up rounds, then one launch each of the partial GEMV and the CTA-staged kernel.
+    Twelve weight copies rotate so the timed launches stream from HBM."""
+    from b200serve.models.gguf_gpu import to_quant_weight
+    ws = [to_quant_weight(torch.randn(N, K, device="cuda") * 0.02, kind) for _ in range(12)]
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    for i in range(4):
+        w = ws[i % 12]
+        ops.qlinear_partial(x, w)
+        w = ws[(i + 6) % 12]
+        ops.ext().gguf_gemm(x, w.codes, w.meta, N, w.bits, w.group, y)
+    torch.cuda.synchronize()
+    print(json.dumps({"case": "gguf_one", "N": N, "K": K, "M": M, "type": kind, "ok": True}))
 
 
 def sample_one(B=32, V=151936, iters=5):
@@ -553,6 +571,10 @@ if __name__ == "__main__":
         sys.exit(0)
     if what == "gguf_gemv":
         gguf_gemv_suite(*[int(v) for v in sys.argv[2:3]])
+        sys.exit(0)
+    if what == "gguf_one":
+        a = sys.argv[2:]
+        gguf_one(*[int(v) for v in a[:3]], *a[3:4])
         sys.exit(0)
     if what == "sample_one":
         sample_one(*[int(v) for v in sys.argv[2:4]])

@@ -44,3 +44,35 @@ def max_over_ranks(value: float, group=None) -> float:
     t = torch.tensor([value], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return float(t.item())
+
+
+def time_graph(fn, calls=16, reps=5, device="cuda") -> float:
+    """Milliseconds per ``fn()`` with the host out of the picture: ``calls`` invocations are
+    captured into one CUDA graph and replayed ``reps`` times after a warm-up replay (median of
+    the replays, divided by ``calls``). ``fn`` must rotate over inputs larger than L2 itself."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        fn()
+        stream.synchronize()
+        with torch.cuda.graph(g, stream=stream):
+            for _ in range(calls):
+                fn()
+    torch.cuda.current_stream(device).wait_stream(stream)
+    g.replay()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        g.replay()
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e) / calls)
+    del g
+    times.sort()
+    return times[len(times) // 2]
