@@ -548,6 +548,8 @@ def create_app(engine=None, keystore: KeyStore = None):
     from b200serve.api.knowledge_api import register_knowledge_routes
     register_agent_routes(app, auth, _get_engine)
     register_knowledge_routes(app, auth, _get_engine)
+    from b200serve.api.files_api import register_file_routes
+    register_file_routes(app, auth)
     return app
 
 
