@@ -245,6 +245,9 @@ class EngineConfig:
     spec_ngram   draft tokens per step for n-gram speculative decoding of greedy
                  requests (0 = off): the longest recent n-gram match in the request's
                  own tokens proposes a continuation, one forward verifies it
+    spec_mtp     speculative decoding with the checkpoint's MTP head (models/mtp.py; random
+                 weights get a random head): one draft per step, verified like the n-gram
+                 drafts; single-rank attention-only models
     shard_cache  directory of pre-sharded per-rank weights (models/shard_cache.py): a
                  valid cache is read instead of the checkpoint, otherwise it is written
     step_timeout_s  watchdog: a forward step running longer fails the requests it holds
@@ -275,6 +278,7 @@ class EngineConfig:
     device: str = "cuda"
     num_layers_override: int = 0
     spec_ngram: int = 0
+    spec_mtp: bool = False
     shard_cache: str = ""
     step_timeout_s: float = 600.0
     quantize: str = ""

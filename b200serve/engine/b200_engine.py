@@ -36,6 +36,18 @@ def _dtype(name):
             "fp32": torch.float32}[name]
 
 
+def _safetensors_getter(path):
+    """name -> tensor (or None) over the safetensors files of a checkpoint directory."""
+    import glob
+    from safetensors import safe_open
+    where = {}
+    for f in sorted(glob.glob(os.path.join(path, "*.safetensors"))):
+        h = safe_open(f, framework="pt")
+        for k in h.keys():
+            where[k] = h
+    return lambda name: where[name].get_tensor(name) if name in where else None
+
+
 def _kv_layers(mc) -> int:
     return sum(1 for i in range(mc.num_layers) if mc.has_kv(i))
 
@@ -43,10 +55,11 @@ def _kv_layers(mc) -> int:
 class B200Engine(BaseEngine):
     stream_starts_in_think = True
 
-    def __init__(self, config: EngineConfig = None, weights=None, tokenizer=None, model_config=None):
+    def __init__(self, config: EngineConfig = None, weights=None, tokenizer=None, model_config=None, mtp=None):
         self.config = (config or EngineConfig()).validate()
         self._injected_model_cfg = model_config
         self._injected_weights = weights
+        self._injected_mtp = mtp                  # models.mtp.MTPWeights for spec_mtp
         self._injected_tokenizer = tokenizer
         self.model_cfg = None
         self.weights = None
@@ -138,15 +151,37 @@ class B200Engine(BaseEngine):
             from b200serve.parallel.worker import BroadcastRunner
             runner = BroadcastRunner(runner, self.comm)
         self.runner = runner
+        if cfgE.spec_mtp:
+            self._attach_mtp(mc, dtype, dev)
         # a prefix-cache hit would skip tokens whose recurrent state a hybrid model needs
         self.scheduler = Scheduler(runner, num_blocks, max_batch=cfgE.max_batch, prefill_chunk=cfgE.prefill_chunk,
                                    max_seq=cfgE.max_seq, prefix_cache=not mc.is_hybrid,
-                                   spec_ngram=0 if mc.is_hybrid else cfgE.spec_ngram)
+                                   spec_ngram=0 if mc.is_hybrid else cfgE.spec_ngram,
+                                   spec_mtp=cfgE.spec_mtp and getattr(runner, "mtp", None) is not None)
         self.tokenizer = self._injected_tokenizer or load_tokenizer(self._model_path(), mc.vocab_size)
         from b200serve.core import inference
         inference._tokenizer = self.tokenizer
         self._loaded_model = cfgE.model
         say(f"b200: ready, {num_blocks} KV pages ({num_blocks * BLOCK} tokens)")
+
+    def _attach_mtp(self, mc, dtype, dev):
+        """Bind the MTP head (checkpoint ``mtp.*`` tensors, or a random head for random weights)
+        to the runner. Single rank, attention-only trunks: a hybrid trunk's recurrent state
+        cannot be rolled back past a rejected draft."""
+        from b200serve.models import mtp as MTP
+        cfgE = self.config
+        if cfgE.tp_size > 1 or mc.is_hybrid or mc.is_moe:
+            _log.warning("b200: MTP drafting runs on one rank with an attention-only dense trunk; off")
+            return
+        head = self._injected_mtp
+        if head is None and cfgE.weights == "random":
+            head = MTP.random_mtp(mc, seed=cfgE.seed, std=cfgE.init_std, dtype=dtype, device=dev)
+        elif head is None and cfgE.weights == "safetensors":
+            head = MTP.mtp_from_getter(mc, _safetensors_getter(cfgE.model), dtype=dtype, device=dev)
+        if head is None:
+            _log.warning("b200: spec_mtp set but the checkpoint has no MTP head; off")
+            return
+        self.runner.mtp = MTP.MTPHead(mc, self.runner.decoder, head, dev)
 
     def _plan_max_seq(self, mc, dev):
         """max_seq = 0: the longest context tier whose KV fits next to the weights."""

@@ -71,6 +71,8 @@ class ModelRunner:
         self._pipe = None
         self.vocab_start = weights.vocab_start
         self.greedy_buf = None
+        self.mtp = None                 # MTPHead when MTP speculative decoding is on
+        self.last_prenorm = self.last_cu = None
         pin = self.device.type == "cuda"
         self.h_pack = torch.zeros(B * (PACK + self.max_blocks), dtype=torch.int32, pin_memory=pin)
         self.s_pack = torch.zeros(B * (PACK + self.max_blocks), **i32)
@@ -319,8 +321,36 @@ class ModelRunner:
                           seq_lens=t(lens), logit_rows=torch.as_tensor(rows, dtype=torch.long).to(d),
                           is_decode=False, cu_q=t(cu), q_start=t(qs), max_q=max(len(s["ids"]) for s in seqs),
                           state_slots=t(sts) if self.lin_state is not None else None, telemetry=watch or None,
-                          hidden=any(s.get("hidden") for s in seqs))
+                          hidden=any(s.get("hidden") for s in seqs),
+                          keep_prenorm=self.mtp is not None and any(s.get("prenorm") for s in seqs))
         if T == 0:
             return None
         with rng(f"prefill T{T}"):
-            return self.decoder.forward(fb)
+            out = self.decoder.forward(fb)
+        # pre-final-norm hidden of every row (for the MTP head), rows of seqs[i] at cu[i]:cu[i+1]
+        self.last_prenorm, self.last_cu = (self.decoder.prenorm, cu) if fb.keep_prenorm else (None, None)
+        return out
+
+    def mtp_step(self, segs):
+        """Run the MTP head over committed rows and return its greedy draft per segment.
+        ``segs``: dicts with h (pre-norm hiddens [n, H] of trunk positions start..start+n-1),
+        next_ids (the n tokens after those positions), start, block_table."""
+        d = self.device
+        ids, pos, slots, cu, qs, lens, rows = [], [], [], [0], [], [], []
+        maxb = max(len(s["block_table"]) for s in segs)
+        bt = torch.zeros(len(segs), maxb, dtype=torch.int32)
+        for i, s in enumerate(segs):
+            n, st, table = len(s["next_ids"]), s["start"], s["block_table"]
+            ids += list(s["next_ids"])
+            pos += list(range(st, st + n))
+            slots += [table[p // 16] * 16 + p % 16 for p in range(st, st + n)]
+            cu.append(cu[-1] + n)
+            qs.append(st)
+            lens.append(st + n)
+            rows.append(cu[-1] - 1)
+            bt[i, : len(table)] = torch.as_tensor(table, dtype=torch.int32)
+        t = lambda x: torch.as_tensor(x, dtype=torch.int32).to(d, non_blocking=True)
+        h = torch.cat([s["h"] for s in segs])
+        logits = self.mtp.forward(h, t(ids), t(pos), t(slots), bt.to(d), t(lens), t(cu), t(qs),
+                                  max(len(s["next_ids"]) for s in segs), torch.as_tensor(rows, dtype=torch.long).to(d))
+        return self.greedy_tokens(logits).tolist()

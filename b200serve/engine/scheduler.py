@@ -73,6 +73,7 @@ class Request:
     state_slot: int = -1             # recurrent-state slot (hybrid models) while running
     telemetry: object = None         # TelemetryCapture: per-token forward frames (eager steps)
     embedding: list = None           # embedding requests: the mean-pooled final hidden state
+    mtp_draft: int = None            # MTP head's guess for the token after tokens[-1]
     done_event: threading.Event = field(default_factory=threading.Event)
 
     def __post_init__(self):
@@ -90,7 +91,7 @@ class Request:
 
 class Scheduler:
     def __init__(self, runner, num_blocks: int, max_batch: int = 64, prefill_chunk: int = 8192,
-                 max_seq: int = 4096, prefix_cache: bool = True, spec_ngram: int = 0):
+                 max_seq: int = 4096, prefix_cache: bool = True, spec_ngram: int = 0, spec_mtp: bool = False):
         self.runner = runner
         self.alloc = BlockAllocator(num_blocks, enable_prefix_cache=prefix_cache)
         self.max_batch = max_batch
@@ -104,6 +105,8 @@ class Scheduler:
         # hybrid (DeltaNet) models keep a recurrent state per running request
         self.free_states = list(range(max_batch)) if getattr(runner, "lin_state", None) is not None else None
         self.spec_ngram = spec_ngram
+        # MTP drafting needs the runner's head (runner.mtp), which sees every committed position
+        self.spec_mtp = bool(spec_mtp) and getattr(runner, "mtp", None) is not None
         self.stats = {"steps": 0, "decode_steps": 0, "mixed_steps": 0, "preemptions": 0,
                       "generated": 0, "prefill_tokens": 0, "prefix_hit_tokens": 0,
                       "spec_steps": 0, "spec_drafted": 0, "spec_accepted": 0}
@@ -363,7 +366,7 @@ class Scheduler:
         self.stats["steps"] += 1
         if any(r.num_computed < len(r.tokens) - 1 for r in self.running):
             return self._mixed_step()
-        if self.spec_ngram and any(self._spec_ok(r) for r in self.running):
+        if (self.spec_ngram or self.spec_mtp) and any(self._spec_ok(r) for r in self.running):
             n = self._spec_step()
             if n:
                 return n
@@ -427,7 +430,7 @@ class Scheduler:
             last = r.num_computed + n == len(r.tokens)
             seqs.append({"ids": r.tokens[r.num_computed:r.num_computed + n], "start": r.num_computed,
                          "block_table": r.blocks, "want_logits": last, "state_slot": r.state_slot,
-                         "telemetry": r.telemetry if last else None})
+                         "telemetry": r.telemetry if last else None, "prenorm": self._mtp_ok(r)})
             reqs.append((r, n))
             if remaining > 1:
                 budget -= n
@@ -441,11 +444,11 @@ class Scheduler:
         logits = self.runner.prefill(seqs)
         self.stats["mixed_steps"] += 1
         sample_reqs = [r for (r, n), s in zip(reqs, seqs) if s["want_logits"]]
+        # MTP: every row this step computed is committed (the head needs the token after each)
+        commits = [(i, r, r.num_computed, n) for i, (r, n) in enumerate(reqs) if seqs[i]["prenorm"]]
         for r, n in reqs:
             r.num_computed += n
-        if not sample_reqs:
-            return 0
-        toks = self._sample(logits, sample_reqs).tolist()
+        toks = self._sample(logits, sample_reqs).tolist() if sample_reqs else []
         for j, (r, t) in enumerate(zip(sample_reqs, toks)):
             if r.telemetry is not None:
                 r.telemetry.finish_token(logits[j], t)
@@ -453,12 +456,48 @@ class Scheduler:
             self._accept_token(r, int(t))
             if r.state == "finished":
                 self.running.remove(r)
+        self._mtp_commit([(i, 0, r, start, n) for i, r, start, n in commits])
         return len(sample_reqs)
 
-    # ------------------------------------------------------------ n-gram speculative decoding
+    # ------------------------------------------------------------ speculative decoding
+    def _mtp_ok(self, r: Request) -> bool:
+        return self.spec_mtp and r.params.greedy and r.params.plain and r.telemetry is None
+
     def _spec_ok(self, r: Request) -> bool:
-        return (r.params.greedy and r.params.plain and r.telemetry is None
-                and ngram_draft(r.tokens, self.spec_ngram) != [])
+        if not (r.params.greedy and r.params.plain and r.telemetry is None):
+            return False
+        if self.spec_mtp:
+            return True          # even without a draft: the verify path keeps the head's K/V complete
+        return ngram_draft(r.tokens, self.spec_ngram) != []
+
+    def _draft(self, r: Request) -> list:
+        if not self._spec_ok(r):
+            return []
+        if self.spec_mtp:
+            return [r.mtp_draft] if r.mtp_draft is not None else []
+        return ngram_draft(r.tokens, self.spec_ngram)
+
+    def _mtp_commit(self, commits):
+        """Feed the MTP head the rows a trunk step committed and take its next drafts.
+        ``commits``: (seq index in the step, first row of that seq's committed rows, request,
+        position of the first committed row, number of committed rows)."""
+        if not self.spec_mtp or not commits:
+            return
+        prenorm, cu = self.runner.last_prenorm, self.runner.last_cu
+        segs, owners = [], []
+        for i, r0, r, start, n in commits:
+            if r.state == "finished" or n <= 0 or len(r.tokens) < start + n + 1:
+                r.mtp_draft = None
+                continue
+            h = prenorm[cu[i] + r0: cu[i] + r0 + n]
+            segs.append({"h": h, "next_ids": r.tokens[start + 1: start + n + 1], "start": start,
+                         "block_table": r.blocks})
+            owners.append(r)
+        if not segs:
+            return
+        drafts = self.runner.mtp_step(segs)
+        for r, d in zip(owners, drafts):
+            r.mtp_draft = int(d)
 
     def _spec_step(self) -> int:
         """Verify n-gram drafts of greedy requests in one forward: each drafting request feeds
@@ -471,7 +510,7 @@ class Scheduler:
         for r in list(self.running):
             if r not in self.running:
                 continue
-            draft = ngram_draft(r.tokens, self.spec_ngram) if self._spec_ok(r) else []
+            draft = self._draft(r)
             room = min(r.params.max_tokens - len(r.output), self.max_seq - len(r.tokens)) - 1
             draft = draft[:max(0, room)]
             if not self._ensure_blocks(r, len(r.tokens) + len(draft)):
@@ -479,7 +518,8 @@ class Scheduler:
             if r not in self.running:
                 continue
             seqs.append({"ids": [r.tokens[-1]] + draft, "start": len(r.tokens) - 1, "block_table": r.blocks,
-                         "want_logits": True, "all_logits": bool(draft), "state_slot": r.state_slot})
+                         "want_logits": True, "all_logits": bool(draft), "state_slot": r.state_slot,
+                         "prenorm": self._mtp_ok(r)})
             plan.append((r, draft))
         keep = [(s, pl) for s, pl in zip(seqs, plan) if pl[0] in self.running]
         if not keep:
@@ -487,9 +527,11 @@ class Scheduler:
         logits = self.runner.prefill([s for s, _ in keep])
         self.stats["spec_steps"] += 1
         row, accepted = 0, 0
-        plain_rows, plain_reqs, spec = [], [], []
-        for _, (r, draft) in keep:
+        plain_rows, plain_reqs, spec, commits = [], [], [], []
+        for si, (s_, (r, draft)) in enumerate(keep):
             n = len(draft) + 1 if draft else 1
+            if s_["prenorm"]:
+                commits.append((si, r, len(r.tokens) - 1))
             if draft:
                 pred = logits[row:row + n].argmax(-1).tolist()
                 a = 0
@@ -505,15 +547,20 @@ class Scheduler:
         if plain_reqs:
             toks = self._sample(logits[plain_rows], plain_reqs).tolist()
             spec += [(r, [t]) for r, t in zip(plain_reqs, toks)]
+        took = {}
         for r, new in spec:
+            took[id(r)] = 0
             for t in new:
                 if r.state == "finished":
                     break
                 r.num_computed = len(r.tokens)
                 self._accept_token(r, int(t))
                 accepted += 1
+                took[id(r)] += 1
             if r.state == "finished" and r in self.running:
                 self.running.remove(r)
+        # MTP: rows 0..(tokens taken - 1) of each verify segment are now committed positions
+        self._mtp_commit([(si, 0, r, start, took.get(id(r), 0)) for si, r, start in commits])
         return accepted
 
     def _sample(self, logits, reqs) -> torch.Tensor:

@@ -46,6 +46,8 @@ class ForwardBatch:
     state_slots: torch.Tensor = None    # hybrid models: recurrent-state slot per sequence
     telemetry: list = None              # [(row, TelemetryCapture)]: per-layer frames for these rows
     hidden: bool = False                # return the final-normed hidden states of logit_rows, no lm_head
+    inputs_embeds: torch.Tensor = None  # [T, H] input rows instead of the embedding lookup (MTP head)
+    keep_prenorm: bool = False          # keep the pre-final-norm hidden of every row in Decoder.prenorm
 
 
 class NoComm:
@@ -431,17 +433,17 @@ class Decoder:
         self._partial_ok = not fb.telemetry
         if hasattr(comm, "begin_step"):
             comm.begin_step()
-        h = ops.embedding(fb.input_ids, w.embed)
+        h = fb.inputs_embeds if fb.inputs_embeds is not None else ops.embedding(fb.input_ids, w.embed)
         if fb.is_decode:
             tps, nsplit = attn_plan or self.decode_attn_plan(T, int(fb.block_tables.shape[1]) * 16)
             ws = self.ensure_attn_workspace(T, nsplit) if nsplit > 1 else None
         quant_kv = self.tq is not None or (self.kv.kv_format == "int4g128" and h.is_cuda and ops._TC_PREFILL)
         tq_pre = self._tq_prefill_pages(fb) if (quant_kv and not fb.is_decode) else None
         plan = (tps, nsplit, ws) if fb.is_decode else (0, 0, None)
-        if self.moe is not None and self._use_ep_a2a(T):
+        if self.moe is not None and not fb.keep_prenorm and self._use_ep_a2a(T):
             return self._forward_ep(fb, h, plan, tq_pre)
         if self.moe is None and not cfg.is_hybrid and not cfg.sandwich_norms and cfg.act == "silu" and \
-                comm.world > 1 and hasattr(comm, "use_rsag") and comm.use_rsag(T):
+                not fb.keep_prenorm and comm.world > 1 and hasattr(comm, "use_rsag") and comm.use_rsag(T):
             return self._forward_rsag(fb, h, plan, tq_pre)
         residual = torch.empty_like(h)
         x = ops.rmsnorm([h], w.layers[0].input_norm, eps, residual_out=residual)
@@ -480,7 +482,9 @@ class Decoder:
             if _NVTX:
                 torch.cuda.nvtx.range_pop()
         rows = fb.logit_rows
-        x = ops.rmsnorm(mlp_parts, w.final_norm, eps, residual=residual)
+        x = ops.rmsnorm(mlp_parts, w.final_norm, eps, residual=residual,
+                        residual_out=residual if fb.keep_prenorm else None)
+        self.prenorm = residual if fb.keep_prenorm else None
         if rows is not None:
             x = x.index_select(0, rows)
         if fb.hidden:
