@@ -406,10 +406,10 @@ def embedding(ids, table, out=None):
 
 # ------------------------------------------------------------------ GEMM
 class PartialParts(list):
-    """Output of a decode GEMM left as fp32 stream-K partial sums (gemm_tc_partial): the row
-    kernel that consumes it (rmsnorm, qkv_post_partial) adds the slots up. Element 0 is a
-    [T, N] bf16 view that only carries the shape; ``part`` and ``plan`` (kb, ctas, total) say
-    where the slots are."""
+    """Output of a decode GEMM left as fp32 stream-K partial sums (gemm_tc_partial, or the GGUF
+    gguf_stream): the row kernel that consumes it (rmsnorm, qkv_post_partial, silu_mul_partial)
+    adds the slots up. Element 0 is a [T, N] bf16 view that only carries the shape; ``part`` and
+    ``plan`` (kb, workers, total, tile width) say where the slots are."""
 
     def __init__(self, like, part, plan):
         super().__init__([like])
@@ -433,6 +433,7 @@ def _partial_buffer(device, floats: int = 4 << 20):
 
 
 _NO_PUSH = torch.zeros(0, dtype=torch.int64)
+_NO_OUT = torch.zeros(0, dtype=torch.float32)
 _dequant_scratch = {}
 
 
@@ -441,30 +442,57 @@ def _quant_parts(w):
     return parts if parts and all(isinstance(p, QuantWeight) for p in parts) else None
 
 
-def qlinear_partial(x, w):
-    """GGUF projection(s) for a decode batch (1..16 rows) as fp32 partial sums: every part of a
-    QuantGroup writes its columns of one [S][M][sum N] slot set (gguf_gemv, K split S), which the
-    consuming row kernel sums (S slots per 128-column tile). None when the path does not apply."""
-    parts = _quant_parts(w)
-    M = x.shape[0]
-    if parts is None or not (x.is_cuda and 1 <= M <= 16) or len({p.K for p in parts}) != 1:
-        return None
-    if any(p.K % 256 or p.N % 16 for p in parts):
-        return None
-    ntot, K = sum(p.N for p in parts), parts[0].K
-    S = min(ext().gguf_gemv_splits(p.N, K) for p in parts)
-    buf = _partial_buffer(x.device)
-    if S * M * ntot > buf.numel():
-        return None
+_gs_scratch = {}
+
+
+def _gguf_scratch(device):
+    """(workspace, counters, SM count) of the GGUF stream GEMV on ``device``: the fp32 partials of
+    slices shared by several warps, the per-slice arrival counters (zero between launches, the last
+    word an error code) and the grid size."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    if key not in _gs_scratch:
+        nsm = torch.cuda.get_device_properties(key).multi_processor_count
+        _gs_scratch[key] = (torch.zeros(nsm * 2 * 4096, dtype=torch.float32, device=device),
+                            torch.zeros(1 << 16, dtype=torch.int32, device=device), nsm)
+    return _gs_scratch[key]
+
+
+def gguf_stream(x, parts, mode, out, ldo, push=None, mc=0):
+    """Launch the stream-K GGUF GEMV (ops/csrc/gguf_stream.cu) over QuantWeights that share x;
+    returns its plan (kb, workers, items)."""
+    ws, counters, nsm = _gguf_scratch(x.device)
     xc = x if (x.stride(1) == 1 and x.stride(0) % 8 == 0) else x.contiguous()
-    col = 0
-    for p in parts:
-        _cuda(x)
-        ext().gguf_gemv(xc, p.codes, p.meta, p.N, p.bits, p.group, 2, S, buf, ntot, col, _NO_PUSH, 0)
-        col += p.N
-    tiles = (ntot + 127) // 128
+    _cuda(x)
+    return ext().gguf_stream(xc, [p.codes for p in parts], [p.meta for p in parts], [p.N for p in parts],
+                             [p.bits for p in parts], [p.group for p in parts], mode,
+                             out if out is not None else _NO_OUT, ldo, ws, counters,
+                             push if push is not None else _NO_PUSH, mc, nsm, 0)
+
+
+def _gs_ok(x, parts, tile=16):
+    return (parts is not None and x.is_cuda and 1 <= x.shape[0] <= 16 and len(parts) <= 4
+            and len({p.K for p in parts}) == 1 and all(p.K % 256 == 0 and p.N % tile == 0 for p in parts))
+
+
+def qlinear_partial(x, w):
+    """GGUF projection(s) for a decode batch (1..16 rows) as fp32 partial sums: the parts of a
+    QuantGroup stream as one stream-K job whose CTAs write [slot][M][sum N] partials (128-column
+    tiles, the contract of the tcgen05 stream-K GEMM) that the consuming row kernel adds up.
+    None when the path does not apply."""
+    parts = _quant_parts(w)
+    if not _gs_ok(x, parts, 128):
+        return None
+    M = x.shape[0]
+    ntot, K = sum(p.N for p in parts), parts[0].K
+    _, _, nsm = _gguf_scratch(x.device)
+    kb, workers, items = ext().gguf_stream_plan(ntot, K, nsm)
+    slots = (kb * workers + items - 1) // items + 1
+    buf = _partial_buffer(x.device)
+    if slots * M * ntot > buf.numel():
+        return None
+    gguf_stream(x, parts, 2, buf, ntot)
     like = buf.view(torch.bfloat16)[: M * ntot].view(M, ntot)
-    return PartialParts(like, buf, (S, S * tiles, S * tiles))
+    return PartialParts(like, buf, (kb, workers, items, 128))
 
 
 def linear_partial(x, w):
@@ -487,7 +515,7 @@ def linear_partial(x, w):
     _cuda(x)
     ext().gemm_tc_partial(x.contiguous() if x.stride(1) != 1 else x, w.data, w.N, buf)
     like = buf.view(torch.bfloat16)[: M * w.N].view(M, w.N)
-    return PartialParts(like, buf, (kb, ctas, total))
+    return PartialParts(like, buf, (kb, ctas, total, 128))
 
 
 def qkv_post_partial(pp, bias, q_norm, k_norm, cos_sin, positions, slots, k_cache, v_cache, nq, nkv, eps, hd):
@@ -680,7 +708,7 @@ def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspac
                 I = w[0].N
                 out = out if out is not None else torch.empty(M, I, dtype=x.dtype, device=x.device)
                 _cuda(x)
-                ext().silu_mul_partial(pp.part, pp.plan[0], M, I, out)
+                ext().silu_mul_partial(pp.part, *pp.plan, M, I, out)
                 return out
         if epilogue == EPI_SWIGLU:
             g, u = (linear(x, p) for p in w)
@@ -698,15 +726,12 @@ def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspac
     N = w.shape[0]
     packed_n = 0
     if isinstance(w, QuantWeight):
-        if (x.is_cuda and M <= 16 and epilogue in (EPI_BF16, EPI_F32) and bias is None and residual is None
-                and w.K % 256 == 0 and w.N % 16 == 0):
+        if epilogue in (EPI_BF16, EPI_F32) and bias is None and residual is None and _gs_ok(x, [w]):
             f32 = epilogue == EPI_F32
             y = out if (out is not None and out.is_contiguous() and
                         out.dtype == (torch.float32 if f32 else x.dtype)) else \
                 torch.empty(M, w.N, dtype=torch.float32 if f32 else x.dtype, device=x.device)
-            _cuda(x)
-            ext().gguf_gemv(x if x.stride(1) == 1 and x.stride(0) % 8 == 0 else x.contiguous(), w.codes, w.meta,
-                            w.N, w.bits, w.group, 1 if f32 else 0, 1, y, w.N, 0, _NO_PUSH, 0)
+            gguf_stream(x, [w], 1 if f32 else 0, y, w.N)
             if out is not None and y is not out:
                 out.copy_(y)
                 return out

@@ -11,11 +11,11 @@ void rmsnorm_lamport(std::vector<torch::Tensor> parts, c10::optional<torch::Tens
                      int64_t err_ptr, bool skip_prior_wait);
 std::vector<int64_t> gemm_partial_plan(int64_t M, int64_t N, int64_t K, int64_t num_sms);
 std::vector<int64_t> gemm_tc_partial(torch::Tensor act, torch::Tensor w, int64_t packed_n, torch::Tensor part);
-void rmsnorm_partial(torch::Tensor like, torch::Tensor part, int64_t kb, int64_t ctas, int64_t total,
+void rmsnorm_partial(torch::Tensor like, torch::Tensor part, int64_t kb, int64_t ctas, int64_t total, int64_t tile,
                      c10::optional<torch::Tensor> residual_in, c10::optional<torch::Tensor> residual_out,
                      torch::Tensor w, torch::Tensor out, double eps);
 void qkv_post_partial(torch::Tensor like, torch::Tensor part, int64_t kb, int64_t ctas, int64_t total,
-                      c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
+                      int64_t tile, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
                       c10::optional<torch::Tensor> kn_w, torch::Tensor cos_sin, torch::Tensor positions,
                       torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache,
                       c10::optional<torch::Tensor> k_scale, c10::optional<torch::Tensor> v_scale, int64_t nq,
@@ -24,7 +24,13 @@ int64_t gguf_gemv_splits(int64_t N, int64_t K);
 void gguf_gemv(torch::Tensor x, torch::Tensor codes, torch::Tensor meta, int64_t N, int64_t bits, int64_t group,
                int64_t mode, int64_t S, torch::Tensor out, int64_t ldo, int64_t col0, torch::Tensor push_ptrs,
                int64_t mc_ptr);
-void silu_mul_partial(torch::Tensor part, int64_t S, int64_t M, int64_t I, torch::Tensor out);
+void silu_mul_partial(torch::Tensor part, int64_t kb, int64_t ctas, int64_t total, int64_t tile, int64_t M, int64_t I,
+                      torch::Tensor out);
+std::vector<int64_t> gguf_stream_plan(int64_t N, int64_t K, int64_t num_sms);
+std::vector<int64_t> gguf_stream(torch::Tensor x, std::vector<torch::Tensor> codes, std::vector<torch::Tensor> metas,
+                                 std::vector<int64_t> ns, std::vector<int64_t> bits, std::vector<int64_t> groups,
+                                 int64_t mode, torch::Tensor out, int64_t ldo, torch::Tensor ws, torch::Tensor counters,
+                                 torch::Tensor push_ptrs, int64_t mc_ptr, int64_t num_sms, int64_t wait_ms);
 void gguf_dequant_packed(torch::Tensor codes, torch::Tensor meta, int64_t N, int64_t K, int64_t bits, int64_t group,
                          torch::Tensor out);
 void gemm_grouped_ep(torch::Tensor act, torch::Tensor w_packed, int64_t N, int64_t E, torch::Tensor offsets,
@@ -174,6 +180,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_dispatch", &ep_dispatch);
   m.def("gguf_dequant_packed", &gguf_dequant_packed);
   m.def("silu_mul_partial", &silu_mul_partial);
+  m.def("gguf_stream_plan", &gguf_stream_plan);
+  m.def("gguf_stream", &gguf_stream);
   m.def("gemm_tc_partial", &gemm_tc_partial);
   m.def("rmsnorm_partial", &rmsnorm_partial);
   m.def("qkv_post_partial", &qkv_post_partial);

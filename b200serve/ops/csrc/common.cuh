@@ -75,22 +75,33 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 // fp32 partial sums of a stream-K GEMM (EPI_PARTIAL) that a row kernel reduces: slot s of
-// column c holds part[s][row][c]. CTA g of `ctas` streamed the flattened k-blocks
-// [g*total/ctas, (g+1)*total/ctas) of the 128-wide column tiles (`kb` k-blocks per tile,
-// total = tiles*kb); tile t's slots are the CTAs from the one holding k-block t*kb to the one
-// holding k-block (t+1)*kb - 1, in that order.
+// column c holds part[s][row][c]. Worker g of `ctas` (a CTA of the tcgen05 GEMM, a warp of the
+// GGUF GEMV) streamed the flattened k-blocks [g*total/ctas, (g+1)*total/ctas) of the `tile`-wide
+// column tiles (`kb` k-blocks per tile, total = tiles*kb); tile t's slots are the workers from
+// the one holding k-block t*kb to the one holding k-block (t+1)*kb - 1, in that order.
 struct PartialIn {
   const float* part;      // nullptr: not in use
   int kb, ctas;
   long long total;
   int rows, cols;
+  int tile;               // columns per tile (128: tcgen05 GEMM, 16: GGUF GEMV)
 };
 
 __device__ __forceinline__ int partial_slots(const PartialIn& pi, int col) {
-  const long long t = col / 128;
+  const long long t = col / pi.tile;
   const long long first = ((t * pi.kb + 1) * pi.ctas + pi.total - 1) / pi.total - 1;
   const long long last = ((t + 1) * pi.kb * pi.ctas + pi.total - 1) / pi.total - 1;
   return (int)(last - first + 1);
+}
+
+// Sum of one column's slots, in slot order (no rounding).
+__device__ __forceinline__ float partial_col(const PartialIn& pi, int row, int col) {
+  const int n = partial_slots(pi, col);
+  const float* src = pi.part + (size_t)row * pi.cols + col;
+  const size_t slot = (size_t)pi.rows * pi.cols;
+  float acc = 0.f;
+  for (int s = 0; s < n; ++s) acc += __ldcg(src + s * slot);
+  return acc;
 }
 
 // Sum of the slots for NE consecutive columns of one tile (NE even; 8-byte aligned, 16-byte

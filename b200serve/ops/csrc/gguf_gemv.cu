@@ -225,26 +225,6 @@ __global__ void __launch_bounds__(kVWarps * 32) gguf_gemv_kernel(const QvArgs a)
   }
 }
 
-// act[t][i] = silu(gate) * up from the S fp32 partial slots of a [gate | up] output of width 2I,
-// each rounded to bf16 first as a bf16 gate/up projection would be.
-__global__ void silu_mul_partial_kernel(const float* __restrict__ part, int S, int M, int I,
-                                        __nv_bfloat16* __restrict__ out) {
-  pdl_wait();
-  pdl_trigger();
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= M * I) return;
-  const int t = idx / I, i = idx % I;
-  const size_t slot = (size_t)M * 2 * I;
-  float gs = 0.f, us = 0.f;
-  for (int s = 0; s < S; ++s) {
-    gs += __ldcg(part + s * slot + (size_t)t * 2 * I + i);
-    us += __ldcg(part + s * slot + (size_t)t * 2 * I + I + i);
-  }
-  const float gr = __bfloat162float(__float2bfloat16_rn(gs)), ur = __bfloat162float(__float2bfloat16_rn(us));
-  const float sg = __bfloat162float(__float2bfloat16_rn(gr / (1.f + __expf(-gr))));
-  out[(size_t)t * I + i] = __float2bfloat16_rn(sg * ur);
-}
-
 // Block-quantised weight -> bf16 in the tile-packed layout of the tcgen05 GEMM
 // ([N/128][K/64][128][64]), for prefill-sized batches: one warp per (slice, k-step), each lane
 // dequantises its fragment (rows g, g+8 x columns 2t, 2t+1, 2t+8, 2t+9) and stores four bf16 pairs.
@@ -369,11 +349,3 @@ void gguf_gemv(torch::Tensor x, torch::Tensor codes, torch::Tensor meta, int64_t
   B200_CHECK_CUDA(cudaGetLastError());
 }
 
-void silu_mul_partial(torch::Tensor part, int64_t S, int64_t M, int64_t I, torch::Tensor out) {
-  TORCH_CHECK(part.scalar_type() == at::kFloat && out.scalar_type() == at::kBFloat16 && out.is_contiguous());
-  TORCH_CHECK(part.numel() >= S * M * 2 * I && out.numel() >= M * I);
-  const int n = (int)(M * I), threads = 256;
-  launch_pdl(silu_mul_partial_kernel, dim3((n + threads - 1) / threads), dim3(threads), 0,
-             at::cuda::getCurrentCUDAStream(), (const float*)part.data_ptr<float>(), (int)S, (int)M, (int)I,
-             reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
-}

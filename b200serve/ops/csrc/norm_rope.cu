@@ -380,11 +380,13 @@ void rmsnorm_fused_wait(std::vector<torch::Tensor> parts, c10::optional<torch::T
 
 // out = RMSNorm(sum of a stream-K GEMM's fp32 partials + residual) * w (see PartialIn);
 // `like` is a bf16 [T, H] tensor that gives the row geometry (its data is not read).
-void rmsnorm_partial(torch::Tensor like, torch::Tensor part, int64_t kb, int64_t ctas, int64_t total,
+void rmsnorm_partial(torch::Tensor like, torch::Tensor part, int64_t kb, int64_t ctas, int64_t total, int64_t tile,
                      c10::optional<torch::Tensor> residual_in, c10::optional<torch::Tensor> residual_out,
                      torch::Tensor w, torch::Tensor out, double eps) {
   TORCH_CHECK(part.scalar_type() == at::kFloat && part.is_contiguous(), "partials: contiguous fp32");
-  PartialIn pin{part.data_ptr<float>(), (int)kb, (int)ctas, (long long)total, (int)like.size(0), (int)like.size(1)};
+  TORCH_CHECK(tile == 16 || tile == 128, "partial tiles are 16 or 128 columns wide");
+  PartialIn pin{part.data_ptr<float>(), (int)kb, (int)ctas, (long long)total, (int)like.size(0), (int)like.size(1),
+                (int)tile};
   rmsnorm_fused_impl({like}, residual_in, residual_out, w, out, eps, nullptr, nullptr, nullptr, AgArgs{}, 0, pin);
 }
 
@@ -470,14 +472,16 @@ void qkv_post(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optiona
 // qkv_post whose input rows are the fp32 stream-K partials of the QKV GEMM (see PartialIn);
 // `like` [T, width] bf16 only gives the geometry. Scales given: int4g128 KV cache.
 void qkv_post_partial(torch::Tensor like, torch::Tensor part, int64_t kb, int64_t ctas, int64_t total,
-                      c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
+                      int64_t tile, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> qn_w,
                       c10::optional<torch::Tensor> kn_w, torch::Tensor cos_sin, torch::Tensor positions,
                       torch::Tensor slots, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache,
                       c10::optional<torch::Tensor> k_scale, c10::optional<torch::Tensor> v_scale, int64_t nq,
                       int64_t nkv, double eps) {
   TORCH_CHECK(part.scalar_type() == at::kFloat && part.is_contiguous(), "partials: contiguous fp32");
   TORCH_CHECK(like.stride(0) == like.size(1), "partials have the row stride of a dense [T, width] output");
-  PartialIn pin{part.data_ptr<float>(), (int)kb, (int)ctas, (long long)total, (int)like.size(0), (int)like.size(1)};
+  TORCH_CHECK(tile == 16 || tile == 128, "partial tiles are 16 or 128 columns wide");
+  PartialIn pin{part.data_ptr<float>(), (int)kb, (int)ctas, (long long)total, (int)like.size(0), (int)like.size(1),
+                (int)tile};
   const bool q4 = k_scale.has_value();
   qkv_post_impl(like, bias, qn_w, kn_w, cos_sin, positions, slots, q_out, k_cache, v_cache,
                 q4 ? reinterpret_cast<__half*>(k_scale->data_ptr()) : nullptr,

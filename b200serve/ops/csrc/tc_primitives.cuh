@@ -40,6 +40,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread may sleep up to `hint_ns` until the phase
+// completes instead of re-polling (fewer issue slots taken from working warps).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: spins until the phase with `parity` completes, the CTA-wide abort
 // flag is raised by another role, or ~2 s of wall time pass (then it records
 // `code` in *err, raises the abort flag and returns false).
@@ -58,6 +72,15 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
       }
     }
   }
+}
+
+// ---------------- bulk copies (no multicast) ----------------
+// `bytes` from global `src` into this CTA's shared memory at `dst` (both 16-byte aligned, bytes a
+// multiple of 16), completing on `bar` (which expects the bytes through arrive.expect_tx).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 
 // ---------------- TMA ----------------

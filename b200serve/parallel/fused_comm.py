@@ -227,8 +227,8 @@ class FusedComm:
         T = x.shape[0]
         if (isinstance(w, ops.QuantWeight) and self.lamport and T <= 16 and x.is_cuda
                 and w.N == self.H and w.K % 256 == 0):
-            # GGUF row-parallel projection: the warp-task GEMV stores its bf16 tiles straight into
-            # every rank's flag-free slot (P2P or one multicast store)
+            # GGUF row-parallel projection: the stream-K GEMV stores each finished bf16 tile straight
+            # into every rank's flag-free slot (P2P or one multicast store)
             site = self.site
             self.site += 1
             assert site < self.n_sites, "more fused sites than allocated"
@@ -241,9 +241,7 @@ class FusedComm:
             dst = self._ptrs[key]
             if self.use_mc:
                 dst = torch.tensor([self._lam_local(rot, self.rank)], dtype=torch.int64)   # unused with mc
-            xc = x if (x.stride(1) == 1 and x.stride(0) % 8 == 0) else x.contiguous()
-            ops._cuda(x)
-            ops.ext().gguf_gemv(xc, w.codes, w.meta, w.N, w.bits, w.group, 4, 1, xc, self.H, 0, dst, mc)
+            ops.gguf_stream(x, [w], 4, None, self.H, dst, mc)
             return LamportParts(self._lam_views(rot, T), self.err_dev, ops.launch_count())
         if T > self.max_tokens or not isinstance(w, (torch.Tensor, ops.PackedWeight)):
             # large chunks (NVLS all-reduce is bandwidth-optimal) and other quantised shapes take NCCL

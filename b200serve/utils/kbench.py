@@ -202,9 +202,9 @@ def gguf_one(M=8, N=6144, K=4096, iters=5):
 
 def gguf_gemv_suite(M=8):
     """Decode GEMV over the Qwen3-8B shapes in the Q4_K_M mix (Q4_K q/k/o/gate/up, Q6_K v/down,
-    Q8_0 lm_head), warp-task kernel vs the CTA-staged mma.sync kernel, as GB/s of quantised bytes
-    and the fraction of the measured copy bandwidth. Weights of ~1 GB per case rotate so every
-    launch streams from HBM."""
+    Q8_0 lm_head): the stream-K kernel (direct output and partials) against the earlier warp-task
+    and CTA-staged mma.sync kernels, as the fraction of the measured copy bandwidth. Weight copies
+    totalling > 2.5x the L2 rotate so every launch streams from HBM."""
     from b200serve.models.gguf_gpu import to_quant_weight
     hbm, _, src = peaks()
     cases = [("q_proj", 4096, 4096, "q4_k"), ("gate", 12288, 4096, "q4_k"), ("o_proj", 4096, 4096, "q4_k"),
@@ -233,7 +233,15 @@ def gguf_gemv_suite(M=8):
             ops.ext().gguf_gemm(xk, w.codes, w.meta, N, w.bits, w.group, y)
             i[0] += 1
 
-        for label, fn in (("gemv", gemv), ("gemv_partial", partial), ("cta_staged", old)):
+        def warp_task():
+            w = ws[i[0] % reps]
+            S = ops.ext().gguf_gemv_splits(N, K)
+            buf = ops._partial_buffer(xk.device)
+            ops.ext().gguf_gemv(xk, w.codes, w.meta, N, w.bits, w.group, 2, S, buf, N, 0, ops._NO_PUSH, 0)
+            i[0] += 1
+
+        for label, fn in (("stream", gemv), ("stream_partial", partial), ("warp_task_partial", warp_task),
+                          ("cta_staged", old)):
             # back-to-back launches in one CUDA graph: the device time of the kernel alone
             ms = time_graph(fn, calls=2 * reps)
             row[label + "_us"] = round(ms * 1e3, 2)
@@ -245,18 +253,16 @@ def gguf_gemv_suite(M=8):
 
 
 def gguf_one(N=4096, K=4096, M=8, kind="q4_k"):
-    """A few launches of each GGUF decode kernel on one shape (a small case for a profiler):
-    three warm-up rounds, then one launch each of the partial GEMV and the CTA-staged kernel.
-    Twelve weight copies rotate so the timed launches stream from HBM."""
+    """A few launches of the stream-K GGUF GEMV on one shape (a small case for a profiler): four
+    rounds of one partial-output and one direct-output launch. Twelve weight copies rotate so
+    every launch streams from HBM."""
     from b200serve.models.gguf_gpu import to_quant_weight
     ws = [to_quant_weight(torch.randn(N, K, device="cuda") * 0.02, kind) for _ in range(12)]
     x = torch.randn(M, K, device="cuda").bfloat16()
     y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
     for i in range(4):
-        w = ws[i % 12]
-        ops.qlinear_partial(x, w)
-        w = ws[(i + 6) % 12]
-        ops.ext().gguf_gemm(x, w.codes, w.meta, N, w.bits, w.group, y)
+        ops.qlinear_partial(x, ws[i % 12])
+        ops.linear(x, ws[(i + 6) % 12], out=y)
     torch.cuda.synchronize()
     print(json.dumps({"case": "gguf_one", "N": N, "K": K, "M": M, "type": kind, "ok": True}))
 

@@ -113,21 +113,60 @@ def _quant_pair(N, K, seed=0):
 
 
 @pytest.mark.parametrize("M", [1, 5, 8, 13, 16])
-def test_gguf_gemv_modes_vs_fp32(M):
+@pytest.mark.parametrize("N,K", [(384, 1024), (4224, 768), (11264, 512), (400, 512)])
+def test_gguf_stream_modes_vs_fp32(M, N, K):
+    """Stream-K GEMV: bf16 and fp32 outputs (slices shared by several warps are finished by the
+    last to arrive), and fp32 partials summed by the RMSNorm, against fp32 PyTorch; repeated
+    launches give bit-identical results."""
     from b200serve import ops
-    N, K = 384, 1024
     x = torch.randn(M, K, device="cuda").bfloat16()
     for qw, ref in _quant_pair(N, K).values():
         y_ref = x.float().cpu() @ ref.t()
-        y = ops.linear(x, qw)                                       # S = 1, bf16
+        y = ops.linear(x, qw)
         assert ((y.float().cpu() - y_ref).norm() / y_ref.norm()).item() < 1e-2
-        y32 = ops.linear(x, qw, epilogue=ops.EPI_F32)               # S = 1, fp32 (logits)
+        assert torch.equal(y, ops.linear(x, qw))
+        y32 = ops.linear(x, qw, epilogue=ops.EPI_F32)
         assert y32.dtype == torch.float32 and ((y32.cpu() - y_ref).norm() / y_ref.norm()).item() < 1e-2
-        pp = ops.qlinear_partial(x, qw)                             # K split, summed by the norm
+        pp = ops.qlinear_partial(x, qw)
+        if N % 128:
+            assert pp is None                              # partials need 128-column tiles
+            continue
+        assert pp.plan[3] == 128
         nw = torch.ones(N, device="cuda").bfloat16()
         yn = ops.rmsnorm(pp, nw, 1e-6)
         r = y_ref * torch.rsqrt(y_ref.pow(2).mean(-1, keepdim=True) + 1e-6)
         assert ((yn.float().cpu() - r).norm() / r.norm()).item() < 2e-2
+    _, counters, _ = ops._gguf_scratch(x.device)
+    assert int(counters.abs().sum()) == 0                  # every arrival counter reset, no error
+
+
+def test_gguf_stream_mixed_group_and_push():
+    """A q | k | v group with Q4_K and Q6_K parts streams as one job (partials summed per column);
+    the push mode stores bf16 tiles into a flag-free slot (world of one)."""
+    from b200serve import ops
+    from b200serve.models import gguf as G
+    K, M = 1024, 8
+    q, qref = _quant_pair(512, K, seed=5)[G.GGML_Q4_K]
+    k, kref = _quant_pair(128, K, seed=6)[G.GGML_Q4_K]
+    v, vref = _quant_pair(128, K, seed=7)[G.GGML_Q6_K]
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    pp = ops.qlinear_partial(x, G.QuantGroup([q, k, v]))
+    ref = torch.cat([x.float().cpu() @ r.t() for r in (qref, kref, vref)], 1)
+    got = torch.empty(M, 768)
+    part = pp.part.cpu()
+    kb, workers, items, tile = pp.plan
+    slot = M * 768
+    for col in range(768):
+        t = col // tile
+        first = ((t * kb + 1) * workers + items - 1) // items - 1
+        last = ((t + 1) * kb * workers + items - 1) // items - 1
+        got[:, col] = sum(part[s * slot: (s + 1) * slot].view(M, 768)[:, col] for s in range(last - first + 1))
+    assert ((got - ref).norm() / ref.norm()).item() < 1e-2
+    slot_buf = torch.full((M, 512), -1, dtype=torch.int16, device="cuda").view(torch.bfloat16)   # 0xFFFF: empty
+    ptrs = torch.tensor([slot_buf.data_ptr()], dtype=torch.int64)
+    ops.gguf_stream(x, [q], 4, None, 512, ptrs, 0)
+    torch.cuda.synchronize()
+    assert ((slot_buf.float().cpu() - x.float().cpu() @ qref.t()).norm() / (x.float().cpu() @ qref.t()).norm()) < 1e-2
 
 
 def test_gguf_group_partial_swiglu_and_packed_dequant():

@@ -457,8 +457,8 @@ def test_stream_k_partial_gemm_into_rmsnorm(M, N, K):
     nw = (torch.rand(N, device=dev) + 0.5).bfloat16()
     pp = ops.linear_partial(x, w)
     assert isinstance(pp, ops.PartialParts)
-    kb, ctas, total = pp.plan
-    assert ctas <= 148 and total == ((N + 127) // 128) * ((K + 63) // 64)
+    kb, ctas, total, tile = pp.plan
+    assert tile == 128 and ctas <= 148 and total == ((N + 127) // 128) * ((K + 63) // 64)
     res_out = torch.empty_like(res)
     y = ops.rmsnorm(pp, nw, 1e-6, residual=res, residual_out=res_out)
     # fp32 reference: matmul on the unpacked weight, residual add, RMSNorm
