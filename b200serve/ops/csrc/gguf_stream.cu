@@ -7,7 +7,7 @@
 // chunks, tile-major. CTA g owns the contiguous items [g*items/G, (g+1)*items/G), so every CTA
 // streams the same number of bytes whatever the shapes. Two CTAs per SM, each with one producer
 // warp and eight consumer warps:
-//   producer  fills a ring of stages with cp.async.bulk copies (no multicast): per item the
+//   producer  fills a ring of stages with cp.async.bulk copies into this CTA only: per item the
 //             codes and scales of the 8 slices plus the item's 256 activation columns of every
 //             token (rows padded by 16 bytes so the B-fragment reads hit 32 distinct banks);
 //             the weights of the first stages are requested before the dependency wait

@@ -74,7 +74,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
-// ---------------- bulk copies (no multicast) ----------------
+// ---------------- bulk copies (this CTA's shared memory only) ----------------
 // `bytes` from global `src` into this CTA's shared memory at `dst` (both 16-byte aligned, bytes a
 // multiple of 16), completing on `bar` (which expects the bytes through arrive.expect_tx).
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

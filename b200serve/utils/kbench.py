@@ -387,10 +387,15 @@ def gemm_chain_trace(layers=2, B=32):
         ok = ti[:, 0] > 0
         ti = ti[ok]
         us = lambda col, f: round(float(f(ti[:, col].double())) / 1000.0, 2)
+        tail = (ti[:, 6] - ti[:, 4]).double() / 1000.0          # last MMA issued -> CTA exit, per CTA
+        epi = (ti[:, 5] - ti[:, 4]).double() / 1000.0           # last MMA issued -> epilogue done
         rows.append({"gemm": names[i % 4], "layer": i // 4, "ctas": int(ok.sum()),
                      "entry_min": us(0, torch.min), "entry_max": us(0, torch.max),
-                     "first_data_med": us(3, torch.median), "mma_done_max": us(4, torch.max),
-                     "exit_max": us(6, torch.max)})
+                     "first_data_med": us(3, torch.median), "mma_done_med": us(4, torch.median),
+                     "mma_done_max": us(4, torch.max), "epi_done_max": us(5, torch.max),
+                     "exit_max": us(6, torch.max), "tail_med": round(float(tail.median()), 2),
+                     "tail_max": round(float(tail.max()), 2), "epi_med": round(float(epi.median()), 2),
+                     "epi_max": round(float(epi.max()), 2)})
     for r in rows:
         print(json.dumps(r))
     del g
