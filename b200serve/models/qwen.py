@@ -331,11 +331,15 @@ class Decoder:
         return self._attn_core(i, q, fb, plan)
 
     def _use_ep_a2a(self, T: int) -> bool:
-        """Token-sharded expert parallelism (all-to-all) for this step? B200_EP_MODE = a2a (always),
-        replicated (never) or auto: steps larger than the fused communicator's decode size."""
+        """Token-sharded expert parallelism (all-to-all) for this step? B200_EP_MODE = a2a (every
+        eager step), replicated (never) or auto: steps larger than the fused communicator's decode
+        size. Steps captured into a CUDA graph stay replicated: the all-to-all sizes its grouped
+        GEMMs from a host read of the exchanged counts."""
         import os
         comm, cfg = self.comm, self.cfg
         if comm.world == 1 or not hasattr(comm, "ep_moe") or cfg.is_hybrid or cfg.sandwich_norms:
+            return False
+        if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
             return False
         mode = os.environ.get("B200_EP_MODE", "auto")
         if mode == "a2a":
