@@ -417,6 +417,8 @@ class PartialParts(list):
 
 
 _PARTIAL = os.environ.get("B200_GEMM_PARTIAL", "1") != "0"
+# decode gate/up: stream-K partials summed by silu_mul_partial instead of the split-K SwiGLU epilogue
+_SWIGLU_PARTIAL = os.environ.get("B200_SWIGLU_PARTIAL", "1") != "0"
 _partial_bufs = {}
 _num_sms = {}
 
@@ -701,6 +703,15 @@ def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspac
         ext().gemm_tc_ag(x, w.data, out, bias, ws.ws, ws.counters, epilogue, w.N, ag.flags_ptr, ag.n,
                          ag.epoch_ptr)
         return out
+    if (epilogue == EPI_SWIGLU and _SWIGLU_PARTIAL and isinstance(w, PackedWeight) and bias is None
+            and residual is None and splits == 0 and x.is_cuda and w.N % 128 == 0):
+        pp = linear_partial(x, w)                  # 64-column gate/up blocks, SwiGLU while summing
+        if pp is not None:
+            I = w.N // 2
+            out = out if out is not None else torch.empty(M, I, dtype=x.dtype, device=x.device)
+            _cuda(x)
+            ext().silu_mul_partial(pp.part, *pp.plan, M, I, out, 64)
+            return out
     if isinstance(w, list):                         # QuantGroup: parts share the input
         if epilogue == EPI_SWIGLU and x.is_cuda and len(w) == 2 and w[0].N == w[1].N:
             pp = qlinear_partial(x, w)             # gate | up as partials, SwiGLU while summing
@@ -948,12 +959,13 @@ def _sample_row_dtype():
 
 
 def sample_rows(logits, temperature, top_k, top_p, min_p, seeds, steps, pen_ids=None, pen_counts=None,
-                pen_vals=None):
+                pen_vals=None, cluster=0):
     """One token per row of fp32 ``logits`` [B, V] (penalties are applied in place).
 
     Per-row lists: temperature (<= 0 = greedy), top_k (0 = off), top_p, min_p, seeds,
     steps (draw counter). pen_ids [B, P] int32 (-1 pad, unique per row), pen_counts
-    [B, P] fp32, pen_vals [B, 3] fp32 = (repeat, presence, frequency)."""
+    [B, P] fp32, pen_vals [B, 3] fp32 = (repeat, presence, frequency). ``cluster``: CTAs per
+    row (1, 2, 4 or 8; 0 = by batch size)."""
     import numpy as np
     B = logits.shape[0]
     rec = np.zeros(B, dtype=_sample_row_dtype())
@@ -967,7 +979,7 @@ def sample_rows(logits, temperature, top_k, top_p, min_p, seeds, steps, pen_ids=
         pen_vals = torch.empty(0, dtype=torch.float32, device=dev)
     out = torch.empty(B, dtype=torch.int32, device=dev)
     _cuda(logits)
-    ext().sample_rows(logits, params, pen_ids, pen_counts, pen_vals, out)
+    ext().sample_rows(logits, params, pen_ids, pen_counts, pen_vals, out, cluster)
     return out
 
 

@@ -86,25 +86,26 @@ __device__ __forceinline__ void dequant_q4_page(const uint8_t* raw, uint8_t* wor
 // TurboQuant page stage (KVQ == 2), per (page, kv head):
 //   K codes [16][64] (one 4-bit index per dim, byte m = dims 2m | 2m+1 << 4) | K QJL signs [16][16]
 //   (bit i = sign of row i of S r) | K (norm, gamma) [16][2] fp16 | V codes [16][64] | V norm [16] fp16.
-// Scores run in the rotated domain over a 256-dim virtual key: [n u_hat | n gamma s] against the
-// query [H q | S H q], so the QJL correction is one more MMA k-range instead of a per-key transform.
+// Scores run in the rotated domain over a 256-dim virtual key: [u_hat | s] against the query
+// [H q | S H q]; the two halves accumulate separately and combine per token as
+// n (q.u_hat) + n gamma (qj.s), so the per-token norms never touch the tiles. V tiles hold the
+// unscaled code values; each token's V norm scales its softmax weight instead.
 constexpr int kTqKCodes = 0, kTqKSign = 1024, kTqKMeta = 1280, kTqVCodes = 1344, kTqVMeta = 2368;
 constexpr int kTqRaw = 2400;
-constexpr int kTqLut = 2 * 256 * 4;                 // pair tables (bf16x2 per code byte) for K and V
+// pair tables (bf16x2 per code byte) for K and V, then the sign table: byte of 8 sign bits ->
+// 8 bf16 of +-1 (uint4)
+constexpr int kTqLut = 2 * 256 * 4 + 256 * 16;
 
-// Dequantise one TurboQuant page into the work stage: K_hat (boxes 0-1), K_sgn (boxes 2-3), V (4-5).
-// Lane l converts row l/2, dims [64*(l&1), +64).
+// Expand one TurboQuant page into the work stage: code values of K (boxes 0-1), +-1 signs of K
+// (boxes 2-3), code values of V (4-5), all by table lookup. Lane l converts row l/2, dims
+// [64*(l&1), +64).
 __device__ __forceinline__ void dequant_tq_page(const uint8_t* raw, uint8_t* work, int lane, const uint32_t* lutk,
-                                                const uint32_t* lutv) {
+                                                const uint32_t* lutv, const uint4* lutg) {
   const int row = lane >> 1, half = lane & 1;
-  const __half* km = reinterpret_cast<const __half*>(raw + kTqKMeta);
-  const float kn = __half2float(km[row * 2]), kg = __half2float(km[row * 2 + 1]);
-  const float vn = __half2float(reinterpret_cast<const __half*>(raw + kTqVMeta)[row]);
 #pragma unroll
   for (int kv = 0; kv < 2; ++kv) {
     const uint4* src = reinterpret_cast<const uint4*>(raw + (kv ? kTqVCodes : kTqKCodes) + row * 64 + half * 32);
     const uint32_t* lut = kv ? lutv : lutk;
-    const uint32_t n2 = pack_bf16x2(kv ? vn : kn, kv ? vn : kn);
     uint8_t* dst = work + (kv ? 4 : 0) * kBoxBytes;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
@@ -112,31 +113,17 @@ __device__ __forceinline__ void dequant_tq_page(const uint8_t* raw, uint8_t* wor
       const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
-        uint32_t r[4];
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const uint32_t e = lut[(wv[w] >> (8 * p)) & 255u];
-          asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r[p]) : "r"(e), "r"(n2));
-        }
-        *reinterpret_cast<uint4*>(dst + swz(row, half * 8 + j * 4 + w)) = make_uint4(r[0], r[1], r[2], r[3]);
+        const uint4 r = make_uint4(lut[wv[w] & 255u], lut[(wv[w] >> 8) & 255u], lut[(wv[w] >> 16) & 255u],
+                                   lut[wv[w] >> 24]);
+        *reinterpret_cast<uint4*>(dst + swz(row, half * 8 + j * 4 + w)) = r;
       }
     }
   }
-  // K_sgn: +-(norm * gamma) per dim from the sign bits (bit 1 = +)
   const uint2 sb = *reinterpret_cast<const uint2*>(raw + kTqKSign + row * 16 + half * 8);
   const uint32_t bw[2] = {sb.x, sb.y};
-  const uint32_t g2 = pack_bf16x2(kn * kg, kn * kg) & 0x7fff7fffu;
 #pragma unroll
-  for (int by = 0; by < 8; ++by) {
-    const uint32_t bits = (bw[by >> 2] >> (8 * (by & 3))) & 255u;   // dims 8*by .. 8*by+7 of this half
-    uint32_t r[4];
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const uint32_t neg_lo = ((bits >> (2 * p)) & 1u) ^ 1u, neg_hi = ((bits >> (2 * p + 1)) & 1u) ^ 1u;
-      r[p] = g2 | (neg_lo << 15) | (neg_hi << 31);
-    }
-    *reinterpret_cast<uint4*>(work + swz(row, 16 + half * 8 + by)) = make_uint4(r[0], r[1], r[2], r[3]);
-  }
+  for (int by = 0; by < 8; ++by)    // dims 8*by .. 8*by+7 of this half
+    *reinterpret_cast<uint4*>(work + swz(row, 16 + half * 8 + by)) = lutg[(bw[by >> 2] >> (8 * (by & 3))) & 255u];
 }
 
 struct TqArgs {
@@ -175,11 +162,19 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcWarps * kWarpBytes) + warp * kTcStages;
   uint32_t* lutk = reinterpret_cast<uint32_t*>(smem + kTcWarps * kWarpBytes + kTcWarps * kTcStages * 8);
   uint32_t* lutv = lutk + 256;
+  uint4* lutg = reinterpret_cast<uint4*>(lutv + 256);
   if constexpr (KVQ == 2) {
     for (int e = threadIdx.x; e < 512; e += blockDim.x) {
       const float* cb = e < 256 ? tq.cbk : tq.cbv;
       const int i = e & 255;
       lutk[e] = pack_bf16x2(cb[i & 15], cb[i >> 4]);
+    }
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+      uint32_t r[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p)      // bit 1: +1 (0x3F80), bit 0: -1 (0xBF80)
+        r[p] = (((b >> (2 * p)) & 1) ? 0x3F80u : 0xBF80u) | ((((b >> (2 * p + 1)) & 1) ? 0x3F80u : 0xBF80u) << 16);
+      lutg[b] = make_uint4(r[0], r[1], r[2], r[3]);
     }
     __syncthreads();
   }
@@ -265,7 +260,7 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
     if constexpr (KVQ == 0) {
       kbase = tc::smem_u32(ring + s * kStageBytes);
     } else if constexpr (KVQ == 2) {
-      dequant_tq_page(ring + s * kTqRaw, work, lane, lutk, lutv);
+      dequant_tq_page(ring + s * kTqRaw, work, lane, lutk, lutv, lutg);
       __syncwarp();
       kbase = tc::smem_u32(work);
     } else {
@@ -276,9 +271,12 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
     const uint32_t vbase = kbase + (KVQ == 2 ? 4 : 2) * kBoxBytes;
     const int tok0 = first + i * kTcWarps * 16;
     // ---- S^T [heads x 16 tokens] ----
-    float sc[2][4];
+    float sc[2][4], sg[2][4];
 #pragma unroll
-    for (int nb = 0; nb < 2; ++nb) sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
+    for (int nb = 0; nb < 2; ++nb) {
+      sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
+      sg[nb][0] = sg[nb][1] = sg[nb][2] = sg[nb][3] = 0.f;
+    }
 #pragma unroll
     for (int kk = 0; kk < KSTEPS; ++kk) {
       // matrices: (tok 0-7, chunk 2kk), (tok 0-7, chunk 2kk+1), (tok 8-15, 2kk), (tok 8-15, 2kk+1)
@@ -286,8 +284,24 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
       const int tok = (mi >> 1) * 8 + r;
       uint32_t kf[4];
       ldsm_x4(kf, kbase + swz(tok, kk * 2 + (mi & 1)));
-      mma16816(sc[0], qa[kk], kf[0], kf[1]);
-      mma16816(sc[1], qa[kk], kf[2], kf[3]);
+      float (*acc)[4] = (KVQ == 2 && kk >= 8) ? sg : sc;      // TurboQuant: QJL half apart
+      mma16816(acc[0], qa[kk], kf[0], kf[1]);
+      mma16816(acc[1], qa[kk], kf[2], kf[3]);
+    }
+    float vn[2][2];                                           // TurboQuant: V norm of this lane's tokens
+    if constexpr (KVQ == 2) {
+      const __half* km = reinterpret_cast<const __half*>(ring + s * kTqRaw + kTqKMeta);
+      const __half* vm = reinterpret_cast<const __half*>(ring + s * kTqRaw + kTqVMeta);
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int tk = nb * 8 + 2 * t4 + e;
+          const float n = __half2float(km[tk * 2]), ng = n * __half2float(km[tk * 2 + 1]);
+          sc[nb][e] = n * sc[nb][e] + ng * sg[nb][e];
+          sc[nb][2 + e] = n * sc[nb][2 + e] + ng * sg[nb][2 + e];
+          vn[nb][e] = __half2float(vm[tk]);
+        }
     }
     // ---- online softmax over the 16 tokens (log2 domain) ----
     float mx_a = -INFINITY, mx_b = -INFINITY;
@@ -319,8 +333,13 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
       const float p2 = exp2f(sc[nb][2] - base_b), p3 = exp2f(sc[nb][3] - base_b);
       ps_a += p0 + p1;
       ps_b += p2 + p3;
-      pa[nb * 2 + 0] = pack_bf16x2(p0, p1);
-      pa[nb * 2 + 1] = pack_bf16x2(p2, p3);
+      if constexpr (KVQ == 2) {      // V rows hold code values: the token's V norm scales its weight
+        pa[nb * 2 + 0] = pack_bf16x2(p0 * vn[nb][0], p1 * vn[nb][1]);
+        pa[nb * 2 + 1] = pack_bf16x2(p2 * vn[nb][0], p3 * vn[nb][1]);
+      } else {
+        pa[nb * 2 + 0] = pack_bf16x2(p0, p1);
+        pa[nb * 2 + 1] = pack_bf16x2(p2, p3);
+      }
     }
     ps_a += __shfl_xor_sync(0xffffffffu, ps_a, 1);
     ps_a += __shfl_xor_sync(0xffffffffu, ps_a, 2);
@@ -328,9 +347,11 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
     ps_b += __shfl_xor_sync(0xffffffffu, ps_b, 2);
     l_a = l_a * al_a + ps_a;
     l_b = l_b * al_b + ps_b;
+    if (__any_sync(0xffffffffu, al_a != 1.f || al_b != 1.f)) {   // skipped while the maxima hold
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      o[j][0] *= al_a; o[j][1] *= al_a; o[j][2] *= al_b; o[j][3] *= al_b;
+      for (int j = 0; j < 16; ++j) {
+        o[j][0] *= al_a; o[j][1] *= al_a; o[j][2] *= al_b; o[j][3] *= al_b;
+      }
     }
     // ---- O [heads x 128] += P [heads x 16] . V [16 x 128] ----
 #pragma unroll

@@ -25,7 +25,7 @@ void gguf_gemv(torch::Tensor x, torch::Tensor codes, torch::Tensor meta, int64_t
                int64_t mode, int64_t S, torch::Tensor out, int64_t ldo, int64_t col0, torch::Tensor push_ptrs,
                int64_t mc_ptr);
 void silu_mul_partial(torch::Tensor part, int64_t kb, int64_t ctas, int64_t total, int64_t tile, int64_t M, int64_t I,
-                      torch::Tensor out);
+                      torch::Tensor out, int64_t inter);
 std::vector<int64_t> gguf_stream_plan(int64_t N, int64_t K, int64_t num_sms);
 std::vector<int64_t> gguf_stream(torch::Tensor x, std::vector<torch::Tensor> codes, std::vector<torch::Tensor> metas,
                                  std::vector<int64_t> ns, std::vector<int64_t> bits, std::vector<int64_t> groups,
@@ -106,7 +106,7 @@ void gemm_grouped(torch::Tensor act, torch::Tensor w_packed, int64_t N, int64_t 
 void argmax_rows(torch::Tensor logits, torch::Tensor out_idx, torch::Tensor out_val, int64_t index_offset);
 void argmax_merge(torch::Tensor vals, torch::Tensor idx, torch::Tensor out);
 void sample_rows(torch::Tensor logits, torch::Tensor params, torch::Tensor pen_ids, torch::Tensor pen_counts,
-                 torch::Tensor pen_vals, torch::Tensor out);
+                 torch::Tensor pen_vals, torch::Tensor out, int64_t cluster);
 
 void paged_decode_attention_tq(torch::Tensor q_rot, torch::Tensor q_jl, torch::Tensor k_codes, torch::Tensor k_sign,
                                torch::Tensor k_meta, torch::Tensor v_codes, torch::Tensor v_meta,
@@ -179,7 +179,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_count", &ep_count);
   m.def("ep_dispatch", &ep_dispatch);
   m.def("gguf_dequant_packed", &gguf_dequant_packed);
-  m.def("silu_mul_partial", &silu_mul_partial);
+  m.def("silu_mul_partial", &silu_mul_partial, py::arg("part"), py::arg("kb"), py::arg("ctas"), py::arg("total"),
+        py::arg("tile"), py::arg("M"), py::arg("I"), py::arg("out"), py::arg("inter") = 0);
   m.def("gguf_stream_plan", &gguf_stream_plan);
   m.def("gguf_stream", &gguf_stream);
   m.def("gemm_tc_partial", &gemm_tc_partial);
@@ -232,7 +233,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped", &gemm_grouped);
   m.def("argmax_rows", &argmax_rows);
   m.def("argmax_merge", &argmax_merge);
-  m.def("sample_rows", &sample_rows);
+  m.def("sample_rows", &sample_rows, py::arg("logits"), py::arg("params"), py::arg("pen_ids"), py::arg("pen_counts"),
+        py::arg("pen_vals"), py::arg("out"), py::arg("cluster") = 0);
   m.def("paged_decode_attention_tq", &paged_decode_attention_tq);
   m.def("tq_qkv", &tq_qkv);
   m.def("tq_dequant", &tq_dequant);

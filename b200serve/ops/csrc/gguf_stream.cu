@@ -431,16 +431,20 @@ __global__ void __launch_bounds__(kGsThreads, 2) gguf_stream_kernel(const GsArgs
   }
 }
 
-// act[t][i] = silu(gate) * up from the fp32 partial slots (PartialIn) of a [gate | up] output of
-// width 2I, each rounded to bf16 first as a bf16 gate/up projection would be.
-__global__ void silu_mul_partial_kernel(const PartialIn pi, int M, int I, __nv_bfloat16* __restrict__ out) {
+// act[t][i] = silu(gate) * up from the fp32 partial slots (PartialIn) of a gate/up output of
+// width 2I, each rounded to bf16 first as a bf16 gate/up projection would be. inter == 0: the
+// columns are [gate | up]; inter == 64: blocks of 64 gate columns then 64 up columns (the
+// interleaved gate/up weight of the tcgen05 GEMM).
+__global__ void silu_mul_partial_kernel(const PartialIn pi, int M, int I, int inter, __nv_bfloat16* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= M * I) return;
   const int t = idx / I, i = idx % I;
-  const float gr = __bfloat162float(__float2bfloat16_rn(partial_col(pi, t, i)));
-  const float ur = __bfloat162float(__float2bfloat16_rn(partial_col(pi, t, I + i)));
+  const int gc = inter ? (i / inter) * 2 * inter + i % inter : i;
+  const int uc = inter ? gc + inter : I + i;
+  const float gr = __bfloat162float(__float2bfloat16_rn(partial_col(pi, t, gc)));
+  const float ur = __bfloat162float(__float2bfloat16_rn(partial_col(pi, t, uc)));
   const float sg = __bfloat162float(__float2bfloat16_rn(gr / (1.f + __expf(-gr))));
   out[(size_t)t * I + i] = __float2bfloat16_rn(sg * ur);
 }
@@ -562,13 +566,15 @@ std::vector<int64_t> gguf_stream(torch::Tensor x, std::vector<torch::Tensor> cod
   return plan;
 }
 
-// out [M, I] = silu(gate) * up from the fp32 partial slots of a [gate | up] group (width 2I).
+// out [M, I] = silu(gate) * up from the fp32 partial slots of a gate/up output (width 2I; inter
+// 0: [gate | up], 64: 64-column gate/up blocks).
 void silu_mul_partial(torch::Tensor part, int64_t kb, int64_t ctas, int64_t total, int64_t tile, int64_t M, int64_t I,
-                      torch::Tensor out) {
+                      torch::Tensor out, int64_t inter) {
   TORCH_CHECK(part.scalar_type() == at::kFloat && out.scalar_type() == at::kBFloat16 && out.is_contiguous());
   TORCH_CHECK(tile == 16 || tile == 128, "partial tiles are 16 or 128 columns wide");
+  TORCH_CHECK(inter == 0 || (inter == 64 && I % 64 == 0), "inter: 0 or 64 (I % 64 == 0)");
   PartialIn pi{part.data_ptr<float>(), (int)kb, (int)ctas, (long long)total, (int)M, (int)(2 * I), (int)tile};
   const int n = (int)(M * I);
   launch_pdl(silu_mul_partial_kernel, dim3((n + 255) / 256), dim3(256), 0, at::cuda::getCurrentCUDAStream(), pi, (int)M,
-             (int)I, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+             (int)I, (int)inter, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
 }

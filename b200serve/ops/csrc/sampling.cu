@@ -163,6 +163,8 @@ struct SampShared {
   } u;
   uint32_t tot_cnt[kSBins];
   float tot_mass[kSBins];
+  uint32_t g_cnt[kSBins];      // cluster sums of tot_* (several CTAs per row)
+  float g_mass[kSBins];
   float red[32];
   int redi[32];
   float wmin[32];
@@ -170,24 +172,52 @@ struct SampShared {
   int n[4];
 };
 
-// Calls f(x, i) for every element of the row (float4 loads when aligned).
+// This CTA's share of a row: [lo, hi), lo a multiple of 4.
+struct Slice {
+  int lo, hi;
+};
+
+// Calls f(x, i) for every element of the slice (float4 loads when aligned).
 template <class F>
-__device__ __forceinline__ void for_row(const float* row, int V, bool vec, F&& f) {
-  const int V4 = vec ? V / 4 : 0;
-  for (int q = threadIdx.x; q < V4; q += blockDim.x) {
-    const float4 v = reinterpret_cast<const float4*>(row)[q];
-    f(v.x, 4 * q);
-    f(v.y, 4 * q + 1);
-    f(v.z, 4 * q + 2);
-    f(v.w, 4 * q + 3);
+__device__ __forceinline__ void for_row(const float* row, Slice sl, bool vec, F&& f) {
+  const int n4 = vec ? (sl.hi - sl.lo) / 4 : 0;
+  const float4* r4 = reinterpret_cast<const float4*>(row + sl.lo);
+  for (int q = threadIdx.x; q < n4; q += blockDim.x) {
+    const float4 v = r4[q];
+    const int i = sl.lo + 4 * q;
+    f(v.x, i);
+    f(v.y, i + 1);
+    f(v.z, i + 2);
+    f(v.w, i + 3);
   }
-  for (int i = V4 * 4 + threadIdx.x; i < V; i += blockDim.x) f(row[i], i);
+  for (int i = sl.lo + n4 * 4 + threadIdx.x; i < sl.hi; i += blockDim.x) f(row[i], i);
+}
+
+// ---- thread-block cluster helpers (C CTAs share one row) ----
+__device__ __forceinline__ void cl_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cl_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+               : "=r"(r)
+               : "r"((uint32_t)__cvta_generic_to_shared(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ uint32_t cl_ld_u32(const void* p, uint32_t rank) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(cl_addr(p, rank)) : "memory");
+  return v;
+}
+__device__ __forceinline__ float cl_ld_f32(const void* p, uint32_t rank) {
+  return __uint_as_float(cl_ld_u32(p, rank));
 }
 
 // Histogram of the surviving tokens' d: level 1 (bsel < 0) over bin1 with scale s1, level 2
 // over the sub-bins of bin1 == bsel. Counts are aggregated per warp (match_any), masses use
 // per-warp shared atomics. Leaves totals in S.tot_cnt / S.tot_mass.
-__device__ void d_histogram(const float* row, int V, bool vec, float m, float inv_t, const DPred& P, float s1,
+template <int C>
+__device__ void d_histogram(const float* row, Slice sl, bool vec, float m, float inv_t, const DPred& P, float s1,
                             int bsel, float lo2, float s2, SampShared& S) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < kSWarps * kSBins; i += blockDim.x) {
@@ -197,7 +227,7 @@ __device__ void d_histogram(const float* row, int V, bool vec, float m, float in
   __syncthreads();
   uint32_t* cnt = S.u.h.cnt[warp];
   float* mass = S.u.h.mass[warp];
-  for_row(row, V, vec, [&](float x, int) {
+  for_row(row, sl, vec, [&](float x, int) {
     const float d = (m - x) * inv_t;
     int b = -1;
     if (dkeep(d, P)) {
@@ -224,6 +254,26 @@ __device__ void d_histogram(const float* row, int V, bool vec, float m, float in
     S.tot_mass[b] = w;
   }
   __syncthreads();
+  if constexpr (C > 1) {
+    // every CTA of the row sums the C local histograms in rank order (same totals everywhere)
+    cl_sync();
+    for (int b = threadIdx.x; b < kSBins; b += blockDim.x) {
+      uint32_t c = 0;
+      float w = 0.f;
+      for (int r = 0; r < C; ++r) {
+        c += cl_ld_u32(&S.tot_cnt[b], (uint32_t)r);
+        w += cl_ld_f32(&S.tot_mass[b], (uint32_t)r);
+      }
+      S.g_cnt[b] = c;
+      S.g_mass[b] = w;
+    }
+    cl_sync();                    // no CTA overwrites its totals while another still reads them
+    for (int b = threadIdx.x; b < kSBins; b += blockDim.x) {
+      S.tot_cnt[b] = S.g_cnt[b];
+      S.tot_mass[b] = S.g_mass[b];
+    }
+    __syncthreads();
+  }
 }
 
 // Warp 0: first bin whose inclusive cumulative count (MASS: mass) reaches the target, which is
@@ -299,7 +349,7 @@ __device__ __forceinline__ float gumbel(int i, uint32_t step, uint32_t row, uint
 // (keep j while the mass before it is <= target; target = top_p * mass of the top-k
 // survivors when mass_target < 0), then the Gumbel-max draw. Returns the vocabulary id.
 __device__ int finish_candidates(int n, int top_k, float top_p, float mass_target, float m, float inv_t,
-                                 uint32_t step, uint2 key, SampShared& S) {
+                                 uint32_t step, uint2 key, int rowid, SampShared& S) {
   int N2 = 32;
   while (N2 < n) N2 <<= 1;
   for (int i = n + threadIdx.x; i < N2; i += blockDim.x) { S.u.c.v[i] = -INFINITY; S.u.c.i[i] = 0x7fffffff; }
@@ -362,12 +412,36 @@ __device__ int finish_candidates(int n, int top_k, float top_p, float mass_targe
   int bi = 0x7fffffff;
   for (int j = threadIdx.x; j < keep; j += blockDim.x) {
     const int id = S.u.c.i[j];
-    better(bv, bi, S.u.c.v[j] * inv_t + gumbel(id, step, blockIdx.x, key), id);
+    better(bv, bi, S.u.c.v[j] * inv_t + gumbel(id, step, (uint32_t)rowid, key), id);
   }
   block_best(bv, bi, S);
   return bi;
 }
 
+// Cluster-wide (value, index) best and minimum: each CTA publishes its own in S.red/S.redi/S.wmin
+// slot 0..2, then every CTA combines the C entries in rank order.
+template <int C>
+__device__ __forceinline__ void cl_best(float& bv, int& bi, float& mn, SampShared& S) {
+  if constexpr (C > 1) {
+    if (threadIdx.x == 0) { S.f[1] = bv; S.n[1] = bi; S.f[3] = mn; }
+    cl_sync();
+    float v = -INFINITY, m2 = INFINITY;
+    int ix = 0x7fffffff;
+    for (int r = 0; r < C; ++r) {
+      better(v, ix, cl_ld_f32(&S.f[1], (uint32_t)r), (int)cl_ld_u32(&S.n[1], (uint32_t)r));
+      m2 = fminf(m2, cl_ld_f32(&S.f[3], (uint32_t)r));
+    }
+    cl_sync();
+    bv = v;
+    bi = ix;
+    mn = m2;
+  }
+}
+
+// C CTAs per row (a thread-block cluster when C > 1): CTA rank r of row b works on the slice
+// [r*V/C, (r+1)*V/C) (multiples of 4); histograms, maxima and candidate sets are merged through
+// distributed shared memory, and rank 0 finishes the draw.
+template <int C>
 __global__ void __launch_bounds__(kSThreads) sample_rows_kernel(float* __restrict__ logits, int V, int ld,
                                                                 const SampleRow* __restrict__ params,
                                                                 const int* __restrict__ pen_ids,
@@ -375,19 +449,24 @@ __global__ void __launch_bounds__(kSThreads) sample_rows_kernel(float* __restric
                                                                 const float* __restrict__ pen_vals,
                                                                 int* __restrict__ out) {
   __shared__ SampShared S;
-  float* row = logits + (size_t)blockIdx.x * ld;
+  pdl_wait();                       // the logits come from the previous kernel
+  pdl_trigger();
+  const int rowid = blockIdx.x / C, rank = blockIdx.x % C;
+  float* row = logits + (size_t)rowid * ld;
   const bool vec = ((reinterpret_cast<uintptr_t>(row) & 15) == 0) && (ld & 3) == 0;
-  const SampleRow pr = params[blockIdx.x];
-  // ---- penalties (ids unique per row): repetition, presence, frequency ----
+  Slice sl;
+  sl.lo = C == 1 ? 0 : ((int)((long long)V * rank / C) & ~3);
+  sl.hi = C == 1 ? V : (rank == C - 1 ? V : ((int)((long long)V * (rank + 1) / C) & ~3));
+  const SampleRow pr = params[rowid];
+  // ---- penalties (ids unique per row) on this CTA's slice: repetition, presence, frequency ----
   if (P > 0) {
-    const float rp = pen_vals[blockIdx.x * 3 + 0], pres = pen_vals[blockIdx.x * 3 + 1],
-                freq = pen_vals[blockIdx.x * 3 + 2];
+    const float rp = pen_vals[rowid * 3 + 0], pres = pen_vals[rowid * 3 + 1], freq = pen_vals[rowid * 3 + 2];
     for (int j = threadIdx.x; j < P; j += blockDim.x) {
-      const int id = pen_ids[blockIdx.x * P + j];
-      if (id < 0 || id >= V) continue;
+      const int id = pen_ids[rowid * P + j];
+      if (id < sl.lo || id >= sl.hi) continue;
       float x = row[id];
       if (rp != 1.f) x = x > 0.f ? x / rp : x * rp;
-      x -= pres + freq * pen_counts[blockIdx.x * P + j];
+      x -= pres + freq * pen_counts[rowid * P + j];
       row[id] = x;
     }
     __syncthreads();
@@ -395,19 +474,22 @@ __global__ void __launch_bounds__(kSThreads) sample_rows_kernel(float* __restric
   // ---- row max (the greedy answer) and min ----
   float bv = -INFINITY, mn = INFINITY;
   int bi = 0x7fffffff;
-  for_row(row, V, vec, [&](float x, int i) { better(bv, bi, x, i); mn = fminf(mn, x); });
+  for_row(row, sl, vec, [&](float x, int i) { better(bv, bi, x, i); mn = fminf(mn, x); });
   mn = -warp_max(-mn);
   if ((threadIdx.x & 31) == 0) S.wmin[threadIdx.x >> 5] = mn;
   block_best(bv, bi, S);
+  float xmin = INFINITY;
+  __syncthreads();
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) xmin = fminf(xmin, S.wmin[w]);
+  __syncthreads();
+  cl_best<C>(bv, bi, xmin, S);
   if (threadIdx.x == 0) { S.f[0] = bv; S.n[0] = bi; }
   __syncthreads();
   const float m = S.f[0];
   const int greedy = S.n[0];
-  float xmin = INFINITY;
-  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) xmin = fminf(xmin, S.wmin[w]);
   __syncthreads();
   if (!(pr.temperature > 0.f)) {
-    if (threadIdx.x == 0) out[blockIdx.x] = greedy;
+    if (threadIdx.x == 0 && rank == 0) out[rowid] = greedy;
     return;
   }
   const float inv_t = 1.f / pr.temperature;
@@ -428,7 +510,7 @@ __global__ void __launch_bounds__(kSThreads) sample_rows_kernel(float* __restric
       const bool mass = stage == 1;
       if (mass ? !use_p : !use_k) continue;
       const float s1 = (float)kSBins / R;
-      d_histogram(row, V, vec, m, inv_t, Pd, s1, -1, 0.f, 0.f, S);
+      d_histogram<C>(row, sl, vec, m, inv_t, Pd, s1, -1, 0.f, 0.f, S);
       if (mass) d_find<true>(0.f, pr.top_p, S);
       else d_find<false>((float)pr.top_k, -1.f, S);
       const int b1 = S.n[0];
@@ -445,7 +527,7 @@ __global__ void __launch_bounds__(kSThreads) sample_rows_kernel(float* __restric
         break;
       }
       const float lo2 = (float)b1 / s1, s2 = s1 * (float)kSBins;
-      d_histogram(row, V, vec, m, inv_t, Pd, s1, b1, lo2, s2, S);
+      d_histogram<C>(row, sl, vec, m, inv_t, Pd, s1, b1, lo2, s2, S);
       if (mass) d_find<true>(tgt - before1, -1.f, S);   // the mass still needed inside bin b1
       else d_find<false>((float)pr.top_k - before1, -1.f, S);
       t.lo2 = lo2;
@@ -459,7 +541,7 @@ __global__ void __launch_bounds__(kSThreads) sample_rows_kernel(float* __restric
       if (threadIdx.x == 0) S.n[2] = 0;
       __syncthreads();
       const int lane = threadIdx.x & 31;
-      for_row(row, V, vec, [&](float x, int i) {
+      for_row(row, sl, vec, [&](float x, int i) {
         const bool k = dkeep((m - x) * inv_t, Pd);
         const unsigned act = __activemask();
         const unsigned bal = __ballot_sync(act, k);
@@ -473,23 +555,41 @@ __global__ void __launch_bounds__(kSThreads) sample_rows_kernel(float* __restric
         }
       });
       __syncthreads();
-      const int n = min(S.n[2], kSCand);
+      int n = min(S.n[2], kSCand);
+      if constexpr (C > 1) {
+        // rank 0 appends the other CTAs' candidates (the global count is <= kSCand)
+        cl_sync();
+        if (rank == 0) {
+          for (int r = 1; r < C; ++r) {
+            const int nr = min((int)cl_ld_u32(&S.n[2], (uint32_t)r), kSCand);
+            for (int j = threadIdx.x; j < nr && n + j < kSCand; j += blockDim.x) {
+              S.u.c.v[n + j] = cl_ld_f32(&S.u.c.v[j], (uint32_t)r);
+              S.u.c.i[n + j] = (int)cl_ld_u32(&S.u.c.i[j], (uint32_t)r);
+            }
+            n = min(kSCand, n + nr);
+          }
+        }
+        cl_sync();                  // the other CTAs keep their shared memory until rank 0 has read it
+        if (rank != 0) return;
+      }
       __syncthreads();
-      result = finish_candidates(n, exact_k, use_p ? pr.top_p : 1.f, mass_target, m, inv_t, pr.step, key, S);
+      result = finish_candidates(n, exact_k, use_p ? pr.top_p : 1.f, mass_target, m, inv_t, pr.step, key, rowid, S);
     }
   }
   if (result < 0) {
     // ---- Gumbel-max draw over every surviving token ----
-    float best = -INFINITY;
+    float best = -INFINITY, unused = INFINITY;
     int best_i = 0x7fffffff;
-    for_row(row, V, vec, [&](float x, int i) {
+    for_row(row, sl, vec, [&](float x, int i) {
       if (!dkeep((m - x) * inv_t, Pd)) return;
-      better(best, best_i, x * inv_t + gumbel(i, pr.step, blockIdx.x, key), i);
+      better(best, best_i, x * inv_t + gumbel(i, pr.step, (uint32_t)rowid, key), i);
     });
     block_best(best, best_i, S);
+    __syncthreads();
+    cl_best<C>(best, best_i, unused, S);
     result = best_i;
   }
-  if (threadIdx.x == 0) out[blockIdx.x] = result == 0x7fffffff ? greedy : result;
+  if (threadIdx.x == 0 && rank == 0) out[rowid] = result == 0x7fffffff ? greedy : result;
 }
 
 }  // namespace b200
@@ -498,15 +598,38 @@ __global__ void __launch_bounds__(kSThreads) sample_rows_kernel(float* __restric
 // (temperature bits, top_p bits, min_p bits, top_k, seed, step); pen_ids [B, P] int32 (-1 pad),
 // pen_counts [B, P] fp32, pen_vals [B, 3] fp32 (repeat, presence, frequency).
 void sample_rows(torch::Tensor logits, torch::Tensor params, torch::Tensor pen_ids, torch::Tensor pen_counts,
-                 torch::Tensor pen_vals, torch::Tensor out) {
+                 torch::Tensor pen_vals, torch::Tensor out, int64_t cluster) {
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1);
   TORCH_CHECK(params.scalar_type() == at::kByte && params.numel() == logits.size(0) * (int64_t)sizeof(b200::SampleRow));
   const int B = logits.size(0), V = logits.size(1);
   if (B == 0) return;
   const int P = pen_ids.numel() ? pen_ids.size(1) : 0;
-  b200::sample_rows_kernel<<<B, b200::kSThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      logits.data_ptr<float>(), V, logits.stride(0), reinterpret_cast<const b200::SampleRow*>(params.data_ptr()),
-      P ? pen_ids.data_ptr<int>() : nullptr, P ? pen_counts.data_ptr<float>() : nullptr, P,
-      P ? pen_vals.data_ptr<float>() : nullptr, out.data_ptr<int>());
-  B200_CHECK_CUDA(cudaGetLastError());
+  // CTAs per row: a thread-block cluster splits each row so that small batches still fill the SMs
+  static int cl = -1;
+  if (cl < 0) {
+    const char* e = getenv("B200_SAMPLER_CLUSTER");
+    cl = e ? atoi(e) : 0;
+  }
+  int C = cluster > 0 ? (int)cluster : cl > 0 ? cl : (B <= 18 ? 8 : B <= 74 ? 4 : 1);
+  if (C != 1 && C != 2 && C != 4 && C != 8) C = 4;
+  if (V < 4096 * C) C = 1;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto lp = reinterpret_cast<const b200::SampleRow*>(params.data_ptr());
+  const int* pi = P ? pen_ids.data_ptr<int>() : nullptr;
+  const float* pc = P ? pen_counts.data_ptr<float>() : nullptr;
+  const float* pv = P ? pen_vals.data_ptr<float>() : nullptr;
+  float* lg = logits.data_ptr<float>();
+  const int ld = logits.stride(0);
+  int* o = out.data_ptr<int>();
+  switch (C) {
+    case 8: b200::launch_pdl_cluster(b200::sample_rows_kernel<8>, dim3(B * 8), dim3(b200::kSThreads), 0, stream, 8,
+                                     lg, V, ld, lp, pi, pc, P, pv, o); break;
+    case 4: b200::launch_pdl_cluster(b200::sample_rows_kernel<4>, dim3(B * 4), dim3(b200::kSThreads), 0, stream, 4,
+                                     lg, V, ld, lp, pi, pc, P, pv, o); break;
+    case 2: b200::launch_pdl_cluster(b200::sample_rows_kernel<2>, dim3(B * 2), dim3(b200::kSThreads), 0, stream, 2,
+                                     lg, V, ld, lp, pi, pc, P, pv, o); break;
+    default:
+      b200::sample_rows_kernel<1><<<B, b200::kSThreads, 0, stream>>>(lg, V, ld, lp, pi, pc, P, pv, o);
+      B200_CHECK_CUDA(cudaGetLastError());
+  }
 }

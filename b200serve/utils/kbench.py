@@ -343,7 +343,7 @@ def decode_step(layers=2, B=32, ctx=2304, iters=3):
     print(json.dumps({"case": "decode_step", "layers": layers, "B": B, "ctx": ctx, "eager_ms": round(ms, 3)}))
 
 
-def gemm_chain_trace(layers=2, B=32):
+def gemm_chain_trace(layers=2, B=32, partial=0):
     """Per-CTA timelines of the four decode GEMMs of ``layers`` Qwen3-8B layers captured in one
     CUDA graph (back to back, as in the decode step): for each launch, when its CTAs start,
     when the first weight tile lands, when the MMAs end and when the CTAs exit, relative to
@@ -360,10 +360,16 @@ def gemm_chain_trace(layers=2, B=32):
 
     def chain():
         for qkv, o, gu, dn in Ws:
-            ops.linear(x, qkv)
-            ops.linear(a, o)
-            ops.linear(x, gu, epilogue=ops.EPI_SWIGLU)
-            ops.linear(act, dn)
+            if partial:        # stream-K partials (consumers omitted: the GEMMs' own timeline)
+                ops.linear_partial(x, qkv)
+                ops.linear_partial(a, o)
+                ops.linear_partial(x, gu)
+                ops.linear_partial(act, dn)
+            else:
+                ops.linear(x, qkv)
+                ops.linear(a, o)
+                ops.linear(x, gu, epilogue=ops.EPI_SWIGLU)
+                ops.linear(act, dn)
 
     chain()
     torch.cuda.synchronize()
@@ -445,8 +451,8 @@ def decode_parts(layers=8, B=32, ctx=2304, tp=1):
             ops.linear(act, lw.down)
 
     def gemms_partial():
-        # the decode path on one rank: QKV, o_proj and down as stream-K partials, each summed by
-        # its consumer kernel (qkv_post, RMSNorm), gate_up with its SwiGLU epilogue
+        # the decode path on one rank: QKV, o_proj, gate_up and down as stream-K partials, each
+        # summed by its consumer kernel (qkv_post, RMSNorm, silu_mul_partial)
         for i, lw in enumerate(w.layers):
             pp = ops.linear_partial(x, lw.qkv)
             ops.qkv_post_partial(pp, None, lw.q_norm, lw.k_norm, dec.cos_sin, fb.positions, fb.slots, kv.k[i],
@@ -473,6 +479,19 @@ def decode_parts(layers=8, B=32, ctx=2304, tp=1):
         finally:
             ops._PARTIAL = prev
 
+    def flags(fn, **kw):
+        # run fn (and so capture its graph) with ops module switches set, e.g. _SWIGLU_PARTIAL
+        def run():
+            prev = {k: getattr(ops, k) for k in kw}
+            for k, v in kw.items():
+                setattr(ops, k, v)
+            try:
+                fn()
+            finally:
+                for k, v in prev.items():
+                    setattr(ops, k, v)
+        return run
+
     def attn():
         for i in range(layers):
             ops.paged_decode_attention(q, kv.k[i], kv.v[i], tables, fb.seq_lens, dec.scale, plan[0], plan[1], ws)
@@ -487,10 +506,15 @@ def decode_parts(layers=8, B=32, ctx=2304, tp=1):
     wbytes = sum(t.N * t.K * 2 for lw in w.layers for t in (lw.qkv, lw.o, lw.gate_up, lw.down)) / layers
     kvbytes = B * (ctx + 1) * nkv * hd * 2 * 2
     ideal = {"full": (wbytes + kvbytes) / hbm / 1e3, "full_dense": (wbytes + kvbytes) / hbm / 1e3,
+             "full_swiglu_epi": (wbytes + kvbytes) / hbm / 1e3,
              "gemms": wbytes / hbm / 1e3, "gemms_partial": wbytes / hbm / 1e3, "gemms_dense": wbytes / hbm / 1e3,
-             "attn": kvbytes / hbm / 1e3}
+             "gemms_partial_swiglu_epi": wbytes / hbm / 1e3, "attn": kvbytes / hbm / 1e3}
     out = {"case": "decode_parts", "layers": layers, "B": B, "ctx": ctx, "tp": tp, "peaks": src}
-    for name, fn in (("full", full), ("full_dense", full_dense), ("gemms", gemms), ("gemms_partial", gemms_partial),
+    # *_swiglu_epi: gate/up through the split-K SwiGLU epilogue instead of partials + silu_mul_partial
+    for name, fn in (("full", full), ("full_dense", full_dense),
+                     ("full_swiglu_epi", flags(full, _SWIGLU_PARTIAL=False)), ("gemms", gemms),
+                     ("gemms_partial", gemms_partial),
+                     ("gemms_partial_swiglu_epi", flags(gemms_partial, _SWIGLU_PARTIAL=False)),
                      ("gemms_dense", gemms_dense), ("attn", attn), ("small", small)):
         for _ in range(2):
             fn()
@@ -591,7 +615,7 @@ if __name__ == "__main__":
         sample_one(*[int(v) for v in sys.argv[2:4]])
         sys.exit(0)
     if what == "gemm_chain_trace":
-        gemm_chain_trace(*[int(v) for v in sys.argv[2:4]])
+        gemm_chain_trace(*[int(v) for v in sys.argv[2:5]])
         sys.exit(0)
     if what == "decode_parts":
         decode_parts(*[int(v) for v in sys.argv[2:6]])

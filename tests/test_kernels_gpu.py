@@ -353,6 +353,26 @@ def test_sampler_wide_candidate_sets():
         assert bool((probs[b, draws[:, b].long()] >= cut * (1 - 1e-3)).all())
 
 
+@pytest.mark.parametrize("cl", [2, 4, 8])
+def test_sampler_cluster_matches_single_cta(cl):
+    """Rows split over a thread-block cluster (histograms, maxima and candidates merged through
+    distributed shared memory) draw the same tokens as one CTA per row: greedy, top-k, min-p,
+    top-k with min-p, and penalties."""
+    V, B = 151936, 6
+    torch.manual_seed(7)
+    logits = torch.randn(B, V, device=dev) * 3
+    ids = torch.randint(0, V, (B, 8), device=dev, dtype=torch.int32)
+    cnt = torch.rand(B, 8, device=dev) * 3
+    vals = torch.tensor([[1.3, 0.5, 0.2]] * B, device=dev)
+    for t, k, minp in ((0.0, 0, 0.0), (0.8, 40, 0.0), (1.0, 0, 0.1), (0.7, 100, 0.02)):
+        for step in range(4):
+            a = ops.sample_rows(logits.clone(), [t] * B, [k] * B, [1.0] * B, [minp] * B, list(range(B)), [step] * B,
+                                ids, cnt, vals, cluster=1)
+            b = ops.sample_rows(logits.clone(), [t] * B, [k] * B, [1.0] * B, [minp] * B, list(range(B)), [step] * B,
+                                ids, cnt, vals, cluster=cl)
+            assert torch.equal(a, b), (t, k, minp, step)
+
+
 def test_sampler_penalties():
     V = 100
     logits = torch.zeros(1, V, device=dev)
