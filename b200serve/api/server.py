@@ -549,7 +549,9 @@ def create_app(engine=None, keystore: KeyStore = None):
     register_agent_routes(app, auth, _get_engine)
     register_knowledge_routes(app, auth, _get_engine)
     from b200serve.api.files_api import register_file_routes
+    from b200serve.api.inventory_api import register_inventory_routes
     register_file_routes(app, auth)
+    register_inventory_routes(app, auth)
     return app
 
 

@@ -121,6 +121,17 @@ class B200Engine(BaseEngine):
         else:
             dev = torch.device("cpu")
         self.device = dev
+        if self._injected_model_cfg is None and not os.path.exists(cfgE.model):
+            # a registered model (core/model_inventory.py): its checkpoint path and serving fields
+            from b200serve.core.model_inventory import engine_overrides
+            try:
+                ov = engine_overrides(cfgE.model)
+            except (OSError, ValueError):
+                ov = None
+            if ov:
+                for k, v in ov.items():
+                    if k != "tp_size":            # the launch decides the ranks
+                        setattr(cfgE, k, v)
         mc = self._injected_model_cfg or get_model_config(cfgE.model, cfgE.num_layers_override)
         self.model_cfg = mc
         if cfgE.max_seq <= 0:
