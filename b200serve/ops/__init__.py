@@ -375,6 +375,51 @@ def softcap_(x, cap):
     return x
 
 
+def layernorm(x, weight, bias, eps, out=None):
+    """LayerNorm over the last dim of bf16 rows (fp32 statistics), with optional bias."""
+    out = out if out is not None else torch.empty_like(x)
+    if _cuda(x):
+        ext().layernorm_rows(x, weight, bias, float(eps), out)
+        return out
+    y = torch.nn.functional.layer_norm(x.float(), (x.shape[-1],), weight.float(),
+                                       bias.float() if bias is not None else None, eps)
+    out.copy_(y.to(x.dtype))
+    return out
+
+
+def gelu_(x, tanh_approx=False):
+    """x = gelu(x) in place (exact erf form, or the tanh approximation)."""
+    if _cuda(x):
+        ext().gelu_rows(x, bool(tanh_approx))
+        return x
+    x.copy_(torch.nn.functional.gelu(x.float(), approximate="tanh" if tanh_approx else "none").to(x.dtype))
+    return x
+
+
+def vision_qkv_rope(qkv, cos, sin, heads, hd, slots, q_out, k_cache, v_cache):
+    """Rotate-half rotary on the q and k of [N, 3 heads hd] rows (cos / sin [N, hd] fp32); q into
+    q_out [N, heads, 128] and K/V into the paged cache [blocks, heads, 16, 128] at ``slots``,
+    zero-padded from hd to 128."""
+    N = qkv.shape[0]
+    if _cuda(qkv):
+        ext().vision_qkv_rope(qkv, torch.stack([cos, sin]).contiguous(), int(heads), int(hd), slots, q_out,
+                              k_cache, v_cache)
+        return q_out
+    t = qkv.float().view(N, 3, heads, hd)
+    q, k, v = t[:, 0], t[:, 1], t[:, 2]
+    c, s = cos[:, None, :], sin[:, None, :]
+
+    def rot(u):
+        h = hd // 2
+        return u * c + torch.cat([-u[..., h:], u[..., :h]], -1) * s
+    pad = lambda u: torch.nn.functional.pad(u, (0, 128 - hd)).to(q_out.dtype)
+    q_out.copy_(pad(rot(q)))
+    sl = slots.long()
+    k_cache.view(-1, heads, 16, 128)[sl // 16, :, sl % 16] = pad(rot(k))
+    v_cache.view(-1, heads, 16, 128)[sl // 16, :, sl % 16] = pad(v)
+    return q_out
+
+
 def gelu_tanh_mul(gu, out=None):
     """act = gelu_tanh(gate) * up (GeGLU) on the 64-column interleaved [g|u] layout."""
     I = gu.shape[-1] // 2

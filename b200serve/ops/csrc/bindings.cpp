@@ -62,6 +62,10 @@ void qkv_post(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::optiona
 void silu_mul(torch::Tensor gu, torch::Tensor act);
 void gelu_tanh_mul(torch::Tensor gu, torch::Tensor act);
 void softcap_(torch::Tensor x, double cap);
+void layernorm_rows(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b, double eps, torch::Tensor out);
+void gelu_rows(torch::Tensor x, bool tanh_approx);
+void vision_qkv_rope(torch::Tensor qkv, torch::Tensor cos_sin, int64_t heads, int64_t hd, torch::Tensor slots,
+                     torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache);
 void row_sigmoid_scale(torch::Tensor x, torch::Tensor g);
 void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
 void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
@@ -204,6 +208,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("silu_mul", &silu_mul);
   m.def("gelu_tanh_mul", &gelu_tanh_mul);
   m.def("softcap_", &softcap_);
+  m.def("layernorm_rows", &layernorm_rows);
+  m.def("gelu_rows", &gelu_rows);
+  m.def("vision_qkv_rope", &vision_qkv_rope);
   m.def("row_sigmoid_scale", &row_sigmoid_scale);
   m.def("embedding", &embedding);
   m.def("paged_decode_attention", &paged_decode_attention);
