@@ -164,6 +164,7 @@ class B200Engine(BaseEngine):
         self.runner = runner
         if cfgE.spec_mtp:
             self._attach_mtp(mc, dtype, dev)
+        self._attach_vision(mc, dtype, dev)
         # a prefix-cache hit would skip tokens whose recurrent state a hybrid model needs
         self.scheduler = Scheduler(runner, num_blocks, max_batch=cfgE.max_batch, prefill_chunk=cfgE.prefill_chunk,
                                    max_seq=cfgE.max_seq, prefix_cache=not mc.is_hybrid,
@@ -174,6 +175,46 @@ class B200Engine(BaseEngine):
         inference._tokenizer = self.tokenizer
         self._loaded_model = cfgE.model
         say(f"b200: ready, {num_blocks} KV pages ({num_blocks * BLOCK} tokens)")
+
+    def _attach_vision(self, mc, dtype, dev):
+        """The vision tower of a vision-language checkpoint (``vision_config`` and ``model.visual.*``
+        tensors), bound to the runner. Single-rank engines."""
+        path = self.config.model
+        cfg_path = os.path.join(path, "config.json") if os.path.isdir(path) else ""
+        if not cfg_path or not os.path.exists(cfg_path) or self.config.weights != "safetensors":
+            return
+        import json
+        with open(cfg_path) as fh:
+            hf = json.load(fh)
+        if "vision_config" not in hf:
+            return
+        if self.config.tp_size > 1:
+            _log.warning("b200: the vision tower runs on single-rank engines; images are refused")
+            return
+        from b200serve.models.qwen_vl import VisionLanguage
+        vl = VisionLanguage.from_checkpoint(hf, _safetensors_getter(path), mc, dev, dtype)
+        if vl is not None:
+            self.runner.vl = vl
+
+    def prepare_images(self, prompt_ids, images):
+        """(expanded prompt ids, multimodal input) for a prompt with image placeholders."""
+        vl = getattr(self.runner, "vl", None)
+        if vl is None:
+            raise ValueError("this model has no vision tower; images are not accepted")
+        return vl.prepare(list(prompt_ids), images)
+
+    def generate_images(self, prompt_ids, images, params: SamplingParams = None, timeout: float = None):
+        """One prompt (token ids with image placeholders) with PIL images -> finished Request."""
+        self.load()
+        params = params or SamplingParams()
+        ids, mm = self.prepare_images(prompt_ids, images)
+        stop_ids = set() if params.ignore_eos else self.tokenizer.stop_ids
+        req = Request(prompt=ids, params=params, stop_ids=stop_ids)
+        req.mm = mm
+        self.submit(req)
+        if not req.done_event.wait(timeout):
+            raise TimeoutError(f"{req.rid} did not finish")
+        return req
 
     def _attach_mtp(self, mc, dtype, dev):
         """Bind the MTP head (checkpoint ``mtp.*`` tensors, or a random head for random weights)
@@ -434,11 +475,16 @@ class B200Engine(BaseEngine):
     def generate_streaming(self, messages, max_tokens, temperature, on_token=None, on_complete=None,
                            enable_thinking=True, grammar=None, response_format=None, raw_output=False,
                            web_tools=False, reasoning_effort=None, on_telemetry=None, sampling=None,
-                           tools=None) -> str:
+                           tools=None, images=None) -> str:
         self.load()
         params = SamplingParams.from_dict(sampling, temperature=temperature,
                                           max_tokens=max_tokens if max_tokens and max_tokens > 0 else 8192)
         prompt, fit = self._fit_prompt(messages, params.max_tokens, enable_thinking, tools)
+        mm = None
+        if images:
+            prompt, mm = self.prepare_images(prompt, images)
+            if len(prompt) >= self.config.max_seq:
+                raise ValueError(f"prompt with images is {len(prompt)} tokens; the context is {self.config.max_seq}")
         if len(prompt) + params.max_tokens > self.config.max_seq:
             params.max_tokens = self.config.max_seq - len(prompt)
         # the reference halts at once on a faked conversational turn (STOP_STRINGS, applied by
@@ -474,6 +520,7 @@ class B200Engine(BaseEngine):
             cap = TelemetryCapture(self.tokenizer)
         req = Request(prompt=prompt, params=params, stop_ids=self.tokenizer.stop_ids, on_token=_cb)
         req.telemetry = cap
+        req.mm = mm
         req = self.submit(req)
         full, t_first, callback_error = "", None, None
         try:

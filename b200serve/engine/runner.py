@@ -72,6 +72,7 @@ class ModelRunner:
         self.vocab_start = weights.vocab_start
         self.greedy_buf = None
         self.mtp = None                 # MTPHead when MTP speculative decoding is on
+        self.vl = None                  # VisionLanguage of a vision-language checkpoint
         self.last_prenorm = self.last_cu = None
         pin = self.device.type == "cuda"
         self.h_pack = torch.zeros(B * (PACK + self.max_blocks), dtype=torch.int32, pin_memory=pin)
@@ -325,11 +326,44 @@ class ModelRunner:
                           keep_prenorm=self.mtp is not None and any(s.get("prenorm") for s in seqs))
         if T == 0:
             return None
+        if self.vl is not None:
+            self._multimodal(fb, seqs, cu)
         with rng(f"prefill T{T}"):
             out = self.decoder.forward(fb)
         # pre-final-norm hidden of every row (for the MTP head), rows of seqs[i] at cu[i]:cu[i+1]
         self.last_prenorm, self.last_cu = (self.decoder.prenorm, cu) if fb.keep_prenorm else (None, None)
         return out
+
+    def _multimodal(self, fb, seqs, cu):
+        """Images in this step (vision-language models): image rows take the vision tower's
+        embeddings and the DeepStack features, and RoPE uses the three-dimensional positions
+        (``rope_pos3`` of a prompt chunk, or the 1-D position plus ``rope_delta`` after it)."""
+        d = self.device
+        parts, any_rope, rows, embs, deeps = [], False, [], [], []
+        for i, s in enumerate(seqs):
+            n, st = len(s["ids"]), s["start"]
+            if s.get("rope_pos3") is not None:
+                parts.append(s["rope_pos3"])
+                any_rope = True
+            else:
+                delta = int(s.get("rope_delta", 0))
+                any_rope = any_rope or delta != 0
+                parts.append((torch.arange(st, st + n) + delta).expand(3, n))
+            if s.get("mm_rows") is not None and len(s["mm_rows"]):
+                rows.append(s["mm_rows"] + cu[i])
+                embs.append(s["mm_embeds"])
+                deeps.append(s.get("mm_deep") or [])
+        if any_rope:
+            fb.rope_cs = self.vl.table(torch.cat(parts, 1))
+            fb.rope_positions = torch.arange(fb.input_ids.shape[0], dtype=torch.int32, device=d)
+        if rows:
+            r = torch.cat(rows).to(d)
+            h = ops.embedding(fb.input_ids, self.decoder.w.embed)
+            h.index_copy_(0, r, torch.cat(embs).to(h.dtype))
+            fb.inputs_embeds = h
+            nl = min(len(x) for x in deeps)
+            if nl:
+                fb.deepstack = (r, [torch.cat([x[l] for x in deeps]) for l in range(nl)])
 
     def mtp_step(self, segs):
         """Run the MTP head over committed rows and return its greedy draft per segment.

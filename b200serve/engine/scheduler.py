@@ -74,6 +74,7 @@ class Request:
     telemetry: object = None         # TelemetryCapture: per-token forward frames (eager steps)
     embedding: list = None           # embedding requests: the mean-pooled final hidden state
     mtp_draft: int = None            # MTP head's guess for the token after tokens[-1]
+    mm: object = None                # models.qwen_vl.MMInput: images of a vision-language prompt
     done_event: threading.Event = field(default_factory=threading.Event)
 
     def __post_init__(self):
@@ -198,7 +199,8 @@ class Scheduler:
                     self.waiting.pop(0)
                     self._finish(req, "abort")
                     continue
-                matched, _ = self.alloc.match_prefix(req.tokens[:-1])
+                # image tokens share one id whatever the image: such prompts never use the prefix cache
+                matched = [] if req.mm is not None else self.alloc.match_prefix(req.tokens[:-1])[0]
                 need = (len(req.tokens) + 1 + BLOCK - 1) // BLOCK - len(matched)
                 if need > self.alloc.num_free:
                     self.alloc.release(matched)
@@ -253,7 +255,8 @@ class Scheduler:
         req.finish_reason = reason
         req.finish_time = time.perf_counter()
         if req.blocks:
-            self.alloc.register(req.blocks, req.tokens[: req.num_computed])
+            if req.mm is None:
+                self.alloc.register(req.blocks, req.tokens[: req.num_computed])
             self.alloc.release(req.blocks)
             req.blocks = []
         req.done_event.set()
@@ -293,7 +296,7 @@ class Scheduler:
         r = self.runner
         return (getattr(r, "use_graphs", False) and hasattr(r, "pipeline_step")
                 and not self.waiting and all(q.params.greedy and q.params.plain and q.telemetry is None
-                                             for q in batch))
+                                             and q.mm is None for q in batch))
 
     def _pipelined_decode(self, batch) -> int:
         """Decode ``batch`` until it changes, keeping one step in flight: step N runs on the
@@ -388,9 +391,10 @@ class Scheduler:
         if not batch:
             return 0
         ids = [r.tokens[-1] for r in batch]
-        pos = [len(r.tokens) - 1 for r in batch]
-        slots = [r.blocks[p // BLOCK] * BLOCK + p % BLOCK for r, p in zip(batch, pos)]
-        lens = [p + 1 for p in pos]
+        real = [len(r.tokens) - 1 for r in batch]
+        slots = [r.blocks[p // BLOCK] * BLOCK + p % BLOCK for r, p in zip(batch, real)]
+        lens = [p + 1 for p in real]
+        pos = [p + (r.mm.delta if r.mm is not None else 0) for r, p in zip(batch, real)]   # RoPE positions
         greedy = all(r.params.greedy and r.params.plain for r in batch)
         watch = [(i, r.telemetry) for i, r in enumerate(batch) if r.telemetry is not None]
         kw = {"telemetry": watch} if watch else {}
@@ -428,9 +432,10 @@ class Scheduler:
             if r not in self.running:
                 continue
             last = r.num_computed + n == len(r.tokens)
-            seqs.append({"ids": r.tokens[r.num_computed:r.num_computed + n], "start": r.num_computed,
-                         "block_table": r.blocks, "want_logits": last, "state_slot": r.state_slot,
-                         "telemetry": r.telemetry if last else None, "prenorm": self._mtp_ok(r)})
+            seqs.append(dict(self._mm_chunk(r, r.num_computed, n),
+                             ids=r.tokens[r.num_computed:r.num_computed + n], start=r.num_computed,
+                             block_table=r.blocks, want_logits=last, state_slot=r.state_slot,
+                             telemetry=r.telemetry if last else None, prenorm=self._mtp_ok(r)))
             reqs.append((r, n))
             if remaining > 1:
                 budget -= n
@@ -458,6 +463,30 @@ class Scheduler:
                 self.running.remove(r)
         self._mtp_commit([(i, 0, r, start, n) for i, r, start, n in commits])
         return len(sample_reqs)
+
+    @staticmethod
+    def _mm_chunk(r: Request, start: int, n: int) -> dict:
+        """Multimodal fields of the step rows [start, start + n) of ``r``: image rows inside the
+        chunk with their embeddings and DeepStack features, and RoPE positions."""
+        if r.mm is None:
+            return {}
+        mm = r.mm
+        L = mm.pos3.shape[1]
+        out = {"rope_delta": mm.delta}
+        if start < L:
+            hi = min(L, start + n)
+            p3 = mm.pos3[:, start:hi]
+            if hi < start + n:                      # rows past the prompt: 1-D position + delta
+                extra = (torch.arange(hi, start + n) + mm.delta).expand(3, start + n - hi)
+                p3 = torch.cat([p3, extra], 1)
+            out["rope_pos3"] = p3
+            sel = (mm.rows >= start) & (mm.rows < start + n)
+            if bool(sel.any()):
+                idx = sel.nonzero().view(-1)
+                out["mm_rows"] = mm.rows[idx] - start
+                out["mm_embeds"] = mm.embeds[idx.to(mm.embeds.device)]
+                out["mm_deep"] = [dd[idx.to(dd.device)] for dd in mm.deep]
+        return out
 
     # ------------------------------------------------------------ speculative decoding
     def _mtp_ok(self, r: Request) -> bool:
@@ -517,9 +546,10 @@ class Scheduler:
                 continue
             if r not in self.running:
                 continue
-            seqs.append({"ids": [r.tokens[-1]] + draft, "start": len(r.tokens) - 1, "block_table": r.blocks,
-                         "want_logits": True, "all_logits": bool(draft), "state_slot": r.state_slot,
-                         "prenorm": self._mtp_ok(r)})
+            seqs.append(dict(self._mm_chunk(r, len(r.tokens) - 1, 1 + len(draft)),
+                             ids=[r.tokens[-1]] + draft, start=len(r.tokens) - 1, block_table=r.blocks,
+                             want_logits=True, all_logits=bool(draft), state_slot=r.state_slot,
+                             prenorm=self._mtp_ok(r)))
             plan.append((r, draft))
         keep = [(s, pl) for s, pl in zip(seqs, plan) if pl[0] in self.running]
         if not keep:

@@ -46,8 +46,11 @@ class ForwardBatch:
     state_slots: torch.Tensor = None    # hybrid models: recurrent-state slot per sequence
     telemetry: list = None              # [(row, TelemetryCapture)]: per-layer frames for these rows
     hidden: bool = False                # return the final-normed hidden states of logit_rows, no lm_head
-    inputs_embeds: torch.Tensor = None  # [T, H] input rows instead of the embedding lookup (MTP head)
+    inputs_embeds: torch.Tensor = None  # [T, H] input rows instead of the embedding lookup (MTP head, images)
     keep_prenorm: bool = False          # keep the pre-final-norm hidden of every row in Decoder.prenorm
+    rope_cs: torch.Tensor = None        # [*, rot] cos|sin rows used instead of the model's table (multimodal RoPE)
+    rope_positions: torch.Tensor = None  # [T] rows of the RoPE table per token (default: positions)
+    deepstack: tuple = None             # (rows [n] long, [features [n, H]]): added after layers 0, 1, ...
 
 
 class NoComm:
@@ -155,7 +158,7 @@ class Decoder:
         kst = torch.empty(nblk, self.nkv, 16, self.hd, dtype=qkv.dtype, device=qkv.device)
         vst = torch.empty_like(kst)
         stage_slots = torch.arange(T, dtype=torch.int32, device=qkv.device)
-        q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.kv_cos[i], fb.positions, stage_slots, kst, vst,
+        q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self._rope_cs(i, fb), self._rope_pos(fb), stage_slots, kst, vst,
                          self.nq, self.nkv, eps, hd=self.hd)
         q_rot, q_jl = ops.tq_qkv(q, kst, vst, fb.slots, tb, kv, i)
         if fb.is_decode:
@@ -207,7 +210,7 @@ class Decoder:
         if qkv.is_cuda:
             q = torch.empty(T, self.nq, self.hd, dtype=qkv.dtype, device=qkv.device)
             ops._cuda(qkv)
-            ops.ext().qkv_post_q4(qkv, None, lw.q_norm, lw.k_norm, self.kv_cos[i], fb.positions, fb.slots, q, kc, vc,
+            ops.ext().qkv_post_q4(qkv, None, lw.q_norm, lw.k_norm, self._rope_cs(i, fb), self._rope_pos(fb), fb.slots, q, kc, vc,
                                   ksc, vsc, self.nq, self.nkv, eps)
             out = torch.empty_like(q)
             if fb.is_decode:
@@ -231,7 +234,7 @@ class Decoder:
         # CPU: quantise the new rows into the cache, attend over dequantised pages
         kb = torch.zeros(kc.shape[0], self.nkv, 16, self.hd, dtype=torch.float32)
         vb = torch.zeros_like(kb)
-        q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.kv_cos[i], fb.positions, fb.slots, kb, vb, self.nq,
+        q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self._rope_cs(i, fb), self._rope_pos(fb), fb.slots, kb, vb, self.nq,
                          self.nkv, eps, hd=self.hd)
         sl = fb.slots.long()
         ok = sl >= 0
@@ -252,14 +255,14 @@ class Decoder:
         plain = not self.cfg.attn_output_gate and self.cos_sin.shape[1] == self.hd
         if plain and self.tq is None and self.kv.kv_format == "bf16" and ops.qkv_fused_ok(x, lw.qkv, self.kv.k[i]):
             kc, vc = self.kv.k[i], self.kv.v[i]
-            q = ops.qkv_fused(x, lw.qkv, lw.qkv_bias, lw.q_norm, lw.k_norm, self.kv_cos[i], fb.positions, fb.slots,
+            q = ops.qkv_fused(x, lw.qkv, lw.qkv_bias, lw.q_norm, lw.k_norm, self._rope_cs(i, fb), self._rope_pos(fb), fb.slots,
                               kc, vc, self.nq, self.nkv, self.cfg.rms_eps, ag=ag)
             return self._attn_core(i, q, fb, plan)
         if (plain and ag is None and fb.is_decode and self.tq is None and self.kv.kv_format == "bf16"
                 and getattr(self, "_partial_ok", False) and x.is_cuda):
             pp = ops.linear_partial(x, lw.qkv)
             if pp is not None:
-                q = ops.qkv_post_partial(pp, lw.qkv_bias, lw.q_norm, lw.k_norm, self.kv_cos[i], fb.positions,
+                q = ops.qkv_post_partial(pp, lw.qkv_bias, lw.q_norm, lw.k_norm, self._rope_cs(i, fb), self._rope_pos(fb),
                                          fb.slots, self.kv.k[i], self.kv.v[i], self.nq, self.nkv, self.cfg.rms_eps,
                                          self.hd)
                 return self._attn_core(i, q, fb, plan)
@@ -270,6 +273,13 @@ class Decoder:
             w0 = (self.nq + 2 * self.nkv) * self.hd
             ops.sigmoid_gate_mul(out.view(T, self.nq * self.hd), qkv[:, w0:w0 + self.nq * self.hd])
         return out
+
+    def _rope_cs(self, i, fb):
+        return fb.rope_cs if fb.rope_cs is not None else self.kv_cos[i]
+
+    @staticmethod
+    def _rope_pos(fb):
+        return fb.rope_positions if fb.rope_positions is not None else fb.positions
 
     def _record(self, i, x, residual, parts, telemetry):
         """Telemetry: residual-stream L2 norm after layer ``i`` (and MoE routes) for the
@@ -326,7 +336,7 @@ class Decoder:
         if self.kv.kv_format == "int4g128":
             return self._attention_q4(i, qkv, lw, fb, T, tps, nsplit, ws, tq_pre)
         kc, vc = self.kv.k[i], self.kv.v[i]
-        q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self.kv_cos[i], fb.positions, fb.slots, kc, vc,
+        q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self._rope_cs(i, fb), self._rope_pos(fb), fb.slots, kc, vc,
                          self.nq, self.nkv, eps, hd=self.hd)
         return self._attn_core(i, q, fb, plan)
 
@@ -444,10 +454,11 @@ class Decoder:
         quant_kv = self.tq is not None or (self.kv.kv_format == "int4g128" and h.is_cuda and ops._TC_PREFILL)
         tq_pre = self._tq_prefill_pages(fb) if (quant_kv and not fb.is_decode) else None
         plan = (tps, nsplit, ws) if fb.is_decode else (0, 0, None)
-        if self.moe is not None and not fb.keep_prenorm and self._use_ep_a2a(T):
+        special = fb.keep_prenorm or fb.deepstack is not None or fb.rope_cs is not None
+        if self.moe is not None and not special and self._use_ep_a2a(T):
             return self._forward_ep(fb, h, plan, tq_pre)
         if self.moe is None and not cfg.is_hybrid and not cfg.sandwich_norms and cfg.act == "silu" and \
-                not fb.keep_prenorm and comm.world > 1 and hasattr(comm, "use_rsag") and comm.use_rsag(T):
+                not special and comm.world > 1 and hasattr(comm, "use_rsag") and comm.use_rsag(T):
             return self._forward_rsag(fb, h, plan, tq_pre)
         residual = torch.empty_like(h)
         x = ops.rmsnorm([h], w.layers[0].input_norm, eps, residual_out=residual)
@@ -481,6 +492,10 @@ class Decoder:
                 mlp_parts = self._row_parallel(act, lw.down, "mlp")
             if lw.mlp_out_norm is not None:
                 mlp_parts = [ops.rmsnorm(mlp_parts, lw.mlp_out_norm, eps)]
+            if fb.deepstack is not None and i < len(fb.deepstack[1]):
+                # DeepStack: the layer output of the image rows gains the tower's feature (the
+                # residual still waits for this layer's MLP output, so adding here is the same)
+                residual.index_add_(0, fb.deepstack[0], fb.deepstack[1][i].to(residual.dtype))
             if fb.telemetry:
                 self._record(i, x, residual, mlp_parts, fb.telemetry)
             if _NVTX:
