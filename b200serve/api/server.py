@@ -195,7 +195,8 @@ def _sampling_from_request(body: ChatCompletionRequest) -> dict:
     return samp
 
 
-def _produce(engine, messages, max_tokens, samp, q: _StreamQueue, enable_thinking, telemetry=False, tools=None):
+def _produce(engine, messages, max_tokens, samp, q: _StreamQueue, enable_thinking, telemetry=False, tools=None,
+             images=None):
     """Producer thread: stream thinking/content pieces (telemetry frames, tool calls) into ``q``."""
     tcf = None
     on_content = lambda t: q.put(("content", t))
@@ -210,6 +211,8 @@ def _produce(engine, messages, max_tokens, samp, q: _StreamQueue, enable_thinkin
         kw = {"on_telemetry": lambda f: q.put(("telemetry", f))} if telemetry else {}
         if tools:
             kw["tools"] = tools
+        if images:
+            kw["images"] = images
         engine.generate_streaming(messages, max_tokens=max_tokens, temperature=samp.get("temperature", 0.7),
                                   on_token=tf.feed, enable_thinking=enable_thinking, sampling=samp, **kw)
         tf.flush()
@@ -368,6 +371,11 @@ def create_app(engine=None, keystore: KeyStore = None):
         messages = [m.model_dump(exclude_none=True) for m in body.messages]
         for m in messages:
             m.setdefault("content", "")
+        from b200serve.api.images import ImageError, extract_images
+        try:
+            messages, images = extract_images(messages, getattr(app.state, "files", None))
+        except ImageError as e:
+            raise HTTPException(status_code=400, detail=str(e))
         tools = body.tools if (body.tools and body.tool_choice != "none") else None
         if not messages:
             raise HTTPException(status_code=400, detail="messages is required")
@@ -394,7 +402,7 @@ def create_app(engine=None, keystore: KeyStore = None):
             async def gen():
                 q = _StreamQueue()
                 th = threading.Thread(target=_produce, args=(eng, messages, max_tokens, samp, q, enable_thinking,
-                                                             bool(opts.get("telemetry")), tools), daemon=True)
+                                                             bool(opts.get("telemetry")), tools, images), daemon=True)
                 th.start()
                 usage = {"prompt_tokens": 0, "completion_tokens": 0}
                 finish = "stop"
@@ -438,6 +446,8 @@ def create_app(engine=None, keystore: KeyStore = None):
                                      headers={"Cache-Control": "no-cache", "X-Accel-Buffering": "no"})
 
         tkw = {"tools": tools} if tools else {}
+        if images:
+            tkw["images"] = images
 
         def _run():
             # the stats are read in the thread that generated: concurrent requests each see their own

@@ -171,6 +171,12 @@ class B200Engine(BaseEngine):
                                    spec_ngram=0 if mc.is_hybrid else cfgE.spec_ngram,
                                    spec_mtp=cfgE.spec_mtp and getattr(runner, "mtp", None) is not None)
         self.tokenizer = self._injected_tokenizer or load_tokenizer(self._model_path(), mc.vocab_size)
+        vl = getattr(self.runner, "vl", None)
+        if vl is not None and hasattr(self.tokenizer, "add_special"):
+            # a checkpoint without tokenizer files: the image markers still encode to their ids
+            t = vl.tokens
+            self.tokenizer.add_special({"<|vision_start|>": t.vision_start, "<|image_pad|>": t.image,
+                                        "<|vision_end|>": t.vision_end})
         from b200serve.core import inference
         inference._tokenizer = self.tokenizer
         self._loaded_model = cfgE.model

@@ -22,9 +22,27 @@ class SyntheticTokenizer:
         self.pad_token_id = self.eos_token_id
         self._special = {self.im_start_id: "<|im_start|>", self.im_end_id: "<|im_end|>",
                          self.eos_token_id: "<|endoftext|>"}
+        self._by_text = {}
+
+    def add_special(self, tokens: dict):
+        """Map marker strings to ids ({"<|image_pad|>": id, ...}) for encode and decode."""
+        for text, i in tokens.items():
+            self._special[int(i)] = text
+            self._by_text[text] = int(i)
 
     def encode(self, text: str, add_special_tokens: bool = False) -> list:
-        return [b + self.BYTE0 for b in text.encode("utf-8")]
+        if not self._by_text:
+            return [b + self.BYTE0 for b in text.encode("utf-8")]
+        out, i = [], 0
+        while i < len(text):
+            hit = next((t for t in self._by_text if text.startswith(t, i)), None)
+            if hit is not None:
+                out.append(self._by_text[hit])
+                i += len(hit)
+                continue
+            out += [b + self.BYTE0 for b in text[i].encode("utf-8")]
+            i += 1
+        return out
 
     def decode(self, ids, skip_special_tokens: bool = True) -> str:
         out = bytearray()

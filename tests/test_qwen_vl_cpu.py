@@ -12,6 +12,7 @@ import torch
 transformers = pytest.importorskip("transformers")
 
 from b200serve.models import qwen_vl as QV  # noqa: E402
+from b200serve.models import vision as V  # noqa: E402,F401
 
 TOK = QV.VLTokens(image=500, vision_start=498, vision_end=499)
 
@@ -83,3 +84,45 @@ def test_engine_matches_hf_generate(tiny_vl):
         lg = hf(input_ids=seq, pixel_values=patches, image_grid_thw=torch.tensor([grid]),
                 mm_token_type_ids=(seq == TOK.image).int()).logits[0]
     assert ours == lg[len(full) - 1:-1].argmax(-1).tolist()
+
+
+def test_chat_completions_with_image(tiny_vl, tmp_path):
+    """/v1/chat/completions with an image part (data URL, then an uploaded file id) reaches the
+    vision tower; a remote URL is refused."""
+    import base64
+    import io
+    from fastapi.testclient import TestClient
+    from PIL import Image
+    from b200serve.api import server
+    from b200serve.core.api_keys import KeyStore
+    from b200serve.core.config import EngineConfig
+    from b200serve.core.file_store import FileStore
+    from b200serve.engine.b200_engine import B200Engine
+    path, _ = tiny_vl
+    buf = io.BytesIO()
+    Image.fromarray(np.random.default_rng(2).integers(0, 255, (64, 64, 3), dtype=np.uint8)).save(buf, "PNG")
+    png = buf.getvalue()
+    eng = B200Engine(EngineConfig(model=path, weights="safetensors", device="cpu", dtype="float32",
+                                  cuda_graphs=False, max_seq=256, max_batch=2))
+    app = server.create_app(engine=eng, keystore=KeyStore(path=""))
+    app.state.files = FileStore(str(tmp_path / "files"))
+    try:
+        with TestClient(app) as c:
+            url = "data:image/png;base64," + base64.b64encode(png).decode()
+            body = {"messages": [{"role": "user", "content": [{"type": "text", "text": "what is this?"},
+                                                              {"type": "image_url", "image_url": {"url": url}}]}],
+                    "max_tokens": 4, "temperature": 0.0}
+            r = c.post("/v1/chat/completions", json=body)
+            assert r.status_code == 200, r.text
+            n_text = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "what is this?"}],
+                                                          "max_tokens": 4, "temperature": 0.0}).json()
+            # the image adds its visual tokens (4 x 4 patches -> 4 merged) and the two markers
+            assert r.json()["usage"]["prompt_tokens"] >= n_text["usage"]["prompt_tokens"] + 6
+            fid = c.post("/v1/files", files={"file": ("x.png", png, "image/png")}).json()["id"]
+            body["messages"][0]["content"][1] = {"type": "image", "image": fid}
+            assert c.post("/v1/chat/completions", json=body).status_code == 200
+            body["messages"][0]["content"][1] = {"type": "image_url", "image_url": {"url": "https://x/y.png"}}
+            assert c.post("/v1/chat/completions", json=body).status_code == 400
+    finally:
+        eng.unload()
+        server.set_engine(None)
