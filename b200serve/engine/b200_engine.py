@@ -155,8 +155,14 @@ class B200Engine(BaseEngine):
         # hybrid models page K/V for their full-attention layers only
         self.kv = KVCache(_kv_layers(mc), num_blocks, nkv_local, mc.head_dim, dtype=dtype, device=dev,
                           kv_format=cfgE.kv_format, key_bits=cfgE.kv_key_bits, value_bits=cfgE.kv_value_bits)
+        kv_b, nb = None, 0
+        if cfgE.kv_format == "turboquant" and cfgE.kv_boundary_layers > 0:
+            nb = cfgE.kv_boundary_layers
+            n_kv = _kv_layers(mc)
+            kv_b = KVCache(min(n_kv, 2 * nb), num_blocks, nkv_local, mc.head_dim, dtype=dtype, device=dev)
         from b200serve.engine.runner import ModelRunner
         runner = ModelRunner(mc, self.weights, self.kv, comm=self.comm, device=dev, max_batch=cfgE.max_batch,
+                             kv_boundary=kv_b, boundary_layers=nb,
                              max_seq=cfgE.max_seq, use_graphs=cfgE.cuda_graphs)
         if tp > 1:
             from b200serve.parallel.worker import BroadcastRunner
@@ -303,8 +309,11 @@ class B200Engine(BaseEngine):
 
     def _size_kv(self, mc, nkv_local, dtype, dev) -> int:
         cfgE = self.config
-        per_block = KVCache.bytes_per_block(_kv_layers(mc), nkv_local, mc.head_dim,
-                                            torch.tensor([], dtype=dtype).element_size(), cfgE.kv_format)
+        esz = torch.tensor([], dtype=dtype).element_size()
+        per_block = KVCache.bytes_per_block(_kv_layers(mc), nkv_local, mc.head_dim, esz, cfgE.kv_format)
+        if cfgE.kv_format == "turboquant" and cfgE.kv_boundary_layers > 0:    # bf16 boundary layers
+            per_block += KVCache.bytes_per_block(min(_kv_layers(mc), 2 * cfgE.kv_boundary_layers), nkv_local,
+                                                 mc.head_dim, esz, "bf16")
         state = 0
         if mc.is_hybrid:
             from b200serve.models.hybrid import LinearState

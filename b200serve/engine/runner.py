@@ -36,10 +36,11 @@ PACK = 5
 
 class ModelRunner:
     def __init__(self, cfg, weights, kv, comm=None, device="cuda", max_batch=64, max_seq=4096,
-                 use_graphs=True):
+                 use_graphs=True, kv_boundary=None, boundary_layers=0):
         self.cfg = cfg
         self.device = torch.device(device)
-        self.decoder = Decoder(cfg, weights, kv, comm=comm, device=self.device)
+        self.decoder = Decoder(cfg, weights, kv, comm=comm, device=self.device, kv_boundary=kv_boundary,
+                               boundary_layers=boundary_layers)
         self.comm = self.decoder.comm
         self.max_batch = max_batch
         self.max_seq = max_seq

@@ -74,10 +74,19 @@ class NoComm:
 
 class Decoder:
     def __init__(self, cfg: ModelConfig, weights: ModelWeights, kv_cache, comm=None, attn_splits=None,
-                 device="cpu"):
+                 device="cpu", kv_boundary=None, boundary_layers: int = 0):
         self.cfg = cfg
         self.w = weights
         self.kv = kv_cache
+        # TurboQuant boundary layers: the first and last ``boundary_layers`` attention layers keep
+        # full-precision K/V in ``kv_boundary`` (reference: core/turboquant_cache.py:318-327)
+        kv_layers = [i for i in range(cfg.num_layers) if cfg.has_kv(i)]
+        nb = boundary_layers if getattr(kv_cache, "kv_format", "bf16") == "turboquant" else 0
+        self.boundary = set(kv_layers[:nb]) | set(kv_layers[len(kv_layers) - nb:]) if nb else set()
+        self.kv_b = kv_boundary if self.boundary else None
+        self.kvi_b = {li: j for j, li in enumerate(sorted(self.boundary))}
+        if self.boundary and (kv_boundary is None or kv_boundary.num_layers < len(self.boundary)):
+            raise ValueError(f"{len(self.boundary)} boundary layers need a bf16 cache with as many layers")
         self.comm = comm or NoComm()
         self.device = torch.device(device)
         tp = weights.tp_size
@@ -111,8 +120,9 @@ class Decoder:
         if want_rot:
             self.tq = ops.TurboQuantTables(kv_cache.key_bits, kv_cache.value_bits, self.device)
         if want_rot != getattr(weights, "o_rotated", False):
-            self._rotate_o()
+            self._rotate_o(skip=self.boundary if want_rot else getattr(weights, "o_rotated_skip", set()))
             weights.o_rotated = want_rot
+            weights.o_rotated_skip = set(self.boundary) if want_rot else set()
         if self.device.type == "cuda":
             self.pack_weights()
         if cfg.is_moe:
@@ -135,12 +145,14 @@ class Decoder:
         if self.device.type == "cuda":
             torch.cuda.empty_cache()
 
-    def _rotate_o(self):
+    def _rotate_o(self, skip=()):
         """TurboQuant KV keeps V in the rotated domain (attention returns H o per head), so the
         o_proj weight absorbs the transform: W_o' = W_o blockdiag(H) (H symmetric, orthonormal).
         H is an involution, so the same call undoes it when the weights go back to a plain KV
         format; ``weights.o_rotated`` records the current state."""
-        for lw in self.w.layers:
+        for li, lw in enumerate(self.w.layers):
+            if li in skip:                      # boundary layers keep full-precision K/V: unrotated
+                continue
             if not isinstance(lw.o, torch.Tensor):
                 raise NotImplementedError("turboquant KV needs a dense (bf16/fp32) o_proj weight")
             o = lw.o
@@ -248,6 +260,18 @@ class Decoder:
         if fb.is_decode:
             return ops.paged_decode_attention(q, kd, vd, fb.block_tables, fb.seq_lens, self.scale)
         return ops.paged_prefill_attention(q, kd, vd, fb.block_tables, fb.seq_lens, fb.q_start, fb.cu_q, self.scale)
+
+    def _attn_layer(self, layer, x, lw, fb, T, plan, tq_pre, ag=None):
+        """Attention of model layer ``layer``: a boundary layer runs on the full-precision cache
+        (TurboQuant off for it), every other one on the main cache."""
+        if layer not in self.boundary:
+            return self._qkv_attend(self.kvi[layer], x, lw, fb, T, plan, tq_pre, ag)
+        saved = (self.kv, self.tq, self.kv_cos)
+        self.kv, self.tq, self.kv_cos = self.kv_b, None, [self.cos_sin] * self.kv_b.num_layers
+        try:
+            return self._qkv_attend(self.kvi_b[layer], x, lw, fb, T, plan, None, ag)
+        finally:
+            self.kv, self.tq, self.kv_cos = saved
 
     def _qkv_attend(self, i, x, lw, fb, T, plan, tq_pre, ag=None):
         """QKV projection + post-processing + attention of layer ``i`` -> [T, nq, hd]. On a bf16
@@ -375,7 +399,7 @@ class Decoder:
         for i, lw in enumerate(w.layers):
             if i > 0:
                 x, ag = comm.norm_ag(parts, lw.input_norm, eps, residual)
-            attn = self._qkv_attend(i, x, lw, fb, T, plan, tq_pre, ag)
+            attn = self._attn_layer(i, x, lw, fb, T, plan, tq_pre, ag)
             parts = comm.rs_linear(attn.view(T, self.nq * self.hd), lw.o, "o")
             x_own = ops.rmsnorm(parts, lw.post_norm, eps, residual=residual, residual_out=residual)
             sh = self.moe.shared(i, x_own)
@@ -410,7 +434,7 @@ class Decoder:
         for i, lw in enumerate(w.layers):
             if i > 0:
                 x, ag = comm.norm_ag(parts, lw.input_norm, eps, residual)
-            attn = self._qkv_attend(i, x, lw, fb, T, plan, tq_pre, ag)
+            attn = self._attn_layer(i, x, lw, fb, T, plan, tq_pre, ag)
             parts = comm.rs_linear(attn.view(T, self.nq * self.hd), lw.o, "o")
             x, ag = comm.norm_ag(parts, lw.post_norm, eps, residual)
             act = ops.linear(x, lw.gate_up, epilogue=ops.EPI_SWIGLU, ag=ag)
@@ -474,7 +498,7 @@ class Decoder:
                 mix = self._conv_mix(i, x, lw, fb)
                 o_parts = self._row_parallel(mix, lw.o, "o")
             else:
-                attn = self._qkv_attend(self.kvi[i], x, lw, fb, T, plan, tq_pre)
+                attn = self._attn_layer(i, x, lw, fb, T, plan, tq_pre)
                 o_parts = self._row_parallel(attn.view(T, self.nq * self.hd), lw.o, "o")
             if lw.attn_out_norm is not None:      # Gemma 3: normalise the sub-block output first
                 o_parts = [ops.rmsnorm(o_parts, lw.attn_out_norm, eps)]

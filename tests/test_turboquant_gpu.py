@@ -113,3 +113,38 @@ def test_engine_turboquant_gpu():
         mc.BUILTIN["tiny-qwen2"] = old
     for a, b in zip(outs["turboquant"], outs["bf16"]):
         assert len(a) == 12 and a[0] == b[0]
+
+
+def test_engine_turboquant_boundary_layers_gpu():
+    """Boundary layers: with every layer a boundary layer the TurboQuant engine is exactly the
+    bf16 engine (greedy tokens and the first step's logits); with the first and last of four
+    layers in bf16 the logits move toward the bf16 ones."""
+    from dataclasses import replace
+    import b200serve.models.config as mc
+    from b200serve.core.config import EngineConfig
+    from b200serve.engine.b200_engine import B200Engine
+    from b200serve.engine.sampler import SamplingParams
+    cfg = replace(mc.BUILTIN["tiny-qwen2"], head_dim=128, num_heads=4, num_kv_heads=2, hidden_size=512,
+                  num_layers=4)
+    old = mc.BUILTIN["tiny-qwen2"]
+    mc.BUILTIN["tiny-qwen2"] = cfg
+    g = torch.Generator().manual_seed(0)
+    ps = [torch.randint(0, 32000, (n,), generator=g).tolist() for n in (40, 200)]
+    out, logits = {}, {}
+    try:
+        for name, fmt, nb in (("bf16", "bf16", 0), ("tq", "turboquant", 0), ("tq_b1", "turboquant", 1),
+                              ("tq_all", "turboquant", 2)):
+            eng = B200Engine(EngineConfig(model="tiny-qwen2", device="cuda", max_seq=512, max_batch=4,
+                                          kv_format=fmt, kv_boundary_layers=nb, cuda_graphs=False))
+            eng.load()
+            bt = eng.scheduler.alloc.allocate((len(ps[1]) + 15) // 16)
+            logits[name] = eng.runner.prefill([{"ids": ps[1], "start": 0, "block_table": bt}])[0].float().cpu()
+            eng.scheduler.alloc.release(bt)
+            out[name] = [r.output for r in eng.generate(ps, SamplingParams(max_tokens=8, ignore_eos=True),
+                                                       timeout=300)]
+            eng.unload()
+    finally:
+        mc.BUILTIN["tiny-qwen2"] = old
+    assert out["tq_all"] == out["bf16"] and torch.equal(logits["tq_all"], logits["bf16"])
+    err = lambda k: ((logits[k] - logits["bf16"]).norm() / logits["bf16"].norm()).item()
+    assert err("tq_b1") < err("tq")
