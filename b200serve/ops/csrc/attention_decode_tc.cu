@@ -92,38 +92,60 @@ __device__ __forceinline__ void dequant_q4_page(const uint8_t* raw, uint8_t* wor
 // unscaled code values; each token's V norm scales its softmax weight instead.
 constexpr int kTqKCodes = 0, kTqKSign = 1024, kTqKMeta = 1280, kTqVCodes = 1344, kTqVMeta = 2368;
 constexpr int kTqRaw = 2400;
-// pair tables (bf16x2 per code byte) for K and V, then the sign table: byte of 8 sign bits ->
-// 8 bf16 of +-1 (uint4)
-constexpr int kTqLut = 2 * 256 * 4 + 256 * 16;
+// pair tables (bf16x2 per code byte) for K and V
+constexpr int kTqLut = 2 * 256 * 4;
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
 
 // Expand one TurboQuant page into the work stage: code values of K (boxes 0-1), +-1 signs of K
-// (boxes 2-3), code values of V (4-5), all by table lookup. Lane l converts row l/2, dims
+// (boxes 2-3), code values of V (4-5). Codes go through the pair tables, signs are set with bit
+// operations; every access names shared memory explicitly. Lane l converts row l/2, dims
 // [64*(l&1), +64).
-__device__ __forceinline__ void dequant_tq_page(const uint8_t* raw, uint8_t* work, int lane, const uint32_t* lutk,
-                                                const uint32_t* lutv, const uint4* lutg) {
+__device__ __forceinline__ void dequant_tq_page(uint32_t raw, uint32_t work, int lane, uint32_t lutk, uint32_t lutv) {
   const int row = lane >> 1, half = lane & 1;
 #pragma unroll
   for (int kv = 0; kv < 2; ++kv) {
-    const uint4* src = reinterpret_cast<const uint4*>(raw + (kv ? kTqVCodes : kTqKCodes) + row * 64 + half * 32);
-    const uint32_t* lut = kv ? lutv : lutk;
-    uint8_t* dst = work + (kv ? 4 : 0) * kBoxBytes;
+    const uint32_t src = raw + (kv ? kTqVCodes : kTqKCodes) + row * 64 + half * 32;
+    const uint32_t lut = kv ? lutv : lutk;
+    const uint32_t dst = work + (kv ? 4 : 0) * kBoxBytes;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const uint4 c = src[j];
+      const uint4 c = lds128(src + j * 16);
       const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
-        const uint4 r = make_uint4(lut[wv[w] & 255u], lut[(wv[w] >> 8) & 255u], lut[(wv[w] >> 16) & 255u],
-                                   lut[wv[w] >> 24]);
-        *reinterpret_cast<uint4*>(dst + swz(row, half * 8 + j * 4 + w)) = r;
+        const uint4 r = make_uint4(lds32(lut + (wv[w] & 255u) * 4), lds32(lut + ((wv[w] >> 8) & 255u) * 4),
+                                   lds32(lut + ((wv[w] >> 16) & 255u) * 4), lds32(lut + (wv[w] >> 24) * 4));
+        sts128(dst + swz(row, half * 8 + j * 4 + w), r);
       }
     }
   }
-  const uint2 sb = *reinterpret_cast<const uint2*>(raw + kTqKSign + row * 16 + half * 8);
-  const uint32_t bw[2] = {sb.x, sb.y};
+  // signs: bit 1 -> +1 (0x3F80), bit 0 -> -1 (0xBF80)
+  const uint32_t s0 = lds32(raw + kTqKSign + row * 16 + half * 8), s1 = lds32(raw + kTqKSign + row * 16 + half * 8 + 4);
 #pragma unroll
-  for (int by = 0; by < 8; ++by)    // dims 8*by .. 8*by+7 of this half
-    *reinterpret_cast<uint4*>(work + swz(row, 16 + half * 8 + by)) = lutg[(bw[by >> 2] >> (8 * (by & 3))) & 255u];
+  for (int by = 0; by < 8; ++by) {    // dims 8*by .. 8*by+7 of this half
+    const uint32_t bits = ((by < 4 ? s0 : s1) >> (8 * (by & 3))) & 255u;
+    uint32_t r[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t neg_lo = ((bits >> (2 * p)) & 1u) ^ 1u, neg_hi = ((bits >> (2 * p + 1)) & 1u) ^ 1u;
+      r[p] = 0x3F803F80u | (neg_lo << 15) | (neg_hi << 31);
+    }
+    sts128(work + swz(row, 16 + half * 8 + by), make_uint4(r[0], r[1], r[2], r[3]));
+  }
 }
 
 struct TqArgs {
@@ -162,19 +184,11 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcWarps * kWarpBytes) + warp * kTcStages;
   uint32_t* lutk = reinterpret_cast<uint32_t*>(smem + kTcWarps * kWarpBytes + kTcWarps * kTcStages * 8);
   uint32_t* lutv = lutk + 256;
-  uint4* lutg = reinterpret_cast<uint4*>(lutv + 256);
   if constexpr (KVQ == 2) {
     for (int e = threadIdx.x; e < 512; e += blockDim.x) {
       const float* cb = e < 256 ? tq.cbk : tq.cbv;
       const int i = e & 255;
       lutk[e] = pack_bf16x2(cb[i & 15], cb[i >> 4]);
-    }
-    for (int b = threadIdx.x; b < 256; b += blockDim.x) {
-      uint32_t r[4];
-#pragma unroll
-      for (int p = 0; p < 4; ++p)      // bit 1: +1 (0x3F80), bit 0: -1 (0xBF80)
-        r[p] = (((b >> (2 * p)) & 1) ? 0x3F80u : 0xBF80u) | ((((b >> (2 * p + 1)) & 1) ? 0x3F80u : 0xBF80u) << 16);
-      lutg[b] = make_uint4(r[0], r[1], r[2], r[3]);
     }
     __syncthreads();
   }
@@ -260,7 +274,8 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
     if constexpr (KVQ == 0) {
       kbase = tc::smem_u32(ring + s * kStageBytes);
     } else if constexpr (KVQ == 2) {
-      dequant_tq_page(ring + s * kTqRaw, work, lane, lutk, lutv, lutg);
+      dequant_tq_page(tc::smem_u32(ring + s * kTqRaw), tc::smem_u32(work), lane, tc::smem_u32(lutk),
+                      tc::smem_u32(lutv));
       __syncwarp();
       kbase = tc::smem_u32(work);
     } else {
@@ -290,18 +305,21 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
     }
     float vn[2][2];                                           // TurboQuant: V norm of this lane's tokens
     if constexpr (KVQ == 2) {
-      const __half* km = reinterpret_cast<const __half*>(ring + s * kTqRaw + kTqKMeta);
-      const __half* vm = reinterpret_cast<const __half*>(ring + s * kTqRaw + kTqVMeta);
+      const uint32_t mb = tc::smem_u32(ring + s * kTqRaw);
 #pragma unroll
-      for (int nb = 0; nb < 2; ++nb)
+      for (int nb = 0; nb < 2; ++nb) {
+        const uint32_t v2 = lds32(mb + kTqVMeta + (nb * 8 + 2 * t4) * 2);       // V norms of both tokens
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int tk = nb * 8 + 2 * t4 + e;
-          const float n = __half2float(km[tk * 2]), ng = n * __half2float(km[tk * 2 + 1]);
+          const uint32_t ng2 = lds32(mb + kTqKMeta + tk * 4);                   // (norm, gamma) fp16
+          const float n = __half2float(__ushort_as_half((unsigned short)(ng2 & 0xffffu)));
+          const float ng = n * __half2float(__ushort_as_half((unsigned short)(ng2 >> 16)));
           sc[nb][e] = n * sc[nb][e] + ng * sg[nb][e];
           sc[nb][2 + e] = n * sc[nb][2 + e] + ng * sg[nb][2 + e];
-          vn[nb][e] = __half2float(vm[tk]);
+          vn[nb][e] = __half2float(__ushort_as_half((unsigned short)(e ? (v2 >> 16) : (v2 & 0xffffu))));
         }
+      }
     }
     // ---- online softmax over the 16 tokens (log2 domain) ----
     float mx_a = -INFINITY, mx_b = -INFINITY;

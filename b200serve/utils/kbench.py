@@ -98,6 +98,18 @@ def run_one(M, N, K, iters=5):
     print(json.dumps({"case": "one", "M": M, "N": N, "K": K, "ok": True}))
 
 
+def partial_one(M, N, K, iters=5):
+    """A few launches of the stream-K partial GEMM (the decode path) at one shape, weights
+    rotating over copies larger than L2 (small case for an ncu capture)."""
+    n = max(2, -(-(320 << 20) // (N * K * 2)))
+    ws = [ops.pack_weight((torch.randn(N, K, device="cuda") * 0.02).bfloat16()) for _ in range(n)]
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    for i in range(iters):
+        ops.linear_partial(x, ws[i % n])
+    torch.cuda.synchronize()
+    print(json.dumps({"case": "partial_one", "M": M, "N": N, "K": K, "copies": n, "ok": True}))
+
+
 def attn_one(B=32, L=2304, nq=32, nkv=8, iters=5):
     """A few launches of the decode attention at one shape (small case for ncu)."""
     hd = 128
@@ -183,21 +195,6 @@ def tq_attn_one(B=32, L=2304, nq=32, nkv=8, kbits=4, vbits=4, iters=5):
     byts = B * L * nkv * (hd + hd // 8 + 6)
     print(json.dumps({"case": "tq_attn_one", "B": B, "L": L, "tps": tps, "nsplit": nsplit, "ms": round(ms, 4),
                       "GBps": round(byts / ms / 1e6, 1), "bf16_equiv_bytes_ratio": round(4 * hd / (hd + hd // 8 + 6), 2)}))
-
-
-def gguf_one(M=8, N=6144, K=4096, iters=5):
-    from b200serve.models.gguf_gpu import to_quant_weight
-    w = (torch.randn(N, K, device="cuda") * 0.02)
-    qw = to_quant_weight(w, "q4_k")
-    x = torch.randn(M, K, device="cuda").bfloat16()
-    for _ in range(iters):
-        ops.linear(x, qw)
-    torch.cuda.synchronize()
-    ms = time_cuda(lambda: ops.linear(x, qw))
-    wbytes = qw.codes.numel() * 4 + qw.meta.numel() * 4
-    ms_bf16 = time_cuda(lambda: ops.linear(x, ops.pack_weight(w.bfloat16())))
-    print(json.dumps({"case": "gguf_q4k", "M": M, "N": N, "K": K, "ms": round(ms, 4),
-                      "GBps_quant": round(wbytes / ms / 1e6, 1), "bf16_gemm_ms": round(ms_bf16, 4)}))
 
 
 def gguf_gemv_suite(M=8):
@@ -601,8 +598,8 @@ if __name__ == "__main__":
     if what == "tq_attn_one":
         tq_attn_one(*[int(v) for v in sys.argv[2:8]])
         sys.exit(0)
-    if what == "gguf_one":
-        gguf_one(*[int(v) for v in sys.argv[2:5]])
+    if what == "partial_one":
+        partial_one(*[int(v) for v in sys.argv[2:5]])
         sys.exit(0)
     if what == "gguf_gemv":
         gguf_gemv_suite(*[int(v) for v in sys.argv[2:3]])
