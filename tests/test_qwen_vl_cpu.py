@@ -38,8 +38,8 @@ def tiny_vl(tmp_path_factory):
     d = tmp_path_factory.mktemp("qwen3vl")
     cfg = Qwen3VLConfig(
         text_config=dict(vocab_size=512, hidden_size=128, num_hidden_layers=3, num_attention_heads=4,
-                         num_key_value_heads=2, head_dim=32, intermediate_size=256, max_position_embeddings=1024,
-                         rope_parameters={"rope_type": "default", "rope_theta": 10000.0, "mrope_section": [6, 5, 5],
+                         num_key_value_heads=2, head_dim=64, intermediate_size=256, max_position_embeddings=1024,
+                         rope_parameters={"rope_type": "default", "rope_theta": 10000.0, "mrope_section": [12, 10, 10],
                                           "mrope_interleaved": True}, tie_word_embeddings=False),
         vision_config=dict(depth=3, hidden_size=96, intermediate_size=192, num_heads=4, out_hidden_size=128,
                            patch_size=16, temporal_patch_size=2, spatial_merge_size=2, num_position_embeddings=64,
