@@ -12,8 +12,17 @@ quantised layer to produce the inputs of layer i + 1. The output directory is a 
 (qweight / qzeros / scales / g_idx per linear, fp16 elsewhere, ``quantization_config`` in
 config.json) that ``models/gptq.py`` and HF-style loaders read.
 
+Mixed precision: ``--rule REGEX=METHOD`` (first match on the linear's name wins, else
+``--bits``) picks per layer ``gptq4`` / ``gptq8`` (GPTQ at 4 / 8 bits), ``e8`` (E8 lattice vectors, one
+byte per 8 weights, models/e8.py, quantised with the same error feedback: each 8-column block takes its
+nearest codebook vector and the block's error is spread over the later columns through the
+Cholesky factor, the block form of the update) or ``bf16`` (kept). E8 layers are written as
+``e8_indices`` / ``e8_scales`` / ``e8_offsets`` with one ``e8_codebook``, 8-bit layers as the
+GPTQ tensors at 8 bits, and ``quantization_config`` records ``has_e8``, ``mixed_precision`` and
+``modules_not_quantized``.
+
   python -m b200serve.models.gptq_quantize --model DIR --output DIR [--bits 4] [--group 128]
-      [--act-order] [--samples 64] [--seqlen 512] [--device cuda]
+      [--act-order] [--samples 64] [--seqlen 512] [--device cuda] [--rule 'mlp[.]down=e8' ...]
 """
 
 from __future__ import annotations
@@ -21,6 +30,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import shutil
 
 import torch
@@ -92,6 +102,47 @@ def gptq_matrix(W: torch.Tensor, H: torch.Tensor, bits: int = 4, group: int = 12
     return Q[:, inv], scales, zeros, g_idx
 
 
+def e8_gptq_matrix(W: torch.Tensor, H: torch.Tensor, codebook: torch.Tensor, group: int = 128,
+                   damp: float = 0.01):
+    """E8 vector quantisation of W [N, K] with GPTQ error feedback over 8-column blocks. Each
+    group's (scale, offset) is set from the group's current values when the group starts (offset
+    = mean, scale = largest deviation); a block's error E moves the later columns by
+    -E U_bb^-1 U_b,later (U the upper Cholesky factor of H^-1). Returns (indices uint8 [N, K/8],
+    scales fp16 [N, G], offsets fp16 [N, G])."""
+    from b200serve.models import e8 as E8
+    W = W.clone().float()
+    H = H.clone().float()
+    N, K = W.shape
+    assert K % group == 0 and group % 8 == 0
+    dead = torch.diag(H) == 0
+    H[dead, dead] = 1.0
+    W[:, dead] = 0.0
+    H += damp * torch.mean(torch.diag(H)) * torch.eye(K, device=W.device)
+    U = torch.linalg.cholesky(torch.cholesky_inverse(torch.linalg.cholesky(H)), upper=True)
+    cb = codebook.float().to(W.device)
+    G = K // group
+    idx = torch.zeros(N, K // 8, dtype=torch.uint8, device=W.device)
+    scales = torch.zeros(N, G, device=W.device)
+    offsets = torch.zeros(N, G, device=W.device)
+    for c in range(0, K, 8):
+        gi = c // group
+        if c % group == 0:
+            grp = W[:, c:c + group]
+            o = grp.mean(1)
+            s = (grp - o[:, None]).abs().amax(1).clamp(min=1e-10)
+            # the checkpoint stores fp16; quantise against the stored values
+            scales[:, gi], offsets[:, gi] = s.half().float(), o.half().float()
+        s, o = scales[:, gi], offsets[:, gi]
+        blk = W[:, c:c + 8]
+        j = E8.nearest((blk - o[:, None]) / s[:, None], cb)
+        idx[:, c // 8] = j.to(torch.uint8)
+        err = blk - (cb[j] * s[:, None] + o[:, None])
+        if c + 8 < K:
+            X = torch.linalg.solve_triangular(U[c:c + 8, c:c + 8], err, upper=True, left=False)
+            W[:, c + 8:] -= X @ U[c:c + 8, c + 8:]
+    return idx, scales.to(torch.float16), offsets.to(torch.float16)
+
+
 def rtn_matrix(W: torch.Tensor, bits: int = 4, group: int = 128):
     """Round-to-nearest on the same grid (the baseline GPTQ improves on)."""
     N, K = W.shape
@@ -132,6 +183,16 @@ def pack_gptq(Q: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor, g_idx:
             "scales": scales.to(torch.float16), "g_idx": g_idx.to(torch.int32)}
 
 
+def _plus_one_zeros(qzeros: torch.Tensor, bits: int) -> torch.Tensor:
+    """GPTQ v1 zeros (zero - 1 per field) -> the zeros themselves (the ``_q8`` tensors' convention)."""
+    p = 32 // bits
+    z = qzeros.to(torch.int64) & 0xFFFFFFFF
+    f = torch.stack([(z >> (bits * i)) & ((1 << bits) - 1) for i in range(p)], -1) + 1
+    assert int(f.max()) < (1 << bits)
+    w = (f << (torch.arange(p, dtype=torch.int64) * bits)).sum(-1)
+    return torch.where(w >= (1 << 31), w - (1 << 32), w).to(torch.int32)
+
+
 # ------------------------------------------------------------------ whole checkpoint
 class _Stop(Exception):
     pass
@@ -154,12 +215,30 @@ def calibration_ids(tokenizer, vocab: int, samples: int, seqlen: int, text_file:
     return torch.randint(0, vocab, (samples, seqlen), generator=g)
 
 
+METHODS = ("gptq4", "gptq8", "e8", "bf16")
+
+
+def method_for(name: str, rules, bits: int) -> str:
+    """The method of linear ``name``: the first (regex, method) rule that matches, else from bits."""
+    for pat, m in rules or ():
+        if re.search(pat, name):
+            return m
+    return {2: "e8", 4: "gptq4", 8: "gptq8", 16: "bf16"}[bits]
+
+
 @torch.no_grad()
 def quantize_checkpoint(model_dir: str, out_dir: str, bits: int = 4, group: int = 128, act_order: bool = False,
                         samples: int = 64, seqlen: int = 512, device: str = None, text_file: str = None,
-                        log=print) -> dict:
-    """GPTQ-quantise every decoder linear of the HF checkpoint at ``model_dir`` into ``out_dir``.
-    Returns {layer linear name: relative output error on the calibration inputs}."""
+                        log=print, rules=None, codebook=None) -> dict:
+    """GPTQ-quantise every decoder linear of the HF checkpoint at ``model_dir`` into ``out_dir``
+    (per-layer methods from ``rules``: [(regex, method)], methods in METHODS; ``codebook`` the
+    E8 codebook, default models/e8.lattice_codebook()). Returns {layer linear name: relative
+    output error on the calibration inputs}."""
+    from b200serve.models import e8 as E8
+    for _, m in rules or ():
+        assert m in METHODS, f"unknown method {m}"
+    cb = (codebook if codebook is not None else E8.lattice_codebook()).float()
+    kept, used = [], set()
     from safetensors.torch import save_file
     from transformers import AutoModelForCausalLM
     from b200serve.core.config import TRUST_REMOTE_CODE
@@ -209,13 +288,34 @@ def quantize_checkpoint(model_dir: str, out_dir: str, bits: int = 4, group: int 
         for hh in hs:
             hh.remove()
         for n, m in lins.items():
-            Q, sc, zr, gi = gptq_matrix(m.weight.data.float(), hess[n], bits, group, act_order=act_order)
-            what = dequant(Q, sc, zr, gi).to(m.weight.dtype)
+            full = f"model.layers.{li}.{n}"
+            meth = method_for(full, rules, bits)
+            used.add(meth)
+            W = m.weight.data.float()
+            if meth == "bf16":
+                kept.append(full)
+                errors[f"layers.{li}.{n}"] = 0.0
+                continue
+            if meth == "e8":
+                gs = group if W.shape[1] % group == 0 else 32
+                idx, sc, of = e8_gptq_matrix(W, hess[n], cb.to(W.device), gs)
+                what = E8.dequantize(idx, sc, of, cb.to(W.device), gs).to(m.weight.dtype)
+                packed[full] = {"e8_indices": E8.pack_indices(idx.cpu()), "e8_scales": sc.t().contiguous().cpu(),
+                                "e8_offsets": of.t().contiguous().cpu()}
+            else:
+                b = 4 if meth == "gptq4" else 8
+                Q, sc, zr, gi = gptq_matrix(W, hess[n], b, group, act_order=act_order)
+                what = dequant(Q, sc, zr, gi).to(m.weight.dtype)
+                t = pack_gptq(Q.cpu(), sc.cpu(), zr.cpu(), gi.cpu(), b)
+                assert not (b == 4 and bits == 8), "4-bit layers need --bits 4 (8-bit layers then use the _q8 names)"
+                if b == 8 and bits != 8:                  # 8-bit layers next to 4-bit ones: the _q8 names, zero as is
+                    t = {"qweight_q8": t["qweight"], "scales_q8": t["scales"], "g_idx_q8": t["g_idx"],
+                         "qzeros_q8": _plus_one_zeros(t["qzeros"], 8)}
+                packed[full] = t
             xs = torch.cat([x for x, _ in outs_ref[n]])
-            ref = xs @ m.weight.data.float().t()
+            ref = xs @ W.t()
             errors[f"layers.{li}.{n}"] = ((xs @ what.float().t() - ref).norm() / ref.norm()).item()
             m.weight.data.copy_(what)
-            packed[f"model.layers.{li}.{n}"] = pack_gptq(Q.cpu(), sc.cpu(), zr.cpu(), gi.cpu(), bits)
         nxt = []
         for x, kw in inputs:                         # the quantised layer feeds the next one
             y = layer(x, **kw)
@@ -232,10 +332,17 @@ def quantize_checkpoint(model_dir: str, out_dir: str, bits: int = 4, group: int 
                 tensors[f"{base}.{suffix}"] = t.contiguous()
         else:
             tensors[k] = v.detach().to(torch.float16).cpu().contiguous()
+    if "e8" in used:
+        tensors["e8_codebook"] = cb.cpu().contiguous()
     save_file(tensors, os.path.join(out_dir, "model.safetensors"), metadata={"format": "pt"})
     cfg = model.config.to_dict()
-    cfg["quantization_config"] = {"quant_method": "gptq", "bits": bits, "group_size": group, "desc_act": act_order,
-                                  "sym": False, "checkpoint_format": "gptq"}
+    main_bits = 8 if bits == 8 else 4
+    cfg["quantization_config"] = {"quant_method": "gptq", "bits": main_bits, "group_size": group,
+                                  "desc_act": act_order, "sym": False, "checkpoint_format": "gptq",
+                                  "mixed_precision": len(used) > 1 or bool(kept) or "e8" in used,
+                                  "has_e8": "e8" in used,
+                                  "has_q8": any(k.endswith("qweight_q8") for t in packed.values() for k in t),
+                                  "modules_not_quantized": kept}
     cfg["torch_dtype"] = "float16"
     with open(os.path.join(out_dir, "config.json"), "w") as fh:
         json.dump(cfg, fh, indent=1)
@@ -250,15 +357,19 @@ def main(argv=None):
     ap = argparse.ArgumentParser("b200serve GPTQ quantiser")
     ap.add_argument("--model", required=True)
     ap.add_argument("--output", required=True)
-    ap.add_argument("--bits", type=int, default=4, choices=[2, 4, 8])
+    ap.add_argument("--bits", type=int, default=4, choices=[2, 4, 8], help="2: E8 vectors, 4 / 8: GPTQ")
     ap.add_argument("--group", type=int, default=128)
     ap.add_argument("--act-order", action="store_true")
     ap.add_argument("--samples", type=int, default=64)
     ap.add_argument("--seqlen", type=int, default=512)
     ap.add_argument("--device", default=None)
     ap.add_argument("--text", default=None, help="calibration text file (default: random token ids)")
+    ap.add_argument("--rule", action="append", default=[],
+                    help="REGEX=METHOD (gptq4, gptq8, e8, bf16) for the linears whose name matches")
     a = ap.parse_args(argv)
-    errs = quantize_checkpoint(a.model, a.output, a.bits, a.group, a.act_order, a.samples, a.seqlen, a.device, a.text)
+    rules = [tuple(r.rsplit("=", 1)) for r in a.rule]
+    errs = quantize_checkpoint(a.model, a.output, a.bits, a.group, a.act_order, a.samples, a.seqlen, a.device, a.text,
+                               rules=rules)
     print(json.dumps({"layers": len(errs), "max_rel_output_error": max(errs.values())}))
 
 

@@ -29,22 +29,28 @@ def _load():
     with _lock:
         if _ext is None and _ext_error is None:
             try:
-                from b200serve.ops.build import build, built_library_path, EXT_NAME
-                path = built_library_path()
+                from b200serve.ops.build import build, built_library_path, _variant
+                checked = _checked_requested()
+                path = built_library_path(checked)
                 if os.path.exists(path) and not os.environ.get("B200_JIT"):
                     # import the in-tree build as is (no ninja staleness check on a copied tree)
                     import importlib.machinery
                     import importlib.util
-                    loader = importlib.machinery.ExtensionFileLoader(EXT_NAME, path)
-                    spec = importlib.util.spec_from_file_location(EXT_NAME, path, loader=loader)
+                    name = _variant(checked)[0]
+                    loader = importlib.machinery.ExtensionFileLoader(name, path)
+                    spec = importlib.util.spec_from_file_location(name, path, loader=loader)
                     mod = importlib.util.module_from_spec(spec)
                     loader.exec_module(mod)
                     _ext = mod
                 else:
-                    _ext = build(verbose=bool(os.environ.get("B200_BUILD_VERBOSE")))
+                    _ext = build(verbose=bool(os.environ.get("B200_BUILD_VERBOSE")), checked=checked)
             except Exception as e:  # recorded and re-raised at first CUDA use
                 _ext_error = e
     return _ext
+
+
+def _checked_requested() -> bool:
+    return os.environ.get("B200_BOUNDS_CHECK", "0") not in ("", "0")
 
 
 def ext():
@@ -61,7 +67,21 @@ def extension_loaded() -> bool:
 
 def extension_path() -> str:
     from b200serve.ops.build import built_library_path
-    return built_library_path()
+    return built_library_path(_checked_requested())
+
+
+def bounds_checked() -> bool:
+    """True when the loaded extension is the bounds-checked build (B200_BOUNDS_CHECK=1)."""
+    return bool(ext().bounds_checked())
+
+
+def bounds_errors(reset: bool = True) -> dict:
+    """{kernel file: first out-of-range index code} recorded by the bounds-checked build since the
+    last reset (synchronises the device). Codes: 0x1xx RoPE/KV write/embedding, 0x2xx decode
+    attention, 0x3xx prefill attention, 0x4xx TurboQuant, 0x5xx recurrent-state slots, 0x6xx
+    expert ids, 0x8xx vision. Always empty for the release build."""
+    torch.cuda.synchronize()
+    return dict(ext().bounds_errors(reset))
 
 
 _launches = [0]
@@ -510,15 +530,20 @@ def gguf_stream(x, parts, mode, out, ldo, push=None, mc=0):
     ws, counters, nsm = _gguf_scratch(x.device)
     xc = x if (x.stride(1) == 1 and x.stride(0) % 8 == 0) else x.contiguous()
     _cuda(x)
+    cb = parts[0].codebook.data_ptr() if parts[0].bits == 2 else 0
     return ext().gguf_stream(xc, [p.codes for p in parts], [p.meta for p in parts], [p.N for p in parts],
                              [p.bits for p in parts], [p.group for p in parts], mode,
                              out if out is not None else _NO_OUT, ldo, ws, counters,
-                             push if push is not None else _NO_PUSH, mc, nsm, 0)
+                             push if push is not None else _NO_PUSH, mc, nsm, 0, cb)
 
 
 def _gs_ok(x, parts, tile=16):
-    return (parts is not None and x.is_cuda and 1 <= x.shape[0] <= 16 and len(parts) <= 4
-            and len({p.K for p in parts}) == 1 and all(p.K % 256 == 0 and p.N % tile == 0 for p in parts))
+    if not (parts is not None and x.is_cuda and 1 <= x.shape[0] <= 16 and len(parts) <= 4
+            and len({p.K for p in parts}) == 1 and all(p.K % 256 == 0 and p.N % tile == 0 for p in parts)):
+        return False
+    e8 = [p.bits == 2 for p in parts]
+    # E8 parts stream together only with E8 parts of the same codebook
+    return not any(e8) or (all(e8) and len({p.codebook.data_ptr() for p in parts}) == 1)
 
 
 def qlinear_partial(x, w):
@@ -633,12 +658,15 @@ class PackedWeight:
 
 
 class QuantWeight:
-    """A GGUF-quantised [N, K] weight in the fragment order of ops/csrc/gguf_gemm.cu:
+    """A block-quantised [N, K] weight in the fragment order of ops/csrc/gguf_gemm.cu:
     4-bit codes with bf16 scale and -min per 32 (Q4_K) or int8 codes with a bf16
-    scale per ``group`` (Q6_K: 16, Q8_0: 32)."""
+    scale per ``group`` (Q6_K: 16, Q8_0: 32); ``bits`` 2: E8 vector codes (one byte per 8
+    weights) with a bf16 scale and offset per ``group``, decoded through ``codebook``
+    (models/e8.py)."""
 
-    def __init__(self, codes, meta, N, K, bits, group):
+    def __init__(self, codes, meta, N, K, bits, group, codebook=None):
         self.codes, self.meta, self.N, self.K, self.bits, self.group = codes, meta, N, K, bits, group
+        self.codebook = codebook
         self.shape = (N, K)
         self.device = codes.device
         self.dtype = torch.bfloat16
@@ -660,12 +688,16 @@ class QuantWeight:
             buf = torch.empty(need, dtype=torch.bfloat16, device=self.device)
             _dequant_scratch[key] = buf
         _cuda(self.codes)
-        ext().gguf_dequant_packed(self.codes, self.meta, self.N, self.K, self.bits, self.group, buf)
+        ext().gguf_dequant_packed(self.codes, self.meta, self.N, self.K, self.bits, self.group, buf,
+                                  self.codebook.data_ptr() if self.bits == 2 else 0)
         return PackedWeight.from_packed(buf[:need].view(-1, 64), self.N, self.K)
 
     def dequantize(self) -> torch.Tensor:
         """bf16 [N, K] (used for prefill-sized batches and tests)."""
         N, K = self.N, self.K
+        if self.bits == 2:
+            from b200serve.models.e8 import dequantize_packed_e8
+            return dequantize_packed_e8(self).to(torch.bfloat16)
         S, KS = N // 16, K // 16
         lanes = torch.arange(32, device=self.device)
         g, t = lanes // 4, lanes % 4
@@ -792,7 +824,8 @@ def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspac
                 out.copy_(y)
                 return out
             return y
-        if x.is_cuda and M <= 32 and epilogue in (EPI_BF16, EPI_F32) and bias is None and residual is None:
+        if (x.is_cuda and M <= 32 and w.bits != 2 and epilogue in (EPI_BF16, EPI_F32) and bias is None
+                and residual is None):
             y = torch.empty(M, N, dtype=x.dtype, device=x.device)
             _cuda(x)
             ext().gguf_gemm(x.contiguous(), w.codes, w.meta, N, w.bits, w.group, y)

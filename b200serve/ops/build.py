@@ -27,27 +27,45 @@ def sources() -> list:
     return sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
 
 
-def build(verbose: bool = False):
+# The bounds-checked variant: every data-dependent global index (KV slots and block-table
+# entries, recurrent-state slots, token and expert ids, RoPE positions) is range-checked in the
+# kernel; an index out of range is recorded in a per-file error word (read with
+# ``bounds_errors()``) and the access is skipped. Loaded instead of the release build when
+# B200_BOUNDS_CHECK=1.
+CHECKED_NAME = EXT_NAME + "_checked"
+CHECKED_DIR = os.path.join(HERE, "_build_checked")
+CHECK_DEFINE = "-DB200_BOUNDS_CHECK"
+
+
+def _variant(checked: bool):
+    return (CHECKED_NAME, CHECKED_DIR) if checked else (EXT_NAME, BUILD_DIR)
+
+
+def build(verbose: bool = False, checked: bool = False):
     """Compile (incrementally, via ninja) and import the extension module."""
     os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
     from torch.utils.cpp_extension import load
-    os.makedirs(BUILD_DIR, exist_ok=True)
+    name, bdir = _variant(checked)
+    os.makedirs(bdir, exist_ok=True)
+    extra = [CHECK_DEFINE] if checked else []
     return load(
-        name=EXT_NAME,
+        name=name,
         sources=sources(),
-        extra_cuda_cflags=NVCC_FLAGS,
-        extra_cflags=["-O3", "-std=c++17"],
+        extra_cuda_cflags=NVCC_FLAGS + extra,
+        extra_cflags=["-O3", "-std=c++17"] + extra,
         extra_ldflags=["-lcuda"],
-        build_directory=BUILD_DIR,
+        build_directory=bdir,
         verbose=verbose,
     )
 
 
-def built_library_path() -> str:
-    return os.path.join(BUILD_DIR, EXT_NAME + ".so")
+def built_library_path(checked: bool = False) -> str:
+    name, bdir = _variant(checked)
+    return os.path.join(bdir, name + ".so")
 
 
 if __name__ == "__main__":
     import sys
-    build(verbose="-v" in sys.argv)
-    print(built_library_path())
+    chk = "--checked" in sys.argv
+    build(verbose="-v" in sys.argv, checked=chk)
+    print(built_library_path(chk))

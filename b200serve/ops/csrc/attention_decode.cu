@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
     const __nv_bfloat16* __restrict__ v_cache, const int* __restrict__ block_tables,
     const int* __restrict__ seq_lens, int max_blocks, int nkv, float scale_log2, int tps,
     float* __restrict__ part_acc, float* __restrict__ part_ml, __nv_bfloat16* __restrict__ out, int nsplit,
-    int window = 0, float softcap = 0.f) {
+    int window = 0, float softcap = 0.f, int nblocks = 0x7fffffff) {
   constexpr int E = HD / 32;          // value dims per lane
   __shared__ float q_s[G][HD];
   __shared__ __align__(16) float p_s[kAttnWarps][kPage][G < 4 ? 4 : G];
@@ -97,7 +97,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
   const int tok = lane & 15, half = lane >> 4;
   const int* bt = block_tables + (size_t)b * max_blocks;
   auto page_offset = [&](int page_start) {
-    return ((size_t)bt[page_start / kPage] * nkv + kvh) * kPage * HD;
+    const int blk = max(table_block(bt, page_start / kPage, max_blocks, nblocks, 0x203), 0);   // checked: block 0
+    return ((size_t)blk * nkv + kvh) * kPage * HD;
   };
 
   // one page: scores, online softmax, p.V
@@ -291,7 +292,8 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tenso
 #define B200_DEC(HDV, GV)                                                                                    \
   launch_pdl(paged_decode_kernel<HDV, GV>, grid, dim3(kAttnWarps * 32), 0, stream, qp, kp, vp,                \
              (const int*)block_tables.data_ptr<int>(), (const int*)seq_lens.data_ptr<int>(),                  \
-             (int)block_tables.size(1), nkv, sl2, (int)tps, pa, pm, op, (int)nsplit, (int)window, (float)softcap)
+             (int)block_tables.size(1), nkv, sl2, (int)tps, pa, pm, op, (int)nsplit, (int)window, (float)softcap, \
+             (int)k_cache.size(0))
   if (HD == 256 && G == 4) B200_DEC(256, 4);
   else if (HD == 256 && G == 2) B200_DEC(256, 2);
   else if (HD == 256 && G == 1) B200_DEC(256, 1);
@@ -437,3 +439,5 @@ extern "C" __attribute__((visibility("default"))) int b200_paged_decode_attentio
   }
   return 0;
 }
+
+B200_BOUNDS_ACCESSOR(attention_decode)

@@ -167,7 +167,8 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
     const __nv_bfloat16* __restrict__ q, const int* __restrict__ block_tables, const int* __restrict__ seq_lens,
     int max_blocks, int nkv, float scale_log2, int tps, float* __restrict__ part_acc, float* __restrict__ part_ml,
     __nv_bfloat16* __restrict__ out, int nsplit, int* err, const uint8_t* __restrict__ kq,
-    const uint8_t* __restrict__ vq, const __half* __restrict__ ks, const __half* __restrict__ vs, const TqArgs tq) {
+    const uint8_t* __restrict__ vq, const __half* __restrict__ ks, const __half* __restrict__ vs, const TqArgs tq,
+    int nblocks) {
   static_assert(G >= 1 && G <= 16, "query heads per kv head");
   constexpr int KSTEPS = KVQ == 2 ? 16 : 8;        // 16-dim MMA k-steps of the (virtual) key
   extern __shared__ uint8_t smem_raw[];
@@ -235,7 +236,8 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
   auto issue = [&](int i) {
     const int s = i % kTcStages;
     const int tok0 = first + i * kTcWarps * 16;
-    const int page = bt[tok0 >> 4] * nkv + kvh;
+    const int blk = max(table_block(bt, tok0 >> 4, max_blocks, nblocks, 0x201), 0);   // checked: block 0
+    const int page = blk * nkv + kvh;
     if constexpr (KVQ == 0) {
       const int y = page * 16;
       uint8_t* st = ring + s * kStageBytes;
@@ -522,7 +524,7 @@ static void decode_tc_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor
     launch_pdl(paged_decode_tc_kernel<GV, KQ>, grid, dim3(kTcWarps * 32), smem, stream, tk, tv,                \
                reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), (const int*)block_tables.data_ptr<int>(),  \
                (const int*)seq_lens.data_ptr<int>(), (int)block_tables.size(1), nkv, sl2, (int)tps, pa, pm, op, \
-               (int)nsplit, decode_tc_err_word(), kq, vq, ksc, vsc, tq);                                       \
+               (int)nsplit, decode_tc_err_word(), kq, vq, ksc, vsc, tq, (int)k_cache.size(0));                 \
   }
 #define B200_TC(GV) { if (kvq == 2) B200_TC1(GV, 2) else if (kvq) B200_TC1(GV, 1) else B200_TC1(GV, 0) }
   switch (G) {
@@ -583,3 +585,5 @@ void paged_decode_attention_tq(torch::Tensor q_rot, torch::Tensor q_jl, torch::T
                  reinterpret_cast<const __half*>(k_meta.data_ptr()), reinterpret_cast<const __half*>(v_meta.data_ptr()),
                  k_codes.size(1), tq);
 }
+
+B200_BOUNDS_ACCESSOR(attention_decode_tc)

@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(
     const int* __restrict__ seq_lens, const int* __restrict__ q_start, const int* __restrict__ cu_q,
     __nv_bfloat16* __restrict__ out, int nq, int nkv, float scale_log2, const uint8_t* __restrict__ kq,
     const uint8_t* __restrict__ vq, const __half* __restrict__ ksc, const __half* __restrict__ vsc, int window,
-    float softcap) {
+    float softcap, int nblocks) {
   constexpr int LD = HD + 8;  // padded smem row (bf16) -> conflict-free 32-bit fragment loads
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(smem_raw);          // [2][64][LD]
@@ -102,8 +102,9 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(
       for (int c = threadIdx.x; c < CH; c += 128) {
         const int tok = c / (HD / 32), part = c % (HD / 32);
         const int abs_tok = tile * PF_BK + tok;
-        const bool ok = abs_tok < kv_end;
-        const int page = ok ? bt[abs_tok >> 4] : 0;
+        const int pg = abs_tok < kv_end ? table_block(bt, abs_tok >> 4, max_blocks, nblocks, 0x301) : -1;
+        const bool ok = pg >= 0;
+        const int page = ok ? pg : 0;
         const size_t row = ((size_t)page * nkv + kvh) * 16 + (abs_tok & 15);
         uint8_t* dk = qraw + ((buf * 2 + 0) * PF_BK + tok) * (HD / 2) + part * 16;
         uint8_t* dv = qraw + ((buf * 2 + 1) * PF_BK + tok) * (HD / 2) + part * 16;
@@ -122,8 +123,9 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(
     for (int c = threadIdx.x; c < CH; c += 128) {
       const int tok = c / (HD / 8), part = c % (HD / 8);
       const int abs_tok = tile * PF_BK + tok;
-      const bool ok = abs_tok < kv_end;
-      const int page = ok ? bt[abs_tok >> 4] : 0;
+      const int pg = abs_tok < kv_end ? table_block(bt, abs_tok >> 4, max_blocks, nblocks, 0x301) : -1;
+      const bool ok = pg >= 0;
+      const int page = ok ? pg : 0;
       const size_t off = (((size_t)page * nkv + kvh) * 16 + (abs_tok & 15)) * HD + part * 8;
       const uint32_t dk = static_cast<uint32_t>(__cvta_generic_to_shared(ks + (buf * PF_BK + tok) * LD + part * 8));
       const uint32_t dv = static_cast<uint32_t>(__cvta_generic_to_shared(vs + (buf * PF_BK + tok) * LD + part * 8));
@@ -269,7 +271,7 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(
 // (2p, 2p+1) of each 8-dim group sit in nibbles (p, p + 4) of the group's 32-bit word.
 __global__ void q4_dequant_pages_kernel(const int* __restrict__ block_ids, int n, int nkv,
                                         const uint32_t* __restrict__ codes, const __half* __restrict__ scales,
-                                        __nv_bfloat16* __restrict__ out) {
+                                        __nv_bfloat16* __restrict__ out, int nblocks) {
   pdl_wait();
   pdl_trigger();
   const int64_t words = (int64_t)n * nkv * 16 * 16;
@@ -277,7 +279,9 @@ __global__ void q4_dequant_pages_kernel(const int* __restrict__ block_ids, int n
     const int64_t row = i >> 4;                      // (j, h, token) row of the output
     const int g = (int)(i & 15);
     const int j = (int)(row / (nkv * 16));
-    const int64_t src_row = (int64_t)block_ids[j] * nkv * 16 + row % (nkv * 16);
+    int blk = block_ids[j];
+    if (!B200_IN_RANGE(blk, nblocks, 0x303)) blk = 0;       // checked builds: read block 0 instead
+    const int64_t src_row = (int64_t)blk * nkv * 16 + row % (nkv * 16);
     const uint32_t w = codes[src_row * 16 + g];
     const float sc = __half2float(scales[src_row]);
     uint32_t o[4];
@@ -321,7 +325,7 @@ static void prefill_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v
         reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()), (const int*)block_tables.data_ptr<int>(),   \
         (int)block_tables.size(1), (const int*)seq_lens.data_ptr<int>(), (const int*)q_start.data_ptr<int>(),    \
         (const int*)cu_q.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nq, nkv, sl2,       \
-        kq, vq, ksc, vsc, window, softcap);                                                                     \
+        kq, vq, ksc, vsc, window, softcap, (int)k_cache.size(0));                                               \
   }
   if (kvq) {
     TORCH_CHECK(HD == 128, "int4 KV cache needs head_dim 128");
@@ -360,5 +364,8 @@ void q4_dequant_pages(torch::Tensor block_ids, torch::Tensor codes, torch::Tenso
   const int blocks = (int)std::min<int64_t>((words + 255) / 256, 148 * 8);
   launch_pdl(q4_dequant_pages_kernel, dim3(blocks), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
              (const int*)block_ids.data_ptr<int>(), n, nkv, reinterpret_cast<const uint32_t*>(codes.data_ptr()),
-             reinterpret_cast<const __half*>(scales.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+             reinterpret_cast<const __half*>(scales.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+             (int)codes.size(0));
 }
+
+B200_BOUNDS_ACCESSOR(attention_prefill)

@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(
     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
     const __nv_bfloat16* __restrict__ q, const int* __restrict__ block_tables, int max_blocks,
     const int* __restrict__ seq_lens, const int* __restrict__ q_start, const int* __restrict__ cu_q,
-    __nv_bfloat16* __restrict__ out, int nq, int nkv, float scale_log2, int* err) {
+    __nv_bfloat16* __restrict__ out, int nq, int nkv, float scale_log2, int* err, int nblocks) {
   constexpr int QT = kPT_Rows / G;                  // query tokens per CTA
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -116,8 +116,9 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(
         tc::mbar_arrive_expect_tx(&kfull[s], kPT_Tile);
         for (int pg = 0; pg < 8; ++pg) {
           const int blk = j * 8 + pg;
-          const int b = blk < max_blocks ? bt[blk] : 0;
-          const int y = (max(b, 0) * nkv + kvh) * 16;
+          const int b0 = blk < max_blocks ? bt[blk] : 0;   // -1 (no block) past the sequence reads block 0
+          const int b = b0 < 0 || !B200_IN_RANGE(b0, nblocks, 0x311) ? 0 : b0;
+          const int y = (b * nkv + kvh) * 16;
           uint8_t* dst = smem + kPT_K + s * kPT_Tile + pg * 2048;
           tc::tma_load_2d(dst, &tm_k, &kfull[s], 0, y, 0ull);
           tc::tma_load_2d(dst + kPT_Half, &tm_k, &kfull[s], 64, y, 0ull);
@@ -126,8 +127,9 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(
         tc::mbar_arrive_expect_tx(&vfull[s], kPT_Tile);
         for (int pg = 0; pg < 8; ++pg) {
           const int blk = j * 8 + pg;
-          const int b = blk < max_blocks ? bt[blk] : 0;
-          const int y = (max(b, 0) * nkv + kvh) * 16;
+          const int b0 = blk < max_blocks ? bt[blk] : 0;   // -1 (no block) past the sequence reads block 0
+          const int b = b0 < 0 || !B200_IN_RANGE(b0, nblocks, 0x311) ? 0 : b0;
+          const int y = (b * nkv + kvh) * 16;
           uint8_t* dst = smem + kPT_V + s * kPT_Tile + pg * 2048;
           tc::tma_load_2d(dst, &tm_v, &vfull[s], 0, y, 0ull);
           tc::tma_load_2d(dst + kPT_Half, &tm_v, &vfull[s], 64, y, 0ull);
@@ -417,7 +419,7 @@ void paged_prefill_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::T
                reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), (const int*)block_tables.data_ptr<int>(), \
                (int)block_tables.size(1), (const int*)seq_lens.data_ptr<int>(),                              \
                (const int*)q_start.data_ptr<int>(), (const int*)cu_q.data_ptr<int>(),                       \
-               reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nq, nkv, sl2, g_pt_err);                  \
+               reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), nq, nkv, sl2, g_pt_err, (int)k_cache.size(0)); \
   }
   switch (G) {
     case 1: B200_PT(1) break;
@@ -428,3 +430,5 @@ void paged_prefill_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::T
   }
 #undef B200_PT
 }
+
+B200_BOUNDS_ACCESSOR(attention_prefill_tc)

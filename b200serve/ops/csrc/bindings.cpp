@@ -30,9 +30,10 @@ std::vector<int64_t> gguf_stream_plan(int64_t N, int64_t K, int64_t num_sms);
 std::vector<int64_t> gguf_stream(torch::Tensor x, std::vector<torch::Tensor> codes, std::vector<torch::Tensor> metas,
                                  std::vector<int64_t> ns, std::vector<int64_t> bits, std::vector<int64_t> groups,
                                  int64_t mode, torch::Tensor out, int64_t ldo, torch::Tensor ws, torch::Tensor counters,
-                                 torch::Tensor push_ptrs, int64_t mc_ptr, int64_t num_sms, int64_t wait_ms);
+                                 torch::Tensor push_ptrs, int64_t mc_ptr, int64_t num_sms, int64_t wait_ms,
+                                 int64_t e8_codebook);
 void gguf_dequant_packed(torch::Tensor codes, torch::Tensor meta, int64_t N, int64_t K, int64_t bits, int64_t group,
-                         torch::Tensor out);
+                         torch::Tensor out, int64_t e8_codebook);
 void gemm_grouped_ep(torch::Tensor act, torch::Tensor w_packed, int64_t N, int64_t E, torch::Tensor offsets,
                      int64_t max_rows, torch::Tensor out, torch::Tensor ws, torch::Tensor counters, int64_t epi,
                      int64_t ag_flags_ptr, int64_t ag_n, int64_t ag_epoch_ptr, torch::Tensor comb_meta,
@@ -166,7 +167,38 @@ void shortconv_layer(torch::Tensor y, torch::Tensor conv_w, torch::Tensor conv_s
                      c10::optional<torch::Tensor> cu_q, torch::Tensor q_start, torch::Tensor slots,
                      torch::Tensor out);
 
+// Error words of the bounds-checked build, one per translation unit with checked indices.
+#define B200_BOUNDS_UNITS(X)                                                                    \
+  X(norm_rope) X(attention_decode) X(attention_decode_tc) X(attention_prefill) X(attention_prefill_tc) \
+  X(kv_turboquant) X(deltanet) X(shortconv) X(ep_a2a) X(vision)
+#define B200_BOUNDS_DECL(u) int64_t bounds_error_##u(bool reset);
+B200_BOUNDS_UNITS(B200_BOUNDS_DECL)
+#undef B200_BOUNDS_DECL
+
+// {unit: first recorded error code} for the units with a recorded error (empty in release builds).
+static py::dict bounds_errors(bool reset) {
+  py::dict d;
+#define B200_BOUNDS_READ(u)                         \
+  {                                                 \
+    const int64_t v = bounds_error_##u(reset);      \
+    if (v) d[#u] = v;                               \
+  }
+  B200_BOUNDS_UNITS(B200_BOUNDS_READ)
+#undef B200_BOUNDS_READ
+  return d;
+}
+
+static bool bounds_checked() {
+#ifdef B200_BOUNDS_CHECK
+  return true;
+#else
+  return false;
+#endif
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("bounds_errors", &bounds_errors, py::arg("reset") = true);
+  m.def("bounds_checked", &bounds_checked);
   m.doc() = "b200serve sm_100a kernels";
   m.def("rmsnorm_fused", &rmsnorm_fused);
   m.def("qkv_post", &qkv_post);

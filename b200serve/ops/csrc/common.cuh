@@ -146,6 +146,42 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 bool pdl_enabled();
 
+// Bounds-checked builds (compiled with -DB200_BOUNDS_CHECK: the b200_ops_checked extension that
+// ops loads when B200_BOUNDS_CHECK=1). B200_IN_RANGE(i, n, code) is false for an index outside
+// [0, n): it records `code` in this translation unit's error word (the first one wins) and the
+// caller skips the access, so a bad index shows up as an error code instead of a fault. Release
+// builds compile the check to `true`. B200_BOUNDS_ACCESSOR(name) defines the host reader
+// `int64_t bounds_error_<name>(bool reset)` of the unit's word (0 in release builds).
+#ifdef B200_BOUNDS_CHECK
+static __device__ int g_b200_bounds_err;
+#define B200_IN_RANGE(i, n, code)                                                           \
+  (((unsigned long long)(long long)(i) < (unsigned long long)(long long)(n)) ||             \
+   (atomicCAS(&g_b200_bounds_err, 0, (int)(code)), false))
+#define B200_BOUNDS_ACCESSOR(name)                                                          \
+  int64_t bounds_error_##name(bool reset) {                                                 \
+    int v = 0;                                                                              \
+    B200_CHECK_CUDA(cudaMemcpyFromSymbol(&v, g_b200_bounds_err, sizeof(int)));              \
+    if (reset) {                                                                            \
+      const int z = 0;                                                                      \
+      B200_CHECK_CUDA(cudaMemcpyToSymbol(g_b200_bounds_err, &z, sizeof(int)));              \
+    }                                                                                       \
+    return v;                                                                               \
+  }
+#else
+#define B200_IN_RANGE(i, n, code) true
+#define B200_BOUNDS_ACCESSOR(name) \
+  int64_t bounds_error_##name(bool) { return 0; }
+#endif
+
+// Block id of table entry `idx` of a paged-KV block-table row: bt[idx] in release builds; in
+// checked builds -1 when idx is outside [0, max_blocks) (recorded as code + 1) or the block id
+// outside [0, nblocks) (recorded as code).
+static __device__ __forceinline__ int table_block(const int* bt, int idx, int max_blocks, int nblocks, int code) {
+  if (!B200_IN_RANGE(idx, max_blocks, code + 1)) return -1;
+  const int blk = bt[idx];
+  return B200_IN_RANGE(blk, nblocks, code) ? blk : -1;
+}
+
 // Deadline (ns) of every cross-GPU flag wait, passed to the kernels as an argument (so a CUDA
 // graph keeps the value it was captured with). Default 2 s; B200_FLAG_WAIT_MS or
 // set_flag_wait_ms() change it.

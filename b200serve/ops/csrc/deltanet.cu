@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(256) dn_prep_kernel(
     const __nv_bfloat16* __restrict__ y, int ystride, const float* __restrict__ conv_w,
     const float* __restrict__ A, const float* __restrict__ dt_bias, const float* __restrict__ conv_state,
     const int* __restrict__ cu_q, const int* __restrict__ q_start, const int* __restrict__ slots,
-    __nv_bfloat16* __restrict__ xc, float* __restrict__ gb, int T, int S, int nk, int nv) {
+    __nv_bfloat16* __restrict__ xc, float* __restrict__ gb, int T, int S, int nk, int nv, int nstates) {
   constexpr int E = D / 32;
   pdl_wait();
   pdl_trigger();
@@ -72,6 +72,7 @@ __global__ void __launch_bounds__(256) dn_prep_kernel(
   const int s = seq_of(cu_q, S, t);
   const int r = t - (cu_q ? cu_q[s] : s);
   const bool hist = q_start[s] > 0;
+  if (!B200_IN_RANGE(slots[s], nstates, 0x501)) return;
   const float* st = conv_state + (size_t)slots[s] * conv_dim * (K - 1);
   float x[E];
 #pragma unroll
@@ -114,7 +115,7 @@ __global__ void __launch_bounds__(2 * D) dn_scan_kernel(
     const __nv_bfloat16* __restrict__ y, int ystride, const __nv_bfloat16* __restrict__ xc,
     const float* __restrict__ gb, const __nv_bfloat16* __restrict__ norm_w, float* __restrict__ conv_state,
     float* __restrict__ rec_state, const int* __restrict__ cu_q, const int* __restrict__ q_start,
-    const int* __restrict__ slots, __nv_bfloat16* __restrict__ out, int nk, int nv, float eps) {
+    const int* __restrict__ slots, __nv_bfloat16* __restrict__ out, int nk, int nv, float eps, int nstates) {
   constexpr int R = D / 2;         // state rows per thread
   constexpr int NW = 2 * D / 32;   // warps
   __shared__ float qs[2][D], ks[2][D];
@@ -129,6 +130,7 @@ __global__ void __launch_bounds__(2 * D) dn_scan_kernel(
   const int t0 = cu_q ? cu_q[s] : s;
   const int n = cu_q ? cu_q[s + 1] - t0 : 1;
   const int slot = slots[s];
+  if (!B200_IN_RANGE(slot, nstates, 0x502)) return;            // whole CTA, before any barrier
   const bool hist = q_start[s] > 0;
   const float scale = rsqrtf((float)D);
   float* rs = rec_state + ((size_t)slot * nv + h) * D * D;
@@ -243,7 +245,7 @@ __global__ void __launch_bounds__(256) dn_chunk_kernel(
     const __nv_bfloat16* __restrict__ y, int ystride, const __nv_bfloat16* __restrict__ xc,
     const float* __restrict__ gb, float* __restrict__ conv_state, float* __restrict__ rec_state,
     const int* __restrict__ cu_q, const int* __restrict__ q_start, const int* __restrict__ slots,
-    float* __restrict__ o_raw, int nk, int nv) {
+    float* __restrict__ o_raw, int nk, int nv, int nstates) {
   using L = DnChunkSmem<D>;
   extern __shared__ __align__(16) float sm[];
   float* Ss = sm + L::S;
@@ -263,6 +265,7 @@ __global__ void __launch_bounds__(256) dn_chunk_kernel(
   const int conv_dim = (2 * nk + nv) * D;
   const int t0 = cu_q[s], n = cu_q[s + 1] - t0;
   const int slot = slots[s];
+  if (!B200_IN_RANGE(slot, nstates, 0x503)) return;            // whole CTA, before any barrier
   const bool hist = q_start[s] > 0;
   const float scale = rsqrtf((float)D);
   float* rs = rec_state + ((size_t)slot * nv + h) * D * D;
@@ -498,6 +501,7 @@ void deltanet_layer(torch::Tensor y, torch::Tensor conv_w, torch::Tensor A, torc
   TORCH_CHECK(xc.size(0) >= T && xc.size(1) == conv_dim && gb.size(0) >= T && out.size(1) == nv * D);
   TORCH_CHECK(slots.size(0) >= S && q_start.size(0) >= S);
   if (T == 0) return;
+  const int nstates = (int)std::min(conv_state.size(0), rec_state.size(0));
   auto stream = at::cuda::getCurrentCUDAStream();
   const int* cu = cu_q ? cu_q->data_ptr<int>() : nullptr;
   const int warps = T * (2 * nk + nv);
@@ -507,12 +511,13 @@ void deltanet_layer(torch::Tensor y, torch::Tensor conv_w, torch::Tensor A, torc
   launch_pdl(dn_prep_kernel<DV, 4>, dim3(blocks), dim3(256), 0, stream,                                         \
              (const __nv_bfloat16*)y.data_ptr(), ys, (const float*)conv_w.data_ptr(), (const float*)A.data_ptr(), \
              (const float*)dt_bias.data_ptr(), (const float*)conv_state.data_ptr(), cu, q_start.data_ptr<int>(),  \
-             slots.data_ptr<int>(), (__nv_bfloat16*)xc.data_ptr(), gb.data_ptr<float>(), T, S, (int)nk, (int)nv);  \
+             slots.data_ptr<int>(), (__nv_bfloat16*)xc.data_ptr(), gb.data_ptr<float>(), T, S, (int)nk, (int)nv,   \
+             nstates);                                                                                          \
   launch_pdl(dn_scan_kernel<DV, 4>, dim3(S, nv), dim3(2 * DV), 0, stream, (const __nv_bfloat16*)y.data_ptr(), ys, \
              (const __nv_bfloat16*)xc.data_ptr(), (const float*)gb.data_ptr(),                                  \
              (const __nv_bfloat16*)norm_w.data_ptr(), conv_state.data_ptr<float>(), rec_state.data_ptr<float>(),  \
              cu, q_start.data_ptr<int>(), slots.data_ptr<int>(), (__nv_bfloat16*)out.data_ptr(), (int)nk,        \
-             (int)nv, (float)eps)
+             (int)nv, (float)eps, nstates)
   // chunked path (prefill): prep, then the chunk kernel writes raw o, then the gated norm
 #define B200_DNC(DV)                                                                                           \
   {                                                                                                            \
@@ -520,7 +525,7 @@ void deltanet_layer(torch::Tensor y, torch::Tensor conv_w, torch::Tensor A, torc
                (const __nv_bfloat16*)y.data_ptr(), ys, (const float*)conv_w.data_ptr(),                          \
                (const float*)A.data_ptr(), (const float*)dt_bias.data_ptr(),                                     \
                (const float*)conv_state.data_ptr(), cu, q_start.data_ptr<int>(), slots.data_ptr<int>(),          \
-               (__nv_bfloat16*)xc.data_ptr(), gb.data_ptr<float>(), T, S, (int)nk, (int)nv);                     \
+               (__nv_bfloat16*)xc.data_ptr(), gb.data_ptr<float>(), T, S, (int)nk, (int)nv, nstates);            \
     const size_t smem = DnChunkSmem<DV>::TOTAL * sizeof(float);                                                \
     static bool attr = false;                                                                                   \
     if (!attr) {                                                                                                \
@@ -531,7 +536,8 @@ void deltanet_layer(torch::Tensor y, torch::Tensor conv_w, torch::Tensor A, torc
     launch_pdl(dn_chunk_kernel<DV, 4>, dim3(S, nv, DV / kDnCW), dim3(256), smem, stream,                       \
                (const __nv_bfloat16*)y.data_ptr(), ys, (const __nv_bfloat16*)xc.data_ptr(),                      \
                (const float*)gb.data_ptr(), conv_state.data_ptr<float>(), rec_state.data_ptr<float>(), cu,        \
-               q_start.data_ptr<int>(), slots.data_ptr<int>(), o_raw->data_ptr<float>(), (int)nk, (int)nv);      \
+               q_start.data_ptr<int>(), slots.data_ptr<int>(), o_raw->data_ptr<float>(), (int)nk, (int)nv,       \
+               nstates);                                                                                        \
     launch_pdl(dn_gnorm_kernel<DV>, dim3((T * nv * 32 + 255) / 256), dim3(256), 0, stream,                     \
                (const float*)o_raw->data_ptr<float>(), (const __nv_bfloat16*)y.data_ptr(), ys,                   \
                (const __nv_bfloat16*)norm_w.data_ptr(), (__nv_bfloat16*)out.data_ptr(), T, (int)nk, (int)nv,     \
@@ -565,3 +571,5 @@ void sigmoid_gate_mul(torch::Tensor attn, torch::Tensor gate) {
              (__nv_bfloat16*)attn.data_ptr(), (const __nv_bfloat16*)gate.data_ptr(), (int)gate.stride(0), T, W);
   B200_CHECK_CUDA(cudaGetLastError());
 }
+
+B200_BOUNDS_ACCESSOR(deltanet)

@@ -57,7 +57,8 @@ __global__ void __launch_bounds__(1024) ep_count_kernel(const int* __restrict__ 
   for (int i = threadIdx.x; i < n; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
   const int pairs = valid * k;
-  for (int p = threadIdx.x; p < pairs; p += blockDim.x) pos[p] = atomicAdd(&cnt[ids[p]], 1);
+  for (int p = threadIdx.x; p < pairs; p += blockDim.x)
+    pos[p] = B200_IN_RANGE(ids[p], n, 0x601) ? atomicAdd(&cnt[ids[p]], 1) : 0;   // checked: skip the pair
   __syncthreads();
   // cnt_all[me] on every rank
   for (int i = threadIdx.x; i < world * n; i += blockDim.x) {
@@ -102,6 +103,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
   if (ok) {
     for (int p = blockIdx.x * 8 + warp; p < pairs; p += gridDim.x * 8) {
       const int e = ids[p], d = e / per, el = e % per;
+      if (!B200_IN_RANGE(e, n, 0x602)) continue;
       const int slot = off[d * per + el] + pos[p];
       const int t = p / k;
       const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * H);
@@ -174,3 +176,5 @@ void ep_dispatch(torch::Tensor x, torch::Tensor ids, torch::Tensor wts, torch::T
              reinterpret_cast<const int*>(epoch_ptr), done.data_ptr<int>(), reinterpret_cast<int*>(err_ptr),
              flag_wait_ns());
 }
+
+B200_BOUNDS_ACCESSOR(ep_a2a)

@@ -1,6 +1,7 @@
 // Shared device helpers of the GGUF block-quantised kernels (gguf_gemm.cu, gguf_gemv.cu):
 // the m16n8k16 bf16 tensor-core MMA and the in-register dequantisation of the fragment-ordered
-// codes (4-bit with a scale and min per 32, 8-bit with a scale per 16/32).
+// codes (4-bit with a scale and min per 32, 8-bit with a scale per 16/32, E8 vector codes with a
+// scale and offset per group).
 #pragma once
 #include "common.cuh"
 
@@ -49,6 +50,25 @@ __device__ __forceinline__ void dequant_s8(uint32_t w0, uint32_t w1, uint32_t sa
     const bool row_b = (i & 1);
     a[i] = bf2_fma(qv, row_b ? sb : sa, 0u);
   }
+}
+
+// E8 vector codes (2 bits per weight: one byte names an 8-value codebook vector): word q holds
+// the indices of (row g, v0), (row g + 8, v0), (row g, v1), (row g + 8, v1), where v0 / v1 are
+// the two 8-column vectors of the k-step; the lane takes pair t4 of each. cbt: the codebook as
+// bf16 pairs [256][4] in shared memory (32-bit address); (s, o) per row as bf16x2 (s, s) and
+// (o, o): w = c * s + o.
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void dequant_e8(uint32_t q, int t4, uint32_t cbt, uint32_t sa, uint32_t oa, uint32_t sb,
+                                           uint32_t ob, uint32_t* a) {
+  const uint32_t lane_off = cbt + 4u * (uint32_t)t4;
+  a[0] = bf2_fma(lds_u32(lane_off + ((q & 255u) << 4)), sa, oa);
+  a[1] = bf2_fma(lds_u32(lane_off + (((q >> 8) & 255u) << 4)), sb, ob);
+  a[2] = bf2_fma(lds_u32(lane_off + (((q >> 16) & 255u) << 4)), sa, oa);
+  a[3] = bf2_fma(lds_u32(lane_off + ((q >> 24) << 4)), sb, ob);
 }
 
 }  // namespace b200

@@ -230,7 +230,8 @@ __global__ void __launch_bounds__(kVWarps * 32) gguf_gemv_kernel(const QvArgs a)
 // dequantises its fragment (rows g, g+8 x columns 2t, 2t+1, 2t+8, 2t+9) and stores four bf16 pairs.
 template <int BITS>
 __global__ void gguf_dequant_packed_kernel(const uint32_t* __restrict__ codes, const uint32_t* __restrict__ meta,
-                                           int N, int K, int group, __nv_bfloat16* __restrict__ out) {
+                                           int N, int K, int group, __nv_bfloat16* __restrict__ out,
+                                           const uint32_t* __restrict__ e8cb) {
   // No early launch of the dependent: the GEMM that reads this weight streams its first weight
   // tiles before its own dependency wait, so it must start only after this grid has finished.
   pdl_wait();
@@ -241,7 +242,16 @@ __global__ void gguf_dequant_packed_kernel(const uint32_t* __restrict__ codes, c
   if (task >= (long long)(N / 16) * ksteps) return;
   const int slice = (int)(task / ksteps), ks = (int)(task % ksteps);
   uint32_t a[4];
-  if constexpr (BITS == 4) {
+  if constexpr (BITS == 2) {
+    // E8: the four codebook indices of the lane's row pair, (s, o) of rows g and g + 8
+    const uint32_t q = __ldg(codes + ((size_t)slice * ksteps + ks) * 8 + g);
+    const uint2* mp = reinterpret_cast<const uint2*>(meta) + ((size_t)slice * (K / group) + (ks * 16) / group) * 16;
+    const uint2 ma = __ldg(mp + g), mc = __ldg(mp + g + 8);
+    const uint32_t idx[4] = {q & 255u, (q >> 8) & 255u, (q >> 16) & 255u, q >> 24};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      a[i] = bf2_fma(__ldg(e8cb + idx[i] * 4 + t4), (i & 1) ? mc.x : ma.x, (i & 1) ? mc.y : ma.y);
+  } else if constexpr (BITS == 4) {
     const uint32_t w = __ldg(codes + ((size_t)slice * ksteps + ks) * 32 + lane);
     const uint32_t* mp = meta + ((size_t)slice * (K / 32) + ks / 2) * 32;
     dequant_u4(w, __ldg(mp + g * 2), __ldg(mp + g * 2 + 1), __ldg(mp + (g + 8) * 2), __ldg(mp + (g + 8) * 2 + 1), a);
@@ -266,7 +276,7 @@ using namespace b200;
 
 // codes/meta (N x K, N % 128 == 0, K % 64 == 0) -> out bf16 [N/128 * K/64 * 128, 64] tile-packed.
 void gguf_dequant_packed(torch::Tensor codes, torch::Tensor meta, int64_t N, int64_t K, int64_t bits, int64_t group,
-                         torch::Tensor out) {
+                         torch::Tensor out, int64_t e8_codebook) {
   TORCH_CHECK(N % 128 == 0 && K % 256 == 0, "tile-packed dequantisation needs N % 128 == 0 and K % 256 == 0");
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.numel() >= N * K, "output too small");
   const long long tasks = (N / 16) * (K / 16);
@@ -275,12 +285,17 @@ void gguf_dequant_packed(torch::Tensor codes, torch::Tensor meta, int64_t N, int
   auto cp = reinterpret_cast<const uint32_t*>(codes.data_ptr());
   auto mp = reinterpret_cast<const uint32_t*>(meta.data_ptr());
   auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
-  if (bits == 4)
+  auto cbp = reinterpret_cast<const uint32_t*>(e8_codebook);
+  if (bits == 2) {
+    TORCH_CHECK(cbp != nullptr && (group == 32 || group == 64 || group == 128 || group == 256), "E8: codebook, group");
+    launch_pdl(gguf_dequant_packed_kernel<2>, grid, dim3(threads), 0, at::cuda::getCurrentCUDAStream(), cp, mp,
+               (int)N, (int)K, (int)group, op, cbp);
+  } else if (bits == 4)
     launch_pdl(gguf_dequant_packed_kernel<4>, grid, dim3(threads), 0, at::cuda::getCurrentCUDAStream(), cp, mp,
-               (int)N, (int)K, (int)group, op);
+               (int)N, (int)K, (int)group, op, cbp);
   else
     launch_pdl(gguf_dequant_packed_kernel<8>, grid, dim3(threads), 0, at::cuda::getCurrentCUDAStream(), cp, mp,
-               (int)N, (int)K, (int)group, op);
+               (int)N, (int)K, (int)group, op, cbp);
 }
 
 // K splits for a matrix of N / 16 slices and K / 256 chunks: about two waves of warp tasks over

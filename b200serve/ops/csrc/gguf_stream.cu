@@ -44,19 +44,25 @@ constexpr int kGsXBytes = 16 * kGsXRow * 2; // activation rows of one stage (up 
 constexpr int kGsSmemBudget = 110 * 1024;   // per CTA: two CTAs per SM
 constexpr int kGsCtl = 5120;                // barriers and flags (128 B) + push staging (8 x 512 B)
 
-// Stage geometry for codes of `bits` (8 also covers groups mixing 4- and 8-bit parts).
+// Stage geometry for codes of `bits` (8 also covers groups mixing 4- and 8-bit parts; 2 is the
+// E8 vector code: one byte per 8 weights, and a 4 KB codebook table after the control block).
 template <int BITS>
 struct GsGeom {
-  static constexpr int code = BITS == 4 ? 2048 : 4096;          // codes of one slice-chunk
+  static constexpr int code = BITS == 4 ? 2048 : BITS == 8 ? 4096 : 512;   // codes of one slice-chunk
   static constexpr int meta = 1024;                             // scales of one slice-chunk (max)
   static constexpr int codes_off = 0;
   static constexpr int meta_off = kGsConsumers * code;
   static constexpr int x_off = meta_off + kGsConsumers * meta;
   static constexpr int bytes = x_off + kGsXBytes;
-  static constexpr int stages = (kGsSmemBudget - kGsCtl) / bytes;
-  static constexpr size_t smem = (size_t)stages * bytes + kGsCtl;
+  static constexpr int table = BITS == 2 ? 4096 : 0;
+  static constexpr int fit = (kGsSmemBudget - kGsCtl - table) / bytes;
+  static constexpr int stages = fit < 4 ? fit : 4;
+  static constexpr size_t smem = (size_t)stages * bytes + kGsCtl + table;
   static_assert(stages >= 2 && stages <= 4, "stage too large or too small");
 };
+
+// E8 meta: (s, s) and (o, o) as bf16x2 per (group, row); bytes of one slice-chunk
+__device__ __forceinline__ uint32_t gs_e8_meta_bytes(int group) { return (uint32_t)(256 / group) * 128u; }
 
 struct GsPart {
   const uint32_t* codes;
@@ -82,6 +88,7 @@ struct GsArgs {
   __nv_bfloat16* push[8];                   // GS_PUSH: this rank's slot base on every rank
   int world;
   __nv_bfloat16* mc;                        // GS_PUSH through a multicast object
+  const uint32_t* e8cb;                     // E8 parts: codebook as bf16 pairs [256][4]
   int* err;
   uint64_t wait_ns;
 };
@@ -131,8 +138,8 @@ __device__ __forceinline__ void gs_issue(const GsArgs& a, int tile, int c, uint8
   using Gm = GsGeom<BITS>;
   const GsPart& p = a.parts[gs_part_of(a, tile)];
   const int ksteps = a.K / 16;
-  const uint32_t cbytes = p.bits == 4 ? 2048u : 4096u;
-  const uint32_t mbytes = p.bits == 4 ? 1024u : (uint32_t)(256 / p.group) * 64u;
+  const uint32_t cbytes = p.bits == 4 ? 2048u : p.bits == 8 ? 4096u : 512u;
+  const uint32_t mbytes = p.bits == 4 ? 1024u : p.bits == 8 ? (uint32_t)(256 / p.group) * 64u : gs_e8_meta_bytes(p.group);
   const int nvalid = min(kGsConsumers, p.slices - (tile - p.tile0) * kGsConsumers);
   if ((what & GS_ANNOUNCE) && lane == 0)
     tc::mbar_arrive_expect_tx(bar, (uint32_t)nvalid * (cbytes + mbytes) + (uint32_t)a.M * 512u);
@@ -140,11 +147,11 @@ __device__ __forceinline__ void gs_issue(const GsArgs& a, int tile, int c, uint8
   if ((what & GS_W) && lane < 2 * kGsConsumers && (lane & 7) < nvalid) {
     const size_t ls = (size_t)(tile - p.tile0) * kGsConsumers + (lane & 7);
     if (lane < kGsConsumers) {
-      const uint32_t* src = p.codes + (ls * ksteps + (size_t)c * 16) * (p.bits == 4 ? 32 : 64);
+      const uint32_t* src = p.codes + (ls * ksteps + (size_t)c * 16) * (p.bits == 4 ? 32 : p.bits == 8 ? 64 : 8);
       tc::bulk_g2s(st + Gm::codes_off + (lane & 7) * Gm::code, src, cbytes, bar);
     } else {
       const uint32_t* src = p.bits == 4 ? p.meta + (ls * (a.K / 32) + (size_t)c * 8) * 32
-                                        : p.meta + (ls * (a.K / p.group) + (size_t)c * (256 / p.group)) * 16;
+                            : p.meta + (ls * (a.K / p.group) + (size_t)c * (256 / p.group)) * (p.bits == 8 ? 16 : 32);
       tc::bulk_g2s(st + Gm::meta_off + (lane & 7) * Gm::meta, src, mbytes, bar);
     }
   }
@@ -158,7 +165,7 @@ __device__ __forceinline__ void gs_issue(const GsArgs& a, int tile, int c, uint8
 // g, g+8, g+8 of the slice x tokens j*8 + 2*t4, +1, +0, +1).
 template <int BITS, int NB>
 __device__ __forceinline__ void gs_compute(const uint8_t* st, int bits, int group, int w, int lane,
-                                           float (&acc)[NB][4]) {
+                                           float (&acc)[NB][4], uint32_t cbt) {
   using Gm = GsGeom<BITS>;
   const int g = lane >> 2, t4 = lane & 3;
   const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(st + Gm::x_off) + g * kGsXRow + 2 * t4;
@@ -168,7 +175,24 @@ __device__ __forceinline__ void gs_compute(const uint8_t* st, int bits, int grou
   float odd[NB][4];
 #pragma unroll
   for (int j = 0; j < NB; ++j) odd[j][0] = odd[j][1] = odd[j][2] = odd[j][3] = 0.f;
-  if (BITS == 4 || bits == 4) {
+  if constexpr (BITS == 2) {
+    const uint32_t* cw = reinterpret_cast<const uint32_t*>(cb);          // [16 k-steps][8 row pairs]
+    const uint2* mt = reinterpret_cast<const uint2*>(mb);                 // [256 / group][16 rows] (s, o)
+    const int gsh = group == 32 ? 1 : group == 64 ? 2 : group == 128 ? 3 : 4;   // k-steps per group, log2
+#pragma unroll
+    for (int ks = 0; ks < 16; ++ks) {
+      const int gi = ks >> gsh;
+      const uint2 ma = mt[gi * 16 + g], mc = mt[gi * 16 + g + 8];
+      uint32_t wv[4];
+      dequant_e8(cw[ks * 8 + g], t4, cbt, ma.x, ma.y, mc.x, mc.y, wv);
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        const __nv_bfloat16* r = xs + j * 8 * kGsXRow + ks * 16;
+        qmma((ks & 1) ? odd[j] : acc[j], wv, *reinterpret_cast<const uint32_t*>(r),
+             *reinterpret_cast<const uint32_t*>(r + 8));
+      }
+    }
+  } else if (BITS == 4 || bits == 4) {
     const uint32_t* cw = reinterpret_cast<const uint32_t*>(cb);
     const uint2* mt = reinterpret_cast<const uint2*>(mb);                 // [8 sub-blocks][16 rows] (s, -m)
 #pragma unroll
@@ -345,6 +369,7 @@ __global__ void __launch_bounds__(kGsThreads, 2) gguf_stream_kernel(const GsArgs
   int* bcast = reinterpret_cast<int*>(empty + 4) + 1;
   volatile int* issued = reinterpret_cast<volatile int*>(empty + 4) + 2;     // producer: items issued, -1 while running
   __nv_bfloat16* pstage = reinterpret_cast<__nv_bfloat16*>(ctl + 128);
+  uint32_t* cbt = reinterpret_cast<uint32_t*>(ctl + kGsCtl);              // E8 codebook (BITS == 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
   const int i0 = gs_begin(a, cta), n = gs_begin(a, cta + 1) - i0;
@@ -357,6 +382,9 @@ __global__ void __launch_bounds__(kGsThreads, 2) gguf_stream_kernel(const GsArgs
     *abort_flag = 0;
     *issued = -1;
     tc::fence_barrier_init();
+  }
+  if constexpr (BITS == 2) {          // a weight: read before the dependency wait
+    for (int i = threadIdx.x; i < 1024; i += kGsThreads) cbt[i] = __ldg(a.e8cb + i);
   }
   __syncthreads();
   if (warp == kGsConsumers) {
@@ -407,7 +435,7 @@ __global__ void __launch_bounds__(kGsThreads, 2) gguf_stream_kernel(const GsArgs
       mine = (cur - pp->tile0) * kGsConsumers + warp < pp->slices;
     }
     if (!*abort_flag && gs_wait(&full[s], ph, a, abort_flag)) {
-      if (mine) gs_compute<BITS, NB>(smem + s * Gm::bytes, pp->bits, pp->group, warp, lane, acc);
+      if (mine) gs_compute<BITS, NB>(smem + s * Gm::bytes, pp->bits, pp->group, warp, lane, acc, tc::smem_u32(cbt));
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&empty[s]);
     }
@@ -480,7 +508,8 @@ static void gs_launch(const GsArgs& a, int mode, int grid, cudaStream_t stream) 
 std::vector<int64_t> gguf_stream(torch::Tensor x, std::vector<torch::Tensor> codes, std::vector<torch::Tensor> metas,
                                  std::vector<int64_t> ns, std::vector<int64_t> bits, std::vector<int64_t> groups,
                                  int64_t mode, torch::Tensor out, int64_t ldo, torch::Tensor ws, torch::Tensor counters,
-                                 torch::Tensor push_ptrs, int64_t mc_ptr, int64_t num_sms, int64_t wait_ms) {
+                                 torch::Tensor push_ptrs, int64_t mc_ptr, int64_t num_sms, int64_t wait_ms,
+                                 int64_t e8_codebook) {
   const int M = x.size(0), K = x.size(1);
   const int np = (int)codes.size();
   TORCH_CHECK(np >= 1 && np <= kGsMaxParts && metas.size() == codes.size() && ns.size() == codes.size() &&
@@ -498,11 +527,16 @@ std::vector<int64_t> gguf_stream(torch::Tensor x, std::vector<torch::Tensor> cod
   for (int p = 0; p < np; ++p) {
     TORCH_CHECK(ns[p] % 16 == 0, "N must be a multiple of 16");
     TORCH_CHECK(mode != GS_PARTIAL || ns[p] % 128 == 0, "partial outputs need N % 128 == 0 (128-column tiles)");
-    TORCH_CHECK(bits[p] == 4 || (bits[p] == 8 && (groups[p] == 16 || groups[p] == 32)),
-                "4-bit codes (group 32) or 8-bit codes with group 16 or 32");
+    TORCH_CHECK(bits[p] == 4 || (bits[p] == 8 && (groups[p] == 16 || groups[p] == 32)) ||
+                    (bits[p] == 2 && (groups[p] == 32 || groups[p] == 64 || groups[p] == 128 || groups[p] == 256)),
+                "4-bit codes (group 32), 8-bit codes with group 16 or 32, or E8 codes with group 32..256");
+    TORCH_CHECK((bits[p] == 2) == (bits[0] == 2), "E8 parts cannot share a launch with other code types");
     const auto cp = reinterpret_cast<uintptr_t>(codes[p].data_ptr()), mp = reinterpret_cast<uintptr_t>(metas[p].data_ptr());
     TORCH_CHECK(cp % 16 == 0 && mp % 16 == 0, "codes and scales must be 16-byte aligned for the bulk copies");
-    TORCH_CHECK(codes[p].numel() * codes[p].element_size() >= ns[p] * K * bits[p] / 8, "codes too small");
+    TORCH_CHECK(codes[p].numel() * codes[p].element_size() >= ns[p] * K / (bits[p] == 2 ? 8 : 8 / bits[p]),
+                "codes too small");
+    if (bits[p] == 2)
+      TORCH_CHECK(metas[p].numel() * metas[p].element_size() >= ns[p] * (K / groups[p]) * 8, "E8 scales too small");
     a.parts[p].codes = reinterpret_cast<const uint32_t*>(cp);
     a.parts[p].meta = reinterpret_cast<const uint32_t*>(mp);
     a.parts[p].tile0 = tiles;
@@ -516,6 +550,10 @@ std::vector<int64_t> gguf_stream(torch::Tensor x, std::vector<torch::Tensor> cod
   }
   auto plan = gguf_stream_plan((int64_t)tiles * 128, K, num_sms);
   a.nparts = np;
+  if (bits[0] == 2) {
+    TORCH_CHECK(e8_codebook != 0 && e8_codebook % 16 == 0, "E8 parts need the codebook table ([256][4] bf16 pairs)");
+    a.e8cb = reinterpret_cast<const uint32_t*>(e8_codebook);
+  }
   a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
   a.ldx = (int)x.stride(0);
   a.M = M;
@@ -556,7 +594,10 @@ std::vector<int64_t> gguf_stream(torch::Tensor x, std::vector<torch::Tensor> cod
                 "output type or size");
   }
   auto stream = at::cuda::getCurrentCUDAStream();
-  if (any8) {
+  if (bits[0] == 2) {
+    if (M <= 8) gs_launch<2, 1>(a, (int)mode, a.ctas, stream);
+    else gs_launch<2, 2>(a, (int)mode, a.ctas, stream);
+  } else if (any8) {
     if (M <= 8) gs_launch<8, 1>(a, (int)mode, a.ctas, stream);
     else gs_launch<8, 2>(a, (int)mode, a.ctas, stream);
   } else {

@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(kTqW * 32) tq_qkv_kernel(
     const int* __restrict__ slots, int T, int nq, int nkv, const float* __restrict__ S,
     __nv_bfloat16* __restrict__ q_rot, __nv_bfloat16* __restrict__ q_jl, uint8_t* __restrict__ kc,
     uint8_t* __restrict__ ksg, __half* __restrict__ kmeta, uint8_t* __restrict__ vc, __half* __restrict__ vmeta,
-    const TqCodec cd, const float* __restrict__ cent_k, const float* __restrict__ cent_v) {
+    const TqCodec cd, const float* __restrict__ cent_k, const float* __restrict__ cent_v, int cache_slots) {
   extern __shared__ float sS[];
   __shared__ float vec[kTqW][128];
   __shared__ float cent[2][8];
@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(kTqW * 32) tq_qkv_kernel(
     const int tv = is_v ? w - nkvv : w;
     const int t = tv / nkv, h = tv % nkv;
     const int slot = slots[t];
-    if (slot < 0) continue;
+    if (slot < 0 || !B200_IN_RANGE(slot, cache_slots, 0x401)) continue;
     const size_t src = ((size_t)(t >> 4) * nkv + h) * 16 + (t & 15);
     const size_t dst = ((size_t)(slot >> 4) * nkv + h) * 16 + (slot & 15);
     load4((is_v ? vst : kst) + src * 128 + 4 * lane, x);
@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(kTqW * 32) tq_dequant_kernel(
     const int* __restrict__ block_ids, int n_blocks, int nkv, const uint8_t* __restrict__ kc,
     const uint8_t* __restrict__ ksg, const __half* __restrict__ kmeta, const uint8_t* __restrict__ vc,
     const __half* __restrict__ vmeta, const float* __restrict__ S, const float* __restrict__ code_vals,
-    __nv_bfloat16* __restrict__ out_k, __nv_bfloat16* __restrict__ out_v) {
+    __nv_bfloat16* __restrict__ out_k, __nv_bfloat16* __restrict__ out_v, int cache_blocks) {
   extern __shared__ float sS[];
   __shared__ float cv[32];
   __shared__ float vec[kTqW][128];
@@ -198,7 +198,9 @@ __global__ void __launch_bounds__(kTqW * 32) tq_dequant_kernel(
   const int rows = n_blocks * nkv * 16;
   for (int rr = blockIdx.x * kTqW + warp; rr < rows; rr += gridDim.x * kTqW) {
     const int j = rr / (nkv * 16), rest = rr % (nkv * 16);
-    const size_t src = (size_t)block_ids[j] * nkv * 16 + rest;
+    int blk = block_ids[j];
+    if (!B200_IN_RANGE(blk, cache_blocks, 0x402)) blk = 0;   // checked builds: read block 0 instead
+    const size_t src = (size_t)blk * nkv * 16 + rest;
     const size_t dst = (size_t)rr;
     // values: dims 4l..4l+3 from code bytes 2l, 2l+1
     const uint32_t vb = *reinterpret_cast<const uint16_t*>(vc + src * 64 + 2 * lane);
@@ -281,7 +283,7 @@ void tq_qkv(torch::Tensor q, torch::Tensor k_stage, torch::Tensor v_stage, torch
              nkv, (const float*)S.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(q_rot.data_ptr()),
              reinterpret_cast<__nv_bfloat16*>(q_jl.data_ptr()), k_codes.data_ptr<uint8_t>(),
              k_sign.data_ptr<uint8_t>(), reinterpret_cast<__half*>(k_meta.data_ptr()), v_codes.data_ptr<uint8_t>(),
-             reinterpret_cast<__half*>(v_meta.data_ptr()), cd, cp, cp + 8);
+             reinterpret_cast<__half*>(v_meta.data_ptr()), cd, cp, cp + 8, (int)(k_codes.size(0) * 16));
 }
 
 // block_ids [n] int32 (device); code_vals [2, 16] fp32 (device); out_k / out_v [n, nkv, 16, 128] bf16.
@@ -303,5 +305,7 @@ void tq_dequant(torch::Tensor block_ids, torch::Tensor k_codes, torch::Tensor k_
              reinterpret_cast<const __half*>(k_meta.data_ptr()), v_codes.data_ptr<uint8_t>(),
              reinterpret_cast<const __half*>(v_meta.data_ptr()), (const float*)S.data_ptr<float>(),
              (const float*)code_vals.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(out_k.data_ptr()),
-             reinterpret_cast<__nv_bfloat16*>(out_v.data_ptr()));
+             reinterpret_cast<__nv_bfloat16*>(out_v.data_ptr()), (int)k_codes.size(0));
 }
+
+B200_BOUNDS_ACCESSOR(kv_turboquant)

@@ -197,7 +197,7 @@ __global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __n
                                 const int* __restrict__ slots, __nv_bfloat16* __restrict__ q_out,
                                 void* __restrict__ k_cache, void* __restrict__ v_cache, __half* __restrict__ k_scale,
                                 __half* __restrict__ v_scale, int T, int nq, int nkv, float eps, int width, int rot,
-                                const PartialIn pin) {
+                                const PartialIn pin, int cache_slots, int max_pos) {
   constexpr int E = HD / 32;
   pdl_wait();
   pdl_trigger();
@@ -231,6 +231,7 @@ __global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __n
     // rotate-half RoPE over the first `rot` dims (pairs (d, d + rot/2)); the rest pass through.
     // The partner of dim d sits rot/2 dims away, i.e. in lane ^ (rot/2/E) (a power of two).
     const int pos = positions[t];
+    if (!B200_IN_RANGE(pos, max_pos, 0x101)) return;
     const int hr = rot >> 1, xo = hr / E;
     const float* cs = cos_sin + (size_t)pos * rot;  // [cos(rot/2) | sin(rot/2)]
     float y[E];
@@ -255,7 +256,7 @@ __global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __n
     for (int i = 0; i < E; ++i) dst[i] = __float2bfloat16_rn(x[i]);
   } else {
     const int slot = slots[t];
-    if (slot < 0) return;
+    if (slot < 0 || !B200_IN_RANGE(slot, cache_slots, 0x102)) return;
     const int kvh = is_k ? h - nq : h - nq - nkv;
     const size_t row = ((size_t)(slot >> 4) * nkv + kvh) * 16 + (slot & 15);
     if constexpr (KVQ == 0) {
@@ -322,6 +323,7 @@ __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat1
   pdl_trigger();
   const int t = blockIdx.x;
   int id = ids[t];
+  (void)B200_IN_RANGE(id, vocab, 0x103);
   id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
   const bf16x8* src = reinterpret_cast<const bf16x8*>(table + (size_t)id * H);
   bf16x8* dst = reinterpret_cast<bf16x8*>(out + (size_t)t * H);
@@ -452,7 +454,8 @@ void qkv_post_impl(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::op
       qn_w ? reinterpret_cast<const __nv_bfloat16*>(qn_w->data_ptr()) : nullptr,                            \
       kn_w ? reinterpret_cast<const __nv_bfloat16*>(kn_w->data_ptr()) : nullptr, cos_sin.data_ptr<float>(), \
       positions.data_ptr<int>(), slots.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), \
-      k_cache.data_ptr(), v_cache.data_ptr(), k_scale, v_scale, T, (int)nq, (int)nkv, (float)eps, width, rot, pin)
+      k_cache.data_ptr(), v_cache.data_ptr(), k_scale, v_scale, T, (int)nq, (int)nkv, (float)eps, width, rot, pin, \
+      (int)(k_cache.size(0) * 16), (int)cos_sin.size(0))
   if (HD == 128) { if (kvq) B200_QKV((qkv_post_kernel<128, 1>)); else B200_QKV((qkv_post_kernel<128, 0>)); }
   else if (HD == 64 && !kvq) B200_QKV((qkv_post_kernel<64, 0>));
   else if (HD == 256 && !kvq) B200_QKV((qkv_post_kernel<256, 0>));
@@ -521,3 +524,5 @@ void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out) {
              reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), H, (int)table.size(0));
   B200_CHECK_CUDA(cudaGetLastError());
 }
+
+B200_BOUNDS_ACCESSOR(norm_rope)

@@ -34,7 +34,7 @@ __device__ __forceinline__ float bx_at(const __nv_bfloat16* __restrict__ y, int 
 __global__ void shortconv_out_kernel(const __nv_bfloat16* __restrict__ y, int ystride, const float* __restrict__ w,
                                      const float* __restrict__ state, const int* __restrict__ cu_q,
                                      const int* __restrict__ q_start, const int* __restrict__ slots,
-                                     __nv_bfloat16* __restrict__ out, int T, int S, int C, int K) {
+                                     __nv_bfloat16* __restrict__ out, int T, int S, int C, int K, int nstates) {
   pdl_wait();
   pdl_trigger();
   const size_t n = (size_t)T * C;
@@ -43,6 +43,7 @@ __global__ void shortconv_out_kernel(const __nv_bfloat16* __restrict__ y, int ys
     const int s = sc_seq_of(cu_q, S, t);
     const int r = t - (cu_q ? cu_q[s] : s);
     const bool hist = q_start[s] > 0;
+    if (!B200_IN_RANGE(slots[s], nstates, 0x511)) continue;
     const float* st = state + ((size_t)slots[s] * C + c) * (K - 1);
     float acc = 0.f;
     for (int j = 0; j < K; ++j) {
@@ -59,7 +60,7 @@ __global__ void shortconv_out_kernel(const __nv_bfloat16* __restrict__ y, int ys
 
 __global__ void shortconv_roll_kernel(const __nv_bfloat16* __restrict__ y, int ystride, float* __restrict__ state,
                                       const int* __restrict__ cu_q, const int* __restrict__ q_start,
-                                      const int* __restrict__ slots, int S, int C, int K) {
+                                      const int* __restrict__ slots, int S, int C, int K, int nstates) {
   pdl_wait();
   pdl_trigger();
   const size_t n = (size_t)S * C;
@@ -69,6 +70,7 @@ __global__ void shortconv_roll_kernel(const __nv_bfloat16* __restrict__ y, int y
     const int len = cu_q ? cu_q[s + 1] - t0 : 1;
     if (len <= 0) continue;
     const bool hist = q_start[s] > 0;
+    if (!B200_IN_RANGE(slots[s], nstates, 0x512)) continue;
     float* st = state + ((size_t)slots[s] * C + c) * (K - 1);
     float old[kMaxTaps];
     for (int q = 0; q < K - 1; ++q) old[q] = hist ? st[q] : 0.f;
@@ -104,11 +106,14 @@ void shortconv_layer(torch::Tensor y, torch::Tensor conv_w, torch::Tensor conv_s
   const int blocks = (int)std::min<long>((n + 255) / 256, 148L * 16);
   launch_pdl(shortconv_out_kernel, dim3(blocks), dim3(256), 0, stream, (const __nv_bfloat16*)y.data_ptr(),
              (int)y.stride(0), conv_w.data_ptr<float>(), (const float*)conv_state.data_ptr<float>(), cu,
-             q_start.data_ptr<int>(), slots.data_ptr<int>(), (__nv_bfloat16*)out.data_ptr(), T, S, C, K);
+             q_start.data_ptr<int>(), slots.data_ptr<int>(), (__nv_bfloat16*)out.data_ptr(), T, S, C, K,
+             (int)conv_state.size(0));
   const long n2 = (long)S * C;
   const int blocks2 = (int)std::min<long>((n2 + 255) / 256, 148L * 16);
   launch_pdl(shortconv_roll_kernel, dim3(blocks2), dim3(256), 0, stream, (const __nv_bfloat16*)y.data_ptr(),
              (int)y.stride(0), conv_state.data_ptr<float>(), cu, q_start.data_ptr<int>(), slots.data_ptr<int>(), S,
-             C, K);
+             C, K, (int)conv_state.size(0));
   B200_CHECK_CUDA(cudaGetLastError());
 }
+
+B200_BOUNDS_ACCESSOR(shortconv)

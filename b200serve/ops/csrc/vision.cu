@@ -57,7 +57,8 @@ __global__ void gelu_rows_kernel(__nv_bfloat16* __restrict__ x, size_t n, int ta
 __global__ void vision_qkv_rope_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ cosv,
                                        const float* __restrict__ sinv, int heads, int hd,
                                        const int* __restrict__ slots, __nv_bfloat16* __restrict__ q_out,
-                                       __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache) {
+                                       __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
+                                       int cache_slots) {
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
@@ -77,6 +78,7 @@ __global__ void vision_qkv_rope_kernel(const __nv_bfloat16* __restrict__ qkv, co
   }
   q_out[((size_t)t * heads + h) * 128 + d] = __float2bfloat16_rn(qv);
   const int slot = slots[t];
+  if (!B200_IN_RANGE(slot, cache_slots, 0x801)) return;
   const size_t kvo = (((size_t)(slot >> 4) * heads + h) * 16 + (slot & 15)) * 128 + d;
   k_cache[kvo] = __float2bfloat16_rn(kv);
   v_cache[kvo] = __float2bfloat16_rn(vv);
@@ -121,5 +123,7 @@ void vision_qkv_rope(torch::Tensor qkv, torch::Tensor cos_sin, int64_t heads, in
              reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), cos_sin.data_ptr<float>(),
              cos_sin.data_ptr<float>() + (size_t)N * hd, (int)heads, (int)hd, slots.data_ptr<int>(),
              reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()),
-             reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()));
+             reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()), (int)(k_cache.size(0) * 16));
 }
+
+B200_BOUNDS_ACCESSOR(vision)

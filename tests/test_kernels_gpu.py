@@ -506,3 +506,36 @@ def test_stream_k_partial_qkv_post_matches_dense():
     q2 = ops.qkv_post(ops.linear(x, w, bias=b), None, qn, kn, cs, pos, slots, kc2, vc2, nq, nkv, 1e-6)
     assert _rel(q, q2) < 1e-2 and _rel(kc, kc2) < 1e-2 and _rel(vc, vc2) < 1e-2
     assert ops.gemm_error_flag() == 0
+
+
+def test_decode_reductions_are_bitwise_repeatable():
+    """Every reduction on the decode path has a fixed order (stream-K partial slots summed in slot
+    order by the norm, split-KV attention merged in split order, the sampler's cluster merge in
+    CTA order), so repeating a step gives bit-identical outputs."""
+    M, N, K = 32, 4096, 4096
+    x = torch.randn(M, K, device=dev).bfloat16()
+    w = ops.pack_weight((torch.randn(N, K, device=dev) * 0.03).bfloat16())
+    res = torch.randn(M, N, device=dev).bfloat16()
+    nw = (torch.rand(N, device=dev) + 0.5).bfloat16()
+    outs = []
+    for _ in range(3):
+        ro = torch.empty_like(res)
+        outs.append((ops.rmsnorm(ops.linear_partial(x, w), nw, 1e-6, residual=res, residual_out=ro), ro))
+    assert all(torch.equal(outs[0][0], o[0]) and torch.equal(outs[0][1], o[1]) for o in outs[1:])
+    # split-KV decode attention
+    B, nq, nkv, hd, L = 8, 32, 8, 128, 1000
+    nb = (L + 15) // 16
+    kc = torch.randn(B * nb, nkv, 16, hd, device=dev).bfloat16()
+    vc = torch.randn_like(kc.float()).bfloat16()
+    bt = torch.arange(B * nb, device=dev, dtype=torch.int32).view(B, nb)
+    lens = torch.full((B,), L, dtype=torch.int32, device=dev)
+    q = torch.randn(B, nq, hd, device=dev).bfloat16()
+    ws = ops.AttnWorkspace(dev, B, nkv, nq // nkv, hd, 8)
+    a = [ops.paged_decode_attention(q, kc, vc, bt, lens, hd ** -0.5, tps=128, nsplit=8, workspace=ws).clone()
+         for _ in range(3)]
+    assert torch.equal(a[0], a[1]) and torch.equal(a[0], a[2])
+    # sampler over clusters of CTAs
+    logits = torch.randn(4, 151936, device=dev)
+    draws = [ops.sample_rows(logits.clone(), [0.8] * 4, [50] * 4, [0.9] * 4, [0.0] * 4, [11, 12, 13, 14], [3] * 4)
+             for _ in range(3)]
+    assert torch.equal(draws[0], draws[1]) and torch.equal(draws[0], draws[2])
