@@ -559,6 +559,74 @@ def q8_0_to_s8(raw: np.ndarray, N: int, K: int):
     return blk["q"].reshape(N, K).astype(np.int32), blk["d"].astype(np.float32).reshape(N, K // 32)
 
 
+# IQ4_NL / IQ4_XS: 4-bit indices into the format's 16-value table (GGML_IQ4_NL_TABLE, read from
+# the gguf package), one fp16 scale per 32 values (IQ4_NL), or per 256 values with a 6-bit
+# sub-scale per 32 (IQ4_XS: scale = d * (ls - 32)). Within a block of 32, byte j holds value j in
+# its low nibble and value j + 16 in its high nibble.
+GGML_IQ4_NL, GGML_IQ4_XS = 20, 23
+
+
+def iq4_table() -> np.ndarray:
+    import gguf
+    return np.asarray(gguf.quants.IQ4_NL.kvalues, dtype=np.float32)
+
+
+def _iq4_nibbles(qs: np.ndarray) -> np.ndarray:
+    """[..., 16] bytes of 32-value blocks -> [..., 32] indices."""
+    return np.concatenate([qs & 15, qs >> 4], -1).astype(np.uint32)
+
+
+def iq4_decode(raw: np.ndarray, ggml_type: int, N: int, K: int):
+    """(indices uint32 [N, K] in 0..15, scales fp32 [N, K / 32]) of an IQ4_NL / IQ4_XS matrix."""
+    raw = np.asarray(raw, dtype=np.uint8)
+    if ggml_type == GGML_IQ4_NL:
+        blk = np.frombuffer(raw, dtype=[("d", "<f2"), ("qs", "u1", 16)]).reshape(N, K // 32)
+        return _iq4_nibbles(blk["qs"]).reshape(N, K), blk["d"].astype(np.float32)
+    blk = np.frombuffer(raw, dtype=[("d", "<f2"), ("sh", "<u2"), ("sl", "u1", 4), ("qs", "u1", 128)]).reshape(N, K // 256)
+    ib = np.arange(8)
+    lo = (blk["sl"][..., ib // 2] >> (4 * (ib % 2))) & 15
+    hi = (blk["sh"][..., None].astype(np.uint32) >> (2 * ib)) & 3
+    ls = (lo.astype(np.int32) | (hi.astype(np.int32) << 4)) - 32
+    scale = (blk["d"].astype(np.float32)[..., None] * ls).reshape(N, K // 32)
+    q = _iq4_nibbles(blk["qs"].reshape(N, K // 256, 8, 16)).reshape(N, K)
+    return q, scale
+
+
+def repack_iq4_for_gpu(q: np.ndarray, scale: np.ndarray):
+    """Indices [N, K] and scales [N, K / 32] -> (codes uint32, meta uint32) for the table-lookup
+    path of the GEMV (``bits`` 5): per lane and k-step one word whose byte i is register i's pair
+    (low nibble the even column), and per 32 columns (scale, scale) as a bf16 pair beside a zero
+    word (the 4-bit meta layout)."""
+    N, K = q.shape
+    v = _lane_values(q.astype(np.uint32))                                 # [S, KS, 32, 4, 2]
+    word = np.zeros(v.shape[:3], dtype=np.uint32)
+    for i in range(4):
+        word |= (v[..., i, 0] | (v[..., i, 1] << 4)) << (8 * i)
+    sb = _pair(_bf16_bits(scale)).reshape(N // 16, 16, K // 32).transpose(0, 2, 1)
+    meta = np.stack([sb, np.zeros_like(sb)], -1)
+    return word.reshape(-1), np.ascontiguousarray(meta).reshape(-1)
+
+
+def iq4_pair_table(device):
+    """[256] int32: bf16 (table[b & 15], table[b >> 4]) for each byte b."""
+    import torch
+    t = _bf16_bits(iq4_table())
+    b = np.arange(256)
+    w = (t[b & 15] | (t[b >> 4] << 16)).astype(np.uint32)
+    return torch.from_numpy(w.view(np.int32).copy()).to(device)
+
+
+_iq4_tables = {}
+
+
+def _iq4_tab(device):
+    import torch
+    key = str(torch.device(device))
+    if key not in _iq4_tables:
+        _iq4_tables[key] = iq4_pair_table(device)
+    return _iq4_tables[key]
+
+
 def gpu_quant_weight(g: "GGUFFile", name: str, device):
     """A GGUF tensor as an ops.QuantWeight on ``device`` (Q4_K, Q6_K, Q8_0), else None."""
     import torch
@@ -581,6 +649,8 @@ def gpu_quant_weight(g: "GGUFFile", name: str, device):
         q, s = q8_0_to_s8(raw, N, K)
         codes, meta = repack_s8_for_gpu(q, s, 32)
         bits, group = 8, 32
+    elif t.ggml_type in (GGML_IQ4_NL, GGML_IQ4_XS):
+        return _repack(raw, t.ggml_type, N, K, device)
     else:
         return None
     to = lambda a: torch.from_numpy(a.view(np.int32).copy()).to(device)
@@ -615,13 +685,18 @@ def _repack(raw, ggml_type, N, K, device):
         q, s = q8_0_to_s8(raw, N, K)
         codes, meta = repack_s8_for_gpu(q, s, 32)
         bits, group = 8, 32
+    elif ggml_type in (GGML_IQ4_NL, GGML_IQ4_XS):
+        q, s = iq4_decode(raw, ggml_type, N, K)
+        codes, meta = repack_iq4_for_gpu(q, s)
+        to = lambda a: torch.from_numpy(a.view(np.int32).copy()).to(device)
+        return ops.QuantWeight(to(codes), to(meta), N, K, 5, 32, codebook=_iq4_tab(device))
     else:
         raise NotImplementedError(TYPE_NAME.get(ggml_type, ggml_type))
     to = lambda a: torch.from_numpy(a.view(np.int32).copy()).to(device)
     return ops.QuantWeight(to(codes), to(meta), N, K, bits, group)
 
 
-QUANT_TYPES = (GGML_Q4_K, GGML_Q6_K, GGML_Q8_0)
+QUANT_TYPES = (GGML_Q4_K, GGML_Q6_K, GGML_Q8_0, GGML_IQ4_NL, GGML_IQ4_XS)
 
 
 class QuantGroup(list):

@@ -530,7 +530,9 @@ def gguf_stream(x, parts, mode, out, ldo, push=None, mc=0):
     ws, counters, nsm = _gguf_scratch(x.device)
     xc = x if (x.stride(1) == 1 and x.stride(0) % 8 == 0) else x.contiguous()
     _cuda(x)
-    cb = parts[0].codebook.data_ptr() if parts[0].bits == 2 else 0
+    # the launch's table: the E8 codebook, or the IQ4 pair table of its bits-5 parts
+    tab = [p.codebook for p in parts if p.bits in (2, 5)]
+    cb = tab[0].data_ptr() if tab else 0
     return ext().gguf_stream(xc, [p.codes for p in parts], [p.meta for p in parts], [p.N for p in parts],
                              [p.bits for p in parts], [p.group for p in parts], mode,
                              out if out is not None else _NO_OUT, ldo, ws, counters,
@@ -542,8 +544,9 @@ def _gs_ok(x, parts, tile=16):
             and len({p.K for p in parts}) == 1 and all(p.K % 256 == 0 and p.N % tile == 0 for p in parts)):
         return False
     e8 = [p.bits == 2 for p in parts]
-    # E8 parts stream together only with E8 parts of the same codebook
-    return not any(e8) or (all(e8) and len({p.codebook.data_ptr() for p in parts}) == 1)
+    # E8 parts stream together only with E8 parts of the same codebook; IQ4 parts share one table
+    tabs = {p.codebook.data_ptr() for p in parts if p.bits in (2, 5)}
+    return (not any(e8) or all(e8)) and len(tabs) <= 1
 
 
 def qlinear_partial(x, w):
@@ -689,7 +692,7 @@ class QuantWeight:
             _dequant_scratch[key] = buf
         _cuda(self.codes)
         ext().gguf_dequant_packed(self.codes, self.meta, self.N, self.K, self.bits, self.group, buf,
-                                  self.codebook.data_ptr() if self.bits == 2 else 0)
+                                  self.codebook.data_ptr() if self.bits in (2, 5) else 0)
         return PackedWeight.from_packed(buf[:need].view(-1, 64), self.N, self.K)
 
     def dequantize(self) -> torch.Tensor:
@@ -698,6 +701,8 @@ class QuantWeight:
         if self.bits == 2:
             from b200serve.models.e8 import dequantize_packed_e8
             return dequantize_packed_e8(self).to(torch.bfloat16)
+        if self.bits == 5:
+            return _dequantize_iq4(self)
         S, KS = N // 16, K // 16
         lanes = torch.arange(32, device=self.device)
         g, t = lanes // 4, lanes % 4
@@ -726,6 +731,27 @@ class QuantWeight:
         scale = sc.permute(0, 2, 1).reshape(N, K // gsz).repeat_interleave(gsz, 1)
         minus = mn.permute(0, 2, 1).reshape(N, K // gsz).repeat_interleave(gsz, 1)
         return (q * scale + minus).to(torch.bfloat16)
+
+
+def _dequantize_iq4(w) -> torch.Tensor:
+    """bf16 [N, K] of a bits-5 QuantWeight (IQ4 indices through the pair table, times the scale)."""
+    N, K = w.N, w.K
+    S, KS = N // 16, K // 16
+    lanes = torch.arange(32, device=w.codes.device)
+    g, t = lanes // 4, lanes % 4
+    rows = torch.stack([g, g + 8, g, g + 8], 1)
+    cols = torch.stack([2 * t, 2 * t, 2 * t + 8, 2 * t + 8], 1)
+    q = w.codes.view(S, KS, 32).long() & 0xFFFFFFFF
+    tab = w.codebook.long() & 0xFFFFFFFF
+    lo = torch.stack([_bf16_from_bits(tab[(q >> (8 * i)) & 255] & 0xFFFF) for i in range(4)], -1)
+    hi = torch.stack([_bf16_from_bits((tab[(q >> (8 * i)) & 255] >> 16) & 0xFFFF) for i in range(4)], -1)
+    v = torch.zeros(S, KS, 16, 16, device=w.codes.device)
+    v[:, :, rows, cols] = lo
+    v[:, :, rows, cols + 1] = hi
+    v = v.permute(0, 2, 1, 3).reshape(N, K)
+    sc = _bf16_from_bits(w.meta.view(S, K // 32, 16, 2)[..., 0].long() & 0xFFFF)
+    scale = sc.permute(0, 2, 1).reshape(N, K // 32).repeat_interleave(32, 1)
+    return (v * scale).to(torch.bfloat16)
 
 
 def _bf16_from_bits(b: torch.Tensor) -> torch.Tensor:
@@ -824,7 +850,7 @@ def linear(x, w, bias=None, residual=None, epilogue=EPI_BF16, out=None, workspac
                 out.copy_(y)
                 return out
             return y
-        if (x.is_cuda and M <= 32 and w.bits != 2 and epilogue in (EPI_BF16, EPI_F32) and bias is None
+        if (x.is_cuda and M <= 32 and w.bits in (4, 8) and epilogue in (EPI_BF16, EPI_F32) and bias is None
                 and residual is None):
             y = torch.empty(M, N, dtype=x.dtype, device=x.device)
             _cuda(x)

@@ -31,9 +31,9 @@ std::vector<int64_t> gguf_stream(torch::Tensor x, std::vector<torch::Tensor> cod
                                  std::vector<int64_t> ns, std::vector<int64_t> bits, std::vector<int64_t> groups,
                                  int64_t mode, torch::Tensor out, int64_t ldo, torch::Tensor ws, torch::Tensor counters,
                                  torch::Tensor push_ptrs, int64_t mc_ptr, int64_t num_sms, int64_t wait_ms,
-                                 int64_t e8_codebook);
+                                 int64_t table);
 void gguf_dequant_packed(torch::Tensor codes, torch::Tensor meta, int64_t N, int64_t K, int64_t bits, int64_t group,
-                         torch::Tensor out, int64_t e8_codebook);
+                         torch::Tensor out, int64_t table);
 void gemm_grouped_ep(torch::Tensor act, torch::Tensor w_packed, int64_t N, int64_t E, torch::Tensor offsets,
                      int64_t max_rows, torch::Tensor out, torch::Tensor ws, torch::Tensor counters, int64_t epi,
                      int64_t ag_flags_ptr, int64_t ag_n, int64_t ag_epoch_ptr, torch::Tensor comb_meta,

@@ -52,23 +52,16 @@ __device__ __forceinline__ void dequant_s8(uint32_t w0, uint32_t w1, uint32_t sa
   }
 }
 
-// E8 vector codes (2 bits per weight: one byte names an 8-value codebook vector): word q holds
-// the indices of (row g, v0), (row g + 8, v0), (row g, v1), (row g + 8, v1), where v0 / v1 are
-// the two 8-column vectors of the k-step; the lane takes pair t4 of each. cbt: the codebook as
-// bf16 pairs [256][4] in shared memory (32-bit address); (s, o) per row as bf16x2 (s, s) and
-// (o, o): w = c * s + o.
+// Explicit shared-memory reads (32-bit addresses) for the table lookups of the E8 and IQ4 paths.
 __device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
   uint32_t v;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
   return v;
 }
-__device__ __forceinline__ void dequant_e8(uint32_t q, int t4, uint32_t cbt, uint32_t sa, uint32_t oa, uint32_t sb,
-                                           uint32_t ob, uint32_t* a) {
-  const uint32_t lane_off = cbt + 4u * (uint32_t)t4;
-  a[0] = bf2_fma(lds_u32(lane_off + ((q & 255u) << 4)), sa, oa);
-  a[1] = bf2_fma(lds_u32(lane_off + (((q >> 8) & 255u) << 4)), sb, ob);
-  a[2] = bf2_fma(lds_u32(lane_off + (((q >> 16) & 255u) << 4)), sa, oa);
-  a[3] = bf2_fma(lds_u32(lane_off + ((q >> 24) << 4)), sb, ob);
+__device__ __forceinline__ uint2 lds_u64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
 }
 
 }  // namespace b200

@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(kVWarps * 32) gguf_gemv_kernel(const QvArgs a)
 template <int BITS>
 __global__ void gguf_dequant_packed_kernel(const uint32_t* __restrict__ codes, const uint32_t* __restrict__ meta,
                                            int N, int K, int group, __nv_bfloat16* __restrict__ out,
-                                           const uint32_t* __restrict__ e8cb) {
+                                           const uint32_t* __restrict__ e8cb) {   // E8 codebook or IQ4 pair table
   // No early launch of the dependent: the GEMM that reads this weight streams its first weight
   // tiles before its own dependency wait, so it must start only after this grid has finished.
   pdl_wait();
@@ -251,6 +251,13 @@ __global__ void gguf_dequant_packed_kernel(const uint32_t* __restrict__ codes, c
 #pragma unroll
     for (int i = 0; i < 4; ++i)
       a[i] = bf2_fma(__ldg(e8cb + idx[i] * 4 + t4), (i & 1) ? mc.x : ma.x, (i & 1) ? mc.y : ma.y);
+  } else if constexpr (BITS == 5) {
+    // IQ4: byte i = register i's pair of indices into the pair table (e8cb here), times the scale
+    const uint32_t w = __ldg(codes + ((size_t)slice * ksteps + ks) * 32 + lane);
+    const uint32_t* mp = meta + ((size_t)slice * (K / 32) + ks / 2) * 32;
+    const uint32_t sa = __ldg(mp + g * 2), sb = __ldg(mp + (g + 8) * 2);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a[i] = bf2_fma(__ldg(e8cb + ((w >> (8 * i)) & 255u)), (i & 1) ? sb : sa, 0u);
   } else if constexpr (BITS == 4) {
     const uint32_t w = __ldg(codes + ((size_t)slice * ksteps + ks) * 32 + lane);
     const uint32_t* mp = meta + ((size_t)slice * (K / 32) + ks / 2) * 32;
@@ -276,7 +283,7 @@ using namespace b200;
 
 // codes/meta (N x K, N % 128 == 0, K % 64 == 0) -> out bf16 [N/128 * K/64 * 128, 64] tile-packed.
 void gguf_dequant_packed(torch::Tensor codes, torch::Tensor meta, int64_t N, int64_t K, int64_t bits, int64_t group,
-                         torch::Tensor out, int64_t e8_codebook) {
+                         torch::Tensor out, int64_t table) {
   TORCH_CHECK(N % 128 == 0 && K % 256 == 0, "tile-packed dequantisation needs N % 128 == 0 and K % 256 == 0");
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.numel() >= N * K, "output too small");
   const long long tasks = (N / 16) * (K / 16);
@@ -285,10 +292,14 @@ void gguf_dequant_packed(torch::Tensor codes, torch::Tensor meta, int64_t N, int
   auto cp = reinterpret_cast<const uint32_t*>(codes.data_ptr());
   auto mp = reinterpret_cast<const uint32_t*>(meta.data_ptr());
   auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
-  auto cbp = reinterpret_cast<const uint32_t*>(e8_codebook);
+  auto cbp = reinterpret_cast<const uint32_t*>(table);
   if (bits == 2) {
     TORCH_CHECK(cbp != nullptr && (group == 32 || group == 64 || group == 128 || group == 256), "E8: codebook, group");
     launch_pdl(gguf_dequant_packed_kernel<2>, grid, dim3(threads), 0, at::cuda::getCurrentCUDAStream(), cp, mp,
+               (int)N, (int)K, (int)group, op, cbp);
+  } else if (bits == 5) {
+    TORCH_CHECK(cbp != nullptr, "IQ4: pair table");
+    launch_pdl(gguf_dequant_packed_kernel<5>, grid, dim3(threads), 0, at::cuda::getCurrentCUDAStream(), cp, mp,
                (int)N, (int)K, (int)group, op, cbp);
   } else if (bits == 4)
     launch_pdl(gguf_dequant_packed_kernel<4>, grid, dim3(threads), 0, at::cuda::getCurrentCUDAStream(), cp, mp,

@@ -13,6 +13,10 @@
 //             the weights of the first stages are requested before the dependency wait
 //   consumer  warp w dequantises slice w of each landed item in registers (gguf_common.cuh)
 //             and runs mma.sync m16n8k16 with the staged activations as the B operand
+// Code types: 4-bit (Q4_K: scale and -min per 32), 8-bit (Q6_K / Q8_0: scale per 16 or 32), 4-bit
+// indices into the 16-value IQ4 table (bits 5: a 256-entry pair table in shared memory, scale per
+// 32), and E8 lattice vectors (bits 2: one byte per 8 weights, a 256 x 8 codebook in shared memory,
+// scale and offset per group; the MMA k-slots are permuted so each lane reads half a vector).
 // All waits are bounded (error 190 in the last counter word, then the CTA drains and exits).
 //
 // A CTA's range starts and ends inside tiles, so a tile's rows are summed over the CTAs
@@ -39,10 +43,16 @@ enum GsMode : int { GS_BF16 = 0, GS_F32 = 1, GS_PARTIAL = 2, GS_PUSH = 4 };
 constexpr int kGsConsumers = 8;             // consumer warps = slices per tile
 constexpr int kGsThreads = (kGsConsumers + 1) * 32;
 constexpr int kGsMaxParts = 4;
-constexpr int kGsXRow = 264;                // bf16 per staged activation row (256 + 8 padding)
-constexpr int kGsXBytes = 16 * kGsXRow * 2; // activation rows of one stage (up to 16 tokens)
+// bf16 per staged activation row: 256 + padding so that the B-fragment reads of a warp hit distinct
+// banks (32-bit reads: a row stride of 4 words mod 32; the E8 path's 64-bit reads: 8 words)
+template <int BITS>
+struct GsX {
+  static constexpr int row = BITS == 2 ? 272 : 264;
+};
+constexpr int kGsXBytes = 16 * 272 * 2;     // activation rows of one stage (up to 16 tokens)
 constexpr int kGsSmemBudget = 110 * 1024;   // per CTA: two CTAs per SM
-constexpr int kGsCtl = 5120;                // barriers and flags (128 B) + push staging (8 x 512 B)
+constexpr int kGsCtl = 6144;                // barriers and flags (128 B) + push staging (8 x 512 B) + IQ4 table (1 KB)
+constexpr int kGsNlTab = 5120;              // offset of the IQ4 pair table in the control block
 
 // Stage geometry for codes of `bits` (8 also covers groups mixing 4- and 8-bit parts; 2 is the
 // E8 vector code: one byte per 8 weights, and a 4 KB codebook table after the control block).
@@ -88,7 +98,8 @@ struct GsArgs {
   __nv_bfloat16* push[8];                   // GS_PUSH: this rank's slot base on every rank
   int world;
   __nv_bfloat16* mc;                        // GS_PUSH through a multicast object
-  const uint32_t* e8cb;                     // E8 parts: codebook as bf16 pairs [256][4]
+  const uint32_t* table;                    // E8 parts: codebook as bf16 pairs [256][4]; IQ4 parts (bits 5):
+                                            // bf16 pairs of the 16-value table for every code byte [256]
   int* err;
   uint64_t wait_ns;
 };
@@ -138,8 +149,9 @@ __device__ __forceinline__ void gs_issue(const GsArgs& a, int tile, int c, uint8
   using Gm = GsGeom<BITS>;
   const GsPart& p = a.parts[gs_part_of(a, tile)];
   const int ksteps = a.K / 16;
-  const uint32_t cbytes = p.bits == 4 ? 2048u : p.bits == 8 ? 4096u : 512u;
-  const uint32_t mbytes = p.bits == 4 ? 1024u : p.bits == 8 ? (uint32_t)(256 / p.group) * 64u : gs_e8_meta_bytes(p.group);
+  const bool b4 = p.bits == 4 || p.bits == 5;                   // 5: 4-bit codes through the IQ4 table
+  const uint32_t cbytes = b4 ? 2048u : p.bits == 8 ? 4096u : 512u;
+  const uint32_t mbytes = b4 ? 1024u : p.bits == 8 ? (uint32_t)(256 / p.group) * 64u : gs_e8_meta_bytes(p.group);
   const int nvalid = min(kGsConsumers, p.slices - (tile - p.tile0) * kGsConsumers);
   if ((what & GS_ANNOUNCE) && lane == 0)
     tc::mbar_arrive_expect_tx(bar, (uint32_t)nvalid * (cbytes + mbytes) + (uint32_t)a.M * 512u);
@@ -147,17 +159,17 @@ __device__ __forceinline__ void gs_issue(const GsArgs& a, int tile, int c, uint8
   if ((what & GS_W) && lane < 2 * kGsConsumers && (lane & 7) < nvalid) {
     const size_t ls = (size_t)(tile - p.tile0) * kGsConsumers + (lane & 7);
     if (lane < kGsConsumers) {
-      const uint32_t* src = p.codes + (ls * ksteps + (size_t)c * 16) * (p.bits == 4 ? 32 : p.bits == 8 ? 64 : 8);
+      const uint32_t* src = p.codes + (ls * ksteps + (size_t)c * 16) * (b4 ? 32 : p.bits == 8 ? 64 : 8);
       tc::bulk_g2s(st + Gm::codes_off + (lane & 7) * Gm::code, src, cbytes, bar);
     } else {
-      const uint32_t* src = p.bits == 4 ? p.meta + (ls * (a.K / 32) + (size_t)c * 8) * 32
+      const uint32_t* src = b4 ? p.meta + (ls * (a.K / 32) + (size_t)c * 8) * 32
                             : p.meta + (ls * (a.K / p.group) + (size_t)c * (256 / p.group)) * (p.bits == 8 ? 16 : 32);
       tc::bulk_g2s(st + Gm::meta_off + (lane & 7) * Gm::meta, src, mbytes, bar);
     }
   }
   if ((what & GS_X) && lane >= 16 && lane < 16 + a.M) {
     const int tok = lane - 16;
-    tc::bulk_g2s(st + Gm::x_off + tok * kGsXRow * 2, a.x + (size_t)tok * a.ldx + (size_t)c * 256, 512u, bar);
+    tc::bulk_g2s(st + Gm::x_off + tok * GsX<BITS>::row * 2, a.x + (size_t)tok * a.ldx + (size_t)c * 256, 512u, bar);
   }
 }
 
@@ -165,8 +177,9 @@ __device__ __forceinline__ void gs_issue(const GsArgs& a, int tile, int c, uint8
 // g, g+8, g+8 of the slice x tokens j*8 + 2*t4, +1, +0, +1).
 template <int BITS, int NB>
 __device__ __forceinline__ void gs_compute(const uint8_t* st, int bits, int group, int w, int lane,
-                                           float (&acc)[NB][4], uint32_t cbt) {
+                                           float (&acc)[NB][4], uint32_t cbt, uint32_t nlt) {
   using Gm = GsGeom<BITS>;
+  constexpr int kGsXRow = GsX<BITS>::row;
   const int g = lane >> 2, t4 = lane & 3;
   const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(st + Gm::x_off) + g * kGsXRow + 2 * t4;
   const uint8_t* cb = st + Gm::codes_off + w * Gm::code;
@@ -176,20 +189,53 @@ __device__ __forceinline__ void gs_compute(const uint8_t* st, int bits, int grou
 #pragma unroll
   for (int j = 0; j < NB; ++j) odd[j][0] = odd[j][1] = odd[j][2] = odd[j][3] = 0.f;
   if constexpr (BITS == 2) {
+    // The 16 k-slots of each MMA are permuted: lane t4's slots (2t4, 2t4+1, 2t4+8, 2t4+9) carry
+    // columns 4t4 .. 4t4+3, i.e. half (t4 & 1) of the k-step's 8-column vector (t4 >> 1). The
+    // staged activations are read in the same order (one 64-bit read per token), and each row's
+    // four weights are one 64-bit codebook read.
     const uint32_t* cw = reinterpret_cast<const uint32_t*>(cb);          // [16 k-steps][8 row pairs]
     const uint2* mt = reinterpret_cast<const uint2*>(mb);                 // [256 / group][16 rows] (s, o)
     const int gsh = group == 32 ? 1 : group == 64 ? 2 : group == 128 ? 3 : 4;   // k-steps per group, log2
+    const int vsh = 16 * (t4 >> 1);                                       // this lane's vector in the word
+    const uint32_t half = cbt + 8u * (uint32_t)(t4 & 1);
+    const __nv_bfloat16* xp = xs + 2 * t4;                                // columns 4t4 .. 4t4+3
 #pragma unroll
     for (int ks = 0; ks < 16; ++ks) {
       const int gi = ks >> gsh;
       const uint2 ma = mt[gi * 16 + g], mc = mt[gi * 16 + g + 8];
+      const uint32_t q = cw[ks * 8 + g] >> vsh;
+      const uint2 ra = lds_u64(half + ((q & 255u) << 4)), rb = lds_u64(half + (((q >> 8) & 255u) << 4));
       uint32_t wv[4];
-      dequant_e8(cw[ks * 8 + g], t4, cbt, ma.x, ma.y, mc.x, mc.y, wv);
+      wv[0] = bf2_fma(ra.x, ma.x, ma.y);
+      wv[1] = bf2_fma(rb.x, mc.x, mc.y);
+      wv[2] = bf2_fma(ra.y, ma.x, ma.y);
+      wv[3] = bf2_fma(rb.y, mc.x, mc.y);
 #pragma unroll
       for (int j = 0; j < NB; ++j) {
-        const __nv_bfloat16* r = xs + j * 8 * kGsXRow + ks * 16;
-        qmma((ks & 1) ? odd[j] : acc[j], wv, *reinterpret_cast<const uint32_t*>(r),
-             *reinterpret_cast<const uint32_t*>(r + 8));
+        const uint2 bx = *reinterpret_cast<const uint2*>(xp + j * 8 * kGsXRow + ks * 16);
+        qmma((ks & 1) ? odd[j] : acc[j], wv, bx.x, bx.y);
+      }
+    }
+  } else if (bits == 5) {
+    // IQ4: byte i of the lane's word is register i's pair of table indices; w = s * table[q]
+    const uint32_t* cw = reinterpret_cast<const uint32_t*>(cb);
+    const uint2* mt = reinterpret_cast<const uint2*>(mb);                 // [8 sub-blocks][16 rows] (s, 0)
+#pragma unroll
+    for (int sb = 0; sb < 8; ++sb) {
+      const uint32_t sa = mt[sb * 16 + g].x, sc = mt[sb * 16 + g + 8].x;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int ks = sb * 2 + h;
+        const uint32_t q = cw[ks * 32 + lane];
+        uint32_t wv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          wv[i] = bf2_fma(lds_u32(nlt + (((q >> (8 * i)) & 255u) << 2)), (i & 1) ? sc : sa, 0u);
+#pragma unroll
+        for (int j = 0; j < NB; ++j) {
+          const __nv_bfloat16* r = xs + j * 8 * kGsXRow + ks * 16;
+          qmma(h ? odd[j] : acc[j], wv, *reinterpret_cast<const uint32_t*>(r), *reinterpret_cast<const uint32_t*>(r + 8));
+        }
       }
     }
   } else if (BITS == 4 || bits == 4) {
@@ -383,8 +429,12 @@ __global__ void __launch_bounds__(kGsThreads, 2) gguf_stream_kernel(const GsArgs
     *issued = -1;
     tc::fence_barrier_init();
   }
-  if constexpr (BITS == 2) {          // a weight: read before the dependency wait
-    for (int i = threadIdx.x; i < 1024; i += kGsThreads) cbt[i] = __ldg(a.e8cb + i);
+  uint32_t* nlt = reinterpret_cast<uint32_t*>(ctl + kGsNlTab);           // IQ4 pair table (bits 5 parts)
+  if constexpr (BITS == 2) {          // weights: read before the dependency wait
+    for (int i = threadIdx.x; i < 1024; i += kGsThreads) cbt[i] = __ldg(a.table + i);
+  } else {
+    if (a.table != nullptr)
+      for (int i = threadIdx.x; i < 256; i += kGsThreads) nlt[i] = __ldg(a.table + i);
   }
   __syncthreads();
   if (warp == kGsConsumers) {
@@ -435,7 +485,9 @@ __global__ void __launch_bounds__(kGsThreads, 2) gguf_stream_kernel(const GsArgs
       mine = (cur - pp->tile0) * kGsConsumers + warp < pp->slices;
     }
     if (!*abort_flag && gs_wait(&full[s], ph, a, abort_flag)) {
-      if (mine) gs_compute<BITS, NB>(smem + s * Gm::bytes, pp->bits, pp->group, warp, lane, acc, tc::smem_u32(cbt));
+      if (mine)
+        gs_compute<BITS, NB>(smem + s * Gm::bytes, pp->bits, pp->group, warp, lane, acc, tc::smem_u32(cbt),
+                             tc::smem_u32(nlt));
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&empty[s]);
     }
@@ -509,7 +561,7 @@ std::vector<int64_t> gguf_stream(torch::Tensor x, std::vector<torch::Tensor> cod
                                  std::vector<int64_t> ns, std::vector<int64_t> bits, std::vector<int64_t> groups,
                                  int64_t mode, torch::Tensor out, int64_t ldo, torch::Tensor ws, torch::Tensor counters,
                                  torch::Tensor push_ptrs, int64_t mc_ptr, int64_t num_sms, int64_t wait_ms,
-                                 int64_t e8_codebook) {
+                                 int64_t table) {
   const int M = x.size(0), K = x.size(1);
   const int np = (int)codes.size();
   TORCH_CHECK(np >= 1 && np <= kGsMaxParts && metas.size() == codes.size() && ns.size() == codes.size() &&
@@ -527,13 +579,14 @@ std::vector<int64_t> gguf_stream(torch::Tensor x, std::vector<torch::Tensor> cod
   for (int p = 0; p < np; ++p) {
     TORCH_CHECK(ns[p] % 16 == 0, "N must be a multiple of 16");
     TORCH_CHECK(mode != GS_PARTIAL || ns[p] % 128 == 0, "partial outputs need N % 128 == 0 (128-column tiles)");
-    TORCH_CHECK(bits[p] == 4 || (bits[p] == 8 && (groups[p] == 16 || groups[p] == 32)) ||
+    TORCH_CHECK(bits[p] == 4 || bits[p] == 5 || (bits[p] == 8 && (groups[p] == 16 || groups[p] == 32)) ||
                     (bits[p] == 2 && (groups[p] == 32 || groups[p] == 64 || groups[p] == 128 || groups[p] == 256)),
-                "4-bit codes (group 32), 8-bit codes with group 16 or 32, or E8 codes with group 32..256");
+                "4-bit codes (group 32; 5: through the IQ4 table), 8-bit codes with group 16 or 32, or E8 codes "
+                "with group 32..256");
     TORCH_CHECK((bits[p] == 2) == (bits[0] == 2), "E8 parts cannot share a launch with other code types");
     const auto cp = reinterpret_cast<uintptr_t>(codes[p].data_ptr()), mp = reinterpret_cast<uintptr_t>(metas[p].data_ptr());
     TORCH_CHECK(cp % 16 == 0 && mp % 16 == 0, "codes and scales must be 16-byte aligned for the bulk copies");
-    TORCH_CHECK(codes[p].numel() * codes[p].element_size() >= ns[p] * K / (bits[p] == 2 ? 8 : 8 / bits[p]),
+    TORCH_CHECK(codes[p].numel() * codes[p].element_size() >= ns[p] * K / (bits[p] == 2 ? 8 : bits[p] == 8 ? 1 : 2),
                 "codes too small");
     if (bits[p] == 2)
       TORCH_CHECK(metas[p].numel() * metas[p].element_size() >= ns[p] * (K / groups[p]) * 8, "E8 scales too small");
@@ -550,9 +603,12 @@ std::vector<int64_t> gguf_stream(torch::Tensor x, std::vector<torch::Tensor> cod
   }
   auto plan = gguf_stream_plan((int64_t)tiles * 128, K, num_sms);
   a.nparts = np;
-  if (bits[0] == 2) {
-    TORCH_CHECK(e8_codebook != 0 && e8_codebook % 16 == 0, "E8 parts need the codebook table ([256][4] bf16 pairs)");
-    a.e8cb = reinterpret_cast<const uint32_t*>(e8_codebook);
+  bool any5 = false;
+  for (int p = 0; p < np; ++p) any5 = any5 || bits[p] == 5;
+  if (bits[0] == 2 || any5) {
+    TORCH_CHECK(table != 0 && table % 16 == 0,
+                "E8 parts need the codebook table ([256][4] bf16 pairs), IQ4 parts the pair table ([256])");
+    a.table = reinterpret_cast<const uint32_t*>(table);
   }
   a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
   a.ldx = (int)x.stride(0);

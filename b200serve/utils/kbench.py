@@ -249,6 +249,57 @@ def gguf_gemv_suite(M=8):
         torch.cuda.empty_cache()
 
 
+def e8_gemv_suite(M=8, group=128):
+    """Decode GEMV of E8 layers (one byte per 8 weights, models/e8.py) over the Qwen3-8B shapes:
+    stream-K direct output and partials, as the fraction of the measured copy bandwidth, with
+    weight copies > 2.5x the L2 rotating; the bf16 tcgen05 stream-K GEMM of the same shape for
+    comparison of the time."""
+    from b200serve.models import e8 as E8
+    hbm, _, src = peaks()
+    cb = E8.lattice_codebook()
+    cases = [("q_proj", 4096, 4096), ("gate_up", 24576, 4096), ("o_proj", 4096, 4096), ("down", 4096, 12288)]
+    for name, N, K in cases:
+        def make():
+            idx = torch.randint(0, 256, (N, K // 8), dtype=torch.uint8, device="cuda")
+            sc = (torch.rand(N, K // group, device="cuda") * 0.02 + 0.01).half()
+            of = (torch.randn(N, K // group, device="cuda") * 0.001).half()
+            return E8.pack(idx, sc, of, cb, group, device="cuda")
+        w0 = make()
+        nbytes = w0.codes.numel() * 4 + w0.meta.numel() * 4
+        reps = max(2, -(-(320 << 20) // nbytes))
+        ws = [w0] + [make() for _ in range(reps - 1)]
+        for w in ws:
+            w.codebook = w0.codebook
+        xk = torch.randn(M, K, device="cuda").bfloat16()
+        row = {"case": "e8_gemv", "shape": name, "M": M, "N": N, "K": K, "group": group, "MB": round(nbytes / 1e6, 2)}
+        i = [0]
+
+        def gemv():
+            ops.linear(xk, ws[i[0] % reps])
+            i[0] += 1
+
+        def partial():
+            ops.qlinear_partial(xk, ws[i[0] % reps])
+            i[0] += 1
+
+        for label, fn in (("stream", gemv), ("stream_partial", partial)):
+            ms = time_graph(fn, calls=2 * reps)
+            row[label + "_us"] = round(ms * 1e3, 2)
+            row[label + "_hbm_frac"] = round(nbytes / (ms * 1e-3) / (hbm * 1e9), 3)
+        del ws
+        bf = [ops.pack_weight((torch.randn(N, K, device="cuda") * 0.02).bfloat16()) for _ in range(2)]
+        j = [0]
+
+        def dense():
+            ops.linear_partial(xk, bf[j[0] % 2])
+            j[0] += 1
+        row["bf16_partial_us"] = round(time_graph(dense, calls=4) * 1e3, 2)
+        row["peaks"] = src
+        print(json.dumps(row), flush=True)
+        del bf
+        torch.cuda.empty_cache()
+
+
 def gguf_one(N=4096, K=4096, M=8, kind="q4_k"):
     """A few launches of the stream-K GGUF GEMV on one shape (a small case for a profiler): four
     rounds of one partial-output and one direct-output launch. Twelve weight copies rotate so
@@ -313,7 +364,7 @@ def gemm_trace(M=32, N=4096, K=4096):
     print(json.dumps(out))
 
 
-def decode_step(layers=2, B=32, ctx=2304, iters=3):
+def decode_step(layers=2, B=32, ctx=2304, iters=3, tp=1):
     """Eager decode steps of the Qwen3-8B shape (``layers`` layers) at batch B and
     context ``ctx``: the kernel sequence of one step, for launch lists / ncu."""
     from b200serve.engine.kv_cache import KVCache
@@ -601,6 +652,9 @@ if __name__ == "__main__":
     if what == "partial_one":
         partial_one(*[int(v) for v in sys.argv[2:5]])
         sys.exit(0)
+    if what == "e8_gemv":
+        e8_gemv_suite(*[int(v) for v in sys.argv[2:4]])
+        sys.exit(0)
     if what == "gguf_gemv":
         gguf_gemv_suite(*[int(v) for v in sys.argv[2:3]])
         sys.exit(0)
@@ -621,7 +675,7 @@ if __name__ == "__main__":
         deltanet_one(*[int(v) for v in sys.argv[2:4]])
         sys.exit(0)
     if what == "decode_step":
-        decode_step(*[int(v) for v in sys.argv[2:5]])
+        decode_step(*[int(v) for v in sys.argv[2:7]])
         sys.exit(0)
     if what in ("gemm", "all"):
         bench_gemm()

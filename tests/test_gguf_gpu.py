@@ -189,3 +189,45 @@ def test_gguf_group_partial_swiglu_and_packed_dequant():
         assert ((yb.float().cpu() - yr).norm() / yr.norm()).item() < 1e-2
         pw = qw.dequantize_packed()
         assert torch.equal(pw.unpacked().cpu(), qw.dequantize().cpu())
+
+
+def _iq4_pair(N, K, t, seed=0):
+    import test_iq4_cpu as IQ
+    raw = IQ.iq4_raw(N, K, t, seed)
+    qw = G._repack(raw, t, N, K, "cuda")
+    return qw, qw.dequantize().float().cpu()          # the kernel's bf16 weights
+
+
+@pytest.mark.parametrize("t", [G.GGML_IQ4_NL, G.GGML_IQ4_XS])
+@pytest.mark.parametrize("M", [1, 8, 16])
+def test_iq4_stream_vs_fp32(t, M):
+    """IQ4 through the table-lookup path of the stream-K GEMV (direct, fp32 and partial outputs)
+    and the prefill dequantisation, against fp32 PyTorch on the same bf16 weights."""
+    N, K = 1024, 2048
+    qw, ref_w = _iq4_pair(N, K, t)
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    ref = x.float().cpu() @ ref_w.t()
+    rel = lambda a, b: ((a.float().cpu() - b).norm() / b.norm()).item()
+    y = ops.linear(x, qw)
+    assert rel(y, ref) < 1e-2 and torch.equal(y, ops.linear(x, qw))
+    assert rel(ops.linear(x, qw, epilogue=ops.EPI_F32), ref) < 1e-2
+    yn = ops.rmsnorm(ops.qlinear_partial(x, qw), torch.ones(N, device="cuda").bfloat16(), 1e-6)
+    r = ref * torch.rsqrt(ref.pow(2).mean(-1, keepdim=True) + 1e-6)
+    assert rel(yn, r) < 2e-2
+    xp = torch.randn(80, K, device="cuda").bfloat16()
+    assert rel(ops.linear(xp, qw), xp.float().cpu() @ ref_w.t()) < 1e-2
+
+
+def test_iq4_in_mixed_groups():
+    """IQ4 parts next to Q4_K (the 4-bit kernel) and next to Q6_K (the 8-bit kernel) in one job."""
+    K, M = 1024, 8
+    iq, iqref = _iq4_pair(512, K, G.GGML_IQ4_XS, seed=3)
+    q4, q4ref = _quant_pair(128, K, seed=4)[G.GGML_Q4_K]
+    q6, q6ref = _quant_pair(128, K, seed=5)[G.GGML_Q6_K]
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    for parts, refs in (([iq, q4], [iqref, q4ref]), ([iq, q6], [iqref, q6ref])):
+        ref = torch.cat([x.float().cpu() @ r.t() for r in refs], 1)
+        n = ref.shape[1]
+        yn = ops.rmsnorm(ops.qlinear_partial(x, G.QuantGroup(parts)), torch.ones(n, device="cuda").bfloat16(), 1e-6)
+        r = ref * torch.rsqrt(ref.pow(2).mean(-1, keepdim=True) + 1e-6)
+        assert ((yn.float().cpu() - r).norm() / r.norm()).item() < 2e-2
