@@ -69,6 +69,8 @@ class ModelRunner:
         self.launches_per_step = {}
         self.last_loop_ms = None
         self.h_toks = None
+        self.h_patch = self.d_patch = None
+        self._patches = []
         self._pipe = None
         self.vocab_start = weights.vocab_start
         self.greedy_buf = None
@@ -255,19 +257,50 @@ class ModelRunner:
         B = len(ids)
         bucket, nbytes = self.load_decode_inputs(ids, pos, slots, block_tables, lens, state_slots)
         self._pipe = {"B": B, "bucket": bucket}
+        self._patches = []
         if self.h_toks is None:
             pin = self.device.type == "cuda"
             self.h_toks = [torch.zeros(self.max_batch, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
         return nbytes
 
     def pipeline_patch_block(self, row: int, block_index: int, block: int):
-        """Point entry ``block_index`` of sequence ``row``'s block table at ``block`` (device)."""
-        self.s_bt[row, block_index] = block
+        """Point entry ``block_index`` of sequence ``row``'s block table at ``block``: queued, and
+        applied on the device by the next pipeline_step() (no host wait on the step in flight)."""
+        self._patches.append((row, block_index, block))
+
+    def _apply_patches(self):
+        """Queued block-table entries -> pinned staging -> one async copy -> scatter on the device.
+        Two stagings alternate; before one is rewritten the host waits for the event recorded
+        after its last copy (long done in practice: a whole step ran in between)."""
+        n = len(self._patches)
+        if self.h_patch is None or self.h_patch[0].shape[1] < n:
+            if self.h_patch is not None:
+                torch.cuda.current_stream().synchronize()
+            pin = self.device.type == "cuda"
+            cap = max(n, 2 * self.max_batch)
+            self.h_patch = [torch.zeros(3, cap, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+            self.d_patch = [torch.zeros(3, cap, dtype=torch.int32, device=self.device) for _ in range(2)]
+            self._patch_ev = [None, None]
+            self._patch_i = 0
+        i = self._patch_i
+        self._patch_i ^= 1
+        if self._patch_ev[i] is not None:
+            self._patch_ev[i].synchronize()
+        hp, dp = self.h_patch[i], self.d_patch[i]
+        hp[:, :n] = torch.as_tensor(self._patches, dtype=torch.int32).t()
+        dp[:, :n].copy_(hp[:, :n], non_blocking=True)
+        self.s_bt.index_put_((dp[0, :n].long(), dp[1, :n].long()), dp[2, :n])
+        ev = torch.cuda.Event()
+        ev.record()
+        self._patch_ev[i] = ev
+        self._patches.clear()
 
     def pipeline_step(self, slot: int):
         """Replay the decode+advance graph once and start copying its tokens into pinned
         buffer ``slot``; returns the CUDA event that marks the copy complete."""
         B, bucket = self._pipe["B"], self._pipe["bucket"]
+        if self._patches:
+            self._apply_patches()
         key = (bucket, "loop", B)
         if key not in self.graphs:
             self._warmup(bucket, True)

@@ -13,7 +13,8 @@ ours (default)
          inputs are far larger than L2.
   e2e    the same metric through the public batch API (B200Engine.generate): per step
          a pinned host->device copy of the step inputs and a device->host read of the
-         sampled tokens. p50 TTFT comes from the same API run (all B requests
+         sampled tokens; max(K, 128) decode tokens per request, timed from the moment the
+         last request has its first token to the last token. p50 TTFT comes from the same API run (all B requests
          submitted at once, prompt 2048).
 reference
   the unmodified reference TransformersEngine (baseline/_ref) with a random-init
@@ -57,6 +58,12 @@ def parse():
     return ap.parse_args()
 
 
+# The end-to-end request decodes at least this many tokens: the window it is timed over starts
+# when the last of the B prompts has its first token (prompts finish prefill chunk by chunk) and
+# ends with the last token, so a short request would mostly time the ramp-down of the batch.
+E2E_MIN_STEPS = 128
+
+
 def emit(d):
     print(json.dumps(d), flush=True)
 
@@ -95,7 +102,8 @@ def run_ours(a):
     torch.cuda.set_device(lrank)
     match = _tp_path_check(a.model, world, rank) if (world > 1 and a.comm == "fused") else None
     B, P, K, W = a.batch, a.prompt, a.steps, a.warmup
-    max_seq = ((P + K + W + 64) + 15) // 16 * 16
+    KE = max(K, E2E_MIN_STEPS)        # decode steps of the end-to-end request
+    max_seq = ((P + KE + W + 64) + 15) // 16 * 16
     moe = a.model == "qwen3-30b-a3b"
     cfg = EngineConfig(model=a.model, tp_size=world, ep_size=world if moe else 1, max_batch=B, max_seq=max_seq,
                        prefill_chunk=8192, cuda_graphs=True, comm=a.comm, num_layers_override=a.layers,
@@ -117,7 +125,7 @@ def run_ours(a):
         _finish_dist(eng)
         return
 
-    sp = SamplingParams(temperature=0.0, max_tokens=K + 1, ignore_eos=True)
+    sp = SamplingParams(temperature=0.0, max_tokens=KE + 1, ignore_eos=True)
     # warm-up through the public API with the timed request shape, so the decode graphs of
     # every bucket and the pipelined loop are captured before the timed call
     eng.generate(_prompts(B, P, vocab, seed=1), sp)
