@@ -236,7 +236,9 @@ class EngineConfig:
     tp_size      tensor-parallel ranks (1/2/4/8); ep_size: expert-parallel ranks
     kv_format    "bf16", "int4g128" (4-bit K/V with fp16 scale per 128 values) or
                  "turboquant" (WHT + Lloyd-Max codes, ``kv_key_bits``/``kv_value_bits``;
-                 ``kv_boundary_layers`` N keeps the first and last N attention layers in bf16)
+                 ``kv_boundary_layers`` N keeps the first and last N attention layers in bf16;
+                 ``kv_residual_tokens`` R keeps each sequence's newest R..R+15 tokens (whole
+                 16-token pages) in bf16 beside their codes; the reference's default is 128)
     kv_block     tokens per KV page
     max_batch    most sequences decoded together (CUDA-graph buckets up to this)
     max_seq      longest sequence (prompt + completion) accepted; 0 = the largest context
@@ -268,6 +270,7 @@ class EngineConfig:
     kv_key_bits: int = 4
     kv_value_bits: int = 4
     kv_boundary_layers: int = 0
+    kv_residual_tokens: int = 0
     kv_block: int = 16
     max_batch: int = 64
     max_seq: int = 4096

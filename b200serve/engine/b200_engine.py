@@ -48,6 +48,12 @@ def _safetensors_getter(path):
     return lambda name: where[name].get_tensor(name) if name in where else None
 
 
+def _window_pages(max_batch: int, window_tokens: int) -> int:
+    """Pages of the bf16 residual-window pool: a ring of window / 16 + 1 pages per sequence slot,
+    one more slot for the padded rows of a decode bucket."""
+    return (max_batch + 1) * (window_tokens // BLOCK + 1)
+
+
 def _kv_layers(mc) -> int:
     return sum(1 for i in range(mc.num_layers) if mc.has_kv(i))
 
@@ -160,9 +166,14 @@ class B200Engine(BaseEngine):
             nb = cfgE.kv_boundary_layers
             n_kv = _kv_layers(mc)
             kv_b = KVCache(min(n_kv, 2 * nb), num_blocks, nkv_local, mc.head_dim, dtype=dtype, device=dev)
+        kv_w, rw = None, 0
+        if cfgE.kv_format == "turboquant" and cfgE.kv_residual_tokens > 0:
+            rw = (cfgE.kv_residual_tokens + BLOCK - 1) // BLOCK * BLOCK
+            kv_w = KVCache(_kv_layers(mc), _window_pages(cfgE.max_batch, rw), nkv_local, mc.head_dim, dtype=dtype,
+                           device=dev)
         from b200serve.engine.runner import ModelRunner
         runner = ModelRunner(mc, self.weights, self.kv, comm=self.comm, device=dev, max_batch=cfgE.max_batch,
-                             kv_boundary=kv_b, boundary_layers=nb,
+                             kv_boundary=kv_b, boundary_layers=nb, kv_window=kv_w, window_tokens=rw,
                              max_seq=cfgE.max_seq, use_graphs=cfgE.cuda_graphs)
         if tp > 1:
             from b200serve.parallel.worker import BroadcastRunner
@@ -173,7 +184,7 @@ class B200Engine(BaseEngine):
         self._attach_vision(mc, dtype, dev)
         # a prefix-cache hit would skip tokens whose recurrent state a hybrid model needs
         self.scheduler = Scheduler(runner, num_blocks, max_batch=cfgE.max_batch, prefill_chunk=cfgE.prefill_chunk,
-                                   max_seq=cfgE.max_seq, prefix_cache=not mc.is_hybrid,
+                                   max_seq=cfgE.max_seq, prefix_cache=not mc.is_hybrid and kv_w is None,
                                    spec_ngram=0 if mc.is_hybrid else cfgE.spec_ngram,
                                    spec_mtp=cfgE.spec_mtp and getattr(runner, "mtp", None) is not None)
         self.tokenizer = self._injected_tokenizer or load_tokenizer(self._model_path(), mc.vocab_size)
@@ -315,6 +326,10 @@ class B200Engine(BaseEngine):
             per_block += KVCache.bytes_per_block(min(_kv_layers(mc), 2 * cfgE.kv_boundary_layers), nkv_local,
                                                  mc.head_dim, esz, "bf16")
         state = 0
+        if cfgE.kv_format == "turboquant" and cfgE.kv_residual_tokens > 0:   # bf16 residual-window pages
+            rw = (cfgE.kv_residual_tokens + BLOCK - 1) // BLOCK * BLOCK
+            state += _window_pages(cfgE.max_batch, rw) * KVCache.bytes_per_block(_kv_layers(mc), nkv_local,
+                                                                                mc.head_dim, esz, "bf16")
         if mc.is_hybrid:
             from b200serve.models.hybrid import LinearState
             state = (cfgE.max_batch + 1) * LinearState.bytes_per_slot(mc, cfgE.tp_size)

@@ -36,11 +36,12 @@ PACK = 5
 
 class ModelRunner:
     def __init__(self, cfg, weights, kv, comm=None, device="cuda", max_batch=64, max_seq=4096,
-                 use_graphs=True, kv_boundary=None, boundary_layers=0):
+                 use_graphs=True, kv_boundary=None, boundary_layers=0, kv_window=None, window_tokens=0):
         self.cfg = cfg
         self.device = torch.device(device)
         self.decoder = Decoder(cfg, weights, kv, comm=comm, device=self.device, kv_boundary=kv_boundary,
-                               boundary_layers=boundary_layers)
+                               boundary_layers=boundary_layers, kv_window=kv_window, window_tokens=window_tokens,
+                               max_batch=max_batch)
         self.comm = self.decoder.comm
         self.max_batch = max_batch
         self.max_seq = max_seq
@@ -63,6 +64,10 @@ class ModelRunner:
             self.lin_state = LinearState(cfg, tp, max_batch, self.device)
             self.decoder.lin_state = self.lin_state
             self.scratch_slot = self.lin_state.scratch
+        if kv_window is not None:
+            self.scratch_slot = max_batch          # the window pool's spare ring (LinearState uses the same index)
+        # per-request slots: the recurrent state of hybrid models, the TurboQuant residual-window ring
+        self.state_slots_used = self.lin_state is not None or kv_window is not None
         self.s_state = torch.full((B,), self.scratch_slot, **i32)
         self.graphs = {}
         self.graph_out = {}
@@ -104,7 +109,7 @@ class ModelRunner:
         return ForwardBatch(input_ids=self.s_ids[:bucket], positions=self.s_pos[:bucket],
                             slots=self.s_slots[:bucket], block_tables=self.s_bt[:bucket],
                             seq_lens=self.s_lens[:bucket], logit_rows=None, is_decode=True,
-                            state_slots=self.s_state[:bucket] if self.lin_state is not None else None)
+                            state_slots=self.s_state[:bucket] if self.state_slots_used else None)
 
     def _decode_body(self, bucket: int, greedy: bool):
         logits = self.decoder.forward(self._decode_fb(bucket), attn_plan=self.attn_plan(bucket))
@@ -355,7 +360,7 @@ class ModelRunner:
         fb = ForwardBatch(input_ids=t(ids), positions=t(pos), slots=t(slots), block_tables=bt.to(d),
                           seq_lens=t(lens), logit_rows=torch.as_tensor(rows, dtype=torch.long).to(d),
                           is_decode=False, cu_q=t(cu), q_start=t(qs), max_q=max(len(s["ids"]) for s in seqs),
-                          state_slots=t(sts) if self.lin_state is not None else None, telemetry=watch or None,
+                          state_slots=t(sts) if self.state_slots_used else None, telemetry=watch or None,
                           hidden=any(s.get("hidden") for s in seqs),
                           keep_prenorm=self.mtp is not None and any(s.get("prenorm") for s in seqs))
         if T == 0:

@@ -103,8 +103,10 @@ class Scheduler:
         self.embed_waiting = []
         self.lock = threading.Lock()
         self.pipeline = True
-        # hybrid (DeltaNet) models keep a recurrent state per running request
-        self.free_states = list(range(max_batch)) if getattr(runner, "lin_state", None) is not None else None
+        # hybrid (DeltaNet) models keep a recurrent state per running request, and the TurboQuant
+        # residual window a ring of bf16 pages
+        inner = getattr(runner, "inner", runner)
+        self.free_states = list(range(max_batch)) if getattr(inner, "state_slots_used", False) else None
         self.spec_ngram = spec_ngram
         # MTP drafting needs the runner's head (runner.mtp), which sees every committed position
         self.spec_mtp = bool(spec_mtp) and getattr(runner, "mtp", None) is not None

@@ -74,7 +74,8 @@ class NoComm:
 
 class Decoder:
     def __init__(self, cfg: ModelConfig, weights: ModelWeights, kv_cache, comm=None, attn_splits=None,
-                 device="cpu", kv_boundary=None, boundary_layers: int = 0):
+                 device="cpu", kv_boundary=None, boundary_layers: int = 0, kv_window=None, window_tokens: int = 0,
+                 max_batch: int = 0):
         self.cfg = cfg
         self.w = weights
         self.kv = kv_cache
@@ -87,6 +88,18 @@ class Decoder:
         self.kvi_b = {li: j for j, li in enumerate(sorted(self.boundary))}
         if self.boundary and (kv_boundary is None or kv_boundary.num_layers < len(self.boundary)):
             raise ValueError(f"{len(self.boundary)} boundary layers need a bf16 cache with as many layers")
+        # TurboQuant residual window (reference: core/turboquant_cache.py:349-394, the newest
+        # ``residual_length`` tokens in full precision): every token is still encoded, and the newest
+        # pages of each sequence are also kept in bf16, rotated like the queries, in a ring of
+        # window / 16 + 1 pages per request slot of ``kv_window``. Attention reads tokens
+        # [0, qlen) from the codes and [qlen, len) from the ring, qlen = (len - window) // 16 * 16.
+        tq_fmt = getattr(kv_cache, "kv_format", "bf16") == "turboquant"
+        self.kvw = kv_window if (tq_fmt and window_tokens > 0) else None
+        self.win_tokens = window_tokens if self.kvw is not None else 0
+        self.win_pages = window_tokens // 16 + 1 if self.kvw is not None else 0
+        if self.kvw is not None and kv_window.num_blocks < (max_batch + 1) * self.win_pages:
+            raise ValueError("the residual-window pool needs (max_batch + 1) x (window / 16 + 1) pages")
+        self._win = None
         self.comm = comm or NoComm()
         self.device = torch.device(device)
         tp = weights.tp_size
@@ -172,14 +185,52 @@ class Decoder:
         stage_slots = torch.arange(T, dtype=torch.int32, device=qkv.device)
         q = ops.qkv_post(qkv, None, lw.q_norm, lw.k_norm, self._rope_cs(i, fb), self._rope_pos(fb), stage_slots, kst, vst,
                          self.nq, self.nkv, eps, hd=self.hd)
-        q_rot, q_jl = ops.tq_qkv(q, kst, vst, fb.slots, tb, kv, i)
+        win = self._win if self.kvw is not None else None
+        wkv = (self.kvw.k[i], self.kvw.v[i], win[0]) if win is not None else None
+        q_rot, q_jl = ops.tq_qkv(q, kst, vst, fb.slots, tb, kv, i, window=wkv)
         if fb.is_decode:
+            if win is not None:
+                return ops.tq_decode_attention_window(q_rot, q_jl, kv, i, tb, fb.block_tables, win[1], self.kvw.k[i],
+                                                      self.kvw.v[i], win[2], fb.seq_lens, self.scale, tps, nsplit, ws)
             return ops.tq_decode_attention(q_rot, q_jl, kv, i, tb, fb.block_tables, fb.seq_lens, self.scale, tps,
                                            nsplit, ws)
         ids, tables, kd, vd = pre
         ops.tq_dequant(ids, kv, i, tb, kd, vd)
+        if win is not None:       # window pages: the exact bf16 rows instead of their codes
+            S, mb = tables.shape
+            P = torch.arange(mb, device=tables.device)[None, :]
+            m = (P >= (win[1] // 16).long()[:, None]) & (P < ((fb.seq_lens + 15) // 16).long()[:, None]) & (tables >= 0)
+            dst, src = tables[m].long(), win[2][:, :mb][m].long()
+            kd.index_copy_(0, dst, self.kvw.k[i].index_select(0, src).to(kd.dtype))
+            vd.index_copy_(0, dst, self.kvw.v[i].index_select(0, src).to(vd.dtype))
         return ops.paged_prefill_attention(q_rot, kd, vd, tables, fb.seq_lens, fb.q_start, fb.cu_q, self.scale,
                                            max_q=fb.max_q)
+
+    def _tq_window_info(self, fb):
+        """(ring slot of each new token or -1, qlen [S] tokens read from the codes, ring page of
+        every logical page [S, max_blocks]) for this step; tokens outside the last window / 16 + 1
+        pages of their sequence are not written to the ring."""
+        W, R = self.win_pages, self.win_tokens
+        lens = fb.seq_lens.long()
+        st = fb.state_slots.long()
+        dev = lens.device
+        if fb.is_decode:
+            seq_of = torch.arange(lens.shape[0], device=dev)
+            p = lens - 1
+        else:
+            T = fb.input_ids.shape[0]
+            cu = fb.cu_q.long()
+            t = torch.arange(T, device=dev)
+            seq_of = torch.searchsorted(cu[1:], t, right=True)
+            p = fb.q_start.long()[seq_of] + (t - cu[seq_of])
+        P = torch.div(p, 16, rounding_mode="floor")
+        last = torch.div(lens[seq_of] - 1, 16, rounding_mode="floor")
+        keep = (P > last - W) & (fb.slots >= 0)
+        slots = torch.where(keep, (st[seq_of] * W + P % W) * 16 + p % 16, torch.full_like(p, -1)).to(torch.int32)
+        qlen = (torch.div((lens - R).clamp(min=0), 16, rounding_mode="floor") * 16).to(torch.int32)
+        mb = fb.block_tables.shape[1]
+        wbt = (st[:, None] * W + torch.arange(mb, device=dev)[None, :] % W).to(torch.int32)
+        return slots, qlen, wbt
 
     def _tq_prefill_pages(self, fb):
         """Unique pages of the prefill batch, tables remapped onto them, and bf16 scratch pages."""
@@ -472,9 +523,12 @@ class Decoder:
         if hasattr(comm, "begin_step"):
             comm.begin_step()
         h = fb.inputs_embeds if fb.inputs_embeds is not None else ops.embedding(fb.input_ids, w.embed)
+        self._win = self._tq_window_info(fb) if (self.kvw is not None and self.tq is not None) else None
         if fb.is_decode:
             tps, nsplit = attn_plan or self.decode_attn_plan(T, int(fb.block_tables.shape[1]) * 16)
-            ws = self.ensure_attn_workspace(T, nsplit) if nsplit > 1 else None
+            # the residual window adds one split after the code splits
+            nws = nsplit + (1 if self._win is not None else 0)
+            ws = self.ensure_attn_workspace(T, nws) if nws > 1 else None
         quant_kv = self.tq is not None or (self.kv.kv_format == "int4g128" and h.is_cuda and ops._TC_PREFILL)
         tq_pre = self._tq_prefill_pages(fb) if (quant_kv and not fb.is_decode) else None
         plan = (tps, nsplit, ws) if fb.is_decode else (0, 0, None)

@@ -1199,17 +1199,28 @@ def _tq_dequant_rows(codes, sgn, meta, tb: TurboQuantTables, keys: bool):
     return n[..., None] * (u + g[..., None] * t)
 
 
-def tq_qkv(q, k_stage, v_stage, slots, tb: TurboQuantTables, kv, layer: int):
+def tq_qkv(q, k_stage, v_stage, slots, tb: TurboQuantTables, kv, layer: int, window=None):
     """Rotate the queries (q_rot = H q, q_jl = S q_rot) and encode the new K/V rows of
     ``k_stage``/``v_stage`` (token t at page t // 16, row t % 16) into the TurboQuant cache at
-    ``slots``. Returns (q_rot, q_jl)."""
+    ``slots``. ``window`` (k_pages, v_pages, win_slots): also store each row rotated (H k, H v)
+    in bf16 at its residual-window slot (-1: none). Returns (q_rot, q_jl)."""
     q_rot = torch.empty_like(q)
     q_jl = torch.empty_like(q)
     if _cuda(q):
+        wk, wv, ws_ = window if window is not None else (_NO_OUT, _NO_OUT, _NO_OUT)
         ext().tq_qkv(q, k_stage, v_stage, slots, tb.S, tb.cents, tb.thr_host, tb.key_bits, tb.value_bits,
                      float(tb.alpha), q_rot, q_jl, kv.k[layer], kv.k_sign[layer], kv.k_scale[layer], kv.v[layer],
-                     kv.v_scale[layer])
+                     kv.v_scale[layer], wk, wv, ws_)
         return q_rot, q_jl
+    if window is not None:
+        wk, wv, wsl = window
+        T = q.shape[0]
+        t = torch.arange(T)
+        ok = wsl.long() >= 0
+        wb, wo = wsl.long()[ok] // 16, wsl.long()[ok] % 16
+        for h in range(k_stage.shape[1]):
+            for stage, dst in ((k_stage, wk), (v_stage, wv)):
+                dst[wb, h, wo] = _fwht(stage[t // 16, h, t % 16].float())[ok].to(dst.dtype)
     T, nq, hd = q.shape
     qr = _fwht(q.float())
     q_rot.copy_(qr)
@@ -1245,6 +1256,39 @@ def tq_dequant(block_ids, kv, layer: int, tb: TurboQuantTables, out_k, out_v):
     out_k[:n] = _tq_dequant_rows(kv.k[layer][ids], kv.k_sign[layer][ids], kv.k_scale[layer][ids], tb,
                                  True).to(out_k.dtype)
     out_v[:n] = _tq_dequant_rows(kv.v[layer][ids], None, kv.v_scale[layer][ids], tb, False).to(out_v.dtype)
+
+
+def tq_decode_attention_window(q_rot, q_jl, kv, layer: int, tb: TurboQuantTables, block_tables, qlen, win_k,
+                               win_v, win_tables, seq_lens, scale, tps=256, nsplit=1, workspace=None):
+    """Decode attention with a bf16 residual window: tokens [0, qlen) from the TurboQuant codes
+    (``nsplit`` splits), tokens [qlen, seq_lens) from the window pages ``win_k``/``win_v`` through
+    ``win_tables`` (one more split), merged by the split-KV combine. Rotated-domain output."""
+    if _cuda(q_rot, 2):
+        out = torch.empty_like(q_rot)
+        assert workspace is not None and workspace.max_splits >= nsplit + 1
+        total = nsplit + 1
+        e = ext()
+        e.paged_decode_attention_tq_part(q_rot, q_jl, kv.k[layer], kv.k_sign[layer], kv.k_scale[layer], kv.v[layer],
+                                         kv.v_scale[layer], tb.code_vals_host, block_tables, qlen, workspace.acc,
+                                         workspace.ml, float(scale), int(tps), int(nsplit), 0, total)
+        e.paged_decode_attention_tc_part(q_rot, win_k, win_v, win_tables, seq_lens, qlen, workspace.acc, workspace.ml,
+                                         float(scale), 1 << 20, 1, nsplit, total)
+        e.paged_decode_combine(workspace.acc, workspace.ml, seq_lens, out, win_k.shape[1],
+                               q_rot.shape[1] // win_k.shape[1], total, 0)
+        return out
+    B = q_rot.shape[0]
+    nb = block_tables.shape[1]
+    ids = block_tables.reshape(-1).clamp_min(0)
+    kd = _tq_dequant_rows(kv.k[layer][ids], kv.k_sign[layer][ids], kv.k_scale[layer][ids], tb, True)
+    vd = _tq_dequant_rows(kv.v[layer][ids], None, kv.v_scale[layer][ids], tb, False)
+    kd = kd.view(B * nb, *kd.shape[1:]).clone()
+    vd = vd.view(B * nb, *vd.shape[1:]).clone()
+    for b in range(B):
+        for P in range(int(qlen[b]) // 16, (int(seq_lens[b]) + 15) // 16):
+            kd[b * nb + P] = win_k[int(win_tables[b, P])].to(kd.dtype)
+            vd[b * nb + P] = win_v[int(win_tables[b, P])].to(vd.dtype)
+    tables = torch.arange(B * nb, dtype=torch.int32).view(B, nb)
+    return paged_decode_attention(q_rot, kd, vd, tables, seq_lens, scale)
 
 
 def tq_decode_attention(q_rot, q_jl, kv, layer: int, tb: TurboQuantTables, block_tables, seq_lens, scale,

@@ -240,7 +240,8 @@ __global__ void paged_decode_combine_kernel(const float* __restrict__ part_acc, 
   const int nq = nkv * G;
   if (warp >= B * nq) return;
   const int b = warp / nq, h = warp % nq, kvh = h / G, g = h % G;
-  const int used = min(nsplit, (seq_lens[b] + tps - 1) / tps);
+  // tps 0: every split holds a share (empty ones carry m = -inf, l = 0)
+  const int used = tps > 0 ? min(nsplit, (seq_lens[b] + tps - 1) / tps) : nsplit;
   float M = -INFINITY;
   for (int s = 0; s < used; ++s) M = fmaxf(M, part_ml[((((size_t)b * nkv + kvh) * nsplit + s) * G + g) * 2]);
   float L = 0.f, A[E];
@@ -319,7 +320,8 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tenso
   }
 }
 
-// Merge split-KV partials into out [B, nq, HD] (used by the tensor-core decode kernel).
+// Merge split-KV partials into out [B, nq, HD] (used by the tensor-core decode kernel); tps 0 merges
+// all nsplit splits of every sequence.
 void paged_decode_combine(torch::Tensor part_acc, torch::Tensor part_ml, torch::Tensor seq_lens, torch::Tensor out,
                           int64_t nkv, int64_t G, int64_t nsplit, int64_t tps) {
   const int B = out.size(0), nq = out.size(1), HD = out.size(2);

@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
     int max_blocks, int nkv, float scale_log2, int tps, float* __restrict__ part_acc, float* __restrict__ part_ml,
     __nv_bfloat16* __restrict__ out, int nsplit, int* err, const uint8_t* __restrict__ kq,
     const uint8_t* __restrict__ vq, const __half* __restrict__ ks, const __half* __restrict__ vs, const TqArgs tq,
-    int nblocks) {
+    int nblocks, const int* __restrict__ tok_lo, int split_base, int nsplit_total) {
   static_assert(G >= 1 && G <= 16, "query heads per kv head");
   constexpr int KSTEPS = KVQ == 2 ? 16 : 8;        // 16-dim MMA k-steps of the (virtual) key
   extern __shared__ uint8_t smem_raw[];
@@ -200,7 +200,8 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int len = seq_lens[b];
   const int nq = nkv * G;
-  const int start = split * tps;
+  // tokens [tok_lo[b], len) when given (a multiple of 16), split into chunks of tps
+  const int start = (tok_lo ? tok_lo[b] : 0) + split * tps;
   const int stop = min(len, start + tps);
   const int* bt = block_tables + (size_t)b * max_blocks;
 
@@ -425,10 +426,10 @@ __global__ void __launch_bounds__(kTcWarps * 32, 2) paged_decode_tc_kernel(
         A += wo[(w * G + hh) * kHD + d] * f;
       }
     }
-    if (nsplit == 1) {
+    if (nsplit_total == 1) {
       out[((size_t)b * nq + kvh * G + hh) * kHD + d] = __float2bfloat16_rn(L > 0.f ? A / L : 0.f);
     } else {
-      const size_t slot = (((size_t)b * nkv + kvh) * nsplit + split) * G + hh;
+      const size_t slot = (((size_t)b * nkv + kvh) * nsplit_total + split_base + split) * G + hh;
       part_acc[slot * kHD + d] = A;
       if (d == 0) { part_ml[slot * 2] = M; part_ml[slot * 2 + 1] = L; }
     }
@@ -488,13 +489,18 @@ void paged_decode_combine(torch::Tensor part_acc, torch::Tensor part_ml, torch::
 static void decode_tc_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                            torch::Tensor seq_lens, torch::Tensor out, torch::Tensor part_acc, torch::Tensor part_ml,
                            double scale, int64_t tps, int64_t nsplit, int kvq, const uint8_t* kq, const uint8_t* vq,
-                           const __half* ksc, const __half* vsc, int nkv, const TqArgs& tq) {
+                           const __half* ksc, const __half* vsc, int nkv, const TqArgs& tq,
+                           const int* tok_lo = nullptr, int split_base = 0, int nsplit_total = 0) {
+  // nsplit_total 0: this launch covers every split and combines them itself
+  const bool own = nsplit_total == 0;
+  if (own) nsplit_total = (int)nsplit;
   const int B = q.size(0), nq = q.size(1), HD = q.size(2);
   const int G = nq / nkv;
   TORCH_CHECK(HD == kHD && k_cache.size(2) == 16 && tps % 16 == 0 && nsplit >= 1);
-  if (nsplit > 1) {
-    TORCH_CHECK(part_acc.numel() >= (int64_t)B * nkv * nsplit * G * HD, "attention workspace too small");
-    TORCH_CHECK(part_ml.numel() >= (int64_t)B * nkv * nsplit * G * 2, "attention workspace too small");
+  TORCH_CHECK(split_base >= 0 && split_base + nsplit <= nsplit_total, "splits out of range");
+  if (nsplit_total > 1) {
+    TORCH_CHECK(part_acc.numel() >= (int64_t)B * nkv * nsplit_total * G * HD, "attention workspace too small");
+    TORCH_CHECK(part_ml.numel() >= (int64_t)B * nkv * nsplit_total * G * 2, "attention workspace too small");
   }
   if (B == 0) return;
   CUtensorMap tk, tv;
@@ -509,9 +515,9 @@ static void decode_tc_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor
   auto stream = at::cuda::getCurrentCUDAStream();
   const float sl2 = (float)(scale * 1.4426950408889634);
   dim3 grid(nsplit, nkv, B);
-  float* pa = nsplit > 1 ? part_acc.data_ptr<float>() : nullptr;
-  float* pm = nsplit > 1 ? part_ml.data_ptr<float>() : nullptr;
-  auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  float* pa = nsplit_total > 1 ? part_acc.data_ptr<float>() : nullptr;
+  float* pm = nsplit_total > 1 ? part_ml.data_ptr<float>() : nullptr;
+  auto op = (out.defined() && out.numel()) ? reinterpret_cast<__nv_bfloat16*>(out.data_ptr()) : nullptr;
   const size_t smem = decode_tc_smem(kvq);
 #define B200_TC1(GV, KQ)                                                                                       \
   {                                                                                                            \
@@ -524,7 +530,8 @@ static void decode_tc_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor
     launch_pdl(paged_decode_tc_kernel<GV, KQ>, grid, dim3(kTcWarps * 32), smem, stream, tk, tv,                \
                reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), (const int*)block_tables.data_ptr<int>(),  \
                (const int*)seq_lens.data_ptr<int>(), (int)block_tables.size(1), nkv, sl2, (int)tps, pa, pm, op, \
-               (int)nsplit, decode_tc_err_word(), kq, vq, ksc, vsc, tq, (int)k_cache.size(0));                 \
+               (int)nsplit, decode_tc_err_word(), kq, vq, ksc, vsc, tq, (int)k_cache.size(0), tok_lo,         \
+               split_base, nsplit_total);                                                                   \
   }
 #define B200_TC(GV) { if (kvq == 2) B200_TC1(GV, 2) else if (kvq) B200_TC1(GV, 1) else B200_TC1(GV, 0) }
   switch (G) {
@@ -537,7 +544,20 @@ static void decode_tc_impl(torch::Tensor q, torch::Tensor k_cache, torch::Tensor
   }
 #undef B200_TC
 #undef B200_TC1
-  if (nsplit > 1) paged_decode_combine(part_acc, part_ml, seq_lens, out, nkv, G, nsplit, tps);
+  if (own && nsplit > 1) paged_decode_combine(part_acc, part_ml, seq_lens, out, nkv, G, nsplit, tps);
+}
+
+// Splits [split_base, split_base + nsplit) of a decode attention whose partials the caller merges
+// (paged_decode_combine over nsplit_total splits, tps 0): bf16 pages over tokens [tok_lo[b], len).
+void paged_decode_attention_tc_part(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                                    torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor tok_lo,
+                                    torch::Tensor part_acc, torch::Tensor part_ml, double scale, int64_t tps,
+                                    int64_t nsplit, int64_t split_base, int64_t nsplit_total) {
+  TORCH_CHECK(nsplit_total >= 2 && tok_lo.scalar_type() == at::kInt && tok_lo.numel() == q.size(0));
+  TqArgs none{};
+  decode_tc_impl(q, k_cache, v_cache, block_tables, seq_lens, torch::Tensor(), part_acc, part_ml, scale, tps, nsplit,
+                 0, nullptr, nullptr, nullptr, nullptr, k_cache.size(1), none, (const int*)tok_lo.data_ptr<int>(),
+                 (int)split_base, (int)nsplit_total);
 }
 
 void paged_decode_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
@@ -584,6 +604,29 @@ void paged_decode_attention_tq(torch::Tensor q_rot, torch::Tensor q_jl, torch::T
                  k_codes.data_ptr<uint8_t>(), v_codes.data_ptr<uint8_t>(),
                  reinterpret_cast<const __half*>(k_meta.data_ptr()), reinterpret_cast<const __half*>(v_meta.data_ptr()),
                  k_codes.size(1), tq);
+}
+
+// The TurboQuant splits [split_base, split_base + nsplit) of a decode attention merged by the caller
+// (the residual window adds a bf16 split after them).
+void paged_decode_attention_tq_part(torch::Tensor q_rot, torch::Tensor q_jl, torch::Tensor k_codes,
+                                    torch::Tensor k_sign, torch::Tensor k_meta, torch::Tensor v_codes,
+                                    torch::Tensor v_meta, torch::Tensor code_vals, torch::Tensor block_tables,
+                                    torch::Tensor seq_lens, torch::Tensor part_acc, torch::Tensor part_ml, double scale,
+                                    int64_t tps, int64_t nsplit, int64_t split_base, int64_t nsplit_total) {
+  TORCH_CHECK(k_codes.size(3) == 64 && k_codes.scalar_type() == at::kByte && k_sign.size(3) == 16,
+              "turboquant codes must be [*, nkv, 16, 64] and signs [*, nkv, 16, 16] uint8");
+  TORCH_CHECK(q_jl.sizes() == q_rot.sizes() && q_jl.is_contiguous() && q_rot.is_contiguous() && nsplit_total >= 2);
+  TORCH_CHECK(code_vals.device().is_cpu(), "code_vals is a host tensor (baked into the launch parameters)");
+  auto cv = code_vals.to(at::kFloat).contiguous();
+  TORCH_CHECK(cv.numel() == 32, "code_vals must hold 2 x 16 values");
+  TqArgs tq{};
+  tq.ksign = k_sign.data_ptr<uint8_t>();
+  tq.qj = reinterpret_cast<const __nv_bfloat16*>(q_jl.data_ptr());
+  for (int i = 0; i < 16; ++i) { tq.cbk[i] = cv.data_ptr<float>()[i]; tq.cbv[i] = cv.data_ptr<float>()[16 + i]; }
+  decode_tc_impl(q_rot, k_codes, v_codes, block_tables, seq_lens, torch::Tensor(), part_acc, part_ml, scale, tps,
+                 nsplit, 2, k_codes.data_ptr<uint8_t>(), v_codes.data_ptr<uint8_t>(),
+                 reinterpret_cast<const __half*>(k_meta.data_ptr()), reinterpret_cast<const __half*>(v_meta.data_ptr()),
+                 k_codes.size(1), tq, nullptr, (int)split_base, (int)nsplit_total);
 }
 
 B200_BOUNDS_ACCESSOR(attention_decode_tc)

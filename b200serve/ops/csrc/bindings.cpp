@@ -121,7 +121,10 @@ void paged_decode_attention_tq(torch::Tensor q_rot, torch::Tensor q_jl, torch::T
 void tq_qkv(torch::Tensor q, torch::Tensor k_stage, torch::Tensor v_stage, torch::Tensor slots, torch::Tensor S,
             torch::Tensor cents, torch::Tensor thr, int64_t kbits, int64_t vbits, double alpha, torch::Tensor q_rot,
             torch::Tensor q_jl, torch::Tensor k_codes, torch::Tensor k_sign, torch::Tensor k_meta,
-            torch::Tensor v_codes, torch::Tensor v_meta);
+            torch::Tensor v_codes, torch::Tensor v_meta, torch::Tensor win_k, torch::Tensor win_v,
+            torch::Tensor win_slots);
+void paged_decode_combine(torch::Tensor part_acc, torch::Tensor part_ml, torch::Tensor seq_lens, torch::Tensor out,
+                          int64_t nkv, int64_t G, int64_t nsplit, int64_t tps);
 void tq_dequant(torch::Tensor block_ids, torch::Tensor k_codes, torch::Tensor k_sign, torch::Tensor k_meta,
                 torch::Tensor v_codes, torch::Tensor v_meta, torch::Tensor S, torch::Tensor code_vals,
                 torch::Tensor out_k, torch::Tensor out_v);
@@ -196,7 +199,20 @@ static bool bounds_checked() {
 #endif
 }
 
+void paged_decode_attention_tc_part(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                                    torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor tok_lo,
+                                    torch::Tensor part_acc, torch::Tensor part_ml, double scale, int64_t tps,
+                                    int64_t nsplit, int64_t split_base, int64_t nsplit_total);
+void paged_decode_attention_tq_part(torch::Tensor q_rot, torch::Tensor q_jl, torch::Tensor k_codes,
+                                    torch::Tensor k_sign, torch::Tensor k_meta, torch::Tensor v_codes,
+                                    torch::Tensor v_meta, torch::Tensor code_vals, torch::Tensor block_tables,
+                                    torch::Tensor seq_lens, torch::Tensor part_acc, torch::Tensor part_ml, double scale,
+                                    int64_t tps, int64_t nsplit, int64_t split_base, int64_t nsplit_total);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("paged_decode_attention_tc_part", &paged_decode_attention_tc_part);
+  m.def("paged_decode_attention_tq_part", &paged_decode_attention_tq_part);
+  m.def("paged_decode_combine", &paged_decode_combine);
   m.def("bounds_errors", &bounds_errors, py::arg("reset") = true);
   m.def("bounds_checked", &bounds_checked);
   m.doc() = "b200serve sm_100a kernels";

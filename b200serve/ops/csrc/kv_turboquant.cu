@@ -83,7 +83,9 @@ __global__ void __launch_bounds__(kTqW * 32) tq_qkv_kernel(
     const int* __restrict__ slots, int T, int nq, int nkv, const float* __restrict__ S,
     __nv_bfloat16* __restrict__ q_rot, __nv_bfloat16* __restrict__ q_jl, uint8_t* __restrict__ kc,
     uint8_t* __restrict__ ksg, __half* __restrict__ kmeta, uint8_t* __restrict__ vc, __half* __restrict__ vmeta,
-    const TqCodec cd, const float* __restrict__ cent_k, const float* __restrict__ cent_v, int cache_slots) {
+    const TqCodec cd, const float* __restrict__ cent_k, const float* __restrict__ cent_v, int cache_slots,
+    __nv_bfloat16* __restrict__ win_k, __nv_bfloat16* __restrict__ win_v, const int* __restrict__ win_slots,
+    int win_cap) {
   extern __shared__ float sS[];
   __shared__ float vec[kTqW][128];
   __shared__ float cent[2][8];
@@ -134,6 +136,13 @@ __global__ void __launch_bounds__(kTqW * 32) tq_qkv_kernel(
 #pragma unroll
     for (int e = 0; e < 4; ++e) u[e] = x[e] / n;
     fwht128(u, lane);
+    if (win_slots != nullptr) {             // residual window: the rotated row n * u in bf16
+      const int wsl = win_slots[t];
+      if (wsl >= 0 && B200_IN_RANGE(wsl, win_cap, 0x403)) {
+        __nv_bfloat16* wd = (is_v ? win_v : win_k) + (((size_t)(wsl >> 4) * nkv + h) * 16 + (wsl & 15)) * 128 + 4 * lane;
+        *reinterpret_cast<uint2*>(wd) = make_uint2(pack_bf16x2(n * u[0], n * u[1]), pack_bf16x2(n * u[2], n * u[3]));
+      }
+    }
     int idx[4];
     float uh[4];
     tq_quant(u, is_v ? cd.thr_v : cd.thr_k, is_v ? cd.lev_v : cd.lev_k, cent[is_v ? 1 : 0], idx, uh);
@@ -264,8 +273,15 @@ static const size_t kTqSmem = (size_t)128 * kSP * 4;
 void tq_qkv(torch::Tensor q, torch::Tensor k_stage, torch::Tensor v_stage, torch::Tensor slots, torch::Tensor S,
             torch::Tensor cents, torch::Tensor thr, int64_t kbits, int64_t vbits, double alpha, torch::Tensor q_rot,
             torch::Tensor q_jl, torch::Tensor k_codes, torch::Tensor k_sign, torch::Tensor k_meta,
-            torch::Tensor v_codes, torch::Tensor v_meta) {
+            torch::Tensor v_codes, torch::Tensor v_meta, torch::Tensor win_k, torch::Tensor win_v,
+            torch::Tensor win_slots) {
   const int T = q.size(0), nq = q.size(1), nkv = k_codes.size(1);
+  const bool win = win_slots.numel() > 0;
+  if (win)
+    TORCH_CHECK(win_k.scalar_type() == at::kBFloat16 && win_k.is_contiguous() && win_v.is_contiguous() &&
+                    win_k.size(1) == nkv && win_k.size(3) == 128 && win_slots.scalar_type() == at::kInt &&
+                    win_slots.numel() == T,
+                "window pages: bf16 [pages, nkv, 16, 128]; window slots: int32 [T]");
   TORCH_CHECK(q.size(2) == 128 && q.is_contiguous() && k_stage.size(3) == 128, "TurboQuant needs head_dim 128");
   TORCH_CHECK(S.scalar_type() == at::kFloat && S.numel() == 128 * 128 && cents.numel() == 16);
   if (T == 0) return;
@@ -283,7 +299,10 @@ void tq_qkv(torch::Tensor q, torch::Tensor k_stage, torch::Tensor v_stage, torch
              nkv, (const float*)S.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(q_rot.data_ptr()),
              reinterpret_cast<__nv_bfloat16*>(q_jl.data_ptr()), k_codes.data_ptr<uint8_t>(),
              k_sign.data_ptr<uint8_t>(), reinterpret_cast<__half*>(k_meta.data_ptr()), v_codes.data_ptr<uint8_t>(),
-             reinterpret_cast<__half*>(v_meta.data_ptr()), cd, cp, cp + 8, (int)(k_codes.size(0) * 16));
+             reinterpret_cast<__half*>(v_meta.data_ptr()), cd, cp, cp + 8, (int)(k_codes.size(0) * 16),
+             win ? reinterpret_cast<__nv_bfloat16*>(win_k.data_ptr()) : nullptr,
+             win ? reinterpret_cast<__nv_bfloat16*>(win_v.data_ptr()) : nullptr,
+             win ? (const int*)win_slots.data_ptr<int>() : nullptr, win ? (int)(win_k.size(0) * 16) : 0);
 }
 
 // block_ids [n] int32 (device); code_vals [2, 16] fp32 (device); out_k / out_v [n, nkv, 16, 128] bf16.

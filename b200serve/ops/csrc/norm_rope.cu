@@ -184,28 +184,23 @@ __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
   }
 }
 
-// QKV post-processing. One warp per (token, head slot); head slots are
+// QKV post-processing of one (token, head slot) by one warp; head slots are
 // [0, nq) query heads, [nq, nq+nkv) key heads, [nq+nkv, nq+2nkv) value heads.
 // E = HD/32 elements per lane; the rotate-half partner of lane l is lane l^16.
 // KVQ = 0: bf16 cache [blocks][nkv][16][HD]; KVQ = 1: int4g128 cache, codes
 // [blocks][nkv][16][HD/2] (two 4-bit offset-binary values per byte, even dim in
 // the low nibble) + fp16 scale per (token, head) in k_scale/v_scale [blocks][nkv][16].
 template <int HD, int KVQ>
-__global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ bias,
-                                const __nv_bfloat16* __restrict__ qn_w, const __nv_bfloat16* __restrict__ kn_w,
-                                const float* __restrict__ cos_sin, const int* __restrict__ positions,
-                                const int* __restrict__ slots, __nv_bfloat16* __restrict__ q_out,
-                                void* __restrict__ k_cache, void* __restrict__ v_cache, __half* __restrict__ k_scale,
-                                __half* __restrict__ v_scale, int T, int nq, int nkv, float eps, int width, int rot,
-                                const PartialIn pin, int cache_slots, int max_pos) {
+__device__ __forceinline__ void qkv_post_one(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ bias,
+                                             const __nv_bfloat16* __restrict__ qn_w,
+                                             const __nv_bfloat16* __restrict__ kn_w, const float* __restrict__ cos_sin,
+                                             const int* __restrict__ positions, const int* __restrict__ slots,
+                                             __nv_bfloat16* __restrict__ q_out, void* __restrict__ k_cache,
+                                             void* __restrict__ v_cache, __half* __restrict__ k_scale,
+                                             __half* __restrict__ v_scale, int nq, int nkv, float eps, int width,
+                                             int rot, const PartialIn& pin, int cache_slots, int max_pos, int t, int h,
+                                             int lane) {
   constexpr int E = HD / 32;
-  pdl_wait();
-  pdl_trigger();
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  const int nslots = nq + 2 * nkv;
-  if (warp >= T * nslots) return;
-  const int t = warp / nslots, h = warp % nslots;
   const __nv_bfloat16* src = qkv + (size_t)t * width + h * HD + lane * E;
   float x[E];
   if (pin.part) partial_sum<E>(pin, t, h * HD + lane * E, x);
@@ -290,6 +285,32 @@ __global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __n
       if (lane == 0) (is_k ? k_scale : v_scale)[row] = scale_h;
     }
   }
+}
+
+// One warp per (token, HPW consecutive head slots): HPW = 1 for decode-sized steps (most warps in
+// flight), 8 for prefill chunks (the token's position and rotary table are read once per warp and
+// the heads' loads overlap).
+template <int HD, int KVQ, int HPW>
+__global__ void qkv_post_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ bias,
+                                const __nv_bfloat16* __restrict__ qn_w, const __nv_bfloat16* __restrict__ kn_w,
+                                const float* __restrict__ cos_sin, const int* __restrict__ positions,
+                                const int* __restrict__ slots, __nv_bfloat16* __restrict__ q_out,
+                                void* __restrict__ k_cache, void* __restrict__ v_cache, __half* __restrict__ k_scale,
+                                __half* __restrict__ v_scale, int T, int nq, int nkv, float eps, int width, int rot,
+                                const PartialIn pin, int cache_slots, int max_pos) {
+  pdl_wait();
+  pdl_trigger();
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nslots = nq + 2 * nkv;
+  const int groups = (nslots + HPW - 1) / HPW;
+  if (warp >= T * groups) return;
+  const int t = warp / groups, h0 = (warp % groups) * HPW;
+#pragma unroll
+  for (int i = 0; i < HPW; ++i)
+    if (h0 + i < nslots)
+      qkv_post_one<HD, KVQ>(qkv, bias, qn_w, kn_w, cos_sin, positions, slots, q_out, k_cache, v_cache, k_scale,
+                            v_scale, nq, nkv, eps, width, rot, pin, cache_slots, max_pos, t, h0 + i, lane);
 }
 
 // act[t, j] = silu(g) * u where the gate/up GEMM output interleaves 64-wide
@@ -443,7 +464,8 @@ void qkv_post_impl(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::op
               "rotary dims must be <= head_dim with (rot/2)/(head_dim/32) a power of two");
   TORCH_CHECK(positions.scalar_type() == at::kInt && slots.scalar_type() == at::kInt);
   if (T == 0) return;
-  const int warps = T * (nq + 2 * nkv);
+  const int hpw = T >= 128 ? 8 : 1;          // heads per warp: see qkv_post_kernel
+  const int warps = T * ((int)(nq + 2 * nkv + hpw - 1) / hpw);
   const int threads = 256;
   const int blocks = (warps * 32 + threads - 1) / threads;
   auto stream = at::cuda::getCurrentCUDAStream();
@@ -456,10 +478,12 @@ void qkv_post_impl(torch::Tensor qkv, c10::optional<torch::Tensor> bias, c10::op
       positions.data_ptr<int>(), slots.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), \
       k_cache.data_ptr(), v_cache.data_ptr(), k_scale, v_scale, T, (int)nq, (int)nkv, (float)eps, width, rot, pin, \
       (int)(k_cache.size(0) * 16), (int)cos_sin.size(0))
-  if (HD == 128) { if (kvq) B200_QKV((qkv_post_kernel<128, 1>)); else B200_QKV((qkv_post_kernel<128, 0>)); }
-  else if (HD == 64 && !kvq) B200_QKV((qkv_post_kernel<64, 0>));
-  else if (HD == 256 && !kvq) B200_QKV((qkv_post_kernel<256, 0>));
+#define B200_QKV2(HDV, KQV) { if (hpw == 8) B200_QKV((qkv_post_kernel<HDV, KQV, 8>)); else B200_QKV((qkv_post_kernel<HDV, KQV, 1>)); }
+  if (HD == 128) { if (kvq) B200_QKV2(128, 1) else B200_QKV2(128, 0) }
+  else if (HD == 64 && !kvq) B200_QKV2(64, 0)
+  else if (HD == 256 && !kvq) B200_QKV2(256, 0)
   else TORCH_CHECK(false, "head_dim must be 64, 128 or 256 (int4 KV: 128)");
+#undef B200_QKV2
 #undef B200_QKV
   B200_CHECK_CUDA(cudaGetLastError());
 }

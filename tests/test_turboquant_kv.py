@@ -87,3 +87,41 @@ def test_engine_turboquant_kv_cpu():
     assert outs["turboquant"][0][0] == outs["bf16"][0][0]     # lossy KV: later tokens may diverge
     assert outs["bf16"][0] == outs["bf16"][1]                  # the o_proj rotation was undone
     assert torch.allclose(w.layers[0].o, o0, atol=1e-5)
+
+
+def _tiny_engine_outputs(fmts, residual=0, max_seq=256, n_prompt=48, new=8, device="cpu"):
+    import b200serve.models.config as mc
+    cfg = replace(BUILTIN["tiny-qwen2"], head_dim=128, num_heads=2, num_kv_heads=2)
+    w = random_weights(cfg, seed=0, dtype=torch.float32 if device == "cpu" else torch.bfloat16, device=device)
+    old = mc.BUILTIN["tiny-qwen2"]
+    mc.BUILTIN["tiny-qwen2"] = cfg
+    outs, logits = {}, {}
+    try:
+        for name, fmt, r in fmts:
+            eng = B200Engine(EngineConfig(model="tiny-qwen2", device=device,
+                                          dtype="float32" if device == "cpu" else "bfloat16",
+                                          cuda_graphs=device != "cpu", max_seq=max_seq, max_batch=4, kv_format=fmt,
+                                          kv_key_bits=4, kv_value_bits=4, kv_residual_tokens=r), weights=w)
+            eng.load()
+            g = torch.Generator().manual_seed(0)
+            p = torch.randint(0, 32000, (n_prompt,), generator=g).tolist()
+            bt = eng.scheduler.alloc.allocate((n_prompt + 15) // 16)
+            logits[name] = eng.runner.prefill([{"ids": p, "start": 0, "block_table": bt,
+                                                "state_slot": 0}])[0].float().cpu()
+            eng.scheduler.alloc.release(bt)
+            outs[name] = eng.generate([p], SamplingParams(max_tokens=new, ignore_eos=True), timeout=300)[0].output
+            eng.unload()
+    finally:
+        mc.BUILTIN["tiny-qwen2"] = old
+    return outs, logits
+
+
+def test_turboquant_residual_window_cpu():
+    """A window longer than the sequence keeps every token exact: the TurboQuant engine then
+    matches the bf16 one; a short window pulls the prefill logits toward the bf16 ones."""
+    outs, logits = _tiny_engine_outputs([("bf16", "bf16", 0), ("tq", "turboquant", 0),
+                                         ("tq_all", "turboquant", 256), ("tq_w", "turboquant", 16)])
+    assert outs["tq_all"] == outs["bf16"]
+    assert torch.allclose(logits["tq_all"], logits["bf16"], atol=1e-3, rtol=1e-3)
+    err = lambda k: ((logits[k] - logits["bf16"]).norm() / logits["bf16"].norm()).item()
+    assert err("tq_w") < err("tq") and len(outs["tq_w"]) == 8
