@@ -87,11 +87,15 @@ struct PartialIn {
   int tile;               // columns per tile (128: tcgen05 GEMM, 16: GGUF GEMV)
 };
 
+// Slots holding a column: the CTAs first(t)..last(t) whose stream-K ranges touch its tile. The
+// products stay below 2^32 (tiles x kb x ctas; checked by the host wrappers), so 32-bit unsigned
+// division does.
 __device__ __forceinline__ int partial_slots(const PartialIn& pi, int col) {
-  const long long t = col / pi.tile;
-  const long long first = ((t * pi.kb + 1) * pi.ctas + pi.total - 1) / pi.total - 1;
-  const long long last = ((t + 1) * pi.kb * pi.ctas + pi.total - 1) / pi.total - 1;
-  return (int)(last - first + 1);
+  const uint32_t t = (uint32_t)(col / pi.tile), kb = (uint32_t)pi.kb, ctas = (uint32_t)pi.ctas;
+  const uint32_t total = (uint32_t)pi.total;
+  const uint32_t first = ((t * kb + 1u) * ctas + total - 1u) / total - 1u;
+  const uint32_t last = ((t + 1u) * kb * ctas + total - 1u) / total - 1u;
+  return (int)(last - first + 1u);
 }
 
 // Sum of one column's slots, in slot order (no rounding).
@@ -135,6 +139,26 @@ __device__ __forceinline__ void partial_sum(const PartialIn& pi, int row, int co
 }  // namespace b200
 
 namespace b200 {
+
+// Thread-block cluster helpers: a cluster-wide barrier (release / acquire), this CTA's rank in its
+// cluster, and 32-bit reads of another CTA's shared memory (distributed shared memory).
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float cluster_ld_f32(const void* p, uint32_t rank) {
+  uint32_t a, v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"((uint32_t)__cvta_generic_to_shared(p)), "r"(rank));
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return __uint_as_float(v);
+}
+__device__ __forceinline__ int cluster_ld_i32(const void* p, uint32_t rank) {
+  return (int)__float_as_uint(cluster_ld_f32(p, rank));
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
 
 // Programmatic dependent launch (PDL). A kernel launched with
 // launch_pdl() may start while the previous kernel on the stream is still

@@ -515,18 +515,23 @@ __global__ void __launch_bounds__(kGsThreads, 2) gguf_stream_kernel(const GsArgs
 // width 2I, each rounded to bf16 first as a bf16 gate/up projection would be. inter == 0: the
 // columns are [gate | up]; inter == 64: blocks of 64 gate columns then 64 up columns (the
 // interleaved gate/up weight of the tcgen05 GEMM).
+// Eight consecutive outputs per thread (I % 8 == 0): their gate and up columns are eight
+// consecutive columns of one tile each, summed with 16-byte reads.
 __global__ void silu_mul_partial_kernel(const PartialIn pi, int M, int I, int inter, __nv_bfloat16* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= M * I) return;
-  const int t = idx / I, i = idx % I;
+  const int per = I / 8;
+  if (idx >= M * per) return;
+  const int t = idx / per, i = (idx % per) * 8;
   const int gc = inter ? (i / inter) * 2 * inter + i % inter : i;
   const int uc = inter ? gc + inter : I + i;
-  const float gr = __bfloat162float(__float2bfloat16_rn(partial_col(pi, t, gc)));
-  const float ur = __bfloat162float(__float2bfloat16_rn(partial_col(pi, t, uc)));
-  const float sg = __bfloat162float(__float2bfloat16_rn(gr / (1.f + __expf(-gr))));
-  out[(size_t)t * I + i] = __float2bfloat16_rn(sg * ur);
+  float g[8], u[8], o[8];
+  partial_sum<8>(pi, t, gc, g);             // rounded to bf16 as a bf16 projection output would be
+  partial_sum<8>(pi, t, uc, u);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) o[k] = __bfloat162float(__float2bfloat16_rn(g[k] / (1.f + __expf(-g[k])))) * u[k];
+  *reinterpret_cast<bf16x8*>(out + (size_t)t * I + i) = pack8(o);
 }
 
 }  // namespace b200
@@ -670,8 +675,11 @@ void silu_mul_partial(torch::Tensor part, int64_t kb, int64_t ctas, int64_t tota
   TORCH_CHECK(part.scalar_type() == at::kFloat && out.scalar_type() == at::kBFloat16 && out.is_contiguous());
   TORCH_CHECK(tile == 16 || tile == 128, "partial tiles are 16 or 128 columns wide");
   TORCH_CHECK(inter == 0 || (inter == 64 && I % 64 == 0), "inter: 0 or 64 (I % 64 == 0)");
+  TORCH_CHECK(I % 8 == 0, "I must be a multiple of 8");
+  TORCH_CHECK((uint64_t)((2 * I + tile - 1) / tile) * (uint64_t)kb * (uint64_t)ctas < (1ull << 32),
+              "stream-K plan too large for 32-bit slot arithmetic");
   PartialIn pi{part.data_ptr<float>(), (int)kb, (int)ctas, (long long)total, (int)M, (int)(2 * I), (int)tile};
-  const int n = (int)(M * I);
-  launch_pdl(silu_mul_partial_kernel, dim3((n + 255) / 256), dim3(256), 0, at::cuda::getCurrentCUDAStream(), pi, (int)M,
+  const int n = (int)(M * I / 8);
+  launch_pdl(silu_mul_partial_kernel, dim3((n + 127) / 128), dim3(128), 0, at::cuda::getCurrentCUDAStream(), pi, (int)M,
              (int)I, (int)inter, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
 }

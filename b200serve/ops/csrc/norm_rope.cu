@@ -184,6 +184,68 @@ __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
   }
 }
 
+// Add + RMSNorm of decode-sized batches without cross-GPU waits, one row per thread-block cluster
+// of C CTAs: CTA r of a row takes columns [r H / C, (r + 1) H / C) (8 per thread), and the row's sum
+// of squares is reduced across the cluster through distributed shared memory. With one CTA per row
+// only T SMs would work (T = 32 decode rows against 148 SMs). Inputs: the bf16 parts summed, or the
+// fp32 stream-K partials (PartialIn); the same rounding as rmsnorm_fused_kernel.
+template <int C>
+__global__ void __launch_bounds__(256) rmsnorm_cluster_kernel(
+    PartPtrs parts, int nparts, const __nv_bfloat16* residual_in, __nv_bfloat16* residual_out,
+    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H, float eps, const PartialIn pin) {
+  __shared__ float red[32];
+  __shared__ float cl_ss;
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x / C;
+  const uint32_t rank = cluster_rank();
+  const int col = (int)rank * (H / C) + threadIdx.x * 8;
+  const size_t base = (size_t)row * H;
+  float v[8];
+  float ss = 0.f;
+  const bool on = col < (int)(rank + 1) * (H / C);
+  if (on) {
+    float acc[8];
+    if (pin.part) {
+      partial_sum<8>(pin, row, col, acc);
+    } else {
+      unpack8(*reinterpret_cast<const bf16x8*>(parts.p[0] + base + col), acc);
+      for (int k = 1; k < nparts; ++k) {
+        float t[8];
+        unpack8(*reinterpret_cast<const bf16x8*>(parts.p[k] + base + col), t);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] += t[i];
+      }
+    }
+    if (residual_in) {
+      float r[8];
+      unpack8(*reinterpret_cast<const bf16x8*>(residual_in + base + col), r);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += r[i];
+    }
+    const bf16x8 rounded = pack8(acc);
+    unpack8(rounded, v);
+    if (residual_out) *reinterpret_cast<bf16x8*>(residual_out + base + col) = rounded;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+  }
+  ss = block_sum(ss, red);
+  if (threadIdx.x == 0) cl_ss = ss;
+  cluster_barrier();
+  float tot = 0.f;
+#pragma unroll
+  for (int r = 0; r < C; ++r) tot += cluster_ld_f32(&cl_ss, (uint32_t)r);   // the same order in every CTA
+  cluster_barrier();                        // no CTA leaves while another still reads its total
+  const float inv = rsqrtf(tot / (float)H + eps);
+  if (on) {
+    float wf[8], o[8];
+    unpack8(*reinterpret_cast<const bf16x8*>(w + col), wf);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = __bfloat162float(__float2bfloat16_rn(v[i] * inv)) * wf[i];
+    *reinterpret_cast<bf16x8*>(out + base + col) = pack8(o);
+  }
+}
+
 // QKV post-processing of one (token, head slot) by one warp; head slots are
 // [0, nq) query heads, [nq, nq+nkv) key heads, [nq+nkv, nq+2nkv) value heads.
 // E = HD/32 elements per lane; the rotate-half partner of lane l is lane l^16.
@@ -376,6 +438,23 @@ void rmsnorm_fused_impl(std::vector<torch::Tensor> parts, c10::optional<torch::T
   auto rout = residual_out ? reinterpret_cast<__nv_bfloat16*>(residual_out->data_ptr()) : nullptr;
   auto wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  // decode-sized batches without cross-GPU waits: a cluster of C CTAs per row (see the kernel);
+  // B200_NORM_CLUSTER overrides C (1: one CTA per row)
+  static const int cl_env = [] { const char* e = getenv("B200_NORM_CLUSTER"); return e ? atoi(e) : -1; }();
+  int C = T <= 18 ? 8 : T <= 37 ? 4 : T <= 74 ? 2 : 1;
+  if (cl_env >= 0) C = cl_env;
+  if (!wait_flags && !lamport && ag.world == 0 && (C == 2 || C == 4 || C == 8) && H % (8 * C) == 0 &&
+      H / (8 * C) <= 256) {
+    const dim3 grid(T * C), block(((H / (8 * C)) + 31) / 32 * 32);
+    const int np = (int)parts.size();
+    switch (C) {
+      case 8: launch_pdl_cluster(rmsnorm_cluster_kernel<8>, grid, block, 0, stream, 8, pp, np, rin, rout, wp, op, H, (float)eps, pin); break;
+      case 4: launch_pdl_cluster(rmsnorm_cluster_kernel<4>, grid, block, 0, stream, 4, pp, np, rin, rout, wp, op, H, (float)eps, pin); break;
+      default: launch_pdl_cluster(rmsnorm_cluster_kernel<2>, grid, block, 0, stream, 2, pp, np, rin, rout, wp, op, H, (float)eps, pin); break;
+    }
+    B200_CHECK_CUDA(cudaGetLastError());
+    return;
+  }
   switch (vpt) {
     case 1: launch_pdl(rmsnorm_fused_kernel<1>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport, pin, nflags < 0 ? (int)parts.size() : nflags); break;
     case 2: launch_pdl(rmsnorm_fused_kernel<2>, dim3(T), dim3(threads), 0, stream, pp, (int)parts.size(), rin, rout, wp, op, H, (float)eps, wait_flags, epoch, err, ag, flag_wait_ns(), lamport, pin, nflags < 0 ? (int)parts.size() : nflags); break;
@@ -408,6 +487,8 @@ void rmsnorm_partial(torch::Tensor like, torch::Tensor part, int64_t kb, int64_t
                      torch::Tensor w, torch::Tensor out, double eps) {
   TORCH_CHECK(part.scalar_type() == at::kFloat && part.is_contiguous(), "partials: contiguous fp32");
   TORCH_CHECK(tile == 16 || tile == 128, "partial tiles are 16 or 128 columns wide");
+  TORCH_CHECK((uint64_t)((like.size(1) + tile - 1) / tile) * (uint64_t)kb * (uint64_t)ctas < (1ull << 32),
+              "stream-K plan too large for 32-bit slot arithmetic");
   PartialIn pin{part.data_ptr<float>(), (int)kb, (int)ctas, (long long)total, (int)like.size(0), (int)like.size(1),
                 (int)tile};
   rmsnorm_fused_impl({like}, residual_in, residual_out, w, out, eps, nullptr, nullptr, nullptr, AgArgs{}, 0, pin);
@@ -507,6 +588,8 @@ void qkv_post_partial(torch::Tensor like, torch::Tensor part, int64_t kb, int64_
   TORCH_CHECK(part.scalar_type() == at::kFloat && part.is_contiguous(), "partials: contiguous fp32");
   TORCH_CHECK(like.stride(0) == like.size(1), "partials have the row stride of a dense [T, width] output");
   TORCH_CHECK(tile == 16 || tile == 128, "partial tiles are 16 or 128 columns wide");
+  TORCH_CHECK((uint64_t)((like.size(1) + tile - 1) / tile) * (uint64_t)kb * (uint64_t)ctas < (1ull << 32),
+              "stream-K plan too large for 32-bit slot arithmetic");
   PartialIn pin{part.data_ptr<float>(), (int)kb, (int)ctas, (long long)total, (int)like.size(0), (int)like.size(1),
                 (int)tile};
   const bool q4 = k_scale.has_value();

@@ -11,24 +11,34 @@ __device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
   if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
 }
 
-// One CTA (512 threads) per row; fp32 logits read as float4.
+// One row per cluster of C CTAs (512 threads each): CTA r scans its slice of the vocabulary
+// (slice starts rounded down to 4 values), fp32 logits read as float4 where aligned; the slices'
+// winners meet in CTA 0 through distributed shared memory (ties: the lowest index, as with C = 1).
+template <int C>
 __global__ void __launch_bounds__(512) argmax_rows_kernel(const float* __restrict__ logits, int V, int ld,
                                                           int* __restrict__ out_idx, float* __restrict__ out_val,
                                                           int index_offset) {
   pdl_wait();
   pdl_trigger();
-  const float* row = logits + (size_t)blockIdx.x * ld;
+  const int rowid = blockIdx.x / C;
+  const int rank = C == 1 ? 0 : (int)cluster_rank();
+  const int lo = C == 1 ? 0 : ((int)((long long)V * rank / C) & ~3);
+  const int hi = C == 1 ? V : (rank == C - 1 ? V : ((int)((long long)V * (rank + 1) / C) & ~3));
+  const float* row = logits + (size_t)rowid * ld;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  const int V4 = ((reinterpret_cast<uintptr_t>(row) & 15) == 0 && (ld & 3) == 0) ? V / 4 : 0;
-  for (int i = threadIdx.x; i < V4; i += blockDim.x) {
-    const float4 v = reinterpret_cast<const float4*>(row)[i];
-    better(bv, bi, v.x, 4 * i);
-    better(bv, bi, v.y, 4 * i + 1);
-    better(bv, bi, v.z, 4 * i + 2);
-    better(bv, bi, v.w, 4 * i + 3);
+  const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0 && (ld & 3) == 0;
+  const int n4 = vec ? (hi - lo) / 4 : 0;
+  const float4* r4 = reinterpret_cast<const float4*>(row + lo);
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+    const float4 v = r4[i];
+    const int c = lo + 4 * i;
+    better(bv, bi, v.x, c);
+    better(bv, bi, v.y, c + 1);
+    better(bv, bi, v.z, c + 2);
+    better(bv, bi, v.w, c + 3);
   }
-  for (int i = V4 * 4 + threadIdx.x; i < V; i += blockDim.x) better(bv, bi, row[i], i);
+  for (int i = lo + n4 * 4 + threadIdx.x; i < hi; i += blockDim.x) better(bv, bi, row[i], i);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -49,10 +59,20 @@ __global__ void __launch_bounds__(512) argmax_rows_kernel(const float* __restric
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       better(bv, bi, ov, oi);
     }
-    if (lane == 0) {
-      out_idx[blockIdx.x] = bi + index_offset;
-      if (out_val) out_val[blockIdx.x] = bv;
+    if (C == 1 && lane == 0) {
+      out_idx[rowid] = bi + index_offset;
+      if (out_val) out_val[rowid] = bv;
     }
+    if (C > 1 && lane == 0) { sv[0] = bv; si[0] = bi; }
+  }
+  if constexpr (C > 1) {
+    cluster_barrier();
+    if (rank == 0 && threadIdx.x == 0) {
+      for (int r = 1; r < C; ++r) better(bv, bi, cluster_ld_f32(&sv[0], (uint32_t)r), cluster_ld_i32(&si[0], (uint32_t)r));
+      out_idx[rowid] = bi + index_offset;
+      if (out_val) out_val[rowid] = bv;
+    }
+    cluster_barrier();                    // CTA 0 has read every slice's winner
   }
 }
 
@@ -75,9 +95,19 @@ void argmax_rows(torch::Tensor logits, torch::Tensor out_idx, torch::Tensor out_
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1);
   const int B = logits.size(0), V = logits.size(1);
   if (B == 0) return;
-  launch_pdl(argmax_rows_kernel, dim3(B), dim3(512), 0, at::cuda::getCurrentCUDAStream(),
-             (const float*)logits.data_ptr<float>(), V, (int)logits.stride(0), out_idx.data_ptr<int>(),
-             out_val.numel() ? out_val.data_ptr<float>() : (float*)nullptr, (int)index_offset);
+  // rows split over clusters so that B x C CTAs fill the SMs (one CTA per row would leave most idle)
+  const int C = V < 4096 * 8 ? 1 : B <= 18 ? 8 : B <= 37 ? 4 : B <= 74 ? 2 : 1;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const float* lp = logits.data_ptr<float>();
+  float* vp = out_val.numel() ? out_val.data_ptr<float>() : (float*)nullptr;
+  const int ld = (int)logits.stride(0), off = (int)index_offset;
+  int* ip = out_idx.data_ptr<int>();
+  switch (C) {
+    case 8: launch_pdl_cluster(argmax_rows_kernel<8>, dim3(B * 8), dim3(512), 0, stream, 8, lp, V, ld, ip, vp, off); break;
+    case 4: launch_pdl_cluster(argmax_rows_kernel<4>, dim3(B * 4), dim3(512), 0, stream, 4, lp, V, ld, ip, vp, off); break;
+    case 2: launch_pdl_cluster(argmax_rows_kernel<2>, dim3(B * 2), dim3(512), 0, stream, 2, lp, V, ld, ip, vp, off); break;
+    default: launch_pdl(argmax_rows_kernel<1>, dim3(B), dim3(512), 0, stream, lp, V, ld, ip, vp, off); break;
+  }
 }
 
 void argmax_merge(torch::Tensor vals, torch::Tensor idx, torch::Tensor out) {

@@ -539,3 +539,37 @@ def test_decode_reductions_are_bitwise_repeatable():
     draws = [ops.sample_rows(logits.clone(), [0.8] * 4, [50] * 4, [0.9] * 4, [0.0] * 4, [11, 12, 13, 14], [3] * 4)
              for _ in range(3)]
     assert torch.equal(draws[0], draws[1]) and torch.equal(draws[0], draws[2])
+
+
+@pytest.mark.parametrize("B,V", [(1, 151936), (16, 151936), (32, 151936), (64, 152064), (100, 151936),
+                                 (8, 1000), (3, 65537)])
+def test_argmax_rows_clusters(B, V):
+    """Row argmax over clusters of CTAs (vocabulary slices merged through distributed shared
+    memory) equals torch.argmax, including a tie across slices (lowest index wins), a row stride
+    that is not a multiple of 4 and the value output."""
+    logits = torch.randn(B, V + 3, device=dev)[:, :V]
+    logits[0, 5] = 50.0
+    logits[0, V - 2] = 50.0
+    idx = torch.empty(B, dtype=torch.int32, device=dev)
+    val = torch.empty(B, dtype=torch.float32, device=dev)
+    ops.argmax_rows(logits, idx, val, 7)
+    ref = logits.argmax(-1)
+    assert torch.equal(idx.long() - 7, ref) and int(idx[0]) == 12
+    assert torch.equal(val, logits.max(-1).values)
+    lc = logits.contiguous()
+    ops.argmax_rows(lc, idx, val, 0)
+    assert torch.equal(idx.long(), ref)
+
+
+@pytest.mark.parametrize("T", [1, 8, 17, 32, 40, 80])
+def test_cluster_rmsnorm_matches_fp32(T):
+    """Add + RMSNorm of decode batches on a cluster of CTAs per row (bf16 parts and residual)."""
+    H = 4096
+    a, b = (torch.randn(T, H, device=dev) * 0.5).bfloat16(), (torch.randn(T, H, device=dev) * 0.5).bfloat16()
+    res = torch.randn(T, H, device=dev).bfloat16()
+    w = (torch.rand(H, device=dev) + 0.5).bfloat16()
+    ro = torch.empty_like(res)
+    y = ops.rmsnorm([a, b], w, 1e-6, residual=res, residual_out=ro)
+    x = a.float() + b.float() + res.float()
+    ref = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+    assert _rel(ro, x) < 1e-2 and _rel(y, ref) < 1e-2

@@ -92,7 +92,9 @@ def test_engine_turboquant_kv_cpu():
 def _tiny_engine_outputs(fmts, residual=0, max_seq=256, n_prompt=48, new=8, device="cpu"):
     import b200serve.models.config as mc
     cfg = replace(BUILTIN["tiny-qwen2"], head_dim=128, num_heads=2, num_kv_heads=2)
-    w = random_weights(cfg, seed=0, dtype=torch.float32 if device == "cpu" else torch.bfloat16, device=device)
+    # CPU: shared fp32 weights; GPU: each engine builds the same random weights from its seed (the
+    # TurboQuant path rotates a dense o_proj before packing)
+    w = random_weights(cfg, seed=0, dtype=torch.float32) if device == "cpu" else None
     old = mc.BUILTIN["tiny-qwen2"]
     mc.BUILTIN["tiny-qwen2"] = cfg
     outs, logits = {}, {}
