@@ -110,27 +110,40 @@ __device__ __forceinline__ float partial_col(const PartialIn& pi, int row, int c
 
 // Sum of the slots for NE consecutive columns of one tile (NE even; 8-byte aligned, 16-byte
 // when NE is a multiple of 4), in slot order, rounded to bf16 as a bf16 GEMM output would be.
-template <int NE>
+// The reads of up to BATCH slots are issued together (slots past n read nothing and add zero), so
+// a column costs one L2 round trip per batch rather than one per slot.
+template <int NE, int BATCH = 8>
 __device__ __forceinline__ void partial_sum(const PartialIn& pi, int row, int col, float* acc) {
+  constexpr int kPartBatch = BATCH;
   const int n = partial_slots(pi, col);
   const float* src = pi.part + (size_t)row * pi.cols + col;
   const size_t slot = (size_t)pi.rows * pi.cols;
 #pragma unroll
   for (int i = 0; i < NE; ++i) acc[i] = 0.f;
-  for (int s = 0; s < n; ++s) {
-    if constexpr (NE % 4 == 0) {
+  for (int s0 = 0; s0 < n; s0 += kPartBatch) {
+    float v[kPartBatch][NE];
 #pragma unroll
-      for (int i = 0; i < NE; i += 4) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(src + s * slot + i));
-        acc[i] += v.x; acc[i + 1] += v.y; acc[i + 2] += v.z; acc[i + 3] += v.w;
-      }
-    } else {
+    for (int u = 0; u < kPartBatch; ++u) {
+      const bool live = s0 + u < n;
+      const float* p = src + (size_t)(s0 + u) * slot;
+      if constexpr (NE % 4 == 0) {
 #pragma unroll
-      for (int i = 0; i < NE; i += 2) {
-        const float2 v = __ldcg(reinterpret_cast<const float2*>(src + s * slot + i));
-        acc[i] += v.x; acc[i + 1] += v.y;
+        for (int i = 0; i < NE; i += 4) {
+          const float4 t = live ? __ldcg(reinterpret_cast<const float4*>(p + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          v[u][i] = t.x; v[u][i + 1] = t.y; v[u][i + 2] = t.z; v[u][i + 3] = t.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < NE; i += 2) {
+          const float2 t = live ? __ldcg(reinterpret_cast<const float2*>(p + i)) : make_float2(0.f, 0.f);
+          v[u][i] = t.x; v[u][i + 1] = t.y;
+        }
       }
     }
+#pragma unroll
+    for (int u = 0; u < kPartBatch; ++u)          // slot order; an absent slot adds +0.0 (no change)
+#pragma unroll
+      for (int i = 0; i < NE; ++i) acc[i] += v[u][i];
   }
 #pragma unroll
   for (int i = 0; i < NE; ++i) acc[i] = __bfloat162float(__float2bfloat16_rn(acc[i]));

@@ -114,8 +114,9 @@ __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
     if (col < H) {
       float acc[8];
       if (pin.part) {
-        // the GEMM's fp32 stream-K partials of this row (one "part"), summed here
-        partial_sum<8>(pin, row, col, acc);
+        // the GEMM's fp32 stream-K partials of this row (one "part"), summed here (a small batch:
+        // this kernel runs up to 1024 threads and keeps VPT x 8 values per thread)
+        partial_sum<8, 2>(pin, row, col, acc);
       } else {
       // partials may have been written by other GPUs: read through L2, not L1
       uint4 a4 = lamport ? lamport_take(parts.p[0] + base + col, wait_ns, err, gave_up)
