@@ -56,6 +56,11 @@ def bench_gemm(cases=None):
              "hbm_frac": round(byts / ms / 1e6 / hbm, 3), "tc_frac": round(flops / ms / 1e9 / tf, 3),
              "cublas_ms": round(ms_ref, 4), "speedup_vs_cublas": round(ms_ref / ms, 3),
              "plan": plan, "peaks": src}
+        if M <= 64 and epi == ops.EPI_BF16:
+            # the decode path: stream-K fp32 partials that the next row kernel sums (no fix-up here)
+            ms_p = time_cuda(lambda: ops.linear_partial(x, w))
+            r["partial_ms"] = round(ms_p, 4)
+            r["partial_speedup_vs_cublas"] = round(ms_ref / ms_p, 3)
         print(json.dumps(r), flush=True)
         out.append(r)
     return out
