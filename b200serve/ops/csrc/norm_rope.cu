@@ -189,15 +189,19 @@ __global__ void __launch_bounds__(1024) rmsnorm_fused_kernel(
 // of C CTAs: CTA r of a row takes columns [r H / C, (r + 1) H / C) (8 per thread), and the row's sum
 // of squares is reduced across the cluster through distributed shared memory. With one CTA per row
 // only T SMs would work (T = 32 decode rows against 148 SMs). Inputs: the bf16 parts summed, or the
-// fp32 stream-K partials (PartialIn); the same rounding as rmsnorm_fused_kernel.
+// fp32 stream-K partials (PartialIn), or the flag-free all-reduce slots of every rank (lamport 1 /
+// 2, as in rmsnorm_fused_kernel: each CTA polls only its own columns, bounded by wait_ns); the
+// same rounding as rmsnorm_fused_kernel.
 template <int C>
 __global__ void __launch_bounds__(256) rmsnorm_cluster_kernel(
     PartPtrs parts, int nparts, const __nv_bfloat16* residual_in, __nv_bfloat16* residual_out,
-    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H, float eps, const PartialIn pin) {
+    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H, float eps, const PartialIn pin,
+    int lamport, uint64_t wait_ns, int* err) {
   __shared__ float red[32];
   __shared__ float cl_ss;
-  pdl_wait();
+  if (lamport != 2) pdl_wait();
   pdl_trigger();
+  bool gave_up = false;
   const int row = blockIdx.x / C;
   const uint32_t rank = cluster_rank();
   const int col = (int)rank * (H / C) + threadIdx.x * 8;
@@ -209,6 +213,16 @@ __global__ void __launch_bounds__(256) rmsnorm_cluster_kernel(
     float acc[8];
     if (pin.part) {
       partial_sum<8>(pin, row, col, acc);
+    } else if (lamport) {
+      uint4 a4 = lamport_take(parts.p[0] + base + col, wait_ns, err, gave_up);
+      unpack8(*reinterpret_cast<bf16x8*>(&a4), acc);
+      for (int k = 1; k < nparts; ++k) {           // rank order: the same sum on every rank
+        float t[8];
+        uint4 t4 = lamport_take(parts.p[k] + base + col, wait_ns, err, gave_up);
+        unpack8(*reinterpret_cast<bf16x8*>(&t4), t);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] += t[i];
+      }
     } else {
       unpack8(*reinterpret_cast<const bf16x8*>(parts.p[0] + base + col), acc);
       for (int k = 1; k < nparts; ++k) {
@@ -444,14 +458,19 @@ void rmsnorm_fused_impl(std::vector<torch::Tensor> parts, c10::optional<torch::T
   static const int cl_env = [] { const char* e = getenv("B200_NORM_CLUSTER"); return e ? atoi(e) : -1; }();
   int C = T <= 18 ? 8 : T <= 37 ? 4 : T <= 74 ? 2 : 1;
   if (cl_env >= 0) C = cl_env;
-  if (!wait_flags && !lamport && ag.world == 0 && (C == 2 || C == 4 || C == 8) && H % (8 * C) == 0 &&
-      H / (8 * C) <= 256) {
+  // the flag-free (lamport) receive slots take the cluster path only with B200_NORM_CLUSTER_LAMPORT=1:
+  // measured at TP2 (8B, batch 32) it was 1.4% slower (7743 against 7850 tok/s), four times as many
+  // CTAs polling the slots while the pushing GEMM still runs
+  static const bool cl_lamport = [] { const char* e = getenv("B200_NORM_CLUSTER_LAMPORT"); return e && atoi(e) != 0; }();
+  if (!wait_flags && (!lamport || cl_lamport) && ag.world == 0 && (C == 2 || C == 4 || C == 8) &&
+      H % (8 * C) == 0 && H / (8 * C) <= 256) {
     const dim3 grid(T * C), block(((H / (8 * C)) + 31) / 32 * 32);
     const int np = (int)parts.size();
+    const uint64_t wns = flag_wait_ns();
     switch (C) {
-      case 8: launch_pdl_cluster(rmsnorm_cluster_kernel<8>, grid, block, 0, stream, 8, pp, np, rin, rout, wp, op, H, (float)eps, pin); break;
-      case 4: launch_pdl_cluster(rmsnorm_cluster_kernel<4>, grid, block, 0, stream, 4, pp, np, rin, rout, wp, op, H, (float)eps, pin); break;
-      default: launch_pdl_cluster(rmsnorm_cluster_kernel<2>, grid, block, 0, stream, 2, pp, np, rin, rout, wp, op, H, (float)eps, pin); break;
+      case 8: launch_pdl_cluster(rmsnorm_cluster_kernel<8>, grid, block, 0, stream, 8, pp, np, rin, rout, wp, op, H, (float)eps, pin, lamport, wns, err); break;
+      case 4: launch_pdl_cluster(rmsnorm_cluster_kernel<4>, grid, block, 0, stream, 4, pp, np, rin, rout, wp, op, H, (float)eps, pin, lamport, wns, err); break;
+      default: launch_pdl_cluster(rmsnorm_cluster_kernel<2>, grid, block, 0, stream, 2, pp, np, rin, rout, wp, op, H, (float)eps, pin, lamport, wns, err); break;
     }
     B200_CHECK_CUDA(cudaGetLastError());
     return;
