@@ -371,7 +371,9 @@ void gemm_tc_push(torch::Tensor act, torch::Tensor w, torch::Tensor dst_ptrs, in
 // slots}; part must hold slots * M * N floats (gemm_partial_slots gives the size up front).
 std::vector<int64_t> gemm_partial_plan(int64_t M, int64_t N, int64_t K, int64_t num_sms) {
   const int64_t kb = (K + 63) / 64, tiles = (N + 127) / 128, total = tiles * kb;
-  // CTAs per SM (B200_GEMM_PARTIAL_PER_SM, 1 or 2; the decode ring of ~104 KB lets two share an SM)
+  // CTAs per SM (B200_GEMM_PARTIAL_PER_SM, 1 or 2; the decode ring of ~104 KB lets two share an SM).
+  // Two measured no better on the 8B decode step (6084 against 6055 tok/s, within run-to-run noise),
+  // so one is the default.
   static const int per_sm = [] { const char* e = getenv("B200_GEMM_PARTIAL_PER_SM"); return e && atoi(e) == 2 ? 2 : 1; }();
   // at least 4 k-blocks (64 KB of weights) per CTA, so every piece amortises its pipeline start
   const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>(per_sm * num_sms, total / 4));
